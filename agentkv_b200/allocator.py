@@ -1,0 +1,451 @@
+"""SlabAllocator — KV block pool with a device-resident free list and refcounts.
+
+Same public surface as the reference's SlabAllocator
+(agentkv/core/slab_allocator.py:98-447): ``alloc``, ``inc_ref``, ``dec_ref``,
+``copy_block``, ``zero_block``, ``get_block_tensor``, ``ref_count``, read
+sections, ``maybe_advance_epoch``, ``free_count``, ``allocated_count``,
+``stats`` — with the same exceptions and messages.  The state those methods
+mutate lives on the GPU:
+
+* ``_kv_data``       the pool tensor [N, L, 2, H, bs, D] (unchanged layout);
+* ``_ref_counts``    int32 [N] refcounts;
+* ``_free_ring``     the free deque as a ring (pop right, recycled ids left);
+* ``_limbo_*``       retired ids waiting for the reclaimer (deferred + pending);
+* ``_ctl``           cursors and counters (op count, epoch, stats).
+
+Every operation is a launch of the C ABI (akv_alloc_batch / akv_incref_batch
+/ akv_decref_batch / akv_cow_batch / akv_limbo_release / akv_epoch_advance)
+that reproduces the reference's sequential semantics, including the order in
+which ids leave and re-enter the free list.  The single-op methods wait for
+their result (they return ids / booleans or raise at once, like the
+reference); the ``*_batch`` methods enqueue one launch for a whole batch and
+return device tensors without waiting — device-detected errors then surface
+at the next waiting call (or ``check()``).
+
+The pool itself must live on a CUDA device, or on ``meta`` for the
+metadata-only pools of the vLLM / SGLang adapters (their free list and
+refcounts then live on the current CUDA device).  A CPU pool is rejected:
+this package has no CPU implementation of the path.
+"""
+
+from __future__ import annotations
+
+import threading
+from typing import Optional, Tuple
+
+import numpy as np
+import torch
+
+from . import _native as N
+from .config import PoolConfig, torch_dtype
+from .kernels import copy_blocks as _copy_blocks
+from .kernels import stream_handle
+from .reclamation import EpochReclaimer
+
+INVALID_BLOCK: int = -1
+
+_INT64_MAX = (1 << 63) - 1
+
+
+class BlockHandle:
+    """Opaque handle to a KV block (agentkv/core/slab_allocator.py:71-95)."""
+
+    __slots__ = ("block_id",)
+
+    def __init__(self, block_id: int) -> None:
+        self.block_id = block_id
+
+    def is_valid(self) -> bool:
+        return self.block_id != INVALID_BLOCK
+
+    def __repr__(self) -> str:
+        return f"BlockHandle(id={self.block_id})"
+
+    def __eq__(self, other: object) -> bool:
+        if isinstance(other, BlockHandle):
+            return self.block_id == other.block_id
+        return NotImplemented
+
+    def __hash__(self) -> int:
+        return hash(self.block_id)
+
+
+def _metadata_device(device: str) -> torch.device:
+    dev = torch.device(device)
+    if dev.type == "cuda":
+        if not torch.cuda.is_available():
+            raise RuntimeError("agentkv_b200: a CUDA pool was requested but no CUDA device is visible")
+        return torch.device("cuda", dev.index if dev.index is not None else torch.cuda.current_device())
+    if dev.type == "meta":
+        if not torch.cuda.is_available():
+            raise RuntimeError(
+                "agentkv_b200: a metadata-only (meta) pool keeps its free list and refcounts "
+                "on a CUDA device, and none is visible"
+            )
+        return torch.device("cuda", torch.cuda.current_device())
+    raise ValueError(
+        f"agentkv_b200 pools live on a CUDA device (or 'meta' for metadata-only pools); "
+        f"got device={device!r}"
+    )
+
+
+class SlabAllocator:
+    """Fixed-capacity KV block pool; see the module docstring."""
+
+    def __init__(self, config: PoolConfig) -> None:
+        if config.epoch_interval <= 0:
+            raise ValueError(f"epoch_interval must be > 0, got {config.epoch_interval}")
+        self._cfg = config
+        self._lock = threading.RLock()
+        self._dev = _metadata_device(config.device)
+        n = config.total_blocks
+        self._kv_data: torch.Tensor = torch.zeros(
+            n, config.num_layers, 2, config.num_kv_heads, config.block_size, config.head_dim,
+            dtype=torch_dtype(config.dtype), device=config.device,
+        )
+        dev = self._dev
+        i32, i64 = torch.int32, torch.int64
+        self._ref_counts = torch.zeros(n, dtype=i32, device=dev)
+        self._free_ring = torch.empty(n, dtype=i32, device=dev)
+        self._limbo_ids = torch.empty(n, dtype=i32, device=dev)
+        self._limbo_epochs = torch.empty(n, dtype=i64, device=dev)
+        self._ctl = torch.zeros(N.CTL_WORDS, dtype=i64, device=dev)
+        self._scratch_count = torch.zeros(n, dtype=i32, device=dev)
+        self._scratch_last = torch.zeros(n, dtype=i32, device=dev)
+        self._scratch_aux = torch.zeros(N.AUX_WORDS, dtype=i32, device=dev)
+        # io: [0:8] AkvStatus, [8:40] small outputs, [40:64] small inputs
+        self._io = torch.zeros(64, dtype=i32, device=dev)
+        self._status = self._io[0:8]
+        self._h_in = torch.zeros(24, dtype=i32, pin_memory=True)
+        self._h_out = torch.zeros(64, dtype=i32, pin_memory=True)
+        self._state = N.AkvAllocState(
+            self._ref_counts.data_ptr(), self._free_ring.data_ptr(), self._limbo_ids.data_ptr(),
+            self._limbo_epochs.data_ptr(), self._ctl.data_ptr(), self._scratch_count.data_ptr(),
+            self._scratch_last.data_ptr(), self._scratch_aux.data_ptr(), n, 0,
+        )
+        self._reclaimer = EpochReclaimer(self)
+        with torch.cuda.device(dev):
+            N.check(N.lib.akv_alloc_init(self._state, self._stream()))
+
+    # ── plumbing ──────────────────────────────────────────────────────────────
+    def _stream(self) -> int:
+        return stream_handle(self._dev)
+
+    @property
+    def device(self) -> torch.device:
+        """Device that holds the free list and refcounts."""
+        return self._dev
+
+    @property
+    def config(self) -> PoolConfig:
+        return self._cfg
+
+    def _tick(self) -> N.AkvTick:
+        return self._reclaimer.tick(self._cfg.epoch_interval)
+
+    def _sync_io(self, n_out: int = 16) -> np.ndarray:
+        """Copy status + the first outputs to the host and wait."""
+        h = self._h_out[: 8 + n_out]
+        h.copy_(self._io[: 8 + n_out], non_blocking=True)
+        torch.cuda.current_stream(self._dev).synchronize()
+        return h.numpy().copy()
+
+    def _stage_ids(self, ids) -> int:
+        """Put up to 24 ids into the device input slots; returns the pointer."""
+        k = len(ids)
+        self._h_in[:k] = torch.as_tensor(ids, dtype=torch.int32)
+        self._io[40 : 40 + k].copy_(self._h_in[:k], non_blocking=True)
+        return self._io[40:].data_ptr()
+
+    def _raise_status(self, io: np.ndarray, op: str = "") -> None:
+        code = int(io[0])
+        if code == 0:
+            return
+        index, bid, observed = int(io[1]), int(io[2]), int(io[3])
+        self._status.zero_()
+        raise self._exception(code, bid, observed, op, index)
+
+    def _exception(self, code: int, bid: int, observed: int, op: str, index: int = 0) -> Exception:
+        n = self._cfg.total_blocks
+        if code == N.AKV_ERR_EXHAUSTED:
+            return MemoryError(
+                f"AgentKV pool exhausted: all {n} blocks are in use. "
+                "Increase PoolConfig.total_blocks or free some agents."
+            )
+        if code == N.AKV_ERR_NOT_ALLOCATED:
+            return ValueError(
+                f"inc_ref on block {bid} with ref_count={observed} "
+                "(not allocated — double-inc or use-after-free?)"
+            )
+        if code == N.AKV_ERR_DOUBLE_FREE:
+            return ValueError(
+                f"dec_ref on block {bid} with ref_count={observed} (already free or double-free?)"
+            )
+        if code == N.AKV_ERR_NOT_EXCLUSIVE:
+            if op == "zero_block":
+                return ValueError(
+                    f"zero_block: block {bid} must be exclusively owned (ref_count=1, got {observed})"
+                )
+            return ValueError(
+                f"copy_block: dst block {bid} must have ref_count=1 (got {observed}). "
+                "Only exclusively-owned blocks may be written."
+            )
+        if code == N.AKV_ERR_OUT_OF_RANGE:
+            return ValueError(f"block_id {bid} out of range [0, {n})")
+        return RuntimeError(
+            f"agentkv_b200 device error: {N.ERROR_NAMES.get(code, code)} "
+            f"(position {index}, id {bid}, observed {observed})"
+        )
+
+    def _validate_handle(self, handle: BlockHandle) -> None:
+        if not isinstance(handle, BlockHandle):
+            raise TypeError(f"Expected BlockHandle, got {type(handle)}")
+        if not handle.is_valid():
+            raise ValueError("BlockHandle is invalid (block_id == INVALID_BLOCK)")
+        if handle.block_id < 0 or handle.block_id >= self._cfg.total_blocks:
+            raise ValueError(f"block_id {handle.block_id} out of range [0, {self._cfg.total_blocks})")
+
+    # ── single operations (reference semantics, wait for the result) ──────────
+    def alloc(self) -> BlockHandle:
+        """Claim a free block (ref_count 1); MemoryError when exhausted."""
+        with self._lock:
+            out = self._io[8:].data_ptr()
+            N.check(N.lib.akv_alloc_batch(self._state, 1, out, self._tick(), self._status.data_ptr(),
+                                          self._stream()))
+            io = self._sync_io(1)
+            self._raise_status(io, "alloc")
+            return BlockHandle(int(io[8]))
+
+    def inc_ref(self, handle: BlockHandle) -> None:
+        self._validate_handle(handle)
+        with self._lock:
+            ptr = self._stage_ids([handle.block_id])
+            N.check(N.lib.akv_incref_batch(self._state, ptr, 1, self._tick(), self._status.data_ptr(),
+                                           self._stream()))
+            self._raise_status(self._sync_io(0), "inc_ref")
+
+    def dec_ref(self, handle: BlockHandle) -> bool:
+        """Decrement; True when the count reached zero (block retired)."""
+        self._validate_handle(handle)
+        with self._lock:
+            ptr = self._stage_ids([handle.block_id])
+            N.check(N.lib.akv_decref_batch(self._state, ptr, 1, self._tick(), None,
+                                           self._status.data_ptr(), self._stream()))
+            self._h_out[40:42].copy_(self._ctl[N.CTL_LAST_RETIRED : N.CTL_LAST_RETIRED + 1].view(torch.int32),
+                                     non_blocking=True)
+            io = self._sync_io(0)
+            self._raise_status(io, "dec_ref")
+            return int(self._h_out[40]) > 0
+
+    def get_block_tensor(self, handle: BlockHandle) -> torch.Tensor:
+        self._validate_handle(handle)
+        return self._kv_data[handle.block_id]
+
+    def copy_block(self, src: BlockHandle, dst: BlockHandle) -> None:
+        """Copy src's KV data into dst, which must be exclusively owned."""
+        self._validate_handle(src)
+        self._validate_handle(dst)
+        with self._lock:
+            if self._kv_data.device.type == "meta":
+                rc = int(self._ref_counts[dst.block_id].item())
+                if rc != 1:
+                    raise self._exception(N.AKV_ERR_NOT_EXCLUSIVE, dst.block_id, rc, "copy_block")
+                return
+            ptr = self._stage_ids([src.block_id, dst.block_id])
+            N.check(N.lib.akv_copy_blocks(self._kv_data.data_ptr(), self._cfg.bytes_per_block,
+                                          self._cfg.total_blocks, ptr, 1, self._ref_counts.data_ptr(),
+                                          self._status.data_ptr(), self._stream()))
+            self._raise_status(self._sync_io(0), "copy_block")
+
+    def zero_block(self, handle: BlockHandle) -> None:
+        """Write +0.0 over an exclusively owned block."""
+        self._validate_handle(handle)
+        with self._lock:
+            if self._kv_data.device.type == "meta":
+                rc = int(self._ref_counts[handle.block_id].item())
+                if rc != 1:
+                    raise self._exception(N.AKV_ERR_NOT_EXCLUSIVE, handle.block_id, rc, "zero_block")
+                return
+            ptr = self._stage_ids([handle.block_id])
+            N.check(N.lib.akv_zero_blocks(self._kv_data.data_ptr(), self._cfg.bytes_per_block,
+                                          self._cfg.total_blocks, ptr, 1, self._ref_counts.data_ptr(),
+                                          self._status.data_ptr(), self._stream()))
+            self._raise_status(self._sync_io(0), "zero_block")
+
+    # ── epoch / reclamation ───────────────────────────────────────────────────
+    def enter_read_section(self) -> int:
+        return self._reclaimer.enter_read_section()
+
+    def leave_read_section(self, token: int) -> None:
+        self._reclaimer.leave_read_section(token)
+
+    def maybe_advance_epoch(self) -> None:
+        self._reclaimer.maybe_advance()
+
+    # ── introspection ─────────────────────────────────────────────────────────
+    def ref_count(self, handle: BlockHandle) -> int:
+        self._validate_handle(handle)
+        with self._lock:
+            return int(self._ref_counts[handle.block_id].item())
+
+    def ctl(self) -> np.ndarray:
+        """Host copy of the control words (waits)."""
+        with self._lock:
+            return self._ctl.cpu().numpy()
+
+    @property
+    def free_count(self) -> int:
+        return int(self.ctl()[N.CTL_FREE_SIZE])
+
+    @property
+    def allocated_count(self) -> int:
+        c = self.ctl()
+        return int(self._cfg.total_blocks - c[N.CTL_FREE_SIZE] - (c[N.CTL_LIMBO_TAIL] - c[N.CTL_LIMBO_HEAD]))
+
+    def stats(self) -> dict:
+        c = self.ctl()
+        n = self._cfg.total_blocks
+        return {
+            "total_blocks": n,
+            "free_blocks": int(c[N.CTL_FREE_SIZE]),
+            "allocated_blocks": int(n - c[N.CTL_FREE_SIZE] - (c[N.CTL_LIMBO_TAIL] - c[N.CTL_LIMBO_HEAD])),
+            "peak_allocated": int(c[N.CTL_PEAK]),
+            "total_allocs": int(c[N.CTL_ALLOCS]),
+            "total_frees": int(c[N.CTL_FREES]),
+            "pending_reclamation": int(c[N.CTL_LIMBO_TAIL] - c[N.CTL_LIMBO_REL]),
+            "epoch": int(c[N.CTL_EPOCH]),
+            "pool_size_gb": self._cfg.total_gb,
+        }
+
+    def free_list(self) -> np.ndarray:
+        """The free list left to right (waits)."""
+        with self._lock:
+            c = self._ctl.cpu().numpy()
+            ring = self._free_ring.cpu().numpy()
+        n = self._cfg.total_blocks
+        idx = (int(c[N.CTL_FREE_LEFT]) + np.arange(int(c[N.CTL_FREE_SIZE]))) % n
+        return ring[idx]
+
+    def limbo(self) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+        """(deferred ids, pending ids, pending epochs) in FIFO order (waits)."""
+        with self._lock:
+            c = self._ctl.cpu().numpy()
+            ids = self._limbo_ids.cpu().numpy()
+            eps = self._limbo_epochs.cpu().numpy()
+        n = self._cfg.total_blocks
+        h, r, t = (int(c[k]) for k in (N.CTL_LIMBO_HEAD, N.CTL_LIMBO_REL, N.CTL_LIMBO_TAIL))
+        d_idx = np.arange(h, r) % n
+        p_idx = np.arange(r, t) % n
+        return ids[d_idx], ids[p_idx], eps[p_idx]
+
+    # ── batched operations (one launch each, no waiting) ──────────────────────
+    def _device_ids(self, ids) -> torch.Tensor:
+        if isinstance(ids, torch.Tensor) and ids.device == self._dev and ids.dtype == torch.int32:
+            return ids.contiguous()
+        t = torch.as_tensor(ids, dtype=torch.int32)
+        if t.device.type == "cpu" and not t.is_pinned():
+            t = t.pin_memory()
+        return t.to(self._dev, non_blocking=True)
+
+    def alloc_batch(self, n: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """n alloc() calls in one launch; returns the ids (device int32)."""
+        if out is None:
+            out = torch.empty(max(n, 0), dtype=torch.int32, device=self._dev)
+        with self._lock:
+            N.check(N.lib.akv_alloc_batch(self._state, n, out.data_ptr() if n else None, self._tick(),
+                                          self._status.data_ptr(), self._stream()))
+        return out
+
+    def inc_ref_batch(self, ids) -> None:
+        t = self._device_ids(ids)
+        with self._lock:
+            N.check(N.lib.akv_incref_batch(self._state, t.data_ptr(), t.numel(), self._tick(),
+                                           self._status.data_ptr(), self._stream()))
+
+    def dec_ref_batch(self, ids, retired_out: Optional[torch.Tensor] = None) -> None:
+        """n dec_ref() calls; retired ids (in retirement order) go to
+        `retired_out` when given; their count is ctl[LAST_RETIRED]."""
+        t = self._device_ids(ids)
+        with self._lock:
+            N.check(N.lib.akv_decref_batch(self._state, t.data_ptr(), t.numel(), self._tick(),
+                                           retired_out.data_ptr() if retired_out is not None else None,
+                                           self._status.data_ptr(), self._stream()))
+
+    def cow_batch(self, blocks, out_blocks: Optional[torch.Tensor] = None,
+                  out_copied: Optional[torch.Tensor] = None,
+                  pairs: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """ensure_mutable over a batch of residual blocks (distinct slots), in
+        order: copy-on-write wherever the refcount is > 1.  Returns
+        (blocks now owned, 1 where a copy happened)."""
+        t = self._device_ids(blocks)
+        n = t.numel()
+        if out_blocks is None:
+            out_blocks = torch.empty(n, dtype=torch.int32, device=self._dev)
+        if out_copied is None:
+            out_copied = torch.empty(n, dtype=torch.int32, device=self._dev)
+        if pairs is None:
+            pairs = torch.empty(2 * max(n, 1), dtype=torch.int32, device=self._dev)
+        meta = self._kv_data.device.type == "meta"
+        with self._lock:
+            N.check(N.lib.akv_cow_batch(
+                self._state, None if meta else self._kv_data.data_ptr(),
+                0 if meta else self._cfg.bytes_per_block, t.data_ptr(), n, out_blocks.data_ptr(),
+                out_copied.data_ptr(), pairs.data_ptr(), self._tick(), self._status.data_ptr(),
+                self._stream()))
+        return out_blocks, out_copied
+
+    def fanout_level(self, parent_tables: torch.Tensor, parent_off: torch.Tensor, parent_lens,
+                     fanout: int, append: int, *, pool: Optional[torch.Tensor] = None,
+                     copy: bool = True) -> dict:
+        """One fork level on device-resident block tables (akv_fanout_plan):
+        every parent is forked `fanout` times; each child copy-on-writes its
+        last inherited block and appends `append` fresh blocks.  Block ids,
+        refcounts and the free list end exactly as after the reference's
+        per-child fork / ensure_mutable_block(-1) / allocate_block calls.
+
+        parent_tables / parent_off are device int32 / int64 tensors (tables
+        concatenated, offsets[P + 1]); parent_lens the P table lengths on the
+        host (all >= 1).  The copies go to `pool` (default: this allocator's
+        pool; a head slice of it on a sharded pool), or are skipped with
+        copy=False (then `pairs` in the result is what to copy).  Returns the
+        device tensors child_tables, child_off, pairs and the launch count."""
+        lens = np.asarray(parent_lens, np.int64)
+        if (lens < 1).any():
+            raise ValueError("fanout_level: every parent needs at least one residual block")
+        P, K, A = len(lens), int(fanout), int(append)
+        nc = P * K
+        total = int(lens.sum())
+        dev = self._dev
+        fresh = self.alloc_batch((1 + A) * nc)
+        child_tables = torch.empty(K * total + nc * A, dtype=torch.int32, device=dev)
+        child_off = torch.empty(nc + 1, dtype=torch.int64, device=dev)
+        inc_ids = torch.empty(K * total, dtype=torch.int32, device=dev)
+        pairs = torch.empty(2 * nc, dtype=torch.int32, device=dev)
+        dec_ids = torch.empty(nc, dtype=torch.int32, device=dev)
+        with self._lock:
+            N.check(N.lib.akv_fanout_plan(parent_tables.data_ptr(), parent_off.data_ptr(), P, K, A,
+                                          fresh.data_ptr(), child_tables.data_ptr(), child_off.data_ptr(),
+                                          inc_ids.data_ptr(), pairs.data_ptr(), dec_ids.data_ptr(),
+                                          self._stream()))
+        self.inc_ref_batch(inc_ids)
+        launches = 1 + 1 + 2
+        target = pool if pool is not None else self._kv_data
+        if copy and target.device.type != "meta":
+            _copy_blocks(target, pairs.view(-1, 2), status=self._status)
+            launches += 1
+        self.dec_ref_batch(dec_ids)
+        launches += 4
+        return {"child_tables": child_tables, "child_off": child_off, "pairs": pairs.view(-1, 2),
+                "child_lens": np.repeat(lens + A, K), "launches": launches}
+
+    def copy_blocks(self, pairs, *, check_refs: bool = True) -> None:
+        """Copy a batch of independent (src, dst) pairs; dsts must be exclusive."""
+        if self._kv_data.device.type == "meta":
+            return
+        _copy_blocks(self._kv_data, self._device_ids(pairs),
+                     ref_counts=self._ref_counts if check_refs else None, status=self._status)
+
+    def check(self) -> None:
+        """Wait for queued work and raise the first device-detected error."""
+        with self._lock:
+            self._raise_status(self._sync_io(0))

@@ -1,0 +1,519 @@
+// akv_blocks.cu — batched copy / zero of whole KV blocks (sm_100a).
+//
+// The pool is total_blocks contiguous spans of bytes_per_block bytes (the
+// reference's `_kv_data[block_id]` view, agentkv/core/slab_allocator.py:
+// 155-164).  A batch of n pairs is split into tiles that never cross a block
+// boundary, so every tile is one contiguous read span and one contiguous write
+// span.  Two copy kernels are provided:
+//   * vec  — 16-byte loads/stores, UNROLL independent loads in flight per
+//            thread, grid-stride over tiles, grid = a multiple of the SM count;
+//   * bulk — one issuing thread per CTA moves 32 KiB chunks with the bulk
+//            async copy engine (cp.async.bulk global→shared, then shared→
+//            global), STAGES chunks in flight, completion tracked by mbarriers.
+// Zero is write-only: vector stores of +0, or bulk stores of a zeroed shared
+// buffer.  Neither reads the old block, unlike the reference Triton kernel
+// that loads `x` and stores `x * 0` (agentkv/core/triton_kernels.py:161-162).
+#include <algorithm>
+
+#include "akv_common.cuh"
+
+namespace {
+
+// ── pair / id validation shared by all kernels ─────────────────────────────
+// Returns true when pair p may be copied.  The CTA that owns chunk 0 of the
+// pair records the error, so each bad pair is reported at most once.
+AKV_DEV bool pair_ok(const int32_t* __restrict__ pairs, int32_t p, int32_t total,
+                     const int32_t* __restrict__ refs, bool report, AkvStatus* st,
+                     int32_t& src, int32_t& dst) {
+  src = pairs[2 * p];
+  dst = pairs[2 * p + 1];
+  if (static_cast<uint32_t>(src) >= static_cast<uint32_t>(total) ||
+      static_cast<uint32_t>(dst) >= static_cast<uint32_t>(total)) {
+    if (report)
+      akv_fail(st, AKV_ERR_OUT_OF_RANGE, p,
+               static_cast<uint32_t>(src) >= static_cast<uint32_t>(total) ? src : dst, total);
+    return false;
+  }
+  if (refs != nullptr) {
+    const int32_t r = refs[dst];
+    if (r != 1) {
+      if (report) akv_fail(st, AKV_ERR_NOT_EXCLUSIVE, p, dst, r);
+      return false;
+    }
+  }
+  return true;
+}
+
+AKV_DEV bool id_ok(const int32_t* __restrict__ ids, int32_t i, int32_t total,
+                   const int32_t* __restrict__ refs, bool report, AkvStatus* st, int32_t& id) {
+  id = ids[i];
+  if (static_cast<uint32_t>(id) >= static_cast<uint32_t>(total)) {
+    if (report) akv_fail(st, AKV_ERR_OUT_OF_RANGE, i, id, total);
+    return false;
+  }
+  if (refs != nullptr) {
+    const int32_t r = refs[id];
+    if (r != 1) {
+      if (report) akv_fail(st, AKV_ERR_NOT_EXCLUSIVE, i, id, r);
+      return false;
+    }
+  }
+  return true;
+}
+
+// ── vector kernels ─────────────────────────────────────────────────────────
+template <typename W, int THREADS, int UNROLL>
+__global__ void __launch_bounds__(THREADS)
+k_copy_vec(char* __restrict__ pool, int64_t bpb, int32_t total,
+           const int32_t* __restrict__ pairs, int32_t n_pairs, int64_t tiles_per_block,
+           const int32_t* __restrict__ refs, AkvStatus* st, const int64_t* __restrict__ n_dev) {
+  if (akv_failed(st)) return;
+  // A device-side count (written by an earlier kernel) caps the batch.
+  if (n_dev != nullptr) n_pairs = static_cast<int32_t>(min(static_cast<int64_t>(n_pairs), *n_dev));
+  constexpr int64_t kTileW = static_cast<int64_t>(THREADS) * UNROLL;
+  const int64_t words_per_block = bpb / static_cast<int64_t>(sizeof(W));
+  const int64_t n_tiles = static_cast<int64_t>(n_pairs) * tiles_per_block;
+  for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+    const int32_t p = static_cast<int32_t>(t / tiles_per_block);
+    const int64_t c = t - static_cast<int64_t>(p) * tiles_per_block;
+    int32_t src, dst;
+    if (!pair_ok(pairs, p, total, refs, c == 0 && threadIdx.x == 0, st, src, dst)) continue;
+    const W* __restrict__ s =
+        reinterpret_cast<const W*>(pool + static_cast<int64_t>(src) * bpb) + c * kTileW;
+    W* __restrict__ d = reinterpret_cast<W*>(pool + static_cast<int64_t>(dst) * bpb) + c * kTileW;
+    const int64_t rem = words_per_block - c * kTileW;
+    if (rem >= kTileW) {
+      W v[UNROLL];
+#pragma unroll
+      for (int k = 0; k < UNROLL; ++k) v[k] = s[threadIdx.x + k * THREADS];
+#pragma unroll
+      for (int k = 0; k < UNROLL; ++k) d[threadIdx.x + k * THREADS] = v[k];
+    } else {
+      for (int64_t i = threadIdx.x; i < rem; i += THREADS) d[i] = s[i];
+    }
+  }
+}
+
+template <typename W, int THREADS, int UNROLL>
+__global__ void __launch_bounds__(THREADS)
+k_zero_vec(char* __restrict__ pool, int64_t bpb, int32_t total, const int32_t* __restrict__ ids,
+           int32_t n, int64_t tiles_per_block, const int32_t* __restrict__ refs, AkvStatus* st) {
+  if (akv_failed(st)) return;
+  constexpr int64_t kTileW = static_cast<int64_t>(THREADS) * UNROLL;
+  const int64_t words_per_block = bpb / static_cast<int64_t>(sizeof(W));
+  const int64_t n_tiles = static_cast<int64_t>(n) * tiles_per_block;
+  W z;
+  memset(&z, 0, sizeof(W));
+  for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+    const int32_t i = static_cast<int32_t>(t / tiles_per_block);
+    const int64_t c = t - static_cast<int64_t>(i) * tiles_per_block;
+    int32_t id;
+    if (!id_ok(ids, i, total, refs, c == 0 && threadIdx.x == 0, st, id)) continue;
+    W* __restrict__ d = reinterpret_cast<W*>(pool + static_cast<int64_t>(id) * bpb) + c * kTileW;
+    const int64_t rem = words_per_block - c * kTileW;
+    if (rem >= kTileW) {
+#pragma unroll
+      for (int k = 0; k < UNROLL; ++k) d[threadIdx.x + k * THREADS] = z;
+    } else {
+      for (int64_t i2 = threadIdx.x; i2 < rem; i2 += THREADS) d[i2] = z;
+    }
+  }
+}
+
+// ── bulk-async (TMA engine) kernels ────────────────────────────────────────
+constexpr int kBulkChunk = 32 * 1024;  // bytes per bulk copy
+constexpr int kBulkStages = 6;         // chunks in flight per CTA (192 KiB smem)
+
+AKV_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+AKV_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+AKV_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+      "r"(bytes)
+      : "memory");
+}
+
+// Waits for phase `parity` of the barrier, giving up after kAkvWaitLimitNs.
+AKV_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = akv_globaltimer();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (akv_globaltimer() - t0 > kAkvWaitLimitNs) return false;
+  }
+}
+
+AKV_DEV void bulk_load(uint32_t smem_dst, const void* gsrc, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_dst),
+      "l"(gsrc), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+AKV_DEV void bulk_store(void* gdst, uint32_t smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+               "r"(smem_src), "r"(bytes)
+               : "memory");
+}
+
+AKV_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+template <int N>
+AKV_DEV void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+AKV_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+struct BulkDesc {
+  char* dst;
+  uint32_t bytes;
+};
+
+// One issuing thread per CTA.  Items are (pair, chunk) in the global order
+// t = blockIdx.x + j * gridDim.x; invalid pairs are skipped by the load cursor
+// and the store cursor replays the loads' descriptors from shared memory.
+__global__ void __launch_bounds__(32)
+k_copy_bulk(char* __restrict__ pool, int64_t bpb, int32_t total,
+            const int32_t* __restrict__ pairs, int32_t n_pairs, int64_t chunks_per_block,
+            const int32_t* __restrict__ refs, AkvStatus* st, const int64_t* __restrict__ n_dev) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ __align__(8) uint64_t bars[kBulkStages];
+  __shared__ BulkDesc desc[kBulkStages];
+  if (threadIdx.x != 0) return;
+  if (akv_failed(st)) return;
+  if (n_dev != nullptr) n_pairs = static_cast<int32_t>(min(static_cast<int64_t>(n_pairs), *n_dev));
+  for (int s = 0; s < kBulkStages; ++s) mbar_init(smem_u32(&bars[s]), 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+
+  const int64_t n_items = static_cast<int64_t>(n_pairs) * chunks_per_block;
+  int64_t t = blockIdx.x;
+  // Advances t to the next valid item of this CTA; false at the end.
+  auto next_valid = [&](int32_t& src, int32_t& dst, int64_t& c) -> bool {
+    while (t < n_items) {
+      const int32_t p = static_cast<int32_t>(t / chunks_per_block);
+      c = t - static_cast<int64_t>(p) * chunks_per_block;
+      if (pair_ok(pairs, p, total, refs, c == 0, st, src, dst)) return true;
+      t += gridDim.x;
+    }
+    return false;
+  };
+  auto issue_load = [&](int64_t m, int32_t src, int32_t dst, int64_t c) {
+    const int s = static_cast<int>(m % kBulkStages);
+    const int64_t off = c * kBulkChunk;
+    const int64_t left = bpb - off;
+    const uint32_t bytes = static_cast<uint32_t>(left < kBulkChunk ? left : kBulkChunk);
+    desc[s].dst = pool + static_cast<int64_t>(dst) * bpb + off;
+    desc[s].bytes = bytes;
+    const uint32_t bar = smem_u32(&bars[s]);
+    mbar_expect_tx(bar, bytes);
+    bulk_load(smem_u32(smem + static_cast<size_t>(s) * kBulkChunk),
+              pool + static_cast<int64_t>(src) * bpb + off, bytes, bar);
+  };
+
+  int64_t loads = 0, stores = 0;
+  int32_t src, dst;
+  int64_t c;
+  while (loads < kBulkStages && next_valid(src, dst, c)) {
+    issue_load(loads++, src, dst, c);
+    t += gridDim.x;
+  }
+  bool timed_out = false;
+  while (stores < loads) {
+    const int s = static_cast<int>(stores % kBulkStages);
+    const uint32_t parity = static_cast<uint32_t>((stores / kBulkStages) & 1);
+    if (!mbar_wait(smem_u32(&bars[s]), parity)) {
+      akv_fail(st, AKV_ERR_TIMEOUT, static_cast<int32_t>(blockIdx.x), -1, 0, stores);
+      timed_out = true;
+      break;
+    }
+    bulk_store(desc[s].dst, smem_u32(smem + static_cast<size_t>(s) * kBulkChunk), desc[s].bytes);
+    bulk_commit();
+    ++stores;
+    // The store issued one iteration ago has now finished reading its stage:
+    // refill that stage with the next load.
+    if (stores >= 2) {
+      bulk_wait_read<1>();
+      if (next_valid(src, dst, c)) {
+        issue_load(loads++, src, dst, c);
+        t += gridDim.x;
+      }
+    }
+  }
+  if (timed_out) {
+    // Let every load still in flight land before shared memory is released;
+    // each wait is bounded as well.
+    for (int64_t m = stores + 1; m < loads; ++m)
+      mbar_wait(smem_u32(&bars[m % kBulkStages]), static_cast<uint32_t>((m / kBulkStages) & 1));
+  }
+  bulk_wait_all();
+}
+
+__global__ void __launch_bounds__(256)
+k_zero_bulk(char* __restrict__ pool, int64_t bpb, int32_t total, const int32_t* __restrict__ ids,
+            int32_t n, int64_t chunks_per_block, const int32_t* __restrict__ refs,
+            AkvStatus* st) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ int failed;
+  if (threadIdx.x == 0) failed = akv_failed(st) ? 1 : 0;
+  __syncthreads();
+  if (failed) return;
+  // Zero one chunk of shared memory with all threads, then hand it to the
+  // async proxy.
+  uint4* z = reinterpret_cast<uint4*>(smem);
+  for (int i = threadIdx.x; i < kBulkChunk / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  const uint32_t zs = smem_u32(smem);
+  const int64_t n_items = static_cast<int64_t>(n) * chunks_per_block;
+  int issued = 0;
+  for (int64_t t = blockIdx.x; t < n_items; t += gridDim.x) {
+    const int32_t i = static_cast<int32_t>(t / chunks_per_block);
+    const int64_t c = t - static_cast<int64_t>(i) * chunks_per_block;
+    int32_t id;
+    if (!id_ok(ids, i, total, refs, c == 0, st, id)) continue;
+    const int64_t off = c * kBulkChunk;
+    const int64_t left = bpb - off;
+    const uint32_t bytes = static_cast<uint32_t>(left < kBulkChunk ? left : kBulkChunk);
+    bulk_store(pool + static_cast<int64_t>(id) * bpb + off, zs, bytes);
+    bulk_commit();
+    if (++issued % 8 == 0) bulk_wait_read<8>();
+  }
+  bulk_wait_all();
+}
+
+// ── pair independence check ────────────────────────────────────────────────
+// mark[id]: bit0 = used as a dst, bit1 = read as a src by a pair whose dst is
+// another block.  A dst seen twice, or a dst that another pair reads, makes
+// the batch order-dependent.  A self pair (x, x) is a no-op and only marks x
+// as a dst.
+__global__ void k_check_mark(const int32_t* __restrict__ pairs, int32_t n, int32_t total,
+                             int32_t* __restrict__ mark, AkvStatus* st) {
+  for (int32_t p = blockIdx.x * blockDim.x + threadIdx.x; p < n; p += gridDim.x * blockDim.x) {
+    const int32_t s = pairs[2 * p], d = pairs[2 * p + 1];
+    if (static_cast<uint32_t>(s) >= static_cast<uint32_t>(total) ||
+        static_cast<uint32_t>(d) >= static_cast<uint32_t>(total)) {
+      akv_fail(st, AKV_ERR_OUT_OF_RANGE, p,
+               static_cast<uint32_t>(s) >= static_cast<uint32_t>(total) ? s : d, total);
+      continue;
+    }
+    const int32_t old_d = atomicOr(&mark[d], 1);
+    if (old_d & 1) akv_fail(st, AKV_ERR_DEPENDENT_PAIRS, p, d, old_d);
+    if (s != d) atomicOr(&mark[s], 2);
+  }
+}
+
+__global__ void k_check_scan(const int32_t* __restrict__ pairs, int32_t n, int32_t total,
+                             const int32_t* __restrict__ mark, AkvStatus* st) {
+  for (int32_t p = blockIdx.x * blockDim.x + threadIdx.x; p < n; p += gridDim.x * blockDim.x) {
+    const int32_t d = pairs[2 * p + 1];
+    if (static_cast<uint32_t>(d) < static_cast<uint32_t>(total)) {
+      const int32_t m = mark[d];
+      if (m & 2) akv_fail(st, AKV_ERR_DEPENDENT_PAIRS, p, d, m);
+    }
+  }
+}
+
+__global__ void k_check_clear(const int32_t* __restrict__ pairs, int32_t n, int32_t total,
+                              int32_t* __restrict__ mark) {
+  for (int32_t p = blockIdx.x * blockDim.x + threadIdx.x; p < n; p += gridDim.x * blockDim.x) {
+    const int32_t s = pairs[2 * p], d = pairs[2 * p + 1];
+    if (static_cast<uint32_t>(s) < static_cast<uint32_t>(total)) mark[s] = 0;
+    if (static_cast<uint32_t>(d) < static_cast<uint32_t>(total)) mark[d] = 0;
+  }
+}
+
+// ── launch helpers ─────────────────────────────────────────────────────────
+constexpr int kVecThreads = 256;
+constexpr int kVecUnroll = 4;
+constexpr int kVecCtasPerSm = 8;
+
+int word_bytes_for(const void* pool, int64_t bpb) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(pool);
+  for (int w = 16; w > 1; w >>= 1)
+    if (bpb % w == 0 && a % w == 0) return w;
+  return 1;
+}
+
+template <typename W>
+int launch_copy_vec(char* pool, int64_t bpb, int32_t total, const int32_t* pairs, int32_t n,
+                    const int32_t* refs, AkvStatus* st, cudaStream_t s,
+                    const int64_t* n_dev = nullptr) {
+  const int64_t tile_bytes = static_cast<int64_t>(kVecThreads) * kVecUnroll * sizeof(W);
+  const int64_t tiles = (bpb + tile_bytes - 1) / tile_bytes;
+  const int64_t work = tiles * n;
+  const int64_t max_grid = static_cast<int64_t>(kAkvSMs) * kVecCtasPerSm;
+  const int grid = static_cast<int>(work < max_grid ? work : max_grid);
+  k_copy_vec<W, kVecThreads, kVecUnroll><<<grid, kVecThreads, 0, s>>>(pool, bpb, total, pairs, n,
+                                                                      tiles, refs, st, n_dev);
+  AKV_LAUNCH_CHECK("akv_copy_blocks(vec)");
+  return AKV_OK;
+}
+
+template <typename W>
+int launch_zero_vec(char* pool, int64_t bpb, int32_t total, const int32_t* ids, int32_t n,
+                    const int32_t* refs, AkvStatus* st, cudaStream_t s) {
+  const int64_t tile_bytes = static_cast<int64_t>(kVecThreads) * kVecUnroll * sizeof(W);
+  const int64_t tiles = (bpb + tile_bytes - 1) / tile_bytes;
+  const int64_t work = tiles * n;
+  const int64_t max_grid = static_cast<int64_t>(kAkvSMs) * kVecCtasPerSm;
+  const int grid = static_cast<int>(work < max_grid ? work : max_grid);
+  k_zero_vec<W, kVecThreads, kVecUnroll><<<grid, kVecThreads, 0, s>>>(pool, bpb, total, ids, n,
+                                                                      tiles, refs, st);
+  AKV_LAUNCH_CHECK("akv_zero_blocks(vec)");
+  return AKV_OK;
+}
+
+int copy_vec_dispatch(char* pool, int64_t bpb, int32_t total, const int32_t* pairs, int32_t n,
+                      const int32_t* refs, AkvStatus* st, cudaStream_t s,
+                      const int64_t* n_dev = nullptr) {
+  switch (word_bytes_for(pool, bpb)) {
+    case 16: return launch_copy_vec<uint4>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+    case 8: return launch_copy_vec<uint2>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+    case 4: return launch_copy_vec<uint32_t>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+    case 2: return launch_copy_vec<uint16_t>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+    default: return launch_copy_vec<uint8_t>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+  }
+}
+
+int zero_vec_dispatch(char* pool, int64_t bpb, int32_t total, const int32_t* ids, int32_t n,
+                      const int32_t* refs, AkvStatus* st, cudaStream_t s) {
+  switch (word_bytes_for(pool, bpb)) {
+    case 16: return launch_zero_vec<uint4>(pool, bpb, total, ids, n, refs, st, s);
+    case 8: return launch_zero_vec<uint2>(pool, bpb, total, ids, n, refs, st, s);
+    case 4: return launch_zero_vec<uint32_t>(pool, bpb, total, ids, n, refs, st, s);
+    case 2: return launch_zero_vec<uint16_t>(pool, bpb, total, ids, n, refs, st, s);
+    default: return launch_zero_vec<uint8_t>(pool, bpb, total, ids, n, refs, st, s);
+  }
+}
+
+bool bulk_eligible(const void* pool, int64_t bpb) {
+  return (reinterpret_cast<uintptr_t>(pool) % 16 == 0) && (bpb % 16 == 0);
+}
+
+int copy_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* pairs, int32_t n,
+                     const int32_t* refs, AkvStatus* st, cudaStream_t s,
+                     const int64_t* n_dev = nullptr) {
+  static thread_local bool attr_set = false;
+  const int smem = kBulkStages * kBulkChunk;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(k_copy_bulk, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return akv_cuda_fail(e, "akv_copy_blocks(bulk): smem attribute");
+    attr_set = true;
+  }
+  const int64_t chunks = (bpb + kBulkChunk - 1) / kBulkChunk;
+  const int64_t work = chunks * n;
+  const int grid = static_cast<int>(work < kAkvSMs ? work : kAkvSMs);
+  k_copy_bulk<<<grid, 32, smem, s>>>(pool, bpb, total, pairs, n, chunks, refs, st, n_dev);
+  AKV_LAUNCH_CHECK("akv_copy_blocks(bulk)");
+  return AKV_OK;
+}
+
+int zero_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* ids, int32_t n,
+                     const int32_t* refs, AkvStatus* st, cudaStream_t s) {
+  const int64_t chunks = (bpb + kBulkChunk - 1) / kBulkChunk;
+  const int64_t work = chunks * n;
+  const int64_t max_grid = static_cast<int64_t>(kAkvSMs) * 4;
+  const int grid = static_cast<int>(work < max_grid ? work : max_grid);
+  k_zero_bulk<<<grid, 256, kBulkChunk, s>>>(pool, bpb, total, ids, n, chunks, refs, st);
+  AKV_LAUNCH_CHECK("akv_zero_blocks(bulk)");
+  return AKV_OK;
+}
+
+}  // namespace
+
+// Copy with the pair count read on the device from *n_dev (capped at n_max);
+// used by the CoW batch, whose planner decides on the device how many of its
+// requests copy.  Pairs come from the allocator, so no refcount check.
+int akv_launch_copy_counted(void* pool, int64_t bpb, int32_t total, const int32_t* pairs,
+                            int32_t n_max, const int64_t* n_dev, AkvStatus* st, cudaStream_t s) {
+  if (n_max <= 0) return AKV_OK;
+  return copy_vec_dispatch(static_cast<char*>(pool), bpb, total, pairs, n_max, nullptr, st, s, n_dev);
+}
+
+// ── C ABI ───────────────────────────────────────────────────────────────────
+extern "C" int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int32_t total_blocks,
+                                       const int32_t* pairs, int32_t n_pairs,
+                                       const int32_t* ref_counts, AkvStatus* status,
+                                       int32_t variant, void* stream) {
+  AKV_ARG_CHECK(n_pairs >= 0, "akv_copy_blocks: n_pairs=%d < 0", n_pairs);
+  if (n_pairs == 0) return AKV_OK;
+  AKV_ARG_CHECK(pool != nullptr && pairs != nullptr, "akv_copy_blocks: NULL pool or pairs");
+  AKV_ARG_CHECK(bytes_per_block > 0, "akv_copy_blocks: bytes_per_block=%lld",
+                static_cast<long long>(bytes_per_block));
+  AKV_ARG_CHECK(total_blocks > 0, "akv_copy_blocks: total_blocks=%d", total_blocks);
+  AKV_ARG_CHECK(variant >= 0 && variant <= 2, "akv_copy_blocks: unknown variant %d", variant);
+  char* p = static_cast<char*>(pool);
+  cudaStream_t s = akv_stream(stream);
+  if (variant == 0) variant = 1;
+  if (variant == 2 && bulk_eligible(pool, bytes_per_block))
+    return copy_bulk_launch(p, bytes_per_block, total_blocks, pairs, n_pairs, ref_counts, status, s);
+  return copy_vec_dispatch(p, bytes_per_block, total_blocks, pairs, n_pairs, ref_counts, status, s);
+}
+
+extern "C" int akv_copy_blocks(void* pool, int64_t bytes_per_block, int32_t total_blocks,
+                               const int32_t* pairs, int32_t n_pairs, const int32_t* ref_counts,
+                               AkvStatus* status, void* stream) {
+  return akv_copy_blocks_variant(pool, bytes_per_block, total_blocks, pairs, n_pairs, ref_counts,
+                                 status, 0, stream);
+}
+
+extern "C" int akv_zero_blocks_variant(void* pool, int64_t bytes_per_block, int32_t total_blocks,
+                                       const int32_t* ids, int32_t n, const int32_t* ref_counts,
+                                       AkvStatus* status, int32_t variant, void* stream) {
+  AKV_ARG_CHECK(n >= 0, "akv_zero_blocks: n=%d < 0", n);
+  if (n == 0) return AKV_OK;
+  AKV_ARG_CHECK(pool != nullptr && ids != nullptr, "akv_zero_blocks: NULL pool or ids");
+  AKV_ARG_CHECK(bytes_per_block > 0, "akv_zero_blocks: bytes_per_block=%lld",
+                static_cast<long long>(bytes_per_block));
+  AKV_ARG_CHECK(total_blocks > 0, "akv_zero_blocks: total_blocks=%d", total_blocks);
+  AKV_ARG_CHECK(variant >= 0 && variant <= 2, "akv_zero_blocks: unknown variant %d", variant);
+  char* p = static_cast<char*>(pool);
+  cudaStream_t s = akv_stream(stream);
+  if (variant == 0) variant = 1;
+  if (variant == 2 && bulk_eligible(pool, bytes_per_block))
+    return zero_bulk_launch(p, bytes_per_block, total_blocks, ids, n, ref_counts, status, s);
+  return zero_vec_dispatch(p, bytes_per_block, total_blocks, ids, n, ref_counts, status, s);
+}
+
+extern "C" int akv_zero_blocks(void* pool, int64_t bytes_per_block, int32_t total_blocks,
+                               const int32_t* ids, int32_t n, const int32_t* ref_counts,
+                               AkvStatus* status, void* stream) {
+  return akv_zero_blocks_variant(pool, bytes_per_block, total_blocks, ids, n, ref_counts, status, 0,
+                                 stream);
+}
+
+extern "C" int akv_check_pairs(const int32_t* pairs, int32_t n_pairs, int32_t total_blocks,
+                               int32_t* mark, AkvStatus* status, void* stream) {
+  AKV_ARG_CHECK(n_pairs >= 0, "akv_check_pairs: n_pairs=%d < 0", n_pairs);
+  if (n_pairs == 0) return AKV_OK;
+  AKV_ARG_CHECK(pairs != nullptr && mark != nullptr && status != nullptr,
+                "akv_check_pairs: NULL argument");
+  AKV_ARG_CHECK(total_blocks > 0, "akv_check_pairs: total_blocks=%d", total_blocks);
+  cudaStream_t s = akv_stream(stream);
+  const int threads = 256;
+  const int grid = std::min(akv_ceil_div(n_pairs, threads), kAkvSMs * 4);
+  k_check_mark<<<grid, threads, 0, s>>>(pairs, n_pairs, total_blocks, mark, status);
+  AKV_LAUNCH_CHECK("akv_check_pairs(mark)");
+  k_check_scan<<<grid, threads, 0, s>>>(pairs, n_pairs, total_blocks, mark, status);
+  AKV_LAUNCH_CHECK("akv_check_pairs(scan)");
+  k_check_clear<<<grid, threads, 0, s>>>(pairs, n_pairs, total_blocks, mark);
+  AKV_LAUNCH_CHECK("akv_check_pairs(clear)");
+  return AKV_OK;
+}

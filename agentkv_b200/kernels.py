@@ -1,0 +1,247 @@
+"""Block-movement entry points: the drop-in for agentkv/core/triton_kernels.py.
+
+``copy_block(src, dst)`` and ``zero_block(block)`` keep the reference's
+signatures (triton_kernels.py:171, :206) and are what SlabAllocator calls;
+``copy_blocks`` / ``zero_blocks`` take a whole batch of block ids in one
+launch.  Every call goes to the sm_100a kernels of libagentkv_b200.so through
+its C ABI; there is no Triton, no multi-backend dispatch and no CPU path.
+A CPU tensor is rejected.  A ``meta`` tensor (the metadata-only pools the
+vLLM / SGLang adapters build) holds no bytes, so there is nothing to move and
+the call returns.
+
+Semantics: copy is byte-identical.  zero writes +0.0 (all bits clear) like the
+reference's CPU path ``block.zero_()``; the reference's Triton kernel stores
+``x * 0`` instead (-0.0 for negative inputs, NaN for NaN/Inf).
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _native as N
+
+_STATUS: dict = {}
+
+
+def _status_buffer(device: torch.device) -> torch.Tensor:
+    """A per-device scratch AkvStatus for calls that do not pass their own."""
+    key = (device.type, device.index)
+    buf = _STATUS.get(key)
+    if buf is None:
+        buf = torch.zeros(N.STATUS_BYTES // 4, dtype=torch.int32, device=device)
+        _STATUS[key] = buf
+    return buf
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> bool:
+    """True for a CUDA tensor, False for meta (nothing to do); raises otherwise."""
+    if t.device.type == "cuda":
+        return True
+    if t.device.type == "meta":
+        return False
+    raise ValueError(
+        f"{what}: agentkv_b200 moves KV blocks with its CUDA kernels only; "
+        f"got a {t.device.type} tensor"
+    )
+
+
+def read_status(status: torch.Tensor) -> tuple:
+    """(code, index, id, observed, aux) of a device AkvStatus; synchronises."""
+    s = status.cpu()
+    aux = int(s[4].item()) | (int(s[5].item()) << 32)
+    return int(s[0]), int(s[1]), int(s[2]), int(s[3]), aux
+
+
+def raise_for_status(status: torch.Tensor, clear: bool = True) -> None:
+    code, index, bid, observed, aux = read_status(status)
+    if code == 0:
+        return
+    if clear:
+        status.zero_()
+    raise BlockOpError(code, index, bid, observed, aux)
+
+
+class BlockOpError(RuntimeError):
+    """A device-detected failure of a batched block operation."""
+
+    def __init__(self, code: int, index: int, block_id: int, observed: int, aux: int = 0) -> None:
+        self.code, self.index, self.block_id, self.observed, self.aux = code, index, block_id, observed, aux
+        super().__init__(
+            f"{N.ERROR_NAMES.get(code, code)} at batch position {index}: "
+            f"block {block_id} (observed {observed})"
+        )
+
+
+# ── drop-ins for triton_kernels.copy_block / zero_block ──────────────────────
+def copy_block(src: torch.Tensor, dst: torch.Tensor) -> None:
+    """Copy one KV block (triton_kernels.py:171-203) — src and dst are two
+    block views of one pool tensor, as SlabAllocator passes them."""
+    assert src.shape == dst.shape, f"Shape mismatch: {src.shape} vs {dst.shape}"
+    if not _require_cuda(src, "copy_block"):
+        return
+    if not (src.is_contiguous() and dst.is_contiguous()) or src.dtype != dst.dtype:
+        raise ValueError("copy_block: src and dst must be contiguous blocks of one dtype")
+    nbytes = src.numel() * src.element_size()
+    if nbytes == 0:
+        return
+    a, b = src.data_ptr(), dst.data_ptr()
+    base = min(a, b)
+    if (max(a, b) - base) % nbytes != 0:
+        raise ValueError("copy_block: src and dst must be blocks of one pool tensor")
+    pairs = torch.tensor([[(a - base) // nbytes, (b - base) // nbytes]], dtype=torch.int32, device=src.device)
+    total = (max(a, b) - base) // nbytes + 1
+    N.check(
+        N.lib.akv_copy_blocks(base, nbytes, total, pairs.data_ptr(), 1, None, None, stream_handle(src.device))
+    )
+
+
+def zero_block(block: torch.Tensor) -> None:
+    """Zero one KV block with +0.0 (triton_kernels.py:206-229)."""
+    if not _require_cuda(block, "zero_block"):
+        return
+    if not block.is_contiguous():
+        raise ValueError("zero_block: block must be contiguous")
+    nbytes = block.numel() * block.element_size()
+    if nbytes == 0:
+        return
+    ids = torch.zeros(1, dtype=torch.int32, device=block.device)
+    N.check(N.lib.akv_zero_blocks(block.data_ptr(), nbytes, 1, ids.data_ptr(), 1, None, None,
+                                  stream_handle(block.device)))
+
+
+# ── batched block movement ───────────────────────────────────────────────────
+def _pool_geometry(pool: torch.Tensor) -> tuple:
+    if pool.dim() < 1 or not pool.is_contiguous():
+        raise ValueError("pool must be a contiguous tensor whose first dim indexes blocks")
+    total = pool.shape[0]
+    bpb = (pool.numel() // max(total, 1)) * pool.element_size()
+    return total, bpb
+
+
+def _as_device_i32(x, device: torch.device) -> torch.Tensor:
+    if isinstance(x, torch.Tensor):
+        if x.dtype != torch.int32:
+            x = x.to(torch.int32)
+        if x.device != device:
+            x = x.to(device, non_blocking=True)
+        return x.contiguous()
+    return torch.as_tensor(x, dtype=torch.int32).to(device, non_blocking=True)
+
+
+def copy_blocks(
+    pool: torch.Tensor,
+    pairs,
+    *,
+    ref_counts: Optional[torch.Tensor] = None,
+    status: Optional[torch.Tensor] = None,
+    variant: int = N.VARIANT_AUTO,
+    check: bool = False,
+    validate: bool = False,
+) -> None:
+    """Copy a batch of (src, dst) block pairs of `pool` in one launch.
+
+    The pairs must be independent (no dst repeated, no dst used as another
+    pair's src); `validate=True` checks that on the host before launching.
+    With `ref_counts` every dst must have refcount 1.  Device-detected errors
+    land in `status` (a per-device buffer by default) and raise on `check=True`
+    (which synchronises).
+    """
+    if not _require_cuda(pool, "copy_blocks"):
+        return
+    total, bpb = _pool_geometry(pool)
+    pairs_t = _as_device_i32(pairs, pool.device).reshape(-1, 2)
+    n = pairs_t.shape[0]
+    if n == 0:
+        return
+    if validate:
+        validate_pairs(pairs_t.cpu().numpy(), total)
+    st = status if status is not None else _status_buffer(pool.device)
+    N.check(
+        N.lib.akv_copy_blocks_variant(
+            pool.data_ptr(), bpb, total, pairs_t.data_ptr(), n,
+            ref_counts.data_ptr() if ref_counts is not None else None, st.data_ptr(), int(variant),
+            stream_handle(pool.device),
+        )
+    )
+    if check:
+        raise_for_status(st)
+
+
+def zero_blocks(
+    pool: torch.Tensor,
+    ids,
+    *,
+    ref_counts: Optional[torch.Tensor] = None,
+    status: Optional[torch.Tensor] = None,
+    variant: int = N.VARIANT_AUTO,
+    check: bool = False,
+) -> None:
+    """Write +0.0 over a batch of blocks of `pool` in one launch."""
+    if not _require_cuda(pool, "zero_blocks"):
+        return
+    total, bpb = _pool_geometry(pool)
+    ids_t = _as_device_i32(ids, pool.device).reshape(-1)
+    n = ids_t.shape[0]
+    if n == 0:
+        return
+    st = status if status is not None else _status_buffer(pool.device)
+    N.check(
+        N.lib.akv_zero_blocks_variant(
+            pool.data_ptr(), bpb, total, ids_t.data_ptr(), n,
+            ref_counts.data_ptr() if ref_counts is not None else None, st.data_ptr(), int(variant),
+            stream_handle(pool.device),
+        )
+    )
+    if check:
+        raise_for_status(st)
+
+
+def check_pairs_on_device(pairs: torch.Tensor, total_blocks: int, mark: torch.Tensor,
+                          status: torch.Tensor) -> None:
+    """Enqueue the device-side independence check (akv_check_pairs)."""
+    pairs = pairs.reshape(-1, 2)
+    N.check(N.lib.akv_check_pairs(pairs.data_ptr(), pairs.shape[0], total_blocks, mark.data_ptr(),
+                                  status.data_ptr(), stream_handle(pairs.device)))
+
+
+def validate_pairs(pairs, total_blocks: int) -> None:
+    """Host check that a pair batch is in range and independent."""
+    import numpy as np
+
+    p = np.asarray(pairs, dtype=np.int64).reshape(-1, 2)
+    if p.size == 0:
+        return
+    if p.min() < 0 or p.max() >= total_blocks:
+        raise ValueError(f"copy_blocks: block id out of range [0, {total_blocks})")
+    src, dst = p[:, 0], p[:, 1]
+    if len(np.unique(dst)) != len(dst):
+        raise ValueError("copy_blocks: a dst block appears twice in the batch")
+    moving = src != dst
+    if np.intersect1d(src[moving], dst).size:
+        raise ValueError("copy_blocks: a dst block is also read as another pair's src")
+
+
+def is_native_available() -> bool:
+    return N.LIB_PATH.exists() and torch.cuda.is_available()
+
+
+def kernel_info() -> dict:
+    gpu = torch.cuda.get_device_name(0) if torch.cuda.is_available() else "N/A"
+    cap = torch.cuda.get_device_capability(0) if torch.cuda.is_available() else None
+    major, minor = N.version()
+    return {
+        "library": str(N.LIB_PATH),
+        "library_version": f"{major}.{minor}",
+        "cuda_available": torch.cuda.is_available(),
+        "gpu_name": gpu,
+        "gpu_arch": f"sm_{cap[0]}{cap[1]}" if cap else "cpu",
+        "kernels": "sm_100a: vectorised / bulk-async block copy, write-only zero, "
+        "device free list + refcounts, warp-per-query match_prefix",
+        "fallback": None,
+    }

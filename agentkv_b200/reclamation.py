@@ -1,0 +1,79 @@
+"""EpochReclaimer — host side of the two-epoch safe reclamation.
+
+The reference's EpochReclaimer (agentkv/core/reclamation.py:55-190) keeps the
+epoch counter, the set of epochs that hold an open read section, and a FIFO
+of retired block ids that may only return to the free list once no reader
+that could still see them remains.  Here the ids never leave the GPU: the
+retired-id FIFO and the epoch / op counters live in the allocator's device
+state, and this class keeps what only the host knows — the reader set — and
+turns each reclaimer call into one launch:
+
+* ``enter_read_section`` reads the current epoch (the reader's token) and
+  adds it to the set — a set, as in the reference, so two readers of one
+  epoch share one entry;
+* ``leave_read_section`` discards the token and launches the release of every
+  pending id older than the oldest remaining reader (all of them when no
+  reader is left), ``_try_retire`` in the reference (reclamation.py:147-173);
+* ``maybe_advance`` launches the epoch bump (unless a reader holds the current
+  epoch) followed by the same release.
+
+Each allocator batch carries a summary of the reader set (AkvTick) so the
+device applies the reference's rules for ids that retire while readers are
+open.
+"""
+
+from __future__ import annotations
+
+from typing import TYPE_CHECKING, Set
+
+from . import _native as N
+
+if TYPE_CHECKING:  # pragma: no cover
+    from .allocator import SlabAllocator
+
+_INT64_MAX = (1 << 63) - 1
+
+
+class EpochReclaimer:
+    def __init__(self, allocator: "SlabAllocator") -> None:
+        self._alloc = allocator
+        self._active_reader_epochs: Set[int] = set()
+
+    def tick(self, epoch_interval: int) -> N.AkvTick:
+        r = self._active_reader_epochs
+        if r:
+            return N.AkvTick(min(r), max(r), epoch_interval, 1)
+        return N.AkvTick(0, 0, epoch_interval, 0)
+
+    def enter_read_section(self) -> int:
+        a = self._alloc
+        with a._lock:
+            token = int(a.ctl()[N.CTL_EPOCH])
+            self._active_reader_epochs.add(token)
+            return token
+
+    def leave_read_section(self, token: int) -> None:
+        a = self._alloc
+        with a._lock:
+            self._active_reader_epochs.discard(token)
+            safe = min(self._active_reader_epochs) if self._active_reader_epochs else _INT64_MAX
+            N.check(N.lib.akv_limbo_release(a._state, safe, a._stream()))
+
+    def maybe_advance(self) -> None:
+        a = self._alloc
+        with a._lock:
+            N.check(N.lib.akv_epoch_advance(a._state, self.tick(a._cfg.epoch_interval), a._stream()))
+
+    def stats(self) -> dict:
+        c = self._alloc.ctl()
+        return {
+            "epoch": int(c[N.CTL_EPOCH]),
+            "pending_blocks": int(c[N.CTL_LIMBO_TAIL] - c[N.CTL_LIMBO_REL]),
+            "active_readers": len(self._active_reader_epochs),
+            "epoch_advances": int(c[N.CTL_ADVANCES]),
+            "blocks_freed": int(c[N.CTL_RELEASED]),
+        }
+
+    def pending_count(self) -> int:
+        c = self._alloc.ctl()
+        return int(c[N.CTL_LIMBO_TAIL] - c[N.CTL_LIMBO_REL])

@@ -1,0 +1,302 @@
+/*
+ * agentkv_b200.h — C ABI of the B200 block-movement and prefix-lookup path.
+ *
+ * Every entry point takes plain device pointers and sizes, enqueues work on
+ * the caller's CUDA stream (`stream` is a cudaStream_t; NULL means the legacy
+ * default stream) and returns an AKV_* host status.  A host status other than
+ * AKV_OK means nothing was enqueued; `akv_last_error` then describes why.
+ *
+ * Errors that only the device can see (a block id out of range, a refcount
+ * that would go below zero, an exhausted free list, a destination that is not
+ * exclusively owned) are written into an AkvStatus record in device memory
+ * that the caller owns.  The first error sticks: every mutating kernel reads
+ * the record on entry and does nothing while it holds an error, so a failed
+ * batch never half-applies the batches queued behind it.  The caller reads
+ * the record after synchronising the stream and clears it with
+ * cudaMemsetAsync (or akv_status_clear).
+ *
+ * The library allocates no memory on any path: the pool, ids, refcounts,
+ * free list, tree arrays and outputs are all owned by the caller (PyTorch
+ * tensors in the Python package).  Functions keep no mutable host state
+ * except a thread-local last-error string, so they are reentrant.
+ *
+ * Reference interfaces each group replaces are cited by file:line within the
+ * agentkv project.
+ */
+#ifndef AGENTKV_B200_H
+#define AGENTKV_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AKV_API __attribute__((visibility("default")))
+#else
+#define AKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ── status codes ───────────────────────────────────────────────────────── */
+enum {
+  AKV_OK = 0,
+  AKV_ERR_INVALID_ARG = 1,     /* bad pointer / size / alignment (host) */
+  AKV_ERR_OUT_OF_RANGE = 2,    /* block id outside [0, total_blocks) */
+  AKV_ERR_EXHAUSTED = 3,       /* free list has fewer ids than requested */
+  AKV_ERR_DOUBLE_FREE = 4,     /* dec_ref of a block whose ref_count <= 0 */
+  AKV_ERR_NOT_ALLOCATED = 5,   /* inc_ref of a block whose ref_count <= 0 */
+  AKV_ERR_NOT_EXCLUSIVE = 6,   /* copy/zero destination with ref_count != 1 */
+  AKV_ERR_DEPENDENT_PAIRS = 7, /* a batch's dst is another pair's src/dst */
+  AKV_ERR_CUDA = 8,            /* a CUDA runtime call failed (host) */
+  AKV_ERR_TIMEOUT = 9,         /* a bounded device wait gave up */
+  AKV_ERR_TREE = 10            /* malformed tree replica (bad node index) */
+};
+
+/* Device-side status record (32 bytes).  code = first AKV_ERR_* seen,
+ * index = batch position of the offending element, id = offending block id
+ * (or node id), observed = the refcount (or other value) that failed the
+ * check, aux = extra detail (e.g. the iteration count of a timed-out wait). */
+typedef struct AkvStatus {
+  int32_t code;
+  int32_t index;
+  int32_t id;
+  int32_t observed;
+  int64_t aux;
+  int64_t _reserved;
+} AkvStatus;
+
+/* ── library ────────────────────────────────────────────────────────────── */
+AKV_API int akv_version(void);                     /* (major << 16) | minor */
+AKV_API int akv_last_error(char* buf, int len);    /* copies the thread's last message */
+AKV_API int akv_status_clear(AkvStatus* status, void* stream);
+
+/* ── block movement ─────────────────────────────────────────────────────────
+ * The pool is the reference's `_kv_data` tensor
+ * [total_blocks, L, 2, H_kv, block_size, D] (agentkv/core/slab_allocator.py:155-164)
+ * seen as total_blocks contiguous spans of bytes_per_block bytes
+ * (agentkv/core/config.py:95-98).
+ *
+ * akv_copy_blocks replaces triton_kernels.copy_block / _copy_block_kernel
+ * (agentkv/core/triton_kernels.py:171-203, :107-132), which moves ONE block
+ * per launch, with one launch for a batch of (src, dst) pairs.  `pairs` is a
+ * device int32 array [n_pairs][2].  The pairs must be independent: no dst is
+ * repeated and no dst is another pair's src (the batch is applied in
+ * parallel; akv_check_pairs verifies this on the device).  When `ref_counts`
+ * is non-NULL every dst must have ref_count == 1, the check
+ * SlabAllocator.copy_block makes under its lock
+ * (agentkv/core/slab_allocator.py:307-313); an offending pair is skipped and
+ * reported.
+ */
+AKV_API int akv_copy_blocks(void* pool, int64_t bytes_per_block, int32_t total_blocks,
+                    const int32_t* pairs, int32_t n_pairs,
+                    const int32_t* ref_counts, AkvStatus* status, void* stream);
+
+/* Same, with an explicit kernel choice: 0 = automatic, 1 = 16-byte vector
+ * loads/stores, 2 = bulk-async (TMA) copies staged through shared memory. */
+AKV_API int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int32_t total_blocks,
+                            const int32_t* pairs, int32_t n_pairs,
+                            const int32_t* ref_counts, AkvStatus* status,
+                            int32_t variant, void* stream);
+
+/* akv_zero_blocks replaces triton_kernels.zero_block / _zero_block_kernel
+ * (agentkv/core/triton_kernels.py:206-229, :134-162) and
+ * SlabAllocator.zero_block (agentkv/core/slab_allocator.py:321-334).  It
+ * writes +0.0 (all-zero bits), the result of the reference's CPU path
+ * `block.zero_()`; the reference's Triton path stores `x * 0`, which keeps the
+ * sign of negative inputs and propagates NaN.  Write-only: no read of the
+ * old contents. */
+AKV_API int akv_zero_blocks(void* pool, int64_t bytes_per_block, int32_t total_blocks,
+                    const int32_t* ids, int32_t n, const int32_t* ref_counts,
+                    AkvStatus* status, void* stream);
+
+AKV_API int akv_zero_blocks_variant(void* pool, int64_t bytes_per_block, int32_t total_blocks,
+                            const int32_t* ids, int32_t n, const int32_t* ref_counts,
+                            AkvStatus* status, int32_t variant, void* stream);
+
+/* Verify on the device that a pair batch is independent (see
+ * akv_copy_blocks) and in range; sets AKV_ERR_DEPENDENT_PAIRS /
+ * AKV_ERR_OUT_OF_RANGE.  `mark` is caller-owned scratch of total_blocks
+ * int32 that must be all zero on entry; it is all zero again on return. */
+AKV_API int akv_check_pairs(const int32_t* pairs, int32_t n_pairs, int32_t total_blocks,
+                    int32_t* mark, AkvStatus* status, void* stream);
+
+/* ── slab allocator: device free list and refcounts ─────────────────────────
+ * Replaces SlabAllocator.alloc / inc_ref / dec_ref / _do_free /
+ * _drain_deferred / _tick (agentkv/core/slab_allocator.py:194-278, 387-437)
+ * and the id-moving half of EpochReclaimer (agentkv/core/reclamation.py:
+ * 114-173).  All state lives in caller-owned device arrays:
+ *
+ *   ref_counts[N]     int32 — the reference's `_ref_counts`
+ *   free_ring[N]      int32 — the `_free_list` deque as a ring; initially
+ *                     0..N-1, pops from the right, recycled ids pushed left
+ *   limbo_ids[N]      int32 — retired ids not yet on the free list, FIFO with
+ *                     monotonic cursors head <= rel <= tail: [head, rel) is
+ *                     the reference's `_deferred_free`, [rel, tail) the
+ *                     reclaimer's `_pending` queue
+ *   limbo_epochs[N]   int64 — epoch each pending id retired in
+ *   ctl[AKV_CTL_WORDS] int64 — cursors and counters, see AKV_CTL_*
+ *   scratch_count[N], scratch_last[N] int32 — per-id work space; all zero
+ *                     on entry and again on return of every call
+ *   scratch_aux[AKV_AUX_WORDS] int32 — per-launch work space
+ *
+ * Batches follow the reference's sequential semantics op by op: ids come
+ * off the free list in the order repeated alloc() calls return them, and
+ * retired ids reach the free list in the order repeated dec_ref() calls put
+ * them there, including the deferred-drain and epoch rules.  The op counter
+ * and the epoch are device counters; the host describes its reader set in
+ * AkvTick.  A batch is validated as a whole before anything is mutated.
+ * Calls on one allocator state must be ordered on one stream.
+ */
+enum {
+  AKV_CTL_FREE_LEFT = 0,    /* ring index of the leftmost free id */
+  AKV_CTL_FREE_SIZE = 1,    /* number of free ids (len(_free_list)) */
+  AKV_CTL_LIMBO_HEAD = 2,   /* limbo cursors (monotonic, index mod N) */
+  AKV_CTL_LIMBO_REL = 3,
+  AKV_CTL_LIMBO_TAIL = 4,
+  AKV_CTL_OPS = 5,          /* SlabAllocator._op_count */
+  AKV_CTL_EPOCH = 6,        /* EpochReclaimer._epoch */
+  AKV_CTL_ALLOCS = 7,       /* _alloc_count */
+  AKV_CTL_FREES = 8,        /* _free_count (blocks retired) */
+  AKV_CTL_PEAK = 9,         /* _peak_allocated */
+  AKV_CTL_LAST_RETIRED = 10,/* ids retired by the last dec_ref batch */
+  AKV_CTL_LAST_COPIED = 11, /* copies made by the last CoW batch chunk */
+  AKV_CTL_DONE = 12,        /* internal CTA completion counter */
+  AKV_CTL_ADVANCES = 13,    /* EpochReclaimer._advance_count */
+  AKV_CTL_RELEASED = 14,    /* EpochReclaimer._freed_count */
+  AKV_CTL_WORDS = 16
+};
+
+#define AKV_AUX_PLAN_OFFSET 1024
+#define AKV_AUX_WORDS 2048
+
+typedef struct AkvAllocState {
+  int32_t* ref_counts;
+  int32_t* free_ring;
+  int32_t* limbo_ids;
+  int64_t* limbo_epochs;
+  int64_t* ctl;
+  int32_t* scratch_count;
+  int32_t* scratch_last;
+  int32_t* scratch_aux;
+  int32_t total_blocks;
+  int32_t _pad;
+} AkvAllocState;
+
+/* The host's reader set when the batch starts (EpochReclaimer's
+ * `_active_reader_epochs`, reclamation.py:79) and PoolConfig.epoch_interval
+ * (agentkv/core/config.py:62), which must be > 0. */
+typedef struct AkvTick {
+  int64_t readers_min;    /* smallest epoch holding a reader */
+  int64_t readers_max;    /* largest epoch holding a reader */
+  int32_t epoch_interval;
+  int32_t readers_active; /* 0: no read section open */
+} AkvTick;
+
+/* Reset to the constructor state: refcounts 0, free ring 0..N-1, limbo empty,
+ * counters 0, scratch zeroed. */
+AKV_API int akv_alloc_init(const AkvAllocState* st, void* stream);
+
+/* n alloc() calls: out_ids[k] receives the k-th id, its refcount set to 1.
+ * AKV_ERR_EXHAUSTED (nothing mutated) if the calls would run dry. */
+AKV_API int akv_alloc_batch(const AkvAllocState* st, int32_t n, int32_t* out_ids,
+                    const AkvTick* tick, AkvStatus* status, void* stream);
+
+/* n inc_ref() calls (ids may repeat).  AKV_ERR_NOT_ALLOCATED if any id has
+ * ref_count <= 0 on entry. */
+AKV_API int akv_incref_batch(const AkvAllocState* st, const int32_t* ids, int32_t n,
+                     const AkvTick* tick, AkvStatus* status, void* stream);
+
+/* n dec_ref() calls (ids may repeat).  AKV_ERR_DOUBLE_FREE if an id would go
+ * below zero.  Ids reaching zero retire at the position of their last
+ * occurrence; `retired_out` (optional, n entries) receives them in
+ * retirement order and ctl[AKV_CTL_LAST_RETIRED] their count. */
+AKV_API int akv_decref_batch(const AkvAllocState* st, const int32_t* ids, int32_t n,
+                     const AkvTick* tick, int32_t* retired_out,
+                     AkvStatus* status, void* stream);
+
+/* EpochReclaimer._try_retire (reclamation.py:147-173): release every pending
+ * id whose epoch is < safe_before_epoch, in FIFO order (INT64_MAX releases
+ * all).  Released ids join the free list at the next allocator op. */
+AKV_API int akv_limbo_release(const AkvAllocState* st, int64_t safe_before_epoch, void* stream);
+
+/* EpochReclaimer.maybe_advance (reclamation.py:129-143): bump the epoch unless
+ * a reader holds it, then try_retire. */
+AKV_API int akv_epoch_advance(const AkvAllocState* st, const AkvTick* tick, void* stream);
+
+/* CoW of a batch of residual blocks — DualRadixTree.ensure_mutable_block
+ * (agentkv/core/radix_tree.py:286-314) for n requests on distinct
+ * (handle, index) slots whose current block ids are `blocks[n]`, applied in
+ * request order: a request copies iff its block's refcount is > 1 at that
+ * point; it then allocates a fresh id, copies the block into it and dec_refs
+ * the old one.  out_blocks[i] receives the block request i ends up owning
+ * (the fresh id, or blocks[i] when no copy was needed); out_copied[i] is 1
+ * when a copy happened.  `pairs_scratch` (int32 [n][2], caller-owned)
+ * receives the (src, dst) pairs.  With pool == NULL (a metadata-only pool)
+ * nothing is copied. */
+AKV_API int akv_cow_batch(const AkvAllocState* st, void* pool, int64_t bytes_per_block,
+                  const int32_t* blocks, int32_t n, int32_t* out_blocks,
+                  int32_t* out_copied, int32_t* pairs_scratch,
+                  const AkvTick* tick, AkvStatus* status, void* stream);
+
+/* One fork level on device-resident block tables (a Tree-of-Thought level):
+ * each of n_parents parents (residual tables concatenated in parent_tables,
+ * offsets parent_off[n_parents + 1], every table non-empty) is forked
+ * `fanout` times and each child copy-on-writes its last inherited block and
+ * appends `append` blocks — per child, the reference's fork()
+ * (agentkv/core/radix_tree.py:222-264), ensure_mutable_block(child, -1)
+ * (:286-314) and `append` allocate_block() calls (:266-284).  `fresh_ids`
+ * holds the (1 + append) * fanout * n_parents ids of one akv_alloc_batch.
+ * Writes the children's tables (child_tables, child_off[n_children + 1]),
+ * the fork's inc_ref list (inc_ids: every parent block once per child), the
+ * CoW pairs (pairs [n_children][2]) and the CoW dec_ref list (dec_ids), which
+ * akv_incref_batch, akv_copy_blocks and akv_decref_batch then apply. */
+AKV_API int akv_fanout_plan(const int32_t* parent_tables, const int64_t* parent_off,
+                            int32_t n_parents, int32_t fanout, int32_t append,
+                            const int32_t* fresh_ids, int32_t* child_tables, int64_t* child_off,
+                            int32_t* inc_ids, int32_t* pairs, int32_t* dec_ids, void* stream);
+
+/* ── shared radix tree: device replica and match_prefix ─────────────────────
+ * Replaces DualRadixTree._match_prefix_locked (agentkv/core/radix_tree.py:
+ * 513-570), reached from create_root (:203) and match_prefix (:379-416).
+ * The replica mirrors the host tree's SharedNode table (:82-103):
+ *   node_edge_off[cap] int64 — start of the node's edge in `tokens`
+ *   node_edge_len[cap] int32 — edge length (0 for the root / unused ids)
+ *   slots[mask+1]      int32x4 {parent, first_token, child, 0} — the
+ *                      `children` dicts of all nodes as one open-addressing
+ *                      hash table; parent = -1 empty, -2 deleted
+ * Node ids are the tree's own ids (root = 0).
+ */
+typedef struct AkvTreeView {
+  const int32_t* tokens;
+  const int64_t* node_edge_off;
+  const int32_t* node_edge_len;
+  const int32_t* slots;
+  int64_t n_tokens;
+  int32_t n_nodes;     /* capacity of the node arrays */
+  int32_t slot_mask;   /* number of slots - 1, a power of two minus one */
+} AkvTreeView;
+
+/* Hash of (parent, first_token) into the slot table; the host builder and
+ * the device lookup both use this function. */
+AKV_API uint32_t akv_tree_hash(int32_t parent, int32_t token);
+
+/* Apply a batch of replica updates: slot_updates int32 [n_slot][4]
+ * {slot, parent, first_token, child}; node_updates int64 [n_node][3]
+ * {node, edge_off, edge_len}.  (Token arena appends are plain copies.) */
+AKV_API int akv_tree_apply(const AkvTreeView* tree, const int32_t* slot_updates, int32_t n_slot,
+                   const int64_t* node_updates, int32_t n_node,
+                   AkvStatus* status, void* stream);
+
+/* One warp per query.  Query q is tokens[q_off[q] .. q_off[q+1]).  Writes
+ * the reference's (node_id, match_len) — (-1, 0) when nothing matched — and
+ * the number of token comparisons the reference loop performs. */
+AKV_API int akv_match_prefix(const AkvTreeView* tree, const int32_t* tokens, const int64_t* q_off,
+                     int32_t nq, int32_t block_size, int32_t* out_node, int32_t* out_len,
+                     int64_t* out_compared, AkvStatus* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AGENTKV_B200_H */

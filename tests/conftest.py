@@ -1,0 +1,47 @@
+"""Shared pytest configuration.
+
+Markers:
+    gpu  — needs a CUDA device (a B200 for the sm_100a library); run with
+           `pytest -m gpu`.  Skipped automatically when no GPU is visible.
+    slow — longer parity cases (full-size workloads).
+"""
+
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+GOLDEN = REPO / "tests" / "golden"
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: test needs a CUDA GPU (sm_100a)")
+    config.addinivalue_line("markers", "slow: longer parity case")
+
+
+def _cuda_available() -> bool:
+    try:
+        import torch
+
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+def pytest_collection_modifyitems(config, items):
+    if _cuda_available():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device visible")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)
+
+
+@pytest.fixture(scope="session")
+def golden_dir() -> Path:
+    return GOLDEN

@@ -1,0 +1,475 @@
+"""Generate golden fixtures by running the reference AgentKV implementation.
+
+Run in a container that has the reference checked out (read-only) at
+/root/reference:
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [--skip-full-match]
+
+It imports the reference's own `agentkv` package and records, for seeded
+inputs, what the reference's code returns: allocator op traces (ids,
+refcounts, free-list order, reclaimer queues, counters), tree op traces
+(block tables, tree structure, match results), the quickstart and
+Tree-of-Thought workloads, copy/zero contents and match_prefix results on
+the stress tree.  The fixtures are what the oracle and the CUDA path are
+pinned against; nothing at test time reads the reference.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import random
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+REF = Path("/root/reference")
+OUT = Path(__file__).resolve().parent
+REPO = OUT.parent.parent
+sys.path.insert(0, str(REF))
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+from agentkv.core.config import PoolConfig  # noqa: E402
+from agentkv.core.slab_allocator import SlabAllocator, BlockHandle  # noqa: E402
+from agentkv.core.radix_tree import DualRadixTree, INVALID_NODE_ID  # noqa: E402
+from agentkv.pool import AgentKVPool  # noqa: E402
+
+from agentkv_b200 import workloads as W  # noqa: E402  (seeded generators only)
+
+# opcodes shared with the replaying tests
+A_ALLOC, A_INC, A_DEC, A_ENTER, A_LEAVE, A_ADVANCE = range(6)
+ERR_EXHAUSTED, ERR_DOUBLE_FREE, ERR_NOT_ALLOCATED = 3, 4, 5
+
+
+def alloc_snapshot(a: SlabAllocator) -> dict:
+    r = a._reclaimer
+    return {
+        "ref": a._ref_counts.numpy().astype(np.int32).copy(),
+        "free": np.asarray(list(a._free_list), np.int32),
+        "pend_ids": np.asarray([b for _, b in r._pending], np.int32),
+        "pend_eps": np.asarray([e for e, _ in r._pending], np.int64),
+        "deferred": np.asarray(list(a._deferred_free), np.int32),
+        "ctl": np.asarray(
+            [a._op_count, r._epoch, a._alloc_count, a._free_count, a._peak_allocated,
+             r._advance_count, r._freed_count, len(a._free_list),
+             int((a._ref_counts > 0).sum())], np.int64),
+    }
+
+
+# ── A. allocator traces ──────────────────────────────────────────────────────
+def alloc_trace(seed: int, n_blocks: int, interval: int, n_ops: int) -> dict:
+    cfg = PoolConfig(total_blocks=n_blocks, block_size=4, num_layers=1, num_kv_heads=1,
+                     head_dim=4, dtype="float16", device="meta", epoch_interval=interval)
+    a = SlabAllocator(cfg)
+    rng = random.Random(seed)
+    tokens_open: list[int] = []
+    ops, args, results = [], [], []
+    snaps = []
+    burst = 0
+    for _ in range(n_ops):
+        live = [i for i in range(n_blocks) if int(a._ref_counts[i]) > 0]
+        r = rng.random()
+        if burst > 0:
+            op = A_ALLOC
+            burst -= 1
+        elif r < 0.28:
+            op = A_ALLOC
+        elif r < 0.30:
+            op, burst = A_ALLOC, rng.randint(5, 20)
+        elif r < 0.45:
+            op = A_INC
+        elif r < 0.78:
+            op = A_DEC
+        elif r < 0.85:
+            op = A_ENTER
+        elif r < 0.92:
+            op = A_LEAVE
+        else:
+            op = A_ADVANCE
+        arg = 0
+        if op == A_ALLOC:
+            try:
+                res = a.alloc().block_id
+            except MemoryError:
+                res = -ERR_EXHAUSTED
+        elif op in (A_INC, A_DEC):
+            if live and rng.random() < 0.93:
+                arg = rng.choice(live)
+            else:
+                arg = rng.randrange(n_blocks)
+            try:
+                if op == A_INC:
+                    a.inc_ref(BlockHandle(arg))
+                    res = 0
+                else:
+                    res = 1 if a.dec_ref(BlockHandle(arg)) else 0
+            except ValueError:
+                res = -(ERR_NOT_ALLOCATED if op == A_INC else ERR_DOUBLE_FREE)
+        elif op == A_ENTER:
+            res = a.enter_read_section()
+            tokens_open.append(res)
+        elif op == A_LEAVE:
+            if tokens_open:
+                arg = tokens_open.pop(rng.randrange(len(tokens_open)))
+                a.leave_read_section(arg)
+                res = 0
+            else:
+                op, res = A_ADVANCE, 0
+                a.maybe_advance_epoch()
+        else:
+            a.maybe_advance_epoch()
+            res = 0
+        ops.append(op)
+        args.append(arg)
+        results.append(res)
+        snaps.append(alloc_snapshot(a))
+    out = {
+        "n_blocks": np.int64(n_blocks), "interval": np.int64(interval),
+        "ops": np.asarray(ops, np.int32), "args": np.asarray(args, np.int64),
+        "results": np.asarray(results, np.int64),
+        "ref": np.stack([s["ref"] for s in snaps]),
+        "ctl": np.stack([s["ctl"] for s in snaps]),
+    }
+    # ragged arrays: concatenated with offsets
+    for key in ("free", "pend_ids", "pend_eps", "deferred"):
+        vals = [s[key] for s in snaps]
+        off = np.zeros(len(vals) + 1, np.int64)
+        np.cumsum([len(v) for v in vals], out=off[1:])
+        out[key] = np.concatenate(vals) if off[-1] else np.zeros(0, vals[0].dtype)
+        out[key + "_off"] = off
+    return out
+
+
+# ── B. tree traces ───────────────────────────────────────────────────────────
+T_CREATE, T_FORK, T_ALLOC, T_COW, T_APPEND, T_COMMIT, T_FREE, T_MATCH, T_ADVANCE, T_ZERO = range(10)
+
+
+def tree_state(pool: AgentKVPool, live: dict) -> dict:
+    tree, a = pool._tree, pool._allocator
+    nodes = {}
+    for nid, n in sorted(tree._shared_nodes.items()):
+        nodes[str(nid)] = {
+            "parent": n.parent_id, "edge": list(n.edge_tokens), "blocks": [b.block_id for b in n.blocks],
+            "children": sorted([int(k), int(v)] for k, v in n.children.items()), "ref": n.ref_count,
+        }
+    return {
+        "tables": {str(h): tree.get_block_ids(hd) for h, hd in sorted(live.items())},
+        "shared": {str(h): [hd.shared_node_id, hd.shared_match_len] for h, hd in sorted(live.items())},
+        "nodes": nodes,
+        "ref": a._ref_counts.tolist(),
+        "free": list(a._free_list),
+        "stats": pool.stats(),
+    }
+
+
+def tree_trace(seed: int, n_ops: int, n_blocks: int = 96, bs: int = 4) -> dict:
+    cfg = PoolConfig(total_blocks=n_blocks, block_size=bs, num_layers=1, num_kv_heads=2,
+                     head_dim=4, dtype="float16", device="cpu", epoch_interval=7)
+    pool = AgentKVPool(config=cfg)
+    torch.manual_seed(seed)
+    pool._allocator._kv_data.copy_(torch.randn_like(pool._allocator._kv_data, dtype=torch.float32).half())
+    rng = random.Random(seed)
+    bases = [[rng.randrange(6) for _ in range(40)] for _ in range(4)]
+
+    def gen_tokens():
+        b = rng.choice(bases)
+        cut = rng.randint(0, 40)
+        tail = [rng.randrange(6) for _ in range(rng.randint(0, 14))]
+        return b[:cut] + tail
+
+    live: dict = {}
+    ops, states = [], []
+    for step in range(n_ops):
+        hs = sorted(live)
+        r = rng.random()
+        op = (T_CREATE if (not hs or r < 0.16) else T_FORK if r < 0.28 else T_ALLOC if r < 0.46
+              else T_COW if r < 0.56 else T_APPEND if r < 0.62 else T_COMMIT if r < 0.76
+              else T_FREE if r < 0.86 else T_MATCH if r < 0.95 else T_ADVANCE if r < 0.98 else T_ZERO)
+        rec = {"op": op}
+        try:
+            if op == T_CREATE:
+                toks = gen_tokens()
+                h = pool.create_root(toks)
+                live[h.handle_id] = h
+                rec.update(tokens=toks, out=[h.handle_id, h.shared_node_id, h.shared_match_len])
+            elif op == T_FORK:
+                p = live[rng.choice(hs)]
+                c = pool.fork(p)
+                live[c.handle_id] = c
+                rec.update(h=p.handle_id, out=c.handle_id)
+            elif op == T_ALLOC:
+                h = live[rng.choice(hs)]
+                pool.allocate_block(h)
+                rec.update(h=h.handle_id, out=h.residual_blocks[-1].block_id)
+            elif op == T_COW:
+                h = live[rng.choice(hs)]
+                if not h.residual_blocks:
+                    rec.update(op=T_ADVANCE)
+                    pool.maybe_advance_epoch()
+                else:
+                    idx = rng.randrange(len(h.residual_blocks))
+                    pool.ensure_mutable_block(h, idx)
+                    rec.update(h=h.handle_id, idx=idx, out=h.residual_blocks[idx].block_id)
+            elif op == T_APPEND:
+                h = live[rng.choice(hs)]
+                toks = [rng.randrange(6) for _ in range(rng.randint(0, 9))]
+                pool.append_tokens(h, toks)
+                rec.update(h=h.handle_id, tokens=toks)
+            elif op == T_COMMIT:
+                h = live[rng.choice(hs)]
+                k = rng.randint(0, len(h.residual_blocks) + 1)
+                length = k * bs if rng.random() < 0.9 else k * bs + 1
+                rec.update(h=h.handle_id, length=length)
+                pool.commit_prefix(h, length)
+                rec.update(out=[h.shared_node_id, h.shared_match_len])
+            elif op == T_FREE:
+                h = live.pop(rng.choice(hs))
+                pool.free(h)
+                rec.update(h=h.handle_id)
+            elif op == T_MATCH:
+                toks = gen_tokens()
+                mh, mlen = pool._tree.match_prefix(toks)
+                rec.update(tokens=toks, out=[-1 if mh is None else mh.handle_id, mlen,
+                                              INVALID_NODE_ID if mh is None else mh.shared_node_id])
+                if mh is not None:
+                    live[mh.handle_id] = mh
+            elif op == T_ADVANCE:
+                pool.maybe_advance_epoch()
+            elif op == T_ZERO:
+                h = live[rng.choice(hs)]
+                if h.residual_blocks:
+                    b = rng.choice(h.residual_blocks)
+                    rec.update(h=h.handle_id, block=b.block_id)
+                    pool._allocator.zero_block(b)
+                else:
+                    rec.update(op=T_ADVANCE)
+                    pool.maybe_advance_epoch()
+        except (ValueError, MemoryError) as e:
+            rec["error"] = type(e).__name__
+        ops.append(rec)
+        if step % 10 == 9 or step == n_ops - 1:
+            states.append([step, tree_state(pool, live)])
+    digests = [hashlib.sha256(pool._allocator._kv_data[i].numpy().tobytes()).hexdigest()
+               for i in range(n_blocks)]
+    return {"seed": seed, "n_blocks": n_blocks, "block_size": bs, "ops": ops, "states": states,
+            "block_sha256": digests}
+
+
+# ── C. quickstart ────────────────────────────────────────────────────────────
+def quickstart() -> dict:
+    N, bs, L, H, D, dt = W.QUICKSTART_GEOMETRY
+    cfg = PoolConfig(total_blocks=N, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D,
+                     dtype=dt, device="cpu")
+    pool = AgentKVPool(config=cfg)
+    torch.manual_seed(0)
+    pool._allocator._kv_data.copy_(torch.randn(pool._allocator._kv_data.shape, dtype=torch.float16))
+    pairs = []
+    orig = pool._allocator.copy_block
+
+    def rec_copy(src, dst):
+        pairs.append([src.block_id, dst.block_id])
+        orig(src, dst)
+
+    pool._allocator.copy_block = rec_copy
+    root = pool.create_root(list(range(32)))
+    pool.allocate_block(root)
+    kids = [pool.fork(root) for _ in range(3)]
+    for c in kids:
+        pool.allocate_block(c)
+    for c in kids:
+        pool.ensure_mutable_block(c, 0)
+    pool.commit_prefix(root, 16)
+    matches = []
+    for q in W.quickstart_queries():
+        mh, mlen = pool._tree.match_prefix(q)
+        matches.append([-1 if mh is None else mh.shared_node_id, mlen])
+    kv = pool._allocator._kv_data
+    return {
+        "children": [pool.get_block_ids(c) for c in kids],
+        "root": pool.get_block_ids(root),
+        "pairs": pairs,
+        "ref": pool._allocator._ref_counts.tolist(),
+        "free": list(pool._allocator._free_list),
+        "matches": matches,
+        "queries": W.quickstart_queries(),
+        "stats": pool.stats(),
+        "block_sha256": [hashlib.sha256(kv[i].numpy().tobytes()).hexdigest() for i in range(N)],
+    }
+
+
+# ── D. Tree-of-Thought fan-out (metadata, full 60,000-block pool) ────────────
+def tot() -> dict:
+    N, bs, L, H, D, dt = W.LLAMA3_8B_GEOMETRY
+    spec = W.ToTSpec()
+    cfg = PoolConfig(total_blocks=N, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D,
+                     dtype=dt, device="meta")
+    pool = AgentKVPool(config=cfg)
+    pairs = []
+    orig = pool._allocator.copy_block
+
+    def rec_copy(src, dst):
+        pairs.append((src.block_id, dst.block_id))
+        orig(src, dst)
+
+    pool._allocator.copy_block = rec_copy
+    root = pool.create_root(W.tot_root_tokens(spec))
+    for _ in range(spec.root_tokens // bs):
+        pool.allocate_block(root)
+    level = [root]
+    kids_all = []
+    level_pairs = []
+    for lvl in range(spec.levels):
+        nxt = []
+        p0 = len(pairs)
+        for pi, parent in enumerate(level):
+            for k in range(spec.fanout):
+                c = pool.fork(parent)
+                pool.ensure_mutable_block(c, len(c.residual_blocks) - 1)
+                pool.append_tokens(c, W.tot_append_tokens(spec, lvl, pi * spec.fanout + k))
+                for _ in range(spec.appended_blocks):
+                    pool.allocate_block(c)
+                nxt.append(c)
+        level_pairs.append(np.asarray(pairs[p0:], np.int32))
+        kids_all.extend(nxt)
+        level = nxt
+    a = pool._allocator
+    after_fanout = {
+        "tables": [np.asarray(pool.get_block_ids(c), np.int32) for c in kids_all],
+        "ref": a._ref_counts.numpy().astype(np.int32).copy(),
+        "free": np.asarray(list(a._free_list), np.int32),
+        "stats": pool.stats(),
+    }
+    for c in kids_all:
+        pool.free(c)
+    after_free = {
+        "ref": a._ref_counts.numpy().astype(np.int32).copy(),
+        "free": np.asarray(list(a._free_list), np.int32),
+        "stats": pool.stats(),
+    }
+    tables = after_fanout["tables"]
+    t_off = np.zeros(len(tables) + 1, np.int64)
+    np.cumsum([len(t) for t in tables], out=t_off[1:])
+    return {
+        "root_table": np.asarray(pool.get_block_ids(root), np.int32),
+        "tables": np.concatenate(tables), "tables_off": t_off,
+        "pairs_l0": level_pairs[0], "pairs_l1": level_pairs[1], "pairs_l2": level_pairs[2],
+        "ref_fanout": after_fanout["ref"], "free_fanout": after_fanout["free"],
+        "ref_freed": after_free["ref"], "free_freed": after_free["free"],
+        "stats_fanout": np.asarray(json.dumps(after_fanout["stats"])),
+        "stats_freed": np.asarray(json.dumps(after_free["stats"])),
+    }
+
+
+# ── E. copy / zero contents on the CPU path ──────────────────────────────────
+def copy_zero() -> dict:
+    cfg = PoolConfig(total_blocks=32, block_size=4, num_layers=2, num_kv_heads=2, head_dim=8,
+                     dtype="bfloat16", device="cpu")
+    a = SlabAllocator(cfg)
+    torch.manual_seed(11)
+    a._kv_data.copy_(torch.randn(a._kv_data.shape, dtype=torch.float32).to(torch.bfloat16))
+    a._kv_data[3].fill_(-1.5)  # negative values: CPU zero gives +0.0, Triton x*0 gives -0.0
+    a._kv_data[4].fill_(float("nan"))
+    handles = [a.alloc() for _ in range(32)]  # ids 31..0
+    by_id = {h.block_id: h for h in handles}
+    rng = random.Random(12)
+    ops = []
+    for _ in range(40):
+        if rng.random() < 0.6:
+            s, d = rng.sample(range(32), 2)
+            a.copy_block(by_id[s], by_id[d])
+            ops.append(["copy", s, d])
+        else:
+            z = rng.randrange(32)
+            a.zero_block(by_id[z])
+            ops.append(["zero", z])
+    a.zero_block(by_id[3])
+    a.zero_block(by_id[4])
+    ops += [["zero", 3], ["zero", 4]]
+    a.inc_ref(by_id[7])
+    errs = []
+    for fn, args, msg_key in ((a.copy_block, (by_id[1], by_id[7]), "copy"), (a.zero_block, (by_id[7],), "zero")):
+        try:
+            fn(*args)
+        except ValueError as e:
+            errs.append([msg_key, str(e)])
+    kv = a._kv_data
+    return {"ops": ops, "errors": errs,
+            "block_sha256": [hashlib.sha256(kv[i].view(torch.int16).numpy().tobytes()).hexdigest() for i in range(32)],
+            "seed": 11}
+
+
+# ── F. match_prefix on the stress tree ───────────────────────────────────────
+def match_stress(spec: W.MatchSpec, n_queries: int) -> dict:
+    prefixes = W.match_prefixes(spec)
+    corpus = W.match_sequences(spec, prefixes)
+    total_blocks = sum(-(-len(s) // 16) for s in corpus) + 16
+    cfg = PoolConfig(total_blocks=total_blocks, block_size=16, num_layers=1, num_kv_heads=1,
+                     head_dim=1, dtype="float16", device="meta")
+    pool = AgentKVPool(config=cfg)
+    t0 = time.time()
+    for seq in corpus:
+        toks = seq.tolist()
+        h = pool.create_root(toks)
+        need = -(-len(toks) // 16)
+        have = len(pool.get_block_ids(h))
+        for _ in range(need - have):
+            pool.allocate_block(h)
+        share = (len(toks) // 16) * 16 - h.shared_match_len
+        if share > 0:
+            pool.commit_prefix(h, share)
+    t_build = time.time() - t0
+    queries = W.match_queries(spec, corpus, prefixes, batch=0, n=n_queries)
+    t0 = time.time()
+    res = np.asarray([pool._tree._match_prefix_locked(q.tolist()) for q in queries], np.int32)
+    t_match = time.time() - t0
+    return {
+        "node": res[:, 0].copy(), "len": res[:, 1].copy(),
+        "n_nodes": np.int64(len(pool._tree._shared_nodes)),
+        "next_node_id": np.int64(pool._tree._next_node_id),
+        "free_blocks": np.int64(pool.free_blocks),
+        "total_blocks": np.int64(total_blocks),
+        "build_s": np.float64(t_build), "match_s": np.float64(t_match),
+        "spec": np.asarray(json.dumps(spec.__dict__)),
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--skip-full-match", action="store_true")
+    ap.add_argument("--only", default="")
+    args = ap.parse_args()
+    todo = set(args.only.split(",")) if args.only else {"alloc", "tree", "quick", "tot", "copy", "match", "match_full"}
+    if "alloc" in todo:
+        for seed, (n, iv, nops) in {1: (48, 5, 700), 2: (32, 3, 700), 3: (64, 64, 900), 4: (16, 2, 500)}.items():
+            np.savez_compressed(OUT / f"alloc_trace_{seed}.npz", **alloc_trace(seed, n, iv, nops))
+            print("alloc trace", seed)
+    if "tree" in todo:
+        for seed in (1, 2, 3):
+            (OUT / f"tree_trace_{seed}.json").write_text(json.dumps(tree_trace(seed, 400)))
+            print("tree trace", seed)
+    if "quick" in todo:
+        (OUT / "quickstart.json").write_text(json.dumps(quickstart(), indent=0))
+        print("quickstart")
+    if "tot" in todo:
+        np.savez_compressed(OUT / "tot_8b.npz", **tot())
+        print("tot")
+    if "copy" in todo:
+        (OUT / "copy_zero.json").write_text(json.dumps(copy_zero(), indent=0))
+        print("copy/zero")
+    if "match" in todo:
+        small = W.MatchSpec(n_sequences=600, n_queries=256)
+        np.savez_compressed(OUT / "match_small.npz", **match_stress(small, 256))
+        print("match small")
+    if "match_full" in todo and not args.skip_full_match:
+        d = match_stress(W.MatchSpec(), 4096)
+        np.savez_compressed(OUT / "match_full.npz", **d)
+        print("match full", d["n_nodes"], d["build_s"], d["match_s"])
+
+
+if __name__ == "__main__":
+    main()

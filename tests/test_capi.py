@@ -1,0 +1,100 @@
+"""The C-ABI library loads, exports exactly what include/agentkv_b200.h
+declares, and its structs have the layout the Python binding assumes.  No
+call here touches a GPU: only argument validation paths that return before
+any CUDA call, and the pure host function akv_tree_hash."""
+
+import ctypes as C
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from agentkv_b200 import _native as N
+from agentkv_b200.device_tree import tree_hash, tree_hash_np
+
+REPO = Path(__file__).resolve().parent.parent
+HEADERS = sorted((REPO / "include").glob("*.h"))
+
+
+def declared_symbols():
+    names = set()
+    for h in HEADERS:
+        for m in re.finditer(r"^AKV_API\s+\w+\s+(akv_\w+)\s*\(", h.read_text(), re.M):
+            names.add(m.group(1))
+    return names
+
+
+def exported_symbols():
+    out = subprocess.run(["nm", "-D", "--defined-only", str(N.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if " T " in line}
+
+
+def test_library_exports_every_declared_symbol():
+    decl = declared_symbols()
+    assert len(decl) >= 18
+    assert exported_symbols() == decl
+    for name in decl:
+        assert hasattr(N.lib, name)
+        assert name in N.SIGNATURES
+
+
+def test_struct_layouts_match_header(tmp_path):
+    src = tmp_path / "probe.c"
+    src.write_text(r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "agentkv_b200.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu\n", sizeof(AkvStatus), sizeof(AkvAllocState),
+         sizeof(AkvTick), sizeof(AkvTreeView), offsetof(AkvAllocState, total_blocks),
+         offsetof(AkvTick, epoch_interval), offsetof(AkvTreeView, n_tokens),
+         offsetof(AkvTreeView, slot_mask));
+  printf("%d %d %d\n", AKV_CTL_WORDS, AKV_AUX_WORDS, AKV_CTL_RELEASED);
+  return 0;
+}
+""")
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", f"-I{REPO / 'include'}", str(src), "-o", str(exe)], check=True)
+    lines = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    c_vals = [int(x) for x in lines[0].split()]
+    py_vals = [C.sizeof(N.AkvStatus), C.sizeof(N.AkvAllocState), C.sizeof(N.AkvTick),
+               C.sizeof(N.AkvTreeView), N.AkvAllocState.total_blocks.offset,
+               N.AkvTick.epoch_interval.offset, N.AkvTreeView.n_tokens.offset,
+               N.AkvTreeView.slot_mask.offset]
+    assert c_vals == py_vals
+    assert [int(x) for x in lines[1].split()] == [N.CTL_WORDS, N.AUX_WORDS, N.CTL_RELEASED]
+
+
+def test_version_and_last_error():
+    assert N.version() >= (0, 3)
+    # Rejected on the host before any CUDA call.
+    rc = N.lib.akv_copy_blocks(None, 64, 4, None, -1, None, None, None)
+    assert rc == N.AKV_ERR_INVALID_ARG
+    assert "n_pairs" in N.last_error()
+    rc = N.lib.akv_zero_blocks(None, 64, 4, None, 3, None, None, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "NULL" in N.last_error()
+    with pytest.raises(N.NativeError):
+        N.check(N.AKV_ERR_INVALID_ARG)
+
+
+def test_empty_batches_are_noops_without_gpu():
+    assert N.lib.akv_copy_blocks(None, 64, 4, None, 0, None, None, None) == N.AKV_OK
+    assert N.lib.akv_zero_blocks(None, 64, 4, None, 0, None, None, None) == N.AKV_OK
+
+
+def test_match_prefix_rejects_bad_tree_view():
+    v = N.AkvTreeView(None, None, None, None, 0, 0, 0)
+    rc = N.lib.akv_match_prefix(C.byref(v), None, None, 1, 16, None, None, None, None, None)
+    assert rc == N.AKV_ERR_INVALID_ARG
+
+
+def test_tree_hash_python_equals_c():
+    rng = np.random.default_rng(0)
+    parents = rng.integers(-5, 2**31 - 1, size=2000)
+    tokens = rng.integers(-(2**31), 2**31 - 1, size=2000)
+    c = np.array([N.lib.akv_tree_hash(int(p), int(t)) for p, t in zip(parents, tokens)], np.uint32)
+    assert all(tree_hash(int(p), int(t)) == int(h) for p, t, h in zip(parents[:200], tokens[:200], c[:200]))
+    np.testing.assert_array_equal(tree_hash_np(parents, tokens), c)

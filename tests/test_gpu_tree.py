@@ -1,0 +1,304 @@
+"""The product pool (AgentKVPool on a B200) against the reference's fixtures.
+
+* Recorded tree traces (create_root / fork / allocate_block /
+  ensure_mutable_block / commit_prefix / free / match_prefix / zero_block,
+  with errors) replayed on a CUDA pool seeded with the same contents: every
+  result, block table, tree node, refcount, free-list entry and final block
+  digest must match.
+* The quickstart workload: block tables, CoW pairs, refcounts, match results
+  and pool bytes.
+* The Tree-of-Thought fan-out on the full 60,000-block pool, through the
+  single-op API and through the batched API.
+* match_prefix on the stress tree: device results equal the reference's
+  (node, length) for every query, and the oracle's comparison counts.
+"""
+
+import hashlib
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from agentkv_b200 import AgentKVPool, PoolConfig
+from agentkv_b200 import workloads as W
+from agentkv_b200.allocator import BlockHandle
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+T_CREATE, T_FORK, T_ALLOC, T_COW, T_APPEND, T_COMMIT, T_FREE, T_MATCH, T_ADVANCE, T_ZERO = range(10)
+
+
+def pool_digests(pool: AgentKVPool, as_int16=False):
+    kv = pool._allocator._kv_data
+    n = kv.shape[0]
+    raw = kv.view(torch.int16) if as_int16 else kv
+    host = raw.cpu().numpy()
+    return [hashlib.sha256(host[i].tobytes()).hexdigest() for i in range(n)]
+
+
+def tree_nodes(pool: AgentKVPool) -> dict:
+    return {
+        str(nid): {"parent": n.parent_id, "edge": n.edge_tokens, "blocks": [b.block_id for b in n.blocks],
+                   "children": sorted([int(k), int(v)] for k, v in n.children.items()), "ref": n.ref_count}
+        for nid, n in sorted(pool._tree._shared_nodes.items())
+    }
+
+
+@pytest.mark.parametrize("seed", [1, 2, 3])
+def test_reference_tree_trace(golden_dir, seed):
+    g = json.loads((golden_dir / f"tree_trace_{seed}.json").read_text())
+    n, bs = g["n_blocks"], g["block_size"]
+    cfg = PoolConfig(total_blocks=n, block_size=bs, num_layers=1, num_kv_heads=2, head_dim=4,
+                     dtype="float16", device="cuda", epoch_interval=7)
+    pool = AgentKVPool(config=cfg)
+    torch.manual_seed(seed)
+    pool._allocator._kv_data.copy_(torch.randn(pool._allocator._kv_data.shape, dtype=torch.float32).half())
+    live = {}
+    states = {step: st for step, st in g["states"]}
+    for step, rec in enumerate(g["ops"]):
+        op = rec["op"]
+        err = None
+        try:
+            if op == T_CREATE:
+                h = pool.create_root(rec["tokens"])
+                live[h.handle_id] = h
+                assert [h.handle_id, h.shared_node_id, h.shared_match_len] == rec["out"]
+            elif op == T_FORK:
+                c = pool.fork(live[rec["h"]])
+                live[c.handle_id] = c
+                assert c.handle_id == rec["out"]
+            elif op == T_ALLOC:
+                h = live[rec["h"]]
+                pool.allocate_block(h)
+                assert h.residual_blocks[-1].block_id == rec["out"]
+            elif op == T_COW:
+                h = live[rec["h"]]
+                pool.ensure_mutable_block(h, rec["idx"])
+                assert h.residual_blocks[rec["idx"]].block_id == rec["out"]
+            elif op == T_APPEND:
+                pool.append_tokens(live[rec["h"]], rec["tokens"])
+            elif op == T_COMMIT:
+                h = live[rec["h"]]
+                pool.commit_prefix(h, rec["length"])
+                assert [h.shared_node_id, h.shared_match_len] == rec["out"]
+            elif op == T_FREE:
+                pool.free(live.pop(rec["h"]))
+            elif op == T_MATCH:
+                mh, mlen = pool._tree.match_prefix(rec["tokens"])
+                got = [-1 if mh is None else mh.handle_id, mlen, -1 if mh is None else mh.shared_node_id]
+                assert got == rec["out"]
+                if mh is not None:
+                    live[mh.handle_id] = mh
+            elif op == T_ADVANCE:
+                pool.maybe_advance_epoch()
+            elif op == T_ZERO:
+                pool._allocator.zero_block(BlockHandle(rec["block"]))
+        except (ValueError, MemoryError) as e:
+            err = e
+        assert (err is not None) == ("error" in rec), f"step {step}: {rec} -> {err!r}"
+        if step in states:
+            st = states[step]
+            assert {str(k): pool.get_block_ids(h) for k, h in sorted(live.items())} == st["tables"]
+            assert {str(k): [h.shared_node_id, h.shared_match_len] for k, h in sorted(live.items())} == st["shared"]
+            assert tree_nodes(pool) == st["nodes"]
+            assert pool._allocator._ref_counts.cpu().tolist() == st["ref"]
+            assert pool._allocator.free_list().tolist() == st["free"]
+            s = pool.stats()
+            for k, v in st["stats"].items():
+                assert s[k] == v, (k, s[k], v)
+    assert pool_digests(pool) == g["block_sha256"]
+
+
+def test_quickstart_workload(golden_dir):
+    g = json.loads((golden_dir / "quickstart.json").read_text())
+    N_, bs, L, H, D, dt = W.QUICKSTART_GEOMETRY
+    cfg = PoolConfig(total_blocks=N_, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D, dtype=dt,
+                     device="cuda")
+    pool = AgentKVPool(config=cfg)
+    torch.manual_seed(0)
+    pool._allocator._kv_data.copy_(torch.randn(pool._allocator._kv_data.shape, dtype=torch.float16))
+    root = pool.create_root(list(range(32)))
+    pool.allocate_block(root)
+    kids = [pool.fork(root) for _ in range(3)]
+    for c in kids:
+        pool.allocate_block(c)
+    for c in kids:
+        pool.ensure_mutable_block(c, 0)
+    pool.commit_prefix(root, 16)
+    matches = []
+    for q in g["queries"]:
+        mh, mlen = pool._tree.match_prefix(q)
+        matches.append([-1 if mh is None else mh.shared_node_id, mlen])
+    assert [pool.get_block_ids(c) for c in kids] == g["children"]
+    assert pool.get_block_ids(root) == g["root"]
+    assert matches == g["matches"]
+    assert pool._allocator._ref_counts.cpu().tolist() == g["ref"]
+    assert pool._allocator.free_list().tolist() == g["free"]
+    assert pool_digests(pool) == g["block_sha256"]
+    s = pool.stats()
+    for k, v in g["stats"].items():
+        assert s[k] == v, k
+
+
+def _tot_pool():
+    N_, bs, L, H, D, dt = W.LLAMA3_8B_GEOMETRY
+    cfg = PoolConfig(total_blocks=N_, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D, dtype=dt,
+                     device="meta")
+    return AgentKVPool(config=cfg)
+
+
+def _check_tot(pool, g, kids):
+    tables = np.concatenate([np.asarray(pool.get_block_ids(c), np.int32) for c in kids])
+    np.testing.assert_array_equal(tables, g["tables"])
+    np.testing.assert_array_equal(pool._allocator._ref_counts.cpu().numpy(), g["ref_fanout"])
+    np.testing.assert_array_equal(pool._allocator.free_list(), g["free_fanout"])
+    st = json.loads(str(g["stats_fanout"]))
+    s = pool.stats()
+    for k in ("free_blocks", "allocated_blocks", "peak_allocated", "total_allocs", "epoch", "active_handles"):
+        assert s[k] == st[k], k
+
+
+@pytest.mark.slow
+def test_tot_single_op_api(golden_dir):
+    g = np.load(golden_dir / "tot_8b.npz")
+    spec = W.ToTSpec()
+    pool = _tot_pool()
+    root = pool.create_root(W.tot_root_tokens(spec))
+    for _ in range(spec.root_tokens // 16):
+        pool.allocate_block(root)
+    level, kids = [root], []
+    for lvl in range(spec.levels):
+        nxt = []
+        for pi, parent in enumerate(level):
+            for k in range(spec.fanout):
+                c = pool.fork(parent)
+                pool.ensure_mutable_block(c, len(c.residual_blocks) - 1)
+                pool.append_tokens(c, W.tot_append_tokens(spec, lvl, pi * spec.fanout + k))
+                for _ in range(spec.appended_blocks):
+                    pool.allocate_block(c)
+                nxt.append(c)
+        kids.extend(nxt)
+        level = nxt
+    _check_tot(pool, g, kids)
+    for c in kids:
+        pool.free(c)
+    np.testing.assert_array_equal(pool._allocator._ref_counts.cpu().numpy(), g["ref_freed"])
+    np.testing.assert_array_equal(pool._allocator.free_list(), g["free_freed"])
+
+
+def test_tot_batched_api(golden_dir):
+    """Same fan-out with one launch per batch: fork_many, ensure_mutable_batch,
+    allocate_blocks, free_many."""
+    g = np.load(golden_dir / "tot_8b.npz")
+    spec = W.ToTSpec()
+    pool = _tot_pool()
+    root = pool.create_root(W.tot_root_tokens(spec))
+    pool.allocate_blocks(root, spec.root_tokens // 16)
+    level, kids = [root], []
+    for lvl in range(spec.levels):
+        nxt = []
+        for parent in level:
+            nxt.extend(pool.fork_many(parent, spec.fanout))
+        # CoW and appends keep the reference's per-child order: child c's CoW
+        # id, then its appended ids, then child c + 1.
+        for c in nxt:
+            pool.ensure_mutable_batch([(c, len(c.residual_blocks) - 1)])
+            pool.allocate_blocks(c, spec.appended_blocks)
+        kids.extend(nxt)
+        level = nxt
+    _check_tot(pool, g, kids)
+    pool.free_many(kids)
+    np.testing.assert_array_equal(pool._allocator._ref_counts.cpu().numpy(), g["ref_freed"])
+    np.testing.assert_array_equal(pool._allocator.free_list(), g["free_freed"])
+
+
+def _build_match_tree(spec, total_blocks):
+    prefixes = W.match_prefixes(spec)
+    corpus = W.match_sequences(spec, prefixes)
+    cfg = PoolConfig(total_blocks=total_blocks, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1,
+                     dtype="float16", device="meta")
+    pool = AgentKVPool(config=cfg)
+    for seq in corpus:
+        h = pool.create_root(seq)
+        need = -(-len(seq) // 16) - len(pool.get_block_ids(h))
+        pool.allocate_blocks(h, need)
+        share = (len(seq) // 16) * 16 - h.shared_match_len
+        if share > 0:
+            pool.commit_prefix(h, share)
+    return pool, prefixes, corpus
+
+
+@pytest.mark.parametrize("name", ["match_small", pytest.param("match_full", marks=pytest.mark.slow)])
+def test_match_prefix_stress_tree(golden_dir, name):
+    g = np.load(golden_dir / f"{name}.npz")
+    spec = W.MatchSpec(**json.loads(str(g["spec"])))
+    pool, prefixes, corpus = _build_match_tree(spec, int(g["total_blocks"]))
+    assert len(pool._tree._shared_nodes) == int(g["n_nodes"])
+    assert pool._tree._next_node_id == int(g["next_node_id"])
+    assert pool.free_blocks == int(g["free_blocks"])
+    queries = W.match_queries(spec, corpus, prefixes, batch=0, n=len(g["node"]))
+    node, mlen, cmp_ = pool.match_prefix_batch(queries, with_compared=True)
+    np.testing.assert_array_equal(node, g["node"])
+    np.testing.assert_array_equal(mlen, g["len"])
+    # single-query path agrees with the batch
+    for i, q in enumerate(queries[:16]):
+        want = (int(node[i]), int(mlen[i])) if mlen[i] else (-1, 0)
+        assert pool._tree._match_prefix_locked(q) == want
+    # comparison counts equal the oracle's restatement over the same tree
+    otree = _oracle_tree_from(pool)
+    flat, q_off = O.pack_queries([q.tolist() for q in queries])
+    on, ol, oc = O.match_prefix_csr(otree, flat, q_off, 16)
+    np.testing.assert_array_equal(on, node)
+    np.testing.assert_array_equal(ol, mlen)
+    np.testing.assert_array_equal(oc, cmp_)
+
+
+def _oracle_tree_from(pool) -> dict:
+    """CSR arrays of the product tree for the oracle's C match."""
+    nodes = pool._tree._shared_nodes
+    n = max(nodes) + 1
+    child_ptr = np.zeros(n + 1, np.int64)
+    keys, ids, toks = [], [], []
+    edge_off = np.zeros(n, np.int64)
+    edge_len = np.zeros(n, np.int32)
+    pos = 0
+    for nid in range(n):
+        nd = nodes.get(nid)
+        if nd is not None:
+            for k in sorted(nd.children):
+                keys.append(k)
+                ids.append(nd.children[k])
+            e = np.asarray(nd.edge, np.int32)
+            edge_off[nid], edge_len[nid] = pos, len(e)
+            toks.append(e)
+            pos += len(e)
+        child_ptr[nid + 1] = len(keys)
+    return {"child_ptr": child_ptr, "child_key": np.asarray(keys or [0], np.int32),
+            "child_id": np.asarray(ids or [0], np.int32), "edge_off": edge_off, "edge_len": edge_len,
+            "edge_tokens": np.concatenate(toks) if pos else np.zeros(1, np.int32)}
+
+
+def test_match_edge_cases():
+    cfg = PoolConfig(total_blocks=64, block_size=4, num_layers=1, num_kv_heads=1, head_dim=1,
+                     dtype="float16", device="meta")
+    pool = AgentKVPool(config=cfg)
+    # empty tree, empty query, single token
+    assert pool._tree._match_prefix_locked([]) == (-1, 0)
+    assert pool._tree._match_prefix_locked([5]) == (-1, 0)
+    h = pool.create_root(list(range(12)))
+    pool.allocate_blocks(h, 3)
+    pool.commit_prefix(h, 8)
+    # exact, longer, partial edge (no credit), mismatch at first token
+    assert pool._tree._match_prefix_locked(list(range(8)))[1] == 8
+    assert pool._tree._match_prefix_locked(list(range(20)))[1] == 8
+    assert pool._tree._match_prefix_locked(list(range(7))) == (-1, 0)
+    assert pool._tree._match_prefix_locked([1, 2, 3]) == (-1, 0)
+    # a non-aligned edge (commit with fewer tokens than blocks) is floored
+    h2 = pool.create_root([100, 101, 102])
+    pool.allocate_blocks(h2, 2)
+    pool.commit_prefix(h2, 8)  # edge holds only 3 tokens
+    assert pool._tree._match_prefix_locked([100, 101, 102, 9]) == (-1, 0)
+    node, mlen = pool.match_prefix_batch([[100, 101, 102], list(range(9)), []])
+    assert mlen.tolist() == [0, 8, 0]

@@ -1,0 +1,120 @@
+"""Host-side logic that needs no GPU: config validation (same rules and
+messages as the reference), the device-tree mirror's hash table, pair
+validation, and the seeded workload generators."""
+
+import numpy as np
+import pytest
+
+from agentkv_b200 import workloads as W
+from agentkv_b200.config import PoolConfig
+from agentkv_b200.device_tree import DELETED, EMPTY, tree_hash
+
+
+class TestPoolConfig:
+    def test_bytes_per_block(self):
+        c = PoolConfig(total_blocks=10, block_size=16, num_layers=32, num_kv_heads=8, head_dim=128,
+                       dtype="bfloat16", device="cuda")
+        assert c.bytes_per_block == 2 * 1024 * 1024
+        assert c.total_bytes == 10 * c.bytes_per_block
+
+    @pytest.mark.parametrize("kw,msg", [
+        ({"dtype": "int8"}, "dtype must be one of"),
+        ({"block_size": 12}, "power of 2"),
+        ({"block_size": 0}, "power of 2"),
+        ({"total_blocks": 0}, "total_blocks must be > 0"),
+        ({"max_agents": 0}, "max_agents must be > 0"),
+    ])
+    def test_validation(self, kw, msg):
+        with pytest.raises(ValueError, match=msg):
+            PoolConfig(**kw)
+
+    def test_from_capacity_rounds_down_to_power_of_two(self):
+        c = PoolConfig.from_capacity_gb(1.0, num_layers=32, num_kv_heads=8, head_dim=128, dtype="float16")
+        assert c.total_blocks == 512  # 1 GiB / 2 MiB
+        c = PoolConfig.from_capacity_gb(0.9, num_layers=32, num_kv_heads=8, head_dim=128)
+        assert c.total_blocks == 256
+        with pytest.raises(ValueError, match="too small"):
+            PoolConfig.from_capacity_gb(1e-9)
+
+    def test_repr(self):
+        assert "GiB" in repr(PoolConfig(total_blocks=4, device="cpu"))
+
+
+def _kernel_style_lookup(slots, parent, token):
+    """The device lookup rule: 32-slot windows from the hash; first hit wins,
+    an empty slot before any hit ends the probe."""
+    mask = len(slots) - 1
+    h = tree_hash(parent, token)
+    for w in range(len(slots) // 32 + 1):
+        win = [(h + w * 32 + lane) & mask for lane in range(32)]
+        hits = [i for i, s in enumerate(win) if slots[s, 0] == parent and slots[s, 1] == token]
+        empties = [i for i, s in enumerate(win) if slots[s, 0] == EMPTY]
+        if hits:
+            return int(slots[win[hits[0]], 2]) if not empties or hits[0] < empties[0] else -1
+        if empties:
+            return -1
+    return -1
+
+
+def test_device_tree_hash_table_mirror():
+    from agentkv_b200.device_tree import DeviceTree
+    import torch
+
+    t = DeviceTree(torch.device("cpu"), slot_cap=64)
+    ref = {}
+    rng = np.random.default_rng(5)
+    for step in range(3000):
+        p, k = int(rng.integers(0, 40)), int(rng.integers(0, 12))
+        if rng.random() < 0.65:
+            c = int(rng.integers(1, 10_000))
+            t.set_child(p, k, c)
+            ref[(p, k)] = c
+        else:
+            t.del_child(p, k)
+            ref.pop((p, k), None)
+        if step % 97 == 0:
+            for pp in range(40):
+                for kk in range(12):
+                    assert _kernel_style_lookup(t.h_slots, pp, kk) == ref.get((pp, kk), -1)
+    assert t.live == len(ref)
+    assert 2 * (t.live + t.dead) <= len(t.h_slots)
+    assert (t.h_slots[:, 0] >= DELETED).all()
+
+
+def test_device_tree_arena_and_nodes():
+    from agentkv_b200.device_tree import DeviceTree
+    import torch
+
+    t = DeviceTree(torch.device("cpu"), node_cap=2, token_cap=4)
+    o1 = t.append_tokens(np.arange(5))
+    o2 = t.append_tokens(np.arange(100, 103))
+    assert (o1, o2) == (0, 5)
+    t.set_node(7, o2, 3)
+    assert t.edge(o2, 3).tolist() == [100, 101, 102]
+    assert len(t.h_off) >= 8 and t.h_len[7] == 3
+
+
+def test_validate_pairs():
+    from agentkv_b200.kernels import validate_pairs
+
+    validate_pairs([[0, 1], [2, 3], [4, 4]], 5)
+    with pytest.raises(ValueError, match="out of range"):
+        validate_pairs([[0, 5]], 5)
+    with pytest.raises(ValueError, match="appears twice"):
+        validate_pairs([[0, 1], [2, 1]], 5)
+    with pytest.raises(ValueError, match="read as another"):
+        validate_pairs([[0, 1], [1, 2]], 5)
+
+
+def test_workloads_are_deterministic():
+    a = W.copy_sweep_pairs(512)
+    b = W.copy_sweep_pairs(512)
+    np.testing.assert_array_equal(a, b)
+    assert len(np.unique(a)) == 1024 and a.max() < 60_000
+    assert not np.array_equal(a, W.copy_sweep_pairs(512, rotation=1))
+    spec = W.MatchSpec(n_sequences=50, n_queries=16)
+    s1, s2 = W.match_sequences(spec), W.match_sequences(spec)
+    assert all(np.array_equal(x, y) for x, y in zip(s1, s2))
+    assert all(512 <= len(x) <= 8192 for x in s1)
+    assert W.quickstart_queries() == W.quickstart_queries()
+    assert len(W.tot_root_tokens()) == 4096
