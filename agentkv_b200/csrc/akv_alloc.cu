@@ -339,10 +339,13 @@ __global__ void k_dec_plan(AkvAllocState st, int32_t n, int32_t n_ctas, int32_t*
   p.readers = tk.readers_active;
   p.allowed = (!tk.readers_active || ctl[C_EPOCH] > tk.readers_max) ? 1 : 0;
   if (!tk.readers_active) {
+    // No reader: every retirement passes straight through the reclaimer's
+    // release (_try_retire counts it in _freed_count) to the free list.
     p.left_new = wrap(left - d - n_ret, N);
     ctl[C_LEFT] = p.left_new;
     ctl[C_SIZE] = f + d + n_ret;
     ctl[C_HEAD] = rel;
+    ctl[C_RELEASED] += n_ret;
   } else {
     p.left_new = wrap(left - d, N);
     ctl[C_LEFT] = p.left_new;
