@@ -438,6 +438,63 @@ class SlabAllocator:
         return {"child_tables": child_tables, "child_off": child_off, "pairs": pairs.view(-1, 2),
                 "child_lens": np.repeat(lens + A, K), "launches": launches}
 
+    def fanout_tree(self, root_tables: torch.Tensor, root_lens, levels: int, fanout: int, append: int,
+                    *, level_offsets=None, on_level=None) -> dict:
+        """A whole multi-level fan-out (Tree-of-Thought): `levels` rounds of
+        fanout_level starting from the roots, children of one round being the
+        parents of the next, children in (parent, child) order.
+
+        The end state equals the reference's per-child sequence (fork,
+        ensure_mutable_block(-1), `append` allocate_block calls, level after
+        level): every round's allocations and plan run first, in order — they
+        fix which ids each child gets — then one inc_ref batch for all forks
+        and one dec_ref batch for all copy-on-write sources.  Every CoW source
+        keeps a refcount >= 1 throughout, so no id retires and the order of
+        the refcount updates cannot change the result.  No copy is made:
+        `pairs[l]` lists round l's (src, dst) block copies, ready once
+        `on_level(l)` has been called (e.g. to record an event) — copy them
+        on any stream after that point.  Returns per-round device tensors
+        child_tables / pairs and the launch count."""
+        K, A = int(fanout), int(append)
+        lens = np.asarray(root_lens, np.int64)
+        if (lens < 1).any():
+            raise ValueError("fanout_tree: every root needs at least one residual block")
+        dev = self._dev
+        tables = root_tables
+        out_tables, out_pairs, incs, decs = [], [], [], []
+        launches = 0
+        for lvl in range(levels):
+            P, nc, total = len(lens), len(lens) * K, int(lens.sum())
+            if level_offsets is not None:
+                off_d = level_offsets[lvl]
+            else:
+                off = np.zeros(P + 1, np.int64)
+                np.cumsum(lens, out=off[1:])
+                off_d = torch.from_numpy(off).to(dev, non_blocking=True)
+            fresh = self.alloc_batch((1 + A) * nc)
+            child_tables = torch.empty(K * total + nc * A, dtype=torch.int32, device=dev)
+            child_off = torch.empty(nc + 1, dtype=torch.int64, device=dev)
+            inc_ids = torch.empty(K * total, dtype=torch.int32, device=dev)
+            pairs = torch.empty(2 * nc, dtype=torch.int32, device=dev)
+            dec_ids = torch.empty(nc, dtype=torch.int32, device=dev)
+            with self._lock:
+                N.check(N.lib.akv_fanout_plan(tables.data_ptr(), off_d.data_ptr(), P, K, A, fresh.data_ptr(),
+                                              child_tables.data_ptr(), child_off.data_ptr(), inc_ids.data_ptr(),
+                                              pairs.data_ptr(), dec_ids.data_ptr(), self._stream()))
+            launches += 2
+            if on_level is not None:
+                on_level(lvl)
+            out_tables.append(child_tables)
+            out_pairs.append(pairs.view(-1, 2))
+            incs.append(inc_ids)
+            decs.append(dec_ids)
+            tables = child_tables
+            lens = np.repeat(lens + A, K)
+        self.inc_ref_batch(torch.cat(incs) if len(incs) > 1 else incs[0])
+        self.dec_ref_batch(torch.cat(decs) if len(decs) > 1 else decs[0])
+        launches += 2 + 4
+        return {"child_tables": out_tables, "pairs": out_pairs, "launches": launches}
+
     def copy_blocks(self, pairs, *, check_refs: bool = True) -> None:
         """Copy a batch of independent (src, dst) pairs; dsts must be exclusive."""
         if self._kv_data.device.type == "meta":

@@ -444,6 +444,8 @@ int zero_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* ids,
 int akv_launch_copy_counted(void* pool, int64_t bpb, int32_t total, const int32_t* pairs,
                             int32_t n_max, const int64_t* n_dev, AkvStatus* st, cudaStream_t s) {
   if (n_max <= 0) return AKV_OK;
+  if (bulk_eligible(pool, bpb))
+    return copy_bulk_launch(static_cast<char*>(pool), bpb, total, pairs, n_max, nullptr, st, s, n_dev);
   return copy_vec_dispatch(static_cast<char*>(pool), bpb, total, pairs, n_max, nullptr, st, s, n_dev);
 }
 
@@ -461,7 +463,9 @@ extern "C" int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int3
   AKV_ARG_CHECK(variant >= 0 && variant <= 2, "akv_copy_blocks: unknown variant %d", variant);
   char* p = static_cast<char*>(pool);
   cudaStream_t s = akv_stream(stream);
-  if (variant == 0) variant = 1;
+  // Automatic choice: the bulk-async engine whenever the spans are 16-byte
+  // aligned (measured faster from 64 pairs of 2 MiB up, equal below).
+  if (variant == 0) variant = bulk_eligible(pool, bytes_per_block) ? 2 : 1;
   if (variant == 2 && bulk_eligible(pool, bytes_per_block))
     return copy_bulk_launch(p, bytes_per_block, total_blocks, pairs, n_pairs, ref_counts, status, s);
   return copy_vec_dispatch(p, bytes_per_block, total_blocks, pairs, n_pairs, ref_counts, status, s);
@@ -486,7 +490,7 @@ extern "C" int akv_zero_blocks_variant(void* pool, int64_t bytes_per_block, int3
   AKV_ARG_CHECK(variant >= 0 && variant <= 2, "akv_zero_blocks: unknown variant %d", variant);
   char* p = static_cast<char*>(pool);
   cudaStream_t s = akv_stream(stream);
-  if (variant == 0) variant = 1;
+  if (variant == 0) variant = bulk_eligible(pool, bytes_per_block) ? 2 : 1;
   if (variant == 2 && bulk_eligible(pool, bytes_per_block))
     return zero_bulk_launch(p, bytes_per_block, total_blocks, ids, n, ref_counts, status, s);
   return zero_vec_dispatch(p, bytes_per_block, total_blocks, ids, n, ref_counts, status, s);

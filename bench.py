@@ -67,8 +67,13 @@ def parse_args():
     ap.add_argument("--blocks", type=int, default=W.LLAMA3_8B_GEOMETRY[0], help="blocks per tree/GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch every kernel from Python each step")
     ap.add_argument("--match", action="store_true", help="also time match_prefix on the stress tree")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--case", default="tot", choices=["tot", "sweep"],
+                    help="tot: the headline step; sweep: batched copy/zero sweep (prints its own line)")
+    ap.add_argument("--batches", default="1,8,64,512,4096", help="sweep batch sizes")
+    ap.add_argument("--rotations", type=int, default=8, help="sweep: distinct pair sets cycled")
     return ap.parse_args()
 
 
@@ -130,7 +135,14 @@ class ClockSampler:
 
 # ── the device step ──────────────────────────────────────────────────────────
 class ToTBench:
-    """One ToT fan-out + free per step on device-resident block tables."""
+    """One ToT fan-out + free per step on device-resident block tables.
+
+    Rank 0 runs the allocator kernels (alloc, fan-out plan, inc_ref, dec_ref)
+    on a side stream; the copies run on the current stream, each level's copy
+    waiting only for that level's plan.  Allocator kernels never read or write
+    pool bytes, so they overlap the copies; every copy is ordered after the
+    previous ones on its stream, which keeps a block that is freed and handed
+    out again from being overwritten before an older copy has read it."""
 
     def __init__(self, rank: int, world: int, blocks_per_tree: int, variant: int):
         import torch
@@ -157,93 +169,122 @@ class ToTBench:
         self.slice_bytes = L * 2 * self.slice_heads * bs * D * 2
         self.variant = variant
         self.alloc = None
+        self.pairs_per_level = [self.trees * c for c in self.spec.children_per_level()]
+        root_len = self.spec.root_tokens // bs
+        # parent table lengths per level are fixed by the workload
+        self.level_lens = []
+        lens = np.full(self.trees, root_len, np.int64)
+        for _ in range(self.spec.levels):
+            self.level_lens.append(lens)
+            lens = np.repeat(lens + self.spec.appended_blocks, self.spec.fanout)
+        self.level_off = []
+        for lens in self.level_lens:
+            off = np.zeros(len(lens) + 1, np.int64)
+            np.cumsum(lens, out=off[1:])
+            self.level_off.append(torch.from_numpy(off).to(self.dev))
+        self.pairs_bufs = [torch.empty((n, 2), dtype=torch.int32, device=self.dev) for n in self.pairs_per_level]
         if rank == 0:
             cfg = PoolConfig(total_blocks=self.n_blocks, block_size=bs, num_layers=L, num_kv_heads=H,
                              head_dim=D, dtype=dt, device="meta")
             self.alloc = SlabAllocator(cfg)
-            roots = self.alloc.alloc_batch(self.spec.root_tokens // bs * self.trees)
-            self.root_tables = roots
-            self.root_lens = np.full(self.trees, self.spec.root_tokens // bs, np.int64)
+            self.root_tables = self.alloc.alloc_batch(root_len * self.trees)
             self.alloc.check()
-        self.pairs_per_level = [self.trees * c for c in self.spec.children_per_level()]
+            self.root_host = self.root_tables.cpu().pin_memory()
+            self.meta = torch.cuda.Stream(self.dev)
+            n_child_entries = sum(int(x.sum()) * self.spec.fanout + len(x) * self.spec.fanout *
+                                  self.spec.appended_blocks for x in self.level_lens)
+            self.host_tables = torch.empty(n_child_entries, dtype=torch.int32, pin_memory=True)
+            self.host_status = torch.empty(8, dtype=torch.int32, pin_memory=True)
         self.launches_per_step = 0
         self.copy_events = []
 
-    def _offsets(self, lens):
-        off = np.zeros(len(lens) + 1, np.int64)
-        np.cumsum(lens, out=off[1:])
-        return off
+    def join(self):
+        """Make the current stream wait for the allocator stream."""
+        if self.rank == 0:
+            self.torch.cuda.current_stream(self.dev).wait_stream(self.meta)
 
-    def step(self, e2e=False, time_copies=False):
-        """Returns (h2d_bytes, d2h_bytes)."""
+    def step(self, e2e=False, time_copies=False, capture=False):
+        """Returns (h2d_bytes, d2h_bytes) of the host-driven variant."""
         torch = self.torch
         from agentkv_b200 import kernels as K
 
+        cs = torch.cuda.current_stream(self.dev)
         h2d = d2h = 0
         launches = 0
-        tables, lens = (self.root_tables, self.root_lens) if self.rank == 0 else (None, None)
-        host_tables = None
-        if e2e and self.rank == 0:
-            host_tables = self.root_tables.cpu().numpy()
-        kids_tables = []
+        events = []
+        if self.rank == 0:
+            if capture:
+                self.meta.wait_stream(cs)  # fork the allocator stream into the capture
+            with torch.cuda.stream(self.meta):
+                if e2e:
+                    roots = self.root_host.to(self.dev, non_blocking=True)
+                    h2d += self.root_host.numel() * 4
+                else:
+                    roots = self.root_tables
+
+                def on_level(_lvl):
+                    ev = torch.cuda.Event()
+                    ev.record(self.meta)
+                    events.append(ev)
+
+                res = self.alloc.fanout_tree(roots, self.level_lens[0], self.spec.levels, self.spec.fanout,
+                                             self.spec.appended_blocks, level_offsets=self.level_off,
+                                             on_level=on_level)
+                launches += res["launches"]
+                frees = torch.cat(res["child_tables"])
+                self.alloc.dec_ref_batch(frees)  # every child freed, in creation order
+                launches += 4
+                if e2e:
+                    self.host_tables.copy_(frees, non_blocking=True)
+                    self.host_status.copy_(self.alloc._status, non_blocking=True)
+                    d2h += self.host_tables.numel() * 4 + self.host_status.numel() * 4
         for lvl, n_pairs in enumerate(self.pairs_per_level):
             if self.rank == 0:
-                off = self._offsets(lens)
-                if e2e:
-                    pin = torch.from_numpy(host_tables).pin_memory()
-                    tables = pin.to(self.dev, non_blocking=True)
-                    h2d += pin.numel() * 4
-                off_pin = torch.from_numpy(off).pin_memory()
-                off_d = off_pin.to(self.dev, non_blocking=True)
-                h2d += off.nbytes if e2e else 0
-                res = self.alloc.fanout_level(tables, off_d, lens, self.spec.fanout, self.spec.appended_blocks,
-                                              copy=False)
-                launches += res["launches"]
-                pairs = res["pairs"]
-                tables, lens = res["child_tables"], res["child_lens"]
-                kids_tables.append(tables)
-                if e2e:
-                    host_tables = tables.cpu().numpy()  # waits: the host needs the tables
-                    d2h += host_tables.nbytes
+                pairs = res["pairs"][lvl]
+                pairs.record_stream(cs)
+                cs.wait_event(events[lvl])
             else:
-                pairs = torch.empty((n_pairs, 2), dtype=torch.int32, device=self.dev)
+                pairs = self.pairs_bufs[lvl]
             if self.world > 1:
                 torch.distributed.broadcast(pairs, src=0)
             if time_copies:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
+                e0.record(cs)
             K.copy_blocks(self.pool, pairs, variant=self.variant)
             launches += 1
             if time_copies:
-                e1.record()
+                e1.record(cs)
                 self.copy_events.append((e0, e1, n_pairs))
-        if self.rank == 0:
-            frees = torch.cat(kids_tables)
-            if e2e:
-                hf = frees.cpu()  # the host releases the children it holds
-                pin = hf.pin_memory()
-                frees = pin.to(self.dev, non_blocking=True)
-                h2d += pin.numel() * 4
-            self.alloc.dec_ref_batch(frees)
-            launches += 4
-            if e2e:
-                st = self.alloc._status.cpu()
-                d2h += st.numel() * 4
-                if int(st[0]):
-                    self.alloc.check()
+        if capture:
+            self.join()
+        if e2e and self.rank == 0:
+            self.join()
+            torch.cuda.synchronize(self.dev)  # the host reads its tables and the status
+            if int(self.host_status[0]):
+                self.alloc.check()
         self.launches_per_step = launches
         return h2d, d2h
+
+    def capture(self):
+        """Record one step as a CUDA graph (single GPU); returns the graph."""
+        torch = self.torch
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step(capture=True)
+        return g
 
     def copy_bytes_per_step_global(self):
         """Algorithmic bytes of all copies of one step, all ranks together."""
         return sum(self.pairs_per_level) * 2 * self.slice_bytes * self.world
 
 
-def timed(fn, steps, warmup, world):
+def timed(fn, steps, warmup, world, join=None):
     import torch
 
     for _ in range(warmup):
         fn()
+    if join is not None:
+        join()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
@@ -253,6 +294,8 @@ def timed(fn, steps, warmup, world):
     e0.record()
     for _ in range(steps):
         fn()
+    if join is not None:
+        join()
     e1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
@@ -407,6 +450,68 @@ def match_figure(steps: int, warmup: int) -> dict:
     }
 
 
+# ── copy / zero sweep ────────────────────────────────────────────────────────
+def sweep_case(args) -> None:
+    """Batched copy and zero over disjoint random pairs of a Llama-3-8B-shaped
+    pool of --blocks blocks; each batch size cycles --rotations pair sets so
+    small batches do not stay in L2."""
+    import torch
+
+    from agentkv_b200 import kernels as K
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    n_blocks, bs, L, H, D, _ = W.LLAMA3_8B_GEOMETRY
+    n_blocks = args.blocks
+    pool = torch.empty((n_blocks, L, 2, H, bs, D), dtype=torch.bfloat16, device=dev)
+    pool.normal_(generator=torch.Generator(device=dev).manual_seed(3))
+    bpb = L * 2 * H * bs * D * 2
+    peak, peak_kind = measured_peak()
+    out = {"case": "copy_zero_sweep", "pool_blocks": n_blocks, "bytes_per_block": bpb,
+           "variant": args.variant, "peak_gbs": peak, "peak_source": peak_kind, "batches": {}}
+    for n in [int(x) for x in args.batches.split(",")]:
+        if 2 * n > n_blocks:
+            continue
+        sets = [torch.from_numpy(W.copy_sweep_pairs(n, n_blocks, rotation=r)).to(dev)
+                for r in range(args.rotations)]
+        dsts = [p_[:, 1].contiguous() for p_ in sets]
+        for i in range(args.warmup):
+            K.copy_blocks(pool, sets[i % len(sets)], variant=args.variant)
+            K.zero_blocks(pool, dsts[i % len(dsts)], variant=args.variant)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            K.copy_blocks(pool, sets[i % len(sets)], variant=args.variant)
+        e1.record()
+        torch.cuda.synchronize()
+        c_ms = e0.elapsed_time(e1) / args.steps
+        e0.record()
+        for i in range(args.steps):
+            K.zero_blocks(pool, dsts[i % len(dsts)], variant=args.variant)
+        e1.record()
+        torch.cuda.synchronize()
+        z_ms = e0.elapsed_time(e1) / args.steps
+        K.raise_for_status(K._status_buffer(dev))
+        c_gbs = 2 * bpb * n / (c_ms / 1e3) / 1e9
+        z_gbs = bpb * n / (z_ms / 1e3) / 1e9
+        out["batches"][str(n)] = {"copy_ms": round(c_ms, 5), "copy_gbs": round(c_gbs, 1),
+                                  "copy_frac": round(c_gbs / peak, 4), "zero_ms": round(z_ms, 5),
+                                  "zero_gbs": round(z_gbs, 1), "zero_frac": round(z_gbs / peak, 4)}
+    print(json.dumps(out), flush=True)
+
+
+def level3_traffic():
+    """DRAM bytes (read + write) of the level-3 copy launch from the committed
+    ncu summary, or None."""
+    p = REPO / "profiles" / "copy_blocks_tot_level3.md"
+    if p.exists():
+        for line in p.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1])
+    return None
+
+
 # ── main arm ─────────────────────────────────────────────────────────────────
 def main():
     args = parse_args()
@@ -415,6 +520,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return
+    if args.case == "sweep":
+        sweep_case(args)
         return
     import torch
 
@@ -425,9 +533,25 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
     bench = ToTBench(rank, world, args.blocks, args.variant)
+    graph = None
+    if world == 1 and not args.no_graph:
+        for _ in range(2):  # load every kernel and settle the allocator pools before capture
+            bench.step()
+        bench.join()
+        torch.cuda.synchronize()
+        graph = bench.capture()
+        run_step = graph.replay
+    else:
+        run_step = bench.step
     sampler = ClockSampler(local)
     with sampler:
-        ms, wall = timed(lambda: bench.step(), args.steps, args.warmup, world)
+        ms, wall = timed(run_step, args.steps, args.warmup, world, join=bench.join)
+    if bench.alloc is not None:
+        # every step frees what it allocated: only the roots remain allocated
+        bench.alloc.check()
+        st = bench.alloc.stats()
+        assert st["allocated_blocks"] == len(bench.root_host), st
+        assert st["pending_reclamation"] == 0, st
     clocks = sampler.summary()
     step_ms = ms / args.steps
     copy_bytes = bench.copy_bytes_per_step_global()
@@ -437,6 +561,7 @@ def main():
     bench.copy_events = []
     for _ in range(3):
         bench.step(time_copies=True)
+    bench.join()
     torch.cuda.synchronize()
     kbytes = sum(2 * bench.slice_bytes * n for (_, _, n) in bench.copy_events)
     kms = sum(e0.elapsed_time(e1) for (e0, e1, _) in bench.copy_events)
@@ -444,7 +569,11 @@ def main():
     for (e0, e1, n) in bench.copy_events:
         per_level.setdefault(n, []).append(e0.elapsed_time(e1))
     peak, peak_kind = measured_peak()
-    achieved = kbytes / (kms / 1e3) / 1e9
+    # the dominant launch is the largest level (512 pairs at N = 1)
+    big = max(per_level)
+    big_ms = statistics.mean(per_level[big])
+    achieved = 2 * bench.slice_bytes * big / (big_ms / 1e3) / 1e9
+    traffic = level3_traffic() if world == 1 else None
     launches = len(bench.copy_events)
 
     e2e = None
@@ -454,7 +583,7 @@ def main():
         def e2e_step():
             res["io"] = bench.step(e2e=True)
 
-        e_ms, _ = timed(e2e_step, max(3, args.steps // 2), 1, world)
+        e_ms, _ = timed(e2e_step, max(3, args.steps // 2), 1, world, join=bench.join)
         e_step = e_ms / max(3, args.steps // 2)
         h2d, d2h = res["io"]
         e2e = {"value": round(copy_bytes / (e_step / 1e3) / 1e9, 2), "unit": UNIT,
@@ -496,11 +625,15 @@ def main():
                 "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
                 "l2": "inputs larger than L2 (each step touches ~2.4 GB per GPU)",
                 "copy_variant": args.variant,
+                "cuda_graph": graph is not None,
             },
             "roofline": {
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": None,
-                "kernel": "akv copy_blocks", "peak_source": peak_kind,
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "kernel": f"akv copy_blocks, {big}-pair launch", "peak_source": peak_kind,
+                "algorithmic_bytes_per_launch": 2 * bench.slice_bytes * big,
+                "dram_gbs": round(traffic / (big_ms / 1e3) / 1e9, 1) if traffic else None,
+                "all_levels_gbs": round(kbytes / (kms / 1e3) / 1e9, 1),
                 "per_level_ms": {str(k): round(statistics.mean(v), 4) for k, v in sorted(per_level.items())},
                 "note": "algorithmic bytes = 2 x bytes_per_block per pair; the 8 (64, 512) pairs of a level "
                         "read 1 (8, 64) distinct source blocks, so L2 serves repeated reads",

@@ -302,3 +302,63 @@ def test_match_edge_cases():
     assert pool._tree._match_prefix_locked([100, 101, 102, 9]) == (-1, 0)
     node, mlen = pool.match_prefix_batch([[100, 101, 102], list(range(9)), []])
     assert mlen.tolist() == [0, 8, 0]
+
+
+@pytest.mark.parametrize("mode", ["tree", "levels"])
+def test_tot_device_tables(golden_dir, mode):
+    """The device-resident fan-out (SlabAllocator.fanout_tree / fanout_level)
+    ends in the reference's state: child tables, pairs, refcounts, free list,
+    and after freeing every child in creation order the same again."""
+    g = np.load(golden_dir / "tot_8b.npz")
+    spec = W.ToTSpec()
+    pool = _tot_pool()
+    a = pool._allocator
+    roots = a.alloc_batch(spec.root_tokens // 16)
+    if mode == "tree":
+        res = a.fanout_tree(roots, [spec.root_tokens // 16], spec.levels, spec.fanout, spec.appended_blocks)
+        tables, pairs = res["child_tables"], res["pairs"]
+    else:
+        tables, pairs = [], []
+        t, lens = roots, np.array([spec.root_tokens // 16])
+        for _ in range(spec.levels):
+            off = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)])).to(a.device)
+            r = a.fanout_level(t, off, lens, spec.fanout, spec.appended_blocks)
+            tables.append(r["child_tables"])
+            pairs.append(r["pairs"])
+            t, lens = r["child_tables"], r["child_lens"]
+    a.check()
+    np.testing.assert_array_equal(torch.cat(tables).cpu().numpy(), g["tables"])
+    for lvl in range(3):
+        np.testing.assert_array_equal(pairs[lvl].cpu().numpy(), g[f"pairs_l{lvl}"])
+    np.testing.assert_array_equal(a._ref_counts.cpu().numpy(), g["ref_fanout"])
+    np.testing.assert_array_equal(a.free_list(), g["free_fanout"])
+    st = json.loads(str(g["stats_fanout"]))
+    s = a.stats()
+    for k in ("free_blocks", "allocated_blocks", "peak_allocated", "total_allocs", "epoch"):
+        assert s[k] == st[k], k
+    a.dec_ref_batch(torch.cat(tables))
+    a.check()
+    np.testing.assert_array_equal(a._ref_counts.cpu().numpy(), g["ref_freed"])
+    np.testing.assert_array_equal(a.free_list(), g["free_freed"])
+    st = json.loads(str(g["stats_freed"]))
+    s = a.stats()
+    for k in ("free_blocks", "allocated_blocks", "total_frees", "epoch"):
+        assert s[k] == st[k], k
+
+
+def test_tot_fanout_copies_data():
+    """fanout_level with a real pool copies each child's CoW block bit-exactly."""
+    cfg = PoolConfig(total_blocks=400, block_size=16, num_layers=2, num_kv_heads=2, head_dim=64,
+                     dtype="bfloat16", device="cuda")
+    pool = AgentKVPool(config=cfg)
+    a = pool._allocator
+    a._kv_data.view(torch.int16).random_(-30000, 30000)
+    roots = a.alloc_batch(6)
+    off = torch.tensor([0, 3, 6], dtype=torch.int64, device=a.device)
+    before = a._kv_data.clone()
+    r = a.fanout_level(roots, off, [3, 3], 4, 2)
+    a.check()
+    pairs = r["pairs"].cpu().numpy()
+    assert len(pairs) == 8
+    for s_, d_ in pairs:
+        assert torch.equal(a._kv_data[d_].view(torch.int16), before[s_].view(torch.int16))
