@@ -58,6 +58,7 @@ CTL_ADVANCES = 13
 CTL_RELEASED = 14
 CTL_WORDS = 16
 AUX_WORDS = 2048
+NOALLOC_MAX_BLOCKS = 262144
 
 # Copy kernel variants (akv_copy_blocks_variant).
 VARIANT_AUTO = 0
@@ -133,6 +134,10 @@ SIGNATURES = {
     "akv_alloc_batch": (C.c_int, [C.POINTER(AkvAllocState), _I32, _P, C.POINTER(AkvTick), _P, _P]),
     "akv_incref_batch": (C.c_int, [C.POINTER(AkvAllocState), _P, _I32, C.POINTER(AkvTick), _P, _P]),
     "akv_decref_batch": (
+        C.c_int,
+        [C.POINTER(AkvAllocState), _P, _I32, C.POINTER(AkvTick), _P, _P, _P],
+    ),
+    "akv_decref_batch_noalloc": (
         C.c_int,
         [C.POINTER(AkvAllocState), _P, _I32, C.POINTER(AkvTick), _P, _P, _P],
     ),

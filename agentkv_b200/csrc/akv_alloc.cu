@@ -32,6 +32,7 @@
 //   * whatever sat in deferred when the batch started is drained at the
 //     batch's first tick — after op 0 has done its own pop / retire.
 #include <algorithm>
+#include <mutex>
 
 #include "akv_common.cuh"
 
@@ -701,5 +702,89 @@ extern "C" int akv_cow_batch(const AkvAllocState* st, void* pool, int64_t bytes_
       if (rc != AKV_OK) return rc;
     }
   }
+  return AKV_OK;
+}
+
+// ── dec_ref batch without caller-provided scratch ──────────────────────────
+// For callers that cannot allocate device memory at the point where they free
+// blocks: a block manager running inside a serving engine's memory-pool hook
+// or after the engine has reserved all free GPU memory up front, where a
+// cudaMalloc (or a framework allocation) would fail or re-enter the pool.
+// The per-id work space of the dec_ref batch lives in this file-scope device
+// array instead of the AkvAllocState's scratch pointers.  Every GPU that loads
+// the library holds it (2 MiB + 8 KiB) until the process exits.
+namespace {
+
+constexpr int32_t kNoAllocMaxBlocks = AKV_NOALLOC_MAX_BLOCKS;
+constexpr int64_t kNoAllocWords = 2 * static_cast<int64_t>(kNoAllocMaxBlocks) + AKV_AUX_WORDS;
+
+static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocWords];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+int32_t* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device.  In host code the symbol itself is only a host-side stand-in:
+// passing it to a kernel would fault, so kernels get this address.
+int noalloc_scratch(int32_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return akv_cuda_fail(e, "akv_decref_batch_noalloc: cudaGetDevice");
+  AKV_ARG_CHECK(dev >= 0 && dev < kNoAllocMaxDevices, "akv_decref_batch_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return akv_cuda_fail(e, "akv_decref_batch_noalloc: cudaGetSymbolAddress");
+    g_noalloc_ptr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return AKV_OK;
+}
+
+}  // namespace
+
+extern "C" int akv_decref_batch_noalloc(const AkvAllocState* st, const int32_t* ids, int32_t n,
+                                        const AkvTick* tick, int32_t* retired_out,
+                                        AkvStatus* status, void* stream) {
+  AKV_ARG_CHECK(st != nullptr && st->ref_counts && st->free_ring && st->limbo_ids &&
+                    st->limbo_epochs && st->ctl && st->total_blocks > 0,
+                "akv_decref_batch_noalloc: incomplete allocator state");
+  AKV_ARG_CHECK(st->total_blocks <= kNoAllocMaxBlocks,
+                "akv_decref_batch_noalloc: total_blocks=%d exceeds the %d blocks its static "
+                "scratch covers; use akv_decref_batch with caller-provided scratch",
+                st->total_blocks, kNoAllocMaxBlocks);
+  AKV_ARG_CHECK(tick != nullptr && tick->epoch_interval > 0, "akv_decref_batch_noalloc: bad tick");
+  AKV_ARG_CHECK(status != nullptr, "akv_decref_batch_noalloc: status is NULL");
+  AKV_ARG_CHECK(n >= 0, "akv_decref_batch_noalloc: n=%d < 0", n);
+  if (n == 0) return AKV_OK;
+  AKV_ARG_CHECK(ids != nullptr, "akv_decref_batch_noalloc: ids is NULL");
+  int32_t* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != AKV_OK) return rc;
+  AkvAllocState s2 = *st;
+  s2.scratch_count = scratch;
+  s2.scratch_last = scratch + kNoAllocMaxBlocks;
+  s2.scratch_aux = scratch + 2 * static_cast<int64_t>(kNoAllocMaxBlocks);
+  cudaStream_t s = akv_stream(stream);
+  // The array keeps whatever the previous call left; the counters must start
+  // at zero.
+  const size_t bytes = static_cast<size_t>(st->total_blocks) * sizeof(int32_t);
+  cudaError_t e = cudaMemsetAsync(s2.scratch_count, 0, bytes, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(s2.scratch_last, 0, bytes, s);
+  if (e != cudaSuccess) return akv_cuda_fail(e, "akv_decref_batch_noalloc: clear scratch");
+  const int n_ctas = grid_for(n, kDecThreads, kDecMaxCtas);
+  const int32_t chunk = akv_ceil_div(n, n_ctas);
+  int32_t* cta_counts = s2.scratch_aux;
+  DecPlan* plan = reinterpret_cast<DecPlan*>(s2.scratch_aux + AKV_AUX_PLAN_OFFSET);
+  k_dec_count<<<grid_for(n, 256, kAkvSMs * 4), 256, 0, s>>>(s2, ids, n, status);
+  AKV_LAUNCH_CHECK("akv_decref_batch_noalloc(count)");
+  k_dec_flag<<<n_ctas, kDecThreads, 0, s>>>(s2, ids, n, chunk, cta_counts, status);
+  AKV_LAUNCH_CHECK("akv_decref_batch_noalloc(flag)");
+  k_dec_plan<<<1, 1024, 0, s>>>(s2, n, n_ctas, cta_counts, ids, plan, *tick, status);
+  AKV_LAUNCH_CHECK("akv_decref_batch_noalloc(plan)");
+  k_dec_apply<<<n_ctas, kDecThreads, 0, s>>>(s2, ids, n, chunk, cta_counts, plan, retired_out, *tick);
+  AKV_LAUNCH_CHECK("akv_decref_batch_noalloc(apply)");
   return AKV_OK;
 }

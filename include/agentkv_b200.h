@@ -215,6 +215,27 @@ AKV_API int akv_decref_batch(const AkvAllocState* st, const int32_t* ids, int32_
                      const AkvTick* tick, int32_t* retired_out,
                      AkvStatus* status, void* stream);
 
+/* akv_decref_batch for callers that cannot allocate device memory where they
+ * free blocks (a block manager called from a serving engine's memory-pool
+ * hook, or running after the engine reserved all free GPU memory up front,
+ * where a cudaMalloc would fail or re-enter the pool).  No counterpart in the
+ * reference.  Same arguments and results as akv_decref_batch; the state's
+ * scratch_count / scratch_last / scratch_aux pointers are ignored (they may
+ * be NULL) and a static device array inside the library is used instead:
+ *   - it covers total_blocks <= AKV_NOALLOC_MAX_BLOCKS; larger states are
+ *     rejected with AKV_ERR_INVALID_ARG and nothing is enqueued;
+ *   - every GPU that loads the library holds it (2 MiB + 8 KiB) until exit;
+ *   - the first call on a device looks up its device address, so make that
+ *     first call before any stream capture;
+ *   - all calls in the process share it: calls whose kernels can overlap on
+ *     the GPU (different streams, or concurrent host threads) race; issue
+ *     them on one stream.
+ * Allocates nothing: no cudaMalloc, no cudaFree, no allocating library call. */
+#define AKV_NOALLOC_MAX_BLOCKS 262144
+AKV_API int akv_decref_batch_noalloc(const AkvAllocState* st, const int32_t* ids, int32_t n,
+                                     const AkvTick* tick, int32_t* retired_out,
+                                     AkvStatus* status, void* stream);
+
 /* EpochReclaimer._try_retire (reclamation.py:147-173): release every pending
  * id whose epoch is < safe_before_epoch, in FIFO order (INT64_MAX releases
  * all).  Released ids join the free list at the next allocator op. */

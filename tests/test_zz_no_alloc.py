@@ -1,0 +1,96 @@
+"""akv_decref_batch_noalloc — the dec_ref batch for callers that cannot
+allocate device memory where they free blocks (for example a block manager
+called from a serving engine's memory-pool hook, or one running after the
+engine reserved all free GPU memory up front).  It keeps its work space in a
+static device array inside the library instead of caller-provided scratch.
+
+Checked through the C ABI against akv_decref_batch on identical allocator
+states, for two calls in a row: refcounts, free-list order, reclaimer
+queues, counters and the retired ids must be identical (integer work:
+bit-exact).  This file is collected last so that a failure here leaves
+every other test already run.
+"""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from agentkv_b200 import _native as N
+from agentkv_b200.allocator import SlabAllocator
+from agentkv_b200.config import PoolConfig
+
+pytestmark = pytest.mark.gpu
+
+
+def _alloc(n):
+    cfg = PoolConfig(total_blocks=n, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1,
+                     dtype="float16", device="meta", epoch_interval=7)
+    return SlabAllocator(cfg)
+
+
+def _state(a: SlabAllocator):
+    c = a.ctl()
+    deferred, pending, eps = a.limbo()
+    return {"ref": a._ref_counts.cpu().numpy(), "free": a.free_list(), "deferred": deferred,
+            "pending": pending, "eps": eps, "ctl": np.delete(c, N.CTL_DONE)}
+
+
+def _same(a, b):
+    sa, sb = _state(a), _state(b)
+    for k in sa:
+        np.testing.assert_array_equal(sa[k], sb[k], err_msg=k)
+
+
+def test_noalloc_decref_matches_decref_batch():
+    n_blocks = 5000
+    rng = np.random.default_rng(2024)
+    a, b = _alloc(n_blocks), _alloc(n_blocks)
+    for x in (a, b):
+        x.alloc_batch(3000)
+    live = a.alloc_batch(0)  # no-op, keeps both states identical
+    ids = np.arange(n_blocks - 3000, n_blocks, dtype=np.int32)[::-1].copy()
+    extra = np.repeat(ids, rng.integers(0, 3, size=len(ids)))
+    for x in (a, b):
+        x.inc_ref_batch(extra)
+    a.check()
+    b.check()
+    _same(a, b)
+    refs = a._ref_counts.cpu().numpy()
+    # b's state with its scratch pointers removed: the entry point must not need them
+    st = N.AkvAllocState.from_buffer_copy(b._state)
+    st.scratch_count = None
+    st.scratch_last = None
+    st.scratch_aux = None
+    stream = torch.cuda.current_stream(b.device).cuda_stream
+    for call in range(2):
+        alive = ids[refs[ids] > 0]
+        pick = rng.choice(alive, size=1200, replace=False)
+        decs = np.concatenate([np.repeat(pick[:700], refs[pick[:700]]), pick[700:]]).astype(np.int32)
+        rng.shuffle(decs)
+        out_a = torch.full((len(decs),), -1, dtype=torch.int32, device=a.device)
+        out_b = torch.full((len(decs),), -1, dtype=torch.int32, device=b.device)
+        a.dec_ref_batch(decs, retired_out=out_a)
+        d = torch.from_numpy(decs).to(b.device)
+        rc = N.lib.akv_decref_batch_noalloc(C.byref(st), d.data_ptr(), len(decs), b._tick(), out_b.data_ptr(),
+                                            b._status.data_ptr(), stream)
+        assert rc == N.AKV_OK, N.last_error()
+        a.check()
+        b.check()
+        _same(a, b)
+        n_ret = int(a.ctl()[N.CTL_LAST_RETIRED])
+        assert n_ret > 0
+        np.testing.assert_array_equal(out_a.cpu().numpy(), out_b.cpu().numpy())
+        refs = a._ref_counts.cpu().numpy()
+    del live
+
+
+def test_noalloc_rejects_states_beyond_its_scratch():
+    big = _alloc(N.NOALLOC_MAX_BLOCKS + 1)
+    ids = torch.zeros(1, dtype=torch.int32, device=big.device)
+    rc = N.lib.akv_decref_batch_noalloc(big._state, ids.data_ptr(), 1, big._tick(), None,
+                                        big._status.data_ptr(), torch.cuda.current_stream(big.device).cuda_stream)
+    assert rc == N.AKV_ERR_INVALID_ARG
+    assert "exceeds" in N.last_error()
+    assert int(big._ref_counts[0].item()) == 0
