@@ -1,0 +1,65 @@
+"""KV-head sharding of the block pool across the GPUs of one node.
+
+Every block `[L, 2, H, bs, D]` splits by KV head: with `world` ranks, rank r
+holds heads [r*H/world, (r+1)*H/world) of every block, as one contiguous
+span per block (`[N, L, 2, H/world, bs, D]`).  All ranks use the same global
+block ids, so a copy-on-write pair (src, dst) is the same pair on every rank
+and each rank copies only its own slice: no KV byte crosses a GPU.
+
+Rank `src` (0) owns the allocator and the tree; after planning a batch it
+broadcasts the int32 pair list (8 B per pair) over the process group — NCCL
+over NVLink on GPUs — and every rank runs akv_copy_blocks on its slice.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import kernels as K
+
+
+def heads_per_rank(num_kv_heads: int, world: int) -> int:
+    if world < 1 or num_kv_heads % world:
+        raise ValueError(f"{world} ranks do not divide {num_kv_heads} KV heads")
+    return num_kv_heads // world
+
+
+def slice_shape(total_blocks: int, num_layers: int, num_kv_heads: int, block_size: int, head_dim: int,
+                world: int) -> tuple:
+    return (total_blocks, num_layers, 2, heads_per_rank(num_kv_heads, world), block_size, head_dim)
+
+
+def head_slice(pool: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Rank `rank`'s heads of a full pool tensor [N, L, 2, H, bs, D] (a view)."""
+    h = heads_per_rank(pool.shape[3], world)
+    return pool[:, :, :, rank * h : (rank + 1) * h]
+
+
+class ShardedCopier:
+    """Applies rank 0's copy batches to this rank's head slice."""
+
+    def __init__(self, pool_slice: torch.Tensor, group=None, src: int = 0) -> None:
+        import torch.distributed as dist
+
+        self.pool = pool_slice
+        self.group = group
+        self.src = src
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+
+    def share_pairs(self, pairs: Optional[torch.Tensor], n_pairs: int, out: Optional[torch.Tensor] = None):
+        """Rank src passes its (n, 2) int32 pair list, the others receive it."""
+        import torch.distributed as dist
+
+        if self.rank == self.src:
+            buf = pairs.reshape(-1, 2)
+        else:
+            buf = out if out is not None else torch.empty((n_pairs, 2), dtype=torch.int32, device=self.pool.device)
+        if self.world > 1:
+            dist.broadcast(buf, src=self.src, group=self.group)
+        return buf
+
+    def copy(self, pairs: torch.Tensor, **kw) -> None:
+        K.copy_blocks(self.pool, pairs, **kw)

@@ -68,6 +68,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every kernel from Python each step")
+    ap.add_argument("--graph-nccl", type=int, default=1,
+                    help="N > 1: capture the step, NCCL pair broadcast included, as a CUDA graph")
     ap.add_argument("--match", action="store_true", help="also time match_prefix on the stress tree")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--case", default="tot", choices=["tot", "sweep"],
@@ -183,6 +185,9 @@ class ToTBench:
             np.cumsum(lens, out=off[1:])
             self.level_off.append(torch.from_numpy(off).to(self.dev))
         self.pairs_bufs = [torch.empty((n, 2), dtype=torch.int32, device=self.dev) for n in self.pairs_per_level]
+        from agentkv_b200.sharded import ShardedCopier
+
+        self.copier = ShardedCopier(self.pool)
         if rank == 0:
             cfg = PoolConfig(total_blocks=self.n_blocks, block_size=bs, num_layers=L, num_kv_heads=H,
                              head_dim=D, dtype=dt, device="meta")
@@ -245,12 +250,11 @@ class ToTBench:
                 cs.wait_event(events[lvl])
             else:
                 pairs = self.pairs_bufs[lvl]
-            if self.world > 1:
-                torch.distributed.broadcast(pairs, src=0)
+            pairs = self.copier.share_pairs(pairs, n_pairs, out=self.pairs_bufs[lvl])
             if time_copies:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(cs)
-            K.copy_blocks(self.pool, pairs, variant=self.variant)
+            self.copier.copy(pairs, variant=self.variant)
             launches += 1
             if time_copies:
                 e1.record(cs)
@@ -266,10 +270,12 @@ class ToTBench:
         return h2d, d2h
 
     def capture(self):
-        """Record one step as a CUDA graph (single GPU); returns the graph."""
+        """Record one step as a CUDA graph; returns the graph.  With N ranks
+        every rank captures its own step (the pair broadcast included) and
+        the ranks replay in lockstep."""
         torch = self.torch
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
             self.step(capture=True)
         return g
 
@@ -534,15 +540,18 @@ def main():
                                              device_id=torch.device("cuda", local))
     bench = ToTBench(rank, world, args.blocks, args.variant)
     graph = None
-    if world == 1 and not args.no_graph:
+    if not args.no_graph and (world == 1 or args.graph_nccl):
         for _ in range(2):  # load every kernel and settle the allocator pools before capture
             bench.step()
         bench.join()
         torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
         graph = bench.capture()
         run_step = graph.replay
     else:
         run_step = bench.step
+    use_graph = graph is not None
     sampler = ClockSampler(local)
     with sampler:
         ms, wall = timed(run_step, args.steps, args.warmup, world, join=bench.join)
@@ -602,6 +611,8 @@ def main():
 
     if world > 1:
         torch.distributed.barrier()
+    torch.cuda.synchronize()
+    del graph, run_step  # a graph holding NCCL calls must go before the process group
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -625,7 +636,7 @@ def main():
                 "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
                 "l2": "inputs larger than L2 (each step touches ~2.4 GB per GPU)",
                 "copy_variant": args.variant,
-                "cuda_graph": graph is not None,
+                "cuda_graph": use_graph,
             },
             "roofline": {
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

@@ -1,0 +1,91 @@
+"""Host-side logic of the KV-head sharded pool with 2 CPU ranks (gloo).
+
+Rank 0 plans a batch of copy-on-write pairs (with the oracle's allocator as
+the planner stand-in on CPU), shares it through ShardedCopier.share_pairs,
+and each rank applies the pairs to its own head slice (with the oracle's
+copy, since the product copy kernel needs a GPU).  Reassembled, the slices
+must equal the full pool after the same copies: sharding by head loses
+nothing and the broadcast delivers rank 0's exact list.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from agentkv_b200 import sharded as S
+
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import oracle as O
+
+        n, L, H, bs, D = 24, 2, 4, 4, 8
+        g = torch.Generator().manual_seed(5)
+        full = torch.randint(-(2**30), 2**30, (n, L, 2, H, bs, D), dtype=torch.int32, generator=g)
+        mine = S.head_slice(full, rank, world).contiguous()
+        copier = S.ShardedCopier(mine)
+        if rank == 0:
+            a = O.OracleAllocator(n)
+            a.alloc_batch(8)
+            src = np.arange(n - 8, n, dtype=np.int32)
+            dst = a.alloc_batch(8)
+            pairs = torch.from_numpy(np.stack([src, dst], 1).astype(np.int32))
+        else:
+            pairs = None
+        got = copier.share_pairs(pairs, 8)
+        host = mine.numpy().view(np.uint8).reshape(n, -1).copy()
+        O.copy_blocks(host, host.shape[1], got.numpy())
+        mine_after = torch.from_numpy(host.view(np.int32).reshape(mine.shape))
+        parts = [torch.empty_like(mine_after) for _ in range(world)]
+        dist.all_gather(parts, mine_after)
+        all_pairs = [torch.empty_like(got) for _ in range(world)]
+        dist.all_gather(all_pairs, got)
+        if rank == 0:
+            fhost = full.numpy().view(np.uint8).reshape(n, -1).copy()
+            O.copy_blocks(fhost, fhost.shape[1], got.numpy())
+            want = torch.from_numpy(fhost.view(np.int32).reshape(full.shape))
+            re = torch.cat(parts, dim=3)
+            q.put((bool(torch.equal(re, want)), bool(torch.equal(all_pairs[0], all_pairs[1]))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_pairs_and_slices_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    same_pool, same_pairs = q.get(timeout=5)
+    assert same_pairs, "ranks saw different pair lists"
+    assert same_pool, "reassembled head slices differ from the unsharded copy"
+
+
+def test_head_slicing_math():
+    assert S.heads_per_rank(8, 8) == 1 and S.heads_per_rank(8, 2) == 4
+    with pytest.raises(ValueError):
+        S.heads_per_rank(8, 3)
+    assert S.slice_shape(100, 32, 8, 16, 128, 4) == (100, 32, 2, 2, 16, 128)
+    full = torch.arange(2 * 1 * 2 * 8 * 1 * 1).reshape(2, 1, 2, 8, 1, 1)
+    parts = [S.head_slice(full, r, 4) for r in range(4)]
+    assert torch.equal(torch.cat(parts, dim=3), full)
