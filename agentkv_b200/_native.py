@@ -154,6 +154,10 @@ SIGNATURES = {
         C.c_int,
         [C.POINTER(AkvTreeView), _P, _P, _I32, _I32, _P, _P, _P, _P, _P],
     ),
+    "akv_match_prefix_variant": (
+        C.c_int,
+        [C.POINTER(AkvTreeView), _P, _P, _I32, _I32, _P, _P, _P, _P, _P, _I32, _P],
+    ),
 }
 
 

@@ -188,10 +188,14 @@ struct BulkDesc {
 // One issuing thread per CTA.  Items are (pair, chunk) in the global order
 // t = blockIdx.x + j * gridDim.x; invalid pairs are skipped by the load cursor
 // and the store cursor replays the loads' descriptors from shared memory.
+// CHUNK bytes per bulk copy, STAGES chunks in flight.
+template <int CHUNK, int STAGES>
 __global__ void __launch_bounds__(32)
 k_copy_bulk(char* __restrict__ pool, int64_t bpb, int32_t total,
             const int32_t* __restrict__ pairs, int32_t n_pairs, int64_t chunks_per_block,
             const int32_t* __restrict__ refs, AkvStatus* st, const int64_t* __restrict__ n_dev) {
+  constexpr int kBulkChunk = CHUNK;
+  constexpr int kBulkStages = STAGES;
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ __align__(8) uint64_t bars[kBulkStages];
   __shared__ BulkDesc desc[kBulkStages];
@@ -407,22 +411,38 @@ bool bulk_eligible(const void* pool, int64_t bpb) {
   return (reinterpret_cast<uintptr_t>(pool) % 16 == 0) && (bpb % 16 == 0);
 }
 
-int copy_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* pairs, int32_t n,
-                     const int32_t* refs, AkvStatus* st, cudaStream_t s,
-                     const int64_t* n_dev = nullptr) {
+template <int CHUNK, int STAGES, int CTAS_PER_SM>
+int copy_bulk_launch_t(char* pool, int64_t bpb, int32_t total, const int32_t* pairs, int32_t n,
+                       const int32_t* refs, AkvStatus* st, cudaStream_t s, const int64_t* n_dev) {
   static thread_local bool attr_set = false;
-  const int smem = kBulkStages * kBulkChunk;
+  const int smem = STAGES * CHUNK;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_copy_bulk, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(k_copy_bulk<CHUNK, STAGES>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return akv_cuda_fail(e, "akv_copy_blocks(bulk): smem attribute");
     attr_set = true;
   }
-  const int64_t chunks = (bpb + kBulkChunk - 1) / kBulkChunk;
+  const int64_t chunks = (bpb + CHUNK - 1) / CHUNK;
   const int64_t work = chunks * n;
-  const int grid = static_cast<int>(work < kAkvSMs ? work : kAkvSMs);
-  k_copy_bulk<<<grid, 32, smem, s>>>(pool, bpb, total, pairs, n, chunks, refs, st, n_dev);
+  const int64_t max_grid = static_cast<int64_t>(kAkvSMs) * CTAS_PER_SM;
+  const int grid = static_cast<int>(work < max_grid ? work : max_grid);
+  k_copy_bulk<CHUNK, STAGES><<<grid, 32, smem, s>>>(pool, bpb, total, pairs, n, chunks, refs, st, n_dev);
   AKV_LAUNCH_CHECK("akv_copy_blocks(bulk)");
   return AKV_OK;
+}
+
+// Bulk-copy shapes (chunk bytes, chunks in flight, CTAs per SM), variant 2 first.
+int copy_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* pairs, int32_t n,
+                     const int32_t* refs, AkvStatus* st, cudaStream_t s,
+                     const int64_t* n_dev = nullptr, int shape = 0) {
+  switch (shape) {
+    case 1: return copy_bulk_launch_t<16384, 12, 1>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+    case 2: return copy_bulk_launch_t<32768, 3, 2>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+    case 3: return copy_bulk_launch_t<65536, 3, 1>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+    case 4: return copy_bulk_launch_t<16384, 6, 2>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+    case 5: return copy_bulk_launch_t<8192, 24, 1>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+    default: return copy_bulk_launch_t<32768, 6, 1>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+  }
 }
 
 int zero_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* ids, int32_t n,
@@ -460,14 +480,15 @@ extern "C" int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int3
   AKV_ARG_CHECK(bytes_per_block > 0, "akv_copy_blocks: bytes_per_block=%lld",
                 static_cast<long long>(bytes_per_block));
   AKV_ARG_CHECK(total_blocks > 0, "akv_copy_blocks: total_blocks=%d", total_blocks);
-  AKV_ARG_CHECK(variant >= 0 && variant <= 2, "akv_copy_blocks: unknown variant %d", variant);
+  AKV_ARG_CHECK(variant >= 0 && variant <= 7, "akv_copy_blocks: unknown variant %d", variant);
   char* p = static_cast<char*>(pool);
   cudaStream_t s = akv_stream(stream);
   // Automatic choice: the bulk-async engine whenever the spans are 16-byte
   // aligned (measured faster from 64 pairs of 2 MiB up, equal below).
   if (variant == 0) variant = bulk_eligible(pool, bytes_per_block) ? 2 : 1;
-  if (variant == 2 && bulk_eligible(pool, bytes_per_block))
-    return copy_bulk_launch(p, bytes_per_block, total_blocks, pairs, n_pairs, ref_counts, status, s);
+  if (variant >= 2 && bulk_eligible(pool, bytes_per_block))
+    return copy_bulk_launch(p, bytes_per_block, total_blocks, pairs, n_pairs, ref_counts, status, s,
+                            nullptr, variant - 2);
   return copy_vec_dispatch(p, bytes_per_block, total_blocks, pairs, n_pairs, ref_counts, status, s);
 }
 

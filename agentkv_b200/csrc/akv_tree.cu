@@ -6,7 +6,8 @@
 //       append-only token arena (an edge split only narrows ranges);
 //   slots — every node's `children` dict (first edge token → child id) as one
 //       open-addressing hash table keyed by (parent id, first token), 16 bytes
-//       per slot, linear probing, -1 = empty, -2 = deleted.
+//       per slot {parent, token, child, child's edge length}, linear probing,
+//       -1 = empty, -2 = deleted.
 // The host applies every tree mutation to its mirror and ships the changed
 // slots / node ranges as a delta (akv_tree_apply); new edge tokens are
 // appended to the arena with a plain copy.
@@ -14,17 +15,18 @@
 // match_prefix runs one warp per query and restates
 // DualRadixTree._match_prefix_locked (radix_tree.py:513-570):
 //   from the root, look up the child keyed by the next query token; compare
-//   the child's edge with the query (32 tokens per step, __ballot_sync +
-//   __ffs find the first mismatch); stop on a missing child, a mismatch
-//   anywhere in the edge or a query that ends inside the edge (a partial edge
-//   earns no credit); otherwise descend.  The match is floored to the block
-//   size; a zero match reports (-1, 0).
+//   the child's edge with the query (__ballot_sync + __ffs find the first
+//   mismatch); stop on a missing child, a mismatch anywhere in the edge or a
+//   query that ends inside the edge (a partial edge earns no credit);
+//   otherwise descend.  The match is floored to the block size; a zero match
+//   reports (-1, 0).  The walk chases up to 32 hops ahead and verifies their
+//   edges together (see k_match).
 #include "akv_common.cuh"
 
 namespace {
 
 constexpr int kEmpty = -1;  // a deleted slot holds parent -2 and never matches
-constexpr int kMatchWarpsPerCta = 8;
+constexpr int kMatchWarpsPerCta = 4;
 
 AKV_DEV uint32_t tree_hash(int32_t parent, int32_t token) {
   // MurmurHash3's 64-bit finalizer over (parent, token).
@@ -38,24 +40,31 @@ AKV_DEV uint32_t tree_hash(int32_t parent, int32_t token) {
   return static_cast<uint32_t>(k);
 }
 
-// Warp-cooperative lookup of (parent, token): each step reads 32 consecutive
-// slots (512 B), the first matching lane wins; an empty slot before any match
-// ends the probe.  Returns the child id or -1.
+// Warp-cooperative lookup of (parent, token): each step reads kProbe
+// consecutive slots (one 128-byte line), lane i the i-th; the first matching
+// slot wins; an empty slot before any match ends the probe.  The table is at
+// most half full, so a key almost always sits in the first line.  Returns the
+// child id (or -1) and its edge length.
+constexpr int kProbe = 8;
+
 AKV_DEV int32_t warp_lookup(const int4* __restrict__ slots, int32_t mask, int32_t parent,
-                            int32_t token, int lane) {
+                            int32_t token, int lane, int32_t& child_len) {
   const uint32_t h = tree_hash(parent, token);
-  const int32_t windows = (mask >> 5) + 1;
+  const int32_t windows = (mask + 1) / kProbe + 1;
   for (int32_t w = 0; w < windows; ++w) {
-    const uint32_t idx = (h + static_cast<uint32_t>(w) * 32u + static_cast<uint32_t>(lane)) &
-                         static_cast<uint32_t>(mask);
-    const int4 s = __ldg(&slots[idx]);
-    const uint32_t hit = __ballot_sync(0xffffffffu, s.x == parent && s.y == token);
-    const uint32_t empty = __ballot_sync(0xffffffffu, s.x == kEmpty);
+    int4 s = make_int4(kEmpty + 1, 0, 0, 0);  // lanes >= kProbe hold a non-matching, non-empty slot
+    if (lane < kProbe) {
+      const uint32_t idx = (h + static_cast<uint32_t>(w) * kProbe + static_cast<uint32_t>(lane)) &
+                           static_cast<uint32_t>(mask);
+      s = __ldg(&slots[idx]);
+    }
+    const uint32_t hit = __ballot_sync(0xffffffffu, lane < kProbe && s.x == parent && s.y == token);
+    const uint32_t empty = __ballot_sync(0xffffffffu, lane < kProbe && s.x == kEmpty);
     if (hit) {
-      // A key is only ever placed before the first empty slot of its probe.
       const int first_hit = __ffs(hit) - 1;
       const int first_empty = empty ? __ffs(empty) - 1 : 32;
       const int32_t c = __shfl_sync(0xffffffffu, s.z, first_hit);
+      child_len = __shfl_sync(0xffffffffu, s.w, first_hit);
       return first_hit < first_empty ? c : -1;
     }
     if (empty) return -1;
@@ -63,70 +72,204 @@ AKV_DEV int32_t warp_lookup(const int4* __restrict__ slots, int32_t mask, int32_
   return -1;
 }
 
+constexpr int kWinPerLane = 8;  // query tokens a lane keeps: a 256-token window per warp
+constexpr int kSegment = 32;    // hops chased before their edges are verified (one per lane)
+
+// One warp per query.  The walk alternates two phases:
+//  chase  — follow up to 32 hops using only each edge's first token: the next
+//           token position is the current depth plus the child's edge length,
+//           which the hash slot carries, and the query's tokens come from a
+//           256-token window held in registers, so a hop costs one dependent
+//           probe.  It stops at a missing child, at the end of the query, or
+//           at an edge that runs past the end of the query.
+//  verify — compare all tokens of the chased edges at once (their positions
+//           flattened across the warp) and find the first mismatch.  The
+//           reference's loop would have stopped at the first edge that
+//           mismatches or only partly fits; everything before it is matched.
+// Hops past a mismatch are speculation and are discarded.  The comparison
+// count is the one the reference's loop makes: every token of each fully
+// matched edge, plus, on the stopping edge, its matched tokens and the
+// mismatching one.
+template <int kVerifyChunks>
 __global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
 k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
         int32_t nq, int32_t block_size, int32_t* __restrict__ out_node,
-        int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared, AkvStatus* st) {
+        int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared,
+        const int32_t* __restrict__ order, AkvStatus* st) {
+  constexpr uint32_t kFull = 0xffffffffu;
   const int lane = threadIdx.x & 31;
-  const int32_t q = blockIdx.x * kMatchWarpsPerCta + (threadIdx.x >> 5);
-  if (q >= nq) return;
+  const int32_t w = blockIdx.x * kMatchWarpsPerCta + (threadIdx.x >> 5);
+  if (w >= nq) return;
+  // `order` (optional) lists the queries longest first, so the long walks
+  // start early and spread over the SMs.
+  const int32_t q = order != nullptr ? order[w] : w;
+  if (static_cast<uint32_t>(q) >= static_cast<uint32_t>(nq)) {
+    if (lane == 0) akv_fail(st, AKV_ERR_INVALID_ARG, w, q, nq);
+    return;
+  }
   const int64_t qlo = q_off[q];
   const int64_t L = q_off[q + 1] - qlo;
   const int32_t* __restrict__ Q = tokens + qlo;
   const int4* __restrict__ slots = reinterpret_cast<const int4*>(tree.slots);
+
+  int32_t win[kWinPerLane];
+  int64_t wbase = -(1LL << 40);
+  auto qtoken = [&](int64_t pos) -> int32_t {  // pos is warp-uniform and < L
+    if (pos < wbase || pos >= wbase + 32 * kWinPerLane) {
+      wbase = pos;
+#pragma unroll
+      for (int u = 0; u < kWinPerLane; ++u) {
+        const int64_t i = pos + u * 32 + lane;
+        win[u] = i < L ? Q[i] : 0;
+      }
+    }
+    const int64_t r = pos - wbase;
+    const int u = static_cast<int>(r >> 5);
+    int32_t v = 0;
+#pragma unroll
+    for (int uu = 0; uu < kWinPerLane; ++uu) v = (uu == u) ? win[uu] : v;
+    return __shfl_sync(kFull, v, static_cast<int>(r & 31));
+  };
+
   int32_t cur = 0;  // ROOT_NODE_ID
   int64_t matched = 0, compared = 0;
   bool bad = false;
-  while (matched < L) {
-    const int32_t t = Q[matched];
-    const int32_t child = warp_lookup(slots, tree.slot_mask, cur, t, lane);
-    if (child < 0) break;
-    if (child >= tree.n_nodes) {
-      bad = true;
-      if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, child, tree.n_nodes);
-      break;
-    }
-    const int64_t eoff = tree.node_edge_off[child];
-    const int64_t elen = tree.node_edge_len[child];
-    if (eoff < 0 || elen < 0 || eoff + elen > tree.n_tokens) {
-      bad = true;
-      if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, child, static_cast<int32_t>(elen), eoff);
-      break;
-    }
-    const int32_t* __restrict__ E = tree.tokens + eoff;
-    const int32_t* __restrict__ Qm = Q + matched;
-    const int64_t rem = L - matched;
-    const int64_t lim = elen < rem ? elen : rem;
-    int64_t em = lim;
-    bool mismatch = false;
-    // Two 32-token chunks per step keep two loads per array in flight.
-    for (int64_t base = 0; base < lim; base += 64) {
-      const int64_t i0 = base + lane, i1 = base + 32 + lane;
-      const bool ok0 = i0 < lim, ok1 = i1 < lim;
-      const int32_t a0 = ok0 ? Qm[i0] : 0, b0 = ok0 ? __ldg(&E[i0]) : 0;
-      const int32_t a1 = ok1 ? Qm[i1] : 0, b1 = ok1 ? __ldg(&E[i1]) : 0;
-      const uint32_t m0 = __ballot_sync(0xffffffffu, ok0 && a0 != b0);
-      const uint32_t m1 = __ballot_sync(0xffffffffu, ok1 && a1 != b1);
-      if (m0) {
-        em = base + __ffs(m0) - 1;
-        mismatch = true;
+  while (!bad) {
+    // ── chase ──
+    int n = 0;
+    int64_t d = matched;
+    int32_t node = cur;
+    bool last_segment = false;
+    int32_t my_child = -1, my_len = 0;
+    int64_t my_d = 0;
+    while (n < kSegment) {
+      if (d >= L) {
+        last_segment = true;
         break;
       }
-      if (m1) {
-        em = base + 32 + __ffs(m1) - 1;
-        mismatch = true;
+      const int32_t t = qtoken(d);
+      int32_t clen = 0;
+      const int32_t child = warp_lookup(slots, tree.slot_mask, node, t, lane, clen);
+      if (child < 0) {
+        last_segment = true;
         break;
       }
+      if (child >= tree.n_nodes || clen < 0) {
+        bad = true;
+        if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, child, tree.n_nodes);
+        break;
+      }
+      if (lane == n) {
+        my_child = child;
+        my_len = clen;
+        my_d = d;
+      }
+      ++n;
+      if (clen == 0 || d + clen > L) {  // empty edge / edge past the query end: the walk ends here
+        last_segment = true;
+        break;
+      }
+      d += clen;
+      node = child;
     }
-    // The reference evaluates `tokens[matched + i] != et` once per matched
-    // token plus once for the token that differs.
-    compared += em + (mismatch ? 1 : 0);
-    if (em == 0 || em < elen) break;
-    matched += elen;
-    cur = child;
+    if (bad || n == 0) break;
+    // ── verify ──
+    int64_t my_off = 0;
+    bool my_bad = false;
+    if (lane < n) {
+      my_off = tree.node_edge_off[my_child];
+      my_bad = my_off < 0 || my_off + my_len > tree.n_tokens ||
+               tree.node_edge_len[my_child] != my_len;
+    }
+    const uint32_t badm = __ballot_sync(kFull, my_bad);
+    if (badm) {
+      bad = true;
+      if (lane == __ffs(badm) - 1) akv_fail(st, AKV_ERR_TREE, q, my_child, my_len, my_off);
+      break;
+    }
+    const int32_t lim = lane < n ? static_cast<int32_t>(my_len < L - my_d ? my_len : L - my_d) : 0;
+    int32_t incl = lim;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int32_t excl = incl - lim;
+    const int32_t total = __shfl_sync(kFull, incl, 31);
+    // entry holding flattened position p: the last e < n with excl_e <= p
+    auto entry_of = [&](int32_t p) -> int {
+      int lo = 0, hi = n - 1;
+#pragma unroll
+      for (int k = 0; k < 5; ++k) {
+        const int mid = (lo + hi + 1) >> 1;
+        const int32_t v = __shfl_sync(kFull, excl, mid);
+        if (lo < hi) {
+          if (v <= p) lo = mid;
+          else hi = mid - 1;
+        }
+      }
+      return lo;
+    };
+    int32_t first = -1;
+    for (int32_t base = 0; base < total; base += 32 * kVerifyChunks) {
+      int32_t a[kVerifyChunks], b[kVerifyChunks];
+      // Fast path: the whole step lies inside one edge (long edges).
+      const int e0 = entry_of(base);
+      const int32_t ex0 = __shfl_sync(kFull, excl, e0);
+      const int32_t lim0 = __shfl_sync(kFull, lim, e0);
+      if (ex0 + lim0 >= base + 32 * kVerifyChunks || e0 == n - 1) {
+        const int64_t de = __shfl_sync(kFull, my_d, e0) - ex0;
+        const int64_t oe = __shfl_sync(kFull, my_off, e0) - ex0;
+#pragma unroll
+        for (int u = 0; u < kVerifyChunks; ++u) {
+          const int32_t p = base + u * 32 + lane;
+          const bool ok = p < total;
+          a[u] = ok ? Q[de + p] : 0;
+          b[u] = ok ? __ldg(&tree.tokens[oe + p]) : 0;
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < kVerifyChunks; ++u) {
+          const int32_t p = base + u * 32 + lane;
+          const int e = entry_of(p < total ? p : total - 1);
+          const int32_t j = p - __shfl_sync(kFull, excl, e);
+          const int64_t de = __shfl_sync(kFull, my_d, e);
+          const int64_t oe = __shfl_sync(kFull, my_off, e);
+          const bool ok = p < total;
+          a[u] = ok ? Q[de + j] : 0;
+          b[u] = ok ? __ldg(&tree.tokens[oe + j]) : 0;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kVerifyChunks; ++u) {
+        const uint32_t m = __ballot_sync(kFull, a[u] != b[u]);
+        if (m && first < 0) first = base + u * 32 + __ffs(m) - 1;
+      }
+      if (first >= 0) break;
+    }
+    // the first entry the reference would stop in
+    const int e_mis = first >= 0 ? entry_of(first) : kSegment;
+    const uint32_t short_m = __ballot_sync(kFull, lane < n && (lim < my_len || my_len == 0));
+    const int e_short = short_m ? __ffs(short_m) - 1 : kSegment;
+    const int e_stop = e_mis < e_short ? e_mis : e_short;
+    if (e_stop == kSegment) {  // every chased edge matched in full
+      compared += total;
+      matched = __shfl_sync(kFull, my_d, n - 1) + __shfl_sync(kFull, my_len, n - 1);
+      cur = __shfl_sync(kFull, my_child, n - 1);
+      if (last_segment) break;
+      continue;
+    }
+    const int32_t ex = __shfl_sync(kFull, excl, e_stop);
+    const bool mism = e_mis == e_stop;
+    const int32_t em = mism ? first - ex : __shfl_sync(kFull, lim, e_stop);
+    compared += ex + em + (mism ? 1 : 0);
+    matched = __shfl_sync(kFull, my_d, e_stop);
+    const int32_t prev_child = __shfl_sync(kFull, my_child, e_stop > 0 ? e_stop - 1 : 0);
+    cur = e_stop > 0 ? prev_child : cur;
+    break;
   }
   if (lane == 0) {
-    int64_t m = bad ? 0 : (matched / block_size) * block_size;
+    const int64_t m = bad ? 0 : (matched / block_size) * block_size;
     out_node[q] = m == 0 ? -1 : cur;
     out_len[q] = static_cast<int32_t>(m);
     if (out_compared != nullptr) out_compared[q] = compared;
@@ -140,12 +283,12 @@ __global__ void k_tree_apply(AkvTreeView tree, const int32_t* __restrict__ su, i
   int32_t* len = const_cast<int32_t*>(tree.node_edge_len);
   const int32_t stride = gridDim.x * blockDim.x;
   for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n_slot; i += stride) {
-    const int32_t slot = su[4 * i];
+    const int32_t slot = su[5 * i];
     if (slot < 0 || slot > tree.slot_mask) {
       akv_fail(st, AKV_ERR_TREE, i, slot, tree.slot_mask);
       continue;
     }
-    slots[slot] = make_int4(su[4 * i + 1], su[4 * i + 2], su[4 * i + 3], 0);
+    slots[slot] = make_int4(su[5 * i + 1], su[5 * i + 2], su[5 * i + 3], su[5 * i + 4]);
   }
   for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n_node; i += stride) {
     const int64_t node = nu[3 * i];
@@ -188,10 +331,11 @@ extern "C" int akv_tree_apply(const AkvTreeView* tree, const int32_t* slot_updat
   return AKV_OK;
 }
 
-extern "C" int akv_match_prefix(const AkvTreeView* tree, const int32_t* tokens, const int64_t* q_off,
-                                int32_t nq, int32_t block_size, int32_t* out_node,
-                                int32_t* out_len, int64_t* out_compared, AkvStatus* status,
-                                void* stream) {
+extern "C" int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* tokens,
+                                        const int64_t* q_off, int32_t nq, int32_t block_size,
+                                        int32_t* out_node, int32_t* out_len, int64_t* out_compared,
+                                        const int32_t* order, AkvStatus* status, int32_t chunks,
+                                        void* stream) {
   AKV_ARG_CHECK(tree != nullptr && tree->tokens && tree->node_edge_off && tree->node_edge_len &&
                     tree->slots,
                 "akv_match_prefix: incomplete tree view");
@@ -204,9 +348,40 @@ extern "C" int akv_match_prefix(const AkvTreeView* tree, const int32_t* tokens, 
   if (nq == 0) return AKV_OK;
   AKV_ARG_CHECK(tokens != nullptr && q_off != nullptr && out_node != nullptr && out_len != nullptr,
                 "akv_match_prefix: NULL query or output array");
+  AKV_ARG_CHECK(chunks == 0 || chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8,
+                "akv_match_prefix: chunks=%d not in {0,1,2,4,8}", chunks);
+  if (chunks == 0) chunks = 4;
   const int grid = akv_ceil_div(nq, kMatchWarpsPerCta);
-  k_match<<<grid, kMatchWarpsPerCta * 32, 0, akv_stream(stream)>>>(
-      *tree, tokens, q_off, nq, block_size, out_node, out_len, out_compared, status);
+  cudaStream_t s = akv_stream(stream);
+  switch (chunks) {
+    case 1:
+      k_match<1><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
+                                                          out_len, out_compared, order, status);
+      break;
+    case 4:
+      k_match<4><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
+                                                          out_len, out_compared, order, status);
+      break;
+    case 8:
+      k_match<8><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
+                                                          out_len, out_compared, order, status);
+      break;
+    case 2:
+      k_match<2><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
+                                                          out_len, out_compared, order, status);
+      break;
+    default:
+      k_match<4><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
+                                                          out_len, out_compared, order, status);
+  }
   AKV_LAUNCH_CHECK("akv_match_prefix");
   return AKV_OK;
+}
+
+extern "C" int akv_match_prefix(const AkvTreeView* tree, const int32_t* tokens, const int64_t* q_off,
+                                int32_t nq, int32_t block_size, int32_t* out_node,
+                                int32_t* out_len, int64_t* out_compared, AkvStatus* status,
+                                void* stream) {
+  return akv_match_prefix_variant(tree, tokens, q_off, nq, block_size, out_node, out_len, out_compared,
+                                  nullptr, status, 0, stream);
 }

@@ -9,7 +9,8 @@ as a delta before the next lookup:
                     tree's own node ids (an edge split only narrows ranges,
                     so no token is ever rewritten);
 * ``slots``         all nodes' ``children`` dicts as one open-addressing hash
-                    table of {parent, first token, child, 0} int32x4 slots,
+                    table of {parent, first token, child, child's edge length}
+                    int32x4 slots,
                     linear probing, parent -1 = empty, -2 = deleted.  The hash
                     is akv_tree_hash (MurmurHash3's 64-bit finalizer over
                     (parent, token)); ``tree_hash`` below is the same function
@@ -139,7 +140,9 @@ class DeviceTree:
             i = (i + 1) & mask
         return -1, free
 
-    def set_child(self, parent: int, token: int, child: int) -> None:
+    def set_child(self, parent: int, token: int, child: int, child_len: int) -> None:
+        """children[parent][token] = child; the slot also carries the child's
+        edge length (the device walk chases hops with it)."""
         key = (parent, token)
         s = self._slot_of.get(key)
         if s is None:
@@ -150,7 +153,7 @@ class DeviceTree:
                 self.dead -= 1
             self.live += 1
             self._slot_of[key] = s
-        self.h_slots[s] = (parent, token, child, 0)
+        self.h_slots[s] = (parent, token, child, child_len)
         self._dirty_slots.add(s)
 
     def del_child(self, parent: int, token: int) -> None:
@@ -167,15 +170,15 @@ class DeviceTree:
         while cap < 2 * min_slots:
             cap <<= 1
         cap = max(cap, 64)
-        entries = [(k, int(self.h_slots[s, 2])) for k, s in self._slot_of.items()]
+        entries = [(k, int(self.h_slots[s, 2]), int(self.h_slots[s, 3])) for k, s in self._slot_of.items()]
         self.h_slots = np.full((cap, 4), EMPTY, np.int32)
         self.h_slots[:, 3] = 0
         self._slot_of = {}
         self.live = self.dead = 0
         self._dirty_slots.clear()
-        for (p, t), c in entries:
+        for (p, t), c, ln in entries:
             _, s = self._probe(p, t)
-            self.h_slots[s] = (p, t, c, 0)
+            self.h_slots[s] = (p, t, c, ln)
             self._slot_of[(p, t)] = s
             self.live += 1
         self._full = True
@@ -213,9 +216,9 @@ class DeviceTree:
         nu = None
         if self._dirty_slots:
             idx = np.fromiter(self._dirty_slots, np.int64, len(self._dirty_slots))
-            su = np.empty((len(idx), 4), np.int32)
+            su = np.empty((len(idx), 5), np.int32)
             su[:, 0] = idx
-            su[:, 1:] = self.h_slots[idx, :3]
+            su[:, 1:] = self.h_slots[idx, :4]
         if self._dirty_nodes:
             idx = np.fromiter(self._dirty_nodes, np.int64, len(self._dirty_nodes))
             nu = np.empty((len(idx), 3), np.int64)
@@ -240,14 +243,17 @@ class DeviceTree:
 
     # ── lookups ──────────────────────────────────────────────────────────────
     def match(self, tokens: torch.Tensor, q_off: torch.Tensor, nq: int, block_size: int,
-              out_node: torch.Tensor, out_len: torch.Tensor, out_cmp: Optional[torch.Tensor]) -> None:
+              out_node: torch.Tensor, out_len: torch.Tensor, out_cmp: Optional[torch.Tensor],
+              chunks: int = 0, order: Optional[torch.Tensor] = None) -> None:
         """Enqueue akv_match_prefix for nq queries packed in `tokens` / `q_off`
-        (device int32 / int64 tensors)."""
+        (device int32 / int64 tensors); `order` (device int32) is the launch
+        order of the queries, longest first by default in pack_queries."""
         self.flush()
-        N.check(N.lib.akv_match_prefix(
+        N.check(N.lib.akv_match_prefix_variant(
             self.view(), tokens.data_ptr(), q_off.data_ptr(), nq, block_size, out_node.data_ptr(),
             out_len.data_ptr(), out_cmp.data_ptr() if out_cmp is not None else None,
-            self.status.data_ptr(), stream_handle(self.device)))
+            order.data_ptr() if order is not None else None, self.status.data_ptr(), chunks,
+            stream_handle(self.device)))
 
     def check(self) -> None:
         s = self.status.cpu()

@@ -323,10 +323,12 @@ class DualRadixTree:
             tok, q_off = pack_queries(queries, self._alloc.device)
             nq = len(queries)
             dev = self._alloc.device
+            lens = np.fromiter((len(q) for q in queries), np.int64, nq)
+            order = torch.from_numpy(np.argsort(-lens, kind="stable").astype(np.int32)).to(dev)
             node = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
             mlen = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
             cmp_ = torch.empty(max(nq, 1), dtype=torch.int64, device=dev) if with_compared else None
-            self._dev_tree.match(tok, q_off, nq, self._cfg.block_size, node, mlen, cmp_)
+            self._dev_tree.match(tok, q_off, nq, self._cfg.block_size, node, mlen, cmp_, order=order)
             self._dev_tree.check()
             res = (node[:nq].cpu().numpy(), mlen[:nq].cpu().numpy())
             if with_compared:
@@ -409,7 +411,7 @@ class DualRadixTree:
 
     def _set_child(self, parent: SharedNode, token: int, child_id: int) -> None:
         parent.children[token] = child_id
-        self._dev_tree.set_child(parent.node_id, token, child_id)
+        self._dev_tree.set_child(parent.node_id, token, child_id, self._shared_nodes[child_id].edge_len)
 
     def _insert_shared_locked(self, parent_id: int, tokens: np.ndarray, blocks: List[BlockHandle]) -> int:
         """Insert under parent, splitting an edge on a block boundary
@@ -520,6 +522,14 @@ def pack_queries(queries: Sequence, device: torch.device) -> Tuple[torch.Tensor,
     tok = torch.from_numpy(flat).pin_memory().to(device, non_blocking=True)
     off = torch.from_numpy(q_off).pin_memory().to(device, non_blocking=True)
     return tok, off
+
+
+def longest_first(q_off, device: torch.device) -> torch.Tensor:
+    """Launch order for akv_match_prefix: query indices by decreasing length
+    (stable), so the longest walks start first and spread over the SMs."""
+    q_off = np.asarray(q_off.cpu() if isinstance(q_off, torch.Tensor) else q_off, np.int64)
+    order = np.argsort(-np.diff(q_off), kind="stable").astype(np.int32)
+    return torch.from_numpy(order).pin_memory().to(device, non_blocking=True)
 
 
 CoWRadixTree = DualRadixTree

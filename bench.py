@@ -72,7 +72,9 @@ def parse_args():
                     help="N > 1: capture the step, NCCL pair broadcast included, as a CUDA graph")
     ap.add_argument("--match", action="store_true", help="also time match_prefix on the stress tree")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--case", default="tot", choices=["tot", "sweep"],
+    ap.add_argument("--match-seqs", type=int, default=W.MatchSpec.n_sequences)
+    ap.add_argument("--match-queries", type=int, default=W.MatchSpec.n_queries)
+    ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match"],
                     help="tot: the headline step; sweep: batched copy/zero sweep (prints its own line)")
     ap.add_argument("--batches", default="1,8,64,512,4096", help="sweep batch sizes")
     ap.add_argument("--rotations", type=int, default=8, help="sweep: distinct pair sets cycled")
@@ -398,13 +400,14 @@ def reference_arm(args, rank, world):
 
 
 # ── match_prefix figure ──────────────────────────────────────────────────────
-def match_figure(steps: int, warmup: int) -> dict:
+def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
+                 n_queries: int = W.MatchSpec.n_queries) -> dict:
     import torch
 
     from agentkv_b200 import AgentKVPool, PoolConfig
-    from agentkv_b200.radix_tree import pack_queries
+    from agentkv_b200.radix_tree import longest_first, pack_queries
 
-    spec = W.MatchSpec()
+    spec = W.MatchSpec(n_sequences=n_seqs, n_queries=n_queries)
     prefixes = W.match_prefixes(spec)
     corpus = W.match_sequences(spec, prefixes)
     total_blocks = sum(-(-len(s) // 16) for s in corpus) + 16
@@ -423,6 +426,7 @@ def match_figure(steps: int, warmup: int) -> dict:
     dev = pool._allocator.device
     batches = [W.match_queries(spec, corpus, prefixes, batch=b) for b in range(4)]
     packed = [pack_queries(q, dev) for q in batches]
+    orders = [longest_first(off, dev) for _, off in packed]
     nq = spec.n_queries
     node = torch.empty(nq, dtype=torch.int32, device=dev)
     mlen = torch.empty(nq, dtype=torch.int32, device=dev)
@@ -430,15 +434,15 @@ def match_figure(steps: int, warmup: int) -> dict:
     tree._dev_tree.flush()
     compared = []
     qtokens = []
-    for tok, off in packed:
-        tree._dev_tree.match(tok, off, nq, 16, node, mlen, cmp_)
+    for (tok, off), order in zip(packed, orders):
+        tree._dev_tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order)
         compared.append(int(cmp_.sum()))
         qtokens.append(int(off[-1]))
     tree._dev_tree.check()
 
     def run():
-        for tok, off in packed:
-            tree._dev_tree.match(tok, off, nq, 16, node, mlen, cmp_)
+        for (tok, off), order in zip(packed, orders):
+            tree._dev_tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order)
 
     ms, _ = timed(run, steps, warmup, 1)
     per_batch_ms = ms / (steps * len(packed))
@@ -481,9 +485,10 @@ def sweep_case(args) -> None:
         sets = [torch.from_numpy(W.copy_sweep_pairs(n, n_blocks, rotation=r)).to(dev)
                 for r in range(args.rotations)]
         dsts = [p_[:, 1].contiguous() for p_ in sets]
+        zv = args.variant if args.variant <= 2 else 0  # zero has no tuning shapes
         for i in range(args.warmup):
             K.copy_blocks(pool, sets[i % len(sets)], variant=args.variant)
-            K.zero_blocks(pool, dsts[i % len(dsts)], variant=args.variant)
+            K.zero_blocks(pool, dsts[i % len(dsts)], variant=zv)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -494,7 +499,7 @@ def sweep_case(args) -> None:
         c_ms = e0.elapsed_time(e1) / args.steps
         e0.record()
         for i in range(args.steps):
-            K.zero_blocks(pool, dsts[i % len(dsts)], variant=args.variant)
+            K.zero_blocks(pool, dsts[i % len(dsts)], variant=zv)
         e1.record()
         torch.cuda.synchronize()
         z_ms = e0.elapsed_time(e1) / args.steps
@@ -529,6 +534,12 @@ def main():
         return
     if args.case == "sweep":
         sweep_case(args)
+        return
+    if args.case == "match":
+        import torch
+
+        torch.cuda.set_device(0)
+        print(json.dumps(match_figure(args.steps, args.warmup, args.match_seqs, args.match_queries)), flush=True)
         return
     import torch
 
@@ -607,7 +618,8 @@ def main():
                "sample": f"{steps} Tree-of-Thought steps ({steps * 584} CoW copies of {bpb} B) on a "
                          f"4096-block host pool, {secs:.1f} s"}
 
-    match = match_figure(max(5, args.steps), args.warmup) if (args.match and rank == 0) else None
+    match = (match_figure(max(5, args.steps), args.warmup, args.match_seqs, args.match_queries)
+             if (args.match and rank == 0) else None)
 
     if world > 1:
         torch.distributed.barrier()

@@ -93,7 +93,10 @@ AKV_API int akv_copy_blocks(void* pool, int64_t bytes_per_block, int32_t total_b
                     const int32_t* ref_counts, AkvStatus* status, void* stream);
 
 /* Same, with an explicit kernel choice: 0 = automatic, 1 = 16-byte vector
- * loads/stores, 2 = bulk-async (TMA) copies staged through shared memory. */
+ * loads/stores, 2 = bulk-async (TMA) copies staged through shared memory
+ * (32 KiB chunks, 6 in flight, 1 CTA per SM); 3-7 = other bulk shapes
+ * (16 KiB x 12; 32 KiB x 3 with 2 CTAs per SM; 64 KiB x 3; 16 KiB x 6 with
+ * 2 CTAs per SM; 8 KiB x 24) for tuning. */
 AKV_API int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int32_t total_blocks,
                             const int32_t* pairs, int32_t n_pairs,
                             const int32_t* ref_counts, AkvStatus* status,
@@ -283,9 +286,10 @@ AKV_API int akv_fanout_plan(const int32_t* parent_tables, const int64_t* parent_
  * The replica mirrors the host tree's SharedNode table (:82-103):
  *   node_edge_off[cap] int64 — start of the node's edge in `tokens`
  *   node_edge_len[cap] int32 — edge length (0 for the root / unused ids)
- *   slots[mask+1]      int32x4 {parent, first_token, child, 0} — the
- *                      `children` dicts of all nodes as one open-addressing
- *                      hash table; parent = -1 empty, -2 deleted
+ *   slots[mask+1]      int32x4 {parent, first_token, child, child_edge_len}
+ *                      — the `children` dicts of all nodes as one
+ *                      open-addressing hash table; parent = -1 empty,
+ *                      -2 deleted
  * Node ids are the tree's own ids (root = 0).
  */
 typedef struct AkvTreeView {
@@ -302,8 +306,8 @@ typedef struct AkvTreeView {
  * the device lookup both use this function. */
 AKV_API uint32_t akv_tree_hash(int32_t parent, int32_t token);
 
-/* Apply a batch of replica updates: slot_updates int32 [n_slot][4]
- * {slot, parent, first_token, child}; node_updates int64 [n_node][3]
+/* Apply a batch of replica updates: slot_updates int32 [n_slot][5]
+ * {slot, parent, first_token, child, child_edge_len}; node_updates int64 [n_node][3]
  * {node, edge_off, edge_len}.  (Token arena appends are plain copies.) */
 AKV_API int akv_tree_apply(const AkvTreeView* tree, const int32_t* slot_updates, int32_t n_slot,
                    const int64_t* node_updates, int32_t n_node,
@@ -315,6 +319,16 @@ AKV_API int akv_tree_apply(const AkvTreeView* tree, const int32_t* slot_updates,
 AKV_API int akv_match_prefix(const AkvTreeView* tree, const int32_t* tokens, const int64_t* q_off,
                      int32_t nq, int32_t block_size, int32_t* out_node, int32_t* out_len,
                      int64_t* out_compared, AkvStatus* status, void* stream);
+
+/* Same, with an optional processing order (`order[nq]`, a permutation of
+ * the query indices; launching the longest queries first balances the SMs)
+ * and the number of 32-token chunks a warp compares per step (1, 2, 4 or 8;
+ * 0 = default) for tuning.  Outputs stay indexed by query. */
+AKV_API int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* tokens,
+                                     const int64_t* q_off, int32_t nq, int32_t block_size,
+                                     int32_t* out_node, int32_t* out_len, int64_t* out_compared,
+                                     const int32_t* order, AkvStatus* status, int32_t chunks,
+                                     void* stream);
 
 #ifdef __cplusplus
 }

@@ -67,7 +67,7 @@ def test_device_tree_hash_table_mirror():
         p, k = int(rng.integers(0, 40)), int(rng.integers(0, 12))
         if rng.random() < 0.65:
             c = int(rng.integers(1, 10_000))
-            t.set_child(p, k, c)
+            t.set_child(p, k, c, 3)
             ref[(p, k)] = c
         else:
             t.del_child(p, k)
