@@ -19,8 +19,11 @@ in HBM; each step touches ~2.4 GB, above the 126 MB L2.
 With N GPUs (torchrun, one process per GPU) the pool is sharded by KV head:
 each rank holds an 8/N-head slice of every block, and the step runs N trees
 (60,000 x N blocks), so the bytes each GPU moves per step stay constant
-(weak scaling).  Rank 0 owns the allocator and broadcasts each level's
-(src, dst) pair list over NCCL; every rank copies its own slice.
+(weak scaling).  Every rank runs the same deterministic allocator kernels on
+its own copy of the block metadata, so all ranks derive identical (src, dst)
+pair lists with no collective in the step, and each copies its own slice
+(--plan bcast-level / bcast-once instead let rank 0 plan and broadcast the
+pair lists over NCCL).
 
 Also reported: `e2e` (the same step driven from host-held block tables: each
 level's parent tables copied in from pinned host memory, child tables copied
@@ -68,6 +71,11 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every kernel from Python each step")
+    ap.add_argument("--trees", type=int, default=0, help="fan-outs per step (default: one per GPU)")
+    ap.add_argument("--heads-per-rank", type=int, default=0, help="KV heads per rank (default: 8 / GPUs)")
+    ap.add_argument("--plan", default="replicated", choices=["bcast-level", "bcast-once", "replicated"],
+                    help="N > 1: every rank runs the same deterministic allocator (default, no collective "
+                         "in the step), or rank 0 plans and broadcasts each level's pairs / all pairs once")
     ap.add_argument("--graph-nccl", type=int, default=1,
                     help="N > 1: capture the step, NCCL pair broadcast included, as a CUDA graph")
     ap.add_argument("--match", action="store_true", help="also time match_prefix on the stress tree")
@@ -148,7 +156,8 @@ class ToTBench:
     previous ones on its stream, which keeps a block that is freed and handed
     out again from being overwritten before an older copy has read it."""
 
-    def __init__(self, rank: int, world: int, blocks_per_tree: int, variant: int):
+    def __init__(self, rank: int, world: int, blocks_per_tree: int, variant: int, trees: int = 0,
+                 heads_per_rank: int = 0, plan: str = "bcast-once"):
         import torch
 
         from agentkv_b200.allocator import SlabAllocator
@@ -161,9 +170,11 @@ class ToTBench:
         if H % world:
             raise SystemExit(f"--gpus {world} must divide the {H} KV heads")
         self.spec = W.ToTSpec()
-        self.trees = world
+        self.trees = trees or world
         self.n_blocks = blocks_per_tree * self.trees
-        self.slice_heads = H // world
+        self.slice_heads = heads_per_rank or H // world
+        self.plan = plan if world > 1 else "replicated"
+        self.planner = rank == 0 or self.plan == "replicated"
         # this rank's head slice of every block: [N, L, 2, H/world, bs, D]
         self.pool = torch.empty((self.n_blocks, L, 2, self.slice_heads, bs, D), dtype=torch.bfloat16,
                                 device=self.dev)
@@ -187,10 +198,11 @@ class ToTBench:
             np.cumsum(lens, out=off[1:])
             self.level_off.append(torch.from_numpy(off).to(self.dev))
         self.pairs_bufs = [torch.empty((n, 2), dtype=torch.int32, device=self.dev) for n in self.pairs_per_level]
+        self.all_pairs_buf = torch.empty((sum(self.pairs_per_level), 2), dtype=torch.int32, device=self.dev)
         from agentkv_b200.sharded import ShardedCopier
 
         self.copier = ShardedCopier(self.pool)
-        if rank == 0:
+        if self.planner:
             cfg = PoolConfig(total_blocks=self.n_blocks, block_size=bs, num_layers=L, num_kv_heads=H,
                              head_dim=D, dtype=dt, device="meta")
             self.alloc = SlabAllocator(cfg)
@@ -207,7 +219,7 @@ class ToTBench:
 
     def join(self):
         """Make the current stream wait for the allocator stream."""
-        if self.rank == 0:
+        if self.planner:
             self.torch.cuda.current_stream(self.dev).wait_stream(self.meta)
 
     def step(self, e2e=False, time_copies=False, capture=False):
@@ -219,7 +231,7 @@ class ToTBench:
         h2d = d2h = 0
         launches = 0
         events = []
-        if self.rank == 0:
+        if self.planner:
             if capture:
                 self.meta.wait_stream(cs)  # fork the allocator stream into the capture
             with torch.cuda.stream(self.meta):
@@ -245,14 +257,29 @@ class ToTBench:
                     self.host_tables.copy_(frees, non_blocking=True)
                     self.host_status.copy_(self.alloc._status, non_blocking=True)
                     d2h += self.host_tables.numel() * 4 + self.host_status.numel() * 4
-        for lvl, n_pairs in enumerate(self.pairs_per_level):
+        level_pairs = []
+        if self.plan == "bcast-once":
+            # one broadcast of every level's pairs once the last level is planned
             if self.rank == 0:
+                for p_ in res["pairs"]:
+                    p_.record_stream(cs)
+                cs.wait_event(events[-1])
+                allp = torch.cat(res["pairs"])
+            else:
+                allp = None
+            allp = self.copier.share_pairs(allp, sum(self.pairs_per_level), out=self.all_pairs_buf)
+            level_pairs = list(torch.split(allp, self.pairs_per_level))
+        for lvl, n_pairs in enumerate(self.pairs_per_level):
+            if self.plan == "bcast-once":
+                pairs = level_pairs[lvl]
+            elif self.planner:
                 pairs = res["pairs"][lvl]
                 pairs.record_stream(cs)
                 cs.wait_event(events[lvl])
-            else:
-                pairs = self.pairs_bufs[lvl]
-            pairs = self.copier.share_pairs(pairs, n_pairs, out=self.pairs_bufs[lvl])
+                if self.plan == "bcast-level":
+                    pairs = self.copier.share_pairs(pairs, n_pairs, out=self.pairs_bufs[lvl])
+            else:  # bcast-level, receiving rank
+                pairs = self.copier.share_pairs(None, n_pairs, out=self.pairs_bufs[lvl])
             if time_copies:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(cs)
@@ -263,7 +290,7 @@ class ToTBench:
                 self.copy_events.append((e0, e1, n_pairs))
         if capture:
             self.join()
-        if e2e and self.rank == 0:
+        if e2e and self.planner:
             self.join()
             torch.cuda.synchronize(self.dev)  # the host reads its tables and the status
             if int(self.host_status[0]):
@@ -359,6 +386,17 @@ def cpu_tot_run(trees: int, steps: int, warmup: int, threads: int, max_seconds: 
         for _ in range(trees):
             one_tree()
 
+    if threads <= 0:
+        # use the thread count that copies fastest on this host (one step each)
+        best = None
+        for t in cpu_thread_candidates():
+            threads = t
+            t0 = time.perf_counter()
+            one_step()
+            dt = time.perf_counter() - t0
+            if best is None or dt < best[0]:
+                best = (dt, t)
+        threads = best[1]
     for _ in range(warmup):
         one_step()
     times = []
@@ -371,18 +409,18 @@ def cpu_tot_run(trees: int, steps: int, warmup: int, threads: int, max_seconds: 
             break
     copies = trees * sum(spec.children_per_level())
     gbs = 2 * bpb * copies * len(times) / sum(times) / 1e9
-    return gbs, len(times), sum(times), bpb
+    return gbs, len(times), sum(times), bpb, threads
 
 
-def cpu_threads() -> int:
-    return max(1, min(os.cpu_count() or 1, 32))
+def cpu_thread_candidates():
+    n = os.cpu_count() or 1
+    return sorted({t for t in (1, 4, 8, 16, 32, 64, n) if t <= n})
 
 
 def reference_arm(args, rank, world):
     if rank != 0:
         return
-    threads = cpu_threads()
-    gbs, steps, secs, bpb = cpu_tot_run(world, args.steps, args.warmup, threads)
+    gbs, steps, secs, bpb, threads = cpu_tot_run(world, args.steps, args.warmup, 0)
     sample = (f"{world} Tree-of-Thought fan-out(s) per step ({world * 584} CoW copies of {bpb} B), "
               f"host pool of 4096 blocks, {steps} steps in {secs:.1f} s")
     line = {
@@ -549,7 +587,7 @@ def main():
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
-    bench = ToTBench(rank, world, args.blocks, args.variant)
+    bench = ToTBench(rank, world, args.blocks, args.variant, args.trees, args.heads_per_rank, args.plan)
     graph = None
     if not args.no_graph and (world == 1 or args.graph_nccl):
         for _ in range(2):  # load every kernel and settle the allocator pools before capture
@@ -593,7 +631,7 @@ def main():
     big = max(per_level)
     big_ms = statistics.mean(per_level[big])
     achieved = 2 * bench.slice_bytes * big / (big_ms / 1e3) / 1e9
-    traffic = level3_traffic() if world == 1 else None
+    traffic = level3_traffic() if bench.slice_heads == 8 and bench.trees == 1 else None
     launches = len(bench.copy_events)
 
     e2e = None
@@ -612,8 +650,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = cpu_threads()
-        gbs, steps, secs, bpb = cpu_tot_run(1, 1000, 1, threads, max_seconds=args.cpu_seconds)
+        gbs, steps, secs, bpb, threads = cpu_tot_run(1, 1000, 1, 0, max_seconds=args.cpu_seconds)
         cpu = {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"{steps} Tree-of-Thought steps ({steps * 584} CoW copies of {bpb} B) on a "
                          f"4096-block host pool, {secs:.1f} s"}
@@ -646,6 +683,8 @@ def main():
                 "bytes_per_block": bench.slice_bytes * world,
                 "cow_copies_per_step": sum(bench.pairs_per_level),
                 "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                "pair_lists": bench.plan if world > 1 else "local",
+                "heads_per_rank": bench.slice_heads,
                 "l2": "inputs larger than L2 (each step touches ~2.4 GB per GPU)",
                 "copy_variant": args.variant,
                 "cuda_graph": use_graph,

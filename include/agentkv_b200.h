@@ -94,8 +94,9 @@ AKV_API int akv_copy_blocks(void* pool, int64_t bytes_per_block, int32_t total_b
 
 /* Same, with an explicit kernel choice: 0 = automatic, 1 = 16-byte vector
  * loads/stores, 2 = bulk-async (TMA) copies staged through shared memory
- * (32 KiB chunks, 6 in flight, 1 CTA per SM); 3-7 = other bulk shapes
- * (16 KiB x 12; 32 KiB x 3 with 2 CTAs per SM; 64 KiB x 3; 16 KiB x 6 with
+ * (16 KiB chunks x 12 in flight for blocks >= 1 MiB, 64 KiB x 3 below, one
+ * CTA per SM); 3-7 = fixed bulk shapes
+ * (32 KiB x 6; 32 KiB x 3 with 2 CTAs per SM; 64 KiB x 3; 16 KiB x 6 with
  * 2 CTAs per SM; 8 KiB x 24) for tuning. */
 AKV_API int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int32_t total_blocks,
                             const int32_t* pairs, int32_t n_pairs,
