@@ -3,7 +3,9 @@
 Public API mirrors the reference package `agentkv`:
   AgentKVPool, DualRadixTree / CoWRadixTree, SlabAllocator, PoolConfig,
   BlockHandle, NodeHandle; kernels.copy_block / kernels.zero_block are the
-  drop-ins for agentkv.core.triton_kernels.
+  drop-ins for agentkv.core.triton_kernels.  FanoutGraph replays a whole
+  Tree-of-Thought fan-out (forks, copy-on-write copies, appends, frees) as
+  one CUDA graph.
 
 The hot path (block copy / zero, free list and refcounts, match_prefix) runs
 as sm_100a CUDA kernels in libagentkv_b200.so behind a C ABI
@@ -29,6 +31,7 @@ _EXPORTS = {
     "SharedNode": "radix_tree",
     "ROOT_NODE_ID": "radix_tree",
     "INVALID_NODE_ID": "radix_tree",
+    "FanoutGraph": "fanout",
 }
 
 __all__ = ["__version__", *_EXPORTS]

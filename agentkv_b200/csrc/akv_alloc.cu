@@ -590,6 +590,23 @@ int grid_for(int64_t work, int threads, int max_ctas) {
 
 }  // namespace
 
+int akv_alloc_prepare() {
+#define AKV_LOAD(fn) if (int rc = akv_load_kernel(reinterpret_cast<const void*>(fn), "akv_prepare: " #fn)) return rc
+  AKV_LOAD(k_init);
+  AKV_LOAD(k_alloc);
+  AKV_LOAD(k_incref_check);
+  AKV_LOAD(k_incref_apply);
+  AKV_LOAD(k_dec_count);
+  AKV_LOAD(k_dec_flag);
+  AKV_LOAD(k_dec_plan);
+  AKV_LOAD(k_dec_apply);
+  AKV_LOAD(k_release);
+  AKV_LOAD(k_advance);
+  AKV_LOAD(k_cow_plan);
+#undef AKV_LOAD
+  return AKV_OK;
+}
+
 // Shared with the block-movement launcher in akv_blocks.cu.
 int akv_launch_copy_counted(void* pool, int64_t bpb, int32_t total, const int32_t* pairs,
                             int32_t n_max, const int64_t* n_dev, AkvStatus* st, cudaStream_t s);

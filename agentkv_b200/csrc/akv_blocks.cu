@@ -14,6 +14,7 @@
 // buffer.  Neither reads the old block, unlike the reference Triton kernel
 // that loads `x` and stores `x * 0` (agentkv/core/triton_kernels.py:161-162).
 #include <algorithm>
+#include <atomic>
 
 #include "akv_common.cuh"
 
@@ -414,13 +415,18 @@ bool bulk_eligible(const void* pool, int64_t bpb) {
 template <int CHUNK, int STAGES, int CTAS_PER_SM>
 int copy_bulk_launch_t(char* pool, int64_t bpb, int32_t total, const int32_t* pairs, int32_t n,
                        const int32_t* refs, AkvStatus* st, cudaStream_t s, const int64_t* n_dev) {
-  static thread_local bool attr_set = false;
+  // The shared-memory limit is a per-device function attribute: set it
+  // once for each device this process launches on.
+  static std::atomic<uint64_t> attr_set{0};
   const int smem = STAGES * CHUNK;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_copy_bulk<CHUNK, STAGES>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return akv_cuda_fail(e, "akv_copy_blocks(bulk): cudaGetDevice");
+  const uint64_t bit = uint64_t{1} << (dev & 63);
+  if (!(attr_set.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(k_copy_bulk<CHUNK, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return akv_cuda_fail(e, "akv_copy_blocks(bulk): smem attribute");
-    attr_set = true;
+    attr_set.fetch_or(bit, std::memory_order_release);
   }
   const int64_t chunks = (bpb + CHUNK - 1) / CHUNK;
   const int64_t work = chunks * n;
@@ -463,6 +469,44 @@ int zero_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* ids,
 }
 
 }  // namespace
+
+// Loads every kernel of this file and sets the bulk kernels' shared-memory
+// limits on the current device; idempotent.
+int akv_blocks_prepare() {
+  struct Item { const void* fn; int smem; const char* name; };
+#define AKV_ITEM(fn, smem) {reinterpret_cast<const void*>(fn), smem, "akv_prepare: " #fn}
+  const Item items[] = {
+      AKV_ITEM((k_copy_bulk<16384, 12>), 16384 * 12),
+      AKV_ITEM((k_copy_bulk<32768, 6>), 32768 * 6),
+      AKV_ITEM((k_copy_bulk<32768, 3>), 32768 * 3),
+      AKV_ITEM((k_copy_bulk<65536, 3>), 65536 * 3),
+      AKV_ITEM((k_copy_bulk<16384, 6>), 16384 * 6),
+      AKV_ITEM((k_copy_bulk<8192, 24>), 8192 * 24),
+      AKV_ITEM(k_zero_bulk, 0),
+      AKV_ITEM((k_copy_vec<uint4, kVecThreads, kVecUnroll>), 0),
+      AKV_ITEM((k_copy_vec<uint2, kVecThreads, kVecUnroll>), 0),
+      AKV_ITEM((k_copy_vec<uint32_t, kVecThreads, kVecUnroll>), 0),
+      AKV_ITEM((k_copy_vec<uint16_t, kVecThreads, kVecUnroll>), 0),
+      AKV_ITEM((k_copy_vec<uint8_t, kVecThreads, kVecUnroll>), 0),
+      AKV_ITEM((k_zero_vec<uint4, kVecThreads, kVecUnroll>), 0),
+      AKV_ITEM((k_zero_vec<uint2, kVecThreads, kVecUnroll>), 0),
+      AKV_ITEM((k_zero_vec<uint32_t, kVecThreads, kVecUnroll>), 0),
+      AKV_ITEM((k_zero_vec<uint16_t, kVecThreads, kVecUnroll>), 0),
+      AKV_ITEM((k_zero_vec<uint8_t, kVecThreads, kVecUnroll>), 0),
+      AKV_ITEM(k_check_mark, 0),
+      AKV_ITEM(k_check_scan, 0),
+      AKV_ITEM(k_check_clear, 0),
+  };
+#undef AKV_ITEM
+  for (const Item& it : items) {
+    if (int rc = akv_load_kernel(it.fn, it.name)) return rc;
+    if (it.smem > 48 * 1024) {
+      const cudaError_t e = cudaFuncSetAttribute(it.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, it.smem);
+      if (e != cudaSuccess) return akv_cuda_fail(e, it.name);
+    }
+  }
+  return AKV_OK;
+}
 
 // Copy with the pair count read on the device from *n_dev (capped at n_max);
 // used by the CoW batch, whose planner decides on the device how many of its

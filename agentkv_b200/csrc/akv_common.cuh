@@ -47,6 +47,22 @@ AKV_DEV uint64_t akv_globaltimer() {
 void akv_set_error(const char* fmt, ...);
 int akv_cuda_fail(cudaError_t err, const char* what);
 
+// Loads a kernel into the current device's context now rather than at its
+// first launch (CUDA 12 loads kernels lazily by default); used by
+// akv_prepare so that no first launch happens inside a stream capture.
+inline int akv_load_kernel(const void* fn, const char* name) {
+  cudaFuncAttributes attr;
+  const cudaError_t e = cudaFuncGetAttributes(&attr, fn);
+  if (e != cudaSuccess) return akv_cuda_fail(e, name);
+  return 0;
+}
+
+// Per-file halves of akv_prepare: load every kernel, set attributes.
+int akv_blocks_prepare();
+int akv_alloc_prepare();
+int akv_tree_prepare();
+int akv_fanout_prepare();
+
 #define AKV_ARG_CHECK(cond, ...)              \
   do {                                        \
     if (!(cond)) {                            \

@@ -58,6 +58,10 @@ __global__ void k_fanout_plan(const int32_t* __restrict__ parent_tables,
 
 }  // namespace
 
+int akv_fanout_prepare() {
+  return akv_load_kernel(reinterpret_cast<const void*>(k_fanout_plan), "akv_prepare: k_fanout_plan");
+}
+
 extern "C" int akv_fanout_plan(const int32_t* parent_tables, const int64_t* parent_off, int32_t n_parents,
                                int32_t fanout, int32_t append, const int32_t* fresh_ids,
                                int32_t* child_tables, int64_t* child_off, int32_t* inc_ids,

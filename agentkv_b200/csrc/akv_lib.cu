@@ -35,3 +35,10 @@ extern "C" int akv_status_clear(AkvStatus* status, void* stream) {
   if (e != cudaSuccess) return akv_cuda_fail(e, "akv_status_clear");
   return AKV_OK;
 }
+
+extern "C" int akv_prepare(void) {
+  if (int rc = akv_blocks_prepare()) return rc;
+  if (int rc = akv_alloc_prepare()) return rc;
+  if (int rc = akv_tree_prepare()) return rc;
+  return akv_fanout_prepare();
+}

@@ -303,6 +303,17 @@ __global__ void k_tree_apply(AkvTreeView tree, const int32_t* __restrict__ su, i
 
 }  // namespace
 
+int akv_tree_prepare() {
+#define AKV_LOAD(fn) if (int rc = akv_load_kernel(reinterpret_cast<const void*>(fn), "akv_prepare: " #fn)) return rc
+  AKV_LOAD(k_match<1>);
+  AKV_LOAD(k_match<2>);
+  AKV_LOAD(k_match<4>);
+  AKV_LOAD(k_match<8>);
+  AKV_LOAD(k_tree_apply);
+#undef AKV_LOAD
+  return AKV_OK;
+}
+
 extern "C" uint32_t akv_tree_hash(int32_t parent, int32_t token) {
   uint64_t k = (static_cast<uint64_t>(static_cast<uint32_t>(parent)) << 32) |
                static_cast<uint64_t>(static_cast<uint32_t>(token));

@@ -1,0 +1,125 @@
+"""FanoutGraph — a Tree-of-Thought fan-out replayed as one CUDA graph.
+
+Agent frameworks fork the same shape of tree over and over (a root forked K
+ways for a few levels, every child copy-on-writing the block it will extend
+and appending a few blocks).  FanoutGraph records that step once — the host
+-> device copy of the root block tables, SlabAllocator.fanout_tree (allocs,
+plans, one inc_ref and one dec_ref batch), the block copies and, optionally,
+the frees of every child — and each run() replays it: the caller's host root
+tables go in, every child's block table and the status word come back to
+host memory, one synchronisation per call.
+
+Capturing executes nothing, so the allocator sees exactly the operations of
+the runs, in order: ids, refcounts and the free list stay those of the
+reference's per-child calls.  Requirements: the roots' table lengths are
+fixed at construction, and nothing else uses the allocator between runs on
+another stream.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _native as N
+from . import kernels as K
+from .allocator import SlabAllocator
+
+
+class FanoutGraph:
+    def __init__(self, alloc: SlabAllocator, root_lens, levels: int, fanout: int, append: int, *,
+                 pool: Optional[torch.Tensor] = None, free_children: bool = False, variant: int = 0) -> None:
+        self.alloc = alloc
+        self.dev = alloc.device
+        self.levels, self.fanout, self.append = int(levels), int(fanout), int(append)
+        self.root_lens = np.asarray(root_lens, np.int64)
+        if (self.root_lens < 1).any():
+            raise ValueError("FanoutGraph: every root needs at least one block")
+        self.pool = pool if pool is not None else alloc._kv_data
+        self.free_children = free_children
+        self.variant = variant
+        # fixed shapes of every level
+        lens = self.root_lens
+        self.level_off = []
+        n_child_entries = 0
+        for _ in range(self.levels):
+            off = np.zeros(len(lens) + 1, np.int64)
+            np.cumsum(lens, out=off[1:])
+            self.level_off.append(torch.from_numpy(off).to(self.dev))
+            lens = np.repeat(lens + self.append, self.fanout)
+            n_child_entries += int(lens.sum())
+        self.child_lens = lens
+        self.n_child_entries = n_child_entries
+        self.h_roots = torch.empty(int(self.root_lens.sum()), dtype=torch.int32, pin_memory=True)
+        self.h_tables = torch.empty(n_child_entries, dtype=torch.int32, pin_memory=True)
+        self.h_status = torch.empty(N.STATUS_BYTES // 4, dtype=torch.int32, pin_memory=True)
+        self.d_roots = torch.empty(int(self.root_lens.sum()), dtype=torch.int32, device=self.dev)
+        # copy errors land in the allocator's status word when both share a device
+        self._copy_status = alloc._status if self.pool.device == alloc.device else None
+        self.copies_per_run = int(sum(len(self.root_lens) * self.fanout ** (lv + 1) for lv in range(self.levels)))
+        self.launches_per_run = 0
+        N.check(N.lib.akv_prepare())
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
+            self._record()
+
+    def _record(self) -> None:
+        # Allocator kernels on a side stream; each level's copy on the
+        # capture stream waits only for that level's plan.  Allocator kernels
+        # never touch pool bytes, so they overlap the copies.
+        cs = torch.cuda.current_stream(self.dev)
+        meta = self._meta = torch.cuda.Stream(self.dev)
+        meta.wait_stream(cs)
+        events = []
+        with torch.cuda.stream(meta):
+            self.d_roots.copy_(self.h_roots, non_blocking=True)
+
+            def on_level(_lvl):
+                ev = torch.cuda.Event()
+                ev.record(meta)
+                events.append(ev)
+
+            res = self.alloc.fanout_tree(self.d_roots, self.root_lens, self.levels, self.fanout, self.append,
+                                         level_offsets=self.level_off, on_level=on_level)
+            launches = res["launches"]
+            tables = torch.cat(res["child_tables"])
+            if self.free_children:
+                self.alloc.dec_ref_batch(tables)
+                launches += 4
+            self.h_tables.copy_(tables, non_blocking=True)
+        if self.pool.device.type != "meta":
+            for lvl, pairs in enumerate(res["pairs"]):
+                cs.wait_event(events[lvl])
+                K.copy_blocks(self.pool, pairs, variant=self.variant, status=self._copy_status)
+                launches += 1
+        cs.wait_stream(meta)
+        self.h_status.copy_(self.alloc._status, non_blocking=True)
+        self._keep = (res, tables, events)
+        self.launches_per_run = launches
+
+    @property
+    def h2d_bytes(self) -> int:
+        return self.h_roots.numel() * 4
+
+    @property
+    def d2h_bytes(self) -> int:
+        return (self.h_tables.numel() + self.h_status.numel()) * 4
+
+    def run(self, root_tables, copy: bool = True) -> np.ndarray:
+        """Fan out from `root_tables` (host ints, the roots' tables
+        concatenated); returns every child's block table concatenated, level
+        by level, children in (parent, child) order.  With copy=False the
+        result is a view of the pinned read-back buffer, valid until the next
+        run()."""
+        roots = np.asarray(root_tables, np.int32).reshape(-1)
+        if roots.size != self.h_roots.numel():
+            raise ValueError(f"FanoutGraph.run: expected {self.h_roots.numel()} root ids, got {roots.size}")
+        self.h_roots.numpy()[:] = roots
+        self.graph.replay()
+        torch.cuda.current_stream(self.dev).synchronize()
+        if int(self.h_status[0]):
+            self.alloc.check()
+        out = self.h_tables.numpy()
+        return out.copy() if copy else out

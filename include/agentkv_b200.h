@@ -70,6 +70,10 @@ typedef struct AkvStatus {
 AKV_API int akv_version(void);                     /* (major << 16) | minor */
 AKV_API int akv_last_error(char* buf, int len);    /* copies the thread's last message */
 AKV_API int akv_status_clear(AkvStatus* status, void* stream);
+/* One-time set-up of the current device's kernel attributes (shared-memory
+ * limits).  The entry points do it on first use; call this first when the
+ * first use would happen inside a CUDA stream capture. */
+AKV_API int akv_prepare(void);
 
 /* ── block movement ─────────────────────────────────────────────────────────
  * The pool is the reference's `_kv_data` tensor

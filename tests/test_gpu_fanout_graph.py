@@ -1,0 +1,145 @@
+"""FanoutGraph (a Tree-of-Thought fan-out replayed as one CUDA graph) against
+the oracle's per-child sequence.
+
+The oracle runs the reference's calls child by child — fork, then
+ensure_mutable_block(child, -1) copying the shared block, then `append`
+allocate_block calls, level after level — and frees every child in creation
+order.  After every replay the returned child tables, the refcounts, the
+free list, the reclaimer queues and counters, and the pool bytes must equal
+the oracle's.  The Llama-3-8B Tree-of-Thought case is also checked against
+the reference's own recorded fan-out.
+"""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from agentkv_b200 import AgentKVPool, PoolConfig
+from agentkv_b200 import workloads as W
+from agentkv_b200.fanout import FanoutGraph
+from oracle import oracle as O
+
+from test_gpu_alloc import assert_same_as_oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle_fanout(tree, roots, levels, fanout, append, free):
+    parents, made = roots, []
+    for _ in range(levels):
+        kids = []
+        for p in parents:
+            for _ in range(fanout):
+                c = tree.fork(p)
+                tree.ensure_mutable_block(c, -1)
+                for _ in range(append):
+                    tree.allocate_block(c)
+                kids.append(c)
+        made += kids
+        parents = kids
+    tables = np.concatenate([np.asarray(c.residual, np.int32) for c in made])
+    if free:
+        for c in made:
+            tree.free(c)
+    return tables
+
+
+@pytest.mark.parametrize("free", [True, False])
+@pytest.mark.parametrize("root_lens,levels,fanout,append", [
+    ([3, 5], 2, 3, 2),
+    ([1], 3, 4, 0),
+    ([2, 1, 4], 1, 5, 1),
+])
+def test_fanout_graph_matches_oracle(root_lens, levels, fanout, append, free):
+    n_blocks = 1024
+    cfg = PoolConfig(total_blocks=n_blocks, block_size=16, num_layers=2, num_kv_heads=2, head_dim=64,
+                     dtype="bfloat16", device="cuda")
+    pool = AgentKVPool(config=cfg)
+    a = pool._allocator
+    a._kv_data.view(torch.int16).random_(-30000, 30000)
+    host = a._kv_data.view(torch.uint8).reshape(n_blocks, -1).cpu().numpy().copy()
+    bpb = host.shape[1]
+
+    o = O.OracleAllocator(n_blocks, cfg.epoch_interval)
+    tree = O.OracleTree(o, 16, copy_cb=lambda s, d: O.copy_blocks(host, bpb, np.array([[s, d]], np.int32)))
+    roots = []
+    for ln in root_lens:
+        h = tree.create_root([])
+        for _ in range(ln):
+            tree.allocate_block(h)
+        roots.append(h)
+    d_roots = a.alloc_batch(sum(root_lens)).cpu().numpy()
+    want_roots = np.concatenate([np.asarray(h.residual, np.int32) for h in roots])
+    np.testing.assert_array_equal(d_roots, want_roots)
+
+    fg = FanoutGraph(a, root_lens, levels, fanout, append, free_children=free)
+    assert fg.copies_per_run == len(root_lens) * sum(fanout ** (lv + 1) for lv in range(levels))
+    for run in range(3):
+        got = fg.run(d_roots)
+        want = _oracle_fanout(tree, roots, levels, fanout, append, free)
+        np.testing.assert_array_equal(got, want, err_msg=f"tables, run {run}")
+        assert_same_as_oracle(a, o, f"run {run}")
+        dev = a._kv_data.view(torch.uint8).reshape(n_blocks, -1).cpu().numpy()
+        assert np.array_equal(dev, host), f"pool bytes, run {run}"
+
+
+def test_fanout_graph_tot_8b_reference_fixture(golden_dir):
+    """The Llama-3-8B Tree-of-Thought fan-out (a 256-block root forked 8 ways
+    for 3 levels, 4 blocks appended per child) equals the reference's
+    recorded tables, refcounts and free list; with the frees in the graph,
+    every replay returns the refcounts to the reference's freed state and
+    follows the oracle's per-child sequence."""
+    g = np.load(golden_dir / "tot_8b.npz")
+    spec = W.ToTSpec()
+    N_, bs, L, H, D, dt = W.LLAMA3_8B_GEOMETRY
+    cfg = PoolConfig(total_blocks=N_, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D, dtype=dt,
+                     device="meta")
+    a = AgentKVPool(config=cfg)._allocator
+    root_len = spec.root_tokens // bs
+    roots = a.alloc_batch(root_len).cpu().numpy()
+    fg = FanoutGraph(a, [root_len], spec.levels, spec.fanout, spec.appended_blocks)
+    np.testing.assert_array_equal(fg.run(roots), g["tables"])
+    np.testing.assert_array_equal(a._ref_counts.cpu().numpy(), g["ref_fanout"])
+    np.testing.assert_array_equal(a.free_list(), g["free_fanout"])
+    st = json.loads(str(g["stats_fanout"]))
+    for k in ("free_blocks", "allocated_blocks", "peak_allocated", "total_allocs", "epoch"):
+        assert a.stats()[k] == st[k], k
+    a.dec_ref_batch(torch.from_numpy(g["tables"]).to(a.device))
+    a.check()
+    np.testing.assert_array_equal(a.free_list(), g["free_freed"])
+
+    # with the frees in the graph: the first replay ends in the reference's
+    # freed state; later replays (the freed ids now sit at the other end of
+    # the free list) follow the oracle's per-child sequence
+    a2 = AgentKVPool(config=cfg)._allocator
+    roots2 = a2.alloc_batch(root_len).cpu().numpy()
+    fg2 = FanoutGraph(a2, [root_len], spec.levels, spec.fanout, spec.appended_blocks, free_children=True)
+    o = O.OracleAllocator(N_, cfg.epoch_interval)
+    tree = O.OracleTree(o, bs)
+    root = tree.create_root([])
+    for _ in range(root_len):
+        tree.allocate_block(root)
+    for run in range(3):
+        got = fg2.run(roots2)
+        if run == 0:
+            np.testing.assert_array_equal(got, g["tables"])
+            np.testing.assert_array_equal(a2.free_list(), g["free_freed"])
+        want = _oracle_fanout(tree, [root], spec.levels, spec.fanout, spec.appended_blocks, True)
+        np.testing.assert_array_equal(got, want, err_msg=f"run {run}")
+        np.testing.assert_array_equal(a2._ref_counts.cpu().numpy(), g["ref_freed"])
+        assert_same_as_oracle(a2, o, f"run {run}")
+
+
+def test_fanout_graph_exhaustion_raises():
+    cfg = PoolConfig(total_blocks=40, block_size=4, num_layers=1, num_kv_heads=1, head_dim=4,
+                     dtype="float16", device="cuda")
+    a = AgentKVPool(config=cfg)._allocator
+    roots = a.alloc_batch(2).cpu().numpy()
+    fg = FanoutGraph(a, [2], 2, 3, 1)  # 24 blocks per replay, children kept
+    fg.run(roots)
+    with pytest.raises(MemoryError):
+        fg.run(roots)
+    with pytest.raises(ValueError):
+        fg.run(roots[:1])
