@@ -549,6 +549,23 @@ extern "C" int akv_copy_blocks(void* pool, int64_t bytes_per_block, int32_t tota
                                  status, 0, stream);
 }
 
+extern "C" int akv_copy_blocks_counted(void* pool, int64_t bytes_per_block, int32_t total_blocks,
+                                       const int32_t* pairs, int32_t n_max, const int64_t* n_dev,
+                                       const int32_t* ref_counts, AkvStatus* status, void* stream) {
+  AKV_ARG_CHECK(n_max >= 0, "akv_copy_blocks_counted: n_max=%d < 0", n_max);
+  if (n_max == 0) return AKV_OK;
+  AKV_ARG_CHECK(pool != nullptr && pairs != nullptr && n_dev != nullptr,
+                "akv_copy_blocks_counted: NULL pool, pairs or count");
+  AKV_ARG_CHECK(bytes_per_block > 0, "akv_copy_blocks_counted: bytes_per_block=%lld",
+                static_cast<long long>(bytes_per_block));
+  AKV_ARG_CHECK(total_blocks > 0, "akv_copy_blocks_counted: total_blocks=%d", total_blocks);
+  char* p = static_cast<char*>(pool);
+  cudaStream_t s = akv_stream(stream);
+  if (bulk_eligible(pool, bytes_per_block))
+    return copy_bulk_launch(p, bytes_per_block, total_blocks, pairs, n_max, ref_counts, status, s, n_dev);
+  return copy_vec_dispatch(p, bytes_per_block, total_blocks, pairs, n_max, ref_counts, status, s, n_dev);
+}
+
 extern "C" int akv_zero_blocks_variant(void* pool, int64_t bytes_per_block, int32_t total_blocks,
                                        const int32_t* ids, int32_t n, const int32_t* ref_counts,
                                        AkvStatus* status, int32_t variant, void* stream) {

@@ -173,6 +173,36 @@ def copy_blocks(
         raise_for_status(st)
 
 
+def copy_blocks_counted(
+    pool: torch.Tensor,
+    pairs: torch.Tensor,
+    count: torch.Tensor,
+    *,
+    ref_counts: Optional[torch.Tensor] = None,
+    status: Optional[torch.Tensor] = None,
+) -> None:
+    """copy_blocks where the number of valid pairs lives on the device:
+    `pairs` is a device int32 [n_max, 2] buffer, `count` a device int64
+    tensor whose first element says how many of its rows to copy (capped at
+    n_max; read by the kernel, never by the host)."""
+    if not _require_cuda(pool, "copy_blocks_counted"):
+        return
+    total, bpb = _pool_geometry(pool)
+    if pairs.dtype != torch.int32 or pairs.device != pool.device or not pairs.is_contiguous():
+        raise ValueError("copy_blocks_counted: pairs must be a contiguous int32 tensor on the pool's device")
+    if count.dtype != torch.int64 or count.device != pool.device or count.numel() < 1:
+        raise ValueError("copy_blocks_counted: count must be an int64 tensor on the pool's device")
+    n_max = pairs.numel() // 2
+    st = status if status is not None else _status_buffer(pool.device)
+    N.check(
+        N.lib.akv_copy_blocks_counted(
+            pool.data_ptr(), bpb, total, pairs.data_ptr(), n_max, count.data_ptr(),
+            ref_counts.data_ptr() if ref_counts is not None else None, st.data_ptr(),
+            stream_handle(pool.device),
+        )
+    )
+
+
 def zero_blocks(
     pool: torch.Tensor,
     ids,

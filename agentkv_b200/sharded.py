@@ -9,12 +9,17 @@ and each rank copies only its own slice: no KV byte crosses a GPU.
 Rank `src` (0) owns the allocator and the tree; after planning a batch it
 broadcasts the int32 pair list (8 B per pair) over the process group — NCCL
 over NVLink on GPUs — and every rank runs akv_copy_blocks on its slice.
+Batches of varying size travel as one fixed-size buffer (`pack_batch`): an
+int64 pair count followed by room for `max_pairs` pairs; the copy reads the
+count on the device (akv_copy_blocks_counted), so receiving ranks never wait
+on the host for it.
 """
 
 from __future__ import annotations
 
 from typing import Optional
 
+import numpy as np
 import torch
 
 from . import kernels as K
@@ -63,3 +68,46 @@ class ShardedCopier:
 
     def copy(self, pairs: torch.Tensor, **kw) -> None:
         K.copy_blocks(self.pool, pairs, **kw)
+
+    # ── variable-size batches: [int64 count | max_pairs x (src, dst)] ────────
+    @staticmethod
+    def batch_words(max_pairs: int) -> int:
+        return 2 + 2 * max_pairs
+
+    def batch_buffer(self, max_pairs: int) -> torch.Tensor:
+        return torch.zeros(self.batch_words(max_pairs), dtype=torch.int32, device=self.pool.device)
+
+    @staticmethod
+    def pack_batch(pairs, buf: torch.Tensor) -> torch.Tensor:
+        """Write (n, 2) host pairs and their count into `buf` (rank src)."""
+        p = np.asarray(pairs, np.int32).reshape(-1, 2)
+        cap = (buf.numel() - 2) // 2
+        if len(p) > cap:
+            raise ValueError(f"pack_batch: {len(p)} pairs exceed the buffer's {cap}")
+        host = np.zeros(2 + 2 * len(p), np.int32)
+        host[:2].view(np.int64)[0] = len(p)
+        host[2:] = p.reshape(-1)
+        buf[: host.size].copy_(torch.from_numpy(host))
+        return buf
+
+    def share_batch(self, buf: torch.Tensor) -> torch.Tensor:
+        """One broadcast of the whole batch buffer from rank src."""
+        import torch.distributed as dist
+
+        if self.world > 1:
+            dist.broadcast(buf, src=self.src, group=self.group)
+        return buf
+
+    @staticmethod
+    def batch_count(buf: torch.Tensor) -> torch.Tensor:
+        """The int64 count as a one-element tensor view of `buf`."""
+        return buf[:2].view(torch.int64)
+
+    @staticmethod
+    def batch_pairs(buf: torch.Tensor) -> torch.Tensor:
+        return buf[2:].view(-1, 2)
+
+    def copy_batch(self, buf: torch.Tensor, **kw) -> None:
+        """Copy the batch's pairs on this rank's slice; the count is read on
+        the device."""
+        K.copy_blocks_counted(self.pool, self.batch_pairs(buf), self.batch_count(buf), **kw)

@@ -157,18 +157,83 @@ def match_queries(spec: MatchSpec, corpus: List[np.ndarray], prefixes: List[np.n
 # ── ReAct multi-agent ────────────────────────────────────────────────────────
 @dataclass(frozen=True)
 class ReActSpec:
+    """A 16,384-token shared prefix committed to the tree, 32 agents forked
+    from it, and `steps` rounds in which every agent slot, in slot order,
+    takes one action drawn with weights (fork 2, cow 4, free 2, advance 1,
+    append 3):
+
+    * fork    — agent s branches: the agent in another slot t (drawn) is freed
+                and replaced by fork(agent s), sharing s's residual blocks;
+    * cow     — ensure_mutable_block(agent s, -1): the tail block is copied if
+                it is shared (after a fork), else nothing moves; an agent with
+                no residual block allocates one instead;
+    * free    — agent s is freed and restarts as a fork of the prefix root;
+    * advance — maybe_advance_epoch();
+    * append  — allocate_block(agent s) (16 more tokens).
+    """
+
     prefix_tokens: int = 16_384
     agents: int = 32
     steps: int = 1000
     seed: int = 5
+    block_size: int = 16
 
 
-REACT_ACTIONS = ("fork", "cow", "free", "advance", "append")
+REACT_FORK, REACT_COW, REACT_FREE, REACT_ADVANCE, REACT_APPEND = range(5)
+REACT_WEIGHTS = (2, 4, 2, 1, 3)
 
 
-def react_actions(spec: ReActSpec) -> List[Tuple[str, int]]:
-    """(action, agent slot) per step; weights favour appends and CoW copies."""
+def react_prefix(spec: ReActSpec) -> List[int]:
     rng = random.Random(spec.seed)
-    weights = (2, 4, 2, 1, 3)
-    return [(rng.choices(REACT_ACTIONS, weights=weights)[0], rng.randrange(spec.agents))
-            for _ in range(spec.steps)]
+    return [rng.randrange(VOCAB) for _ in range(spec.prefix_tokens)]
+
+
+def react_trace(spec: ReActSpec) -> List[List[Tuple[int, int, int]]]:
+    """Per step, one (action, slot, target slot) per agent in slot order; the
+    target is used by fork only (never the acting slot)."""
+    rng = random.Random(spec.seed * 1_000_003 + 1)
+    kinds = list(range(5))
+    out = []
+    for _ in range(spec.steps):
+        step = []
+        for s in range(spec.agents):
+            k = rng.choices(kinds, weights=REACT_WEIGHTS)[0]
+            t = rng.randrange(spec.agents - 1)
+            step.append((k, s, t if t < s else t + 1))
+        out.append(step)
+    return out
+
+
+def react_setup(api, spec: ReActSpec):
+    """Commit the shared prefix and fork the agents (each with one private
+    block).  `api` offers the pool's calls (create_root, allocate_block,
+    allocate_blocks, commit_prefix, fork) plus residual_len(handle)."""
+    root = api.create_root(react_prefix(spec))
+    api.allocate_blocks(root, spec.prefix_tokens // spec.block_size)
+    api.commit_prefix(root, spec.prefix_tokens)
+    agents = []
+    for _ in range(spec.agents):
+        a = api.fork(root)
+        api.allocate_block(a)
+        agents.append(a)
+    return root, agents
+
+
+def react_step(api, root, agents: list, actions) -> None:
+    """Apply one step's actions, in order, through `api` (see ReActSpec)."""
+    for kind, s, t in actions:
+        if kind == REACT_FORK:
+            api.free(agents[t])
+            agents[t] = api.fork(agents[s])
+        elif kind == REACT_COW:
+            if api.residual_len(agents[s]):
+                api.ensure_mutable_block(agents[s], -1)
+            else:
+                api.allocate_block(agents[s])
+        elif kind == REACT_FREE:
+            api.free(agents[s])
+            agents[s] = api.fork(root)
+        elif kind == REACT_ADVANCE:
+            api.maybe_advance_epoch()
+        else:
+            api.allocate_block(agents[s])

@@ -107,6 +107,18 @@ AKV_API int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int32_t
                             const int32_t* ref_counts, AkvStatus* status,
                             int32_t variant, void* stream);
 
+/* akv_copy_blocks with the pair count in device memory: `pairs` has room for
+ * n_max pairs and the kernel reads the int64 *n_dev (written by an earlier
+ * kernel, a copy or a broadcast) and copies the first min(*n_dev, n_max).
+ * No counterpart in the reference, which copies one pair per call
+ * (agentkv/core/triton_kernels.py:171-203): it lets a batch of variable size
+ * travel as one buffer (count and pairs) in one broadcast to the ranks of a
+ * head-sharded pool, and a captured launch replay batches of any size up to
+ * n_max.  Same checks and errors as akv_copy_blocks. */
+AKV_API int akv_copy_blocks_counted(void* pool, int64_t bytes_per_block, int32_t total_blocks,
+                            const int32_t* pairs, int32_t n_max, const int64_t* n_dev,
+                            const int32_t* ref_counts, AkvStatus* status, void* stream);
+
 /* akv_zero_blocks replaces triton_kernels.zero_block / _zero_block_kernel
  * (agentkv/core/triton_kernels.py:206-229, :134-162) and
  * SlabAllocator.zero_block (agentkv/core/slab_allocator.py:321-334).  It

@@ -365,6 +365,62 @@ def tot() -> dict:
     }
 
 
+# ── D2. ReAct multi-agent trace (metadata, 70B geometry, 40,000 blocks) ─────
+class _RefReActAPI:
+    """The reference pool's calls as workloads.react_setup / react_step use them."""
+
+    def __init__(self, pool):
+        self.p = pool
+
+    def __getattr__(self, name):
+        return getattr(self.p, name)
+
+    def allocate_blocks(self, h, n):
+        for _ in range(n):
+            self.p.allocate_block(h)
+
+    def residual_len(self, h):
+        return len(h.residual_blocks)
+
+
+def react(spec: W.ReActSpec, checkpoints=(200, 1000)) -> dict:
+    N, bs, L, H, D, dt = W.LLAMA3_70B_GEOMETRY
+    cfg = PoolConfig(total_blocks=N, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D,
+                     dtype=dt, device="meta")
+    pool = AgentKVPool(config=cfg)
+    pairs = []
+    orig = pool._allocator.copy_block
+
+    def rec_copy(src, dst):
+        pairs.append((src.block_id, dst.block_id))
+        orig(src, dst)
+
+    pool._allocator.copy_block = rec_copy
+    api = _RefReActAPI(pool)
+    root, agents = W.react_setup(api, spec)
+    out = {"setup_pairs": np.asarray(pairs, np.int32).reshape(-1, 2)}
+    step_off = [len(pairs)]
+    a = pool._allocator
+    for i, actions in enumerate(W.react_trace(spec)):
+        W.react_step(api, root, agents, actions)
+        step_off.append(len(pairs))
+        if i + 1 in checkpoints:
+            tables = [np.asarray(pool.get_block_ids(h), np.int32) for h in agents]
+            t_off = np.zeros(len(tables) + 1, np.int64)
+            np.cumsum([len(t) for t in tables], out=t_off[1:])
+            k = f"s{i + 1}"
+            out[f"{k}_tables"] = np.concatenate(tables)
+            out[f"{k}_tables_off"] = t_off
+            out[f"{k}_ref"] = a._ref_counts.numpy().astype(np.int32).copy()
+            out[f"{k}_free"] = np.asarray(list(a._free_list), np.int32)
+            out[f"{k}_stats"] = np.asarray(json.dumps(pool.stats()))
+    out["pairs"] = np.asarray(pairs, np.int32).reshape(-1, 2)
+    out["step_off"] = np.asarray(step_off, np.int64)
+    out["root_table"] = np.asarray(pool.get_block_ids(root), np.int32)
+    out["spec"] = np.asarray(json.dumps(spec.__dict__))
+    return out
+
+
 # ── E. copy / zero contents on the CPU path ──────────────────────────────────
 def copy_zero() -> dict:
     cfg = PoolConfig(total_blocks=32, block_size=4, num_layers=2, num_kv_heads=2, head_dim=8,
@@ -443,7 +499,8 @@ def main() -> None:
     ap.add_argument("--skip-full-match", action="store_true")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
-    todo = set(args.only.split(",")) if args.only else {"alloc", "tree", "quick", "tot", "copy", "match", "match_full"}
+    todo = set(args.only.split(",")) if args.only else {"alloc", "tree", "quick", "tot", "react", "copy", "match",
+                                                                   "match_full"}
     if "alloc" in todo:
         for seed, (n, iv, nops) in {1: (48, 5, 700), 2: (32, 3, 700), 3: (64, 64, 900), 4: (16, 2, 500)}.items():
             np.savez_compressed(OUT / f"alloc_trace_{seed}.npz", **alloc_trace(seed, n, iv, nops))
@@ -458,6 +515,9 @@ def main() -> None:
     if "tot" in todo:
         np.savez_compressed(OUT / "tot_8b.npz", **tot())
         print("tot")
+    if "react" in todo:
+        np.savez_compressed(OUT / "react_70b.npz", **react(W.ReActSpec()))
+        print("react")
     if "copy" in todo:
         (OUT / "copy_zero.json").write_text(json.dumps(copy_zero(), indent=0))
         print("copy/zero")

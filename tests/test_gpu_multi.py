@@ -1,9 +1,15 @@
-"""Two GPUs, NCCL: the KV-head sharded fan-out (needs >= 2 visible GPUs).
+"""Two GPUs, NCCL: the KV-head sharded pool (needs >= 2 visible GPUs).
 
-Rank 0 plans a Tree-of-Thought fan-out on its allocator and broadcasts each
-level's pair list; every rank copies its head slice.  Each rank's slice must
-equal the corresponding slice of a single-GPU copy of the same pool, and both
-ranks must have received the same pairs as rank 0 planned.
+* Rank 0 plans a Tree-of-Thought fan-out on its allocator and broadcasts each
+  level's pair list; every rank copies its head slice.  Each rank's slice must
+  equal the corresponding slice of a single-GPU copy of the same pool, and
+  both ranks must have received the same pairs as rank 0 planned.
+* The ReAct multi-agent trace (70B geometry, 1000 steps): rank 0 runs the
+  pool calls on a metadata-only pool and records each step's CoW pairs; each
+  step's batch (count + pairs) goes to every rank in one broadcast and each
+  rank copies its head slice with the count read on the device.  Every slice
+  must equal the same heads of the oracle's pool after the reference's
+  recorded pairs.
 """
 
 import os
@@ -74,6 +80,98 @@ def _worker(rank, port, q):
         q.put((rank, ok, same))
     finally:
         dist.destroy_process_group()
+
+
+def _react_worker(rank, port, q, golden):
+    import datetime
+    import json
+
+    import torch.distributed as dist
+
+    from agentkv_b200 import AgentKVPool, PoolConfig
+    from agentkv_b200 import sharded as S
+    from agentkv_b200 import workloads as W
+    from oracle import oracle as O
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        g = np.load(golden)
+        spec = W.ReActSpec(**json.loads(str(g["spec"])))
+        N_, bs, L, H, D, dt = W.LLAMA3_70B_GEOMETRY
+        gen = torch.Generator(device="cpu").manual_seed(21)
+        full = torch.randint(-30000, 30000, (N_, 1, 2, 2, bs, 32), dtype=torch.int16, generator=gen)
+        mine = S.head_slice(full, rank, WORLD).contiguous().to(dev)
+        copier = S.ShardedCopier(mine)
+        buf = copier.batch_buffer(spec.agents)
+        trace = W.react_trace(spec)
+        pairs_ok = True
+        if rank == 0:
+            meta = AgentKVPool(config=PoolConfig(total_blocks=N_, block_size=bs, num_layers=L, num_kv_heads=H,
+                                                 head_dim=D, dtype=dt, device="meta"))
+            rec = []
+            orig = meta._allocator.copy_block
+
+            def record(src, dst):
+                rec.append((src.block_id, dst.block_id))
+                orig(src, dst)
+
+            meta._allocator.copy_block = record
+
+            class Api:
+                def __getattr__(self, name):
+                    return getattr(meta, name)
+
+                @staticmethod
+                def residual_len(h):
+                    return len(h.residual_blocks)
+
+            api = Api()
+            root, agents = W.react_setup(api, spec)
+        so = g["step_off"]
+        for i, actions in enumerate(trace):
+            if rank == 0:
+                rec.clear()
+                W.react_step(api, root, agents, actions)
+                got = np.asarray(rec, np.int32).reshape(-1, 2)
+                pairs_ok &= np.array_equal(got, g["pairs"][so[i]:so[i + 1]])
+                copier.pack_batch(got, buf)
+            copier.share_batch(buf)
+            copier.copy_batch(buf)
+        torch.cuda.synchronize()
+        host = full.numpy().view(np.uint8).reshape(N_, -1).copy()
+        O.copy_blocks(host, host.shape[1], g["pairs"])
+        want = S.head_slice(torch.from_numpy(host.view(np.int16).reshape(full.shape)), rank, WORLD)
+        ok = bool(torch.equal(mine.cpu(), want.contiguous()))
+        q.put((rank, ok, bool(pairs_ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(target, extra=()):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=target, args=(r, port, q, *extra)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return sorted(q.get(timeout=5) for _ in range(WORLD))
+
+
+def test_sharded_react_two_gpus(golden_dir):
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+    res = _spawn(_react_worker, (str(golden_dir / "react_70b.npz"),))
+    assert all(ok for _, ok, _ in res), res
+    assert all(pairs_ok for _, _, pairs_ok in res), res
 
 
 def test_sharded_fanout_two_gpus():

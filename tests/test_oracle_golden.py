@@ -210,6 +210,37 @@ def test_oracle_tot_metadata(golden_dir):
     assert s["epoch"] == st["epoch"] and s["total_frees"] == st["total_frees"]
 
 
+def test_oracle_react_trace(golden_dir):
+    """The ReAct multi-agent trace (70B geometry, 40,000 blocks, 32 agents,
+    1000 steps): every step's CoW pairs, and at the checkpoints the agents'
+    block tables, refcounts, free list and counters, equal the reference's."""
+    from react_apis import OracleReActAPI
+
+    g = np.load(golden_dir / "react_70b.npz")
+    spec = W.ReActSpec(**json.loads(str(g["spec"])))
+    N_, bs = W.LLAMA3_70B_GEOMETRY[:2]
+    pairs = []
+    api = OracleReActAPI(N_, bs, copy_cb=lambda s, t: pairs.append((s, t)))
+    root, agents = W.react_setup(api, spec)
+    assert not pairs
+    np.testing.assert_array_equal(np.asarray(api.get_block_ids(root), np.int32), g["root_table"])
+    so = g["step_off"]
+    for i, actions in enumerate(W.react_trace(spec)):
+        W.react_step(api, root, agents, actions)
+        np.testing.assert_array_equal(np.asarray(pairs[so[i]:], np.int32).reshape(-1, 2),
+                                      g["pairs"][so[i]:so[i + 1]], err_msg=f"step {i}")
+        k = f"s{i + 1}"
+        if k + "_ref" in g.files:
+            tables = np.concatenate([np.asarray(api.get_block_ids(h), np.int32) for h in agents])
+            np.testing.assert_array_equal(tables, g[k + "_tables"])
+            s = api.alloc.state()
+            np.testing.assert_array_equal(s["ref_counts"], g[k + "_ref"])
+            np.testing.assert_array_equal(s["free_list"], g[k + "_free"])
+            st = json.loads(str(g[k + "_stats"]))
+            assert (s["epoch"], s["total_allocs"], s["total_frees"], s["peak_allocated"]) == \
+                (st["epoch"], st["total_allocs"], st["total_frees"], st["peak_allocated"])
+
+
 def test_oracle_copy_zero_contents(golden_dir):
     g = json.loads((golden_dir / "copy_zero.json").read_text())
     torch.manual_seed(g["seed"])

@@ -66,17 +66,65 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_sharded_pairs_and_slices_gloo():
+def _batch_worker(rank, world, port, q, golden):
+    """Variable-size batches (count + pairs in one buffer) of the ReAct
+    trace's recorded pairs, one broadcast per step."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import oracle as O
+
+        g = np.load(golden)
+        so = g["step_off"][:151]
+        n = int(g["pairs"][: so[-1]].max()) + 1
+        gen = torch.Generator().manual_seed(6)
+        full = torch.randint(-(2**30), 2**30, (n, 1, 2, 4, 2, 4), dtype=torch.int32, generator=gen)
+        mine = S.head_slice(full, rank, world).contiguous()
+        copier = S.ShardedCopier(mine)
+        buf = copier.batch_buffer(32)
+        host = mine.numpy().view(np.uint8).reshape(n, -1).copy()
+        counts = []
+        for i in range(len(so) - 1):
+            if rank == 0:
+                copier.pack_batch(g["pairs"][so[i]:so[i + 1]], buf)
+            copier.share_batch(buf)
+            k = int(copier.batch_count(buf)[0])
+            counts.append(k)
+            O.copy_blocks(host, host.shape[1], copier.batch_pairs(buf)[:k].numpy())
+        mine_after = torch.from_numpy(host.view(np.int32).reshape(mine.shape))
+        parts = [torch.empty_like(mine_after) for _ in range(world)]
+        dist.all_gather(parts, mine_after)
+        if rank == 0:
+            fhost = full.numpy().view(np.uint8).reshape(n, -1).copy()
+            O.copy_blocks(fhost, fhost.shape[1], g["pairs"][: so[-1]])
+            want = torch.from_numpy(fhost.view(np.int32).reshape(full.shape))
+            q.put((bool(torch.equal(torch.cat(parts, dim=3), want)), counts == np.diff(so).tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(target, extra=()):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=target, args=(r, WORLD, port, q, *extra)) for r in range(WORLD)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    same_pool, same_pairs = q.get(timeout=5)
+    return q.get(timeout=5)
+
+
+def test_variable_batches_gloo(golden_dir):
+    same_pool, counts_ok = _run(_batch_worker, (str(golden_dir / "react_70b.npz"),))
+    assert counts_ok, "receivers decoded other pair counts"
+    assert same_pool, "reassembled head slices differ from the unsharded copies"
+
+
+def test_sharded_pairs_and_slices_gloo():
+    same_pool, same_pairs = _run(_worker)
     assert same_pairs, "ranks saw different pair lists"
     assert same_pool, "reassembled head slices differ from the unsharded copy"
 
