@@ -24,7 +24,7 @@ warp per query.
 
 from __future__ import annotations
 
-from typing import Optional, Tuple
+from typing import Optional, Sequence, Tuple
 
 import numpy as np
 import torch
@@ -61,6 +61,19 @@ def tree_hash_np(parent: np.ndarray, token: np.ndarray) -> np.ndarray:
     return (k & np.uint64(0xFFFFFFFF)).astype(np.uint32)
 
 
+class _Changes:
+    """Changes of the host mirror not yet taken by one consumer (the local
+    device upload, or the replicas on other GPUs)."""
+
+    __slots__ = ("slots", "nodes", "tok_from", "full")
+
+    def __init__(self) -> None:
+        self.slots: set = set()
+        self.nodes: set = set()
+        self.tok_from = 0
+        self.full = True
+
+
 class DeviceTree:
     """Host mirror + HBM copy of the shared tree; see the module docstring."""
 
@@ -76,10 +89,9 @@ class DeviceTree:
         self.live = 0
         self.dead = 0
         self._slot_of: dict = {}  # (parent, token) -> slot index
-        self._dirty_slots: set = set()
-        self._dirty_nodes: set = set()
-        self._tok_flushed = 0
-        self._full = True  # next flush uploads everything
+        self._local = _Changes()  # for this GPU's arrays
+        self._peers: Optional[_Changes] = None  # for replicas (track_peers)
+        self._dev_tokens = 0  # tokens on the device
         self.d_tokens = torch.zeros(token_cap, dtype=torch.int32, device=device)
         self.d_off = torch.zeros(node_cap, dtype=torch.int64, device=device)
         self.d_len = torch.zeros(node_cap, dtype=torch.int32, device=device)
@@ -96,7 +108,7 @@ class DeviceTree:
             grown = np.zeros(cap, np.int32)
             grown[: self.n_tokens] = self.h_tokens[: self.n_tokens]
             self.h_tokens = grown
-            self._full = True
+            self._mark_full()
         off = self.n_tokens
         self.h_tokens[off:need] = toks
         self.n_tokens = need
@@ -113,10 +125,11 @@ class DeviceTree:
                 new = np.zeros(cap, old.dtype)
                 new[: len(old)] = old
                 setattr(self, name, new)
-            self._full = True
+            self._mark_full()
         self.h_off[nid] = off
         self.h_len[nid] = length
-        self._dirty_nodes.add(nid)
+        for c in self._trackers():
+            c.nodes.add(nid)
 
     def clear_node(self, nid: int) -> None:
         if nid < len(self.h_off):
@@ -154,7 +167,8 @@ class DeviceTree:
             self.live += 1
             self._slot_of[key] = s
         self.h_slots[s] = (parent, token, child, child_len)
-        self._dirty_slots.add(s)
+        for c in self._trackers():
+            c.slots.add(s)
 
     def del_child(self, parent: int, token: int) -> None:
         s = self._slot_of.pop((parent, token), None)
@@ -163,7 +177,8 @@ class DeviceTree:
         self.h_slots[s] = (DELETED, 0, 0, 0)
         self.live -= 1
         self.dead += 1
-        self._dirty_slots.add(s)
+        for c in self._trackers():
+            c.slots.add(s)
 
     def _rehash(self, min_slots: int) -> None:
         cap = 1
@@ -175,70 +190,119 @@ class DeviceTree:
         self.h_slots[:, 3] = 0
         self._slot_of = {}
         self.live = self.dead = 0
-        self._dirty_slots.clear()
         for (p, t), c, ln in entries:
             _, s = self._probe(p, t)
             self.h_slots[s] = (p, t, c, ln)
             self._slot_of[(p, t)] = s
             self.live += 1
-        self._full = True
+        self._mark_full()
+
+    def _trackers(self):
+        return (self._local,) if self._peers is None else (self._local, self._peers)
+
+    def _mark_full(self) -> None:
+        for c in self._trackers():
+            c.full = True
+            c.slots.clear()
+            c.nodes.clear()
+
+    def as_replica(self) -> None:
+        """This tree's device arrays come from another GPU's deltas
+        (apply_delta): its own (empty) host mirror is never uploaded."""
+        self._local.full = False
+
+    def track_peers(self) -> None:
+        """Also record changes for replicas on other GPUs (take_delta(peers=True));
+        the first peer delta is a full one."""
+        if self._peers is None:
+            self._peers = _Changes()
 
     # ── upload ───────────────────────────────────────────────────────────────
     def flush(self) -> None:
         """Ship pending changes to the device (on the current stream)."""
+        d = self.take_delta()
+        if d is not None:
+            self.apply_delta(d)
+
+    def take_delta(self, peers: bool = False) -> Optional[dict]:
+        """Changes of the host mirror not yet taken by this consumer (the local
+        upload, or with peers=True the replicas), as host arrays; None when
+        there are none.  A delta is either full (the whole arrays, after a
+        resize or rehash) or incremental (appended tokens, changed slots as
+        [slot, parent, token, child, child_len] rows, changed nodes as
+        [node, edge_off, edge_len] rows)."""
+        c = self._peers if peers else self._local
+        if c is None:
+            raise RuntimeError("take_delta(peers=True) needs track_peers() first")
+        if c.full:
+            d = {"full": True, "n_tokens": self.n_tokens, "tokens": self.h_tokens[: self.n_tokens],
+                 "token_cap": len(self.h_tokens), "off": self.h_off, "len": self.h_len, "slots": self.h_slots}
+            c.full = False
+        else:
+            lo, hi = c.tok_from, self.n_tokens
+            if hi == lo and not (c.nodes or c.slots):
+                return None
+            su = np.empty((len(c.slots), 5), np.int32)
+            if len(su):
+                idx = np.fromiter(c.slots, np.int64, len(c.slots))
+                su[:, 0] = idx
+                su[:, 1:] = self.h_slots[idx, :4]
+            nu = np.empty((len(c.nodes), 3), np.int64)
+            if len(nu):
+                idx = np.fromiter(c.nodes, np.int64, len(c.nodes))
+                nu[:, 0] = idx
+                nu[:, 1] = self.h_off[idx]
+                nu[:, 2] = self.h_len[idx]
+            d = {"full": False, "n_tokens": hi, "tok_lo": lo, "tokens": self.h_tokens[lo:hi], "su": su, "nu": nu}
+        c.tok_from = self.n_tokens
+        c.nodes.clear()
+        c.slots.clear()
+        return d
+
+    def apply_delta(self, d: dict) -> None:
+        """Bring the device arrays up to date with a delta (from take_delta on
+        this tree or, for a replica on another GPU, on the owner's tree).  Its
+        arrays may be host (numpy) or device tensors."""
         dev = self.device
-        if self._full:
-            if self.d_tokens.numel() < len(self.h_tokens):
-                self.d_tokens = torch.zeros(len(self.h_tokens), dtype=torch.int32, device=dev)
-            if self.d_off.numel() != len(self.h_off):
-                self.d_off = torch.zeros(len(self.h_off), dtype=torch.int64, device=dev)
-                self.d_len = torch.zeros(len(self.h_len), dtype=torch.int32, device=dev)
-            if self.d_slots.shape[0] != len(self.h_slots):
-                self.d_slots = torch.zeros((len(self.h_slots), 4), dtype=torch.int32, device=dev)
-            self.d_tokens[: self.n_tokens].copy_(torch.from_numpy(self.h_tokens[: self.n_tokens]))
-            self.d_off.copy_(torch.from_numpy(self.h_off))
-            self.d_len.copy_(torch.from_numpy(self.h_len))
-            self.d_slots.copy_(torch.from_numpy(self.h_slots))
-            self._tok_flushed = self.n_tokens
-            self._dirty_nodes.clear()
-            self._dirty_slots.clear()
-            self._full = False
+
+        def on_dev(a, dtype):
+            if isinstance(a, torch.Tensor):
+                return a.to(dev, dtype=dtype)
+            return torch.from_numpy(np.ascontiguousarray(a)).to(dev, dtype=dtype)
+
+        if d["full"]:
+            cap = int(d["token_cap"])
+            if self.d_tokens.numel() < cap:
+                self.d_tokens = torch.zeros(cap, dtype=torch.int32, device=dev)
+            n = int(d["n_tokens"])
+            if n:
+                self.d_tokens[:n].copy_(on_dev(d["tokens"], torch.int32))
+            self.d_off = on_dev(d["off"], torch.int64).clone()
+            self.d_len = on_dev(d["len"], torch.int32).clone()
+            self.d_slots = on_dev(d["slots"], torch.int32).reshape(-1, 4).clone()
+            self._dev_tokens = n
             self._view = None
             return
-        if self.n_tokens > self._tok_flushed:
-            lo, hi = self._tok_flushed, self.n_tokens
-            self.d_tokens[lo:hi].copy_(torch.from_numpy(self.h_tokens[lo:hi]))
-            self._tok_flushed = hi
+        lo, hi = int(d["tok_lo"]), int(d["n_tokens"])
+        if hi > lo:
+            self.d_tokens[lo:hi].copy_(on_dev(d["tokens"], torch.int32))
+            self._dev_tokens = hi
             self._view = None
-        if not (self._dirty_nodes or self._dirty_slots):
+        n_su, n_nu = len(d["su"]), len(d["nu"])
+        if n_su == 0 and n_nu == 0:
             return
-        su = None
-        nu = None
-        if self._dirty_slots:
-            idx = np.fromiter(self._dirty_slots, np.int64, len(self._dirty_slots))
-            su = np.empty((len(idx), 5), np.int32)
-            su[:, 0] = idx
-            su[:, 1:] = self.h_slots[idx, :4]
-        if self._dirty_nodes:
-            idx = np.fromiter(self._dirty_nodes, np.int64, len(self._dirty_nodes))
-            nu = np.empty((len(idx), 3), np.int64)
-            nu[:, 0] = idx
-            nu[:, 1] = self.h_off[idx]
-            nu[:, 2] = self.h_len[idx]
-        su_d = torch.from_numpy(su).to(dev) if su is not None else None
-        nu_d = torch.from_numpy(nu).to(dev) if nu is not None else None
+        su_d = on_dev(d["su"], torch.int32) if n_su else None
+        nu_d = on_dev(d["nu"], torch.int64) if n_nu else None
         N.check(N.lib.akv_tree_apply(
-            self.view(), su_d.data_ptr() if su_d is not None else None, 0 if su is None else len(su),
-            nu_d.data_ptr() if nu_d is not None else None, 0 if nu is None else len(nu),
+            self.view(), su_d.data_ptr() if su_d is not None else None, n_su,
+            nu_d.data_ptr() if nu_d is not None else None, n_nu,
             self.status.data_ptr(), stream_handle(dev)))
-        self._dirty_nodes.clear()
-        self._dirty_slots.clear()
 
     def view(self) -> N.AkvTreeView:
         if self._view is None:
             self._view = N.AkvTreeView(
                 self.d_tokens.data_ptr(), self.d_off.data_ptr(), self.d_len.data_ptr(),
-                self.d_slots.data_ptr(), self._tok_flushed, self.d_off.numel(), self.d_slots.shape[0] - 1)
+                self.d_slots.data_ptr(), self._dev_tokens, self.d_off.numel(), self.d_slots.shape[0] - 1)
         return self._view
 
     # ── lookups ──────────────────────────────────────────────────────────────
@@ -262,3 +326,46 @@ class DeviceTree:
             raise RuntimeError(
                 f"agentkv_b200 tree replica error: {N.ERROR_NAMES.get(int(s[0]), int(s[0]))} "
                 f"(query/update {int(s[1])}, node {int(s[2])})")
+
+
+# ── batched lookups on any tree replica ───────────────────────────────────────
+def pack_queries(queries: Sequence, device: torch.device) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Concatenate token sequences into device (tokens int32, offsets int64)."""
+    lens = np.fromiter((len(q) for q in queries), np.int64, len(queries))
+    q_off = np.zeros(len(queries) + 1, np.int64)
+    np.cumsum(lens, out=q_off[1:])
+    flat = np.empty(max(int(q_off[-1]), 1), np.int32)
+    for i, q in enumerate(queries):
+        flat[q_off[i] : q_off[i + 1]] = np.asarray(q, np.int32)
+    tok = torch.from_numpy(flat).pin_memory().to(device, non_blocking=True)
+    off = torch.from_numpy(q_off).pin_memory().to(device, non_blocking=True)
+    return tok, off
+
+
+def longest_first(q_off, device: torch.device) -> torch.Tensor:
+    """Launch order for akv_match_prefix: query indices by decreasing length
+    (stable), so the longest walks start first and spread over the SMs."""
+    q_off = np.asarray(q_off.cpu() if isinstance(q_off, torch.Tensor) else q_off, np.int64)
+    order = np.argsort(-np.diff(q_off), kind="stable").astype(np.int32)
+    return torch.from_numpy(order).pin_memory().to(device, non_blocking=True)
+
+
+def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_compared: bool = False):
+    """Longest shared prefix of many queries in one akv_match_prefix launch on
+    `tree` (the owner's replica or another GPU's): (node ids, match lengths
+    [, tokens compared]) as numpy arrays, each equal to the reference's
+    _match_prefix_locked (agentkv/core/radix_tree.py:513-570) on that query."""
+    dev = tree.device
+    nq = len(queries)
+    tok, q_off = pack_queries(queries, dev)
+    lens = np.fromiter((len(q) for q in queries), np.int64, nq)
+    order = torch.from_numpy(np.argsort(-lens, kind="stable").astype(np.int32)).to(dev)
+    node = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
+    mlen = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
+    cmp_ = torch.empty(max(nq, 1), dtype=torch.int64, device=dev) if with_compared else None
+    tree.match(tok, q_off, nq, block_size, node, mlen, cmp_, order=order)
+    tree.check()
+    res = (node[:nq].cpu().numpy(), mlen[:nq].cpu().numpy())
+    if with_compared:
+        res = res + (cmp_[:nq].cpu().numpy(),)
+    return res

@@ -34,7 +34,7 @@ import torch
 
 from .allocator import BlockHandle, SlabAllocator
 from .config import PoolConfig
-from .device_tree import DeviceTree
+from .device_tree import DeviceTree, longest_first, match_batch, pack_queries  # noqa: F401
 
 ROOT_NODE_ID: int = 0
 INVALID_NODE_ID: int = -1
@@ -320,20 +320,7 @@ class DualRadixTree:
         creating handles: (node ids, match lengths[, tokens compared]) as numpy
         arrays.  Each result equals _match_prefix_locked on that query."""
         with self._lock:
-            tok, q_off = pack_queries(queries, self._alloc.device)
-            nq = len(queries)
-            dev = self._alloc.device
-            lens = np.fromiter((len(q) for q in queries), np.int64, nq)
-            order = torch.from_numpy(np.argsort(-lens, kind="stable").astype(np.int32)).to(dev)
-            node = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
-            mlen = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
-            cmp_ = torch.empty(max(nq, 1), dtype=torch.int64, device=dev) if with_compared else None
-            self._dev_tree.match(tok, q_off, nq, self._cfg.block_size, node, mlen, cmp_, order=order)
-            self._dev_tree.check()
-            res = (node[:nq].cpu().numpy(), mlen[:nq].cpu().numpy())
-            if with_compared:
-                res = res + (cmp_[:nq].cpu().numpy(),)
-            return res
+            return match_batch(self._dev_tree, queries, self._cfg.block_size, with_compared=with_compared)
 
     def commit_prefix(self, handle: NodeHandle, length: int) -> None:
         with self._lock:
@@ -509,27 +496,6 @@ class DualRadixTree:
             )
         if handle.is_freed:
             raise ValueError(f"NodeHandle {handle.handle_id} has already been freed")
-
-
-def pack_queries(queries: Sequence, device: torch.device) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Concatenate token sequences into device (tokens int32, offsets int64)."""
-    lens = np.fromiter((len(q) for q in queries), np.int64, len(queries))
-    q_off = np.zeros(len(queries) + 1, np.int64)
-    np.cumsum(lens, out=q_off[1:])
-    flat = np.empty(max(int(q_off[-1]), 1), np.int32)
-    for i, q in enumerate(queries):
-        flat[q_off[i] : q_off[i + 1]] = np.asarray(q, np.int32)
-    tok = torch.from_numpy(flat).pin_memory().to(device, non_blocking=True)
-    off = torch.from_numpy(q_off).pin_memory().to(device, non_blocking=True)
-    return tok, off
-
-
-def longest_first(q_off, device: torch.device) -> torch.Tensor:
-    """Launch order for akv_match_prefix: query indices by decreasing length
-    (stable), so the longest walks start first and spread over the SMs."""
-    q_off = np.asarray(q_off.cpu() if isinstance(q_off, torch.Tensor) else q_off, np.int64)
-    order = np.argsort(-np.diff(q_off), kind="stable").astype(np.int32)
-    return torch.from_numpy(order).pin_memory().to(device, non_blocking=True)
 
 
 CoWRadixTree = DualRadixTree

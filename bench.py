@@ -441,61 +441,86 @@ def reference_arm(args, rank, world):
 
 # ── match_prefix figure ──────────────────────────────────────────────────────
 def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
-                 n_queries: int = W.MatchSpec.n_queries) -> dict:
+                 n_queries: int = W.MatchSpec.n_queries, rank: int = 0, world: int = 1) -> dict:
+    """match_prefix on the stress tree.  With N ranks, rank 0 builds the tree
+    through the pool API and broadcasts it (TreeReplicaSync) to every rank's
+    replica; each rank then matches its own 4096-query batches (weak
+    scaling), timed as the max over ranks."""
     import torch
 
     from agentkv_b200 import AgentKVPool, PoolConfig
-    from agentkv_b200.radix_tree import longest_first, pack_queries
+    from agentkv_b200.device_tree import DeviceTree, longest_first, pack_queries
+    from agentkv_b200.sharded_tree import TreeReplicaSync
 
     spec = W.MatchSpec(n_sequences=n_seqs, n_queries=n_queries)
     prefixes = W.match_prefixes(spec)
     corpus = W.match_sequences(spec, prefixes)
-    total_blocks = sum(-(-len(s) // 16) for s in corpus) + 16
-    cfg = PoolConfig(total_blocks=total_blocks, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1,
-                     dtype="float16", device="meta")
-    pool = AgentKVPool(config=cfg)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    build_s = 0.0
+    n_nodes = None
+    if rank == 0:
+        total_blocks = sum(-(-len(s) // 16) for s in corpus) + 16
+        cfg = PoolConfig(total_blocks=total_blocks, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1,
+                         dtype="float16", device="meta")
+        pool = AgentKVPool(config=cfg)
+        t0 = time.perf_counter()
+        for seq in corpus:
+            h = pool.create_root(seq)
+            pool.allocate_blocks(h, -(-len(seq) // 16) - len(pool.get_block_ids(h)))
+            share = (len(seq) // 16) * 16 - h.shared_match_len
+            if share > 0:
+                pool.commit_prefix(h, share)
+        build_s = time.perf_counter() - t0
+        tree = pool._tree._dev_tree
+        n_nodes = len(pool._tree._shared_nodes)
+    else:
+        tree = DeviceTree(dev)
     t0 = time.perf_counter()
-    for seq in corpus:
-        h = pool.create_root(seq)
-        pool.allocate_blocks(h, -(-len(seq) // 16) - len(pool.get_block_ids(h)))
-        share = (len(seq) // 16) * 16 - h.shared_match_len
-        if share > 0:
-            pool.commit_prefix(h, share)
-    build_s = time.perf_counter() - t0
-    tree = pool._tree
-    dev = pool._allocator.device
-    batches = [W.match_queries(spec, corpus, prefixes, batch=b) for b in range(4)]
+    if world > 1:
+        TreeReplicaSync(tree).sync()
+    else:
+        tree.flush()
+    torch.cuda.synchronize()
+    sync_s = time.perf_counter() - t0
+    batches = [W.match_queries(spec, corpus, prefixes, batch=rank * 4 + b) for b in range(4)]
     packed = [pack_queries(q, dev) for q in batches]
     orders = [longest_first(off, dev) for _, off in packed]
     nq = spec.n_queries
     node = torch.empty(nq, dtype=torch.int32, device=dev)
     mlen = torch.empty(nq, dtype=torch.int32, device=dev)
     cmp_ = torch.empty(nq, dtype=torch.int64, device=dev)
-    tree._dev_tree.flush()
     compared = []
     qtokens = []
     for (tok, off), order in zip(packed, orders):
-        tree._dev_tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order)
+        tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order)
         compared.append(int(cmp_.sum()))
         qtokens.append(int(off[-1]))
-    tree._dev_tree.check()
+    tree.check()
 
     def run():
         for (tok, off), order in zip(packed, orders):
-            tree._dev_tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order)
+            tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order)
 
-    ms, _ = timed(run, steps, warmup, 1)
+    ms, _ = timed(run, steps, warmup, world)
     per_batch_ms = ms / (steps * len(packed))
     tok_cmp = statistics.mean(compared)
+    if world > 1:
+        t = torch.tensor([tok_cmp], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t)
+        tok_cmp = float(t) / world
     return {
         "metric": "match_prefix queries/s (stress tree)",
-        "value": round(nq / (per_batch_ms / 1e3), 1),
+        "value": round(world * nq / (per_batch_ms / 1e3), 1),
         "unit": "queries/s",
-        "tokens_compared_per_ms": round(tok_cmp / per_batch_ms, 1),
+        "n_gpus": world,
+        "scaling": "weak",
+        "tokens_compared_per_ms": round(world * tok_cmp / per_batch_ms, 1),
+        "tokens_compared_per_ms_per_gpu": round(tok_cmp / per_batch_ms, 1),
         "ms_per_batch": round(per_batch_ms, 4),
-        "batch": nq,
-        "tree_nodes": len(tree._shared_nodes),
+        "batch_per_gpu": nq,
+        "tree_nodes": n_nodes,
         "tree_build_s": round(build_s, 1),
+        "replica_sync_s": round(sync_s, 2),
         "query_tokens_per_batch": int(statistics.mean(qtokens)),
     }
 
@@ -578,8 +603,17 @@ def main():
     if args.case == "match":
         import torch
 
-        torch.cuda.set_device(0)
-        print(json.dumps(match_figure(args.steps, args.warmup, args.match_seqs, args.match_queries)), flush=True)
+        torch.cuda.set_device(local)
+        if world > 1:
+            import datetime
+
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                                 device_id=torch.device("cuda", local))
+        fig = match_figure(args.steps, args.warmup, args.match_seqs, args.match_queries, rank, world)
+        if rank == 0:
+            print(json.dumps(fig), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
         return
     import torch
 

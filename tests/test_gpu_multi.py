@@ -10,6 +10,10 @@
   rank copies its head slice with the count read on the device.  Every slice
   must equal the same heads of the oracle's pool after the reference's
   recorded pairs.
+* match_prefix over replicas: rank 0 builds the stress tree through the pool
+  API and broadcasts its deltas as it grows; each rank matches its
+  contiguous range of the reference's recorded queries on its own replica;
+  the gathered results equal the reference's.
 """
 
 import os
@@ -149,6 +153,59 @@ def _react_worker(rank, port, q, golden):
         q.put((rank, ok, bool(pairs_ok)))
     finally:
         dist.destroy_process_group()
+
+
+def _match_worker(rank, port, q, golden):
+    import datetime
+    import json
+
+    import torch.distributed as dist
+
+    from agentkv_b200 import AgentKVPool, PoolConfig
+    from agentkv_b200 import workloads as W
+    from agentkv_b200.device_tree import DeviceTree
+    from agentkv_b200.sharded_tree import TreeReplicaSync, match_split
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        g = np.load(golden)
+        spec = W.MatchSpec(**json.loads(str(g["spec"])))
+        prefixes = W.match_prefixes(spec)
+        corpus = W.match_sequences(spec, prefixes)
+        if rank == 0:
+            pool = AgentKVPool(config=PoolConfig(total_blocks=int(g["total_blocks"]), block_size=16,
+                                                 num_layers=1, num_kv_heads=1, head_dim=1, dtype="float16",
+                                                 device="meta"))
+            tree = pool._tree._dev_tree
+        else:
+            tree = DeviceTree(dev)
+        sync = TreeReplicaSync(tree)
+        for i, seq in enumerate(corpus):
+            if rank == 0:
+                h = pool.create_root(seq)
+                pool.allocate_blocks(h, -(-len(seq) // 16) - len(pool.get_block_ids(h)))
+                share = (len(seq) // 16) * 16 - h.shared_match_len
+                if share > 0:
+                    pool.commit_prefix(h, share)
+            if i % 50 == 49 or i == len(corpus) - 1:
+                sync.sync()
+        queries = W.match_queries(spec, corpus, prefixes, batch=0, n=len(g["node"]))
+        node, mlen = match_split(sync, queries, 16)
+        ok = bool(np.array_equal(node, g["node"]) and np.array_equal(mlen, g["len"]))
+        q.put((rank, ok, True))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_match_split_over_replicas_two_gpus(golden_dir):
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+    res = _spawn(_match_worker, (str(golden_dir / "match_small.npz"),))
+    assert all(ok for _, ok, _ in res), res
 
 
 def _spawn(target, extra=()):

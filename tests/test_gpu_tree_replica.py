@@ -1,0 +1,64 @@
+"""Tree replicas: a second DeviceTree fed only with the owner's deltas
+(TreeReplicaSync.share, the arrays that a broadcast would carry) answers
+match_prefix exactly like the owner, on the reference's recorded stress
+queries, with deltas taken while the tree grows (full deltas after resizes
+and rehashes, incremental ones between)."""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from agentkv_b200 import AgentKVPool, PoolConfig
+from agentkv_b200 import workloads as W
+from agentkv_b200.device_tree import DeviceTree, match_batch
+from agentkv_b200.sharded_tree import TreeReplicaSync
+
+pytestmark = pytest.mark.gpu
+
+
+def test_replica_from_deltas_matches_reference(golden_dir):
+    g = np.load(golden_dir / "match_small.npz")
+    spec = W.MatchSpec(**json.loads(str(g["spec"])))
+    prefixes = W.match_prefixes(spec)
+    corpus = W.match_sequences(spec, prefixes)
+    cfg = PoolConfig(total_blocks=int(g["total_blocks"]), block_size=16, num_layers=1, num_kv_heads=1,
+                     head_dim=1, dtype="float16", device="meta")
+    pool = AgentKVPool(config=cfg)
+    owner = pool._tree._dev_tree
+    sync = TreeReplicaSync(owner)
+    replica = DeviceTree(owner.device)
+    replica.as_replica()
+    kinds = []
+    queries = W.match_queries(spec, corpus, prefixes, batch=0, n=len(g["node"]))
+    for i, seq in enumerate(corpus):
+        h = pool.create_root(seq)
+        pool.allocate_blocks(h, -(-len(seq) // 16) - len(pool.get_block_ids(h)))
+        share = (len(seq) // 16) * 16 - h.shared_match_len
+        if share > 0:
+            pool.commit_prefix(h, share)
+        if i % 37 == 0 or i == len(corpus) - 1:
+            d = sync.share()
+            if d is not None:
+                kinds.append(d["full"])
+                replica.apply_delta(d)
+            if i % 111 == 0:
+                # mid-build: the replica answers like the owner
+                n0, l0 = match_batch(owner, queries[:64], 16)
+                n1, l1 = match_batch(replica, queries[:64], 16)
+                np.testing.assert_array_equal(n1, n0)
+                np.testing.assert_array_equal(l1, l0)
+    assert any(kinds) and not all(kinds), kinds  # both full and incremental deltas
+    node, mlen, cmp_ = match_batch(replica, queries, 16, with_compared=True)
+    np.testing.assert_array_equal(node, g["node"])
+    np.testing.assert_array_equal(mlen, g["len"])
+    _, _, cmp_owner = match_batch(owner, queries, 16, with_compared=True)
+    np.testing.assert_array_equal(cmp_, cmp_owner)
+    # the arrays themselves are identical
+    n = owner.n_tokens
+    assert torch.equal(replica.d_tokens[:n], owner.d_tokens[:n])
+    assert torch.equal(replica.d_slots, owner.d_slots)
+    assert torch.equal(replica.d_off, owner.d_off) and torch.equal(replica.d_len, owner.d_len)
+    # nothing pending: share() says so
+    assert sync.share() is None

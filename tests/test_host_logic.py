@@ -118,3 +118,15 @@ def test_workloads_are_deterministic():
     assert all(512 <= len(x) <= 8192 for x in s1)
     assert W.quickstart_queries() == W.quickstart_queries()
     assert len(W.tot_root_tokens()) == 4096
+
+
+def test_query_ranges_cover_the_batch():
+    from agentkv_b200.sharded_tree import query_range
+
+    for n in (0, 1, 7, 256, 4096, 4097):
+        for w in (1, 2, 3, 8):
+            r = [query_range(n, i, w) for i in range(w)]
+            assert r[0][0] == 0 and r[-1][1] == n
+            assert all(r[i][1] == r[i + 1][0] for i in range(w - 1))
+            sizes = [b - a for a, b in r]
+            assert max(sizes) - min(sizes) <= 1

@@ -104,6 +104,102 @@ def _batch_worker(rank, world, port, q, golden):
         dist.destroy_process_group()
 
 
+class _HostReplica:
+    """What akv_tree_apply does to a replica's arrays, on the host."""
+
+    def __init__(self):
+        self.tokens = self.off = self.len = self.slots = None
+        self.n = 0
+
+    def apply(self, d):
+        if d["full"]:
+            self.tokens = np.zeros(int(d["token_cap"]), np.int32)
+            self.n = int(d["n_tokens"])
+            self.tokens[: self.n] = d["tokens"].numpy()
+            self.off = d["off"].numpy().copy()
+            self.len = d["len"].numpy().copy()
+            self.slots = d["slots"].numpy().reshape(-1, 4).copy()
+            return
+        lo, hi = int(d["tok_lo"]), int(d["n_tokens"])
+        self.tokens[lo:hi] = d["tokens"].numpy()
+        self.n = hi
+        for r in d["su"].numpy():
+            self.slots[r[0]] = r[1:]
+        for r in d["nu"].numpy():
+            self.off[r[0]] = r[1]
+            self.len[r[0]] = r[2]
+
+    def digest(self):
+        import hashlib
+
+        h = hashlib.sha256()
+        for a in (self.tokens[: self.n], self.off, self.len, self.slots):
+            h.update(np.ascontiguousarray(a).tobytes())
+        return int.from_bytes(h.digest()[:7], "little")
+
+
+def _tree_worker(rank, world, port, q):
+    """Rank 0 mutates a tree (nodes, edges, child slots, splits, deletions,
+    growth and rehash); after every round the deltas reach rank 1, whose
+    replica must equal rank 0's arrays."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from agentkv_b200.device_tree import DeviceTree
+        from agentkv_b200.sharded_tree import TreeReplicaSync
+
+        tree = DeviceTree(torch.device("cpu"), node_cap=8, slot_cap=16, token_cap=32)
+        sync = TreeReplicaSync(tree)
+        rep = _HostReplica()
+        rng = np.random.default_rng(9)
+        nodes = {0: None}  # node id -> (parent, first token)
+        next_id = 1
+        ok = True
+        for rnd in range(40):
+            if rank == 0:
+                for _ in range(int(rng.integers(0, 12))):
+                    op = rng.integers(0, 10)
+                    if op < 6 or len(nodes) < 3:
+                        parent = int(rng.choice(list(nodes)))
+                        toks = rng.integers(0, 1000, size=int(rng.integers(1, 40)), dtype=np.int32)
+                        off = tree.append_tokens(toks)
+                        tree.set_node(next_id, off, len(toks))
+                        tree.set_child(parent, int(toks[0]), next_id, len(toks))
+                        nodes[next_id] = (parent, int(toks[0]))
+                        next_id += 1
+                    elif op < 8:
+                        nid = int(rng.choice([k for k in nodes if k]))
+                        o, ln = int(tree.h_off[nid]), int(tree.h_len[nid])
+                        if ln > 1:
+                            tree.set_node(nid, o + 1, ln - 1)
+                    else:
+                        nid = int(rng.choice([k for k in nodes if k]))
+                        parent, tok = nodes.pop(nid)
+                        tree.del_child(parent, tok)
+                        tree.clear_node(nid)
+            d = sync.share()
+            if rank == 0:
+                rep.tokens, rep.n = tree.h_tokens, tree.n_tokens
+                rep.off, rep.len, rep.slots = tree.h_off, tree.h_len, tree.h_slots
+            elif d is not None:
+                rep.apply(d)
+            dig = torch.tensor([rep.digest()], dtype=torch.int64)
+            both = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+            dist.all_gather(both, dig)
+            ok &= bool(both[0] == both[1])
+        if rank == 0:
+            q.put((ok, next_id))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tree_replica_deltas_gloo():
+    ok, n_nodes = _run(_tree_worker)
+    assert n_nodes > 100
+    assert ok, "a replica built from the broadcast deltas differs from the owner's arrays"
+
+
 def _run(target, extra=()):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
