@@ -186,49 +186,111 @@ struct BulkDesc {
   uint32_t bytes;
 };
 
-// One issuing thread per CTA.  Items are (pair, chunk) in the global order
-// t = blockIdx.x + j * gridDim.x; invalid pairs are skipped by the load cursor
-// and the store cursor replays the loads' descriptors from shared memory.
-// CHUNK bytes per bulk copy, STAGES chunks in flight.
-template <int CHUNK, int STAGES>
+// Where a block's bytes live.  A block is `segs()` spans of `span()` bytes;
+// span s of block id starts at `at(s, id)`.
+// One pool (the AgentKV layout): block id is one span at pool + id * bpb.
+struct OnePool {
+  static constexpr bool kOneSpan = true;
+  char* pool;
+  int64_t bpb;
+  AKV_HD int64_t segs() const { return 1; }
+  AKV_HD int64_t span() const { return bpb; }
+  AKV_DEV char* at(int64_t, int32_t id) const { return pool + static_cast<int64_t>(id) * bpb; }
+  AKV_DEV bool valid(AkvStatus*) const { return true; }  // checked on the host
+};
+
+// Per-layer caches (a serving engine's K and V tensors, one per layer): span
+// s of block id is bytes [id * stride, id * stride + span) of cache s.
+struct LayerCaches {
+  static constexpr bool kOneSpan = false;
+  const uint64_t* __restrict__ bases;
+  int32_t n;
+  int64_t bytes;
+  int64_t stride;
+  AKV_HD int64_t segs() const { return n; }
+  AKV_HD int64_t span() const { return bytes; }
+  AKV_DEV char* at(int64_t s, int32_t id) const {
+    return reinterpret_cast<char*>(bases[s]) + static_cast<int64_t>(id) * stride;
+  }
+  // The cache addresses live in device memory, so the kernel checks them
+  // itself (one warp, every lane a share): every bulk copy needs 16-byte
+  // aligned addresses.
+  AKV_DEV bool valid(AkvStatus* st) const {
+    int32_t bad = n;
+    for (int32_t s = threadIdx.x; s < n; s += 32) {
+      if (bases[s] == 0 || (bases[s] & 15u) != 0) {
+        bad = s;
+        break;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) bad = min(bad, __shfl_xor_sync(0xffffffffu, bad, o));
+    if (bad < n && threadIdx.x == 0) akv_fail(st, AKV_ERR_INVALID_ARG, bad, -1, 0);
+    return bad == n;
+  }
+};
+
+// One issuing thread per CTA.  Items are (pair, span, chunk) in the global
+// order t = blockIdx.x + j * gridDim.x — pair-major (all chunks of pair 0,
+// then pair 1, ...) or, with CHUNK_MAJOR, chunk-major (chunk 0 of every pair,
+// then chunk 1, ...) so that the CTAs in flight at any moment touch many
+// blocks; invalid pairs are skipped by the load cursor and the store cursor
+// replays the loads' descriptors from shared memory.  CHUNK bytes per bulk
+// copy, STAGES chunks in flight.
+template <int CHUNK, int STAGES, typename Layout, bool CHUNK_MAJOR = false>
 __global__ void __launch_bounds__(32)
-k_copy_bulk(char* __restrict__ pool, int64_t bpb, int32_t total,
-            const int32_t* __restrict__ pairs, int32_t n_pairs, int64_t chunks_per_block,
-            const int32_t* __restrict__ refs, AkvStatus* st, const int64_t* __restrict__ n_dev) {
+k_copy_bulk(Layout lay, int32_t total, const int32_t* __restrict__ pairs, int32_t n_pairs,
+            int64_t chunks_per_span, const int32_t* __restrict__ refs, AkvStatus* st,
+            const int64_t* __restrict__ n_dev) {
   constexpr int kBulkChunk = CHUNK;
   constexpr int kBulkStages = STAGES;
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ __align__(8) uint64_t bars[kBulkStages];
   __shared__ BulkDesc desc[kBulkStages];
+  if (!lay.valid(st)) return;  // the whole warp takes part
   if (threadIdx.x != 0) return;
   if (akv_failed(st)) return;
   if (n_dev != nullptr) n_pairs = static_cast<int32_t>(min(static_cast<int64_t>(n_pairs), *n_dev));
   for (int s = 0; s < kBulkStages; ++s) mbar_init(smem_u32(&bars[s]), 1);
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 
-  const int64_t n_items = static_cast<int64_t>(n_pairs) * chunks_per_block;
+  const int64_t per_pair = lay.segs() * chunks_per_span;
+  const int64_t n_items = static_cast<int64_t>(n_pairs) * per_pair;
   int64_t t = blockIdx.x;
   // Advances t to the next valid item of this CTA; false at the end.
-  auto next_valid = [&](int32_t& src, int32_t& dst, int64_t& c) -> bool {
+  auto next_valid = [&](int32_t& src, int32_t& dst, int64_t& k) -> bool {
     while (t < n_items) {
-      const int32_t p = static_cast<int32_t>(t / chunks_per_block);
-      c = t - static_cast<int64_t>(p) * chunks_per_block;
-      if (pair_ok(pairs, p, total, refs, c == 0, st, src, dst)) return true;
+      int32_t p;
+      if constexpr (CHUNK_MAJOR) {
+        k = t / n_pairs;
+        p = static_cast<int32_t>(t - k * n_pairs);
+      } else {
+        p = static_cast<int32_t>(t / per_pair);
+        k = t - static_cast<int64_t>(p) * per_pair;
+      }
+      if (pair_ok(pairs, p, total, refs, k == 0, st, src, dst)) return true;
       t += gridDim.x;
     }
     return false;
   };
-  auto issue_load = [&](int64_t m, int32_t src, int32_t dst, int64_t c) {
+  auto issue_load = [&](int64_t m, int32_t src, int32_t dst, int64_t k) {
     const int s = static_cast<int>(m % kBulkStages);
-    const int64_t off = c * kBulkChunk;
-    const int64_t left = bpb - off;
+    int64_t seg = 0, off = k * kBulkChunk;
+    if constexpr (!Layout::kOneSpan) {
+      if (chunks_per_span != 1) {
+        seg = k / chunks_per_span;
+        off = (k - seg * chunks_per_span) * kBulkChunk;
+      } else {
+        seg = k;
+        off = 0;
+      }
+    }
+    const int64_t left = lay.span() - off;
     const uint32_t bytes = static_cast<uint32_t>(left < kBulkChunk ? left : kBulkChunk);
-    desc[s].dst = pool + static_cast<int64_t>(dst) * bpb + off;
+    desc[s].dst = lay.at(seg, dst) + off;
     desc[s].bytes = bytes;
     const uint32_t bar = smem_u32(&bars[s]);
     mbar_expect_tx(bar, bytes);
-    bulk_load(smem_u32(smem + static_cast<size_t>(s) * kBulkChunk),
-              pool + static_cast<int64_t>(src) * bpb + off, bytes, bar);
+    bulk_load(smem_u32(smem + static_cast<size_t>(s) * kBulkChunk), lay.at(seg, src) + off, bytes, bar);
   };
 
   int64_t loads = 0, stores = 0;
@@ -412,8 +474,8 @@ bool bulk_eligible(const void* pool, int64_t bpb) {
   return (reinterpret_cast<uintptr_t>(pool) % 16 == 0) && (bpb % 16 == 0);
 }
 
-template <int CHUNK, int STAGES, int CTAS_PER_SM>
-int copy_bulk_launch_t(char* pool, int64_t bpb, int32_t total, const int32_t* pairs, int32_t n,
+template <int CHUNK, int STAGES, int CTAS_PER_SM, typename Layout = OnePool, bool CHUNK_MAJOR = false>
+int copy_bulk_launch_t(Layout lay, int32_t total, const int32_t* pairs, int32_t n,
                        const int32_t* refs, AkvStatus* st, cudaStream_t s, const int64_t* n_dev) {
   // The shared-memory limit is a per-device function attribute: set it
   // once for each device this process launches on.
@@ -424,15 +486,18 @@ int copy_bulk_launch_t(char* pool, int64_t bpb, int32_t total, const int32_t* pa
   if (e != cudaSuccess) return akv_cuda_fail(e, "akv_copy_blocks(bulk): cudaGetDevice");
   const uint64_t bit = uint64_t{1} << (dev & 63);
   if (!(attr_set.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(k_copy_bulk<CHUNK, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = cudaFuncSetAttribute(k_copy_bulk<CHUNK, STAGES, Layout, CHUNK_MAJOR>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem);
     if (e != cudaSuccess) return akv_cuda_fail(e, "akv_copy_blocks(bulk): smem attribute");
     attr_set.fetch_or(bit, std::memory_order_release);
   }
-  const int64_t chunks = (bpb + CHUNK - 1) / CHUNK;
-  const int64_t work = chunks * n;
+  const int64_t chunks = (lay.span() + CHUNK - 1) / CHUNK;
+  const int64_t work = chunks * lay.segs() * n;
   const int64_t max_grid = static_cast<int64_t>(kAkvSMs) * CTAS_PER_SM;
   const int grid = static_cast<int>(work < max_grid ? work : max_grid);
-  k_copy_bulk<CHUNK, STAGES><<<grid, 32, smem, s>>>(pool, bpb, total, pairs, n, chunks, refs, st, n_dev);
+  k_copy_bulk<CHUNK, STAGES, Layout, CHUNK_MAJOR><<<grid, 32, smem, s>>>(lay, total, pairs, n, chunks, refs,
+                                                                        st, n_dev);
   AKV_LAUNCH_CHECK("akv_copy_blocks(bulk)");
   return AKV_OK;
 }
@@ -447,13 +512,18 @@ int copy_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* pair
                      const int32_t* refs, AkvStatus* st, cudaStream_t s,
                      const int64_t* n_dev = nullptr, int shape = 0) {
   if (shape == 0 && bpb < (int64_t{1} << 20)) shape = 3;
+  const OnePool lay{pool, bpb};
   switch (shape) {
-    case 1: return copy_bulk_launch_t<32768, 6, 1>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
-    case 2: return copy_bulk_launch_t<32768, 3, 2>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
-    case 3: return copy_bulk_launch_t<65536, 3, 1>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
-    case 4: return copy_bulk_launch_t<16384, 6, 2>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
-    case 5: return copy_bulk_launch_t<8192, 24, 1>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
-    default: return copy_bulk_launch_t<16384, 12, 1>(pool, bpb, total, pairs, n, refs, st, s, n_dev);
+    case 1: return copy_bulk_launch_t<32768, 6, 1>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 2: return copy_bulk_launch_t<32768, 3, 2>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 3: return copy_bulk_launch_t<65536, 3, 1>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 4: return copy_bulk_launch_t<16384, 6, 2>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 5: return copy_bulk_launch_t<8192, 24, 1>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 6: return copy_bulk_launch_t<32768, 3, 1, OnePool, true>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 7: return copy_bulk_launch_t<16384, 12, 1, OnePool, true>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 8: return copy_bulk_launch_t<32768, 6, 1, OnePool, true>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 9: return copy_bulk_launch_t<32768, 3, 1>(lay, total, pairs, n, refs, st, s, n_dev);
+    default: return copy_bulk_launch_t<16384, 12, 1>(lay, total, pairs, n, refs, st, s, n_dev);
   }
 }
 
@@ -476,12 +546,18 @@ int akv_blocks_prepare() {
   struct Item { const void* fn; int smem; const char* name; };
 #define AKV_ITEM(fn, smem) {reinterpret_cast<const void*>(fn), smem, "akv_prepare: " #fn}
   const Item items[] = {
-      AKV_ITEM((k_copy_bulk<16384, 12>), 16384 * 12),
-      AKV_ITEM((k_copy_bulk<32768, 6>), 32768 * 6),
-      AKV_ITEM((k_copy_bulk<32768, 3>), 32768 * 3),
-      AKV_ITEM((k_copy_bulk<65536, 3>), 65536 * 3),
-      AKV_ITEM((k_copy_bulk<16384, 6>), 16384 * 6),
-      AKV_ITEM((k_copy_bulk<8192, 24>), 8192 * 24),
+      AKV_ITEM((k_copy_bulk<16384, 12, OnePool>), 16384 * 12),
+      AKV_ITEM((k_copy_bulk<32768, 6, OnePool>), 32768 * 6),
+      AKV_ITEM((k_copy_bulk<32768, 3, OnePool>), 32768 * 3),
+      AKV_ITEM((k_copy_bulk<65536, 3, OnePool>), 65536 * 3),
+      AKV_ITEM((k_copy_bulk<16384, 6, OnePool>), 16384 * 6),
+      AKV_ITEM((k_copy_bulk<8192, 24, OnePool>), 8192 * 24),
+      AKV_ITEM((k_copy_bulk<32768, 3, OnePool, true>), 32768 * 3),
+      AKV_ITEM((k_copy_bulk<16384, 12, OnePool, true>), 16384 * 12),
+      AKV_ITEM((k_copy_bulk<32768, 6, OnePool, true>), 32768 * 6),
+      AKV_ITEM((k_copy_bulk<16384, 12, LayerCaches>), 16384 * 12),
+      AKV_ITEM((k_copy_bulk<32768, 6, LayerCaches>), 32768 * 6),
+      AKV_ITEM((k_copy_bulk<65536, 3, LayerCaches>), 65536 * 3),
       AKV_ITEM(k_zero_bulk, 0),
       AKV_ITEM((k_copy_vec<uint4, kVecThreads, kVecUnroll>), 0),
       AKV_ITEM((k_copy_vec<uint2, kVecThreads, kVecUnroll>), 0),
@@ -530,7 +606,7 @@ extern "C" int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int3
   AKV_ARG_CHECK(bytes_per_block > 0, "akv_copy_blocks: bytes_per_block=%lld",
                 static_cast<long long>(bytes_per_block));
   AKV_ARG_CHECK(total_blocks > 0, "akv_copy_blocks: total_blocks=%d", total_blocks);
-  AKV_ARG_CHECK(variant >= 0 && variant <= 7, "akv_copy_blocks: unknown variant %d", variant);
+  AKV_ARG_CHECK(variant >= 0 && variant <= 11, "akv_copy_blocks: unknown variant %d", variant);
   char* p = static_cast<char*>(pool);
   cudaStream_t s = akv_stream(stream);
   // Automatic choice: the bulk-async engine whenever the spans are 16-byte
@@ -547,6 +623,33 @@ extern "C" int akv_copy_blocks(void* pool, int64_t bytes_per_block, int32_t tota
                                AkvStatus* status, void* stream) {
   return akv_copy_blocks_variant(pool, bytes_per_block, total_blocks, pairs, n_pairs, ref_counts,
                                  status, 0, stream);
+}
+
+extern "C" int akv_copy_blocks_layers(const uint64_t* cache_bases, int32_t n_caches, int64_t block_bytes,
+                                      int64_t block_stride, int32_t total_blocks, const int32_t* pairs,
+                                      int32_t n_pairs, const int32_t* ref_counts, AkvStatus* status,
+                                      int32_t variant, void* stream) {
+  AKV_ARG_CHECK(n_pairs >= 0 && n_caches >= 0, "akv_copy_blocks_layers: n_pairs=%d n_caches=%d", n_pairs,
+                n_caches);
+  if (n_pairs == 0 || n_caches == 0) return AKV_OK;
+  AKV_ARG_CHECK(cache_bases != nullptr && pairs != nullptr, "akv_copy_blocks_layers: NULL caches or pairs");
+  AKV_ARG_CHECK(block_bytes > 0 && block_bytes % 16 == 0 && block_stride >= block_bytes &&
+                    block_stride % 16 == 0,
+                "akv_copy_blocks_layers: block_bytes=%lld block_stride=%lld (multiples of 16, stride >= "
+                "bytes)",
+                static_cast<long long>(block_bytes), static_cast<long long>(block_stride));
+  AKV_ARG_CHECK(total_blocks > 0, "akv_copy_blocks_layers: total_blocks=%d", total_blocks);
+  AKV_ARG_CHECK(variant >= 0 && variant <= 3, "akv_copy_blocks_layers: unknown variant %d", variant);
+  const LayerCaches lay{cache_bases, n_caches, block_bytes, block_stride};
+  cudaStream_t s = akv_stream(stream);
+  // Automatic: one chunk per span when the spans are 32 KiB multiples (the
+  // Llama-3 shapes), else 16 KiB chunks.
+  if (variant == 0) variant = (block_bytes % 32768 == 0) ? 2 : 1;
+  switch (variant) {
+    case 2: return copy_bulk_launch_t<32768, 6, 1>(lay, total_blocks, pairs, n_pairs, ref_counts, status, s, nullptr);
+    case 3: return copy_bulk_launch_t<65536, 3, 1>(lay, total_blocks, pairs, n_pairs, ref_counts, status, s, nullptr);
+    default: return copy_bulk_launch_t<16384, 12, 1>(lay, total_blocks, pairs, n_pairs, ref_counts, status, s, nullptr);
+  }
 }
 
 extern "C" int akv_copy_blocks_counted(void* pool, int64_t bytes_per_block, int32_t total_blocks,

@@ -11,6 +11,7 @@
 #define AKV_VERSION_MINOR 3
 
 #define AKV_DEV __device__ __forceinline__
+#define AKV_HD __host__ __device__ __forceinline__
 
 // Number of SMs on a B200; grids are sized in multiples of it.
 constexpr int kAkvSMs = 148;

@@ -16,7 +16,8 @@ reference's CPU path ``block.zero_()``; the reference's Triton kernel stores
 
 from __future__ import annotations
 
-from typing import Optional
+import weakref
+from typing import Optional, Sequence, Tuple
 
 import torch
 
@@ -201,6 +202,83 @@ def copy_blocks_counted(
             stream_handle(pool.device),
         )
     )
+
+
+_CACHE_TABLES: dict = {}
+
+
+def _cache_table(caches: Sequence[torch.Tensor]) -> Tuple[torch.Tensor, int, int, int]:
+    """Device table of the caches' base addresses plus (num_blocks,
+    block_bytes, block_stride), validated once per set of cache tensors (the
+    same tensor objects, in the same order, reuse the table)."""
+    if not caches:
+        raise ValueError("copy_blocks_layers: no caches")
+    key = tuple(map(id, caches))
+    hit = _CACHE_TABLES.get(key)
+    if hit is not None and all(r() is c for r, c in zip(hit[0], caches)):
+        return hit[1]
+    # new tensor objects over the same memory (an engine slicing K and V out
+    # of per-layer tensors on every call): reuse the table by address
+    akey = tuple((c.data_ptr(), c.stride(0), c.shape[0], c.numel(), c.element_size()) for c in caches)
+    hit = _CACHE_TABLES.get(akey)
+    if hit is not None:
+        return hit[1]
+    dev = caches[0].device
+    n = caches[0].shape[0]
+    esz = caches[0].element_size()
+    block_bytes = (caches[0].numel() // max(n, 1)) * esz
+    stride = caches[0].stride(0) * esz
+    for c in caches:
+        if c.device != dev:
+            raise ValueError("copy_blocks_layers: caches on different devices")
+        if c.shape[0] != n or (c.numel() // max(n, 1)) * c.element_size() != block_bytes:
+            raise ValueError("copy_blocks_layers: caches differ in block count or block size")
+        if c.stride(0) * c.element_size() != stride or not c[0].is_contiguous():
+            raise ValueError("copy_blocks_layers: every cache must hold each block as one span, "
+                             "all with the same block stride")
+        if c.data_ptr() % 16:
+            raise ValueError("copy_blocks_layers: cache base not 16-byte aligned")
+    if block_bytes % 16 or stride % 16 or stride < block_bytes:
+        raise ValueError(f"copy_blocks_layers: block bytes {block_bytes} / stride {stride} must be "
+                         "multiples of 16 with stride >= bytes")
+    table = torch.tensor([c.data_ptr() for c in caches], dtype=torch.int64).to(dev)
+    if len(_CACHE_TABLES) >= 32:
+        _CACHE_TABLES.clear()
+    res = (table, n, block_bytes, stride)
+    _CACHE_TABLES[key] = ([weakref.ref(c) for c in caches], res)
+    _CACHE_TABLES[akey] = (None, res)
+    return res
+
+
+def copy_blocks_layers(caches: Sequence[torch.Tensor], pairs, *, status: Optional[torch.Tensor] = None,
+                       variant: int = 0, check: bool = False) -> None:
+    """Copy every (src, dst) block pair in each of `caches` (tensors whose
+    first dim indexes blocks, e.g. one K and one V cache per layer) in one
+    launch; pairs must be independent."""
+    if caches and caches[0].device.type == "meta":
+        return
+    if not caches or not _require_cuda(caches[0], "copy_blocks_layers"):
+        return
+    table, n_blocks, block_bytes, stride = _cache_table(caches)
+    dev = caches[0].device
+    pairs_t = _as_device_i32(pairs, dev).reshape(-1, 2)
+    if pairs_t.shape[0] == 0:
+        return
+    st = status if status is not None else _status_buffer(dev)
+    N.check(N.lib.akv_copy_blocks_layers(
+        table.data_ptr(), len(caches), block_bytes, stride, n_blocks, pairs_t.data_ptr(), pairs_t.shape[0],
+        None, st.data_ptr(), int(variant), stream_handle(dev)))
+    if check:
+        raise_for_status(st)
+
+
+def copy_blocks_vllm(key_caches: Sequence[torch.Tensor], value_caches: Sequence[torch.Tensor],
+                     block_mapping, *, variant: int = 0) -> None:
+    """Drop-in for vLLM's `copy_blocks(key_caches, value_caches,
+    block_mapping)`: the blocks_to_copy pairs that the reference's vLLM
+    adapter returns from append_slots (integrations/vllm/block_manager.py:
+    134-167), applied to every layer's K and V cache in one launch."""
+    copy_blocks_layers(list(key_caches) + list(value_caches), block_mapping, variant=variant)
 
 
 def zero_blocks(

@@ -84,8 +84,9 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--match-seqs", type=int, default=W.MatchSpec.n_sequences)
     ap.add_argument("--match-queries", type=int, default=W.MatchSpec.n_queries)
-    ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match"],
-                    help="tot: the headline step; sweep: batched copy/zero sweep (prints its own line)")
+    ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers"],
+                    help="tot: the headline step; sweep: batched copy/zero sweep; match: match_prefix on the "
+                         "stress tree; layers: copies on vLLM's per-layer cache layout (each prints its own line)")
     ap.add_argument("--batches", default="1,8,64,512,4096", help="sweep batch sizes")
     ap.add_argument("--rotations", type=int, default=8, help="sweep: distinct pair sets cycled")
     return ap.parse_args()
@@ -577,6 +578,52 @@ def sweep_case(args) -> None:
     print(json.dumps(out), flush=True)
 
 
+def layers_case(args) -> None:
+    """Batched block copies on vLLM's per-layer cache layout at the
+    Llama-3-8B shape: 32 layers, each one [2, N, 16, 8, 128] bf16 tensor
+    (K and V), so a 2 MiB block is 64 spans of 32 KiB in 64 tensors; the
+    blocks_to_copy pairs go to kernels.copy_blocks_vllm (one launch)."""
+    import torch
+
+    from agentkv_b200 import kernels as K
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _, bs, L, H, D, _ = W.LLAMA3_8B_GEOMETRY
+    n_blocks = min(args.blocks, 30_000)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    kv = []
+    for _ in range(L):
+        t = torch.empty((2, n_blocks, bs, H, D), dtype=torch.bfloat16, device=dev)
+        t.normal_(generator=gen)
+        kv.append(t)
+    keys, values = [t[0] for t in kv], [t[1] for t in kv]
+    bpb = L * 2 * bs * H * D * 2
+    peak, peak_kind = measured_peak()
+    out = {"case": "vllm_layer_caches", "variant": args.variant, "layers": L, "cache_blocks": n_blocks, "bytes_per_block": bpb,
+           "span_bytes": bpb // (2 * L), "peak_gbs": peak, "peak_source": peak_kind, "batches": {}}
+    for n in [int(x) for x in args.batches.split(",")]:
+        if 2 * n > n_blocks:
+            continue
+        sets = [torch.from_numpy(W.copy_sweep_pairs(n, n_blocks, rotation=r)).to(dev)
+                for r in range(args.rotations)]
+        for i in range(args.warmup):
+            K.copy_blocks_vllm(keys, values, sets[i % len(sets)], variant=args.variant)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            K.copy_blocks_vllm(keys, values, sets[i % len(sets)], variant=args.variant)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        K.raise_for_status(K._status_buffer(dev))
+        gbs = 2 * bpb * n / (ms / 1e3) / 1e9
+        out["batches"][str(n)] = {"copy_ms": round(ms, 5), "copy_gbs": round(gbs, 1),
+                                  "copy_frac": round(gbs / peak, 4)}
+    print(json.dumps(out), flush=True)
+
+
 def level3_traffic():
     """DRAM bytes (read + write) of the level-3 copy launch from the committed
     ncu summary, or None."""
@@ -599,6 +646,9 @@ def main():
         return
     if args.case == "sweep":
         sweep_case(args)
+        return
+    if args.case == "layers":
+        layers_case(args)
         return
     if args.case == "match":
         import torch

@@ -99,13 +99,32 @@ AKV_API int akv_copy_blocks(void* pool, int64_t bytes_per_block, int32_t total_b
 /* Same, with an explicit kernel choice: 0 = automatic, 1 = 16-byte vector
  * loads/stores, 2 = bulk-async (TMA) copies staged through shared memory
  * (16 KiB chunks x 12 in flight for blocks >= 1 MiB, 64 KiB x 3 below, one
- * CTA per SM); 3-7 = fixed bulk shapes
+ * CTA per SM); 3-11 = fixed bulk shapes for tuning
  * (32 KiB x 6; 32 KiB x 3 with 2 CTAs per SM; 64 KiB x 3; 16 KiB x 6 with
- * 2 CTAs per SM; 8 KiB x 24) for tuning. */
+ * 2 CTAs per SM; 8 KiB x 24; chunk-major order (chunk c of every pair before
+ * chunk c + 1) with 32 KiB x 3, 16 KiB x 12, 32 KiB x 6; 32 KiB x 3). */
 AKV_API int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int32_t total_blocks,
                             const int32_t* pairs, int32_t n_pairs,
                             const int32_t* ref_counts, AkvStatus* status,
                             int32_t variant, void* stream);
+
+/* Copy of a batch of (src, dst) block pairs across a serving engine's
+ * per-layer KV caches: cache c holds block b at
+ * cache_bases[c] + b * block_stride (block_bytes bytes), and every pair is
+ * copied in every cache, all in one launch.  This is what vLLM's
+ * copy_blocks(key_caches, value_caches, block_mapping) does with the
+ * blocks_to_copy list that the reference's vLLM adapter returns from
+ * append_slots (integrations/vllm/block_manager.py:134-167); the caches'
+ * layout (one K and one V tensor per layer) differs from the AgentKV pool's.
+ * cache_bases is a DEVICE array of n_caches addresses; each must be 16-byte
+ * aligned (the kernel checks and reports AKV_ERR_INVALID_ARG), as must
+ * block_bytes and block_stride (checked here).  Pairs must be independent;
+ * ref_counts, when non-NULL, is checked as in akv_copy_blocks.  variant:
+ * 0 = automatic, 1/2/3 = bulk chunks of 16/32/64 KiB (12/6/3 in flight). */
+AKV_API int akv_copy_blocks_layers(const uint64_t* cache_bases, int32_t n_caches, int64_t block_bytes,
+                           int64_t block_stride, int32_t total_blocks, const int32_t* pairs,
+                           int32_t n_pairs, const int32_t* ref_counts, AkvStatus* status,
+                           int32_t variant, void* stream);
 
 /* akv_copy_blocks with the pair count in device memory: `pairs` has room for
  * n_max pairs and the kernel reads the int64 *n_dev (written by an earlier
