@@ -120,7 +120,8 @@ AKV_API int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int32_t
  * aligned (the kernel checks and reports AKV_ERR_INVALID_ARG), as must
  * block_bytes and block_stride (checked here).  Pairs must be independent;
  * ref_counts, when non-NULL, is checked as in akv_copy_blocks.  variant:
- * 0 = automatic, 1/2/3 = bulk chunks of 16/32/64 KiB (12/6/3 in flight). */
+ * 0 = automatic (= 4), 1/2/3/4 = bulk chunks of 16/32/64/32 KiB, 12/6/3/3
+ * in flight per SM. */
 AKV_API int akv_copy_blocks_layers(const uint64_t* cache_bases, int32_t n_caches, int64_t block_bytes,
                            int64_t block_stride, int32_t total_blocks, const int32_t* pairs,
                            int32_t n_pairs, const int32_t* ref_counts, AkvStatus* status,

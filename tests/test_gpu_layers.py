@@ -32,8 +32,9 @@ def _pairs(n_blocks, n, seed):
     return np.stack([perm[:n], perm[n:]], 1).copy()
 
 
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("n_layers,n_blocks,bs,H,D", [(4, 64, 16, 2, 64), (32, 40, 16, 8, 128), (3, 17, 8, 1, 8)])
-def test_flash_layout_kv_caches(n_layers, n_blocks, bs, H, D):
+def test_flash_layout_kv_caches(n_layers, n_blocks, bs, H, D, variant):
     """vLLM's flash-attention layout: one [2, N, bs, H, D] tensor per layer."""
     kv = [_rand((2, n_blocks, bs, H, D), torch.bfloat16, 100 + i) for i in range(n_layers)]
     keys, values = [t[0] for t in kv], [t[1] for t in kv]
@@ -42,7 +43,7 @@ def test_flash_layout_kv_caches(n_layers, n_blocks, bs, H, D):
         pairs = _pairs(n_blocks, n, n)
         for h in host:
             O.copy_blocks(h, h.shape[1], pairs)
-        K.copy_blocks_vllm(keys, values, torch.from_numpy(pairs).long())
+        K.copy_blocks_vllm(keys, values, torch.from_numpy(pairs).long(), variant=variant)
         torch.cuda.synchronize()
         for c, h in zip(keys + values, host):
             assert np.array_equal(_host_blocks(c), h), n
