@@ -129,6 +129,8 @@ SIGNATURES = {
     "akv_copy_blocks": (C.c_int, [_P, _I64, _I32, _P, _I32, _P, _P, _P]),
     "akv_copy_blocks_variant": (C.c_int, [_P, _I64, _I32, _P, _I32, _P, _P, _I32, _P]),
     "akv_copy_blocks_counted": (C.c_int, [_P, _I64, _I32, _P, _I32, _P, _P, _P, _P]),
+    "akv_kv_gather": (C.c_int, [_P, _I32, _I32, _I32, _I32, _I64, _I32, _P, _I32, _I64, _P, _P, _P, _P]),
+    "akv_kv_scatter": (C.c_int, [_P, _I32, _I32, _I32, _I32, _I64, _I32, _P, _I32, _P, _P, _I64, _I64, _P, _P]),
     "akv_copy_blocks_layers": (C.c_int, [_P, _I32, _I64, _I64, _I32, _P, _I32, _P, _P, _I32, _P]),
     "akv_zero_blocks": (C.c_int, [_P, _I64, _I32, _P, _I32, _P, _P, _P]),
     "akv_zero_blocks_variant": (C.c_int, [_P, _I64, _I32, _P, _I32, _P, _P, _I32, _P]),

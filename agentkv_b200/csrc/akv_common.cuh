@@ -63,6 +63,7 @@ int akv_blocks_prepare();
 int akv_alloc_prepare();
 int akv_tree_prepare();
 int akv_fanout_prepare();
+int akv_kvio_prepare();
 
 #define AKV_ARG_CHECK(cond, ...)              \
   do {                                        \

@@ -281,6 +281,61 @@ def copy_blocks_vllm(key_caches: Sequence[torch.Tensor], value_caches: Sequence[
     copy_blocks_layers(list(key_caches) + list(value_caches), block_mapping, variant=variant)
 
 
+def _kv_geometry(pool: torch.Tensor) -> Tuple[int, int, int, int, int, int]:
+    """(total_blocks, layers, heads, block_size, head_dim, row_bytes) of a
+    contiguous [N, L, 2, H, bs, D] pool."""
+    if pool.dim() != 6 or pool.shape[2] != 2 or not pool.is_contiguous():
+        raise ValueError("kv pool must be a contiguous [blocks, layers, 2, heads, block_size, head_dim] tensor")
+    n, L, _, H, bs, D = pool.shape
+    return n, L, H, bs, D, D * pool.element_size()
+
+
+def kv_gather(pool: torch.Tensor, block_ids, layer: int, n_tokens: int, *,
+              status: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Layer `layer`'s K and V of a sequence stored in blocks `block_ids`, as
+    two contiguous [1, heads, n_tokens, head_dim] tensors, in one launch."""
+    n, L, H, bs, D, row = _kv_geometry(pool)
+    dev = pool.device
+    ids = _as_device_i32(block_ids, dev).reshape(-1)
+    out_k = torch.empty((1, H, n_tokens, D), dtype=pool.dtype, device=dev)
+    out_v = torch.empty((1, H, n_tokens, D), dtype=pool.dtype, device=dev)
+    if n_tokens == 0 or not _require_cuda(pool, "kv_gather"):
+        return out_k, out_v
+    st = status if status is not None else _status_buffer(dev)
+    N.check(N.lib.akv_kv_gather(pool.data_ptr(), n, L, H, bs, row, int(layer), ids.data_ptr(), ids.numel(),
+                                int(n_tokens), out_k.data_ptr(), out_v.data_ptr(), st.data_ptr(),
+                                stream_handle(dev)))
+    return out_k, out_v
+
+
+def kv_scatter(pool: torch.Tensor, slots, layer: int, key_states: torch.Tensor, value_states: torch.Tensor, *,
+               status: Optional[torch.Tensor] = None) -> None:
+    """Write new tokens' K and V rows ([1, heads, n, head_dim] states, head_dim
+    contiguous) of layer `layer` to pool slots (block * block_size + position)
+    in one launch."""
+    n, L, H, bs, D, row = _kv_geometry(pool)
+    if not _require_cuda(pool, "kv_scatter"):
+        return
+    dev = pool.device
+    # states in another dtype or on another device are converted, as the
+    # reference's indexed assignment into the pool converts them
+    k = key_states[0].to(device=dev, dtype=pool.dtype)
+    v = value_states[0].to(device=dev, dtype=pool.dtype)
+    for t in (k, v):
+        if t.shape != (H, k.shape[1], D):
+            raise ValueError(f"kv_scatter: states must be [1, {H}, n, {D}], got {tuple(t.shape)}")
+    if k.stride() != v.stride() or k.stride(2) != 1:
+        k, v = k.contiguous(), v.contiguous()
+    s = _as_device_i32(slots, dev).reshape(-1)
+    if s.numel() != k.shape[1]:
+        raise ValueError("kv_scatter: one slot per new token")
+    esz = pool.element_size()
+    st = status if status is not None else _status_buffer(dev)
+    N.check(N.lib.akv_kv_scatter(pool.data_ptr(), n, L, H, bs, row, int(layer), s.data_ptr(), s.numel(),
+                                 k.data_ptr(), v.data_ptr(), k.stride(0) * esz, k.stride(1) * esz,
+                                 st.data_ptr(), stream_handle(dev)))
+
+
 def zero_blocks(
     pool: torch.Tensor,
     ids,

@@ -237,3 +237,68 @@ def react_step(api, root, agents: list, actions) -> None:
             api.maybe_advance_epoch()
         else:
             api.allocate_block(agents[s])
+
+
+# ── HuggingFace cache decode script ──────────────────────────────────────────
+@dataclass(frozen=True)
+class HFSpec:
+    """A small HF-cache session: a 10-token prompt prefilled on a root agent,
+    8 tokens committed to the shared tree, 3 forks decoding one token per
+    step (three tokens at step 2), the root decoding too."""
+
+    total_blocks: int = 64
+    block_size: int = 4
+    num_layers: int = 2
+    num_kv_heads: int = 2
+    head_dim: int = 16
+    dtype: str = "float16"
+    prompt: int = 10
+    commit: int = 8
+    forks: int = 3
+    steps: int = 6
+    seed: int = 6
+
+
+def hf_script(spec: HFSpec) -> List[Tuple[str, int, int]]:
+    """Events (kind, agent, n): prefill agent 0 with n tokens, commit n tokens
+    of agent 0, fork agent 0 (the new agent gets the next index), update
+    agent with n new tokens."""
+    ev = [("prefill", 0, spec.prompt), ("commit", 0, spec.commit)]
+    ev += [("fork", 0, 0)] * spec.forks
+    for step in range(spec.steps):
+        for a in range(1, spec.forks + 1):
+            ev.append(("update", a, 3 if step == 2 else 1))
+        if step % 2 == 0:
+            ev.append(("update", 0, 1))
+    return ev
+
+
+def hf_states(spec: HFSpec, event: int, layer: int, n: int) -> Tuple[np.ndarray, np.ndarray]:
+    """Seeded K and V states [1, heads, n, head_dim] of one update."""
+    rng = np.random.Generator(np.random.PCG64(spec.seed * 1_000_003 + event * 101 + layer))
+    shape = (1, spec.num_kv_heads, n, spec.head_dim)
+    return (rng.standard_normal(shape).astype(spec.dtype), rng.standard_normal(shape).astype(spec.dtype))
+
+
+def hf_run(spec: HFSpec, pool, cache_cls, to_tensor, on_output) -> list:
+    """Play hf_script through `pool` (the AgentKVPool API) and `cache_cls`
+    (the AgentKVCache API); on_output(event, layer, out_k, out_v) sees every
+    update's result.  Returns the agents' caches."""
+    caches = []
+    for e, (kind, a, n) in enumerate(hf_script(spec)):
+        if kind == "prefill":
+            h = pool.create_root(list(range(100, 100 + n)))
+            c = cache_cls(pool, h)
+            c._seen_tokens = 0
+            caches.append(c)
+            kind = "update"
+        if kind == "commit":
+            pool.commit_prefix(caches[a].handle, n)
+        elif kind == "fork":
+            caches.append(caches[a].fork())
+        elif kind == "update":
+            for layer in range(spec.num_layers):
+                k, v = hf_states(spec, e, layer, n)
+                ok, ov = caches[a].update(to_tensor(k), to_tensor(v), layer)
+                on_output(e, layer, ok, ov)
+    return caches

@@ -84,9 +84,10 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--match-seqs", type=int, default=W.MatchSpec.n_sequences)
     ap.add_argument("--match-queries", type=int, default=W.MatchSpec.n_queries)
-    ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers"],
+    ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers", "hf"],
                     help="tot: the headline step; sweep: batched copy/zero sweep; match: match_prefix on the "
-                         "stress tree; layers: copies on vLLM's per-layer cache layout (each prints its own line)")
+                         "stress tree; layers: copies on vLLM's per-layer cache layout; hf: the HF cache's "
+                         "per-layer K/V gather (each prints its own line)")
     ap.add_argument("--batches", default="1,8,64,512,4096", help="sweep batch sizes")
     ap.add_argument("--rotations", type=int, default=8, help="sweep: distinct pair sets cycled")
     return ap.parse_args()
@@ -624,6 +625,64 @@ def layers_case(args) -> None:
     print(json.dumps(out), flush=True)
 
 
+def hf_case(args) -> None:
+    """The HF cache's per-layer K/V assembly at the Llama-3-8B shape: a
+    4096-token sequence in 256 scattered blocks, all 32 layers (one decode
+    step's gathers), kernels.kv_gather against the reference's GPU path for
+    the same result (indexing gather, permute, reshape, truncation)."""
+    import torch
+
+    from agentkv_b200 import kernels as K
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    _, bs, L, H, D, _ = W.LLAMA3_8B_GEOMETRY
+    n_blocks, n_tok = 4096, 4096
+    pool = torch.empty((n_blocks, L, 2, H, bs, D), dtype=torch.bfloat16, device=dev)
+    pool.normal_(generator=torch.Generator(device=dev).manual_seed(7))
+    rng = np.random.default_rng(7)
+    tables = [torch.from_numpy(rng.permutation(n_blocks)[: n_tok // bs].astype(np.int32)).to(dev)
+              for _ in range(4)]
+    tables_l = [t.long() for t in tables]
+
+    def ours(i):
+        for layer in range(L):
+            K.kv_gather(pool, tables[i % 4], layer, n_tok)
+
+    def torch_path(i):
+        for layer in range(L):
+            data = pool[tables_l[i % 4], layer]
+            k = data[:, 0].permute(1, 0, 2, 3).reshape(1, H, -1, D)[:, :, :n_tok]
+            v = data[:, 1].permute(1, 0, 2, 3).reshape(1, H, -1, D)[:, :, :n_tok]
+            del k, v
+
+    k0, v0 = K.kv_gather(pool, tables[0], 5, n_tok)
+    data = pool[tables_l[0], 5]
+    assert torch.equal(k0, data[:, 0].permute(1, 0, 2, 3).reshape(1, H, -1, D))
+    assert torch.equal(v0, data[:, 1].permute(1, 0, 2, 3).reshape(1, H, -1, D))
+    res = {}
+    for name, fn in (("kv_gather", ours), ("torch_index_permute", torch_path)):
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        alg = 2 * 2 * H * n_tok * D * 2 * L  # read + write of K and V, all layers
+        res[name] = {"ms_per_decode_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / L, 2),
+                     "gbs_algorithmic": round(alg / (ms / 1e3) / 1e9, 1)}
+    peak, peak_kind = measured_peak()
+    res["kv_gather"]["frac"] = round(res["kv_gather"]["gbs_algorithmic"] / peak, 4)
+    print(json.dumps({"case": "hf_cache_gather", "tokens": n_tok, "layers": L, "heads": H, "head_dim": D,
+                      "peak_gbs": peak, "peak_source": peak_kind, **res,
+                      "speedup": round(res["torch_index_permute"]["ms_per_decode_step"] /
+                                       res["kv_gather"]["ms_per_decode_step"], 2)}), flush=True)
+
+
 def level3_traffic():
     """DRAM bytes (read + write) of the level-3 copy launch from the committed
     ncu summary, or None."""
@@ -649,6 +708,9 @@ def main():
         return
     if args.case == "layers":
         layers_case(args)
+        return
+    if args.case == "hf":
+        hf_case(args)
         return
     if args.case == "match":
         import torch

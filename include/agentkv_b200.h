@@ -139,6 +139,32 @@ AKV_API int akv_copy_blocks_counted(void* pool, int64_t bytes_per_block, int32_t
                             const int32_t* pairs, int32_t n_max, const int64_t* n_dev,
                             const int32_t* ref_counts, AkvStatus* status, void* stream);
 
+/* One model layer's K and V out of the pool as contiguous tensors: for a
+ * sequence whose blocks are block_ids[0..n_blocks) (device array), writes
+ * out_k and out_v, each [num_kv_heads, n_tokens, head_dim] (row_bytes =
+ * head_dim x element size per row), from layer `layer` of those blocks;
+ * n_tokens <= n_blocks x block_size (the last block may be partly used).
+ * Replaces the gather + permute + reshape + truncation of
+ * AgentKVCache.update / to_legacy_cache
+ * (agentkv/hf_cache.py:129-153, :196-215) with one launch.  Out-of-range
+ * ids are reported (AKV_ERR_OUT_OF_RANGE) and their tiles skipped. */
+AKV_API int akv_kv_gather(const void* pool, int32_t total_blocks, int32_t num_layers, int32_t num_kv_heads,
+                  int32_t block_size, int64_t row_bytes, int32_t layer, const int32_t* block_ids,
+                  int32_t n_blocks, int64_t n_tokens, void* out_k, void* out_v, AkvStatus* status,
+                  void* stream);
+
+/* New tokens' K and V rows of one layer into the pool: token i's rows go to
+ * block slots[i] / block_size, position slots[i] % block_size (slots is a
+ * device array).  k_src / v_src hold head h, token i at
+ * base + h * src_stride_head + i * src_stride_token (strides in BYTES, the
+ * head_dim row contiguous).  Replaces AgentKVCache.update's per-token row
+ * writes (agentkv/hf_cache.py:100-127) with one launch; the caller does the
+ * copy-on-write checks before it, as the reference does. */
+AKV_API int akv_kv_scatter(void* pool, int32_t total_blocks, int32_t num_layers, int32_t num_kv_heads,
+                   int32_t block_size, int64_t row_bytes, int32_t layer, const int32_t* slots, int32_t n_new,
+                   const void* k_src, const void* v_src, int64_t src_stride_head, int64_t src_stride_token,
+                   AkvStatus* status, void* stream);
+
 /* akv_zero_blocks replaces triton_kernels.zero_block / _zero_block_kernel
  * (agentkv/core/triton_kernels.py:206-229, :134-162) and
  * SlabAllocator.zero_block (agentkv/core/slab_allocator.py:321-334).  It

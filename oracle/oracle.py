@@ -557,3 +557,73 @@ def match_prefix_csr(csr: dict, tokens: np.ndarray, q_off: np.ndarray, block_siz
         _ptr(node), _ptr(mlen), _ptr(cmp_),
     )
     return node[:nq], mlen[:nq], cmp_[:nq]
+
+
+# ── HuggingFace cache (agentkv/hf_cache.py) ──────────────────────────────────
+class OracleKVPool:
+    """A pool's calls the HF cache uses — OracleTree over OracleAllocator plus
+    a host array [N, L, 2, H, bs, D] standing for _kv_data (zero-filled, as
+    slab_allocator.py:155-164 creates it); CoW copies move its rows."""
+
+    def __init__(self, total_blocks, block_size, num_layers, num_kv_heads, head_dim, dtype) -> None:
+        self.kv = np.zeros((total_blocks, num_layers, 2, num_kv_heads, block_size, head_dim), dtype)
+        self.alloc = OracleAllocator(total_blocks)
+        self.tree = OracleTree(self.alloc, block_size, copy_cb=self._copy)
+        self.block_size = block_size
+        self.num_layers = num_layers
+
+    def _copy(self, src: int, dst: int) -> None:
+        self.kv[dst] = self.kv[src]
+
+    def __getattr__(self, name):
+        return getattr(self.tree, name)
+
+
+class OracleKVCache:
+    """AgentKVCache restated (agentkv/hf_cache.py:38-185) on OracleKVPool."""
+
+    def __init__(self, pool: OracleKVPool, handle: _Handle) -> None:
+        self.pool = pool
+        self.handle = handle
+        self._seen_tokens = len(handle.tokens)
+        self._next_seen_tokens = self._seen_tokens
+
+    def get_seq_length(self, layer_idx: int = 0) -> int:
+        return self._seen_tokens
+
+    # hf_cache.py:57-160
+    def update(self, key_states: np.ndarray, value_states: np.ndarray, layer_idx: int):
+        if key_states.shape[0] != 1:
+            raise ValueError("AgentKVCache requires batch_size=1")
+        p, h, bs = self.pool, self.handle, self.pool.block_size
+        n_new = key_states.shape[2]
+        if layer_idx == 0:
+            self._next_seen_tokens = self._seen_tokens + n_new
+            required = (self._next_seen_tokens + bs - 1) // bs
+            while len(p.tree.get_block_ids(h)) < required:
+                p.tree.allocate_block(h)
+            if len(h.tokens) < self._next_seen_tokens:
+                p.tree.append_tokens(h, [0] * (self._next_seen_tokens - len(h.tokens)))
+        for i in range(n_new):
+            tok = self._seen_tokens + i
+            blk, pos = tok // bs, tok % bs
+            ridx = blk - h.shared_match_len // bs
+            if ridx < 0:
+                raise RuntimeError("Cannot overwrite shared prefix blocks!")
+            if layer_idx == 0 and (i == 0 or pos == 0):
+                p.tree.ensure_mutable_block(h, ridx)
+            b = p.tree.get_block_ids(h)[blk]
+            p.kv[b, layer_idx, 0, :, pos, :] = key_states[0, :, i, :]
+            p.kv[b, layer_idx, 1, :, pos, :] = value_states[0, :, i, :]
+        ids = p.tree.get_block_ids(h)
+        data = p.kv[ids, layer_idx]  # [nb, 2, H, bs, D]
+        H, D = data.shape[2], data.shape[4]
+        out_k = data[:, 0].transpose(1, 0, 2, 3).reshape(1, H, -1, D)[:, :, : self._next_seen_tokens]
+        out_v = data[:, 1].transpose(1, 0, 2, 3).reshape(1, H, -1, D)[:, :, : self._next_seen_tokens]
+        if layer_idx == p.num_layers - 1:
+            self._seen_tokens = self._next_seen_tokens
+        return out_k, out_v
+
+    # hf_cache.py:162-170
+    def fork(self) -> "OracleKVCache":
+        return OracleKVCache(self.pool, self.pool.tree.fork(self.handle))

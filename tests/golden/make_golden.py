@@ -421,6 +421,32 @@ def react(spec: W.ReActSpec, checkpoints=(200, 1000)) -> dict:
     return out
 
 
+# ── D3. HuggingFace cache session (reference AgentKVCache on a CPU pool) ───
+def hf_session(spec: W.HFSpec) -> dict:
+    from agentkv.hf_cache import AgentKVCache
+
+    cfg = PoolConfig(total_blocks=spec.total_blocks, block_size=spec.block_size, num_layers=spec.num_layers,
+                     num_kv_heads=spec.num_kv_heads, head_dim=spec.head_dim, dtype=spec.dtype, device="cpu")
+    pool = AgentKVPool(config=cfg)
+    outs, keys = [], []
+
+    def on_output(e, layer, ok, ov):
+        keys.append((e, layer, ok.shape[2]))
+        outs.append(np.concatenate([ok.numpy().reshape(-1), ov.numpy().reshape(-1)]))
+
+    caches = W.hf_run(spec, pool, AgentKVCache, torch.from_numpy, on_output)
+    tables = [np.asarray(pool.get_block_ids(c.handle), np.int32) for c in caches]
+    t_off = np.zeros(len(tables) + 1, np.int64)
+    np.cumsum([len(t) for t in tables], out=t_off[1:])
+    return {
+        "out_keys": np.asarray(keys, np.int64), "outs": np.concatenate(outs),
+        "tables": np.concatenate(tables), "tables_off": t_off,
+        "seen": np.asarray([c.get_seq_length() for c in caches], np.int64),
+        "pool": pool._allocator._kv_data.numpy().copy(),
+        "spec": np.asarray(json.dumps(spec.__dict__)),
+    }
+
+
 # ── E. copy / zero contents on the CPU path ──────────────────────────────────
 def copy_zero() -> dict:
     cfg = PoolConfig(total_blocks=32, block_size=4, num_layers=2, num_kv_heads=2, head_dim=8,
@@ -499,8 +525,8 @@ def main() -> None:
     ap.add_argument("--skip-full-match", action="store_true")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
-    todo = set(args.only.split(",")) if args.only else {"alloc", "tree", "quick", "tot", "react", "copy", "match",
-                                                                   "match_full"}
+    todo = set(args.only.split(",")) if args.only else {"alloc", "tree", "quick", "tot", "react", "hf", "copy",
+                                                                   "match", "match_full"}
     if "alloc" in todo:
         for seed, (n, iv, nops) in {1: (48, 5, 700), 2: (32, 3, 700), 3: (64, 64, 900), 4: (16, 2, 500)}.items():
             np.savez_compressed(OUT / f"alloc_trace_{seed}.npz", **alloc_trace(seed, n, iv, nops))
@@ -518,6 +544,9 @@ def main() -> None:
     if "react" in todo:
         np.savez_compressed(OUT / "react_70b.npz", **react(W.ReActSpec()))
         print("react")
+    if "hf" in todo:
+        np.savez_compressed(OUT / "hf_session.npz", **hf_session(W.HFSpec()))
+        print("hf")
     if "copy" in todo:
         (OUT / "copy_zero.json").write_text(json.dumps(copy_zero(), indent=0))
         print("copy/zero")

@@ -241,6 +241,29 @@ def test_oracle_react_trace(golden_dir):
                 (st["epoch"], st["total_allocs"], st["total_frees"], st["peak_allocated"])
 
 
+def test_oracle_hf_session(golden_dir):
+    """The HF cache session (prefill, commit, forks, decode with CoW): every
+    update's K/V output, the final block tables and the final pool bytes
+    equal the reference's AgentKVCache on a CPU pool."""
+    g = np.load(golden_dir / "hf_session.npz")
+    spec = W.HFSpec(**json.loads(str(g["spec"])))
+    pool = O.OracleKVPool(spec.total_blocks, spec.block_size, spec.num_layers, spec.num_kv_heads,
+                          spec.head_dim, spec.dtype)
+    outs, keys = [], []
+
+    def on_output(e, layer, ok, ov):
+        keys.append((e, layer, ok.shape[2]))
+        outs.append(np.concatenate([ok.reshape(-1), ov.reshape(-1)]))
+
+    caches = W.hf_run(spec, pool, O.OracleKVCache, lambda a: a, on_output)
+    np.testing.assert_array_equal(np.asarray(keys), g["out_keys"])
+    assert np.concatenate(outs).tobytes() == g["outs"].tobytes()
+    tables = np.concatenate([np.asarray(pool.get_block_ids(c.handle), np.int32) for c in caches])
+    np.testing.assert_array_equal(tables, g["tables"])
+    assert [c.get_seq_length() for c in caches] == g["seen"].tolist()
+    assert pool.kv.tobytes() == g["pool"].tobytes()
+
+
 def test_oracle_copy_zero_contents(golden_dir):
     g = json.loads((golden_dir / "copy_zero.json").read_text())
     torch.manual_seed(g["seed"])
