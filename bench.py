@@ -627,7 +627,8 @@ def layers_case(args) -> None:
 
 def hf_case(args) -> None:
     """The HF cache's per-layer K/V assembly at the Llama-3-8B shape: a
-    4096-token sequence in 256 scattered blocks, all 32 layers (one decode
+    4096-token sequence in 256 blocks scattered over a pool of up to 4096
+    (--blocks), all 32 layers (one decode
     step's gathers), kernels.kv_gather against the reference's GPU path for
     the same result (indexing gather, permute, reshape, truncation)."""
     import torch
@@ -637,7 +638,7 @@ def hf_case(args) -> None:
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     _, bs, L, H, D, _ = W.LLAMA3_8B_GEOMETRY
-    n_blocks, n_tok = 4096, 4096
+    n_blocks, n_tok = max(256, min(args.blocks, 4096)), 4096
     pool = torch.empty((n_blocks, L, 2, H, bs, D), dtype=torch.bfloat16, device=dev)
     pool.normal_(generator=torch.Generator(device=dev).manual_seed(7))
     rng = np.random.default_rng(7)
