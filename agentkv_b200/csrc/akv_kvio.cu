@@ -20,6 +20,7 @@
 namespace {
 
 constexpr int kKvThreads = 128;
+constexpr int kKvUnroll = 4;
 
 template <typename W>
 __global__ void __launch_bounds__(kKvThreads)
@@ -49,7 +50,21 @@ k_kv_gather(const char* __restrict__ pool, int64_t bpb, int32_t total, int32_t H
     W* __restrict__ dst = reinterpret_cast<W*>((kv ? out_v : out_k) +
                                                (static_cast<int64_t>(h) * n_tokens + first) * row_bytes);
     const int64_t words = rows * row_bytes / static_cast<int64_t>(sizeof(W));
-    for (int64_t w = threadIdx.x; w < words; w += kKvThreads) dst[w] = src[w];
+    // all of a thread's loads of a pass are issued before its stores, so a
+    // 4 KiB tile is one round trip to HBM
+    for (int64_t base = threadIdx.x; base < words; base += kKvThreads * kKvUnroll) {
+      W r[kKvUnroll];
+#pragma unroll
+      for (int u = 0; u < kKvUnroll; ++u) {
+        const int64_t w = base + static_cast<int64_t>(u) * kKvThreads;
+        if (w < words) r[u] = src[w];
+      }
+#pragma unroll
+      for (int u = 0; u < kKvUnroll; ++u) {
+        const int64_t w = base + static_cast<int64_t>(u) * kKvThreads;
+        if (w < words) dst[w] = r[u];
+      }
+    }
   }
 }
 

@@ -297,8 +297,8 @@ def kv_gather(pool: torch.Tensor, block_ids, layer: int, n_tokens: int, *,
     n, L, H, bs, D, row = _kv_geometry(pool)
     dev = pool.device
     ids = _as_device_i32(block_ids, dev).reshape(-1)
-    out_k = torch.empty((1, H, n_tokens, D), dtype=pool.dtype, device=dev)
-    out_v = torch.empty((1, H, n_tokens, D), dtype=pool.dtype, device=dev)
+    out = torch.empty((2, 1, H, n_tokens, D), dtype=pool.dtype, device=dev)  # one allocation for K and V
+    out_k, out_v = out[0], out[1]
     if n_tokens == 0 or not _require_cuda(pool, "kv_gather"):
         return out_k, out_v
     st = status if status is not None else _status_buffer(dev)
