@@ -100,7 +100,8 @@ def test_reference_fork_and_cow_flow():
         c1.update(torch.ones(2, 2, 1, 16, device=DEV), torch.ones(2, 2, 1, 16, device=DEV), 0)
 
 
-@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 12), (torch.float32, 7)])
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 12), (torch.float32, 7),
+                                     (torch.bfloat16, 256)])  # the last: 8 KiB tiles, the general kernel
 def test_gather_scatter_kernels(dtype, D):
     n, L, H, bs = 40, 3, 4, 16
     pool = torch.zeros((n, L, 2, H, bs, D), dtype=dtype, device=DEV)
