@@ -59,6 +59,7 @@ CTL_RELEASED = 14
 CTL_WORDS = 16
 AUX_WORDS = 2048
 NOALLOC_MAX_BLOCKS = 262144
+MAX_FANOUT_LEVELS = 16  # AKV_MAX_FANOUT_LEVELS
 
 # Copy kernel variants (akv_copy_blocks_variant).
 VARIANT_AUTO = 0
@@ -153,6 +154,7 @@ SIGNATURES = {
         [C.POINTER(AkvAllocState), _P, _I64, _P, _I32, _P, _P, _P, C.POINTER(AkvTick), _P, _P],
     ),
     "akv_fanout_plan": (C.c_int, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P]),
+    "akv_fanout_tree_plan": (C.c_int, [_P, _P, _I32, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),
     "akv_tree_hash": (C.c_uint32, [_I32, _I32]),
     "akv_tree_apply": (C.c_int, [C.POINTER(AkvTreeView), _P, _I32, _P, _I32, _P, _P]),
     "akv_match_prefix": (

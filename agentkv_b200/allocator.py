@@ -446,46 +446,66 @@ class SlabAllocator:
 
         The end state equals the reference's per-child sequence (fork,
         ensure_mutable_block(-1), `append` allocate_block calls, level after
-        level): every round's allocations and plan run first, in order — they
-        fix which ids each child gets — then one inc_ref batch for all forks
-        and one dec_ref batch for all copy-on-write sources.  Every CoW source
-        keeps a refcount >= 1 throughout, so no id retires and the order of
-        the refcount updates cannot change the result.  No copy is made:
-        `pairs[l]` lists round l's (src, dst) block copies, ready once
-        `on_level(l)` has been called (e.g. to record an event) — copy them
-        on any stream after that point.  Returns per-round device tensors
-        child_tables / pairs and the launch count."""
+        level): one alloc batch takes every round's ids in the order the
+        per-child calls pop them (nothing is freed in between, so one batch
+        pops exactly what the rounds' batches would), one plan launch per
+        round, then one inc_ref batch for all forks and one dec_ref batch for
+        all copy-on-write sources.  Every CoW source keeps a refcount >= 1
+        throughout, so no id retires and the order of the refcount updates
+        cannot change the result.  No copy is made: `pairs[l]` lists round
+        l's (src, dst) block copies, ready once `on_level(l)` has been called
+        (e.g. to record an event) — copy them on any stream after that point.
+        `all_pairs` holds every round's pairs back to back; with append >= 1
+        (`independent`) no pair's source is another pair's destination (a
+        child's last block, the next round's source, is an appended block),
+        so all rounds may be copied in one launch.  Returns per-round device
+        tensors child_tables / pairs, all_pairs, independent and the launch
+        count."""
         K, A = int(fanout), int(append)
         lens = np.asarray(root_lens, np.int64)
         if (lens < 1).any():
             raise ValueError("fanout_tree: every root needs at least one residual block")
         dev = self._dev
+        shapes, l_ = [], lens
+        for _ in range(levels):
+            shapes.append((len(l_), int(l_.sum())))
+            l_ = np.repeat(l_ + A, K)
+        n_fresh = sum((1 + A) * P * K for P, _ in shapes)
+        n_pairs = sum(P * K for P, _ in shapes)
+        fresh_all = self.alloc_batch(n_fresh)
+        all_pairs = torch.empty((n_pairs, 2), dtype=torch.int32, device=dev)
+        if A >= 1 and 0 < levels <= N.MAX_FANOUT_LEVELS and n_pairs:
+            return self._fanout_tree_fused(root_tables, lens, shapes, K, A, fresh_all, all_pairs,
+                                           level_offsets, on_level)
         tables = root_tables
         out_tables, out_pairs, incs, decs = [], [], [], []
-        launches = 0
-        for lvl in range(levels):
-            P, nc, total = len(lens), len(lens) * K, int(lens.sum())
+        launches = 1
+        f0 = p0 = 0
+        for lvl, (P, total) in enumerate(shapes):
+            nc = P * K
             if level_offsets is not None:
                 off_d = level_offsets[lvl]
             else:
                 off = np.zeros(P + 1, np.int64)
                 np.cumsum(lens, out=off[1:])
                 off_d = torch.from_numpy(off).to(dev, non_blocking=True)
-            fresh = self.alloc_batch((1 + A) * nc)
+            fresh = fresh_all[f0 : f0 + (1 + A) * nc]
+            pairs = all_pairs[p0 : p0 + nc]
+            f0 += (1 + A) * nc
+            p0 += nc
             child_tables = torch.empty(K * total + nc * A, dtype=torch.int32, device=dev)
             child_off = torch.empty(nc + 1, dtype=torch.int64, device=dev)
             inc_ids = torch.empty(K * total, dtype=torch.int32, device=dev)
-            pairs = torch.empty(2 * nc, dtype=torch.int32, device=dev)
             dec_ids = torch.empty(nc, dtype=torch.int32, device=dev)
             with self._lock:
                 N.check(N.lib.akv_fanout_plan(tables.data_ptr(), off_d.data_ptr(), P, K, A, fresh.data_ptr(),
                                               child_tables.data_ptr(), child_off.data_ptr(), inc_ids.data_ptr(),
                                               pairs.data_ptr(), dec_ids.data_ptr(), self._stream()))
-            launches += 2
+            launches += 1
             if on_level is not None:
                 on_level(lvl)
             out_tables.append(child_tables)
-            out_pairs.append(pairs.view(-1, 2))
+            out_pairs.append(pairs)
             incs.append(inc_ids)
             decs.append(dec_ids)
             tables = child_tables
@@ -493,7 +513,44 @@ class SlabAllocator:
         self.inc_ref_batch(torch.cat(incs) if len(incs) > 1 else incs[0])
         self.dec_ref_batch(torch.cat(decs) if len(decs) > 1 else decs[0])
         launches += 2 + 4
-        return {"child_tables": out_tables, "pairs": out_pairs, "launches": launches}
+        return {"child_tables": out_tables, "pairs": out_pairs, "all_pairs": all_pairs,
+                "independent": A >= 1, "launches": launches}
+
+    def _fanout_tree_fused(self, root_tables, lens, shapes, K, A, fresh_all, all_pairs, level_offsets,
+                           on_level) -> dict:
+        """fanout_tree's rounds as one akv_fanout_tree_plan launch (append >= 1)."""
+        dev = self._dev
+        n_tab = sum(K * total + P * K * A for P, total in shapes)
+        n_inc = sum(K * total for _, total in shapes)
+        n_kids = all_pairs.shape[0]
+        tables = torch.empty(n_tab, dtype=torch.int32, device=dev)
+        incs = torch.empty(n_inc, dtype=torch.int32, device=dev)
+        decs = torch.empty(n_kids, dtype=torch.int32, device=dev)
+        if level_offsets is not None:
+            off_d = level_offsets[0]
+        else:
+            off = np.zeros(len(lens) + 1, np.int64)
+            np.cumsum(lens, out=off[1:])
+            off_d = torch.from_numpy(off).to(dev, non_blocking=True)
+        with self._lock:
+            N.check(N.lib.akv_fanout_tree_plan(root_tables.data_ptr(), off_d.data_ptr(), len(lens), int(lens.sum()),
+                                               K, A, len(shapes), fresh_all.data_ptr(), tables.data_ptr(),
+                                               incs.data_ptr(), all_pairs.data_ptr(), decs.data_ptr(),
+                                               self._stream()))
+        out_tables, out_pairs = [], []
+        t0 = p0 = 0
+        for lvl, (P, total) in enumerate(shapes):
+            nt, nc = K * total + P * K * A, P * K
+            out_tables.append(tables[t0 : t0 + nt])
+            out_pairs.append(all_pairs[p0 : p0 + nc])
+            t0 += nt
+            p0 += nc
+            if on_level is not None:
+                on_level(lvl)
+        self.inc_ref_batch(incs)
+        self.dec_ref_batch(decs)
+        return {"child_tables": out_tables, "pairs": out_pairs, "all_pairs": all_pairs, "independent": True,
+                "launches": 2 + 2 + 4}
 
     def copy_blocks(self, pairs, *, check_refs: bool = True) -> None:
         """Copy a batch of independent (src, dst) pairs; dsts must be exclusive."""

@@ -13,6 +13,8 @@
 #define AKV_DEV __device__ __forceinline__
 #define AKV_HD __host__ __device__ __forceinline__
 
+constexpr int kAkvMaxFanoutLevels = AKV_MAX_FANOUT_LEVELS;
+
 // Number of SMs on a B200; grids are sized in multiples of it.
 constexpr int kAkvSMs = 148;
 

@@ -56,10 +56,120 @@ __global__ void k_fanout_plan(const int32_t* __restrict__ parent_tables,
   }
 }
 
+// All levels of a fan-out in one launch, for append >= 1.  With appended
+// blocks every child's table follows from the root's table and the fresh ids
+// of its ancestors alone: for a child x at level l with ancestors a_0..a_l
+// (a_l = x),
+//   T(x) = root[:-1] ++ [cow(a_0)] ++ app(a_0)[:-1] ++ ... ++ [cow(a_l)] ++ app(a_l)
+// (each child drops its parent's last block, an appended block, for its CoW
+// copy and adds `append` blocks), so no level waits for the previous one.
+// Child g (global index, levels back to back, (parent, child) order within
+// a level) owns fresh ids [(1+A) g, (1+A)(g+1)): its CoW block, then its
+// appended blocks — the ids the per-child calls take.  The outputs are laid
+// out exactly as the per-level launches of k_fanout_plan would write them,
+// level after level.
+struct TreeShape {
+  int32_t levels, K, A, R;
+  int64_t first[kAkvMaxFanoutLevels + 1];  // first global child of each level
+  int64_t kpow[kAkvMaxFanoutLevels + 1];   // K^l
+  int64_t tab_base[kAkvMaxFanoutLevels];   // level l's child tables in child_tables
+  int64_t inc_base[kAkvMaxFanoutLevels];   // level l's fork inc_ref ids in inc_ids
+};
+
+__global__ void k_fanout_tree_plan(const int32_t* __restrict__ root_tables, const int64_t* __restrict__ root_off,
+                                   const int32_t* __restrict__ fresh, TreeShape sh,
+                                   int32_t* __restrict__ child_tables, int32_t* __restrict__ inc_ids,
+                                   int32_t* __restrict__ pairs, int32_t* __restrict__ dec_ids) {
+  const int64_t total = sh.first[sh.levels];
+  const int32_t A = sh.A;
+  const int64_t base = root_off[0];
+  for (int64_t g = blockIdx.x; g < total; g += gridDim.x) {
+    int l = 0;
+    while (g >= sh.first[l + 1]) ++l;
+    const int64_t c = g - sh.first[l];
+    const int64_t per_root = sh.kpow[l + 1];
+    const int32_t r = static_cast<int32_t>(c / per_root);
+    const int64_t i_r = c - r * per_root;
+    const int64_t lo = root_off[r] - base;
+    const int64_t L0 = root_off[r + 1] - root_off[r];
+    const int32_t* __restrict__ root = root_tables + lo;
+    // fresh-id base of the ancestor at level m: (1+A) * (first[m] + c / K^(l-m))
+    auto anc = [&](int m) -> int64_t { return (1 + A) * (sh.first[m] + c / sh.kpow[l - m]); };
+    // element j of the table of the ancestor at level `top` (a table of
+    // L0 + (top+1) A entries)
+    auto elem = [&](int top, int64_t j) -> int32_t {
+      if (j < L0 - 1) return root[j];
+      const int64_t k = j - (L0 - 1);
+      int64_t m = k / A, e = k - m * A;
+      if (m > top) {
+        m = top;
+        e = A;
+      }
+      return fresh[anc(static_cast<int>(m)) + e];
+    };
+    const int64_t len_x = L0 + static_cast<int64_t>(l + 1) * A;
+    const int64_t toff = sh.tab_base[l] + per_root * (lo + static_cast<int64_t>(r) * (l + 1) * A) + i_r * len_x;
+    for (int64_t j = threadIdx.x; j < len_x; j += blockDim.x) child_tables[toff + j] = elem(l, j);
+    // the fork's inc_ref of every block of the parent's table
+    const int64_t len_p = L0 + static_cast<int64_t>(l) * A;
+    const int64_t ioff = sh.inc_base[l] + per_root * (lo + static_cast<int64_t>(r) * l * A) + i_r * len_p;
+    for (int64_t j = threadIdx.x; j < len_p; j += blockDim.x)
+      inc_ids[ioff + j] = l == 0 ? root[j] : elem(l - 1, j);
+    if (threadIdx.x == 0) {
+      const int32_t src = l == 0 ? root[L0 - 1] : fresh[anc(l - 1) + A];
+      pairs[2 * g] = src;
+      pairs[2 * g + 1] = fresh[anc(l)];
+      dec_ids[g] = src;
+    }
+  }
+}
+
 }  // namespace
 
 int akv_fanout_prepare() {
+  if (int rc = akv_load_kernel(reinterpret_cast<const void*>(k_fanout_tree_plan), "akv_prepare: k_fanout_tree_plan"))
+    return rc;
   return akv_load_kernel(reinterpret_cast<const void*>(k_fanout_plan), "akv_prepare: k_fanout_plan");
+}
+
+extern "C" int akv_fanout_tree_plan(const int32_t* root_tables, const int64_t* root_off, int32_t n_roots,
+                                    int64_t root_blocks, int32_t fanout, int32_t append, int32_t levels,
+                                    const int32_t* fresh_ids, int32_t* child_tables, int32_t* inc_ids,
+                                    int32_t* pairs, int32_t* dec_ids, void* stream) {
+  AKV_ARG_CHECK(n_roots >= 0 && fanout >= 0 && levels >= 0 && root_blocks >= n_roots,
+                "akv_fanout_tree_plan: roots=%d root_blocks=%lld fanout=%d levels=%d", n_roots,
+                static_cast<long long>(root_blocks), fanout, levels);
+  AKV_ARG_CHECK(append >= 1, "akv_fanout_tree_plan: append=%d (needs >= 1; use akv_fanout_plan per level)",
+                append);
+  AKV_ARG_CHECK(levels <= kAkvMaxFanoutLevels, "akv_fanout_tree_plan: %d levels > %d", levels,
+                kAkvMaxFanoutLevels);
+  if (n_roots == 0 || fanout == 0 || levels == 0) return AKV_OK;
+  AKV_ARG_CHECK(root_tables && root_off && fresh_ids && child_tables && inc_ids && pairs && dec_ids,
+                "akv_fanout_tree_plan: NULL array argument");
+  TreeShape sh{};
+  sh.levels = levels;
+  sh.K = fanout;
+  sh.A = append;
+  sh.R = n_roots;
+  sh.kpow[0] = 1;
+  int64_t tab = 0, inc = 0;
+  sh.first[0] = 0;
+  for (int l = 0; l < levels; ++l) {
+    sh.kpow[l + 1] = sh.kpow[l] * fanout;
+    AKV_ARG_CHECK(sh.kpow[l + 1] * n_roots < (int64_t{1} << 31), "akv_fanout_tree_plan: too many children");
+    const int64_t kids = sh.kpow[l + 1] * n_roots;
+    sh.first[l + 1] = sh.first[l] + kids;
+    sh.tab_base[l] = tab;
+    sh.inc_base[l] = inc;
+    tab += sh.kpow[l + 1] * (root_blocks + static_cast<int64_t>(n_roots) * (l + 1) * append);
+    inc += sh.kpow[l + 1] * (root_blocks + static_cast<int64_t>(n_roots) * l * append);
+  }
+  const int64_t total = sh.first[levels];
+  const int grid = static_cast<int>(total < kAkvSMs * 8 ? total : kAkvSMs * 8);
+  k_fanout_tree_plan<<<grid, 256, 0, akv_stream(stream)>>>(root_tables, root_off, fresh_ids, sh, child_tables,
+                                                            inc_ids, pairs, dec_ids);
+  AKV_LAUNCH_CHECK("akv_fanout_tree_plan");
+  return AKV_OK;
 }
 
 extern "C" int akv_fanout_plan(const int32_t* parent_tables, const int64_t* parent_off, int32_t n_parents,

@@ -7,7 +7,10 @@ and appending a few blocks).  FanoutGraph records that step once — the host
 plans, one inc_ref and one dec_ref batch), the block copies and, optionally,
 the frees of every child — and each run() replays it: the caller's host root
 tables go in, every child's block table and the status word come back to
-host memory, one synchronisation per call.
+host memory, one synchronisation per call.  With appended blocks the levels'
+copy-on-write pairs are independent and are copied in one launch after the
+last level's plan (merge=True); otherwise each level's copy follows its
+plan.
 
 Capturing executes nothing, so the allocator sees exactly the operations of
 the runs, in order: ids, refcounts and the free list stay those of the
@@ -30,7 +33,8 @@ from .allocator import SlabAllocator
 
 class FanoutGraph:
     def __init__(self, alloc: SlabAllocator, root_lens, levels: int, fanout: int, append: int, *,
-                 pool: Optional[torch.Tensor] = None, free_children: bool = False, variant: int = 0) -> None:
+                 pool: Optional[torch.Tensor] = None, free_children: bool = False, variant: int = 0,
+                 merge: bool = True) -> None:
         self.alloc = alloc
         self.dev = alloc.device
         self.levels, self.fanout, self.append = int(levels), int(fanout), int(append)
@@ -40,6 +44,7 @@ class FanoutGraph:
         self.pool = pool if pool is not None else alloc._kv_data
         self.free_children = free_children
         self.variant = variant
+        self.merge = merge
         # fixed shapes of every level
         lens = self.root_lens
         self.level_off = []
@@ -90,10 +95,16 @@ class FanoutGraph:
                 launches += 4
             self.h_tables.copy_(tables, non_blocking=True)
         if self.pool.device.type != "meta":
-            for lvl, pairs in enumerate(res["pairs"]):
-                cs.wait_event(events[lvl])
-                K.copy_blocks(self.pool, pairs, variant=self.variant, status=self._copy_status)
+            if self.merge and res["independent"]:
+                # every level's pairs in one launch once the last level is planned
+                cs.wait_event(events[-1])
+                K.copy_blocks(self.pool, res["all_pairs"], variant=self.variant, status=self._copy_status)
                 launches += 1
+            else:
+                for lvl, pairs in enumerate(res["pairs"]):
+                    cs.wait_event(events[lvl])
+                    K.copy_blocks(self.pool, pairs, variant=self.variant, status=self._copy_status)
+                    launches += 1
         cs.wait_stream(meta)
         self.h_status.copy_(self.alloc._status, non_blocking=True)
         self._keep = (res, tables, events)

@@ -80,6 +80,9 @@ def parse_args():
                          "in the step), or rank 0 plans and broadcasts each level's pairs / all pairs once")
     ap.add_argument("--graph-nccl", type=int, default=1,
                     help="N > 1: capture the step, NCCL pair broadcast included, as a CUDA graph")
+    ap.add_argument("--copy-levels", default="merged", choices=["merged", "per-level"],
+                    help="copy every level's CoW pairs in one launch after the last plan, or one launch per "
+                         "level as soon as its plan is ready")
     ap.add_argument("--match", action="store_true", help="also time match_prefix on the stress tree")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--match-seqs", type=int, default=W.MatchSpec.n_sequences)
@@ -161,7 +164,7 @@ class ToTBench:
     out again from being overwritten before an older copy has read it."""
 
     def __init__(self, rank: int, world: int, blocks_per_tree: int, variant: int, trees: int = 0,
-                 heads_per_rank: int = 0, plan: str = "bcast-once"):
+                 heads_per_rank: int = 0, plan: str = "bcast-once", merge: bool = True):
         import torch
 
         from agentkv_b200.allocator import SlabAllocator
@@ -178,6 +181,9 @@ class ToTBench:
         self.n_blocks = blocks_per_tree * self.trees
         self.slice_heads = heads_per_rank or H // world
         self.plan = plan if world > 1 else "replicated"
+        # all levels' pairs in one copy launch once the last level is planned
+        # (valid because appended blocks make the levels' pairs independent)
+        self.merge = merge and self.spec.appended_blocks >= 1 and self.plan != "bcast-level"
         self.planner = rank == 0 or self.plan == "replicated"
         # this rank's head slice of every block: [N, L, 2, H/world, bs, D]
         self.pool = torch.empty((self.n_blocks, L, 2, self.slice_heads, bs, D), dtype=torch.bfloat16,
@@ -262,6 +268,36 @@ class ToTBench:
                     self.host_status.copy_(self.alloc._status, non_blocking=True)
                     d2h += self.host_tables.numel() * 4 + self.host_status.numel() * 4
         level_pairs = []
+        if self.merge:
+            if self.plan == "bcast-once":
+                if self.rank == 0:
+                    res["all_pairs"].record_stream(cs)
+                    cs.wait_event(events[-1])
+                    allp = res["all_pairs"]
+                else:
+                    allp = None
+                allp = self.copier.share_pairs(allp, sum(self.pairs_per_level), out=self.all_pairs_buf)
+            else:
+                allp = res["all_pairs"]
+                allp.record_stream(cs)
+                cs.wait_event(events[-1])
+            if time_copies:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(cs)
+            self.copier.copy(allp, variant=self.variant)
+            launches += 1
+            if time_copies:
+                e1.record(cs)
+                self.copy_events.append((e0, e1, allp.shape[0]))
+            if capture:
+                self.join()
+            if e2e and self.planner:
+                self.join()
+                torch.cuda.synchronize(self.dev)
+                if int(self.host_status[0]):
+                    self.alloc.check()
+            self.launches_per_step = launches
+            return h2d, d2h
         if self.plan == "bcast-once":
             # one broadcast of every level's pairs once the last level is planned
             if self.rank == 0:
@@ -684,11 +720,13 @@ def hf_case(args) -> None:
                                        res["kv_gather"]["ms_per_decode_step"], 2)}), flush=True)
 
 
-def level3_traffic():
-    """DRAM bytes (read + write) of the level-3 copy launch from the committed
-    ncu summary, or None."""
-    p = REPO / "profiles" / "copy_blocks_tot_level3.md"
-    if p.exists():
+def copy_traffic(n_pairs: int):
+    """DRAM bytes (read + write) of the step's dominant copy launch (all 584
+    pairs merged, or the 512-pair third level) from the committed ncu
+    summary, or None."""
+    name = {584: "copy_blocks_tot_merged.md", 512: "copy_blocks_tot_level3.md"}.get(n_pairs)
+    p = REPO / "profiles" / name if name else None
+    if p is not None and p.exists():
         for line in p.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):
                 return int(line.split(":")[1])
@@ -736,7 +774,8 @@ def main():
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
-    bench = ToTBench(rank, world, args.blocks, args.variant, args.trees, args.heads_per_rank, args.plan)
+    bench = ToTBench(rank, world, args.blocks, args.variant, args.trees, args.heads_per_rank, args.plan,
+                     merge=args.copy_levels == "merged")
     graph = None
     if not args.no_graph and (world == 1 or args.graph_nccl):
         for _ in range(2):  # load every kernel and settle the allocator pools before capture
@@ -780,7 +819,7 @@ def main():
     big = max(per_level)
     big_ms = statistics.mean(per_level[big])
     achieved = 2 * bench.slice_bytes * big / (big_ms / 1e3) / 1e9
-    traffic = level3_traffic() if bench.slice_heads == 8 and bench.trees == 1 else None
+    traffic = copy_traffic(big) if bench.slice_heads == 8 and bench.trees == 1 else None
     launches = len(bench.copy_events)
 
     e2e = None
@@ -853,6 +892,7 @@ def main():
                 "heads_per_rank": bench.slice_heads,
                 "l2": "inputs larger than L2 (each step touches ~2.4 GB per GPU)",
                 "copy_variant": args.variant,
+                "copy_levels": "merged" if bench.merge else "per-level",
                 "cuda_graph": use_graph,
             },
             "roofline": {
@@ -864,7 +904,8 @@ def main():
                 "all_levels_gbs": round(kbytes / (kms / 1e3) / 1e9, 1),
                 "per_level_ms": {str(k): round(statistics.mean(v), 4) for k, v in sorted(per_level.items())},
                 "note": "algorithmic bytes = 2 x bytes_per_block per pair; the 8 (64, 512) pairs of a level "
-                        "read 1 (8, 64) distinct source blocks, so L2 serves repeated reads",
+                        "read 1 (8, 64) distinct source blocks, so L2 serves repeated reads (per_level_ms is "
+                        "keyed by the pairs per launch: 584 = every level in one launch)",
             },
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -46,13 +46,14 @@ def _oracle_fanout(tree, roots, levels, fanout, append, free):
     return tables
 
 
+@pytest.mark.parametrize("merge", [True, False])
 @pytest.mark.parametrize("free", [True, False])
 @pytest.mark.parametrize("root_lens,levels,fanout,append", [
     ([3, 5], 2, 3, 2),
     ([1], 3, 4, 0),
     ([2, 1, 4], 1, 5, 1),
 ])
-def test_fanout_graph_matches_oracle(root_lens, levels, fanout, append, free):
+def test_fanout_graph_matches_oracle(root_lens, levels, fanout, append, free, merge):
     n_blocks = 1024
     cfg = PoolConfig(total_blocks=n_blocks, block_size=16, num_layers=2, num_kv_heads=2, head_dim=64,
                      dtype="bfloat16", device="cuda")
@@ -74,7 +75,7 @@ def test_fanout_graph_matches_oracle(root_lens, levels, fanout, append, free):
     want_roots = np.concatenate([np.asarray(h.residual, np.int32) for h in roots])
     np.testing.assert_array_equal(d_roots, want_roots)
 
-    fg = FanoutGraph(a, root_lens, levels, fanout, append, free_children=free)
+    fg = FanoutGraph(a, root_lens, levels, fanout, append, free_children=free, merge=merge)
     assert fg.copies_per_run == len(root_lens) * sum(fanout ** (lv + 1) for lv in range(levels))
     for run in range(3):
         got = fg.run(d_roots)
@@ -143,3 +144,42 @@ def test_fanout_graph_exhaustion_raises():
         fg.run(roots)
     with pytest.raises(ValueError):
         fg.run(roots[:1])
+
+
+@pytest.mark.parametrize("root_lens,levels,fanout,append", [
+    ([3, 1, 5, 2], 3, 3, 2), ([1], 4, 2, 1), ([7], 1, 6, 3), ([2, 2], 2, 1, 1),
+])
+def test_fused_tree_plan_equals_level_plans(root_lens, levels, fanout, append):
+    """fanout_tree's one-launch plan (append >= 1) against fanout_level run
+    level by level: identical child tables, pairs, refcounts, free lists."""
+    def run(per_level):
+        cfg = PoolConfig(total_blocks=4096, block_size=16, num_layers=1, num_kv_heads=1, head_dim=8,
+                         dtype="float16", device="meta")
+        a = AgentKVPool(config=cfg)._allocator
+        roots = a.alloc_batch(sum(root_lens))
+        if per_level:
+            tables, pairs = [], []
+            t, lens = roots, np.asarray(root_lens)
+            for _ in range(levels):
+                off = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)])).to(a.device)
+                r = a.fanout_level(t, off, lens, fanout, append)
+                tables.append(r["child_tables"])
+                pairs.append(r["pairs"])
+                t, lens = r["child_tables"], r["child_lens"]
+        else:
+            r = a.fanout_tree(roots, root_lens, levels, fanout, append)
+            tables, pairs = r["child_tables"], r["pairs"]
+        a.check()
+        return ([t.cpu().numpy() for t in tables], [p.cpu().numpy() for p in pairs],
+                a._ref_counts.cpu().numpy(), a.free_list(), a.stats())
+
+    t1, p1, r1, f1, s1 = run(False)
+    t2, p2, r2, f2, s2 = run(True)
+    for x, y in zip(t1, t2):
+        np.testing.assert_array_equal(x, y)
+    for x, y in zip(p1, p2):
+        np.testing.assert_array_equal(x.reshape(-1, 2), y.reshape(-1, 2))
+    np.testing.assert_array_equal(r1, r2)
+    np.testing.assert_array_equal(f1, f2)
+    for k in ("free_blocks", "allocated_blocks", "peak_allocated", "total_allocs", "epoch"):
+        assert s1[k] == s2[k], k
