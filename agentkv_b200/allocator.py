@@ -455,7 +455,8 @@ class SlabAllocator:
         cannot change the result.  No copy is made: `pairs[l]` lists round
         l's (src, dst) block copies, ready once `on_level(l)` has been called
         (e.g. to record an event) — copy them on any stream after that point.
-        `all_pairs` holds every round's pairs back to back; with append >= 1
+        `all_pairs` holds every round's pairs back to back (and, with
+        append >= 1, `all_tables` every round's child tables); with append >= 1
         (`independent`) no pair's source is another pair's destination (a
         child's last block, the next round's source, is an appended block),
         so all rounds may be copied in one launch.  Returns per-round device
@@ -549,8 +550,8 @@ class SlabAllocator:
                 on_level(lvl)
         self.inc_ref_batch(incs)
         self.dec_ref_batch(decs)
-        return {"child_tables": out_tables, "pairs": out_pairs, "all_pairs": all_pairs, "independent": True,
-                "launches": 2 + 2 + 4}
+        return {"child_tables": out_tables, "all_tables": tables, "pairs": out_pairs, "all_pairs": all_pairs,
+                "independent": True, "launches": 2 + 2 + 4}
 
     def copy_blocks(self, pairs, *, check_refs: bool = True) -> None:
         """Copy a batch of independent (src, dst) pairs; dsts must be exclusive."""

@@ -89,7 +89,9 @@ class FanoutGraph:
             res = self.alloc.fanout_tree(self.d_roots, self.root_lens, self.levels, self.fanout, self.append,
                                          level_offsets=self.level_off, on_level=on_level)
             launches = res["launches"]
-            tables = torch.cat(res["child_tables"])
+            tables = res.get("all_tables")
+            if tables is None:
+                tables = torch.cat(res["child_tables"])
             if self.free_children:
                 self.alloc.dec_ref_batch(tables)
                 launches += 4

@@ -260,7 +260,9 @@ class ToTBench:
                                              self.spec.appended_blocks, level_offsets=self.level_off,
                                              on_level=on_level)
                 launches += res["launches"]
-                frees = torch.cat(res["child_tables"])
+                frees = res.get("all_tables")
+                if frees is None:
+                    frees = torch.cat(res["child_tables"])
                 self.alloc.dec_ref_batch(frees)  # every child freed, in creation order
                 launches += 4
                 if e2e:
