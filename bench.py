@@ -233,8 +233,12 @@ class ToTBench:
         if self.planner:
             self.torch.cuda.current_stream(self.dev).wait_stream(self.meta)
 
-    def step(self, e2e=False, time_copies=False, capture=False):
-        """Returns (h2d_bytes, d2h_bytes) of the host-driven variant."""
+    def step(self, e2e=False, time_copies=False, capture=False, chain=False):
+        """Returns (h2d_bytes, d2h_bytes) of the host-driven variant.  With
+        chain=True (the second step of a captured pair) the allocator stream
+        continues from the previous step's allocator work without waiting for
+        its copy: the next fan-out's planning touches only block metadata, so
+        it overlaps the previous copy; copies stay ordered on one stream."""
         torch = self.torch
         from agentkv_b200 import kernels as K
 
@@ -243,7 +247,7 @@ class ToTBench:
         launches = 0
         events = []
         if self.planner:
-            if capture:
+            if capture and not chain:
                 self.meta.wait_stream(cs)  # fork the allocator stream into the capture
             with torch.cuda.stream(self.meta):
                 if e2e:
@@ -342,19 +346,53 @@ class ToTBench:
         self.launches_per_step = launches
         return h2d, d2h
 
-    def capture(self):
-        """Record one step as a CUDA graph; returns the graph.  With N ranks
-        every rank captures its own step (the pair broadcast included) and
-        the ranks replay in lockstep."""
+    def capture(self, steps: int = 1):
+        """Record `steps` consecutive steps as one CUDA graph; returns the
+        graph.  With N ranks every rank captures its own steps (the pair
+        broadcast included) and the ranks replay in lockstep."""
         torch = self.torch
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, capture_error_mode="thread_local"):
-            self.step(capture=True)
+            for i in range(steps):
+                self.step(capture=True, chain=i > 0)
         return g
 
     def copy_bytes_per_step_global(self):
         """Algorithmic bytes of all copies of one step, all ranks together."""
         return sum(self.pairs_per_level) * 2 * self.slice_bytes * self.world
+
+
+def timed_steps(run_steps, steps, warmup, world, join=None):
+    """timed() for a runner that takes a step count (graphs holding several
+    steps): the same barriers, events and max over ranks, EXACTLY `steps`
+    steps in the timed region."""
+    import torch
+
+    run_steps(warmup)
+    if join is not None:
+        join()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    run_steps(steps)
+    if join is not None:
+        join()
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, wall
 
 
 def timed(fn, steps, warmup, world, join=None):
@@ -788,14 +826,25 @@ def main():
         torch.cuda.synchronize()
         if world > 1:
             torch.distributed.barrier()
-        graph = bench.capture()
-        run_step = graph.replay
+        # two consecutive steps per graph (the second one's planning overlaps
+        # the first one's copy) and a one-step graph for an odd count
+        graph2 = bench.capture(2)
+        graph = bench.capture(1)
+
+        def run_steps(n):
+            for _ in range(n // 2):
+                graph2.replay()
+            if n % 2:
+                graph.replay()
     else:
-        run_step = bench.step
+        def run_steps(n):
+            for _ in range(n):
+                bench.step()
+        graph2 = None
     use_graph = graph is not None
     sampler = ClockSampler(local)
     with sampler:
-        ms, wall = timed(run_step, args.steps, args.warmup, world, join=bench.join)
+        ms, wall = timed_steps(run_steps, args.steps, args.warmup, world, join=bench.join)
     if bench.alloc is not None:
         # every step frees what it allocated: only the roots remain allocated
         bench.alloc.check()
@@ -892,7 +941,7 @@ def main():
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    del graph, run_step  # a graph holding NCCL calls must go before the process group
+    del graph, graph2, run_steps  # a graph holding NCCL calls must go before the process group
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -920,6 +969,7 @@ def main():
                 "copy_variant": args.variant,
                 "copy_levels": "merged" if bench.merge else "per-level",
                 "cuda_graph": use_graph,
+                "steps_per_graph": 2 if use_graph else None,
             },
             "roofline": {
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
