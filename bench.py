@@ -80,6 +80,9 @@ def parse_args():
                          "in the step), or rank 0 plans and broadcasts each level's pairs / all pairs once")
     ap.add_argument("--graph-nccl", type=int, default=1,
                     help="N > 1: capture the step, NCCL pair broadcast included, as a CUDA graph")
+    ap.add_argument("--graph-steps", type=int, default=2,
+                    help="consecutive steps recorded in one CUDA graph (the next step's planning overlaps the "
+                         "current copy)")
     ap.add_argument("--copy-levels", default="merged", choices=["merged", "per-level"],
                     help="copy every level's CoW pairs in one launch after the last plan, or one launch per "
                          "level as soon as its plan is ready")
@@ -826,15 +829,19 @@ def main():
         torch.cuda.synchronize()
         if world > 1:
             torch.distributed.barrier()
-        # two consecutive steps per graph (the second one's planning overlaps
-        # the first one's copy) and a one-step graph for an odd count
-        graph2 = bench.capture(2)
+        # --graph-steps consecutive steps per graph (each step's planning
+        # overlaps the previous step's copy) and a one-step graph for the
+        # remainder
+        gs = max(1, args.graph_steps)
+        graph2 = bench.capture(gs) if gs > 1 else None
         graph = bench.capture(1)
 
         def run_steps(n):
-            for _ in range(n // 2):
-                graph2.replay()
-            if n % 2:
+            if graph2 is not None:
+                for _ in range(n // gs):
+                    graph2.replay()
+                n %= gs
+            for _ in range(n):
                 graph.replay()
     else:
         def run_steps(n):
@@ -969,7 +976,7 @@ def main():
                 "copy_variant": args.variant,
                 "copy_levels": "merged" if bench.merge else "per-level",
                 "cuda_graph": use_graph,
-                "steps_per_graph": 2 if use_graph else None,
+                "steps_per_graph": max(1, args.graph_steps) if use_graph else None,
             },
             "roofline": {
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
