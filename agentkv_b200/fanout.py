@@ -65,10 +65,11 @@ class FanoutGraph:
         self._copy_status = alloc._status if self.pool.device == alloc.device else None
         self.copies_per_run = int(sum(len(self.root_lens) * self.fanout ** (lv + 1) for lv in range(self.levels)))
         self.launches_per_run = 0
-        N.check(N.lib.akv_prepare())
-        self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
-            self._record()
+        with torch.cuda.device(self.dev):  # kernels prepared and graph recorded on the allocator's GPU
+            N.check(N.lib.akv_prepare())
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
+                self._record()
 
     def _record(self) -> None:
         # Allocator kernels on a side stream; each level's copy on the
@@ -130,8 +131,9 @@ class FanoutGraph:
         if roots.size != self.h_roots.numel():
             raise ValueError(f"FanoutGraph.run: expected {self.h_roots.numel()} root ids, got {roots.size}")
         self.h_roots.numpy()[:] = roots
-        self.graph.replay()
-        torch.cuda.current_stream(self.dev).synchronize()
+        with torch.cuda.device(self.dev):
+            self.graph.replay()
+            torch.cuda.current_stream(self.dev).synchronize()
         if int(self.h_status[0]):
             self.alloc.check()
         out = self.h_tables.numpy()
