@@ -447,6 +447,78 @@ def hf_session(spec: W.HFSpec) -> dict:
     }
 
 
+# ── D4. the reference's own stress runner (tests/test_stress.py), recorded ────
+S_CREATE, S_FORK, S_ALLOC, S_FREE, S_ADVANCE = range(5)
+
+
+class _Recorder:
+    """Forwards to a pool object and logs the runner-level calls."""
+
+    def __init__(self, obj, log):
+        self._obj = obj
+        self._log = log
+
+    def __getattr__(self, name):
+        attr = getattr(self._obj, name)
+        log = self._log
+        if name == "create_root":
+            def f(tokens):
+                h = attr(tokens)
+                log.append((S_CREATE, h.handle_id, 0, list(tokens)))
+                return h
+        elif name == "fork":
+            def f(parent):
+                c = attr(parent)
+                log.append((S_FORK, parent.handle_id, c.handle_id, []))
+                return c
+        elif name == "allocate_block":
+            def f(h):
+                try:
+                    b = attr(h)
+                except MemoryError:
+                    log.append((S_ALLOC, h.handle_id, -3, []))
+                    raise
+                log.append((S_ALLOC, h.handle_id, b.block_id, []))
+                return b
+        elif name == "free":
+            def f(h):
+                attr(h)
+                log.append((S_FREE, h.handle_id, 0, []))
+        elif name == "maybe_advance_epoch":
+            def f():
+                attr()
+                log.append((S_ADVANCE, 0, 0, []))
+        else:
+            return attr
+        return f
+
+
+def stress(seed: int, n_ops: int) -> dict:
+    sys.path.insert(0, str(REF / "tests"))
+    import test_stress as TS  # noqa: E402  (the reference's runner, run as is)
+
+    cfg = PoolConfig(total_blocks=512, block_size=4, num_layers=2, num_kv_heads=2, head_dim=8,
+                     dtype="float16", device="cpu")
+    runner = TS.StressRunner(cfg, n_operations=n_ops, seed=seed)
+    log = []
+    alloc = runner._alloc
+    runner._tree = _Recorder(runner._tree, log)
+    runner._alloc = _Recorder(alloc, log)
+    violations = runner.run()
+    toks = [t for e in log for t in e[3]]
+    t_off = np.zeros(len(log) + 1, np.int64)
+    np.cumsum([len(e[3]) for e in log], out=t_off[1:])
+    return {
+        "ops": np.asarray([(e[0], e[1], e[2]) for e in log], np.int64),
+        "tokens": np.asarray(toks or [0], np.int32), "tokens_off": t_off,
+        "violations": np.asarray(len(violations)),
+        "ref": alloc._ref_counts.numpy().astype(np.int32).copy(),
+        "free": np.asarray(list(alloc._free_list), np.int32),
+        "stats": np.asarray(json.dumps(alloc.stats())),
+        "seed": np.asarray(seed), "n_ops": np.asarray(n_ops),
+    }
+
+
 # ── E. copy / zero contents on the CPU path ──────────────────────────────────
 def copy_zero() -> dict:
     cfg = PoolConfig(total_blocks=32, block_size=4, num_layers=2, num_kv_heads=2, head_dim=8,
@@ -525,8 +597,8 @@ def main() -> None:
     ap.add_argument("--skip-full-match", action="store_true")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
-    todo = set(args.only.split(",")) if args.only else {"alloc", "tree", "quick", "tot", "react", "hf", "copy",
-                                                                   "match", "match_full"}
+    todo = set(args.only.split(",")) if args.only else {"alloc", "tree", "quick", "tot", "react", "hf", "stress",
+                                                                   "copy", "match", "match_full"}
     if "alloc" in todo:
         for seed, (n, iv, nops) in {1: (48, 5, 700), 2: (32, 3, 700), 3: (64, 64, 900), 4: (16, 2, 500)}.items():
             np.savez_compressed(OUT / f"alloc_trace_{seed}.npz", **alloc_trace(seed, n, iv, nops))
@@ -544,6 +616,13 @@ def main() -> None:
     if "react" in todo:
         np.savez_compressed(OUT / "react_70b.npz", **react(W.ReActSpec()))
         print("react")
+    if "stress" in todo:
+        # the seeds and op counts of the reference's stress tests
+        for seed, n in ((1, 1000), (2, 10000), (42, 5000), (137, 5000), (999, 5000), (7, 10000), (13, 10000),
+                        (17, 10000)):
+            d = stress(seed, n)
+            np.savez_compressed(OUT / f"stress_{seed}.npz", **d)
+            print("stress", seed, len(d["ops"]), int(d["violations"]))
     if "hf" in todo:
         np.savez_compressed(OUT / "hf_session.npz", **hf_session(W.HFSpec()))
         print("hf")

@@ -264,6 +264,28 @@ def test_oracle_hf_session(golden_dir):
     assert pool.kv.tobytes() == g["pool"].tobytes()
 
 
+@pytest.mark.parametrize("seed", [1, 2, 7, 13, 17, 42, 137, 999])
+def test_oracle_reference_stress_runner(golden_dir, seed):
+    """The reference's own stress runner (tests/test_stress.py, its seeds and
+    op counts), recorded call by call: the oracle returns every handle id and
+    block id (and every pool-exhausted error) the reference returned, and ends
+    with its refcounts, free-list order and counters."""
+    from stress_replay import replay
+
+    g = np.load(golden_dir / f"stress_{seed}.npz")
+    assert int(g["violations"]) == 0
+    a = O.OracleAllocator(512)
+    tree = O.OracleTree(a, 4)
+    replay(g, tree, a.maybe_advance_epoch,
+           lambda e: isinstance(e, O.OracleError) and e.code == O.ORC_ERR_EXHAUSTED)
+    s = a.state()
+    np.testing.assert_array_equal(s["ref_counts"], g["ref"])
+    np.testing.assert_array_equal(s["free_list"], g["free"])
+    st = json.loads(str(g["stats"]))
+    assert (s["epoch"], s["total_allocs"], s["total_frees"], s["peak_allocated"]) == \
+        (st["epoch"], st["total_allocs"], st["total_frees"], st["peak_allocated"])
+
+
 def test_oracle_copy_zero_contents(golden_dir):
     g = json.loads((golden_dir / "copy_zero.json").read_text())
     torch.manual_seed(g["seed"])
