@@ -652,11 +652,27 @@ def sweep_case(args) -> None:
         torch.cuda.synchronize()
         z_ms = e0.elapsed_time(e1) / args.steps
         K.raise_for_status(K._status_buffer(dev))
+        # the reference's GPU path without Triton: one dst.copy_(src) per pair
+        # (agentkv/core/triton_kernels.py:194-196 via SlabAllocator.copy_block)
+        host_sets = [p_.cpu().tolist() for p_ in sets]
+        reps = max(1, min(args.steps, 4096 // n))
+        for s_, d_ in host_sets[0]:
+            pool[d_].copy_(pool[s_])
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(reps):
+            for s_, d_ in host_sets[i % len(host_sets)]:
+                pool[d_].copy_(pool[s_])
+        e1.record()
+        torch.cuda.synchronize()
+        t_ms = e0.elapsed_time(e1) / reps
         c_gbs = 2 * bpb * n / (c_ms / 1e3) / 1e9
         z_gbs = bpb * n / (z_ms / 1e3) / 1e9
+        t_gbs = 2 * bpb * n / (t_ms / 1e3) / 1e9
         out["batches"][str(n)] = {"copy_ms": round(c_ms, 5), "copy_gbs": round(c_gbs, 1),
                                   "copy_frac": round(c_gbs / peak, 4), "zero_ms": round(z_ms, 5),
-                                  "zero_gbs": round(z_gbs, 1), "zero_frac": round(z_gbs / peak, 4)}
+                                  "zero_gbs": round(z_gbs, 1), "zero_frac": round(z_gbs / peak, 4),
+                                  "torch_per_pair_ms": round(t_ms, 5), "torch_per_pair_gbs": round(t_gbs, 1)}
     print(json.dumps(out), flush=True)
 
 
