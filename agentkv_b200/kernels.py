@@ -36,7 +36,15 @@ def _status_buffer(device: torch.device) -> torch.Tensor:
     return buf
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device) -> int:
+    """The device's current CUDA stream as a raw handle (the cheap accessor
+    when torch has it: this runs on every launch)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(idx)
     return torch.cuda.current_stream(device).cuda_stream
 
 
