@@ -503,15 +503,17 @@ int copy_bulk_launch_t(Layout lay, int32_t total, const int32_t* pairs, int32_t 
 }
 
 // Bulk-copy shapes (chunk bytes, chunks in flight, CTAs per SM).  Shape 0
-// picks by block size: on the Tree-of-Thought copy pattern (8 pairs per
-// source, consecutive destinations) 16 KiB x 12 is fastest for blocks of
-// 1 MiB and more (192 us vs 219-237 us for 2 MiB blocks), 64 KiB x 3 for
-// smaller blocks such as the 256-512 KiB head slices of a sharded pool
-// (187 us vs 249-265 us), for the same bytes per launch.
+// picks by block size, from Tree-of-Thought steps (8 pairs per source,
+// consecutive destinations, the allocator kernels running beside the copy)
+// at equal bytes per step: 16 KiB x 12 for blocks of 2 MiB and more (0.242 ms
+// per step against 0.275 ms with 32 KiB x 6), 32 KiB x 6 below — the 256 KiB,
+// 512 KiB and 1 MiB head slices of a sharded pool (0.280 / 0.253 / 0.255 ms
+// against 0.285-0.287 / 0.256-0.258 / 0.275 ms with 64 KiB x 3 or
+// 16 KiB x 12).
 int copy_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* pairs, int32_t n,
                      const int32_t* refs, AkvStatus* st, cudaStream_t s,
                      const int64_t* n_dev = nullptr, int shape = 0) {
-  if (shape == 0 && bpb < (int64_t{1} << 20)) shape = 3;
+  if (shape == 0 && bpb < (int64_t{1} << 21)) shape = 1;
   const OnePool lay{pool, bpb};
   switch (shape) {
     case 1: return copy_bulk_launch_t<32768, 6, 1>(lay, total, pairs, n, refs, st, s, n_dev);

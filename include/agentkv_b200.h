@@ -98,7 +98,7 @@ AKV_API int akv_copy_blocks(void* pool, int64_t bytes_per_block, int32_t total_b
 
 /* Same, with an explicit kernel choice: 0 = automatic, 1 = 16-byte vector
  * loads/stores, 2 = bulk-async (TMA) copies staged through shared memory
- * (16 KiB chunks x 12 in flight for blocks >= 1 MiB, 64 KiB x 3 below, one
+ * (16 KiB chunks x 12 in flight for blocks >= 2 MiB, 32 KiB x 6 below, one
  * CTA per SM); 3-11 = fixed bulk shapes for tuning
  * (32 KiB x 6; 32 KiB x 3 with 2 CTAs per SM; 64 KiB x 3; 16 KiB x 6 with
  * 2 CTAs per SM; 8 KiB x 24; chunk-major order (chunk c of every pair before
