@@ -6,9 +6,12 @@ contents, 117 GiB).  A root holding a 4096-token prefix (256 blocks) is forked
 8 ways for 3 levels; every child copy-on-writes the last block it inherited
 and appends 64 tokens (4 blocks) — 8 + 64 + 512 = 584 CoW copies of 2 MiB —
 then all 584 children are freed, returning the pool to its starting shape.
-Each level is one batched device step: akv_alloc_batch, akv_fanout_plan
-(fork inc_ref list, CoW pairs, child tables), akv_incref_batch,
-akv_copy_blocks, akv_decref_batch; the frees are one akv_decref_batch.
+On device: one akv_alloc_batch for every level's ids, one
+akv_fanout_tree_plan for all three levels (child tables, the forks' inc_ref
+list, CoW pairs, CoW dec_ref list), one akv_incref_batch, one
+akv_decref_batch, one akv_copy_blocks of all 584 pairs, and one
+akv_decref_batch for the frees; two consecutive steps are recorded as one
+CUDA graph (the second step's planning overlaps the first step's copy).
 Block ids, refcounts and the free list end exactly as after the reference's
 per-child calls (checked by the tests).
 
