@@ -463,10 +463,19 @@ class SlabAllocator:
         tensors child_tables / pairs, all_pairs, independent and the launch
         count."""
         K, A = int(fanout), int(append)
+        if K < 0 or A < 0 or levels < 0:
+            raise ValueError(f"fanout_tree: negative fanout / append / levels ({K}, {A}, {levels})")
         lens = np.asarray(root_lens, np.int64)
         if (lens < 1).any():
             raise ValueError("fanout_tree: every root needs at least one residual block")
         dev = self._dev
+        if levels == 0 or K == 0 or len(lens) == 0:  # no child at all: nothing to do
+            empty = torch.empty(0, dtype=torch.int32, device=dev)
+            for lvl in range(levels):
+                if on_level is not None:
+                    on_level(lvl)
+            return {"child_tables": [empty] * levels, "all_tables": empty, "pairs": [empty.view(0, 2)] * levels,
+                    "all_pairs": empty.view(0, 2), "independent": True, "launches": 0}
         shapes, l_ = [], lens
         for _ in range(levels):
             shapes.append((len(l_), int(l_.sum())))

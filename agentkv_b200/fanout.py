@@ -97,7 +97,7 @@ class FanoutGraph:
                 self.alloc.dec_ref_batch(tables)
                 launches += 4
             self.h_tables.copy_(tables, non_blocking=True)
-        if self.pool.device.type != "meta":
+        if self.pool.device.type != "meta" and events:
             if self.merge and res["independent"]:
                 # every level's pairs in one launch once the last level is planned
                 cs.wait_event(events[-1])

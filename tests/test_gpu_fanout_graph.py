@@ -183,3 +183,30 @@ def test_fused_tree_plan_equals_level_plans(root_lens, levels, fanout, append):
     np.testing.assert_array_equal(f1, f2)
     for k in ("free_blocks", "allocated_blocks", "peak_allocated", "total_allocs", "epoch"):
         assert s1[k] == s2[k], k
+
+
+def test_fanout_edge_cases():
+    """No levels, no children, a single level of one child: the graph and
+    the allocator behave like the reference's (empty) call sequences."""
+    cfg = PoolConfig(total_blocks=64, block_size=4, num_layers=1, num_kv_heads=1, head_dim=4, dtype="float16",
+                     device="cuda")
+    a = AgentKVPool(config=cfg)._allocator
+    roots = a.alloc_batch(2).cpu().numpy()
+    before = (a._ref_counts.cpu().numpy().copy(), a.free_list().copy())
+    for levels, fanout in ((0, 3), (2, 0)):
+        fg = FanoutGraph(a, [2], levels, fanout, 1, free_children=True)
+        assert fg.run(roots).size == 0
+        np.testing.assert_array_equal(a._ref_counts.cpu().numpy(), before[0])
+        np.testing.assert_array_equal(a.free_list(), before[1])
+    o = O.OracleAllocator(64)
+    tree = O.OracleTree(o, 4)
+    r = tree.create_root([])
+    tree.allocate_block(r)
+    tree.allocate_block(r)
+    fg = FanoutGraph(a, [2], 1, 1, 1, free_children=False)
+    got = fg.run(roots)
+    want = _oracle_fanout(tree, [r], 1, 1, 1, False)
+    np.testing.assert_array_equal(got, want)
+    assert_same_as_oracle(a, o, "one child")
+    with pytest.raises(ValueError):
+        FanoutGraph(a, [0], 1, 2, 1)
