@@ -217,44 +217,6 @@ __global__ void k_incref_check(AkvAllocState st, const int32_t* __restrict__ ids
   }
 }
 
-// Duplicate-aware accumulation for the inc / dec batches.  A CTA folds a
-// contiguous window of kAggWindow ids into a shared-memory hash table
-// (count and last position per distinct id) and then updates global memory
-// once per distinct id: a fork batch repeats each parent's table once per
-// child, and a batch of frees repeats the shared prefix of every sibling, so
-// a window holds several copies of the same ids and the global atomics on
-// those few hot counters drop by that factor.  The table is twice the
-// window, so a probe always finds a free slot.
-constexpr int kAggWindow = 1024;
-constexpr int kAggSlots = 2 * kAggWindow;
-
-struct AggTable {
-  int32_t key[kAggSlots];
-  int32_t cnt[kAggSlots];
-  int32_t last[kAggSlots];
-};
-
-AKV_DEV void agg_clear(AggTable& t) {
-  for (int i = threadIdx.x; i < kAggSlots; i += blockDim.x) {
-    t.key[i] = -1;
-    t.cnt[i] = 0;
-    t.last[i] = 0;
-  }
-}
-
-AKV_DEV void agg_add(AggTable& t, int32_t id, int32_t pos1) {
-  uint32_t h = (static_cast<uint32_t>(id) * 2654435761u) & (kAggSlots - 1);
-  for (int probe = 0; probe < kAggSlots; ++probe) {
-    const int32_t old = atomicCAS(&t.key[h], -1, id);
-    if (old == -1 || old == id) {
-      atomicAdd(&t.cnt[h], 1);
-      atomicMax(&t.last[h], pos1);
-      return;
-    }
-    h = (h + 1) & (kAggSlots - 1);
-  }
-}
-
 __global__ void k_incref_apply(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n,
                                AkvTick tk, AkvStatus* status) {
   if (akv_failed(status)) return;
@@ -263,18 +225,7 @@ __global__ void k_incref_apply(AkvAllocState st, const int32_t* __restrict__ ids
   const int64_t left = ctl[C_LEFT], head = ctl[C_HEAD], d = ctl[C_REL] - head;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  __shared__ AggTable agg;
-  for (int64_t base = static_cast<int64_t>(blockIdx.x) * kAggWindow; base < n;
-       base += static_cast<int64_t>(gridDim.x) * kAggWindow) {
-    agg_clear(agg);
-    __syncthreads();
-    const int64_t end = min(static_cast<int64_t>(n), base + kAggWindow);
-    for (int64_t k = base + threadIdx.x; k < end; k += blockDim.x) agg_add(agg, ids[k], 0);
-    __syncthreads();
-    for (int i = threadIdx.x; i < kAggSlots; i += blockDim.x)
-      if (agg.key[i] >= 0) atomicAdd(&st.ref_counts[agg.key[i]], agg.cnt[i]);
-    __syncthreads();
-  }
+  for (int64_t k = tid; k < n; k += stride) atomicAdd(&st.ref_counts[ids[k]], 1);
   for (int64_t j = tid; j < d; j += stride)
     st.free_ring[wrap(left - d + j, N)] = st.limbo_ids[wrap(head + j, N)];
   if (last_cta(ctl) && threadIdx.x == 0) {
@@ -290,29 +241,14 @@ __global__ void k_incref_apply(AkvAllocState st, const int32_t* __restrict__ ids
 __global__ void k_dec_count(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n,
                             AkvStatus* status) {
   if (akv_failed(status)) return;
-  __shared__ AggTable agg;
-  for (int64_t base = static_cast<int64_t>(blockIdx.x) * kAggWindow; base < n;
-       base += static_cast<int64_t>(gridDim.x) * kAggWindow) {
-    agg_clear(agg);
-    __syncthreads();
-    const int64_t end = min(static_cast<int64_t>(n), base + kAggWindow);
-    for (int64_t k = base + threadIdx.x; k < end; k += blockDim.x) {
-      const int32_t x = ids[k];
-      if (static_cast<uint32_t>(x) >= static_cast<uint32_t>(st.total_blocks)) {
-        akv_fail(status, AKV_ERR_OUT_OF_RANGE, static_cast<int32_t>(k), x, st.total_blocks);
-        continue;
-      }
-      agg_add(agg, x, static_cast<int32_t>(k + 1));
+  for (int32_t k = blockIdx.x * blockDim.x + threadIdx.x; k < n; k += gridDim.x * blockDim.x) {
+    const int32_t x = ids[k];
+    if (static_cast<uint32_t>(x) >= static_cast<uint32_t>(st.total_blocks)) {
+      akv_fail(status, AKV_ERR_OUT_OF_RANGE, k, x, st.total_blocks);
+      continue;
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < kAggSlots; i += blockDim.x) {
-      const int32_t x = agg.key[i];
-      if (x >= 0) {
-        atomicAdd(&st.scratch_count[x], agg.cnt[i]);
-        atomicMax(&st.scratch_last[x], agg.last[i]);
-      }
-    }
-    __syncthreads();
+    atomicAdd(&st.scratch_count[x], 1);
+    atomicMax(&st.scratch_last[x], k + 1);
   }
 }
 
@@ -709,7 +645,7 @@ extern "C" int akv_incref_batch(const AkvAllocState* st, const int32_t* ids, int
   const int g = grid_for(n, 256, kAkvSMs * 4);
   k_incref_check<<<g, 256, 0, s>>>(*st, ids, n, status);
   AKV_LAUNCH_CHECK("akv_incref_batch(check)");
-  k_incref_apply<<<grid_for(n, kAggWindow, kAkvSMs * 4), 256, 0, s>>>(*st, ids, n, *tick, status);
+  k_incref_apply<<<g, 256, 0, s>>>(*st, ids, n, *tick, status);
   AKV_LAUNCH_CHECK("akv_incref_batch(apply)");
   return AKV_OK;
 }
@@ -728,7 +664,7 @@ extern "C" int akv_decref_batch(const AkvAllocState* st, const int32_t* ids, int
   const int32_t chunk = akv_ceil_div(n, n_ctas);
   int32_t* cta_counts = st->scratch_aux;
   DecPlan* plan = reinterpret_cast<DecPlan*>(st->scratch_aux + AKV_AUX_PLAN_OFFSET);
-  k_dec_count<<<grid_for(n, kAggWindow, kAkvSMs * 4), 256, 0, s>>>(*st, ids, n, status);
+  k_dec_count<<<grid_for(n, 256, kAkvSMs * 4), 256, 0, s>>>(*st, ids, n, status);
   AKV_LAUNCH_CHECK("akv_decref_batch(count)");
   k_dec_flag<<<n_ctas, kDecThreads, 0, s>>>(*st, ids, n, chunk, cta_counts, status);
   AKV_LAUNCH_CHECK("akv_decref_batch(flag)");
@@ -859,7 +795,7 @@ extern "C" int akv_decref_batch_noalloc(const AkvAllocState* st, const int32_t* 
   const int32_t chunk = akv_ceil_div(n, n_ctas);
   int32_t* cta_counts = s2.scratch_aux;
   DecPlan* plan = reinterpret_cast<DecPlan*>(s2.scratch_aux + AKV_AUX_PLAN_OFFSET);
-  k_dec_count<<<grid_for(n, kAggWindow, kAkvSMs * 4), 256, 0, s>>>(s2, ids, n, status);
+  k_dec_count<<<grid_for(n, 256, kAkvSMs * 4), 256, 0, s>>>(s2, ids, n, status);
   AKV_LAUNCH_CHECK("akv_decref_batch_noalloc(count)");
   k_dec_flag<<<n_ctas, kDecThreads, 0, s>>>(s2, ids, n, chunk, cta_counts, status);
   AKV_LAUNCH_CHECK("akv_decref_batch_noalloc(flag)");
