@@ -125,6 +125,9 @@ class SlabAllocator:
         )
         self._reclaimer = EpochReclaimer(self)
         with torch.cuda.device(dev):
+            # load every kernel and set its attributes on this device now, so
+            # that no first launch happens later inside a graph capture
+            N.check(N.lib.akv_prepare())
             N.check(N.lib.akv_alloc_init(self._state, self._stream()))
 
     # ── plumbing ──────────────────────────────────────────────────────────────
