@@ -1,8 +1,9 @@
 /*
  * akv_oracle.c — CPU restatement of AgentKV's block-movement, allocator and
  * match_prefix algorithms.  TEST INFRASTRUCTURE ONLY: the tests, the smoke
- * check and the CPU-baseline leg of bench.py use it as the checker; the
- * agentkv_b200 package never links or calls it.
+ * check and the CPU-baseline leg of bench.py use it to check results and to
+ * time the reference algorithm on the host; the agentkv_b200 package never
+ * links or calls it.
  *
  * Every function follows the reference's own single-threaded code path, one
  * operation at a time (file:line within the agentkv project):
