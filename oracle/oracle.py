@@ -1,8 +1,9 @@
 """Oracle for the AgentKV hot path — TEST INFRASTRUCTURE ONLY.
 
 A CPU restatement of the reference's algorithms, used by ``tests/``,
-``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` as the
-checker.  The ``agentkv_b200`` package never imports it.
+``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` to check
+results and to time the reference algorithm on the host.  The
+``agentkv_b200`` package never imports it.
 
 * ``OracleAllocator`` wraps the C restatement of SlabAllocator +
   EpochReclaimer (``akv_oracle.c``; agentkv/core/slab_allocator.py:155-437,
