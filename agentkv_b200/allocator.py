@@ -443,26 +443,26 @@ class SlabAllocator:
 
     def fanout_tree(self, root_tables: torch.Tensor, root_lens, levels: int, fanout: int, append: int,
                     *, level_offsets=None, on_level=None) -> dict:
-        """A whole multi-level fan-out (Tree-of-Thought): `levels` rounds of
-        fanout_level starting from the roots, children of one round being the
+        """A whole multi-level fan-out (Tree-of-Thought): `levels` levels of
+        fanout_level starting from the roots, children of one level being the
         parents of the next, children in (parent, child) order.
 
         The end state equals the reference's per-child sequence (fork,
         ensure_mutable_block(-1), `append` allocate_block calls, level after
-        level): one alloc batch takes every round's ids in the order the
+        level): one alloc batch takes every level's ids in the order the
         per-child calls pop them (nothing is freed in between, so one batch
-        pops exactly what the rounds' batches would), one plan launch per
-        round, then one inc_ref batch for all forks and one dec_ref batch for
+        pops exactly what the levels' batches would), one plan launch per
+        level, then one inc_ref batch for all forks and one dec_ref batch for
         all copy-on-write sources.  Every CoW source keeps a refcount >= 1
         throughout, so no id retires and the order of the refcount updates
-        cannot change the result.  No copy is made: `pairs[l]` lists round
+        cannot change the result.  No copy is made: `pairs[l]` lists level
         l's (src, dst) block copies, ready once `on_level(l)` has been called
         (e.g. to record an event) — copy them on any stream after that point.
-        `all_pairs` holds every round's pairs back to back (and, with
-        append >= 1, `all_tables` every round's child tables); with append >= 1
+        `all_pairs` holds every level's pairs back to back (and, with
+        append >= 1, `all_tables` every level's child tables); with append >= 1
         (`independent`) no pair's source is another pair's destination (a
-        child's last block, the next round's source, is an appended block),
-        so all rounds may be copied in one launch.  Returns per-round device
+        child's last block, the next level's source, is an appended block),
+        so all levels may be copied in one launch.  Returns per-level device
         tensors child_tables / pairs, all_pairs, independent and the launch
         count."""
         K, A = int(fanout), int(append)
@@ -531,7 +531,7 @@ class SlabAllocator:
 
     def _fanout_tree_fused(self, root_tables, lens, shapes, K, A, fresh_all, all_pairs, level_offsets,
                            on_level) -> dict:
-        """fanout_tree's rounds as one akv_fanout_tree_plan launch (append >= 1)."""
+        """fanout_tree's levels as one akv_fanout_tree_plan launch (append >= 1)."""
         dev = self._dev
         n_tab = sum(K * total + P * K * A for P, total in shapes)
         n_inc = sum(K * total for _, total in shapes)

@@ -343,15 +343,15 @@ AKV_API int akv_fanout_plan(const int32_t* parent_tables, const int64_t* parent_
                             const int32_t* fresh_ids, int32_t* child_tables, int64_t* child_off,
                             int32_t* inc_ids, int32_t* pairs, int32_t* dec_ids, void* stream);
 
-/* Every level of a fan-out in one launch (append >= 1): `levels` rounds of
+/* Every level of a fan-out in one launch (append >= 1): `levels` levels of
  * akv_fanout_plan from the roots (tables root_tables, offsets root_off
- * [n_roots + 1], root_blocks = their total length), children of a round
+ * [n_roots + 1], root_blocks = their total length), children of a level
  * being the parents of the next.  fresh_ids holds the ids of one
  * akv_alloc_batch of (1 + append) x (all children) — the ids the per-child
- * calls take, round after round.  child_tables, inc_ids, pairs and dec_ids
- * receive what the rounds' akv_fanout_plan launches would write, round after
- * round.  With appended blocks a child's table depends only on its root's
- * table and its ancestors' fresh ids, so no round waits for another.  No
+ * calls take, level after level.  child_tables, inc_ids, pairs and dec_ids
+ * receive what the levels' akv_fanout_plan launches would write, level after
+ * level.  With appended blocks a child's table depends only on its root's
+ * table and its ancestors' fresh ids, so no level waits for another.  No
  * counterpart in the reference beyond the per-child calls it replaces
  * (agentkv/core/radix_tree.py:222-314). */
 #define AKV_MAX_FANOUT_LEVELS 16
