@@ -6,7 +6,6 @@ Markers:
     slow — longer parity cases (full-size workloads).
 """
 
-import os
 import sys
 from pathlib import Path
 

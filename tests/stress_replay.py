@@ -3,8 +3,6 @@ tests/golden/stress_<seed>.npz, recorded from the reference's own
 tests/test_stress.py StressRunner with the seeds and op counts of its tests)
 through any tree + allocator with the reference's call set."""
 
-import numpy as np
-
 S_CREATE, S_FORK, S_ALLOC, S_FREE, S_ADVANCE = range(5)
 
 

@@ -12,7 +12,6 @@ import random
 
 import numpy as np
 import pytest
-import torch
 
 from agentkv_b200 import AgentKVPool, PoolConfig
 from agentkv_b200.allocator import INVALID_BLOCK, BlockHandle, SlabAllocator
