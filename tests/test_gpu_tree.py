@@ -362,3 +362,41 @@ def test_tot_fanout_copies_data():
     assert len(pairs) == 8
     for s_, d_ in pairs:
         assert torch.equal(a._kv_data[d_].view(torch.int16), before[s_].view(torch.int16))
+
+
+def test_match_with_colliding_child_keys():
+    """24 root children whose (parent, first token) keys share the low ten
+    hash bits, so they sit in one probe chain several 8-slot windows long:
+    every inserted sequence is found, and first tokens that join the chain
+    without being in the tree are reported absent (the walk runs to the
+    chain's empty slot), equal to the oracle's answers."""
+    from agentkv_b200.device_tree import tree_hash_np
+
+    toks = np.arange(1, 200000, dtype=np.int64)
+    h = tree_hash_np(np.zeros_like(toks), toks)
+    same = toks[(h & 1023) == (h[0] & 1023)]
+    firsts, absent = same[:24].tolist(), same[24:30].tolist()
+    cfg = PoolConfig(total_blocks=512, block_size=4, num_layers=1, num_kv_heads=1, head_dim=4,
+                     dtype="float16", device="meta")
+    pool = AgentKVPool(config=cfg)
+    ot = O.OracleTree(O.OracleAllocator(512), 4)
+    rng = np.random.default_rng(5)
+    seqs = []
+    for f in firsts:
+        seq = [int(f)] + rng.integers(0, 50000, size=11).tolist()
+        seqs.append(seq)
+        for tree, api in ((pool, "pool"), (ot, "oracle")):
+            hd = tree.create_root(seq)
+            if api == "pool":
+                tree.allocate_blocks(hd, 3)
+            else:
+                for _ in range(3):
+                    tree.allocate_block(hd)
+            tree.commit_prefix(hd, 12)
+    queries = [s + [7, 7, 7] for s in seqs] + [[a] + seqs[0][1:] for a in absent] + [s[:8] for s in seqs[:4]]
+    node, mlen = pool.match_prefix_batch(queries)
+    want = [ot.match(q)[:2] for q in queries]
+    assert [(int(n) if m else -1, int(m)) for n, m in zip(node, mlen)] == \
+        [(int(n) if m else -1, int(m)) for n, m in want]
+    assert all(int(m) == 12 for m in mlen[:24])
+    assert all(int(m) == 0 for m in mlen[24:30])
