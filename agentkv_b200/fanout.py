@@ -3,8 +3,9 @@
 Agent frameworks fork the same shape of tree over and over (a root forked K
 ways for a few levels, every child copy-on-writing the block it will extend
 and appending a few blocks).  FanoutGraph records that step once — the host
--> device copy of the root block tables, SlabAllocator.fanout_tree (allocs,
-plans, one inc_ref and one dec_ref batch), the block copies and, optionally,
+-> device copy of the root block tables, SlabAllocator.fanout_tree (one
+alloc batch, the plan — one launch for all levels when children append
+blocks — one inc_ref and one dec_ref batch), the block copies and, optionally,
 the frees of every child — and each run() replays it: the caller's host root
 tables go in, every child's block table and the status word come back to
 host memory, one synchronisation per call.  With appended blocks the levels'
