@@ -130,3 +130,43 @@ def test_query_ranges_cover_the_batch():
             assert all(r[i][1] == r[i + 1][0] for i in range(w - 1))
             sizes = [b - a for a, b in r]
             assert max(sizes) - min(sizes) <= 1
+
+
+def test_layer_cache_table_validation():
+    """The host checks behind copy_blocks_layers (CPU tensors stand in for
+    device caches: only shapes, strides and addresses are looked at)."""
+    import torch
+
+    from agentkv_b200 import kernels as K
+
+    K._CACHE_TABLES.clear()
+    kv = [torch.zeros(2, 10, 4, 2, 8, dtype=torch.float16) for _ in range(3)]
+    caches = [t[0] for t in kv] + [t[1] for t in kv]
+    table, n, block_bytes, stride = K._cache_table(caches)
+    assert (n, block_bytes, stride) == (10, 4 * 2 * 8 * 2, 4 * 2 * 8 * 2)
+    assert table.tolist() == [c.data_ptr() for c in caches]
+    assert K._cache_table(caches)[0] is table  # same tensors: cached
+    assert K._cache_table([t[0] for t in kv] + [t[1] for t in kv])[0] is table  # new views, same memory
+    with pytest.raises(ValueError):
+        K._cache_table(caches + [torch.zeros(9, 4, 2, 8, dtype=torch.float16)])  # block count differs
+    with pytest.raises(ValueError):
+        K._cache_table([torch.zeros(10, 3, 2, dtype=torch.float16)])  # 12-byte blocks
+    with pytest.raises(ValueError):
+        K._cache_table([torch.zeros(10, 8, dtype=torch.float16)[:, :4]])  # 8-byte blocks 16 bytes apart
+    with pytest.raises(ValueError):
+        K._cache_table([])
+
+
+def test_hf_script_and_states_are_deterministic():
+    from agentkv_b200 import workloads as W
+
+    spec = W.HFSpec()
+    ev = W.hf_script(spec)
+    assert ev[:2] == [("prefill", 0, 10), ("commit", 0, 8)]
+    assert sum(1 for e in ev if e[0] == "fork") == spec.forks
+    k1, v1 = W.hf_states(spec, 7, 1, 3)
+    k2, v2 = W.hf_states(spec, 7, 1, 3)
+    assert k1.shape == (1, spec.num_kv_heads, 3, spec.head_dim) and (k1 == k2).all() and (v1 == v2).all()
+    tr = W.react_trace(W.ReActSpec(steps=5))
+    assert len(tr) == 5 and all(len(st) == 32 for st in tr)
+    assert all(t != s for st in tr for _, s, t in st)
