@@ -114,6 +114,10 @@ class AkvTreeView(C.Structure):
         ("n_tokens", C.c_int64),
         ("n_nodes", C.c_int32),
         ("slot_mask", C.c_int32),
+        ("run_head", C.c_void_p),
+        ("run_entries", C.c_void_p),
+        ("n_runs", C.c_int32),
+        ("run_nodes", C.c_int32),
     ]
 
 

@@ -92,6 +92,10 @@ class DeviceTree:
         self._local = _Changes()  # for this GPU's arrays
         self._peers: Optional[_Changes] = None  # for replicas (track_peers)
         self._dev_tokens = 0  # tokens on the device
+        self._replica = False
+        self._runs_dirty = True
+        self.d_run_head: Optional[torch.Tensor] = None
+        self.d_runs: Optional[torch.Tensor] = None
         self.d_tokens = torch.zeros(token_cap, dtype=torch.int32, device=device)
         self.d_off = torch.zeros(node_cap, dtype=torch.int64, device=device)
         self.d_len = torch.zeros(node_cap, dtype=torch.int32, device=device)
@@ -128,6 +132,7 @@ class DeviceTree:
             self._mark_full()
         self.h_off[nid] = off
         self.h_len[nid] = length
+        self._runs_dirty = True
         for c in self._trackers():
             c.nodes.add(nid)
 
@@ -167,6 +172,7 @@ class DeviceTree:
             self.live += 1
             self._slot_of[key] = s
         self.h_slots[s] = (parent, token, child, child_len)
+        self._runs_dirty = True
         for c in self._trackers():
             c.slots.add(s)
 
@@ -175,6 +181,7 @@ class DeviceTree:
         if s is None:
             return
         self.h_slots[s] = (DELETED, 0, 0, 0)
+        self._runs_dirty = True
         self.live -= 1
         self.dead += 1
         for c in self._trackers():
@@ -210,6 +217,7 @@ class DeviceTree:
         """This tree's device arrays come from another GPU's deltas
         (apply_delta): its own (empty) host mirror is never uploaded."""
         self._local.full = False
+        self._replica = True
 
     def track_peers(self) -> None:
         """Also record changes for replicas on other GPUs (take_delta(peers=True));
@@ -298,23 +306,81 @@ class DeviceTree:
             nu_d.data_ptr() if nu_d is not None else None, n_nu,
             self.status.data_ptr(), stream_handle(dev)))
 
-    def view(self) -> N.AkvTreeView:
+    def view(self, runs: bool = False) -> N.AkvTreeView:
+        """The device arrays as an AkvTreeView; with runs=True it also points
+        at the unary-chain runs (build_runs must be current)."""
         if self._view is None:
             self._view = N.AkvTreeView(
                 self.d_tokens.data_ptr(), self.d_off.data_ptr(), self.d_len.data_ptr(),
-                self.d_slots.data_ptr(), self._dev_tokens, self.d_off.numel(), self.d_slots.shape[0] - 1)
-        return self._view
+                self.d_slots.data_ptr(), self._dev_tokens, self.d_off.numel(), self.d_slots.shape[0] - 1,
+                None, None, 0, 0)
+        if not runs or self.d_run_head is None:
+            return self._view
+        v = N.AkvTreeView.from_buffer_copy(self._view)
+        v.run_head = self.d_run_head.data_ptr()
+        v.run_entries = self.d_runs.data_ptr()
+        v.n_runs = self.d_runs.shape[0]
+        v.run_nodes = self.d_run_head.numel()
+        return v
+
+    # ── unary-chain runs (for the batched lookup) ────────────────────────────
+    def build_runs(self) -> None:
+        """Rebuild the runs from the host mirror when the tree changed since
+        the last build: for every node with exactly one child, the chain it
+        starts (its only child, that child's only child, ... through the
+        first node without exactly one child), stored per maximal chain, each
+        node pointing at its suffix.  A replica without a host mirror has no
+        runs (its lookups use the hash table alone)."""
+        if not self._runs_dirty or self._replica:
+            return
+        n_nodes = len(self.h_off)
+        children: dict = {}
+        parent_of: dict = {}
+        for (p, t), slot in self._slot_of.items():
+            c, ln = int(self.h_slots[slot, 2]), int(self.h_slots[slot, 3])
+            children.setdefault(p, []).append((c, t, ln))
+            parent_of[c] = p
+        unary = {p: ch[0] for p, ch in children.items() if len(ch) == 1}
+        head = np.full(n_nodes, -1, np.int32)
+        entries = []
+        for u0 in unary:
+            if parent_of.get(u0) in unary:
+                continue  # inside a chain; reached from its head
+            chain = []
+            u = u0
+            while u in unary:
+                c, t, ln = unary[u]
+                chain.append((u, c, t, ln))
+                u = c
+                if len(chain) > len(unary):
+                    raise RuntimeError(f"DeviceTree.build_runs: the child links from node {u0} form a cycle")
+            base = len(entries)
+            for k, (u, c, t, ln) in enumerate(chain):
+                if u < n_nodes:
+                    head[u] = base + k
+                entries.append((c, t, ln, len(chain) - k))
+        runs = np.asarray(entries, np.int32).reshape(-1, 4)
+        if len(runs) == 0:
+            runs = np.zeros((1, 4), np.int32)  # keeps a valid pointer; no head points at it
+        self.d_run_head = torch.from_numpy(head).to(self.device)
+        self.d_runs = torch.from_numpy(runs).to(self.device)
+        self._runs_dirty = False
 
     # ── lookups ──────────────────────────────────────────────────────────────
     def match(self, tokens: torch.Tensor, q_off: torch.Tensor, nq: int, block_size: int,
               out_node: torch.Tensor, out_len: torch.Tensor, out_cmp: Optional[torch.Tensor],
-              chunks: int = 0, order: Optional[torch.Tensor] = None) -> None:
+              chunks: int = 0, order: Optional[torch.Tensor] = None, runs: bool = False) -> None:
         """Enqueue akv_match_prefix for nq queries packed in `tokens` / `q_off`
         (device int32 / int64 tensors); `order` (device int32) is the launch
-        order of the queries, longest first by default in pack_queries."""
+        order of the queries, longest first by default in pack_queries.  With
+        runs=True unary chains are followed a run at a time (the runs are
+        rebuilt first if the tree changed: worth it for batches, not for the
+        single lookups of create_root)."""
         self.flush()
+        if runs:
+            self.build_runs()
         N.check(N.lib.akv_match_prefix_variant(
-            self.view(), tokens.data_ptr(), q_off.data_ptr(), nq, block_size, out_node.data_ptr(),
+            self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, block_size, out_node.data_ptr(),
             out_len.data_ptr(), out_cmp.data_ptr() if out_cmp is not None else None,
             order.data_ptr() if order is not None else None, self.status.data_ptr(), chunks,
             stream_handle(self.device)))
@@ -363,7 +429,7 @@ def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_co
     node = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
     mlen = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
     cmp_ = torch.empty(max(nq, 1), dtype=torch.int64, device=dev) if with_compared else None
-    tree.match(tok, q_off, nq, block_size, node, mlen, cmp_, order=order)
+    tree.match(tok, q_off, nq, block_size, node, mlen, cmp_, order=order, runs=True)
     tree.check()
     res = (node[:nq].cpu().numpy(), mlen[:nq].cpu().numpy())
     if with_compared:

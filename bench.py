@@ -105,6 +105,8 @@ def parse_args():
     ap.add_argument("--match", action="store_true", help="also time match_prefix on the stress tree")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--match-seqs", type=int, default=W.MatchSpec.n_sequences)
+    ap.add_argument("--match-runs", type=int, default=1,
+                    help="match_prefix follows unary chains a run at a time (0: one hash probe per hop)")
     ap.add_argument("--match-queries", type=int, default=W.MatchSpec.n_queries)
     ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers", "hf"],
                     help="tot: the headline step; sweep: batched copy/zero sweep; match: match_prefix on the "
@@ -573,7 +575,8 @@ def reference_arm(args, rank, world):
 
 # ── match_prefix figure ──────────────────────────────────────────────────────
 def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
-                 n_queries: int = W.MatchSpec.n_queries, rank: int = 0, world: int = 1) -> dict:
+                 n_queries: int = W.MatchSpec.n_queries, rank: int = 0, world: int = 1,
+                 use_runs: bool = True) -> dict:
     """match_prefix on the stress tree.  With N ranks, rank 0 builds the tree
     through the pool API and broadcasts it (TreeReplicaSync) to every rank's
     replica; each rank then matches its own 4096-query batches (weak
@@ -624,14 +627,14 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
     compared = []
     qtokens = []
     for (tok, off), order in zip(packed, orders):
-        tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order)
+        tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs)
         compared.append(int(cmp_.sum()))
         qtokens.append(int(off[-1]))
     tree.check()
 
     def run():
         for (tok, off), order in zip(packed, orders):
-            tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order)
+            tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs)
 
     ms, _ = timed(run, steps, warmup, world)
     per_batch_ms = ms / (steps * len(packed))
@@ -654,6 +657,7 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         "tree_build_s": round(build_s, 1),
         "replica_sync_s": round(sync_s, 2),
         "query_tokens_per_batch": int(statistics.mean(qtokens)),
+        "unary_runs": bool(use_runs),
     }
 
 
@@ -870,7 +874,8 @@ def main():
 
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                                  device_id=torch.device("cuda", local))
-        fig = match_figure(args.steps, args.warmup, args.match_seqs, args.match_queries, rank, world)
+        fig = match_figure(args.steps, args.warmup, args.match_seqs, args.match_queries, rank, world,
+                           use_runs=bool(args.match_runs))
         if rank == 0:
             print(json.dumps(fig), flush=True)
         if world > 1:

@@ -370,7 +370,19 @@ AKV_API int akv_fanout_tree_plan(const int32_t* root_tables, const int64_t* root
  *                      — the `children` dicts of all nodes as one
  *                      open-addressing hash table; parent = -1 empty,
  *                      -2 deleted
- * Node ids are the tree's own ids (root = 0).
+ *   run_head[run_nodes] int32 — optional (NULL = none): for a node with
+ *                      exactly one child, the index of its run in
+ *                      run_entries, else -1
+ *   run_entries[n_runs] int32x4 {child, first_token, edge_len, remaining} —
+ *                      unary chains: a node's run lists its only child, that
+ *                      child's only child, ... up to and including the first
+ *                      node without exactly one child; `remaining` counts the
+ *                      entries from this one to the end of its chain, so a
+ *                      run starting inside a chain is a suffix of it.  The
+ *                      lookup then follows up to 32 hops of a chain with one
+ *                      load instead of one hash probe per hop.
+ * Node ids are the tree's own ids (root = 0).  Callers that do not use runs
+ * set run_head = run_entries = NULL and n_runs = run_nodes = 0.
  */
 typedef struct AkvTreeView {
   const int32_t* tokens;
@@ -380,6 +392,10 @@ typedef struct AkvTreeView {
   int64_t n_tokens;
   int32_t n_nodes;     /* capacity of the node arrays */
   int32_t slot_mask;   /* number of slots - 1, a power of two minus one */
+  const int32_t* run_head;
+  const int32_t* run_entries;
+  int32_t n_runs;
+  int32_t run_nodes;
 } AkvTreeView;
 
 /* Hash of (parent, first_token) into the slot table; the host builder and

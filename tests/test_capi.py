@@ -86,7 +86,7 @@ def test_empty_batches_are_noops_without_gpu():
 
 
 def test_match_prefix_rejects_bad_tree_view():
-    v = N.AkvTreeView(None, None, None, None, 0, 0, 0)
+    v = N.AkvTreeView(None, None, None, None, 0, 0, 0, None, None, 0, 0)
     rc = N.lib.akv_match_prefix(C.byref(v), None, None, 1, 16, None, None, None, None, None)
     assert rc == N.AKV_ERR_INVALID_ARG
 

@@ -170,3 +170,60 @@ def test_hf_script_and_states_are_deterministic():
     tr = W.react_trace(W.ReActSpec(steps=5))
     assert len(tr) == 5 and all(len(st) == 32 for st in tr)
     assert all(t != s for st in tr for _, s, t in st)
+
+
+def test_unary_runs_follow_the_chains():
+    """DeviceTree.build_runs: every node with exactly one child points at a
+    run whose entries walk its unary chain (only child, its only child, ...)
+    through the first node without exactly one child; other nodes have no
+    run.  Random trees with splits, deletions and growth."""
+    import torch
+
+    from agentkv_b200.device_tree import DeviceTree
+
+    rng = np.random.default_rng(11)
+    for trial in range(5):
+        tree = DeviceTree(torch.device("cpu"), node_cap=8, slot_cap=16, token_cap=32)
+        nodes = {0: None}
+        nxt = 1
+        for _ in range(300):
+            op = rng.integers(0, 10)
+            if op < 7 or len(nodes) < 3:
+                parent = int(rng.choice(list(nodes)))
+                toks = rng.integers(0, 30, size=int(rng.integers(1, 6)), dtype=np.int32)
+                if (parent, int(toks[0])) in tree._slot_of:
+                    continue
+                off = tree.append_tokens(toks)
+                tree.set_node(nxt, off, len(toks))
+                tree.set_child(parent, int(toks[0]), nxt, len(toks))
+                nodes[nxt] = (parent, int(toks[0]))
+                nxt += 1
+            else:
+                nid = int(rng.choice([k for k in nodes if k]))
+                if any(p == nid for p, _ in tree._slot_of):
+                    continue  # only leaves are removed
+                parent, tok = nodes.pop(nid)
+                tree.del_child(parent, tok)
+                tree.clear_node(nid)
+        tree.build_runs()
+        head = tree.d_run_head.numpy()
+        runs = tree.d_runs.numpy()
+        kids = {}
+        for (p, t), s in tree._slot_of.items():
+            kids.setdefault(p, []).append((int(tree.h_slots[s, 2]), t, int(tree.h_slots[s, 3])))
+        for u in range(len(head)):
+            ch = kids.get(u, [])
+            if len(ch) != 1:
+                assert head[u] == -1, (trial, u)
+                continue
+            i, node = int(head[u]), u
+            rem = int(runs[i, 3])
+            for j in range(rem):
+                c, t, ln, r = (int(x) for x in runs[i + j])
+                assert r == rem - j
+                assert kids[node] == [(c, t, ln)]
+                node = c
+            assert len(kids.get(node, [])) != 1  # the chain ends at a non-unary node
+        assert not tree._runs_dirty
+        tree.set_child(0, 12345, 1, 1)
+        assert tree._runs_dirty
