@@ -94,6 +94,7 @@ class DeviceTree:
         self._dev_tokens = 0  # tokens on the device
         self._replica = False
         self._runs_dirty = True
+        self.runs_version = 0  # bumped by every build_runs that rebuilt
         self.d_run_head: Optional[torch.Tensor] = None
         self.d_runs: Optional[torch.Tensor] = None
         self.d_tokens = torch.zeros(token_cap, dtype=torch.int32, device=device)
@@ -290,6 +291,7 @@ class DeviceTree:
             self.d_slots = on_dev(d["slots"], torch.int32).reshape(-1, 4).clone()
             self._dev_tokens = n
             self._view = None
+            self._drop_replica_runs()
             return
         lo, hi = int(d["tok_lo"]), int(d["n_tokens"])
         if hi > lo:
@@ -299,6 +301,7 @@ class DeviceTree:
         n_su, n_nu = len(d["su"]), len(d["nu"])
         if n_su == 0 and n_nu == 0:
             return
+        self._drop_replica_runs()
         su_d = on_dev(d["su"], torch.int32) if n_su else None
         nu_d = on_dev(d["nu"], torch.int64) if n_nu else None
         N.check(N.lib.akv_tree_apply(
@@ -324,6 +327,19 @@ class DeviceTree:
         return v
 
     # ── unary-chain runs (for the batched lookup) ────────────────────────────
+    def _drop_replica_runs(self) -> None:
+        # a replica's runs come from its owner; a structural change makes
+        # them stale until the owner's next runs arrive (set_runs)
+        if self._replica:
+            self.d_run_head = self.d_runs = None
+
+    def set_runs(self, run_head: torch.Tensor, runs: torch.Tensor) -> None:
+        """A replica takes the owner's runs (device int32 tensors in
+        build_runs' layout: a head per node, [n, 4] entries)."""
+        self.d_run_head = run_head.to(self.device, torch.int32).reshape(-1)
+        self.d_runs = runs.to(self.device, torch.int32).reshape(-1, 4)
+        self._runs_dirty = False
+
     def build_runs(self) -> None:
         """Rebuild the runs from the host mirror when the tree changed since
         the last build: for every node with exactly one child, the chain it
@@ -365,6 +381,7 @@ class DeviceTree:
         self.d_run_head = torch.from_numpy(head).to(self.device)
         self.d_runs = torch.from_numpy(runs).to(self.device)
         self._runs_dirty = False
+        self.runs_version += 1
 
     # ── lookups ──────────────────────────────────────────────────────────────
     def match(self, tokens: torch.Tensor, q_off: torch.Tensor, nq: int, block_size: int,
@@ -416,11 +433,13 @@ def longest_first(q_off, device: torch.device) -> torch.Tensor:
     return torch.from_numpy(order).pin_memory().to(device, non_blocking=True)
 
 
-def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_compared: bool = False):
+def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_compared: bool = False,
+                runs: bool = True):
     """Longest shared prefix of many queries in one akv_match_prefix launch on
     `tree` (the owner's replica or another GPU's): (node ids, match lengths
     [, tokens compared]) as numpy arrays, each equal to the reference's
-    _match_prefix_locked (agentkv/core/radix_tree.py:513-570) on that query."""
+    _match_prefix_locked (agentkv/core/radix_tree.py:513-570) on that query.
+    runs=False takes one hash probe per hop instead of the unary-chain runs."""
     dev = tree.device
     nq = len(queries)
     tok, q_off = pack_queries(queries, dev)
@@ -429,7 +448,7 @@ def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_co
     node = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
     mlen = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
     cmp_ = torch.empty(max(nq, 1), dtype=torch.int64, device=dev) if with_compared else None
-    tree.match(tok, q_off, nq, block_size, node, mlen, cmp_, order=order, runs=True)
+    tree.match(tok, q_off, nq, block_size, node, mlen, cmp_, order=order, runs=runs)
     tree.check()
     res = (node[:nq].cpu().numpy(), mlen[:nq].cpu().numpy())
     if with_compared:

@@ -9,12 +9,17 @@ replicas hold identical arrays and each rank answers its queries locally
 (akv_match_prefix), with no exchange per query.
 
 Wire format of one delta: an int64 header
-    [kind, n_tokens, tok_lo, token_cap, node_cap, slot_cap, n_slot_rows, n_node_rows]
+    [kind, n_tokens, tok_lo, token_cap, node_cap, slot_cap, n_slot_rows, n_node_rows,
+     run_nodes, n_runs]
 (kind -1 = nothing changed, 0 = incremental, 1 = full), then, skipping empty
 arrays, for a full delta tokens[n_tokens] i32, edge_off[node_cap] i64,
 edge_len[node_cap] i32, slots[slot_cap x 4] i32; for an incremental one the
 appended tokens[n_tokens - tok_lo] i32, slot rows [n x 5] i32 and node rows
-[n x 3] i64.
+[n x 3] i64.  When the owner's unary-chain runs were rebuilt since the last
+share (run_nodes >= 0), run_head[run_nodes] i32 and run entries
+[n_runs x 4] i32 follow, sent straight from the owner's device arrays; a
+replica whose tree changed without new runs drops its runs and matches with
+the hash table alone.
 """
 
 from __future__ import annotations
@@ -41,6 +46,7 @@ class TreeReplicaSync:
         self.src = src
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self._sent_runs = 0  # the owner's runs_version last sent
         if self.rank == src:
             tree.track_peers()
         else:
@@ -52,27 +58,52 @@ class TreeReplicaSync:
         if self.world > 1 and t.numel():
             dist.broadcast(t, src=self.src, group=self.group)
 
-    def share(self) -> Optional[dict]:
+    def share(self, runs: bool = True) -> Optional[dict]:
         """Collective: rank src takes its pending delta and sends it; every
         rank returns the delta with its arrays as tensors on its device (None
-        when nothing changed)."""
+        when nothing changed).  With runs=True the owner brings its unary-chain
+        runs up to date and sends them when they were rebuilt (keys
+        "run_head" / "runs" of the result)."""
         dev = self.device
+        send_runs = None
         if self.rank == self.src:
             d = self.tree.take_delta(peers=True)
             if d is None:
-                head = [KIND_NONE, 0, 0, 0, 0, 0, 0, 0]
+                head = [KIND_NONE, self.tree.n_tokens, self.tree.n_tokens, 0, 0, 0, 0, 0]
             elif d["full"]:
                 head = [KIND_FULL, d["n_tokens"], 0, d["token_cap"], len(d["off"]), len(d["slots"]), 0, 0]
             else:
                 head = [KIND_INCREMENTAL, d["n_tokens"], d["tok_lo"], 0, 0, 0, len(d["su"]), len(d["nu"])]
+            if runs:
+                self.tree.build_runs()
+            if runs and self.tree.d_run_head is not None and self.tree.runs_version != self._sent_runs:
+                send_runs = (self.tree.d_run_head, self.tree.d_runs)
+                head += [send_runs[0].numel(), send_runs[1].shape[0]]
+                self._sent_runs = self.tree.runs_version
+            else:
+                head += [-1, 0]
             hdr = torch.tensor(head, dtype=torch.int64, device=dev)
         else:
             d = None
-            hdr = torch.empty(8, dtype=torch.int64, device=dev)
+            hdr = torch.empty(10, dtype=torch.int64, device=dev)
         self._bcast(hdr)
-        kind, n_tok, tok_lo, tok_cap, node_cap, slot_cap, n_su, n_nu = (int(x) for x in hdr.cpu())
+        kind, n_tok, tok_lo, tok_cap, node_cap, slot_cap, n_su, n_nu, run_nodes, n_runs = \
+            (int(x) for x in hdr.cpu())
+        run_arrays = {}
+        if run_nodes >= 0:
+            rh, re_ = send_runs if send_runs is not None else (
+                torch.empty(run_nodes, dtype=torch.int32, device=dev),
+                torch.empty((n_runs, 4), dtype=torch.int32, device=dev))
+            self._bcast(rh)
+            self._bcast(re_)
+            run_arrays = {"run_head": rh, "runs": re_}
         if kind == KIND_NONE:
-            return None
+            if not run_arrays:
+                return None
+            # new runs of an unchanged tree: an empty incremental delta carries them
+            empty = torch.empty(0, dtype=torch.int32, device=dev)
+            return {"full": False, "n_tokens": n_tok, "tok_lo": tok_lo, "tokens": empty,
+                    "su": empty.view(0, 5), "nu": empty.to(torch.int64).view(0, 3), **run_arrays}
         if kind == KIND_FULL:
             spec = [("tokens", n_tok, torch.int32), ("off", node_cap, torch.int64),
                     ("len", node_cap, torch.int32), ("slots", slot_cap * 4, torch.int32)]
@@ -90,14 +121,18 @@ class TreeReplicaSync:
         if kind == KIND_INCREMENTAL:
             out["su"] = out["su"].view(-1, 5)
             out["nu"] = out["nu"].view(-1, 3)
+        out.update(run_arrays)
         return out
 
-    def sync(self) -> None:
-        """Collective: bring every rank's device replica up to date with the
-        owner's tree."""
-        d = self.share()
-        if d is not None:
-            self.tree.apply_delta(d)
+    def sync(self, runs: bool = True) -> None:
+        """Collective: bring every rank's device replica (and, with runs=True,
+        its unary-chain runs) up to date with the owner's tree."""
+        d = self.share(runs)
+        if d is None:
+            return
+        self.tree.apply_delta(d)
+        if self.rank != self.src and "run_head" in d:
+            self.tree.set_runs(d["run_head"], d["runs"])
 
 
 def query_range(n_queries: int, rank: int, world: int) -> tuple:

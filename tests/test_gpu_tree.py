@@ -253,6 +253,13 @@ def test_match_prefix_stress_tree(golden_dir, name):
     np.testing.assert_array_equal(on, node)
     np.testing.assert_array_equal(ol, mlen)
     np.testing.assert_array_equal(oc, cmp_)
+    # one hash probe per hop (no unary-chain runs): the same answers
+    from agentkv_b200.device_tree import match_batch
+
+    hn, hl, hc = match_batch(pool._tree._dev_tree, queries, 16, with_compared=True, runs=False)
+    np.testing.assert_array_equal(hn, node)
+    np.testing.assert_array_equal(hl, mlen)
+    np.testing.assert_array_equal(hc, cmp_)
 
 
 def _oracle_tree_from(pool) -> dict:
@@ -400,3 +407,45 @@ def test_match_with_colliding_child_keys():
         [(int(n) if m else -1, int(m)) for n, m in want]
     assert all(int(m) == 12 for m in mlen[:24])
     assert all(int(m) == 0 for m in mlen[24:30])
+
+
+def test_match_long_unary_chains():
+    """A 70-node unary chain (prefixes of one sequence committed one block
+    longer each time) with a branch at depth 100: queries cut at every
+    depth, diverging at every third position (on an edge's first token and
+    inside edges) and running past the chain's end give the oracle's
+    (node, length, tokens compared), with the unary-chain runs (up to 32 hops
+    per load, across the 32-hop segment boundary) and with one hash probe
+    per hop."""
+    from agentkv_b200.device_tree import match_batch
+
+    bs = 4
+    cfg = PoolConfig(total_blocks=1024, block_size=bs, num_layers=1, num_kv_heads=1, head_dim=4,
+                     dtype="float16", device="meta")
+    pool = AgentKVPool(config=cfg)
+    ot = O.OracleTree(O.OracleAllocator(1024), bs)
+    rng = np.random.default_rng(23)
+    seq = rng.integers(0, 50000, size=70 * bs).tolist()
+    branch = seq[:100] + rng.integers(50000, 60000, size=40).tolist()
+    for s in [seq[: bs * k] for k in range(1, 71)] + [branch]:
+        for tree, api in ((pool, "pool"), (ot, "oracle")):
+            hd = tree.create_root(s)
+            need = -(-len(s) // bs)
+            if api == "pool":
+                tree.allocate_blocks(hd, need - len(tree.get_block_ids(hd)))
+            else:
+                while len(tree.get_block_ids(hd)) < need:
+                    tree.allocate_block(hd)
+            tree.commit_prefix(hd, len(s) - hd.shared_match_len)
+    queries = [seq[:n] for n in range(0, len(seq) + 1)] + [seq + [1, 2, 3], branch + [9], branch[:103]]
+    for p in range(0, len(seq), 3):
+        q = list(seq)
+        q[p] = 99999
+        queries.append(q)
+    dev_tree = pool._tree._dev_tree
+    want = [ot.match(q) for q in queries]
+    for runs in (True, False):
+        node, mlen, cmp_ = match_batch(dev_tree, queries, bs, with_compared=True, runs=runs)
+        got = [(int(n) if m else -1, int(m), int(c)) for n, m, c in zip(node, mlen, cmp_)]
+        assert got == [(int(n) if m else -1, int(m), int(c)) for n, m, c in want], runs
+    assert dev_tree.d_run_head is not None and int((dev_tree.d_run_head >= 0).sum()) >= 60

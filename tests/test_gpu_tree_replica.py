@@ -31,6 +31,7 @@ def test_replica_from_deltas_matches_reference(golden_dir):
     replica = DeviceTree(owner.device)
     replica.as_replica()
     kinds = []
+    runs_seen = 0
     queries = W.match_queries(spec, corpus, prefixes, batch=0, n=len(g["node"]))
     for i, seq in enumerate(corpus):
         h = pool.create_root(seq)
@@ -43,6 +44,9 @@ def test_replica_from_deltas_matches_reference(golden_dir):
             if d is not None:
                 kinds.append(d["full"])
                 replica.apply_delta(d)
+                if "run_head" in d:
+                    replica.set_runs(d["run_head"], d["runs"])
+                    runs_seen += 1
             if i % 111 == 0:
                 # mid-build: the replica answers like the owner
                 n0, l0 = match_batch(owner, queries[:64], 16)
@@ -50,6 +54,7 @@ def test_replica_from_deltas_matches_reference(golden_dir):
                 np.testing.assert_array_equal(n1, n0)
                 np.testing.assert_array_equal(l1, l0)
     assert any(kinds) and not all(kinds), kinds  # both full and incremental deltas
+    assert runs_seen > 1 and replica.d_run_head is not None  # the owner's runs reached the replica
     node, mlen, cmp_ = match_batch(replica, queries, 16, with_compared=True)
     np.testing.assert_array_equal(node, g["node"])
     np.testing.assert_array_equal(mlen, g["len"])

@@ -109,6 +109,7 @@ class _HostReplica:
 
     def __init__(self):
         self.tokens = self.off = self.len = self.slots = None
+        self.runs = ()
         self.n = 0
 
     def apply(self, d):
@@ -133,7 +134,7 @@ class _HostReplica:
         import hashlib
 
         h = hashlib.sha256()
-        for a in (self.tokens[: self.n], self.off, self.len, self.slots):
+        for a in (self.tokens[: self.n], self.off, self.len, self.slots, *self.runs):
             h.update(np.ascontiguousarray(a).tobytes())
         return int.from_bytes(h.digest()[:7], "little")
 
@@ -141,7 +142,7 @@ class _HostReplica:
 def _tree_worker(rank, world, port, q):
     """Rank 0 mutates a tree (nodes, edges, child slots, splits, deletions,
     growth and rehash); after every round the deltas reach rank 1, whose
-    replica must equal rank 0's arrays."""
+    replica (unary-chain runs included) must equal rank 0's arrays."""
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -182,8 +183,11 @@ def _tree_worker(rank, world, port, q):
             if rank == 0:
                 rep.tokens, rep.n = tree.h_tokens, tree.n_tokens
                 rep.off, rep.len, rep.slots = tree.h_off, tree.h_len, tree.h_slots
+                rep.runs = (tree.d_run_head.numpy(), tree.d_runs.numpy())
             elif d is not None:
                 rep.apply(d)
+                if "run_head" in d:  # the owner's unary-chain runs, rebuilt after its changes
+                    rep.runs = (d["run_head"].numpy().copy(), d["runs"].numpy().copy())
             dig = torch.tensor([rep.digest()], dtype=torch.int64)
             both = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
             dist.all_gather(both, dig)
