@@ -349,33 +349,56 @@ class DeviceTree:
         runs (its lookups use the hash table alone)."""
         if not self._runs_dirty or self._replica:
             return
-        n_nodes = len(self.h_off)
-        children: dict = {}
-        parent_of: dict = {}
-        for (p, t), slot in self._slot_of.items():
-            c, ln = int(self.h_slots[slot, 2]), int(self.h_slots[slot, 3])
-            children.setdefault(p, []).append((c, t, ln))
-            parent_of[c] = p
-        unary = {p: ch[0] for p, ch in children.items() if len(ch) == 1}
-        head = np.full(n_nodes, -1, np.int32)
-        entries = []
-        for u0 in unary:
-            if parent_of.get(u0) in unary:
-                continue  # inside a chain; reached from its head
-            chain = []
-            u = u0
-            while u in unary:
-                c, t, ln = unary[u]
-                chain.append((u, c, t, ln))
-                u = c
-                if len(chain) > len(unary):
-                    raise RuntimeError(f"DeviceTree.build_runs: the child links from node {u0} form a cycle")
-            base = len(entries)
-            for k, (u, c, t, ln) in enumerate(chain):
-                if u < n_nodes:
-                    head[u] = base + k
-                entries.append((c, t, ln, len(chain) - k))
-        runs = np.asarray(entries, np.int32).reshape(-1, 4)
+        # Array form (no per-node Python): child counts give the unary nodes,
+        # list ranking by pointer doubling gives each one's entries left in
+        # its chain (rem) and its chain's head, and a head's chain occupies
+        # rem[head] consecutive entries from an exclusive scan over the heads.
+        m = len(self._slot_of)
+        rows = self.h_slots[np.fromiter(self._slot_of.values(), np.int64, m)].astype(np.int64)
+        par, tok, ch, ln = rows[:, 0], rows[:, 1], rows[:, 2], rows[:, 3]
+        n = max(len(self.h_off), int(par.max()) + 1 if m else 0, int(ch.max()) + 1 if m else 0)
+        unary = np.bincount(par, minlength=n) == 1
+        sel = unary[par]  # the slot rows of the unary nodes' only children
+        nxt = np.full(n, -1, np.int64)
+        ntok = np.zeros(n, np.int64)
+        nlen = np.zeros(n, np.int64)
+        nxt[par[sel]], ntok[par[sel]], nlen[par[sel]] = ch[sel], tok[sel], ln[sel]
+        parent_of = np.full(n, -1, np.int64)
+        parent_of[ch] = par
+        us = np.flatnonzero(unary)
+        # succ: the chain's next unary node (-1 at its end); pred: its previous one
+        succ = np.full(n, -1, np.int64)
+        succ[us] = np.where(unary[nxt[us]], nxt[us], -1)
+        pred = np.full(n, -1, np.int64)
+        pu = parent_of[us]
+        pred[us] = np.where((pu >= 0) & unary[np.maximum(pu, 0)], pu, -1)
+        rem = unary.astype(np.int64)
+        jump = succ.copy()
+        for _ in range(64):
+            live = np.flatnonzero(jump >= 0)
+            if len(live) == 0:
+                break
+            rem[live] += rem[jump[live]]
+            jump[live] = jump[jump[live]]
+        else:
+            raise RuntimeError("DeviceTree.build_runs: the child links form a cycle")
+        root = np.where(pred >= 0, pred, np.arange(n))
+        for _ in range(64):
+            nr = root[root]
+            if np.array_equal(nr, root):
+                break
+            root = nr
+        else:
+            raise RuntimeError("DeviceTree.build_runs: the child links form a cycle")
+        heads = np.flatnonzero(unary & (pred < 0))
+        base = np.zeros(n, np.int64)
+        base[heads] = np.cumsum(rem[heads]) - rem[heads]
+        pos = base[root[us]] + rem[root[us]] - rem[us]
+        head = np.full(n, -1, np.int32)
+        head[us] = pos
+        entries = np.empty((len(us), 4), np.int64)
+        entries[pos] = np.stack([nxt[us], ntok[us], nlen[us], rem[us]], axis=1)
+        runs = entries.astype(np.int32)
         if len(runs) == 0:
             runs = np.zeros((1, 4), np.int32)  # keeps a valid pointer; no head points at it
         self.d_run_head = torch.from_numpy(head).to(self.device)

@@ -227,3 +227,15 @@ def test_unary_runs_follow_the_chains():
         assert not tree._runs_dirty
         tree.set_child(0, 12345, 1, 1)
         assert tree._runs_dirty
+    # an empty tree has no runs; child links that loop are refused
+    empty = DeviceTree(torch.device("cpu"), node_cap=8, slot_cap=16, token_cap=32)
+    empty.build_runs()
+    assert (empty.d_run_head.numpy() == -1).all()
+    loop = DeviceTree(torch.device("cpu"), node_cap=8, slot_cap=16, token_cap=32)
+    for nid in (1, 2):
+        loop.set_node(nid, loop.append_tokens(np.array([nid], np.int32)), 1)
+    loop.set_child(0, 1, 1, 1)
+    loop.set_child(1, 2, 2, 1)
+    loop.set_child(2, 1, 1, 1)
+    with pytest.raises(RuntimeError, match="cycle"):
+        loop.build_runs()
