@@ -574,13 +574,112 @@ def reference_arm(args, rank, world):
 
 
 # ── match_prefix figure ──────────────────────────────────────────────────────
+MATCH_NODE_BYTES = 32  # per visited node: its child slot (16 B) + edge offset and length, rounded up
+
+
+def match_compulsory_bytes(parent, edge_len, children, queries, out_node, out_cmp) -> dict:
+    """Compulsory DRAM bytes of one match_prefix batch: 4 B per query token
+    compared (the reference loop's comparison count), 4 B per distinct edge
+    token the batch touches (every edge on a matched path in full, the
+    partially compared child of each path end as far as it was compared) and
+    MATCH_NODE_BYTES per distinct visited node.  `parent`, `edge_len` and
+    `children` map node ids of the host tree; `out_node` / `out_cmp` are the
+    batch's results.  A query with no credited match (node -1) is counted
+    from the root."""
+    depth = {0: 0}
+    full = {0}
+    partial: dict = {}
+    q_bytes = 0
+
+    def depth_of(u: int) -> int:
+        stack = []
+        v = u
+        while v not in depth:
+            stack.append(v)
+            v = parent[v]
+        d = depth[v]
+        for w in reversed(stack):
+            d += int(edge_len[w])
+            depth[w] = d
+        return d
+
+    for q, u, c in zip(queries, out_node, out_cmp):
+        c = int(c)
+        q_bytes += 4 * c
+        u = int(u) if int(u) >= 0 else 0
+        v = u
+        while v not in full:  # once a node is in, so are its ancestors
+            full.add(v)
+            v = parent[v]
+        d = depth_of(u)
+        rest = c - d
+        if rest > 0 and d < len(q):
+            ch = children[u].get(int(q[d]))
+            if ch is not None:
+                partial[ch] = max(partial.get(ch, 0), min(rest, int(edge_len[ch])))
+    edge_tokens = sum(int(edge_len[v]) for v in full) + sum(n for v, n in partial.items() if v not in full)
+    nodes = len(full | set(partial))
+    return {"query_bytes": q_bytes, "edge_bytes": 4 * edge_tokens, "node_bytes": MATCH_NODE_BYTES * nodes,
+            "total": q_bytes + 4 * edge_tokens + MATCH_NODE_BYTES * nodes, "nodes": nodes}
+
+
+def match_cpu_baseline(pool, batches, gpu_results, max_seconds: float) -> dict:
+    """The oracle's C restatement of _match_prefix_locked, one host thread,
+    over the same tree and batches (repeated until max_seconds); also checks
+    its answers against the GPU's."""
+    from oracle import oracle as O
+
+    nodes = pool._tree._shared_nodes
+    n = max(nodes) + 1
+    child_ptr = np.zeros(n + 1, np.int64)
+    keys, ids, toks = [], [], []
+    edge_off = np.zeros(n, np.int64)
+    edge_len = np.zeros(n, np.int32)
+    pos = 0
+    for nid in range(n):
+        nd = nodes.get(nid)
+        if nd is not None:
+            for k in sorted(nd.children):
+                keys.append(k)
+                ids.append(nd.children[k])
+            e = np.asarray(nd.edge, np.int32)
+            edge_off[nid], edge_len[nid] = pos, len(e)
+            toks.append(e)
+            pos += len(e)
+        child_ptr[nid + 1] = len(keys)
+    csr = {"child_ptr": child_ptr, "child_key": np.asarray(keys or [0], np.int32),
+           "child_id": np.asarray(ids or [0], np.int32), "edge_off": edge_off, "edge_len": edge_len,
+           "edge_tokens": np.concatenate(toks) if pos else np.zeros(1, np.int32)}
+    packed = [O.pack_queries([q.tolist() for q in b]) for b in batches]
+    same = True
+    for (flat, off), (g_node, g_len) in zip(packed, gpu_results):
+        o_node, o_len, _ = O.match_prefix_csr(csr, flat, off, 16)
+        same &= bool(np.array_equal(o_len, g_len) and np.array_equal(np.where(o_len > 0, o_node, -1),
+                                                                      np.where(g_len > 0, g_node, -1)))
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        flat, off = packed[done % len(packed)]
+        O.match_prefix_csr(csr, flat, off, 16)
+        done += 1
+        secs = time.perf_counter() - t0
+        if secs >= max_seconds:
+            break
+    nq = len(batches[0])
+    return {"value": round(done * nq / secs, 1), "unit": "queries/s", "cores": 1, "kind": "port",
+            "sample": f"{done} batches of {nq} queries on the same tree, {secs:.1f} s, one host thread",
+            "same_answers_as_gpu": same}
+
+
 def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
                  n_queries: int = W.MatchSpec.n_queries, rank: int = 0, world: int = 1,
-                 use_runs: bool = True) -> dict:
+                 use_runs: bool = True, cpu_seconds: float = 0.0) -> dict:
     """match_prefix on the stress tree.  With N ranks, rank 0 builds the tree
     through the pool API and broadcasts it (TreeReplicaSync) to every rank's
     replica; each rank then matches its own 4096-query batches (weak
-    scaling), timed as the max over ranks."""
+    scaling), timed as the max over ranks.  Rank 0 adds the kernel's
+    roofline (compulsory bytes of its batches, match_compulsory_bytes) and,
+    at one rank with cpu_seconds > 0, the CPU baseline."""
     import torch
 
     from agentkv_b200 import AgentKVPool, PoolConfig
@@ -626,11 +725,21 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
     cmp_ = torch.empty(nq, dtype=torch.int64, device=dev)
     compared = []
     qtokens = []
+    results = []
     for (tok, off), order in zip(packed, orders):
         tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs)
         compared.append(int(cmp_.sum()))
         qtokens.append(int(off[-1]))
+        results.append((node.cpu().numpy(), mlen.cpu().numpy(), cmp_.cpu().numpy()))
     tree.check()
+    alg = None
+    if rank == 0:
+        shared = pool._tree._shared_nodes
+        parent = {k: v.parent_id for k, v in shared.items()}
+        elen = {k: v.edge_len for k, v in shared.items()}
+        kids = {k: v.children for k, v in shared.items()}
+        per = [match_compulsory_bytes(parent, elen, kids, q, r[0], r[2]) for q, r in zip(batches, results)]
+        alg = {k: int(statistics.mean(p[k] for p in per)) for k in per[0]}
 
     def run():
         for (tok, off), order in zip(packed, orders):
@@ -643,6 +752,22 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         t = torch.tensor([tok_cmp], dtype=torch.float64, device=dev)
         torch.distributed.all_reduce(t)
         tok_cmp = float(t) / world
+    roofline = cpu = None
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        achieved = alg["total"] / (per_batch_ms / 1e3) / 1e9
+        roofline = {
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_kind,
+            "kernel": f"akv match_prefix (k_match), one {nq}-query batch",
+            "algorithmic_bytes_per_launch": alg,
+            "note": "compulsory bytes: 4 B per query token compared, 4 B per distinct edge token touched, "
+                    f"{MATCH_NODE_BYTES} B per distinct visited node (rank 0's batches); the kernel is "
+                    "bound by dependent-load latency and issue, not by DRAM bandwidth; DRAM traffic was "
+                    "captured on the 2,000-sequence tree only (profiles/match_prefix_stress2k.md)",
+        }
+        if world == 1 and cpu_seconds > 0:
+            cpu = match_cpu_baseline(pool, batches, [(r[0], r[1]) for r in results], cpu_seconds)
     return {
         "metric": "match_prefix queries/s (stress tree)",
         "value": round(world * nq / (per_batch_ms / 1e3), 1),
@@ -658,6 +783,8 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         "replica_sync_s": round(sync_s, 2),
         "query_tokens_per_batch": int(statistics.mean(qtokens)),
         "unary_runs": bool(use_runs),
+        "roofline": roofline,
+        "cpu_baseline": cpu,
     }
 
 
@@ -875,7 +1002,8 @@ def main():
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                                  device_id=torch.device("cuda", local))
         fig = match_figure(args.steps, args.warmup, args.match_seqs, args.match_queries, rank, world,
-                           use_runs=bool(args.match_runs))
+                           use_runs=bool(args.match_runs),
+                           cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds)
         if rank == 0:
             print(json.dumps(fig), flush=True)
         if world > 1:

@@ -239,3 +239,56 @@ def test_unary_runs_follow_the_chains():
     loop.set_child(2, 1, 1, 1)
     with pytest.raises(RuntimeError, match="cycle"):
         loop.build_runs()
+
+
+def test_match_compulsory_bytes():
+    """The match roofline's byte count on a hand-built tree: root -> 1
+    (8-token edge) -> {2, 3} (4-token edges).  A: both edges of 0-1-2
+    compared in full; B: edge 1 in full, 2 tokens of edge 3; C: a mismatch
+    after 3 tokens of edge 1 (no credited match)."""
+    import bench
+
+    parent = {0: -1, 1: 0, 2: 1, 3: 1}
+    edge_len = {0: 0, 1: 8, 2: 4, 3: 4}
+    children = {0: {10: 1}, 1: {20: 2, 30: 3}, 2: {}, 3: {}}
+    qa = np.array([10] + [1] * 7 + [20, 2, 2, 2, 5, 5])
+    qb = np.array([10] + [1] * 7 + [30, 7, 7])
+    qc = np.array([10, 1, 1, 9])
+    got = bench.match_compulsory_bytes(parent, edge_len, children, [qa, qb, qc],
+                                       np.array([2, 1, -1]), np.array([12, 10, 3]))
+    assert got["query_bytes"] == 4 * (12 + 10 + 3)
+    assert got["edge_bytes"] == 4 * (8 + 4 + 2)  # edge 1 once, edge 2 in full, 2 tokens of edge 3
+    assert got["nodes"] == 4
+    assert got["total"] == 100 + 56 + 4 * bench.MATCH_NODE_BYTES
+
+
+def test_match_cpu_baseline_on_a_host_tree():
+    """bench.match_cpu_baseline flattens a host tree (nodes with .children and
+    .edge) for the oracle's C match and reports queries/s; answers equal to
+    the given ones are flagged as such, a planted difference is not."""
+    from types import SimpleNamespace
+
+    import bench
+    from oracle import oracle as O
+
+    ot = O.OracleTree(O.OracleAllocator(256), 16)
+    rng = np.random.default_rng(3)
+    seqs = [rng.integers(0, 40, size=int(rng.integers(16, 80))).tolist() for _ in range(30)]
+    for s in seqs:
+        h = ot.create_root(s)
+        while len(ot.get_block_ids(h)) < -(-len(s) // 16):
+            ot.allocate_block(h)
+        share = (len(s) // 16) * 16 - h.shared_match_len
+        if share > 0:
+            ot.commit_prefix(h, share)
+    batch = [np.asarray(s[: int(rng.integers(1, len(s) + 1))] + [99], np.int32) for s in seqs]
+    want = [ot.match(q.tolist()) for q in batch]
+    node = np.array([w[0] for w in want], np.int32)
+    mlen = np.array([w[1] for w in want], np.int32)
+    pool = SimpleNamespace(_tree=SimpleNamespace(_shared_nodes=ot.nodes))
+    res = bench.match_cpu_baseline(pool, [batch], [(node, mlen)], 0.05)
+    assert res["same_answers_as_gpu"] and res["value"] > 0 and res["cores"] == 1
+    assert mlen.max() > 0
+    planted = mlen.copy()
+    planted[int(np.argmax(mlen))] = 0
+    assert not bench.match_cpu_baseline(pool, [batch], [(node, planted)], 0.01)["same_answers_as_gpu"]
