@@ -758,7 +758,8 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         achieved = alg["total"] / (per_batch_ms / 1e3) / 1e9
         roofline = {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_kind,
+            "frac": round(achieved / peak, 4), "traffic": match_traffic(n_seqs) if use_runs else None,
+            "peak_source": peak_kind,
             "kernel": f"akv match_prefix (k_match), one {nq}-query batch",
             "algorithmic_bytes_per_launch": alg,
             "note": "compulsory bytes: 4 B per query token compared, 4 B per distinct edge token touched, "
@@ -959,6 +960,18 @@ def hf_case(args) -> None:
                       "peak_gbs": peak, "peak_source": peak_kind, **res,
                       "speedup": round(res["torch_index_permute"]["ms_per_decode_step"] /
                                        res["kv_gather"]["ms_per_decode_step"], 2)}), flush=True)
+
+
+def match_traffic(n_seqs: int):
+    """DRAM bytes (read + write) of one k_match batch launch on the
+    2,000-sequence stress tree from the committed ncu summary (the only tree
+    size captured), or None."""
+    p = REPO / "profiles" / "match_prefix_stress2k.md"
+    if n_seqs == 2000 and p.exists():
+        for line in p.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1])
+    return None
 
 
 def copy_traffic(n_pairs: int):
