@@ -20,10 +20,19 @@ A delta is the list of changed slots and node ranges plus the appended token
 range; ``flush`` uploads it (akv_tree_apply) on the caller's stream, or the
 whole arrays after a resize.  Lookups run the akv_match_prefix kernel: one
 warp per query.
+
+Batched lookups also use the unary-chain runs (``build_runs``), derived
+from the slots: every maximal chain of single-child nodes stored once as
+consecutive int32x4 entries {child, first token, edge length, entries left},
+and ``run_head[node]`` the entry of a single-child node's child (-1
+otherwise).  The kernel takes up to 32 hops of a chain from one load instead
+of one dependent hash probe per hop; the runs are rebuilt from the host
+mirror when the tree has changed, and replicas receive the owner's.
 """
 
 from __future__ import annotations
 
+import time
 from typing import Optional, Sequence, Tuple
 
 import numpy as np
@@ -95,6 +104,8 @@ class DeviceTree:
         self._replica = False
         self._runs_dirty = True
         self.runs_version = 0  # bumped by every build_runs that rebuilt
+        self._build_ms: Optional[float] = None  # host time of the last build_runs
+        self._rent_ms = 0.0  # one-probe-per-hop lookup time since the last change
         self.d_run_head: Optional[torch.Tensor] = None
         self.d_runs: Optional[torch.Tensor] = None
         self.d_tokens = torch.zeros(token_cap, dtype=torch.int32, device=device)
@@ -133,7 +144,7 @@ class DeviceTree:
             self._mark_full()
         self.h_off[nid] = off
         self.h_len[nid] = length
-        self._runs_dirty = True
+        self._changed()
         for c in self._trackers():
             c.nodes.add(nid)
 
@@ -173,7 +184,7 @@ class DeviceTree:
             self.live += 1
             self._slot_of[key] = s
         self.h_slots[s] = (parent, token, child, child_len)
-        self._runs_dirty = True
+        self._changed()
         for c in self._trackers():
             c.slots.add(s)
 
@@ -182,7 +193,7 @@ class DeviceTree:
         if s is None:
             return
         self.h_slots[s] = (DELETED, 0, 0, 0)
-        self._runs_dirty = True
+        self._changed()
         self.live -= 1
         self.dead += 1
         for c in self._trackers():
@@ -204,6 +215,11 @@ class DeviceTree:
             self._slot_of[(p, t)] = s
             self.live += 1
         self._mark_full()
+
+    def _changed(self) -> None:
+        # the runs are stale, and a new stable period of the tree begins
+        self._runs_dirty = True
+        self._rent_ms = 0.0
 
     def _trackers(self):
         return (self._local,) if self._peers is None else (self._local, self._peers)
@@ -349,6 +365,7 @@ class DeviceTree:
         runs (its lookups use the hash table alone)."""
         if not self._runs_dirty or self._replica:
             return
+        t0 = time.perf_counter()
         # Array form (no per-node Python): child counts give the unary nodes,
         # list ranking by pointer doubling gives each one's entries left in
         # its chain (rem) and its chain's head, and a head's chain occupies
@@ -405,6 +422,26 @@ class DeviceTree:
         self.d_runs = torch.from_numpy(runs).to(self.device)
         self._runs_dirty = False
         self.runs_version += 1
+        self._build_ms = (time.perf_counter() - t0) * 1e3
+
+    def want_runs(self) -> bool:
+        """Whether a batched lookup should use the unary-chain runs: yes when
+        they are current; on a replica only when the owner's have arrived;
+        otherwise (stale runs) a rebuild is worth it once the one-probe-per-hop
+        lookups since the tree last changed (note_hash_lookup) have taken as
+        long as the previous rebuild — the ski-rental rule, which keeps a tree
+        that changes between every batch from paying a rebuild per batch and
+        costs at most about twice the better of the two choices.  A tree
+        whose runs were never built builds them."""
+        if self._replica:
+            return self.d_run_head is not None
+        if not self._runs_dirty or self._build_ms is None:
+            return True
+        return self._rent_ms >= self._build_ms
+
+    def note_hash_lookup(self, ms: float) -> None:
+        """Record a lookup batch taken without the runs (host milliseconds)."""
+        self._rent_ms += ms
 
     # ── lookups ──────────────────────────────────────────────────────────────
     def match(self, tokens: torch.Tensor, q_off: torch.Tensor, nq: int, block_size: int,
@@ -457,12 +494,17 @@ def longest_first(q_off, device: torch.device) -> torch.Tensor:
 
 
 def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_compared: bool = False,
-                runs: bool = True):
+                runs: Optional[bool] = None):
     """Longest shared prefix of many queries in one akv_match_prefix launch on
     `tree` (the owner's replica or another GPU's): (node ids, match lengths
     [, tokens compared]) as numpy arrays, each equal to the reference's
     _match_prefix_locked (agentkv/core/radix_tree.py:513-570) on that query.
-    runs=False takes one hash probe per hop instead of the unary-chain runs."""
+    runs=True follows the unary-chain runs (rebuilt first when stale),
+    runs=False takes one hash probe per hop, None lets the tree decide
+    (DeviceTree.want_runs); the answers are the same."""
+    t0 = time.perf_counter()
+    if runs is None:
+        runs = tree.want_runs()
     dev = tree.device
     nq = len(queries)
     tok, q_off = pack_queries(queries, dev)
@@ -476,4 +518,6 @@ def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_co
     res = (node[:nq].cpu().numpy(), mlen[:nq].cpu().numpy())
     if with_compared:
         res = res + (cmp_[:nq].cpu().numpy(),)
+    if not runs:
+        tree.note_hash_lookup((time.perf_counter() - t0) * 1e3)
     return res

@@ -61,9 +61,10 @@ class TreeReplicaSync:
     def share(self, runs: bool = True) -> Optional[dict]:
         """Collective: rank src takes its pending delta and sends it; every
         rank returns the delta with its arrays as tensors on its device (None
-        when nothing changed).  With runs=True the owner brings its unary-chain
-        runs up to date and sends them when they were rebuilt (keys
-        "run_head" / "runs" of the result)."""
+        when nothing changed).  With runs=True the owner rebuilds its stale
+        unary-chain runs when DeviceTree.want_runs says a rebuild pays (or
+        the caller built them) and sends them when they changed since the
+        last share (keys "run_head" / "runs" of the result)."""
         dev = self.device
         send_runs = None
         if self.rank == self.src:
@@ -74,7 +75,7 @@ class TreeReplicaSync:
                 head = [KIND_FULL, d["n_tokens"], 0, d["token_cap"], len(d["off"]), len(d["slots"]), 0, 0]
             else:
                 head = [KIND_INCREMENTAL, d["n_tokens"], d["tok_lo"], 0, 0, 0, len(d["su"]), len(d["nu"])]
-            if runs:
+            if runs and self.tree.want_runs():
                 self.tree.build_runs()
             if runs and self.tree.d_run_head is not None and self.tree.runs_version != self._sent_runs:
                 send_runs = (self.tree.d_run_head, self.tree.d_runs)

@@ -40,6 +40,7 @@ def test_replica_from_deltas_matches_reference(golden_dir):
         if share > 0:
             pool.commit_prefix(h, share)
         if i % 37 == 0 or i == len(corpus) - 1:
+            owner.build_runs()  # current runs on every share, so each one travels
             d = sync.share()
             if d is not None:
                 kinds.append(d["full"])

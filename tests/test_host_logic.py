@@ -292,3 +292,39 @@ def test_match_cpu_baseline_on_a_host_tree():
     planted = mlen.copy()
     planted[int(np.argmax(mlen))] = 0
     assert not bench.match_cpu_baseline(pool, [batch], [(node, planted)], 0.01)["same_answers_as_gpu"]
+
+
+def test_run_rebuild_policy():
+    """DeviceTree.want_runs: a never-built tree builds; current runs are used;
+    after a change the one-probe-per-hop lookups pay rent until it reaches
+    the last rebuild's cost; every change restarts the count; a replica uses
+    runs only while it holds the owner's."""
+    import torch
+
+    from agentkv_b200.device_tree import DeviceTree
+
+    t = DeviceTree(torch.device("cpu"), node_cap=8, slot_cap=16, token_cap=32)
+    t.set_node(1, t.append_tokens(np.array([5, 6], np.int32)), 2)
+    t.set_child(0, 5, 1, 2)
+    assert t.want_runs()  # never built
+    t.build_runs()
+    assert t.want_runs() and t._build_ms is not None
+    t._build_ms = 2.0  # a rebuild costs 2 ms
+    t.set_node(2, t.append_tokens(np.array([7], np.int32)), 1)
+    t.set_child(1, 7, 2, 1)
+    assert not t.want_runs()
+    t.note_hash_lookup(1.5)
+    assert not t.want_runs()
+    t.set_child(1, 8, 2, 1)  # a change: the rent starts over
+    t.note_hash_lookup(1.5)
+    assert not t.want_runs()
+    t.note_hash_lookup(0.5)
+    assert t.want_runs()
+    t.build_runs()
+    assert t.want_runs() and not t._runs_dirty
+
+    r = DeviceTree(torch.device("cpu"), node_cap=8, slot_cap=16, token_cap=32)
+    r.as_replica()
+    assert not r.want_runs()
+    r.set_runs(t.d_run_head, t.d_runs)
+    assert r.want_runs()

@@ -179,6 +179,8 @@ def _tree_worker(rank, world, port, q):
                         parent, tok = nodes.pop(nid)
                         tree.del_child(parent, tok)
                         tree.clear_node(nid)
+            if rank == 0:
+                tree.build_runs()  # current runs on every share, so each one travels
             d = sync.share()
             if rank == 0:
                 rep.tokens, rep.n = tree.h_tokens, tree.n_tokens
