@@ -106,6 +106,16 @@ class DeviceTree:
         self.runs_version = 0  # bumped by every build_runs that rebuilt
         self._build_ms: Optional[float] = None  # host time of the last build_runs
         self._rent_ms = 0.0  # one-probe-per-hop lookup time since the last change
+        self._last_batch_ms = 0.0  # host time of the last batched lookup
+        # child structure for the incremental run updates
+        self._kids: dict = {}  # parent -> set of first tokens of its children
+        self._parent_of: dict = {}  # child -> parent
+        self._n_unary = 0  # nodes with exactly one child
+        self._runs_touched: set = set()  # nodes whose children changed since the last build
+        self._h_run_head: Optional[np.ndarray] = None  # host copy of the runs
+        self._h_runs = np.zeros((0, 4), np.int32)
+        self._n_entries = 0  # entries in use, live and superseded
+        self._node_bound = 0  # 1 + the largest node id in a child link
         self.d_run_head: Optional[torch.Tensor] = None
         self.d_runs: Optional[torch.Tensor] = None
         self.d_tokens = torch.zeros(token_cap, dtype=torch.int32, device=device)
@@ -143,8 +153,7 @@ class DeviceTree:
                 setattr(self, name, new)
             self._mark_full()
         self.h_off[nid] = off
-        self.h_len[nid] = length
-        self._changed()
+        self.h_len[nid] = length  # edge ranges are not part of the runs
         for c in self._trackers():
             c.nodes.add(nid)
 
@@ -183,8 +192,17 @@ class DeviceTree:
                 self.dead -= 1
             self.live += 1
             self._slot_of[key] = s
+            kids = self._kids.setdefault(parent, set())
+            self._n_unary += (len(kids) == 0) - (len(kids) == 1)
+            kids.add(token)
+        else:
+            old = int(self.h_slots[s, 2])
+            if old != child and self._parent_of.get(old) == parent:
+                del self._parent_of[old]
+        self._parent_of[child] = parent
+        self._node_bound = max(self._node_bound, parent + 1, child + 1)
         self.h_slots[s] = (parent, token, child, child_len)
-        self._changed()
+        self._changed(parent)
         for c in self._trackers():
             c.slots.add(s)
 
@@ -192,8 +210,16 @@ class DeviceTree:
         s = self._slot_of.pop((parent, token), None)
         if s is None:
             return
+        child = int(self.h_slots[s, 2])
+        if self._parent_of.get(child) == parent:
+            del self._parent_of[child]
+        kids = self._kids[parent]
+        kids.discard(token)
+        self._n_unary += (len(kids) == 1) - (len(kids) == 0)
+        if not kids:
+            del self._kids[parent]
         self.h_slots[s] = (DELETED, 0, 0, 0)
-        self._changed()
+        self._changed(parent)
         self.live -= 1
         self.dead += 1
         for c in self._trackers():
@@ -216,9 +242,11 @@ class DeviceTree:
             self.live += 1
         self._mark_full()
 
-    def _changed(self) -> None:
-        # the runs are stale, and a new stable period of the tree begins
+    def _changed(self, parent: int) -> None:
+        # `parent`'s children changed: the runs through it are stale, and a
+        # new stable period of the tree begins
         self._runs_dirty = True
+        self._runs_touched.add(parent)
         self._rent_ms = 0.0
 
     def _trackers(self):
@@ -317,7 +345,8 @@ class DeviceTree:
         n_su, n_nu = len(d["su"]), len(d["nu"])
         if n_su == 0 and n_nu == 0:
             return
-        self._drop_replica_runs()
+        if n_su:
+            self._drop_replica_runs()  # node rows (edge ranges) leave the runs valid
         su_d = on_dev(d["su"], torch.int32) if n_su else None
         nu_d = on_dev(d["nu"], torch.int64) if n_nu else None
         N.check(N.lib.akv_tree_apply(
@@ -357,15 +386,34 @@ class DeviceTree:
         self._runs_dirty = False
 
     def build_runs(self) -> None:
-        """Rebuild the runs from the host mirror when the tree changed since
-        the last build: for every node with exactly one child, the chain it
-        starts (its only child, that child's only child, ... through the
-        first node without exactly one child), stored per maximal chain, each
-        node pointing at its suffix.  A replica without a host mirror has no
-        runs (its lookups use the hash table alone)."""
+        """Bring the runs up to date with the host mirror when the tree
+        changed since the last build: for every node with exactly one child,
+        the chain it starts (its only child, that child's only child, ...
+        through the first node without exactly one child), stored per maximal
+        chain, each node pointing at its suffix.  After the first build only
+        the chains through nodes whose children changed are written again
+        (appended; the entries they supersede stay unused until a full build
+        compacts them).  A replica without a host mirror has no runs of its
+        own (it uses the owner's, set_runs)."""
         if not self._runs_dirty or self._replica:
             return
         t0 = time.perf_counter()
+        n = max(len(self.h_off), self._node_bound)
+        superseded = self._n_entries - self._n_unary
+        if (self._h_run_head is None or superseded > max(4096, self._n_unary)
+                or len(self._runs_touched) > max(64, n // 64)):
+            self._full_runs(n)
+        else:
+            self._patch_runs(n)
+        self._runs_touched.clear()
+        runs = self._h_runs[: max(self._n_entries, 1)]  # entry 0 keeps a valid pointer when there are none
+        self.d_run_head = torch.from_numpy(self._h_run_head[:n].copy()).to(self.device)
+        self.d_runs = torch.from_numpy(runs.copy()).to(self.device)
+        self._runs_dirty = False
+        self.runs_version += 1
+        self._build_ms = (time.perf_counter() - t0) * 1e3
+
+    def _full_runs(self, n: int) -> None:
         # Array form (no per-node Python): child counts give the unary nodes,
         # list ranking by pointer doubling gives each one's entries left in
         # its chain (rem) and its chain's head, and a head's chain occupies
@@ -373,7 +421,6 @@ class DeviceTree:
         m = len(self._slot_of)
         rows = self.h_slots[np.fromiter(self._slot_of.values(), np.int64, m)].astype(np.int64)
         par, tok, ch, ln = rows[:, 0], rows[:, 1], rows[:, 2], rows[:, 3]
-        n = max(len(self.h_off), int(par.max()) + 1 if m else 0, int(ch.max()) + 1 if m else 0)
         unary = np.bincount(par, minlength=n) == 1
         sel = unary[par]  # the slot rows of the unary nodes' only children
         nxt = np.full(n, -1, np.int64)
@@ -413,35 +460,84 @@ class DeviceTree:
         pos = base[root[us]] + rem[root[us]] - rem[us]
         head = np.full(n, -1, np.int32)
         head[us] = pos
-        entries = np.empty((len(us), 4), np.int64)
-        entries[pos] = np.stack([nxt[us], ntok[us], nlen[us], rem[us]], axis=1)
-        runs = entries.astype(np.int32)
-        if len(runs) == 0:
-            runs = np.zeros((1, 4), np.int32)  # keeps a valid pointer; no head points at it
-        self.d_run_head = torch.from_numpy(head).to(self.device)
-        self.d_runs = torch.from_numpy(runs).to(self.device)
-        self._runs_dirty = False
-        self.runs_version += 1
-        self._build_ms = (time.perf_counter() - t0) * 1e3
+        cap = max(16, 2 * len(us))
+        self._h_runs = np.zeros((cap, 4), np.int32)
+        self._h_runs[pos] = np.stack([nxt[us], ntok[us], nlen[us], rem[us]], axis=1)
+        self._h_run_head = head
+        self._n_entries = len(us)
+
+    def _patch_runs(self, n: int) -> None:
+        # Rewrite every chain that runs through a node whose children changed
+        # (the chain entering it, through its parent, and the one leaving it);
+        # chains split off below a change keep their entries, which are
+        # suffixes of the old chain ending where they still end.
+        kids, parent_of = self._kids, self._parent_of
+        if len(self._h_run_head) < n:
+            grown = np.full(max(n, 2 * len(self._h_run_head)), -1, np.int32)
+            grown[: len(self._h_run_head)] = self._h_run_head
+            self._h_run_head = grown
+        head = self._h_run_head
+        limit = len(parent_of) + 1
+
+        def unary(u) -> bool:
+            k = kids.get(u)
+            return k is not None and len(k) == 1
+
+        starts = set()
+        for p in self._runs_touched:
+            if not unary(p) and p < len(head):
+                head[p] = -1
+            for q in (p, parent_of.get(p)):
+                if q is None or not unary(q):
+                    continue
+                steps = 0
+                while parent_of.get(q) is not None and unary(parent_of[q]):
+                    q = parent_of[q]
+                    steps += 1
+                    if steps > limit:
+                        raise RuntimeError("DeviceTree.build_runs: the child links form a cycle")
+                starts.add(q)
+        for u in starts:
+            chain = []
+            while unary(u):
+                (t,) = kids[u]
+                s = self._slot_of[(u, t)]
+                c = int(self.h_slots[s, 2])
+                chain.append((u, c, t, int(self.h_slots[s, 3])))
+                u = c
+                if len(chain) > limit:
+                    raise RuntimeError("DeviceTree.build_runs: the child links form a cycle")
+            m, base = len(chain), self._n_entries
+            if base + m > len(self._h_runs):
+                grown = np.zeros((max(2 * len(self._h_runs), base + m, 16), 4), np.int32)
+                grown[:base] = self._h_runs[:base]
+                self._h_runs = grown
+            for k, (v, c, t, ln) in enumerate(chain):
+                self._h_runs[base + k] = (c, t, ln, m - k)
+                head[v] = base + k
+            self._n_entries = base + m
 
     def want_runs(self) -> bool:
         """Whether a batched lookup should use the unary-chain runs: yes when
-        they are current; on a replica only when the owner's have arrived;
-        otherwise (stale runs) a rebuild is worth it once the one-probe-per-hop
-        lookups since the tree last changed (note_hash_lookup) have taken as
-        long as the previous rebuild — the ski-rental rule, which keeps a tree
-        that changes between every batch from paying a rebuild per batch and
-        costs at most about twice the better of the two choices.  A tree
-        whose runs were never built builds them."""
+        they are current; on a replica only when the owner's have arrived.
+        With stale runs the rule is ski rental: rebuild once the
+        one-probe-per-hop lookups since the tree last changed, counting the
+        coming one at the last batch's time, have cost as much as the last
+        rebuild did.  An incremental rebuild costs tens of microseconds, so a
+        tree that changes between batches normally rebuilds every time; a
+        tree whose last build was a slow full one rents first.  A tree whose
+        runs were never built builds them."""
         if self._replica:
             return self.d_run_head is not None
         if not self._runs_dirty or self._build_ms is None:
             return True
-        return self._rent_ms >= self._build_ms
+        return self._rent_ms + self._last_batch_ms >= self._build_ms
 
-    def note_hash_lookup(self, ms: float) -> None:
-        """Record a lookup batch taken without the runs (host milliseconds)."""
-        self._rent_ms += ms
+    def note_lookup(self, ms: float, runs: bool) -> None:
+        """Record a batched lookup's host time and whether it used the runs."""
+        self._last_batch_ms = ms
+        if not runs:
+            self._rent_ms += ms
 
     # ── lookups ──────────────────────────────────────────────────────────────
     def match(self, tokens: torch.Tensor, q_off: torch.Tensor, nq: int, block_size: int,
@@ -518,6 +614,5 @@ def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_co
     res = (node[:nq].cpu().numpy(), mlen[:nq].cpu().numpy())
     if with_compared:
         res = res + (cmp_[:nq].cpu().numpy(),)
-    if not runs:
-        tree.note_hash_lookup((time.perf_counter() - t0) * 1e3)
+    tree.note_lookup((time.perf_counter() - t0) * 1e3, runs)
     return res

@@ -172,58 +172,100 @@ def test_hf_script_and_states_are_deterministic():
     assert all(t != s for st in tr for _, s, t in st)
 
 
+def _check_runs(tree, tag):
+    """Every node with exactly one child points at entries that walk its
+    unary chain through the first node without exactly one child (each
+    entry {child, first token, child's edge length, entries left}); every
+    other node points nowhere."""
+    head = tree.d_run_head.numpy()
+    runs = tree.d_runs.numpy()
+    kids = {}
+    for (p, t), s in tree._slot_of.items():
+        kids.setdefault(p, []).append((int(tree.h_slots[s, 2]), t, int(tree.h_slots[s, 3])))
+    assert sum(len(c) == 1 for c in kids.values()) == tree._n_unary, tag
+    for u in range(len(head)):
+        ch = kids.get(u, [])
+        if len(ch) != 1:
+            assert head[u] == -1, (tag, u)
+            continue
+        i, node = int(head[u]), u
+        rem = int(runs[i, 3])
+        assert rem >= 1 and i + rem <= len(runs), (tag, u)
+        for j in range(rem):
+            c, t, ln, r = (int(x) for x in runs[i + j])
+            assert r == rem - j, (tag, u, j)
+            assert kids[node] == [(c, t, ln)], (tag, u, j)
+            node = c
+        assert len(kids.get(node, [])) != 1, (tag, u)  # the chain ends at a non-unary node
+    assert all(u < len(head) for u, c in kids.items() if len(c) == 1), tag
+
+
 def test_unary_runs_follow_the_chains():
-    """DeviceTree.build_runs: every node with exactly one child points at a
-    run whose entries walk its unary chain (only child, its only child, ...)
-    through the first node without exactly one child; other nodes have no
-    run.  Random trees with splits, deletions and growth."""
+    """DeviceTree.build_runs, first in full and then by rewriting only the
+    chains through changed nodes: after every few random changes (new
+    children, edge splits that put a node between a parent and its child,
+    removed leaves), every node with exactly one child walks its chain and
+    no other node has a run; larger change batches take the full build."""
     import torch
 
     from agentkv_b200.device_tree import DeviceTree
 
     rng = np.random.default_rng(11)
-    for trial in range(5):
+    for trial in range(6):
         tree = DeviceTree(torch.device("cpu"), node_cap=8, slot_cap=16, token_cap=32)
-        nodes = {0: None}
+        nodes = {0: None}  # node -> (parent, first token)
         nxt = 1
-        for _ in range(300):
+        builds = 0
+        full = []
+        full_runs = tree._full_runs
+        tree._full_runs = lambda n: (full.append(n), full_runs(n))
+        for step in range(400):
             op = rng.integers(0, 10)
-            if op < 7 or len(nodes) < 3:
+            if op < 5 or len(nodes) < 3:
                 parent = int(rng.choice(list(nodes)))
                 toks = rng.integers(0, 30, size=int(rng.integers(1, 6)), dtype=np.int32)
                 if (parent, int(toks[0])) in tree._slot_of:
                     continue
-                off = tree.append_tokens(toks)
-                tree.set_node(nxt, off, len(toks))
+                tree.set_node(nxt, tree.append_tokens(toks), len(toks))
                 tree.set_child(parent, int(toks[0]), nxt, len(toks))
                 nodes[nxt] = (parent, int(toks[0]))
                 nxt += 1
+            elif op < 8:
+                # split the edge into child c: parent -> mid -> c
+                c = int(rng.choice([k for k in nodes if k]))
+                parent, tok = nodes[c]
+                ln = int(tree.h_len[c])
+                if ln < 2:
+                    continue
+                k = int(rng.integers(1, ln))
+                off = int(tree.h_off[c])
+                t2 = int(tree.h_tokens[off + k])
+                tree.set_node(nxt, off, k)
+                tree.set_node(c, off + k, ln - k)
+                tree.set_child(parent, tok, nxt, k)
+                tree.set_child(nxt, t2, c, ln - k)
+                nodes[nxt] = (parent, tok)
+                nodes[c] = (nxt, t2)
+                nxt += 1
             else:
                 nid = int(rng.choice([k for k in nodes if k]))
-                if any(p == nid for p, _ in tree._slot_of):
+                if nid in tree._kids:
                     continue  # only leaves are removed
                 parent, tok = nodes.pop(nid)
                 tree.del_child(parent, tok)
                 tree.clear_node(nid)
+            every = 150 if trial == 5 else int(rng.integers(1, 6))  # the last trial: > 64 changes per build
+            if step % every == 0:
+                tree.build_runs()
+                builds += 1
+                _check_runs(tree, (trial, step))
         tree.build_runs()
-        head = tree.d_run_head.numpy()
-        runs = tree.d_runs.numpy()
-        kids = {}
-        for (p, t), s in tree._slot_of.items():
-            kids.setdefault(p, []).append((int(tree.h_slots[s, 2]), t, int(tree.h_slots[s, 3])))
-        for u in range(len(head)):
-            ch = kids.get(u, [])
-            if len(ch) != 1:
-                assert head[u] == -1, (trial, u)
-                continue
-            i, node = int(head[u]), u
-            rem = int(runs[i, 3])
-            for j in range(rem):
-                c, t, ln, r = (int(x) for x in runs[i + j])
-                assert r == rem - j
-                assert kids[node] == [(c, t, ln)]
-                node = c
-            assert len(kids.get(node, [])) != 1  # the chain ends at a non-unary node
+        _check_runs(tree, (trial, "end"))
+        assert tree._n_entries >= tree._n_unary
+        if trial < 5:
+            assert builds > 20 and len(full) == 1  # the first build in full, every later one incremental
+        else:
+            assert len(full) >= 2  # a batch of more than 64 changed nodes took a full build
         assert not tree._runs_dirty
         tree.set_child(0, 12345, 1, 1)
         assert tree._runs_dirty
@@ -239,6 +281,16 @@ def test_unary_runs_follow_the_chains():
     loop.set_child(2, 1, 1, 1)
     with pytest.raises(RuntimeError, match="cycle"):
         loop.build_runs()
+    # a loop made after the first build is refused by the incremental update too
+    loop2 = DeviceTree(torch.device("cpu"), node_cap=8, slot_cap=16, token_cap=32)
+    for nid in (1, 2):
+        loop2.set_node(nid, loop2.append_tokens(np.array([nid], np.int32)), 1)
+    loop2.set_child(0, 1, 1, 1)
+    loop2.set_child(1, 2, 2, 1)
+    loop2.build_runs()
+    loop2.set_child(2, 1, 1, 1)
+    with pytest.raises(RuntimeError, match="cycle"):
+        loop2.build_runs()
 
 
 def test_match_compulsory_bytes():
@@ -296,9 +348,10 @@ def test_match_cpu_baseline_on_a_host_tree():
 
 def test_run_rebuild_policy():
     """DeviceTree.want_runs: a never-built tree builds; current runs are used;
-    after a change the one-probe-per-hop lookups pay rent until it reaches
-    the last rebuild's cost; every change restarts the count; a replica uses
-    runs only while it holds the owner's."""
+    after a change the one-probe-per-hop lookups pay rent, the coming one
+    counted at the last batch's time, until it reaches the last rebuild's
+    cost; every change restarts the count; a replica uses runs only while it
+    holds the owner's."""
     import torch
 
     from agentkv_b200.device_tree import DeviceTree
@@ -310,21 +363,78 @@ def test_run_rebuild_policy():
     t.build_runs()
     assert t.want_runs() and t._build_ms is not None
     t._build_ms = 2.0  # a rebuild costs 2 ms
+    t.note_lookup(0.5, True)
     t.set_node(2, t.append_tokens(np.array([7], np.int32)), 1)
     t.set_child(1, 7, 2, 1)
-    assert not t.want_runs()
-    t.note_hash_lookup(1.5)
-    assert not t.want_runs()
+    assert not t.want_runs()  # 0 + 0.5 < 2
+    t.note_lookup(0.7, False)
+    assert not t.want_runs()  # 0.7 + 0.7 < 2
     t.set_child(1, 8, 2, 1)  # a change: the rent starts over
-    t.note_hash_lookup(1.5)
+    t.note_lookup(0.7, False)
     assert not t.want_runs()
-    t.note_hash_lookup(0.5)
-    assert t.want_runs()
+    t.note_lookup(0.7, False)
+    assert t.want_runs()  # 1.4 + 0.7 >= 2
     t.build_runs()
     assert t.want_runs() and not t._runs_dirty
+    t._build_ms = 0.05  # a cheap incremental rebuild: the next change rebuilds at once
+    t.set_child(2, 9, 1, 1)
+    assert t.want_runs()
 
     r = DeviceTree(torch.device("cpu"), node_cap=8, slot_cap=16, token_cap=32)
     r.as_replica()
     assert not r.want_runs()
     r.set_runs(t.d_run_head, t.d_runs)
     assert r.want_runs()
+
+
+def test_unary_runs_under_the_tree_insert_logic():
+    """The incremental run updates follow DualRadixTree's own inserts —
+    children added, edges split on block boundaries with the split node put
+    between parent and child, the split==0 overwrite that orphans a subtree,
+    exact re-commits — on a CPU device tree: after every few inserts of the
+    stress workload's sequences (prefix sharing, block-floored lengths) the
+    runs walk every unary chain."""
+    import torch
+
+    from agentkv_b200.allocator import BlockHandle
+    from agentkv_b200.device_tree import DeviceTree
+    from agentkv_b200.radix_tree import ROOT_NODE_ID, DualRadixTree, SharedNode
+
+    spec = W.MatchSpec(n_prefixes=12, prefix_min=32, prefix_max=160, n_sequences=300, total_min=16,
+                       total_max=320, n_queries=1)
+    prefixes = W.match_prefixes(spec)
+    corpus = W.match_sequences(spec, prefixes)
+    tree = object.__new__(DualRadixTree)
+    tree._cfg = PoolConfig(total_blocks=64, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1,
+                           dtype="float16", device="meta")
+    tree._dev_tree = dt = DeviceTree(torch.device("cpu"), node_cap=8, slot_cap=16, token_cap=64)
+    tree._shared_nodes = {ROOT_NODE_ID: SharedNode(ROOT_NODE_ID, -1, dt)}
+    dt.set_node(ROOT_NODE_ID, 0, 0)
+    tree._next_node_id = 1
+    rng = np.random.default_rng(4)
+    full = []
+    full_runs = dt._full_runs
+    dt._full_runs = lambda n: (full.append(n), full_runs(n))
+    for i, seq in enumerate(corpus):
+        n = (len(seq) // 16) * 16
+        if rng.random() < 0.2:  # a commit cut inside the shared prefix (split == 0 cases included)
+            n = int(rng.integers(0, n // 16 + 1)) * 16
+        if n:
+            tree._insert_shared_locked(ROOT_NODE_ID, np.asarray(seq[:n], np.int32),
+                                       [BlockHandle(b) for b in range(n // 16)])
+        if i % 3 == 0:
+            dt.build_runs()
+            _check_runs(dt, i)
+    dt.build_runs()
+    _check_runs(dt, "end")
+    assert dt._n_unary > 20 and len(full) == 1
+    # and a from-scratch build gives the same chains
+    fresh_head = dt.d_run_head.numpy().copy()
+    fresh_runs = dt.d_runs.numpy().copy()
+    dt._runs_dirty = True
+    dt._full_runs(len(fresh_head))
+    for u in np.flatnonzero(fresh_head >= 0):
+        a, b = int(fresh_head[u]), int(dt._h_run_head[u])
+        r = int(fresh_runs[a, 3])
+        assert r == int(dt._h_runs[b, 3])
+        np.testing.assert_array_equal(fresh_runs[a:a + r], dt._h_runs[b:b + r])
