@@ -108,10 +108,11 @@ def parse_args():
     ap.add_argument("--match-runs", type=int, default=1,
                     help="match_prefix follows unary chains a run at a time (0: one hash probe per hop)")
     ap.add_argument("--match-queries", type=int, default=W.MatchSpec.n_queries)
-    ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers", "hf"],
+    ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers", "hf", "react"],
                     help="tot: the headline step; sweep: batched copy/zero sweep; match: match_prefix on the "
                          "stress tree; layers: copies on vLLM's per-layer cache layout; hf: the HF cache's "
-                         "per-layer K/V gather (each prints its own line)")
+                         "per-layer K/V gather; react: the ReAct multi-agent trace at the Llama-3-70B shape, "
+                         "head-sharded under torchrun (each prints its own line)")
     ap.add_argument("--batches", default="1,8,64,512,4096", help="sweep batch sizes")
     ap.add_argument("--rotations", type=int, default=8, help="sweep: distinct pair sets cycled")
     return ap.parse_args()
@@ -987,6 +988,180 @@ def copy_traffic(n_pairs: int):
     return None
 
 
+# ── ReAct multi-agent trace ──────────────────────────────────────────────────
+class _ReActPool:
+    """The call set workloads.react_setup / react_step drive: the pool's own
+    calls plus residual_len(handle)."""
+
+    def __init__(self, pool) -> None:
+        self.pool = pool
+
+    def __getattr__(self, name):
+        return getattr(self.pool, name)
+
+    @staticmethod
+    def residual_len(h) -> int:
+        return len(h.residual_blocks)
+
+
+class _ReActOracle:
+    """The same call set on the oracle (OracleTree over OracleAllocator)."""
+
+    def __init__(self, n_blocks: int, block_size: int, copy_cb) -> None:
+        from oracle import oracle as O
+
+        self.alloc = O.OracleAllocator(n_blocks)
+        self.tree = O.OracleTree(self.alloc, block_size, copy_cb=copy_cb)
+
+    def __getattr__(self, name):
+        return getattr(self.tree, name)
+
+    def allocate_blocks(self, h, n) -> None:
+        for _ in range(n):
+            self.tree.allocate_block(h)
+
+    def maybe_advance_epoch(self) -> None:
+        self.alloc.maybe_advance_epoch()
+
+    @staticmethod
+    def residual_len(h) -> int:
+        return len(h.residual)
+
+
+def react_cpu_baseline(spec, heads: int, max_seconds: float) -> dict:
+    """The oracle playing the same trace on the host (one thread), each CoW
+    copy moving one head slice's bytes between blocks of a 64-block host
+    pool (ids taken modulo 64): steps per second over a bounded sample."""
+    from oracle import oracle as O
+
+    n_, bs, L, _, D, _ = W.LLAMA3_70B_GEOMETRY
+    bpb = L * 2 * heads * bs * D * 2
+    host = np.zeros((64, bpb), np.uint8)
+    host[:] = np.arange(64, dtype=np.uint8)[:, None]
+    copied = [0]
+
+    def copy_cb(src, dst):
+        a, b = src % 64, dst % 64
+        if a != b:
+            O.copy_blocks(host, bpb, np.array([[a, b]], np.int32))
+        copied[0] += 1
+
+    api = _ReActOracle(n_, bs, copy_cb)
+    root, agents = W.react_setup(api, spec)
+    done = 0
+    t0 = time.perf_counter()
+    for actions in W.react_trace(spec):
+        W.react_step(api, root, agents, actions)
+        done += 1
+        if time.perf_counter() - t0 >= max_seconds:
+            break
+    secs = time.perf_counter() - t0
+    return {"value": round(done / secs, 2), "unit": "steps/s", "cores": 1, "kind": "port",
+            "sample": f"{done} of {spec.steps} trace steps ({copied[0]} CoW copies of {bpb} B), {secs:.1f} s"}
+
+
+def react_case(args) -> None:
+    """The ReAct multi-agent trace (a 16,384-token shared prefix, 32 agents,
+    1,000 steps of forks, CoW tail copies, frees, appends and epoch advances)
+    at the Llama-3-70B KV shape (40,000 blocks).  Rank 0 plays each step
+    through the pool's per-call API on a metadata-only pool (the vLLM
+    adapter's pattern: copy_block replaced on the instance to record the
+    step's pairs), packs the pairs into one count + pairs buffer and
+    broadcasts it; every rank copies its KV-head slice of those blocks
+    (akv_copy_blocks_counted reads the count on the device).  One bench step
+    = one trace step, host calls included; warm-up and timed steps are
+    consecutive steps of the trace."""
+    import torch
+
+    from agentkv_b200 import AgentKVPool, PoolConfig
+    from agentkv_b200.sharded import ShardedCopier
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    spec = W.ReActSpec()
+    n_, bs, L, H, D, dt = W.LLAMA3_70B_GEOMETRY
+    # 8 heads do not fit one GPU (200 GB): one GPU holds the 4-head slice of a 2-GPU run
+    heads = H // max(world, 2)
+    slice_bytes = L * 2 * heads * bs * D * 2
+    pool_slice = torch.empty((n_, L, 2, heads, bs, D), dtype=torch.bfloat16, device=dev)
+    copier = ShardedCopier(pool_slice)
+    buf = copier.batch_buffer(spec.agents)  # at most one CoW per agent per step
+    trace = iter(W.react_trace(spec))
+    warmup = max(3, args.warmup)
+    steps = max(1, min(args.steps, spec.steps - warmup))
+    pairs_done = [0]
+    if rank == 0:
+        meta = AgentKVPool(config=PoolConfig(total_blocks=n_, block_size=bs, num_layers=L, num_kv_heads=H,
+                                             head_dim=D, dtype=dt, device="meta"))
+        step_pairs = []
+        orig = meta._allocator.copy_block
+
+        def record(src, dst):
+            step_pairs.append((src.block_id, dst.block_id))
+            orig(src, dst)
+
+        meta._allocator.copy_block = record
+        api = _ReActPool(meta)
+        root, agents = W.react_setup(api, spec)
+
+    def one_step():
+        if rank == 0:
+            step_pairs.clear()
+            W.react_step(api, root, agents, next(trace))
+            copier.pack_batch(step_pairs, buf)
+            pairs_done[0] += len(step_pairs)
+        copier.share_batch(buf)
+        copier.copy_batch(buf)
+
+    sampler = ClockSampler(local)
+    with sampler:
+        for _ in range(warmup):
+            one_step()
+        pairs_done[0] = 0
+        ms, wall = timed(one_step, steps, 0, world)
+    clocks = sampler.summary()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = react_cpu_baseline(spec, heads, args.cpu_seconds)
+    if rank == 0:
+        step_ms = ms / steps
+        print(json.dumps({
+            "case": "react_70b",
+            "metric": "ReAct trace steps/s (32 agents, Llama-3-70B KV)",
+            "value": round(steps / (ms / 1e3), 2),
+            "unit": "steps/s",
+            "n_gpus": world,
+            "steps": steps,
+            "warmup": warmup,
+            "ms_per_step": round(step_ms, 4),
+            "higher_is_better": True,
+            "scaling": "strong" if world > 1 else None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded trace; pool contents uninitialised: the copies move bytes, nothing reads "
+                    "them)",
+            "config": {"workload": "react_70b", "pool_blocks": n_, "heads_per_rank": heads,
+                       "bytes_per_block_per_rank": slice_bytes,
+                       "parallelism": f"kv-head shard x{world}" if world > 1 else
+                                      "single GPU, 4 of 8 KV heads (the full pool is 200 GB)",
+                       "trace_steps": f"{warmup}..{warmup + steps - 1} of {spec.steps}"},
+            "cow_pairs_per_step": round(pairs_done[0] / steps, 2),
+            "copy_gbs_per_rank": round(pairs_done[0] * 2 * slice_bytes / (ms / 1e3) / 1e9, 1),
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "wall_s_timed": round(wall, 3),
+        }), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 # ── main arm ─────────────────────────────────────────────────────────────────
 def main():
     args = parse_args()
@@ -1004,6 +1179,9 @@ def main():
         return
     if args.case == "hf":
         hf_case(args)
+        return
+    if args.case == "react":
+        react_case(args)
         return
     if args.case == "match":
         import torch

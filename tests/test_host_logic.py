@@ -438,3 +438,15 @@ def test_unary_runs_under_the_tree_insert_logic():
         r = int(fresh_runs[a, 3])
         assert r == int(dt._h_runs[b, 3])
         np.testing.assert_array_equal(fresh_runs[a:a + r], dt._h_runs[b:b + r])
+
+
+def test_react_cpu_baseline_plays_the_trace():
+    """bench.react_cpu_baseline drives the oracle through the ReAct trace with
+    the same call set the parity tests use, and reports steps/s over a
+    bounded sample."""
+    import bench
+
+    spec = W.ReActSpec(steps=30)
+    res = bench.react_cpu_baseline(spec, 1, 60.0)
+    assert res["unit"] == "steps/s" and res["value"] > 0 and res["kind"] == "port"
+    assert res["sample"].startswith("30 of 30 trace steps")
