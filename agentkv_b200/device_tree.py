@@ -576,9 +576,15 @@ def pack_queries(queries: Sequence, device: torch.device) -> Tuple[torch.Tensor,
     flat = np.empty(max(int(q_off[-1]), 1), np.int32)
     for i, q in enumerate(queries):
         flat[q_off[i] : q_off[i + 1]] = np.asarray(q, np.int32)
-    tok = torch.from_numpy(flat).pin_memory().to(device, non_blocking=True)
-    off = torch.from_numpy(q_off).pin_memory().to(device, non_blocking=True)
-    return tok, off
+    return _upload(flat, device), _upload(q_off, device)
+
+
+def _upload(a: np.ndarray, device: torch.device) -> torch.Tensor:
+    # through pinned memory (an asynchronous copy) when the target is a GPU
+    t = torch.from_numpy(a)
+    if device.type == "cuda":
+        t = t.pin_memory()
+    return t.to(device, non_blocking=True)
 
 
 def longest_first(q_off, device: torch.device) -> torch.Tensor:
@@ -586,7 +592,7 @@ def longest_first(q_off, device: torch.device) -> torch.Tensor:
     (stable), so the longest walks start first and spread over the SMs."""
     q_off = np.asarray(q_off.cpu() if isinstance(q_off, torch.Tensor) else q_off, np.int64)
     order = np.argsort(-np.diff(q_off), kind="stable").astype(np.int32)
-    return torch.from_numpy(order).pin_memory().to(device, non_blocking=True)
+    return _upload(order, device)
 
 
 def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_compared: bool = False,

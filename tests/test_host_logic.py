@@ -450,3 +450,107 @@ def test_react_cpu_baseline_plays_the_trace():
     res = bench.react_cpu_baseline(spec, 1, 60.0)
     assert res["unit"] == "steps/s" and res["value"] > 0 and res["kind"] == "port"
     assert res["sample"].startswith("30 of 30 trace steps")
+
+
+def _csr_of(shared_nodes) -> dict:
+    """The oracle's CSR arrays of a host tree's nodes (children, edges)."""
+    n = max(shared_nodes) + 1
+    child_ptr = np.zeros(n + 1, np.int64)
+    keys, ids, toks = [], [], []
+    edge_off = np.zeros(n, np.int64)
+    edge_len = np.zeros(n, np.int32)
+    pos = 0
+    for nid in range(n):
+        nd = shared_nodes.get(nid)
+        if nd is not None:
+            for k in sorted(nd.children):
+                keys.append(k)
+                ids.append(nd.children[k])
+            e = np.asarray(nd.edge, np.int32)
+            edge_off[nid], edge_len[nid] = pos, len(e)
+            toks.append(e)
+            pos += len(e)
+        child_ptr[nid + 1] = len(keys)
+    return {"child_ptr": child_ptr, "child_key": np.asarray(keys or [0], np.int32),
+            "child_id": np.asarray(ids or [0], np.int32), "edge_off": edge_off, "edge_len": edge_len,
+            "edge_tokens": np.concatenate(toks) if pos else np.zeros(1, np.int32)}
+
+
+def test_tree_orchestration_with_kernel_model(monkeypatch):
+    """The host side of match_prefix end to end on CPU, the two tree kernels
+    replaced by their CPU model (tests/tree_kernel_model.py): DualRadixTree
+    inserts mirrored into an owner DeviceTree (full and incremental deltas),
+    a replica fed by TreeReplicaSync deltas with the owner's unary-chain runs,
+    and batched lookups under the rebuild policy, with runs and without —
+    all equal to the oracle's C match over the same host tree, comparison
+    counts included."""
+    import torch
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200.allocator import BlockHandle
+    from agentkv_b200.radix_tree import ROOT_NODE_ID, DualRadixTree, SharedNode
+    from agentkv_b200.sharded_tree import TreeReplicaSync
+    from oracle import oracle as O
+    from tree_kernel_model import TreeKernelModel
+
+    model = TreeKernelModel(N.lib)
+    monkeypatch.setattr(N, "lib", model)
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    cpu = torch.device("cpu")
+    spec = W.MatchSpec(n_prefixes=10, prefix_min=64, prefix_max=256, n_sequences=240, total_min=32,
+                       total_max=480, n_queries=96)
+    prefixes = W.match_prefixes(spec)
+    corpus = W.match_sequences(spec, prefixes)
+    tree = object.__new__(DualRadixTree)
+    tree._cfg = PoolConfig(total_blocks=64, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1,
+                           dtype="float16", device="meta")
+    tree._dev_tree = owner = DT.DeviceTree(cpu, node_cap=8, slot_cap=16, token_cap=64)
+    tree._shared_nodes = {ROOT_NODE_ID: SharedNode(ROOT_NODE_ID, -1, owner)}
+    owner.set_node(ROOT_NODE_ID, 0, 0)
+    tree._next_node_id = 1
+    sync = TreeReplicaSync(owner)
+    replica = DT.DeviceTree(cpu)
+    replica.as_replica()
+    queries = W.match_queries(spec, corpus, prefixes, batch=0, n=spec.n_queries)
+    flat, q_off = O.pack_queries([q.tolist() for q in queries])
+    rng = np.random.default_rng(8)
+    checks = 0
+    for i, seq in enumerate(corpus):
+        n = (len(seq) // 16) * 16
+        if rng.random() < 0.2:
+            n = int(rng.integers(0, n // 16 + 1)) * 16
+        if n:
+            tree._insert_shared_locked(ROOT_NODE_ID, np.asarray(seq[:n], np.int32),
+                                       [BlockHandle(b) for b in range(n // 16)])
+        if i % 7 == 6:
+            if i % 2:
+                owner.build_runs()  # else the policy decides whether new runs travel
+            d = sync.share()
+            if d is not None:
+                replica.apply_delta(d)
+                if "run_head" in d:
+                    replica.set_runs(d["run_head"], d["runs"])
+        if i % 21 == 20:
+            want = O.match_prefix_csr(_csr_of(tree._shared_nodes), flat, q_off, 16)
+            want_node = np.where(want[1] > 0, want[0], -1)
+            for t, runs in ((owner, None), (owner, False), (replica, None)):
+                node, mlen, cmp_ = DT.match_batch(t, queries, 16, with_compared=True, runs=runs)
+                np.testing.assert_array_equal(mlen, want[1], err_msg=f"{i} {runs}")
+                np.testing.assert_array_equal(np.where(mlen > 0, node, -1), want_node)
+                np.testing.assert_array_equal(cmp_, want[2])
+            checks += 1
+    assert checks >= 10 and model.run_hops > 1000, (checks, model.run_hops)
+    # the replica's arrays equal the owner's after a final sync
+    owner.build_runs()
+    d = sync.share()
+    if d is not None:
+        replica.apply_delta(d)
+        if "run_head" in d:
+            replica.set_runs(d["run_head"], d["runs"])
+    owner.flush()
+    n = owner.n_tokens
+    assert torch.equal(replica.d_tokens[:n], owner.d_tokens[:n])
+    assert torch.equal(replica.d_slots, owner.d_slots)
+    assert torch.equal(replica.d_off, owner.d_off) and torch.equal(replica.d_len, owner.d_len)
+    assert torch.equal(replica.d_run_head, owner.d_run_head) and torch.equal(replica.d_runs, owner.d_runs)
