@@ -239,3 +239,75 @@ def test_head_slicing_math():
     full = torch.arange(2 * 1 * 2 * 8 * 1 * 1).reshape(2, 1, 2, 8, 1, 1)
     parts = [S.head_slice(full, r, 4) for r in range(4)]
     assert torch.equal(torch.cat(parts, dim=3), full)
+
+
+def _match_split_worker(rank, world, port, q):
+    """Rank 0 owns a tree built by DualRadixTree's inserts; TreeReplicaSync
+    brings rank 1's replica (and the owner's unary-chain runs) up to date
+    between insert rounds; match_split spreads a query batch over the ranks
+    and all-gathers the answers.  The tree kernels run as their CPU model."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+
+        sys.path.insert(0, os.path.dirname(__file__))
+        from agentkv_b200 import _native as N
+        from agentkv_b200 import device_tree as DT
+        from agentkv_b200 import workloads as W
+        from agentkv_b200.allocator import BlockHandle
+        from agentkv_b200.config import PoolConfig
+        from agentkv_b200.radix_tree import ROOT_NODE_ID, DualRadixTree, SharedNode
+        from agentkv_b200.sharded_tree import TreeReplicaSync, match_split
+        from oracle import oracle as O
+        from test_host_logic import _csr_of
+        from tree_kernel_model import TreeKernelModel
+
+        model = TreeKernelModel(N.lib)
+        N.lib = model
+        DT.stream_handle = lambda dev: 0
+        cpu = torch.device("cpu")
+        spec = W.MatchSpec(n_prefixes=8, prefix_min=64, prefix_max=192, n_sequences=160, total_min=32,
+                           total_max=400, n_queries=75)
+        prefixes = W.match_prefixes(spec)
+        corpus = W.match_sequences(spec, prefixes)
+        queries = W.match_queries(spec, corpus, prefixes, batch=0, n=spec.n_queries)
+        if rank == 0:
+            tree = object.__new__(DualRadixTree)
+            tree._cfg = PoolConfig(total_blocks=64, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1,
+                                   dtype="float16", device="meta")
+            tree._dev_tree = dt = DT.DeviceTree(cpu, node_cap=8, slot_cap=16, token_cap=64)
+            tree._shared_nodes = {ROOT_NODE_ID: SharedNode(ROOT_NODE_ID, -1, dt)}
+            dt.set_node(ROOT_NODE_ID, 0, 0)
+            tree._next_node_id = 1
+        else:
+            dt = DT.DeviceTree(cpu)
+        sync = TreeReplicaSync(dt)
+        ok = True
+        for lo in range(0, len(corpus), 40):
+            if rank == 0:
+                for seq in corpus[lo:lo + 40]:
+                    n = (len(seq) // 16) * 16
+                    tree._insert_shared_locked(ROOT_NODE_ID, np.asarray(seq[:n], np.int32),
+                                               [BlockHandle(b) for b in range(n // 16)])
+                dt.build_runs()
+            sync.sync()
+            node, mlen = match_split(sync, queries, 16)
+            if rank == 0:
+                flat, q_off = O.pack_queries([x.tolist() for x in queries])
+                want = O.match_prefix_csr(_csr_of(tree._shared_nodes), flat, q_off, 16)
+                ok &= bool(np.array_equal(mlen, want[1]) and
+                           np.array_equal(np.where(mlen > 0, node, -1), np.where(want[1] > 0, want[0], -1)))
+        hops = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(hops, torch.tensor([model.run_hops], dtype=torch.int64))
+        if rank == 0:
+            q.put((ok, [int(h) for h in hops]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_match_split_over_replicas_gloo():
+    ok, hops = _run(_match_split_worker)
+    assert ok, "match_split over two replicas differs from the oracle's match on the owner's tree"
+    assert min(hops) > 100, hops  # both ranks' lookups followed unary-chain runs
