@@ -398,3 +398,18 @@ def test_stress_shadow_model(seed, n_ops):
     assert sh.violations == []
     np.testing.assert_array_equal(a._ref_counts.cpu().numpy()[: 512], np.zeros(512))
     assert a.free_count == 512, "leak"
+
+
+def test_serving_lifecycle_equals_oracle():
+    """The prefix-cache serving lifecycle a serving engine's radix-cache
+    adapter drives (tests/serving_pattern.py: lookups adopted as handles,
+    appends, page allocations, commits, finishes, aborts, epoch advances)
+    observes the same hits, block ids and counters on the device pool as on
+    the oracle."""
+    from serving_pattern import OracleServeAPI, PoolServeAPI, serve
+
+    pool = AgentKVPool(config=PoolConfig(total_blocks=512, block_size=16, num_layers=1, num_kv_heads=1,
+                                         head_dim=8, dtype="float16", device="cuda"))
+    got = serve(PoolServeAPI(pool))
+    want = serve(OracleServeAPI(512, 16))
+    assert got == want

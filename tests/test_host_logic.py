@@ -554,3 +554,24 @@ def test_tree_orchestration_with_kernel_model(monkeypatch):
     assert torch.equal(replica.d_slots, owner.d_slots)
     assert torch.equal(replica.d_off, owner.d_off) and torch.equal(replica.d_len, owner.d_len)
     assert torch.equal(replica.d_run_head, owner.d_run_head) and torch.equal(replica.d_runs, owner.d_runs)
+
+
+def test_serving_lifecycle_on_the_oracle():
+    """The serving-lifecycle schedule (tests/serving_pattern.py) on the
+    oracle: deterministic, with page hits that return the committed blocks,
+    misses, aborts, finishes and evictions; the allocated count it reads
+    agrees with the oracle's own counter."""
+    from serving_pattern import OracleServeAPI, serve
+
+    a = serve(OracleServeAPI(512, 16))
+    assert a == serve(OracleServeAPI(512, 16))
+    kinds = {o[0] for o in a}
+    assert {"hit", "miss", "abort", "finish", "evict"} <= kinds, kinds
+    assert sum(1 for o in a if o[0] == "hit") >= 10
+    assert all(o[1] >= 0 for o in a if o[0] == "evict")
+    # hits hand back the committed prefix's blocks, one id per whole page
+    assert all(len(o[3]) == o[2] // 16 and o[2] > 0 for o in a if o[0] == "hit")
+    api = OracleServeAPI(512, 16)
+    serve(api)
+    assert api.allocated_blocks == api.alloc.state()["allocated_blocks"]
+    assert a[-1] == ("end", api.free_blocks, api.allocated_blocks)
