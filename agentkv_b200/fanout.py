@@ -61,6 +61,8 @@ class FanoutGraph:
         self.h_roots = torch.empty(int(self.root_lens.sum()), dtype=torch.int32, pin_memory=True)
         self.h_tables = torch.empty(n_child_entries, dtype=torch.int32, pin_memory=True)
         self.h_status = torch.empty(N.STATUS_BYTES // 4, dtype=torch.int32, pin_memory=True)
+        self._h_status_np = self.h_status.numpy()  # read after each replay without a tensor op
+        self._h_roots_np = self.h_roots.numpy()
         self.d_roots = torch.empty(int(self.root_lens.sum()), dtype=torch.int32, device=self.dev)
         # copy errors land in the allocator's status word when both share a device
         self._copy_status = alloc._status if self.pool.device == alloc.device else None
@@ -131,11 +133,11 @@ class FanoutGraph:
         roots = np.asarray(root_tables, np.int32).reshape(-1)
         if roots.size != self.h_roots.numel():
             raise ValueError(f"FanoutGraph.run: expected {self.h_roots.numel()} root ids, got {roots.size}")
-        self.h_roots.numpy()[:] = roots
+        self._h_roots_np[:] = roots
         with torch.cuda.device(self.dev):
             self.graph.replay()
             torch.cuda.current_stream(self.dev).synchronize()
-        if int(self.h_status[0]):
+        if self._h_status_np[0]:
             self.alloc.check()
         out = self.h_tables.numpy()
         return out.copy() if copy else out
