@@ -2,7 +2,8 @@
 
 Public API mirrors the reference package `agentkv`:
   AgentKVPool, DualRadixTree / CoWRadixTree, SlabAllocator, PoolConfig,
-  BlockHandle, NodeHandle; kernels.copy_block / kernels.zero_block are the
+  AgentKVCache (the HuggingFace cache), BlockHandle, NodeHandle;
+  kernels.copy_block / kernels.zero_block are the
   drop-ins for agentkv.core.triton_kernels.  FanoutGraph replays a whole
   Tree-of-Thought fan-out (forks, copy-on-write copies, appends, frees) as
   one CUDA graph.
@@ -32,6 +33,7 @@ _EXPORTS = {
     "ROOT_NODE_ID": "radix_tree",
     "INVALID_NODE_ID": "radix_tree",
     "FanoutGraph": "fanout",
+    "AgentKVCache": "hf_cache",
 }
 
 __all__ = ["__version__", *_EXPORTS]

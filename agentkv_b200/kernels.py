@@ -402,6 +402,13 @@ def is_native_available() -> bool:
     return N.LIB_PATH.exists() and torch.cuda.is_available()
 
 
+def is_triton_available() -> bool:
+    """triton_kernels.is_triton_available (triton_kernels.py:232): whether
+    block moves run as Triton kernels — never here (they run as this
+    library's CUDA kernels; see is_native_available)."""
+    return False
+
+
 def kernel_info() -> dict:
     gpu = torch.cuda.get_device_name(0) if torch.cuda.is_available() else "N/A"
     cap = torch.cuda.get_device_capability(0) if torch.cuda.is_available() else None

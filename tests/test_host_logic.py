@@ -575,3 +575,17 @@ def test_serving_lifecycle_on_the_oracle():
     serve(api)
     assert api.allocated_blocks == api.alloc.state()["allocated_blocks"]
     assert a[-1] == ("end", api.free_blocks, api.allocated_blocks)
+
+
+def test_package_exports_the_reference_names():
+    """The names the reference package exports at its top level
+    (agentkv/__init__.py) and the triton_kernels helpers resolve here."""
+    import agentkv_b200
+    from agentkv_b200 import kernels as K
+
+    for name in ("AgentKVPool", "CoWRadixTree", "DualRadixTree", "SlabAllocator", "PoolConfig",
+                 "AgentKVCache", "__version__"):
+        assert getattr(agentkv_b200, name) is not None, name
+    assert agentkv_b200.CoWRadixTree is agentkv_b200.DualRadixTree
+    assert K.is_triton_available() is False
+    assert callable(K.copy_block) and callable(K.zero_block) and callable(K.kernel_info)
