@@ -525,6 +525,11 @@ int copy_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* pair
     case 7: return copy_bulk_launch_t<16384, 12, 1, OnePool, true>(lay, total, pairs, n, refs, st, s, n_dev);
     case 8: return copy_bulk_launch_t<32768, 6, 1, OnePool, true>(lay, total, pairs, n, refs, st, s, n_dev);
     case 9: return copy_bulk_launch_t<32768, 3, 1>(lay, total, pairs, n, refs, st, s, n_dev);
+    // Oversubscribed grids: 8 CTAs per SM of which 2 fit at a time, so the
+    // block scheduler hands the remaining CTAs to whichever SMs finish first
+    // (balancing SMs that start late or run slower beside other kernels).
+    case 10: return copy_bulk_launch_t<16384, 6, 8>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 11: return copy_bulk_launch_t<32768, 3, 8>(lay, total, pairs, n, refs, st, s, n_dev);
     default: return copy_bulk_launch_t<16384, 12, 1>(lay, total, pairs, n, refs, st, s, n_dev);
   }
 }
@@ -609,7 +614,7 @@ extern "C" int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int3
   AKV_ARG_CHECK(bytes_per_block > 0, "akv_copy_blocks: bytes_per_block=%lld",
                 static_cast<long long>(bytes_per_block));
   AKV_ARG_CHECK(total_blocks > 0, "akv_copy_blocks: total_blocks=%d", total_blocks);
-  AKV_ARG_CHECK(variant >= 0 && variant <= 11, "akv_copy_blocks: unknown variant %d", variant);
+  AKV_ARG_CHECK(variant >= 0 && variant <= 13, "akv_copy_blocks: unknown variant %d", variant);
   char* p = static_cast<char*>(pool);
   cudaStream_t s = akv_stream(stream);
   // Automatic choice: the bulk-async engine whenever the spans are 16-byte

@@ -99,10 +99,12 @@ AKV_API int akv_copy_blocks(void* pool, int64_t bytes_per_block, int32_t total_b
 /* Same, with an explicit kernel choice: 0 = automatic, 1 = 16-byte vector
  * loads/stores, 2 = bulk-async (TMA) copies staged through shared memory
  * (16 KiB chunks x 12 in flight for blocks >= 2 MiB, 32 KiB x 6 below, one
- * CTA per SM); 3-11 = fixed bulk shapes for tuning
+ * CTA per SM); 3-13 = fixed bulk shapes for tuning
  * (32 KiB x 6; 32 KiB x 3 with 2 CTAs per SM; 64 KiB x 3; 16 KiB x 6 with
  * 2 CTAs per SM; 8 KiB x 24; chunk-major order (chunk c of every pair before
- * chunk c + 1) with 32 KiB x 3, 16 KiB x 12, 32 KiB x 6; 32 KiB x 3). */
+ * chunk c + 1) with 32 KiB x 3, 16 KiB x 12, 32 KiB x 6; 32 KiB x 3;
+ * 16 KiB x 6 and 32 KiB x 3 on grids of 8 CTAs per SM, 2 resident at a
+ * time, the rest placed on whichever SM frees up first). */
 AKV_API int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int32_t total_blocks,
                             const int32_t* pairs, int32_t n_pairs,
                             const int32_t* ref_counts, AkvStatus* status,

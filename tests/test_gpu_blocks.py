@@ -37,7 +37,7 @@ def random_pairs(n_blocks, n, seed):
     return np.stack([perm[:n], perm[n:]], 1).copy()
 
 
-@pytest.mark.parametrize("variant", [N.VARIANT_VEC, N.VARIANT_BULK, 3, 4, 5, 6, 7, 8, 9, 10, 11])
+@pytest.mark.parametrize("variant", [N.VARIANT_VEC, N.VARIANT_BULK, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13])
 @pytest.mark.parametrize("n_blocks,bpb", GEOMETRIES)
 def test_copy_blocks_bitexact(n_blocks, bpb, variant):
     host, pool = random_pool(n_blocks, bpb, seed=n_blocks + bpb)
