@@ -108,6 +108,8 @@ def parse_args():
     ap.add_argument("--match-runs", type=int, default=1,
                     help="match_prefix follows unary chains a run at a time (0: one hash probe per hop)")
     ap.add_argument("--match-queries", type=int, default=W.MatchSpec.n_queries)
+    ap.add_argument("--match-chunks", type=int, default=0, choices=[0, 1, 2, 4, 8],
+                    help="match_prefix verify width: 32-token compares per lane per step (0: the default)")
     ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers", "hf", "react"],
                     help="tot: the headline step; sweep: batched copy/zero sweep; match: match_prefix on the "
                          "stress tree; layers: copies on vLLM's per-layer cache layout; hf: the HF cache's "
@@ -674,7 +676,7 @@ def match_cpu_baseline(pool, batches, gpu_results, max_seconds: float) -> dict:
 
 def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
                  n_queries: int = W.MatchSpec.n_queries, rank: int = 0, world: int = 1,
-                 use_runs: bool = True, cpu_seconds: float = 0.0) -> dict:
+                 use_runs: bool = True, cpu_seconds: float = 0.0, chunks: int = 0) -> dict:
     """match_prefix on the stress tree.  With N ranks, rank 0 builds the tree
     through the pool API and broadcasts it (TreeReplicaSync) to every rank's
     replica; each rank then matches its own 4096-query batches (weak
@@ -728,7 +730,7 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
     qtokens = []
     results = []
     for (tok, off), order in zip(packed, orders):
-        tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs)
+        tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks)
         compared.append(int(cmp_.sum()))
         qtokens.append(int(off[-1]))
         results.append((node.cpu().numpy(), mlen.cpu().numpy(), cmp_.cpu().numpy()))
@@ -744,7 +746,7 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
 
     def run():
         for (tok, off), order in zip(packed, orders):
-            tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs)
+            tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks)
 
     ms, _ = timed(run, steps, warmup, world)
     per_batch_ms = ms / (steps * len(packed))
@@ -752,7 +754,7 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
 
     def run_warm():  # one batch again and again: its query tokens stay in L2
         for _ in range(len(packed)):
-            tree.match(tok0, off0, nq, 16, node, mlen, cmp_, order=order0, runs=use_runs)
+            tree.match(tok0, off0, nq, 16, node, mlen, cmp_, order=order0, runs=use_runs, chunks=chunks)
 
     ms_w, _ = timed(run_warm, steps, warmup, world)
     warm_ms = ms_w / (steps * len(packed))
@@ -798,6 +800,7 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         "replica_sync_s": round(sync_s, 2),
         "query_tokens_per_batch": int(statistics.mean(qtokens)),
         "unary_runs": bool(use_runs),
+        "verify_chunks": chunks or 4,
         "roofline": roofline,
         "cpu_baseline": cpu,
     }
@@ -1207,7 +1210,8 @@ def main():
                                                  device_id=torch.device("cuda", local))
         fig = match_figure(args.steps, args.warmup, args.match_seqs, args.match_queries, rank, world,
                            use_runs=bool(args.match_runs),
-                           cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds)
+                           cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds,
+                           chunks=args.match_chunks)
         if rank == 0:
             print(json.dumps(fig), flush=True)
         if world > 1:
