@@ -551,6 +551,25 @@ def cpu_tot_run(trees: int, steps: int, warmup: int, threads: int, max_seconds: 
     return gbs, len(times), sum(times), bpb, threads
 
 
+def host_cpu() -> dict:
+    """The host's CPU model string and logical CPU count, reported beside
+    every CPU baseline."""
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    if not model:
+        import platform
+
+        model = platform.processor() or platform.machine()
+    return {"cpu_model": model, "logical_cpus": os.cpu_count()}
+
+
 def cpu_thread_candidates():
     n = os.cpu_count() or 1
     return sorted({t for t in (1, 4, 8, 16, 32, 64, n) if t <= n})
@@ -570,7 +589,7 @@ def reference_arm(args, rank, world):
         "config": {"workload": "tot_8b_fanout", "pool_blocks_per_tree": W.LLAMA3_8B_GEOMETRY[0],
                    "bytes_per_block": bpb, "trees_per_step": world},
         "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "host": host_cpu()},
         "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -671,7 +690,7 @@ def match_cpu_baseline(pool, batches, gpu_results, max_seconds: float) -> dict:
     nq = len(batches[0])
     return {"value": round(done * nq / secs, 1), "unit": "queries/s", "cores": 1, "kind": "port",
             "sample": f"{done} batches of {nq} queries on the same tree, {secs:.1f} s, one host thread",
-            "same_answers_as_gpu": same}
+            "same_answers_as_gpu": same, "host": host_cpu()}
 
 
 def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
@@ -1073,7 +1092,8 @@ def react_cpu_baseline(spec, heads: int, max_seconds: float) -> dict:
             break
     secs = time.perf_counter() - t0
     return {"value": round(done / secs, 2), "unit": "steps/s", "cores": 1, "kind": "port",
-            "sample": f"{done} of {spec.steps} trace steps ({copied[0]} CoW copies of {bpb} B), {secs:.1f} s"}
+            "sample": f"{done} of {spec.steps} trace steps ({copied[0]} CoW copies of {bpb} B), {secs:.1f} s",
+            "host": host_cpu()}
 
 
 def react_case(args) -> None:
@@ -1362,7 +1382,7 @@ def main():
         gbs, steps, secs, bpb, threads = cpu_tot_run(1, 1000, 1, 0, max_seconds=args.cpu_seconds)
         cpu = {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"{steps} Tree-of-Thought steps ({steps * 584} CoW copies of {bpb} B) on a "
-                         f"4096-block host pool, {secs:.1f} s"}
+                         f"4096-block host pool, {secs:.1f} s", "host": host_cpu()}
 
     match = (match_figure(max(5, args.steps), args.warmup, args.match_seqs, args.match_queries)
              if (args.match and rank == 0) else None)
