@@ -688,9 +688,22 @@ def match_cpu_baseline(pool, batches, gpu_results, max_seconds: float) -> dict:
         if secs >= max_seconds:
             break
     nq = len(batches[0])
+    # the reference's own loop, in Python, on the first queries of batch 0
+    py_tree = O.csr_children(csr)
+    py_q = [q.tolist() for q in batches[0]]
+    py_done = 0
+    t1 = time.perf_counter()
+    while py_done < len(py_q) and time.perf_counter() - t1 < max_seconds / 2:
+        O.match_prefix_py(py_tree, py_q[py_done:py_done + 16], 16)
+        py_done = min(py_done + 16, len(py_q))
+    py_secs = time.perf_counter() - t1
     return {"value": round(done * nq / secs, 1), "unit": "queries/s", "cores": 1, "kind": "port",
-            "sample": f"{done} batches of {nq} queries on the same tree, {secs:.1f} s, one host thread",
-            "same_answers_as_gpu": same, "host": host_cpu()}
+            "sample": f"{done} batches of {nq} queries on the same tree, {secs:.1f} s, one host thread "
+                      f"(the oracle's C restatement)",
+            "same_answers_as_gpu": same, "host": host_cpu(),
+            "python_loop": {"value": round(py_done / py_secs, 1), "unit": "queries/s",
+                            "sample": f"{py_done} queries of batch 0, {py_secs:.1f} s: the reference's loop "
+                                      f"in pure Python, one thread"}}
 
 
 def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,

@@ -560,6 +560,50 @@ def match_prefix_csr(csr: dict, tokens: np.ndarray, q_off: np.ndarray, block_siz
     return node[:nq], mlen[:nq], cmp_[:nq]
 
 
+def csr_children(csr: dict) -> list:
+    """Per node, its children as a dict first token -> child id, and its edge
+    as a Python list: the shapes the reference's loop walks
+    (radix_tree.py:82-103)."""
+    ptr, keys, ids = csr["child_ptr"], csr["child_key"], csr["child_id"]
+    kids = [dict(zip(keys[ptr[u]:ptr[u + 1]].tolist(), ids[ptr[u]:ptr[u + 1]].tolist()))
+            for u in range(len(ptr) - 1)]
+    off, ln, tok = csr["edge_off"], csr["edge_len"], csr["edge_tokens"]
+    edges = [tok[off[u]:off[u] + ln[u]].tolist() for u in range(len(ln))]
+    return [kids, edges]
+
+
+def match_prefix_py(tree: list, queries, block_size: int):
+    """(node, len, compared) per query by the reference's own loop in pure
+    Python (radix_tree.py:513-570: child by first token, compare the edge token
+    by token, stop at a mismatch or a partial edge, floor to the block size),
+    over csr_children's tree — what the reference's CPU path costs per query."""
+    kids, edges = tree
+    out = []
+    for q in queries:
+        n = len(q)
+        cur, matched, compared = 0, 0, 0
+        while matched < n:
+            child = kids[cur].get(q[matched])
+            if child is None:
+                break
+            edge = edges[child]
+            em = 0
+            for i, et in enumerate(edge):
+                if matched + i >= n:
+                    break
+                compared += 1
+                if q[matched + i] != et:
+                    break
+                em += 1
+            if em == 0 or em < len(edge):
+                break
+            matched += em
+            cur = child
+        m = (matched // block_size) * block_size
+        out.append((cur if m else INVALID_NODE_ID, m, compared))
+    return out
+
+
 # ── HuggingFace cache (agentkv/hf_cache.py) ──────────────────────────────────
 class OracleKVPool:
     """A pool's calls the HF cache uses — OracleTree over OracleAllocator plus

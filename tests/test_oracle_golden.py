@@ -332,3 +332,8 @@ def test_oracle_match_small(golden_dir):
     np.testing.assert_array_equal(mlen, g["len"])
     py_cmp = np.asarray([tree.match(q.tolist())[2] for q in queries])
     np.testing.assert_array_equal(cmp_, py_cmp)
+    # the pure-Python loop over the flattened tree (the CPU baseline's second figure)
+    loop = np.asarray(O.match_prefix_py(O.csr_children(O.tree_csr(tree)), [q.tolist() for q in queries], 16))
+    np.testing.assert_array_equal(loop[:, 0], g["node"])
+    np.testing.assert_array_equal(loop[:, 1], g["len"])
+    np.testing.assert_array_equal(loop[:, 2], cmp_)
