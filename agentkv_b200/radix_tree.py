@@ -121,7 +121,7 @@ class DualRadixTree:
         dev = allocator.device
         self._q_off = torch.zeros(2, dtype=torch.int64, device=dev)
         self._q_out = torch.zeros(4, dtype=torch.int64, device=dev)
-        self._h_q = torch.zeros(4, dtype=torch.int64, pin_memory=True)
+        self._h_q = torch.zeros(4, dtype=torch.int64, pin_memory=dev.type == "cuda")
 
     # ── create / fork / allocate ──────────────────────────────────────────────
     def create_root(self, tokens: List[int]) -> NodeHandle:

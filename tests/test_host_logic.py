@@ -1,6 +1,12 @@
 """Host-side logic that needs no GPU: config validation (same rules and
-messages as the reference), the device-tree mirror's hash table, pair
-validation, and the seeded workload generators."""
+messages as the reference), the device-tree mirror's hash table and
+unary-chain runs, pair validation, the seeded workload generators, the
+bench's byte counts and CPU baselines, and — with the tree kernels replaced
+by their CPU model (tree_kernel_model.py) and the allocator answered by the
+oracle (oracle_slab.py) — the package's tree logic replaying the
+reference's recorded traces and the match path's host orchestration."""
+
+import json
 
 import numpy as np
 import pytest
@@ -589,3 +595,97 @@ def test_package_exports_the_reference_names():
     assert agentkv_b200.CoWRadixTree is agentkv_b200.DualRadixTree
     assert K.is_triton_available() is False
     assert callable(K.copy_block) and callable(K.zero_block) and callable(K.kernel_info)
+
+
+@pytest.mark.parametrize("seed", [1, 2, 3])
+def test_tree_host_logic_replays_reference_traces(golden_dir, seed, monkeypatch):
+    """The package's host-side tree logic (agentkv_b200/radix_tree.py:
+    handles, shared nodes, inserts with their split / overwrite quirks,
+    prunes, CoW dispatch, error checks) replays the reference's recorded
+    tree traces on CPU — the allocator answered by the oracle
+    (tests/oracle_slab.py), the tree kernels by their CPU model — with every
+    result, error, block table, tree node, refcount, free-list entry and
+    block digest as recorded."""
+    import hashlib
+
+    import torch
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200.allocator import BlockHandle
+    from agentkv_b200.radix_tree import DualRadixTree
+    from oracle_slab import OracleSlab
+    from tree_kernel_model import TreeKernelModel
+
+    monkeypatch.setattr(N, "lib", TreeKernelModel(N.lib))
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    g = json.loads((golden_dir / f"tree_trace_{seed}.json").read_text())
+    n, bs = g["n_blocks"], g["block_size"]
+    cfg = PoolConfig(total_blocks=n, block_size=bs, num_layers=1, num_kv_heads=2, head_dim=4,
+                     dtype="float16", device="meta", epoch_interval=7)
+    torch.manual_seed(seed)
+    kv = torch.randn((n, 1, 2, 2, bs, 4), dtype=torch.float32).half()
+    slab = OracleSlab(kv, 7)
+    tree = DualRadixTree(slab, cfg)
+    T_CREATE, T_FORK, T_ALLOC, T_COW, T_APPEND, T_COMMIT, T_FREE, T_MATCH, T_ADVANCE, T_ZERO = range(10)
+    live = {}
+    states = {step: st for step, st in g["states"]}
+    for step, rec in enumerate(g["ops"]):
+        op = rec["op"]
+        err = None
+        try:
+            if op == T_CREATE:
+                h = tree.create_root(rec["tokens"])
+                live[h.handle_id] = h
+                assert [h.handle_id, h.shared_node_id, h.shared_match_len] == rec["out"]
+            elif op == T_FORK:
+                c = tree.fork(live[rec["h"]])
+                live[c.handle_id] = c
+                assert c.handle_id == rec["out"]
+            elif op == T_ALLOC:
+                h = live[rec["h"]]
+                tree.allocate_block(h)
+                assert h.residual_blocks[-1].block_id == rec["out"]
+            elif op == T_COW:
+                h = live[rec["h"]]
+                tree.ensure_mutable_block(h, rec["idx"])
+                assert h.residual_blocks[rec["idx"]].block_id == rec["out"]
+            elif op == T_APPEND:
+                tree.append_tokens(live[rec["h"]], rec["tokens"])
+            elif op == T_COMMIT:
+                h = live[rec["h"]]
+                tree.commit_prefix(h, rec["length"])
+                assert [h.shared_node_id, h.shared_match_len] == rec["out"]
+            elif op == T_FREE:
+                tree.free(live.pop(rec["h"]))
+            elif op == T_MATCH:
+                mh, mlen = tree.match_prefix(rec["tokens"])
+                got = [-1 if mh is None else mh.handle_id, mlen, -1 if mh is None else mh.shared_node_id]
+                assert got == rec["out"]
+                if mh is not None:
+                    live[mh.handle_id] = mh
+            elif op == T_ADVANCE:
+                slab.maybe_advance_epoch()
+            elif op == T_ZERO:
+                slab.zero_block(BlockHandle(rec["block"]))
+        except (ValueError, MemoryError) as e:
+            err = e
+        assert (err is not None) == ("error" in rec), f"step {step}: {rec} -> {err!r}"
+        if step in states:
+            st = states[step]
+            assert {str(k): tree.get_block_ids(h) for k, h in sorted(live.items())} == st["tables"]
+            assert {str(k): [h.shared_node_id, h.shared_match_len] for k, h in sorted(live.items())} == st["shared"]
+            nodes = {str(nid): {"parent": nd.parent_id, "edge": nd.edge_tokens,
+                                "blocks": [b.block_id for b in nd.blocks],
+                                "children": sorted([int(k), int(v)] for k, v in nd.children.items()),
+                                "ref": nd.ref_count}
+                     for nid, nd in sorted(tree._shared_nodes.items())}
+            assert nodes == st["nodes"]
+            ost = slab.o.state()
+            assert ost["ref_counts"].tolist() == st["ref"]
+            assert ost["free_list"].tolist() == st["free"]
+            for k in ("active_handles", "shared_nodes", "shared_blocks"):
+                if k in st["stats"]:
+                    assert tree.stats()[k] == st["stats"][k], k
+    digests = [hashlib.sha256(kv[i].numpy().tobytes()).hexdigest() for i in range(n)]
+    assert digests == g["block_sha256"]
