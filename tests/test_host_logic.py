@@ -689,3 +689,31 @@ def test_tree_host_logic_replays_reference_traces(golden_dir, seed, monkeypatch)
                     assert tree.stats()[k] == st["stats"][k], k
     digests = [hashlib.sha256(kv[i].numpy().tobytes()).hexdigest() for i in range(n)]
     assert digests == g["block_sha256"]
+
+
+@pytest.mark.parametrize("seed", [1, 2, 7, 13, 17, 42, 137, 999])
+def test_tree_host_logic_replays_reference_stress_runner(golden_dir, seed, monkeypatch):
+    """The reference stress runner's recorded calls (tests/stress_replay.py)
+    through the package's tree logic on CPU, the allocator answered by the
+    oracle and the tree kernels by their CPU model: every handle id, block
+    id and exhaustion as recorded, and the recorded end state."""
+    import torch
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200.radix_tree import DualRadixTree
+    from oracle_slab import OracleSlab
+    from stress_replay import replay
+    from tree_kernel_model import TreeKernelModel
+
+    monkeypatch.setattr(N, "lib", TreeKernelModel(N.lib))
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    g = np.load(golden_dir / f"stress_{seed}.npz")
+    cfg = PoolConfig(total_blocks=512, block_size=4, num_layers=2, num_kv_heads=2, head_dim=8, dtype="float16",
+                     device="meta")
+    slab = OracleSlab(torch.zeros((512, 2, 2, 2, 4, 8), dtype=torch.float16), cfg.epoch_interval)
+    tree = DualRadixTree(slab, cfg)
+    replay(g, tree, slab.maybe_advance_epoch, lambda e: isinstance(e, MemoryError) and "exhausted" in str(e))
+    st = slab.o.state()
+    np.testing.assert_array_equal(st["ref_counts"], g["ref"])
+    np.testing.assert_array_equal(st["free_list"], g["free"])
