@@ -717,3 +717,65 @@ def test_tree_host_logic_replays_reference_stress_runner(golden_dir, seed, monke
     st = slab.o.state()
     np.testing.assert_array_equal(st["ref_counts"], g["ref"])
     np.testing.assert_array_equal(st["free_list"], g["free"])
+
+
+def test_hf_cache_host_logic_replays_reference_session(golden_dir, monkeypatch):
+    """The package's HuggingFace cache logic (agentkv_b200/hf_cache.py: block
+    allocation on layer 0, copy-on-write checks in the reference's order,
+    slot arithmetic, truncation) replays the reference's recorded session on
+    CPU — the pool's allocator answered by the oracle, the tree kernels by
+    their CPU model, and the KV scatter / gather by their contract in torch
+    indexing — with every K/V output, block table, sequence length and pool
+    byte as recorded."""
+    import torch
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200 import kernels as K
+    from agentkv_b200.hf_cache import AgentKVCache
+    from agentkv_b200.pool import AgentKVPool
+    from agentkv_b200.radix_tree import DualRadixTree
+    from oracle_slab import OracleSlab
+    from tree_kernel_model import TreeKernelModel
+
+    def kv_scatter(kv, slots, layer, k, v, status=None):
+        bs = kv.shape[4]
+        for i, slot in enumerate(slots.tolist()):
+            kv[slot // bs, layer, 0, :, slot % bs] = k[0, :, i].to(kv.dtype)
+            kv[slot // bs, layer, 1, :, slot % bs] = v[0, :, i].to(kv.dtype)
+
+    def kv_gather(kv, table, layer, n_tokens, status=None):
+        x = kv[table.long(), layer]  # [blocks, 2, H, bs, D]
+        nb, _, h, bs, d = x.shape
+        k = x[:, 0].permute(1, 0, 2, 3).reshape(1, h, nb * bs, d)[:, :, :n_tokens]
+        v = x[:, 1].permute(1, 0, 2, 3).reshape(1, h, nb * bs, d)[:, :, :n_tokens]
+        return k.contiguous(), v.contiguous()
+
+    monkeypatch.setattr(N, "lib", TreeKernelModel(N.lib))
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    monkeypatch.setattr(K, "kv_scatter", kv_scatter)
+    monkeypatch.setattr(K, "kv_gather", kv_gather)
+    g = np.load(golden_dir / "hf_session.npz")
+    spec = W.HFSpec(**json.loads(str(g["spec"])))
+    cfg = PoolConfig(total_blocks=spec.total_blocks, block_size=spec.block_size, num_layers=spec.num_layers,
+                     num_kv_heads=spec.num_kv_heads, head_dim=spec.head_dim, dtype=spec.dtype, device="meta")
+    kv = torch.zeros((spec.total_blocks, spec.num_layers, 2, spec.num_kv_heads, spec.block_size, spec.head_dim),
+                     dtype=getattr(torch, spec.dtype))
+    pool = object.__new__(AgentKVPool)
+    pool._cfg = cfg
+    pool._allocator = OracleSlab(kv, cfg.epoch_interval)
+    pool._allocator._status = torch.zeros(8, dtype=torch.int32)
+    pool._tree = DualRadixTree(pool._allocator, cfg)
+    outs, keys = [], []
+
+    def on_output(e, layer, ok, ov):
+        keys.append((e, layer, ok.shape[2]))
+        outs.append(np.concatenate([ok.numpy().reshape(-1), ov.numpy().reshape(-1)]))
+
+    caches = W.hf_run(spec, pool, AgentKVCache, torch.from_numpy, on_output)
+    np.testing.assert_array_equal(np.asarray(keys), g["out_keys"])
+    assert np.concatenate(outs).tobytes() == g["outs"].tobytes()
+    tables = np.concatenate([np.asarray(pool.get_block_ids(c.handle), np.int32) for c in caches])
+    np.testing.assert_array_equal(tables, g["tables"])
+    assert [c.get_seq_length() for c in caches] == g["seen"].tolist()
+    assert kv.numpy().tobytes() == g["pool"].tobytes()
