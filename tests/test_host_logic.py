@@ -779,3 +779,50 @@ def test_hf_cache_host_logic_replays_reference_session(golden_dir, monkeypatch):
     np.testing.assert_array_equal(tables, g["tables"])
     assert [c.get_seq_length() for c in caches] == g["seen"].tolist()
     assert kv.numpy().tobytes() == g["pool"].tobytes()
+
+
+def test_react_trace_host_logic_replays_reference(golden_dir, monkeypatch):
+    """The ReAct trace (70B geometry, 40,000 blocks, 1,000 steps) through the
+    package's pool and tree logic on CPU with the copy_block hook of the
+    vLLM adapter: every step's recorded CoW pairs, and at the checkpoints the
+    agents' tables, refcounts and free list, as the reference recorded them
+    (allocator answered by the oracle, tree kernels by their CPU model)."""
+    import torch
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200.pool import AgentKVPool
+    from agentkv_b200.radix_tree import DualRadixTree
+    from oracle_slab import OracleSlab
+    from react_apis import PoolReActAPI
+    from tree_kernel_model import TreeKernelModel
+
+    monkeypatch.setattr(N, "lib", TreeKernelModel(N.lib))
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    g = np.load(golden_dir / "react_70b.npz")
+    spec = W.ReActSpec(**json.loads(str(g["spec"])))
+    n_, bs, L, H, D, dt = W.LLAMA3_70B_GEOMETRY
+    cfg = PoolConfig(total_blocks=n_, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D, dtype=dt,
+                     device="meta")
+    slab = OracleSlab(torch.zeros((n_, 1), dtype=torch.uint8), cfg.epoch_interval)
+    pairs = []
+    slab.copy_block = lambda src, dst: pairs.append((src.block_id, dst.block_id))
+    pool = object.__new__(AgentKVPool)
+    pool._cfg, pool._allocator = cfg, slab
+    pool._tree = DualRadixTree(slab, cfg)
+    api = PoolReActAPI(pool)
+    root, agents = W.react_setup(api, spec)
+    np.testing.assert_array_equal(np.asarray(pool.get_block_ids(root), np.int32), g["root_table"])
+    so = g["step_off"]
+    for i, actions in enumerate(W.react_trace(spec)):
+        pairs.clear()
+        W.react_step(api, root, agents, actions)
+        np.testing.assert_array_equal(np.asarray(pairs, np.int32).reshape(-1, 2), g["pairs"][so[i]:so[i + 1]],
+                                      err_msg=f"step {i}")
+        k = f"s{i + 1}"
+        if k + "_ref" in g.files:
+            tables = np.concatenate([np.asarray(pool.get_block_ids(h), np.int32) for h in agents])
+            np.testing.assert_array_equal(tables, g[k + "_tables"], err_msg=k)
+            st = slab.o.state()
+            np.testing.assert_array_equal(st["ref_counts"], g[k + "_ref"])
+            np.testing.assert_array_equal(st["free_list"], g[k + "_free"])
