@@ -826,3 +826,98 @@ def test_react_trace_host_logic_replays_reference(golden_dir, monkeypatch):
             st = slab.o.state()
             np.testing.assert_array_equal(st["ref_counts"], g[k + "_ref"])
             np.testing.assert_array_equal(st["free_list"], g[k + "_free"])
+
+
+def _cpu_pool(cfg, kv, monkeypatch):
+    """An AgentKVPool whose allocator is the oracle (tests/oracle_slab.py)
+    and whose tree kernels run as their CPU model, over the CPU tensor kv."""
+    import torch  # noqa: F401
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200.pool import AgentKVPool
+    from agentkv_b200.radix_tree import DualRadixTree
+    from oracle_slab import OracleSlab
+    from tree_kernel_model import TreeKernelModel
+
+    if not isinstance(N.lib, TreeKernelModel):
+        monkeypatch.setattr(N, "lib", TreeKernelModel(N.lib))
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    pool = object.__new__(AgentKVPool)
+    pool._cfg = cfg
+    pool._allocator = OracleSlab(kv, cfg.epoch_interval)
+    pool._tree = DualRadixTree(pool._allocator, cfg)
+    return pool
+
+
+def test_quickstart_host_logic_replays_reference(golden_dir, monkeypatch):
+    """The quickstart workload through the package's pool logic on CPU:
+    children's tables, the root's, match results, refcounts, free list and
+    every block's bytes as the reference recorded them."""
+    import hashlib
+
+    import torch
+
+    g = json.loads((golden_dir / "quickstart.json").read_text())
+    n_, bs, L, H, D, dt = W.QUICKSTART_GEOMETRY
+    cfg = PoolConfig(total_blocks=n_, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D, dtype=dt,
+                     device="meta")
+    torch.manual_seed(0)
+    kv = torch.randn((n_, L, 2, H, bs, D), dtype=torch.float16)
+    pool = _cpu_pool(cfg, kv, monkeypatch)
+    root = pool.create_root(list(range(32)))
+    pool.allocate_block(root)
+    kids = [pool.fork(root) for _ in range(3)]
+    for c in kids:
+        pool.allocate_block(c)
+    for c in kids:
+        pool.ensure_mutable_block(c, 0)
+    pool.commit_prefix(root, 16)
+    matches = []
+    for q in g["queries"]:
+        mh, mlen = pool._tree.match_prefix(q)
+        matches.append([-1 if mh is None else mh.shared_node_id, mlen])
+    assert [pool.get_block_ids(c) for c in kids] == g["children"]
+    assert pool.get_block_ids(root) == g["root"]
+    assert matches == g["matches"]
+    st = pool._allocator.o.state()
+    assert st["ref_counts"].tolist() == g["ref"]
+    assert st["free_list"].tolist() == g["free"]
+    assert [hashlib.sha256(kv[i].numpy().tobytes()).hexdigest() for i in range(n_)] == g["block_sha256"]
+
+
+def test_tot_batched_host_logic_replays_reference(golden_dir, monkeypatch):
+    """The Tree-of-Thought fan-out on the 60,000-block pool through the
+    package's batched pool calls (fork_many, ensure_mutable_batch,
+    allocate_blocks, free_many) on CPU: child tables, refcounts and free
+    lists after the fan-out and after the frees as the reference recorded
+    them."""
+    import torch
+
+    g = np.load(golden_dir / "tot_8b.npz")
+    spec = W.ToTSpec()
+    n_, bs, L, H, D, dt = W.LLAMA3_8B_GEOMETRY
+    cfg = PoolConfig(total_blocks=n_, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D, dtype=dt,
+                     device="meta")
+    pool = _cpu_pool(cfg, torch.zeros((n_, 1), dtype=torch.uint8), monkeypatch)
+    root = pool.create_root(W.tot_root_tokens(spec))
+    pool.allocate_blocks(root, spec.root_tokens // 16)
+    level, kids = [root], []
+    for lvl in range(spec.levels):
+        nxt = []
+        for parent in level:
+            nxt.extend(pool.fork_many(parent, spec.fanout))
+        for c in nxt:
+            pool.ensure_mutable_batch([(c, len(c.residual_blocks) - 1)])
+            pool.allocate_blocks(c, spec.appended_blocks)
+        kids.extend(nxt)
+        level = nxt
+    tables = np.concatenate([np.asarray(pool.get_block_ids(c), np.int32) for c in kids])
+    np.testing.assert_array_equal(tables, g["tables"])
+    st = pool._allocator.o.state()
+    np.testing.assert_array_equal(st["ref_counts"], g["ref_fanout"])
+    np.testing.assert_array_equal(st["free_list"], g["free_fanout"])
+    pool.free_many(kids)
+    st = pool._allocator.o.state()
+    np.testing.assert_array_equal(st["ref_counts"], g["ref_freed"])
+    np.testing.assert_array_equal(st["free_list"], g["free_freed"])
