@@ -92,6 +92,15 @@ class OracleSlab:
     def maybe_advance_epoch(self) -> None:
         self.o.maybe_advance_epoch()
 
+    @property
+    def free_count(self) -> int:
+        return self.o.free_count
+
+    @property
+    def allocated_count(self) -> int:
+        st = self.o.state()
+        return self.n - len(st["free_list"]) - len(st["pending"]) - len(st["deferred"])
+
     def zero_block(self, bh: BlockHandle) -> None:
         b = self._valid(bh)
         if self.o.ref_count(b) != 1:

@@ -921,3 +921,17 @@ def test_tot_batched_host_logic_replays_reference(golden_dir, monkeypatch):
     st = pool._allocator.o.state()
     np.testing.assert_array_equal(st["ref_counts"], g["ref_freed"])
     np.testing.assert_array_equal(st["free_list"], g["free_freed"])
+
+
+def test_serving_lifecycle_host_logic_equals_oracle(monkeypatch):
+    """The serving-lifecycle schedule through the package's pool logic on CPU
+    (oracle allocator, tree kernel model) observes what the oracle's own
+    tree observes: hits, block ids, finishes, aborts, counters."""
+    import torch
+
+    from serving_pattern import OracleServeAPI, PoolServeAPI, serve
+
+    cfg = PoolConfig(total_blocks=512, block_size=16, num_layers=1, num_kv_heads=1, head_dim=8,
+                     dtype="float16", device="meta")
+    pool = _cpu_pool(cfg, torch.zeros((512, 1), dtype=torch.uint8), monkeypatch)
+    assert serve(PoolServeAPI(pool)) == serve(OracleServeAPI(512, 16))
