@@ -378,6 +378,7 @@ int akv_tree_prepare() {
   AKV_LOAD(k_match<2>);
   AKV_LOAD(k_match<4>);
   AKV_LOAD(k_match<8>);
+  AKV_LOAD(k_match<16>);
   AKV_LOAD(k_tree_apply);
 #undef AKV_LOAD
   return AKV_OK;
@@ -432,8 +433,8 @@ extern "C" int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* 
   if (nq == 0) return AKV_OK;
   AKV_ARG_CHECK(tokens != nullptr && q_off != nullptr && out_node != nullptr && out_len != nullptr,
                 "akv_match_prefix: NULL query or output array");
-  AKV_ARG_CHECK(chunks == 0 || chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8,
-                "akv_match_prefix: chunks=%d not in {0,1,2,4,8}", chunks);
+  AKV_ARG_CHECK(chunks == 0 || chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8 || chunks == 16,
+                "akv_match_prefix: chunks=%d not in {0,1,2,4,8,16}", chunks);
   if (chunks == 0) chunks = 4;
   const int grid = akv_ceil_div(nq, kMatchWarpsPerCta);
   cudaStream_t s = akv_stream(stream);
@@ -453,6 +454,10 @@ extern "C" int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* 
     case 2:
       k_match<2><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
                                                           out_len, out_compared, order, status);
+      break;
+    case 16:
+      k_match<16><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
+                                                           out_len, out_compared, order, status);
       break;
     default:
       k_match<4><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,

@@ -108,7 +108,7 @@ def parse_args():
     ap.add_argument("--match-runs", type=int, default=1,
                     help="match_prefix follows unary chains a run at a time (0: one hash probe per hop)")
     ap.add_argument("--match-queries", type=int, default=W.MatchSpec.n_queries)
-    ap.add_argument("--match-chunks", type=int, default=0, choices=[0, 1, 2, 4, 8],
+    ap.add_argument("--match-chunks", type=int, default=0, choices=[0, 1, 2, 4, 8, 16],
                     help="match_prefix verify width: 32-token compares per lane per step (0: the default)")
     ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers", "hf", "react"],
                     help="tot: the headline step; sweep: batched copy/zero sweep; match: match_prefix on the "

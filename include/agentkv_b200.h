@@ -420,8 +420,8 @@ AKV_API int akv_match_prefix(const AkvTreeView* tree, const int32_t* tokens, con
 
 /* Same, with an optional processing order (`order[nq]`, a permutation of
  * the query indices; launching the longest queries first balances the SMs)
- * and the number of 32-token chunks a warp compares per step (1, 2, 4 or 8;
- * 0 = default) for tuning.  Outputs stay indexed by query. */
+ * and the number of 32-token chunks a warp compares per step (1, 2, 4, 8 or
+ * 16; 0 = default) for tuning.  Outputs stay indexed by query. */
 AKV_API int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* tokens,
                                      const int64_t* q_off, int32_t nq, int32_t block_size,
                                      int32_t* out_node, int32_t* out_len, int64_t* out_compared,
