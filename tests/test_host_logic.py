@@ -935,3 +935,36 @@ def test_serving_lifecycle_host_logic_equals_oracle(monkeypatch):
                      dtype="float16", device="meta")
     pool = _cpu_pool(cfg, torch.zeros((512, 1), dtype=torch.uint8), monkeypatch)
     assert serve(PoolServeAPI(pool)) == serve(OracleServeAPI(512, 16))
+
+
+def test_allocator_error_mapping():
+    """SlabAllocator turns the device status codes into the reference's
+    exception types with the message parts its tests match
+    (tests/test_slab_allocator.py: "exhausted", "not allocated",
+    "double-free", "ref_count=1", "exclusively owned", out-of-range ids),
+    and validates handles like slab_allocator.py:_validate_handle."""
+    from agentkv_b200 import _native as N
+    from agentkv_b200.allocator import INVALID_BLOCK, BlockHandle, SlabAllocator
+
+    a = object.__new__(SlabAllocator)
+    a._cfg = PoolConfig(total_blocks=8, block_size=4, num_layers=1, num_kv_heads=1, head_dim=4,
+                        dtype="float16", device="meta")
+    cases = [
+        (N.AKV_ERR_EXHAUSTED, "alloc", MemoryError, "exhausted"),
+        (N.AKV_ERR_NOT_ALLOCATED, "inc_ref", ValueError, "not allocated"),
+        (N.AKV_ERR_DOUBLE_FREE, "dec_ref", ValueError, "double-free"),
+        (N.AKV_ERR_NOT_EXCLUSIVE, "copy_block", ValueError, "ref_count=1"),
+        (N.AKV_ERR_NOT_EXCLUSIVE, "zero_block", ValueError, "exclusively owned"),
+        (N.AKV_ERR_OUT_OF_RANGE, "copy_block", ValueError, "out of range"),
+    ]
+    for code, op, typ, part in cases:
+        e = a._exception(code, 3, 0, op)
+        assert type(e) is typ and part in str(e), (code, op, e)
+    assert isinstance(a._exception(N.AKV_ERR_TIMEOUT, 0, 0, "copy"), RuntimeError)
+    with pytest.raises(TypeError):
+        a._validate_handle(3)
+    with pytest.raises(ValueError, match="invalid"):
+        a._validate_handle(BlockHandle(INVALID_BLOCK))
+    with pytest.raises(ValueError, match="out of range"):
+        a._validate_handle(BlockHandle(8))
+    a._validate_handle(BlockHandle(7))
