@@ -1,0 +1,377 @@
+"""The package's host-side logic replaying the reference's recorded runs on
+CPU: the tree logic (agentkv_b200/radix_tree.py), the pool facade and the
+HuggingFace cache, with the allocator answered by the oracle
+(oracle_slab.py), the tree kernels by their CPU model
+(tree_kernel_model.py) and the KV scatter / gather by their contract in
+torch indexing.  Every result, error, block table, tree node, refcount,
+free-list entry and byte must be the recorded one; the kernels themselves
+are the GPU tests' business."""
+
+import json
+
+import numpy as np
+import pytest
+
+from agentkv_b200 import workloads as W
+from agentkv_b200.config import PoolConfig
+
+
+@pytest.mark.parametrize("seed", [1, 2, 3])
+def test_tree_host_logic_replays_reference_traces(golden_dir, seed, monkeypatch):
+    """The package's host-side tree logic (agentkv_b200/radix_tree.py:
+    handles, shared nodes, inserts with their split / overwrite quirks,
+    prunes, CoW dispatch, error checks) replays the reference's recorded
+    tree traces on CPU — the allocator answered by the oracle
+    (tests/oracle_slab.py), the tree kernels by their CPU model — with every
+    result, error, block table, tree node, refcount, free-list entry and
+    block digest as recorded."""
+    import hashlib
+
+    import torch
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200.allocator import BlockHandle
+    from agentkv_b200.radix_tree import DualRadixTree
+    from oracle_slab import OracleSlab
+    from tree_kernel_model import TreeKernelModel
+
+    monkeypatch.setattr(N, "lib", TreeKernelModel(N.lib))
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    g = json.loads((golden_dir / f"tree_trace_{seed}.json").read_text())
+    n, bs = g["n_blocks"], g["block_size"]
+    cfg = PoolConfig(total_blocks=n, block_size=bs, num_layers=1, num_kv_heads=2, head_dim=4,
+                     dtype="float16", device="meta", epoch_interval=7)
+    torch.manual_seed(seed)
+    kv = torch.randn((n, 1, 2, 2, bs, 4), dtype=torch.float32).half()
+    slab = OracleSlab(kv, 7)
+    tree = DualRadixTree(slab, cfg)
+    T_CREATE, T_FORK, T_ALLOC, T_COW, T_APPEND, T_COMMIT, T_FREE, T_MATCH, T_ADVANCE, T_ZERO = range(10)
+    live = {}
+    states = {step: st for step, st in g["states"]}
+    for step, rec in enumerate(g["ops"]):
+        op = rec["op"]
+        err = None
+        try:
+            if op == T_CREATE:
+                h = tree.create_root(rec["tokens"])
+                live[h.handle_id] = h
+                assert [h.handle_id, h.shared_node_id, h.shared_match_len] == rec["out"]
+            elif op == T_FORK:
+                c = tree.fork(live[rec["h"]])
+                live[c.handle_id] = c
+                assert c.handle_id == rec["out"]
+            elif op == T_ALLOC:
+                h = live[rec["h"]]
+                tree.allocate_block(h)
+                assert h.residual_blocks[-1].block_id == rec["out"]
+            elif op == T_COW:
+                h = live[rec["h"]]
+                tree.ensure_mutable_block(h, rec["idx"])
+                assert h.residual_blocks[rec["idx"]].block_id == rec["out"]
+            elif op == T_APPEND:
+                tree.append_tokens(live[rec["h"]], rec["tokens"])
+            elif op == T_COMMIT:
+                h = live[rec["h"]]
+                tree.commit_prefix(h, rec["length"])
+                assert [h.shared_node_id, h.shared_match_len] == rec["out"]
+            elif op == T_FREE:
+                tree.free(live.pop(rec["h"]))
+            elif op == T_MATCH:
+                mh, mlen = tree.match_prefix(rec["tokens"])
+                got = [-1 if mh is None else mh.handle_id, mlen, -1 if mh is None else mh.shared_node_id]
+                assert got == rec["out"]
+                if mh is not None:
+                    live[mh.handle_id] = mh
+            elif op == T_ADVANCE:
+                slab.maybe_advance_epoch()
+            elif op == T_ZERO:
+                slab.zero_block(BlockHandle(rec["block"]))
+        except (ValueError, MemoryError) as e:
+            err = e
+        assert (err is not None) == ("error" in rec), f"step {step}: {rec} -> {err!r}"
+        if step in states:
+            st = states[step]
+            assert {str(k): tree.get_block_ids(h) for k, h in sorted(live.items())} == st["tables"]
+            assert {str(k): [h.shared_node_id, h.shared_match_len] for k, h in sorted(live.items())} == st["shared"]
+            nodes = {str(nid): {"parent": nd.parent_id, "edge": nd.edge_tokens,
+                                "blocks": [b.block_id for b in nd.blocks],
+                                "children": sorted([int(k), int(v)] for k, v in nd.children.items()),
+                                "ref": nd.ref_count}
+                     for nid, nd in sorted(tree._shared_nodes.items())}
+            assert nodes == st["nodes"]
+            ost = slab.o.state()
+            assert ost["ref_counts"].tolist() == st["ref"]
+            assert ost["free_list"].tolist() == st["free"]
+            for k in ("active_handles", "shared_nodes", "shared_blocks"):
+                if k in st["stats"]:
+                    assert tree.stats()[k] == st["stats"][k], k
+    digests = [hashlib.sha256(kv[i].numpy().tobytes()).hexdigest() for i in range(n)]
+    assert digests == g["block_sha256"]
+
+
+@pytest.mark.parametrize("seed", [1, 2, 7, 13, 17, 42, 137, 999])
+def test_tree_host_logic_replays_reference_stress_runner(golden_dir, seed, monkeypatch):
+    """The reference stress runner's recorded calls (tests/stress_replay.py)
+    through the package's tree logic on CPU, the allocator answered by the
+    oracle and the tree kernels by their CPU model: every handle id, block
+    id and exhaustion as recorded, and the recorded end state."""
+    import torch
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200.radix_tree import DualRadixTree
+    from oracle_slab import OracleSlab
+    from stress_replay import replay
+    from tree_kernel_model import TreeKernelModel
+
+    monkeypatch.setattr(N, "lib", TreeKernelModel(N.lib))
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    g = np.load(golden_dir / f"stress_{seed}.npz")
+    cfg = PoolConfig(total_blocks=512, block_size=4, num_layers=2, num_kv_heads=2, head_dim=8, dtype="float16",
+                     device="meta")
+    slab = OracleSlab(torch.zeros((512, 2, 2, 2, 4, 8), dtype=torch.float16), cfg.epoch_interval)
+    tree = DualRadixTree(slab, cfg)
+    replay(g, tree, slab.maybe_advance_epoch, lambda e: isinstance(e, MemoryError) and "exhausted" in str(e))
+    st = slab.o.state()
+    np.testing.assert_array_equal(st["ref_counts"], g["ref"])
+    np.testing.assert_array_equal(st["free_list"], g["free"])
+
+
+def test_hf_cache_host_logic_replays_reference_session(golden_dir, monkeypatch):
+    """The package's HuggingFace cache logic (agentkv_b200/hf_cache.py: block
+    allocation on layer 0, copy-on-write checks in the reference's order,
+    slot arithmetic, truncation) replays the reference's recorded session on
+    CPU — the pool's allocator answered by the oracle, the tree kernels by
+    their CPU model, and the KV scatter / gather by their contract in torch
+    indexing — with every K/V output, block table, sequence length and pool
+    byte as recorded."""
+    import torch
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200 import kernels as K
+    from agentkv_b200.hf_cache import AgentKVCache
+    from agentkv_b200.pool import AgentKVPool
+    from agentkv_b200.radix_tree import DualRadixTree
+    from oracle_slab import OracleSlab
+    from tree_kernel_model import TreeKernelModel
+
+    def kv_scatter(kv, slots, layer, k, v, status=None):
+        bs = kv.shape[4]
+        for i, slot in enumerate(slots.tolist()):
+            kv[slot // bs, layer, 0, :, slot % bs] = k[0, :, i].to(kv.dtype)
+            kv[slot // bs, layer, 1, :, slot % bs] = v[0, :, i].to(kv.dtype)
+
+    def kv_gather(kv, table, layer, n_tokens, status=None):
+        x = kv[table.long(), layer]  # [blocks, 2, H, bs, D]
+        nb, _, h, bs, d = x.shape
+        k = x[:, 0].permute(1, 0, 2, 3).reshape(1, h, nb * bs, d)[:, :, :n_tokens]
+        v = x[:, 1].permute(1, 0, 2, 3).reshape(1, h, nb * bs, d)[:, :, :n_tokens]
+        return k.contiguous(), v.contiguous()
+
+    monkeypatch.setattr(N, "lib", TreeKernelModel(N.lib))
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    monkeypatch.setattr(K, "kv_scatter", kv_scatter)
+    monkeypatch.setattr(K, "kv_gather", kv_gather)
+    g = np.load(golden_dir / "hf_session.npz")
+    spec = W.HFSpec(**json.loads(str(g["spec"])))
+    cfg = PoolConfig(total_blocks=spec.total_blocks, block_size=spec.block_size, num_layers=spec.num_layers,
+                     num_kv_heads=spec.num_kv_heads, head_dim=spec.head_dim, dtype=spec.dtype, device="meta")
+    kv = torch.zeros((spec.total_blocks, spec.num_layers, 2, spec.num_kv_heads, spec.block_size, spec.head_dim),
+                     dtype=getattr(torch, spec.dtype))
+    pool = object.__new__(AgentKVPool)
+    pool._cfg = cfg
+    pool._allocator = OracleSlab(kv, cfg.epoch_interval)
+    pool._allocator._status = torch.zeros(8, dtype=torch.int32)
+    pool._tree = DualRadixTree(pool._allocator, cfg)
+    outs, keys = [], []
+
+    def on_output(e, layer, ok, ov):
+        keys.append((e, layer, ok.shape[2]))
+        outs.append(np.concatenate([ok.numpy().reshape(-1), ov.numpy().reshape(-1)]))
+
+    caches = W.hf_run(spec, pool, AgentKVCache, torch.from_numpy, on_output)
+    np.testing.assert_array_equal(np.asarray(keys), g["out_keys"])
+    assert np.concatenate(outs).tobytes() == g["outs"].tobytes()
+    tables = np.concatenate([np.asarray(pool.get_block_ids(c.handle), np.int32) for c in caches])
+    np.testing.assert_array_equal(tables, g["tables"])
+    assert [c.get_seq_length() for c in caches] == g["seen"].tolist()
+    assert kv.numpy().tobytes() == g["pool"].tobytes()
+
+
+def test_react_trace_host_logic_replays_reference(golden_dir, monkeypatch):
+    """The ReAct trace (70B geometry, 40,000 blocks, 1,000 steps) through the
+    package's pool and tree logic on CPU with the copy_block hook of the
+    vLLM adapter: every step's recorded CoW pairs, and at the checkpoints the
+    agents' tables, refcounts and free list, as the reference recorded them
+    (allocator answered by the oracle, tree kernels by their CPU model)."""
+    import torch
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200.pool import AgentKVPool
+    from agentkv_b200.radix_tree import DualRadixTree
+    from oracle_slab import OracleSlab
+    from react_apis import PoolReActAPI
+    from tree_kernel_model import TreeKernelModel
+
+    monkeypatch.setattr(N, "lib", TreeKernelModel(N.lib))
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    g = np.load(golden_dir / "react_70b.npz")
+    spec = W.ReActSpec(**json.loads(str(g["spec"])))
+    n_, bs, L, H, D, dt = W.LLAMA3_70B_GEOMETRY
+    cfg = PoolConfig(total_blocks=n_, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D, dtype=dt,
+                     device="meta")
+    slab = OracleSlab(torch.zeros((n_, 1), dtype=torch.uint8), cfg.epoch_interval)
+    pairs = []
+    slab.copy_block = lambda src, dst: pairs.append((src.block_id, dst.block_id))
+    pool = object.__new__(AgentKVPool)
+    pool._cfg, pool._allocator = cfg, slab
+    pool._tree = DualRadixTree(slab, cfg)
+    api = PoolReActAPI(pool)
+    root, agents = W.react_setup(api, spec)
+    np.testing.assert_array_equal(np.asarray(pool.get_block_ids(root), np.int32), g["root_table"])
+    so = g["step_off"]
+    for i, actions in enumerate(W.react_trace(spec)):
+        pairs.clear()
+        W.react_step(api, root, agents, actions)
+        np.testing.assert_array_equal(np.asarray(pairs, np.int32).reshape(-1, 2), g["pairs"][so[i]:so[i + 1]],
+                                      err_msg=f"step {i}")
+        k = f"s{i + 1}"
+        if k + "_ref" in g.files:
+            tables = np.concatenate([np.asarray(pool.get_block_ids(h), np.int32) for h in agents])
+            np.testing.assert_array_equal(tables, g[k + "_tables"], err_msg=k)
+            st = slab.o.state()
+            np.testing.assert_array_equal(st["ref_counts"], g[k + "_ref"])
+            np.testing.assert_array_equal(st["free_list"], g[k + "_free"])
+
+
+def _cpu_pool(cfg, kv, monkeypatch):
+    """An AgentKVPool whose allocator is the oracle (tests/oracle_slab.py)
+    and whose tree kernels run as their CPU model, over the CPU tensor kv."""
+    import torch  # noqa: F401
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200.pool import AgentKVPool
+    from agentkv_b200.radix_tree import DualRadixTree
+    from oracle_slab import OracleSlab
+    from tree_kernel_model import TreeKernelModel
+
+    if not isinstance(N.lib, TreeKernelModel):
+        monkeypatch.setattr(N, "lib", TreeKernelModel(N.lib))
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    pool = object.__new__(AgentKVPool)
+    pool._cfg = cfg
+    pool._allocator = OracleSlab(kv, cfg.epoch_interval)
+    pool._tree = DualRadixTree(pool._allocator, cfg)
+    return pool
+
+
+def test_quickstart_host_logic_replays_reference(golden_dir, monkeypatch):
+    """The quickstart workload through the package's pool logic on CPU:
+    children's tables, the root's, match results, refcounts, free list and
+    every block's bytes as the reference recorded them."""
+    import hashlib
+
+    import torch
+
+    g = json.loads((golden_dir / "quickstart.json").read_text())
+    n_, bs, L, H, D, dt = W.QUICKSTART_GEOMETRY
+    cfg = PoolConfig(total_blocks=n_, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D, dtype=dt,
+                     device="meta")
+    torch.manual_seed(0)
+    kv = torch.randn((n_, L, 2, H, bs, D), dtype=torch.float16)
+    pool = _cpu_pool(cfg, kv, monkeypatch)
+    root = pool.create_root(list(range(32)))
+    pool.allocate_block(root)
+    kids = [pool.fork(root) for _ in range(3)]
+    for c in kids:
+        pool.allocate_block(c)
+    for c in kids:
+        pool.ensure_mutable_block(c, 0)
+    pool.commit_prefix(root, 16)
+    matches = []
+    for q in g["queries"]:
+        mh, mlen = pool._tree.match_prefix(q)
+        matches.append([-1 if mh is None else mh.shared_node_id, mlen])
+    assert [pool.get_block_ids(c) for c in kids] == g["children"]
+    assert pool.get_block_ids(root) == g["root"]
+    assert matches == g["matches"]
+    st = pool._allocator.o.state()
+    assert st["ref_counts"].tolist() == g["ref"]
+    assert st["free_list"].tolist() == g["free"]
+    assert [hashlib.sha256(kv[i].numpy().tobytes()).hexdigest() for i in range(n_)] == g["block_sha256"]
+
+
+def test_tot_batched_host_logic_replays_reference(golden_dir, monkeypatch):
+    """The Tree-of-Thought fan-out on the 60,000-block pool through the
+    package's batched pool calls (fork_many, ensure_mutable_batch,
+    allocate_blocks, free_many) on CPU: child tables, refcounts and free
+    lists after the fan-out and after the frees as the reference recorded
+    them."""
+    import torch
+
+    g = np.load(golden_dir / "tot_8b.npz")
+    spec = W.ToTSpec()
+    n_, bs, L, H, D, dt = W.LLAMA3_8B_GEOMETRY
+    cfg = PoolConfig(total_blocks=n_, block_size=bs, num_layers=L, num_kv_heads=H, head_dim=D, dtype=dt,
+                     device="meta")
+    pool = _cpu_pool(cfg, torch.zeros((n_, 1), dtype=torch.uint8), monkeypatch)
+    root = pool.create_root(W.tot_root_tokens(spec))
+    pool.allocate_blocks(root, spec.root_tokens // 16)
+    level, kids = [root], []
+    for lvl in range(spec.levels):
+        nxt = []
+        for parent in level:
+            nxt.extend(pool.fork_many(parent, spec.fanout))
+        for c in nxt:
+            pool.ensure_mutable_batch([(c, len(c.residual_blocks) - 1)])
+            pool.allocate_blocks(c, spec.appended_blocks)
+        kids.extend(nxt)
+        level = nxt
+    tables = np.concatenate([np.asarray(pool.get_block_ids(c), np.int32) for c in kids])
+    np.testing.assert_array_equal(tables, g["tables"])
+    st = pool._allocator.o.state()
+    np.testing.assert_array_equal(st["ref_counts"], g["ref_fanout"])
+    np.testing.assert_array_equal(st["free_list"], g["free_fanout"])
+    pool.free_many(kids)
+    st = pool._allocator.o.state()
+    np.testing.assert_array_equal(st["ref_counts"], g["ref_freed"])
+    np.testing.assert_array_equal(st["free_list"], g["free_freed"])
+
+
+def test_serving_lifecycle_on_the_oracle():
+    """The serving-lifecycle schedule (tests/serving_pattern.py) on the
+    oracle: deterministic, with page hits that return the committed blocks,
+    misses, aborts, finishes and evictions; the allocated count it reads
+    agrees with the oracle's own counter."""
+    from serving_pattern import OracleServeAPI, serve
+
+    a = serve(OracleServeAPI(512, 16))
+    assert a == serve(OracleServeAPI(512, 16))
+    kinds = {o[0] for o in a}
+    assert {"hit", "miss", "abort", "finish", "evict"} <= kinds, kinds
+    assert sum(1 for o in a if o[0] == "hit") >= 10
+    assert all(o[1] >= 0 for o in a if o[0] == "evict")
+    # hits hand back the committed prefix's blocks, one id per whole page
+    assert all(len(o[3]) == o[2] // 16 and o[2] > 0 for o in a if o[0] == "hit")
+    api = OracleServeAPI(512, 16)
+    serve(api)
+    assert api.allocated_blocks == api.alloc.state()["allocated_blocks"]
+    assert a[-1] == ("end", api.free_blocks, api.allocated_blocks)
+
+
+def test_serving_lifecycle_host_logic_equals_oracle(monkeypatch):
+    """The serving-lifecycle schedule through the package's pool logic on CPU
+    (oracle allocator, tree kernel model) observes what the oracle's own
+    tree observes: hits, block ids, finishes, aborts, counters."""
+    import torch
+
+    from serving_pattern import OracleServeAPI, PoolServeAPI, serve
+
+    cfg = PoolConfig(total_blocks=512, block_size=16, num_layers=1, num_kv_heads=1, head_dim=8,
+                     dtype="float16", device="meta")
+    pool = _cpu_pool(cfg, torch.zeros((512, 1), dtype=torch.uint8), monkeypatch)
+    assert serve(PoolServeAPI(pool)) == serve(OracleServeAPI(512, 16))

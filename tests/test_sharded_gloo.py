@@ -261,7 +261,7 @@ def _match_split_worker(rank, world, port, q):
         from agentkv_b200.radix_tree import ROOT_NODE_ID, DualRadixTree, SharedNode
         from agentkv_b200.sharded_tree import TreeReplicaSync, match_split
         from oracle import oracle as O
-        from test_host_logic import _csr_of
+        from test_host_runs import _csr_of
         from tree_kernel_model import TreeKernelModel
 
         model = TreeKernelModel(N.lib)
