@@ -124,6 +124,7 @@ class DeviceTree:
         self.d_slots = torch.zeros((slot_cap, 4), dtype=torch.int32, device=device)
         self.status = torch.zeros(N.STATUS_BYTES // 4, dtype=torch.int32, device=device)
         self._view: Optional[N.AkvTreeView] = None
+        self._stage: Optional["QueryStage"] = None  # match_batch's reusable buffers
 
     # ── mutations (host mirror) ──────────────────────────────────────────────
     def append_tokens(self, toks: np.ndarray) -> int:
@@ -573,10 +574,57 @@ def pack_queries(queries: Sequence, device: torch.device) -> Tuple[torch.Tensor,
     lens = np.fromiter((len(q) for q in queries), np.int64, len(queries))
     q_off = np.zeros(len(queries) + 1, np.int64)
     np.cumsum(lens, out=q_off[1:])
-    flat = np.empty(max(int(q_off[-1]), 1), np.int32)
-    for i, q in enumerate(queries):
-        flat[q_off[i] : q_off[i + 1]] = np.asarray(q, np.int32)
+    flat = np.zeros(max(int(q_off[-1]), 1), np.int32)
+    if int(q_off[-1]):
+        np.concatenate([np.asarray(q, np.int32) for q in queries], out=flat[: int(q_off[-1])])
     return _upload(flat, device), _upload(q_off, device)
+
+
+class QueryStage:
+    """Reusable buffers for packing lookup batches: host buffers (pinned on a
+    GPU, so the uploads are asynchronous) and device buffers that grow with
+    the largest batch seen.  Fresh host memory is not free — first-touch page
+    faults on a new 70 MB token buffer cost more than the lookup itself — so
+    after the first batches nothing is allocated.  A batch's buffers are
+    reused by the next pack(): the caller finishes the lookup (reads its
+    results) first, as match_batch does."""
+
+    def __init__(self, device: torch.device) -> None:
+        self.device = device
+        self._tok_cap = self._q_cap = 0
+
+    def _grow(self, total: int, nq: int) -> None:
+        pin = self.device.type == "cuda"
+        if total > self._tok_cap:
+            cap = max(total, self._tok_cap + self._tok_cap // 2, 1 << 16)
+            self.h_tok = torch.empty(cap, dtype=torch.int32, pin_memory=pin)
+            self.d_tok = torch.empty(cap, dtype=torch.int32, device=self.device)
+            self._tok_cap = cap
+        if nq + 1 > self._q_cap:
+            cap = max(nq + 1, self._q_cap + self._q_cap // 2, 1024)
+            self.h_off = torch.empty(cap, dtype=torch.int64, pin_memory=pin)
+            self.h_ord = torch.empty(cap, dtype=torch.int32, pin_memory=pin)
+            self.d_off = torch.empty(cap, dtype=torch.int64, device=self.device)
+            self.d_ord = torch.empty(cap, dtype=torch.int32, device=self.device)
+            self._q_cap = cap
+
+    def pack(self, queries: Sequence) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """(tokens int32, offsets int64, longest-first order int32) on the
+        device, enqueued on the current stream."""
+        nq = len(queries)
+        lens = np.fromiter((len(q) for q in queries), np.int64, nq)
+        total = int(lens.sum())
+        self._grow(total, nq)
+        if total:
+            np.concatenate([np.asarray(q, np.int32) for q in queries], out=self.h_tok.numpy()[:total])
+        off = self.h_off.numpy()[: nq + 1]
+        off[0] = 0
+        np.cumsum(lens, out=off[1:])
+        self.h_ord.numpy()[:nq] = np.argsort(-lens, kind="stable")
+        self.d_tok[:total].copy_(self.h_tok[:total], non_blocking=True)
+        self.d_off[: nq + 1].copy_(self.h_off[: nq + 1], non_blocking=True)
+        self.d_ord[:nq].copy_(self.h_ord[:nq], non_blocking=True)
+        return self.d_tok[: max(total, 1)], self.d_off[: nq + 1], self.d_ord[: max(nq, 1)]
 
 
 def _upload(a: np.ndarray, device: torch.device) -> torch.Tensor:
@@ -609,9 +657,9 @@ def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_co
         runs = tree.want_runs()
     dev = tree.device
     nq = len(queries)
-    tok, q_off = pack_queries(queries, dev)
-    lens = np.fromiter((len(q) for q in queries), np.int64, nq)
-    order = torch.from_numpy(np.argsort(-lens, kind="stable").astype(np.int32)).to(dev)
+    if tree._stage is None:
+        tree._stage = QueryStage(dev)
+    tok, q_off, order = tree._stage.pack(queries)
     node = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
     mlen = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
     cmp_ = torch.empty(max(nq, 1), dtype=torch.int64, device=dev) if with_compared else None
