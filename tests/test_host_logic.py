@@ -286,3 +286,33 @@ def test_allocator_error_mapping():
     with pytest.raises(ValueError, match="out of range"):
         a._validate_handle(BlockHandle(8))
     a._validate_handle(BlockHandle(7))
+
+
+def test_query_packing():
+    """pack_queries and QueryStage.pack lay a batch out as the lookup kernel
+    reads it (tokens back to back, int64 offsets, longest-first order),
+    including empty queries, an empty batch and a stage reused for batches
+    larger and smaller than the last."""
+    import torch
+
+    from agentkv_b200.device_tree import QueryStage, longest_first, pack_queries
+
+    cpu = torch.device("cpu")
+    rng = np.random.default_rng(2)
+    stage = QueryStage(cpu)
+    for nq in (5, 300, 0, 40, 2000, 3):
+        qs = [rng.integers(0, 1000, size=int(rng.integers(0, 90))).astype(np.int32) for _ in range(nq)]
+        if nq > 2:
+            qs[1] = []  # an empty query (a Python list)
+        lens = np.array([len(q) for q in qs], np.int64)
+        off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+        flat = np.concatenate([np.asarray(q, np.int32) for q in qs]) if nq else np.zeros(0, np.int32)
+        tok, q_off = pack_queries(qs, cpu)
+        np.testing.assert_array_equal(q_off.numpy(), off)
+        np.testing.assert_array_equal(tok.numpy()[: off[-1]], flat)
+        t2, o2, order = stage.pack(qs)
+        np.testing.assert_array_equal(o2.numpy(), off)
+        np.testing.assert_array_equal(t2.numpy()[: off[-1]], flat)
+        want_order = np.argsort(-lens, kind="stable")
+        np.testing.assert_array_equal(order.numpy()[:nq], want_order)
+        np.testing.assert_array_equal(longest_first(q_off, cpu).numpy(), want_order)
