@@ -795,7 +795,22 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         t = torch.tensor([tok_cmp], dtype=torch.float64, device=dev)
         torch.distributed.all_reduce(t)
         tok_cmp = float(t) / world
-    roofline = cpu = None
+    roofline = cpu = e2e = None
+    if rank == 0 and world == 1:
+        # through the public call with host queries: pack into the pinned
+        # stage, upload, look up, read the answers back (one batch per call)
+        for b in range(min(2, len(batches))):
+            pool.match_prefix_batch(batches[b])
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        reps = 4
+        for i in range(reps):
+            pool.match_prefix_batch(batches[i % len(batches)])
+        e2e_s = (time.perf_counter() - t0) / reps
+        h2d = int(statistics.mean(qtokens)) * 4 + (nq + 1) * 8 + nq * 4
+        e2e = {"value": round(nq / e2e_s, 1), "unit": "queries/s", "ms_per_batch": round(e2e_s * 1e3, 3),
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": nq * 8,
+               "api": "AgentKVPool.match_prefix_batch (host token lists in, numpy answers out)"}
     if rank == 0:
         peak, peak_kind = measured_peak()
         achieved = alg["total"] / (per_batch_ms / 1e3) / 1e9
@@ -835,6 +850,7 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         "verify_chunks": chunks or 4,
         "roofline": roofline,
         "cpu_baseline": cpu,
+        "e2e": e2e,
     }
 
 
