@@ -15,7 +15,9 @@ plan.
 
 Capturing executes nothing, so the allocator sees exactly the operations of
 the runs, in order: ids, refcounts and the free list stay those of the
-reference's per-child calls.  Requirements: the roots' table lengths are
+reference's per-child calls.  run_many() pipelines a sequence of runs over
+two recorded instances, hiding the host's read-back and relaunch behind the
+other instance's replay.  Requirements: the roots' table lengths are
 fixed at construction, and nothing else uses the allocator between runs on
 another stream.
 """
@@ -68,6 +70,7 @@ class FanoutGraph:
         self._copy_status = alloc._status if self.pool.device == alloc.device else None
         self.copies_per_run = int(sum(len(self.root_lens) * self.fanout ** (lv + 1) for lv in range(self.levels)))
         self.launches_per_run = 0
+        self._twin: Optional["FanoutGraph"] = None  # run_many's second instance
         with torch.cuda.device(self.dev):  # kernels prepared and graph recorded on the allocator's GPU
             N.check(N.lib.akv_prepare())
             self.graph = torch.cuda.CUDAGraph()
@@ -141,3 +144,50 @@ class FanoutGraph:
             self.alloc.check()
         out = self.h_tables.numpy()
         return out.copy() if copy else out
+
+    def _twin_graph(self) -> "FanoutGraph":
+        if self._twin is None:
+            self._twin = FanoutGraph(self.alloc, self.root_lens, self.levels, self.fanout, self.append,
+                                     pool=self.pool, free_children=self.free_children, variant=self.variant,
+                                     merge=self.merge)
+        return self._twin
+
+    def run_many(self, roots_list) -> list:
+        """run() on each entry of `roots_list` in turn, with the same results
+        (each child table array, in order), keeping the GPU busy: two
+        recorded instances of the fan-out alternate, so that while one
+        replays, the host reads the other's child tables and writes its next
+        roots.  The replays are ordered on one stream, so the allocator sees
+        the runs one after another exactly as with run()."""
+        graphs = (self, self._twin_graph())
+        n_roots = self.h_roots.numel()
+        outs = []
+        with torch.cuda.device(self.dev):
+            stream = torch.cuda.current_stream(self.dev)
+            done = (torch.cuda.Event(), torch.cuda.Event())
+            held = [False, False]
+
+            def collect(j: int) -> None:
+                done[j].synchronize()
+                g = graphs[j]
+                if g._h_status_np[0]:
+                    self.alloc.check()
+                outs.append(g.h_tables.numpy().copy())
+                held[j] = False
+
+            for i, roots in enumerate(roots_list):
+                j = i % 2
+                r = np.asarray(roots, np.int32).reshape(-1)
+                if r.size != n_roots:
+                    raise ValueError(f"FanoutGraph.run_many: expected {n_roots} root ids, got {r.size}")
+                if held[j]:
+                    collect(j)  # run i - 2, before this instance is reused
+                graphs[j]._h_roots_np[:] = r
+                graphs[j].graph.replay()
+                done[j].record(stream)
+                held[j] = True
+            n = len(roots_list)
+            for i in (n - 2, n - 1):
+                if i >= 0 and held[i % 2]:
+                    collect(i % 2)
+        return outs

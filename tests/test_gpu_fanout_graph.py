@@ -210,3 +210,41 @@ def test_fanout_edge_cases():
     assert_same_as_oracle(a, o, "one child")
     with pytest.raises(ValueError):
         FanoutGraph(a, [0], 1, 2, 1)
+
+
+@pytest.mark.parametrize("merge", [True, False])
+def test_run_many_matches_oracle(merge):
+    """FanoutGraph.run_many (two recorded instances alternating) returns, for
+    each of its runs in order, what the oracle's per-child sequence gives,
+    and leaves the allocator, the reclaimer and the pool bytes as the oracle
+    leaves them; runs mixed with run() stay in sequence."""
+    n_blocks, root_lens, levels, fanout, append = 1024, [3, 2], 2, 3, 1
+    cfg = PoolConfig(total_blocks=n_blocks, block_size=16, num_layers=2, num_kv_heads=2, head_dim=64,
+                     dtype="bfloat16", device="cuda")
+    a = AgentKVPool(config=cfg)._allocator
+    a._kv_data.view(torch.int16).random_(-30000, 30000)
+    host = a._kv_data.view(torch.uint8).reshape(n_blocks, -1).cpu().numpy().copy()
+    bpb = host.shape[1]
+    o = O.OracleAllocator(n_blocks, cfg.epoch_interval)
+    tree = O.OracleTree(o, 16, copy_cb=lambda s, d: O.copy_blocks(host, bpb, np.array([[s, d]], np.int32)))
+    roots = []
+    for ln in root_lens:
+        h = tree.create_root([])
+        for _ in range(ln):
+            tree.allocate_block(h)
+        roots.append(h)
+    d_roots = a.alloc_batch(sum(root_lens)).cpu().numpy()
+    fg = FanoutGraph(a, root_lens, levels, fanout, append, free_children=True, merge=merge)
+    for n_runs in (1, 5, 2):
+        got = fg.run_many([d_roots] * n_runs)
+        assert len(got) == n_runs
+        for r in range(n_runs):
+            want = _oracle_fanout(tree, roots, levels, fanout, append, True)
+            np.testing.assert_array_equal(got[r], want, err_msg=f"{n_runs} runs, run {r}")
+        got1 = fg.run(d_roots)
+        np.testing.assert_array_equal(got1, _oracle_fanout(tree, roots, levels, fanout, append, True))
+        assert_same_as_oracle(a, o, f"after {n_runs} runs")
+        dev = a._kv_data.view(torch.uint8).reshape(n_blocks, -1).cpu().numpy()
+        assert np.array_equal(dev, host)
+    with pytest.raises(ValueError, match="root ids"):
+        fg.run_many([d_roots[:-1]])
