@@ -316,3 +316,68 @@ def test_query_packing():
         want_order = np.argsort(-lens, kind="stable")
         np.testing.assert_array_equal(order.numpy()[:nq], want_order)
         np.testing.assert_array_equal(longest_first(q_off, cpu).numpy(), want_order)
+
+
+def test_run_many_sequencing(monkeypatch):
+    """FanoutGraph.run_many's host sequencing, with the CUDA graph, events and
+    device context replaced by recording stand-ins: the two instances
+    alternate, an instance is read back (its event waited for) before it is
+    relaunched, every run's tables come back in run order, and a wrong root
+    count is refused before anything is launched."""
+    import contextlib
+
+    import torch
+
+    from agentkv_b200 import fanout as F
+
+    log = []
+
+    class Event:
+        def __init__(self):
+            self.tag = None
+
+        def record(self, stream):
+            self.tag = log[-1]
+
+        def synchronize(self):
+            log.append(("wait", self.tag))
+
+    monkeypatch.setattr(F.torch.cuda, "device", lambda dev: contextlib.nullcontext())
+    monkeypatch.setattr(F.torch.cuda, "current_stream", lambda dev=None: None)
+    monkeypatch.setattr(F.torch.cuda, "Event", Event)
+
+    def fake(name):
+        g = object.__new__(F.FanoutGraph)
+        g.dev = torch.device("cpu")
+        g.h_roots = torch.zeros(3, dtype=torch.int32)
+        g._h_roots_np = g.h_roots.numpy()
+        g.h_tables = torch.zeros(6, dtype=torch.int32)
+        g._h_status_np = np.zeros(8, np.int32)
+        g.alloc = None
+
+        class Graph:
+            def replay(self_inner):
+                # the "run": child tables computed from the roots written in
+                g.h_tables.numpy()[:] = np.tile(g._h_roots_np, 2) * 10
+                log.append(("replay", name, int(g._h_roots_np[0])))
+
+        g.graph = Graph()
+        return g
+
+    a, b = fake("a"), fake("b")
+    a._twin = b
+    roots = [np.array([i, i + 1, i + 2], np.int32) for i in range(5)]
+    outs = a.run_many(roots)
+    assert [int(o[0]) for o in outs] == [0, 10, 20, 30, 40]
+    assert all(np.array_equal(o, np.tile(r, 2) * 10) for o, r in zip(outs, roots))
+    replays = [e for e in log if e[0] == "replay"]
+    assert [e[1] for e in replays] == ["a", "b", "a", "b", "a"]
+    # instance a is waited for (run 0 read back) before its relaunch with run 2
+    i_wait = log.index(("wait", ("replay", "a", 0)))
+    i_relaunch = log.index(("replay", "a", 2))
+    assert i_wait < i_relaunch
+    log.clear()
+    with pytest.raises(ValueError, match="root ids"):
+        a.run_many([np.zeros(2, np.int32)])
+    assert not log
+    assert a.run_many([]) == []
