@@ -674,7 +674,7 @@ def match_cpu_baseline(pool, batches, gpu_results, max_seconds: float) -> dict:
     csr = {"child_ptr": child_ptr, "child_key": np.asarray(keys or [0], np.int32),
            "child_id": np.asarray(ids or [0], np.int32), "edge_off": edge_off, "edge_len": edge_len,
            "edge_tokens": np.concatenate(toks) if pos else np.zeros(1, np.int32)}
-    packed = [O.pack_queries([q.tolist() for q in b]) for b in batches]
+    packed = [O.pack_queries(b) for b in batches]
     same = True
     for (flat, off), (g_node, g_len) in zip(packed, gpu_results):
         o_node, o_len, _ = O.match_prefix_csr(csr, flat, off, 16)
@@ -692,13 +692,13 @@ def match_cpu_baseline(pool, batches, gpu_results, max_seconds: float) -> dict:
     nq = len(batches[0])
     # the reference's own loop, in Python, on the first queries of batch 0
     py_tree = O.csr_children(csr)
-    py_q = [q.tolist() for q in batches[0]]
-    py_done = 0
-    t1 = time.perf_counter()
-    while py_done < len(py_q) and time.perf_counter() - t1 < max_seconds / 2:
-        O.match_prefix_py(py_tree, py_q[py_done:py_done + 16], 16)
-        py_done = min(py_done + 16, len(py_q))
-    py_secs = time.perf_counter() - t1
+    py_done, py_secs = 0, 0.0
+    while py_done < len(batches[0]) and py_secs < max_seconds / 2:
+        chunk = [q.tolist() for q in batches[0][py_done:py_done + 16]]  # the reference's token lists
+        t1 = time.perf_counter()
+        O.match_prefix_py(py_tree, chunk, 16)
+        py_secs += time.perf_counter() - t1
+        py_done += len(chunk)
     return {"value": round(done * nq / secs, 1), "unit": "queries/s", "cores": 1, "kind": "port",
             "sample": f"{done} batches of {nq} queries on the same tree, {secs:.1f} s, one host thread "
                       f"(the oracle's C restatement)",

@@ -560,6 +560,22 @@ def match_prefix_csr(csr: dict, tokens: np.ndarray, q_off: np.ndarray, block_siz
     return node[:nq], mlen[:nq], cmp_[:nq]
 
 
+class _Edges:
+    """Node edges as Python lists, converted from the CSR arena when first
+    walked (a large tree's arena as Python ints would take gigabytes)."""
+
+    def __init__(self, csr: dict) -> None:
+        self._off, self._len, self._tok = csr["edge_off"], csr["edge_len"], csr["edge_tokens"]
+        self._lists: dict = {}
+
+    def __getitem__(self, u: int) -> list:
+        e = self._lists.get(u)
+        if e is None:
+            o = int(self._off[u])
+            e = self._lists[u] = self._tok[o:o + int(self._len[u])].tolist()
+        return e
+
+
 def csr_children(csr: dict) -> list:
     """Per node, its children as a dict first token -> child id, and its edge
     as a Python list: the shapes the reference's loop walks
@@ -567,9 +583,7 @@ def csr_children(csr: dict) -> list:
     ptr, keys, ids = csr["child_ptr"], csr["child_key"], csr["child_id"]
     kids = [dict(zip(keys[ptr[u]:ptr[u + 1]].tolist(), ids[ptr[u]:ptr[u + 1]].tolist()))
             for u in range(len(ptr) - 1)]
-    off, ln, tok = csr["edge_off"], csr["edge_len"], csr["edge_tokens"]
-    edges = [tok[off[u]:off[u] + ln[u]].tolist() for u in range(len(ln))]
-    return [kids, edges]
+    return [kids, _Edges(csr)]
 
 
 def match_prefix_py(tree: list, queries, block_size: int):
