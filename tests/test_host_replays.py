@@ -375,3 +375,33 @@ def test_serving_lifecycle_host_logic_equals_oracle(monkeypatch):
                      dtype="float16", device="meta")
     pool = _cpu_pool(cfg, torch.zeros((512, 1), dtype=torch.uint8), monkeypatch)
     assert serve(PoolServeAPI(pool)) == serve(OracleServeAPI(512, 16))
+
+
+def test_match_stress_tree_host_logic_replays_reference(golden_dir, monkeypatch):
+    """The match stress tree (600 sequences) built through the pool calls on
+    CPU (create_root's lookups, block allocation, commits), then one batched
+    lookup: tree size, node-id counter, free count and every query's
+    (node, length) as the reference recorded them."""
+    import torch
+
+    g = np.load(golden_dir / "match_small.npz")
+    spec = W.MatchSpec(**json.loads(str(g["spec"])))
+    prefixes = W.match_prefixes(spec)
+    corpus = W.match_sequences(spec, prefixes)
+    n = int(g["total_blocks"])
+    cfg = PoolConfig(total_blocks=n, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1, dtype="float16",
+                     device="meta")
+    pool = _cpu_pool(cfg, torch.zeros((n, 1), dtype=torch.uint8), monkeypatch)
+    for seq in corpus:
+        h = pool.create_root(seq)
+        pool.allocate_blocks(h, -(-len(seq) // 16) - len(pool.get_block_ids(h)))
+        share = (len(seq) // 16) * 16 - h.shared_match_len
+        if share > 0:
+            pool.commit_prefix(h, share)
+    assert len(pool._tree._shared_nodes) == int(g["n_nodes"])
+    assert pool._tree._next_node_id == int(g["next_node_id"])
+    assert pool.free_blocks == int(g["free_blocks"])
+    queries = W.match_queries(spec, corpus, prefixes, batch=0, n=len(g["node"]))
+    node, mlen = pool.match_prefix_batch(queries)
+    np.testing.assert_array_equal(node, g["node"])
+    np.testing.assert_array_equal(mlen, g["len"])
