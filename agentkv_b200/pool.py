@@ -3,7 +3,7 @@
 Thin delegation to DualRadixTree + SlabAllocator, exactly as in the reference,
 plus the batched entry points the device path makes cheap
 (``allocate_blocks``, ``fork_many``, ``ensure_mutable_batch``, ``free_many``,
-``match_prefix_batch``).
+``match_prefix_batch``, ``match_prefix_many``).
 """
 
 from __future__ import annotations
@@ -107,6 +107,10 @@ class AgentKVPool:
 
     def match_prefix_batch(self, queries: Sequence, *, with_compared: bool = False):
         return self._tree.match_prefix_batch(queries, with_compared=with_compared)
+
+    def match_prefix_many(self, queries: Sequence) -> List[Tuple[Optional[NodeHandle], int]]:
+        """The tree's match_prefix on every query (handles included), one lookup launch."""
+        return self._tree.match_prefix_many(queries)
 
     def __repr__(self) -> str:
         s = self.stats()

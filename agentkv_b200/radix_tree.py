@@ -315,6 +315,32 @@ class DualRadixTree:
         finally:
             self._alloc.leave_read_section(epoch_token)
 
+    def match_prefix_many(self, queries: Sequence) -> List[Tuple[Optional[NodeHandle], int]]:
+        """match_prefix on each query in order, with the lookups of all of
+        them in one launch: the same (handle, length) pairs, handle ids,
+        shared-node refcounts and reclaimer state as the calls one by one.
+        One read section spans the batch; the calls' sections would each
+        have released the same pending blocks, in the same order, with
+        nothing else happening in between."""
+        epoch_token = self._alloc.enter_read_section()
+        try:
+            with self._lock:
+                node, mlen = match_batch(self._dev_tree, queries, self._cfg.block_size)
+                out: List[Tuple[Optional[NodeHandle], int]] = []
+                for q, nid, m in zip(queries, node.tolist(), mlen.tolist()):
+                    if nid == INVALID_NODE_ID or m == 0:
+                        out.append((None, 0))
+                        continue
+                    self._inc_shared_ref_locked(nid)
+                    h = NodeHandle(handle_id=self._next_handle_id, shared_node_id=nid, shared_match_len=m,
+                                   tokens=list(q[:m]))
+                    self._next_handle_id += 1
+                    self._handles[h.handle_id] = h
+                    out.append((h, m))
+                return out
+        finally:
+            self._alloc.leave_read_section(epoch_token)
+
     def match_prefix_batch(self, queries: Sequence, *, with_compared: bool = False):
         """Longest shared prefix of many queries in one launch, without
         creating handles: (node ids, match lengths[, tokens compared]) as numpy

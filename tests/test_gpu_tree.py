@@ -449,3 +449,27 @@ def test_match_long_unary_chains():
         got = [(int(n) if m else -1, int(m), int(c)) for n, m, c in zip(node, mlen, cmp_)]
         assert got == [(int(n) if m else -1, int(m), int(c)) for n, m, c in want], runs
     assert dev_tree.d_run_head is not None and int((dev_tree.d_run_head >= 0).sum()) >= 60
+
+
+def test_match_prefix_many_equals_one_by_one(golden_dir):
+    """AgentKVPool.match_prefix_many (one lookup launch) gives the handles,
+    shared-node refcounts and allocator state of match_prefix called on each
+    query in turn, on the device pool."""
+    g = np.load(golden_dir / "match_small.npz")
+    spec = W.MatchSpec(**json.loads(str(g["spec"])))
+    pools = [_build_match_tree(spec, int(g["total_blocks"]))[0] for _ in range(2)]
+    prefixes = W.match_prefixes(spec)
+    corpus = W.match_sequences(spec, prefixes)
+    queries = W.match_queries(spec, corpus, prefixes, batch=0, n=200)
+    a, b = pools
+    many = a.match_prefix_many(queries)
+    one = [b._tree.match_prefix(q) for q in queries]
+    assert sum(1 for h, _ in many if h is not None) > 20
+    for (h1, m1), (h2, m2) in zip(many, one):
+        assert m1 == m2 and (h1 is None) == (h2 is None)
+        if h1 is not None:
+            assert (h1.handle_id, h1.shared_node_id) == (h2.handle_id, h2.shared_node_id)
+    assert {k: n.ref_count for k, n in a._tree._shared_nodes.items()} == \
+        {k: n.ref_count for k, n in b._tree._shared_nodes.items()}
+    np.testing.assert_array_equal(a._allocator.free_list(), b._allocator.free_list())
+    np.testing.assert_array_equal(a._allocator._ref_counts.cpu().numpy(), b._allocator._ref_counts.cpu().numpy())

@@ -405,3 +405,61 @@ def test_match_stress_tree_host_logic_replays_reference(golden_dir, monkeypatch)
     node, mlen = pool.match_prefix_batch(queries)
     np.testing.assert_array_equal(node, g["node"])
     np.testing.assert_array_equal(mlen, g["len"])
+
+
+def test_match_prefix_many_equals_one_by_one(golden_dir, monkeypatch):
+    """AgentKVPool.match_prefix_many (one lookup launch for the batch) gives
+    the handles — ids, shared nodes, lengths, tokens — the shared-node
+    refcounts and the allocator / reclaimer state of match_prefix called on
+    each query in turn, also while another reader holds a read section and
+    freed blocks wait in the pending queue (CPU: oracle allocator, tree
+    kernel model)."""
+    import torch
+
+    g = np.load(golden_dir / "match_small.npz")
+    spec = W.MatchSpec(**json.loads(str(g["spec"])))
+    prefixes = W.match_prefixes(spec)
+    corpus = W.match_sequences(spec, prefixes)[:200]
+    queries = W.match_queries(spec, corpus, prefixes, batch=0, n=120)
+    n = int(g["total_blocks"])
+    cfg = PoolConfig(total_blocks=n, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1, dtype="float16",
+                     device="meta")
+    pools = []
+    for _ in range(2):
+        pool = _cpu_pool(cfg, torch.zeros((n, 1), dtype=torch.uint8), monkeypatch)
+        live = []
+        for seq in corpus:
+            h = pool.create_root(seq)
+            pool.allocate_blocks(h, -(-len(seq) // 16) - len(pool.get_block_ids(h)))
+            share = (len(seq) // 16) * 16 - h.shared_match_len
+            if share > 0:
+                pool.commit_prefix(h, share)
+            live.append(h)
+        reader = pool._allocator.enter_read_section()  # another reader: freed blocks stay pending
+        for h in live[::3]:
+            pool.free(h)
+        pools.append((pool, reader))
+    (a, ra), (b, rb) = pools
+    assert len(a._allocator.o.state()["pending"]) > 0
+    many = a.match_prefix_many(queries)
+    one = [b._tree.match_prefix(q) for q in queries]
+    assert sum(1 for h, _ in many if h is not None) > 20
+    for (h1, m1), (h2, m2) in zip(many, one):
+        assert m1 == m2
+        if h1 is None:
+            assert h2 is None
+            continue
+        assert (h1.handle_id, h1.shared_node_id, h1.shared_match_len) == (h2.handle_id, h2.shared_node_id,
+                                                                          h2.shared_match_len)
+        assert list(h1.tokens) == list(h2.tokens)
+
+    def state(pool):
+        st = pool._allocator.o.state()
+        refs = {nid: nd.ref_count for nid, nd in pool._tree._shared_nodes.items()}
+        return (st["ref_counts"].tolist(), st["free_list"].tolist(), st["pending"].tolist(),
+                st["deferred"].tolist(), refs, pool._tree._next_handle_id)
+
+    assert state(a) == state(b)
+    a._allocator.leave_read_section(ra)
+    b._allocator.leave_read_section(rb)
+    assert state(a) == state(b)
