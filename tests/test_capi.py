@@ -98,3 +98,34 @@ def test_tree_hash_python_equals_c():
     c = np.array([N.lib.akv_tree_hash(int(p), int(t)) for p, t in zip(parents, tokens)], np.uint32)
     assert all(tree_hash(int(p), int(t)) == int(h) for p, t, h in zip(parents[:200], tokens[:200], c[:200]))
     np.testing.assert_array_equal(tree_hash_np(parents, tokens), c)
+
+
+def test_host_argument_checks_of_tuning_entry_points():
+    """Arguments the library refuses on the host, before any CUDA call: copy
+    variants past 13, layer-copy variants past 4 and unaligned layer spans,
+    match widths outside {1,2,4,8,16}, run arrays without their entries,
+    fan-out plans deeper than AKV_MAX_FANOUT_LEVELS or without appended
+    blocks.  (Pointers are dummies: nothing is dereferenced.)"""
+    P = 16  # a dummy non-NULL pointer
+    rc = N.lib.akv_copy_blocks_variant(P, 64, 4, P, 1, None, None, 14, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "variant 14" in N.last_error()
+    rc = N.lib.akv_copy_blocks_layers(P, 2, 4096, 4096, 8, P, 1, None, None, 5, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "variant 5" in N.last_error()
+    rc = N.lib.akv_copy_blocks_layers(P, 2, 4100, 4100, 8, P, 1, None, None, 0, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "multiples of 16" in N.last_error()
+    assert N.lib.akv_copy_blocks_layers(P, 0, 4096, 4096, 8, P, 1, None, None, 0, None) == N.AKV_OK
+
+    v = N.AkvTreeView(P, P, P, P, 8, 4, 31, None, None, 0, 0)
+    rc = N.lib.akv_match_prefix_variant(C.byref(v), P, P, 1, 16, P, P, None, None, None, 3, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "chunks=3" in N.last_error()
+    v_runs = N.AkvTreeView(P, P, P, P, 8, 4, 31, P, None, 0, 4)
+    rc = N.lib.akv_match_prefix_variant(C.byref(v_runs), P, P, 1, 16, P, P, None, None, None, 0, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "run_head" in N.last_error()
+    v_mask = N.AkvTreeView(P, P, P, P, 8, 4, 30, None, None, 0, 0)
+    rc = N.lib.akv_match_prefix_variant(C.byref(v_mask), P, P, 1, 16, P, P, None, None, None, 0, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "power of two" in N.last_error()
+
+    rc = N.lib.akv_fanout_tree_plan(P, P, 1, 4, 2, 1, N.MAX_FANOUT_LEVELS + 1, P, P, P, P, P, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "levels" in N.last_error()
+    rc = N.lib.akv_fanout_tree_plan(P, P, 1, 4, 2, 0, 2, P, P, P, P, P, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "append" in N.last_error()
