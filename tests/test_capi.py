@@ -129,3 +129,19 @@ def test_host_argument_checks_of_tuning_entry_points():
     assert rc == N.AKV_ERR_INVALID_ARG and "levels" in N.last_error()
     rc = N.lib.akv_fanout_tree_plan(P, P, 1, 4, 2, 0, 2, P, P, P, P, P, None)
     assert rc == N.AKV_ERR_INVALID_ARG and "append" in N.last_error()
+
+
+def test_host_argument_checks_of_kv_io():
+    """akv_kv_gather / akv_kv_scatter refuse on the host: NULL buffers, a
+    layer past the model, more tokens than the table's blocks hold; an empty
+    gather is a no-op.  (Dummy pointers: nothing is dereferenced.)"""
+    P = 16
+    rc = N.lib.akv_kv_gather(None, 8, 2, 2, 16, 256, 0, P, 1, 4, P, P, None, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "NULL" in N.last_error()
+    rc = N.lib.akv_kv_gather(P, 8, 2, 2, 16, 256, 2, P, 1, 4, P, P, None, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "layer 2 of 2" in N.last_error()
+    rc = N.lib.akv_kv_gather(P, 8, 2, 2, 16, 256, 0, P, 1, 17, P, P, None, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "17 tokens exceed 1 blocks of 16" in N.last_error()
+    assert N.lib.akv_kv_gather(P, 8, 2, 2, 16, 256, 0, P, 1, 0, P, P, None, None) == N.AKV_OK
+    rc = N.lib.akv_kv_scatter(P, 8, 2, 2, 16, 256, 5, P, 1, P, P, 256, 512, None, None)
+    assert rc == N.AKV_ERR_INVALID_ARG
