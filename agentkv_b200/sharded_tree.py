@@ -146,7 +146,10 @@ def query_range(n_queries: int, rank: int, world: int) -> tuple:
 def match_split(sync: TreeReplicaSync, queries, block_size: int, *, gather: bool = True):
     """One batch spread over the ranks: each rank matches its contiguous range
     on its own replica; with gather=True (a collective) every rank returns
-    the whole batch's (node ids, match lengths), else its own range's."""
+    the whole batch's (node ids, match lengths), else its own range's.  On
+    the owner's rank the lookup runs on the owner's DeviceTree directly:
+    call it where the pool's tree is not being changed by another thread
+    (between commits, as after sync())."""
     import torch.distributed as dist
 
     from .device_tree import match_batch
