@@ -104,7 +104,8 @@ class DeviceTree:
         self._replica = False
         self._runs_dirty = True
         self.runs_version = 0  # bumped by every build_runs that rebuilt
-        self._build_ms: Optional[float] = None  # host time of the last build_runs
+        self._full_ms: Optional[float] = None  # host time of the last full build_runs
+        self._patch_ms: Optional[float] = None  # host time of the last incremental one
         self._rent_ms = 0.0  # one-probe-per-hop lookup time since the last change
         self._last_batch_ms = 0.0  # host time of the last batched lookup
         # child structure for the incremental run updates
@@ -400,9 +401,8 @@ class DeviceTree:
             return
         t0 = time.perf_counter()
         n = max(len(self.h_off), self._node_bound)
-        superseded = self._n_entries - self._n_unary
-        if (self._h_run_head is None or superseded > max(4096, self._n_unary)
-                or len(self._runs_touched) > max(64, n // 64)):
+        full = self._next_build_is_full(n)
+        if full:
             self._full_runs(n)
         else:
             self._patch_runs(n)
@@ -412,7 +412,18 @@ class DeviceTree:
         self.d_runs = torch.from_numpy(runs.copy()).to(self.device)
         self._runs_dirty = False
         self.runs_version += 1
-        self._build_ms = (time.perf_counter() - t0) * 1e3
+        ms = (time.perf_counter() - t0) * 1e3
+        if full:
+            self._full_ms = ms
+        else:
+            self._patch_ms = ms
+
+    def _next_build_is_full(self, n: int) -> bool:
+        # a full build the first time, to compact superseded entries, and when
+        # so many nodes changed that rewriting their chains would cost more
+        superseded = self._n_entries - self._n_unary
+        return (self._h_run_head is None or superseded > max(4096, self._n_unary)
+                or len(self._runs_touched) > max(64, n // 64))
 
     def _full_runs(self, n: int) -> None:
         # Array form (no per-node Python): child counts give the unary nodes,
@@ -523,16 +534,21 @@ class DeviceTree:
         they are current; on a replica only when the owner's have arrived.
         With stale runs the rule is ski rental: rebuild once the
         one-probe-per-hop lookups since the tree last changed, counting the
-        coming one at the last batch's time, have cost as much as the last
-        rebuild did.  An incremental rebuild costs tens of microseconds, so a
-        tree that changes between batches normally rebuilds every time; a
-        tree whose last build was a slow full one rents first.  A tree whose
-        runs were never built builds them."""
+        coming one at the last batch's time, have cost as much as the
+        rebuild would — the last build of the kind the next one will be (an
+        incremental one costs tens of microseconds, so a tree that changes
+        between batches normally rebuilds every time; a full one, needed
+        after many changes or to compact, is paid for by renting first).  A
+        tree whose runs were never built builds them."""
         if self._replica:
             return self.d_run_head is not None
-        if not self._runs_dirty or self._build_ms is None:
+        if not self._runs_dirty or self._full_ms is None:
             return True
-        return self._rent_ms + self._last_batch_ms >= self._build_ms
+        if self._next_build_is_full(max(len(self.h_off), self._node_bound)):
+            cost = self._full_ms
+        else:
+            cost = self._patch_ms or 0.0  # no incremental build yet: try one
+        return self._rent_ms + self._last_batch_ms >= cost
 
     def note_lookup(self, ms: float, runs: bool) -> None:
         """Record a batched lookup's host time and whether it used the runs."""

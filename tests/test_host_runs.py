@@ -136,9 +136,10 @@ def test_unary_runs_follow_the_chains():
 def test_run_rebuild_policy():
     """DeviceTree.want_runs: a never-built tree builds; current runs are used;
     after a change the one-probe-per-hop lookups pay rent, the coming one
-    counted at the last batch's time, until it reaches the last rebuild's
-    cost; every change restarts the count; a replica uses runs only while it
-    holds the owner's."""
+    counted at the last batch's time, until it reaches the cost of the
+    rebuild due (the last incremental one, or the last full one when more
+    than 64 nodes changed); every change restarts the count; a replica uses
+    runs only while it holds the owner's."""
     import torch
 
     from agentkv_b200.device_tree import DeviceTree
@@ -148,8 +149,8 @@ def test_run_rebuild_policy():
     t.set_child(0, 5, 1, 2)
     assert t.want_runs()  # never built
     t.build_runs()
-    assert t.want_runs() and t._build_ms is not None
-    t._build_ms = 2.0  # a rebuild costs 2 ms
+    assert t.want_runs() and t._full_ms is not None
+    t._patch_ms = 2.0  # an incremental rebuild costs 2 ms
     t.note_lookup(0.5, True)
     t.set_node(2, t.append_tokens(np.array([7], np.int32)), 1)
     t.set_child(1, 7, 2, 1)
@@ -163,9 +164,15 @@ def test_run_rebuild_policy():
     assert t.want_runs()  # 1.4 + 0.7 >= 2
     t.build_runs()
     assert t.want_runs() and not t._runs_dirty
-    t._build_ms = 0.05  # a cheap incremental rebuild: the next change rebuilds at once
+    t._patch_ms = 0.05  # a cheap incremental rebuild: the next change rebuilds at once
     t.set_child(2, 9, 1, 1)
     assert t.want_runs()
+    # a change touching more than 64 nodes needs a full build: priced at the full build's time
+    t._full_ms = 50.0
+    for p in range(3, 80):
+        t.set_child(p, 5, p + 1, 1)
+    t.note_lookup(1.0, False)
+    assert not t.want_runs()
 
     r = DeviceTree(torch.device("cpu"), node_cap=8, slot_cap=16, token_cap=32)
     r.as_replica()
