@@ -463,3 +463,62 @@ def test_match_prefix_many_equals_one_by_one(golden_dir, monkeypatch):
     a._allocator.leave_read_section(ra)
     b._allocator.leave_read_section(rb)
     assert state(a) == state(b)
+
+
+def test_tree_replica_flow_on_cpu(golden_dir, monkeypatch):
+    """The tree-replica flow of the GPU test (owner pool built through the
+    pool calls, TreeReplicaSync deltas with the owner's runs into a second
+    DeviceTree, lookups on both) run on CPU with the stand-ins: the replica's
+    answers equal the reference's recorded ones and the owner's comparison
+    counts, and its arrays equal the owner's."""
+    import torch
+
+    from agentkv_b200.device_tree import DeviceTree, match_batch
+    from agentkv_b200.sharded_tree import TreeReplicaSync
+
+    g = np.load(golden_dir / "match_small.npz")
+    spec = W.MatchSpec(**json.loads(str(g["spec"])))
+    prefixes = W.match_prefixes(spec)
+    corpus = W.match_sequences(spec, prefixes)
+    n = int(g["total_blocks"])
+    cfg = PoolConfig(total_blocks=n, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1, dtype="float16",
+                     device="meta")
+    pool = _cpu_pool(cfg, torch.zeros((n, 1), dtype=torch.uint8), monkeypatch)
+    owner = pool._tree._dev_tree
+    sync = TreeReplicaSync(owner)
+    replica = DeviceTree(owner.device)
+    replica.as_replica()
+    kinds, runs_seen = [], 0
+    queries = W.match_queries(spec, corpus, prefixes, batch=0, n=len(g["node"]))
+    for i, seq in enumerate(corpus):
+        h = pool.create_root(seq)
+        pool.allocate_blocks(h, -(-len(seq) // 16) - len(pool.get_block_ids(h)))
+        share = (len(seq) // 16) * 16 - h.shared_match_len
+        if share > 0:
+            pool.commit_prefix(h, share)
+        if i % 37 == 0 or i == len(corpus) - 1:
+            owner.build_runs()
+            d = sync.share()
+            if d is not None:
+                kinds.append(d["full"])
+                replica.apply_delta(d)
+                if "run_head" in d:
+                    replica.set_runs(d["run_head"], d["runs"])
+                    runs_seen += 1
+            if i % 111 == 0:
+                n0, l0 = match_batch(owner, queries[:64], 16)
+                n1, l1 = match_batch(replica, queries[:64], 16)
+                np.testing.assert_array_equal(n1, n0)
+                np.testing.assert_array_equal(l1, l0)
+    assert any(kinds) and not all(kinds), kinds
+    assert runs_seen > 1 and replica.d_run_head is not None
+    node, mlen, cmp_ = match_batch(replica, queries, 16, with_compared=True)
+    np.testing.assert_array_equal(node, g["node"])
+    np.testing.assert_array_equal(mlen, g["len"])
+    _, _, cmp_owner = match_batch(owner, queries, 16, with_compared=True)
+    np.testing.assert_array_equal(cmp_, cmp_owner)
+    m = owner.n_tokens
+    assert torch.equal(replica.d_tokens[:m], owner.d_tokens[:m])
+    assert torch.equal(replica.d_slots, owner.d_slots)
+    assert torch.equal(replica.d_off, owner.d_off) and torch.equal(replica.d_len, owner.d_len)
+    assert sync.share() is None
