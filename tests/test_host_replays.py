@@ -522,3 +522,45 @@ def test_tree_replica_flow_on_cpu(golden_dir, monkeypatch):
     assert torch.equal(replica.d_slots, owner.d_slots)
     assert torch.equal(replica.d_off, owner.d_off) and torch.equal(replica.d_len, owner.d_len)
     assert sync.share() is None
+
+
+def test_long_unary_chain_flow_on_cpu(monkeypatch):
+    """The long-chain lookup test of the GPU suite on CPU with the stand-ins:
+    a 70-node unary chain with a branch at depth 100, queries cut at every
+    depth, diverging every third position and running past the end — the
+    oracle's (node, length, comparisons) with the runs and without."""
+    import torch
+
+    from agentkv_b200.device_tree import match_batch
+    from oracle import oracle as O
+
+    bs = 4
+    cfg = PoolConfig(total_blocks=1024, block_size=bs, num_layers=1, num_kv_heads=1, head_dim=4,
+                     dtype="float16", device="meta")
+    pool = _cpu_pool(cfg, torch.zeros((1024, 1), dtype=torch.uint8), monkeypatch)
+    ot = O.OracleTree(O.OracleAllocator(1024), bs)
+    rng = np.random.default_rng(23)
+    seq = rng.integers(0, 50000, size=70 * bs).tolist()
+    branch = seq[:100] + rng.integers(50000, 60000, size=40).tolist()
+    for s in [seq[: bs * k] for k in range(1, 71)] + [branch]:
+        for tree, api in ((pool, "pool"), (ot, "oracle")):
+            hd = tree.create_root(s)
+            need = -(-len(s) // bs)
+            if api == "pool":
+                tree.allocate_blocks(hd, need - len(tree.get_block_ids(hd)))
+            else:
+                while len(tree.get_block_ids(hd)) < need:
+                    tree.allocate_block(hd)
+            tree.commit_prefix(hd, len(s) - hd.shared_match_len)
+    queries = [seq[:n] for n in range(0, len(seq) + 1)] + [seq + [1, 2, 3], branch + [9], branch[:103]]
+    for p in range(0, len(seq), 3):
+        q = list(seq)
+        q[p] = 99999
+        queries.append(q)
+    dev_tree = pool._tree._dev_tree
+    want = [ot.match(q) for q in queries]
+    for runs in (True, False):
+        node, mlen, cmp_ = match_batch(dev_tree, queries, bs, with_compared=True, runs=runs)
+        got = [(int(n) if m else -1, int(m), int(c)) for n, m, c in zip(node, mlen, cmp_)]
+        assert got == [(int(n) if m else -1, int(m), int(c)) for n, m, c in want], runs
+    assert int((dev_tree.d_run_head >= 0).sum()) >= 60
