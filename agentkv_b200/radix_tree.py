@@ -118,6 +118,10 @@ class DualRadixTree:
         self._next_node_id: int = 1
         self._handles: Dict[int, NodeHandle] = {}
         self._next_handle_id: int = 0
+        # get_block_ids results per handle, valid while nothing changed:
+        # every mutating call bumps _version
+        self._version = 0
+        self._ids_cache: Dict[int, Tuple[tuple, List[int]]] = {}
         dev = allocator.device
         self._q_off = torch.zeros(2, dtype=torch.int64, device=dev)
         self._q_out = torch.zeros(4, dtype=torch.int64, device=dev)
@@ -126,6 +130,7 @@ class DualRadixTree:
     # ── create / fork / allocate ──────────────────────────────────────────────
     def create_root(self, tokens: List[int]) -> NodeHandle:
         with self._lock:
+            self._version += 1
             shared_node_id, match_len = self._match_prefix_locked(tokens)
             handle = NodeHandle(
                 handle_id=self._next_handle_id,
@@ -143,6 +148,7 @@ class DualRadixTree:
 
     def fork(self, parent: NodeHandle) -> NodeHandle:
         with self._lock:
+            self._version += 1
             self._validate_handle_locked(parent)
             if parent.residual_blocks:
                 self._alloc.inc_ref_batch([b.block_id for b in parent.residual_blocks])
@@ -163,6 +169,7 @@ class DualRadixTree:
     def fork_many(self, parent: NodeHandle, k: int) -> List[NodeHandle]:
         """k forks of one parent with a single inc_ref launch."""
         with self._lock:
+            self._version += 1
             self._validate_handle_locked(parent)
             if parent.residual_blocks and k > 0:
                 ids = np.tile(np.fromiter((b.block_id for b in parent.residual_blocks), np.int32), k)
@@ -180,6 +187,7 @@ class DualRadixTree:
 
     def allocate_block(self, handle: NodeHandle) -> BlockHandle:
         with self._lock:
+            self._version += 1
             self._validate_handle_locked(handle)
             bh = self._alloc.alloc()
             handle.residual_blocks.append(bh)
@@ -188,6 +196,7 @@ class DualRadixTree:
     def allocate_blocks(self, handle: NodeHandle, n: int) -> List[BlockHandle]:
         """n allocate_block() calls in one launch (one wait for the ids)."""
         with self._lock:
+            self._version += 1
             self._validate_handle_locked(handle)
             if n <= 0:
                 return []
@@ -200,6 +209,7 @@ class DualRadixTree:
     # ── copy-on-write ─────────────────────────────────────────────────────────
     def ensure_mutable_block(self, handle: NodeHandle, block_idx: int) -> BlockHandle:
         with self._lock:
+            self._version += 1
             self._validate_handle_locked(handle)
             bh = handle.residual_blocks[block_idx]
             if "copy_block" in self._alloc.__dict__:
@@ -224,6 +234,7 @@ class DualRadixTree:
         """ensure_mutable_block for many (handle, index) slots, applied in
         order with one launch; returns which requests copied."""
         with self._lock:
+            self._version += 1
             if not requests:
                 return []
             seen = set()
@@ -249,6 +260,7 @@ class DualRadixTree:
     # ── frees / tokens ────────────────────────────────────────────────────────
     def free_block(self, handle: NodeHandle, block: BlockHandle) -> None:
         with self._lock:
+            self._version += 1
             self._validate_handle_locked(handle)
             if block not in handle.residual_blocks:
                 raise ValueError(
@@ -264,6 +276,7 @@ class DualRadixTree:
 
     def free(self, handle: NodeHandle) -> None:
         with self._lock:
+            self._version += 1
             self._validate_handle_locked(handle)
             if handle.is_freed:
                 raise ValueError(f"double-free of handle {handle.handle_id}")
@@ -275,10 +288,12 @@ class DualRadixTree:
                 self._alloc.dec_ref_batch(np.asarray(decs, np.int32))
             handle.is_freed = True
             del self._handles[handle.handle_id]
+            self._ids_cache.pop(handle.handle_id, None)
 
     def free_many(self, handles: Sequence[NodeHandle]) -> None:
         """free() of several handles, in order, with one dec_ref launch."""
         with self._lock:
+            self._version += 1
             decs: List[int] = []
             for h in handles:
                 self._validate_handle_locked(h)
@@ -291,6 +306,7 @@ class DualRadixTree:
                     self._dec_shared_ref_locked(h.shared_node_id, decs)
                 h.is_freed = True
                 del self._handles[h.handle_id]
+                self._ids_cache.pop(h.handle_id, None)
             if decs:
                 self._alloc.dec_ref_batch(np.asarray(decs, np.int32))
 
@@ -299,6 +315,7 @@ class DualRadixTree:
         epoch_token = self._alloc.enter_read_section()
         try:
             with self._lock:
+                self._version += 1
                 node_id, match_len = self._match_prefix_locked(tokens)
                 if node_id == INVALID_NODE_ID or match_len == 0:
                     return None, 0
@@ -325,6 +342,7 @@ class DualRadixTree:
         epoch_token = self._alloc.enter_read_section()
         try:
             with self._lock:
+                self._version += 1
                 node, mlen = match_batch(self._dev_tree, queries, self._cfg.block_size)
                 out: List[Tuple[Optional[NodeHandle], int]] = []
                 for q, nid, m in zip(queries, node.tolist(), mlen.tolist()):
@@ -350,6 +368,7 @@ class DualRadixTree:
 
     def commit_prefix(self, handle: NodeHandle, length: int) -> None:
         with self._lock:
+            self._version += 1
             self._validate_handle_locked(handle)
             bs = self._cfg.block_size
             if length % bs != 0:
@@ -377,12 +396,19 @@ class DualRadixTree:
     def get_block_ids(self, handle: NodeHandle) -> List[int]:
         with self._lock:
             self._validate_handle_locked(handle)
+            # the walk up the shared chain is repeated only after a change
+            # (a model layer's update asks once per layer)
+            key = (self._version, handle.shared_node_id, id(handle.residual_blocks), len(handle.residual_blocks))
+            hit = self._ids_cache.get(handle.handle_id)
+            if hit is not None and hit[0] == key:
+                return list(hit[1])
             ids: List[int] = []
             if handle.shared_node_id != INVALID_NODE_ID:
                 for node in self._collect_shared_chain_locked(handle.shared_node_id):
                     ids.extend(bh.block_id for bh in node.blocks)
             ids.extend(bh.block_id for bh in handle.residual_blocks)
-            return ids
+            self._ids_cache[handle.handle_id] = (key, ids)
+            return list(ids)
 
     def stats(self) -> dict:
         with self._lock:

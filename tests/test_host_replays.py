@@ -564,3 +564,53 @@ def test_long_unary_chain_flow_on_cpu(monkeypatch):
         got = [(int(n) if m else -1, int(m), int(c)) for n, m, c in zip(node, mlen, cmp_)]
         assert got == [(int(n) if m else -1, int(m), int(c)) for n, m, c in want], runs
     assert int((dev_tree.d_run_head >= 0).sum()) >= 60
+
+
+def test_block_table_cache_follows_changes(monkeypatch):
+    """get_block_ids answers from its per-handle cache only while nothing
+    changed: after allocations, copy-on-write, commits (edge splits among
+    them), forks and frees it returns the freshly walked table, equal to
+    the oracle's, and callers get their own list."""
+    import torch
+
+    from oracle import oracle as O
+
+    cfg = PoolConfig(total_blocks=256, block_size=4, num_layers=1, num_kv_heads=1, head_dim=4,
+                     dtype="float16", device="meta")
+    pool = _cpu_pool(cfg, torch.zeros((256, 1), dtype=torch.uint8), monkeypatch)
+    ot = O.OracleTree(O.OracleAllocator(256, cfg.epoch_interval), 4)
+    rng = np.random.default_rng(12)
+    live = []
+    for step in range(300):
+        op = int(rng.integers(0, 6))
+        if op == 0 or len(live) < 2:
+            toks = rng.integers(0, 6, size=int(rng.integers(0, 24))).tolist()
+            live.append((pool.create_root(toks), ot.create_root(toks)))
+        elif op == 1:
+            i = int(rng.integers(0, len(live)))
+            live.append((pool.fork(live[i][0]), ot.fork(live[i][1])))
+        elif op == 2:
+            h, o = live[int(rng.integers(0, len(live)))]
+            pool.allocate_block(h)
+            ot.allocate_block(o)
+        elif op == 3:
+            h, o = live[int(rng.integers(0, len(live)))]
+            if h.residual_blocks:
+                k = int(rng.integers(0, len(h.residual_blocks)))
+                pool.ensure_mutable_block(h, k)
+                ot.ensure_mutable_block(o, k)
+        elif op == 4:
+            h, o = live[int(rng.integers(0, len(live)))]
+            n = min(len(h.residual_blocks), (len(h.tokens) - h.shared_match_len) // 4)
+            if n > 0:
+                pool.commit_prefix(h, 4 * n)
+                ot.commit_prefix(o, 4 * n)
+        else:
+            h, o = live.pop(int(rng.integers(0, len(live))))
+            pool.free(h)
+            ot.free(o)
+        for h, o in live:
+            a = pool.get_block_ids(h)
+            assert a == ot.get_block_ids(o), step
+            a.append(-1)  # the caller's list is its own
+            assert pool.get_block_ids(h) == ot.get_block_ids(o), step
