@@ -45,6 +45,9 @@ class AgentKVCache(DynamicCache):
         self.value_cache = []
         self._table: Optional[list] = None
         self._table_dev: Optional[torch.Tensor] = None
+        self._table_version = 0  # bumped whenever _table_dev is replaced
+        self._slots_key: Optional[tuple] = None  # (first new token, count, table version) of _slots_dev
+        self._slots_dev: Optional[torch.Tensor] = None
 
     def get_seq_length(self, layer_idx: Optional[int] = 0) -> int:
         return self._seen_tokens
@@ -53,6 +56,7 @@ class AgentKVCache(DynamicCache):
         if self._table != ids:
             self._table = list(ids)
             self._table_dev = torch.tensor(ids, dtype=torch.int32).to(self.pool._allocator._kv_data.device)
+            self._table_version += 1
         return self._table_dev
 
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
@@ -81,11 +85,17 @@ class AgentKVCache(DynamicCache):
         ids = pool.get_block_ids(h)
         kv = pool._allocator._kv_data
         st = pool._allocator._status
+        table = self._device_table(ids)
         if n_new:
-            slots = np.asarray(ids, np.int64)[blk] * bs + tok % bs
-            K.kv_scatter(kv, torch.from_numpy(slots.astype(np.int32)), layer_idx, key_states, value_states,
-                         status=st)
-        out_k, out_v = K.kv_gather(kv, self._device_table(ids), layer_idx, self._next_seen_tokens, status=st)
+            # the new tokens' slots are the same for every layer of a step:
+            # computed and uploaded once
+            key = (self._seen_tokens, n_new, self._table_version)
+            if self._slots_key != key:
+                slots = np.asarray(ids, np.int64)[blk] * bs + tok % bs
+                self._slots_dev = torch.from_numpy(slots.astype(np.int32)).to(kv.device)
+                self._slots_key = key
+            K.kv_scatter(kv, self._slots_dev, layer_idx, key_states, value_states, status=st)
+        out_k, out_v = K.kv_gather(kv, table, layer_idx, self._next_seen_tokens, status=st)
         if layer_idx == pool.config.num_layers - 1:
             self._seen_tokens = self._next_seen_tokens
         return out_k, out_v
