@@ -1023,10 +1023,56 @@ def hf_case(args) -> None:
                      "gbs_algorithmic": round(alg / (ms / 1e3) / 1e9, 1)}
     peak, peak_kind = measured_peak()
     res["kv_gather"]["frac"] = round(res["kv_gather"]["gbs_algorithmic"] / peak, 4)
+    del pool
+    res["update_e2e"] = hf_update_figure(n_blocks, n_tok, args.steps, args.warmup)
     print(json.dumps({"case": "hf_cache_gather", "tokens": n_tok, "layers": L, "heads": H, "head_dim": D,
                       "peak_gbs": peak, "peak_source": peak_kind, **res,
                       "speedup": round(res["torch_index_permute"]["ms_per_decode_step"] /
                                        res["kv_gather"]["ms_per_decode_step"], 2)}), flush=True)
+
+
+def hf_update_figure(n_blocks: int, n_tok: int, steps: int, warmup: int) -> dict:
+    """Decode steps through the public call, AgentKVCache.update on every
+    layer (block allocation and copy-on-write checks on layer 0, the new
+    token's rows written, the layer's K/V assembled): an agent forked from a
+    committed n_tok-token prompt held as a 16-node shared chain, one new
+    token per step, host logic included."""
+    import torch
+
+    from agentkv_b200 import AgentKVPool, PoolConfig
+    from agentkv_b200.hf_cache import AgentKVCache
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    _, bs, L, H, D, _ = W.LLAMA3_8B_GEOMETRY
+    pool = AgentKVPool(config=PoolConfig(total_blocks=n_blocks, block_size=bs, num_layers=L, num_kv_heads=H,
+                                         head_dim=D, dtype="bfloat16", device="cuda"))
+    root = pool.create_root(list(range(n_tok)))
+    pool.allocate_blocks(root, n_tok // bs)
+    for _ in range(16):
+        pool.commit_prefix(root, n_tok // 16)
+    cache = AgentKVCache(pool, pool.fork(root))
+    k = torch.randn((1, H, 1, D), generator=torch.Generator(device=dev).manual_seed(8), device=dev,
+                    dtype=torch.float32).to(torch.bfloat16)
+
+    def step():
+        for layer in range(L):
+            cache.update(k, k, layer)
+
+    for _ in range(max(3, warmup)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) / steps
+    ms = e0.elapsed_time(e1) / steps
+    return {"ms_per_decode_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / L, 2),
+            "host_wall_ms_per_step": round(wall * 1e3, 4), "tokens_at_start": n_tok,
+            "api": "AgentKVCache.update, every layer, one new token per step"}
 
 
 def match_traffic(n_seqs: int):
