@@ -592,13 +592,43 @@ def match_stress(spec: W.MatchSpec, n_queries: int) -> dict:
     }
 
 
+def serving() -> dict:
+    """The serving-lifecycle schedule of tests/serving_pattern.py (the
+    SGLang adapter's call pattern) played on the reference pool."""
+    sys.path.insert(0, str(OUT.parent))
+    from serving_pattern import serve
+
+    pool = AgentKVPool(config=PoolConfig(total_blocks=512, block_size=16, num_layers=1, num_kv_heads=1,
+                                         head_dim=8, dtype="float16", device="cpu"))
+
+    class API:
+        def __getattr__(self, name):
+            return getattr(pool, name)
+
+        def tree_match_prefix(self, tokens):
+            return pool._tree.match_prefix(tokens)
+
+        def tree_free(self, h):
+            pool._tree.free(h)
+
+        @property
+        def free_blocks(self):
+            return pool.free_blocks
+
+        @property
+        def allocated_blocks(self):
+            return pool.allocated_blocks
+
+    return {"obs": json.loads(json.dumps(serve(API())))}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-full-match", action="store_true")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
     todo = set(args.only.split(",")) if args.only else {"alloc", "tree", "quick", "tot", "react", "hf", "stress",
-                                                                   "copy", "match", "match_full"}
+                                                                   "copy", "match", "match_full", "serving"}
     if "alloc" in todo:
         for seed, (n, iv, nops) in {1: (48, 5, 700), 2: (32, 3, 700), 3: (64, 64, 900), 4: (16, 2, 500)}.items():
             np.savez_compressed(OUT / f"alloc_trace_{seed}.npz", **alloc_trace(seed, n, iv, nops))
@@ -629,6 +659,9 @@ def main() -> None:
     if "copy" in todo:
         (OUT / "copy_zero.json").write_text(json.dumps(copy_zero(), indent=0))
         print("copy/zero")
+    if "serving" in todo:
+        (OUT / "serving.json").write_text(json.dumps(serving()))
+        print("serving")
     if "match" in todo:
         small = W.MatchSpec(n_sequences=600, n_queries=256)
         np.savez_compressed(OUT / "match_small.npz", **match_stress(small, 256))

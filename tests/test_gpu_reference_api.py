@@ -400,7 +400,7 @@ def test_stress_shadow_model(seed, n_ops):
     assert a.free_count == 512, "leak"
 
 
-def test_serving_lifecycle_equals_oracle():
+def test_serving_lifecycle_equals_oracle(golden_dir):
     """The prefix-cache serving lifecycle a serving engine's radix-cache
     adapter drives (tests/serving_pattern.py: lookups adopted as handles,
     appends, page allocations, commits, finishes, aborts, epoch advances)
@@ -413,3 +413,7 @@ def test_serving_lifecycle_equals_oracle():
     got = serve(PoolServeAPI(pool))
     want = serve(OracleServeAPI(512, 16))
     assert got == want
+    # and what the reference pool observed (tests/golden/serving.json)
+    import json
+
+    assert json.loads(json.dumps(got)) == json.loads((golden_dir / "serving.json").read_text())["obs"]

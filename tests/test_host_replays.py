@@ -342,7 +342,7 @@ def test_tot_batched_host_logic_replays_reference(golden_dir, monkeypatch):
     np.testing.assert_array_equal(st["free_list"], g["free_freed"])
 
 
-def test_serving_lifecycle_on_the_oracle():
+def test_serving_lifecycle_on_the_oracle(golden_dir):
     """The serving-lifecycle schedule (tests/serving_pattern.py) on the
     oracle: deterministic, with page hits that return the committed blocks,
     misses, aborts, finishes and evictions; the allocated count it reads
@@ -351,6 +351,8 @@ def test_serving_lifecycle_on_the_oracle():
 
     a = serve(OracleServeAPI(512, 16))
     assert a == serve(OracleServeAPI(512, 16))
+    # pinned: the reference pool observed exactly this (tests/golden/serving.json)
+    assert json.loads(json.dumps(a)) == json.loads((golden_dir / "serving.json").read_text())["obs"]
     kinds = {o[0] for o in a}
     assert {"hit", "miss", "abort", "finish", "evict"} <= kinds, kinds
     assert sum(1 for o in a if o[0] == "hit") >= 10
@@ -363,7 +365,7 @@ def test_serving_lifecycle_on_the_oracle():
     assert a[-1] == ("end", api.free_blocks, api.allocated_blocks)
 
 
-def test_serving_lifecycle_host_logic_equals_oracle(monkeypatch):
+def test_serving_lifecycle_host_logic_equals_oracle(golden_dir, monkeypatch):
     """The serving-lifecycle schedule through the package's pool logic on CPU
     (oracle allocator, tree kernel model) observes what the oracle's own
     tree observes: hits, block ids, finishes, aborts, counters."""
@@ -374,7 +376,9 @@ def test_serving_lifecycle_host_logic_equals_oracle(monkeypatch):
     cfg = PoolConfig(total_blocks=512, block_size=16, num_layers=1, num_kv_heads=1, head_dim=8,
                      dtype="float16", device="meta")
     pool = _cpu_pool(cfg, torch.zeros((512, 1), dtype=torch.uint8), monkeypatch)
-    assert serve(PoolServeAPI(pool)) == serve(OracleServeAPI(512, 16))
+    got = serve(PoolServeAPI(pool))
+    assert got == serve(OracleServeAPI(512, 16))
+    assert json.loads(json.dumps(got)) == json.loads((golden_dir / "serving.json").read_text())["obs"]
 
 
 def test_match_stress_tree_host_logic_replays_reference(golden_dir, monkeypatch):
