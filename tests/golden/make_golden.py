@@ -622,13 +622,30 @@ def serving() -> dict:
     return {"obs": json.loads(json.dumps(serve(API())))}
 
 
+def match_scenarios() -> dict:
+    """(node, length) of the reference's _match_prefix_locked on every query
+    of tests/match_scenarios.py's hard tree shapes."""
+    sys.path.insert(0, str(OUT.parent))
+    from match_scenarios import SCENARIOS, build
+
+    out = {}
+    for name, make in SCENARIOS.items():
+        sc = make()
+        pool = AgentKVPool(config=PoolConfig(total_blocks=1024, block_size=sc["block_size"], num_layers=1,
+                                             num_kv_heads=1, head_dim=4, dtype="float16", device="cpu"))
+        build(pool, sc, pool.allocate_block)
+        out[name] = [list(pool._tree._match_prefix_locked(q)) for q in sc["queries"]]
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-full-match", action="store_true")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
     todo = set(args.only.split(",")) if args.only else {"alloc", "tree", "quick", "tot", "react", "hf", "stress",
-                                                                   "copy", "match", "match_full", "serving"}
+                                                                   "copy", "match", "match_full", "serving",
+                                                                   "match_scenarios"}
     if "alloc" in todo:
         for seed, (n, iv, nops) in {1: (48, 5, 700), 2: (32, 3, 700), 3: (64, 64, 900), 4: (16, 2, 500)}.items():
             np.savez_compressed(OUT / f"alloc_trace_{seed}.npz", **alloc_trace(seed, n, iv, nops))
@@ -659,6 +676,9 @@ def main() -> None:
     if "copy" in todo:
         (OUT / "copy_zero.json").write_text(json.dumps(copy_zero(), indent=0))
         print("copy/zero")
+    if "match_scenarios" in todo:
+        (OUT / "match_scenarios.json").write_text(json.dumps(match_scenarios()))
+        print("match scenarios")
     if "serving" in todo:
         (OUT / "serving.json").write_text(json.dumps(serving()))
         print("serving")

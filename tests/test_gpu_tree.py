@@ -473,3 +473,21 @@ def test_match_prefix_many_equals_one_by_one(golden_dir):
         {k: n.ref_count for k, n in b._tree._shared_nodes.items()}
     np.testing.assert_array_equal(a._allocator.free_list(), b._allocator.free_list())
     np.testing.assert_array_equal(a._allocator._ref_counts.cpu().numpy(), b._allocator._ref_counts.cpu().numpy())
+
+
+@pytest.mark.parametrize("name", ["colliding", "long_chain"])
+def test_match_scenarios_match_reference(golden_dir, name):
+    """The hard lookup shapes of tests/match_scenarios.py on the device pool,
+    with the unary-chain runs and with one probe per hop: the reference's
+    recorded (node, length) per query."""
+    from agentkv_b200.device_tree import match_batch
+    from match_scenarios import SCENARIOS, build
+
+    want = json.loads((golden_dir / "match_scenarios.json").read_text())[name]
+    sc = SCENARIOS[name]()
+    pool = AgentKVPool(config=PoolConfig(total_blocks=1024, block_size=sc["block_size"], num_layers=1,
+                                         num_kv_heads=1, head_dim=4, dtype="float16", device="meta"))
+    build(pool, sc, pool.allocate_block)
+    for runs in (True, False):
+        node, mlen = match_batch(pool._tree._dev_tree, sc["queries"], sc["block_size"], runs=runs)
+        assert [[int(n) if m else -1, int(m)] for n, m in zip(node, mlen)] == want, runs

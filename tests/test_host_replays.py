@@ -618,3 +618,25 @@ def test_block_table_cache_follows_changes(monkeypatch):
             assert a == ot.get_block_ids(o), step
             a.append(-1)  # the caller's list is its own
             assert pool.get_block_ids(h) == ot.get_block_ids(o), step
+
+
+@pytest.mark.parametrize("name", ["colliding", "long_chain"])
+def test_match_scenarios_host_logic(golden_dir, name, monkeypatch):
+    """The hard lookup shapes through the package's pool on CPU (tree kernels
+    as their CPU model), with the unary-chain runs and with one probe per
+    hop: the reference's recorded (node, length) per query."""
+    import torch
+
+    from agentkv_b200.device_tree import match_batch
+    from match_scenarios import SCENARIOS, build
+
+    want = json.loads((golden_dir / "match_scenarios.json").read_text())[name]
+    sc = SCENARIOS[name]()
+    cfg = PoolConfig(total_blocks=1024, block_size=sc["block_size"], num_layers=1, num_kv_heads=1, head_dim=4,
+                     dtype="float16", device="meta")
+    pool = _cpu_pool(cfg, torch.zeros((1024, 1), dtype=torch.uint8), monkeypatch)
+    build(pool, sc, pool.allocate_block)
+    for runs in (True, False):
+        node, mlen = match_batch(pool._tree._dev_tree, sc["queries"], sc["block_size"], runs=runs)
+        got = [[int(n) if m else -1, int(m)] for n, m in zip(node, mlen)]
+        assert got == want, runs

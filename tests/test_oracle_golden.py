@@ -337,3 +337,17 @@ def test_oracle_match_small(golden_dir):
     np.testing.assert_array_equal(loop[:, 0], g["node"])
     np.testing.assert_array_equal(loop[:, 1], g["len"])
     np.testing.assert_array_equal(loop[:, 2], cmp_)
+
+
+@pytest.mark.parametrize("name", ["colliding", "long_chain"])
+def test_oracle_match_scenarios(golden_dir, name):
+    """The oracle's match on the hard tree shapes of tests/match_scenarios.py
+    (a long probe chain of colliding keys, a 70-node unary chain with a
+    branch) equals the reference's recorded (node, length) per query."""
+    from match_scenarios import SCENARIOS, build
+
+    want = json.loads((golden_dir / "match_scenarios.json").read_text())[name]
+    sc = SCENARIOS[name]()
+    ot = O.OracleTree(O.OracleAllocator(1024), sc["block_size"])
+    build(ot, sc, ot.allocate_block)
+    assert [list(ot.match(q)[:2]) for q in sc["queries"]] == want
