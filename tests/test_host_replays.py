@@ -138,6 +138,54 @@ def test_tree_host_logic_replays_reference_stress_runner(golden_dir, seed, monke
     np.testing.assert_array_equal(st["free_list"], g["free"])
 
 
+def _kv_scatter(kv, slots, layer, k, v, status=None):
+    """akv_kv_scatter's contract in torch indexing: token i's rows of every
+    head to slot slots[i] (block * block_size + position) of `layer`."""
+    bs = kv.shape[4]
+    for i, slot in enumerate(slots.tolist()):
+        kv[slot // bs, layer, 0, :, slot % bs] = k[0, :, i].to(kv.dtype)
+        kv[slot // bs, layer, 1, :, slot % bs] = v[0, :, i].to(kv.dtype)
+
+
+def _kv_gather(kv, table, layer, n_tokens, status=None):
+    """akv_kv_gather's contract: the table's blocks of `layer` as contiguous
+    [1, heads, tokens, head_dim] K and V, cut to n_tokens."""
+    x = kv[table.long(), layer]  # [blocks, 2, H, bs, D]
+    nb, _, h, bs, d = x.shape
+    k = x[:, 0].permute(1, 0, 2, 3).reshape(1, h, nb * bs, d)[:, :, :n_tokens]
+    v = x[:, 1].permute(1, 0, 2, 3).reshape(1, h, nb * bs, d)[:, :, :n_tokens]
+    return k.contiguous(), v.contiguous()
+
+
+def _hf_cpu_pool(spec, monkeypatch):
+    import torch
+
+    from agentkv_b200 import kernels as K
+
+    monkeypatch.setattr(K, "kv_scatter", _kv_scatter)
+    monkeypatch.setattr(K, "kv_gather", _kv_gather)
+    cfg = PoolConfig(total_blocks=spec.total_blocks, block_size=spec.block_size, num_layers=spec.num_layers,
+                     num_kv_heads=spec.num_kv_heads, head_dim=spec.head_dim, dtype=spec.dtype, device="meta")
+    kv = torch.zeros((spec.total_blocks, spec.num_layers, 2, spec.num_kv_heads, spec.block_size, spec.head_dim),
+                     dtype=getattr(torch, spec.dtype))
+    pool = _cpu_pool(cfg, kv, monkeypatch)
+    pool._allocator._status = torch.zeros(8, dtype=torch.int32)
+    return pool, kv
+
+
+def _hf_session(spec, pool, cache_cls, to_tensor):
+    outs, keys = [], []
+
+    def on_output(e, layer, ok, ov):
+        ok = ok.numpy() if hasattr(ok, "numpy") else ok
+        ov = ov.numpy() if hasattr(ov, "numpy") else ov
+        keys.append((e, layer, ok.shape[2]))
+        outs.append(np.concatenate([ok.reshape(-1), ov.reshape(-1)]))
+
+    caches = W.hf_run(spec, pool, cache_cls, to_tensor, on_output)
+    return caches, keys, np.concatenate(outs)
+
+
 def test_hf_cache_host_logic_replays_reference_session(golden_dir, monkeypatch):
     """The package's HuggingFace cache logic (agentkv_b200/hf_cache.py: block
     allocation on layer 0, copy-on-write checks in the reference's order,
@@ -148,56 +196,45 @@ def test_hf_cache_host_logic_replays_reference_session(golden_dir, monkeypatch):
     byte as recorded."""
     import torch
 
-    from agentkv_b200 import _native as N
-    from agentkv_b200 import device_tree as DT
-    from agentkv_b200 import kernels as K
     from agentkv_b200.hf_cache import AgentKVCache
-    from agentkv_b200.pool import AgentKVPool
-    from agentkv_b200.radix_tree import DualRadixTree
-    from oracle_slab import OracleSlab
-    from tree_kernel_model import TreeKernelModel
 
-    def kv_scatter(kv, slots, layer, k, v, status=None):
-        bs = kv.shape[4]
-        for i, slot in enumerate(slots.tolist()):
-            kv[slot // bs, layer, 0, :, slot % bs] = k[0, :, i].to(kv.dtype)
-            kv[slot // bs, layer, 1, :, slot % bs] = v[0, :, i].to(kv.dtype)
-
-    def kv_gather(kv, table, layer, n_tokens, status=None):
-        x = kv[table.long(), layer]  # [blocks, 2, H, bs, D]
-        nb, _, h, bs, d = x.shape
-        k = x[:, 0].permute(1, 0, 2, 3).reshape(1, h, nb * bs, d)[:, :, :n_tokens]
-        v = x[:, 1].permute(1, 0, 2, 3).reshape(1, h, nb * bs, d)[:, :, :n_tokens]
-        return k.contiguous(), v.contiguous()
-
-    monkeypatch.setattr(N, "lib", TreeKernelModel(N.lib))
-    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
-    monkeypatch.setattr(K, "kv_scatter", kv_scatter)
-    monkeypatch.setattr(K, "kv_gather", kv_gather)
     g = np.load(golden_dir / "hf_session.npz")
     spec = W.HFSpec(**json.loads(str(g["spec"])))
-    cfg = PoolConfig(total_blocks=spec.total_blocks, block_size=spec.block_size, num_layers=spec.num_layers,
-                     num_kv_heads=spec.num_kv_heads, head_dim=spec.head_dim, dtype=spec.dtype, device="meta")
-    kv = torch.zeros((spec.total_blocks, spec.num_layers, 2, spec.num_kv_heads, spec.block_size, spec.head_dim),
-                     dtype=getattr(torch, spec.dtype))
-    pool = object.__new__(AgentKVPool)
-    pool._cfg = cfg
-    pool._allocator = OracleSlab(kv, cfg.epoch_interval)
-    pool._allocator._status = torch.zeros(8, dtype=torch.int32)
-    pool._tree = DualRadixTree(pool._allocator, cfg)
-    outs, keys = [], []
-
-    def on_output(e, layer, ok, ov):
-        keys.append((e, layer, ok.shape[2]))
-        outs.append(np.concatenate([ok.numpy().reshape(-1), ov.numpy().reshape(-1)]))
-
-    caches = W.hf_run(spec, pool, AgentKVCache, torch.from_numpy, on_output)
+    pool, kv = _hf_cpu_pool(spec, monkeypatch)
+    caches, keys, outs = _hf_session(spec, pool, AgentKVCache, torch.from_numpy)
     np.testing.assert_array_equal(np.asarray(keys), g["out_keys"])
-    assert np.concatenate(outs).tobytes() == g["outs"].tobytes()
+    assert outs.tobytes() == g["outs"].tobytes()
     tables = np.concatenate([np.asarray(pool.get_block_ids(c.handle), np.int32) for c in caches])
     np.testing.assert_array_equal(tables, g["tables"])
     assert [c.get_seq_length() for c in caches] == g["seen"].tolist()
     assert kv.numpy().tobytes() == g["pool"].tobytes()
+
+
+@pytest.mark.parametrize("spec", [
+    W.HFSpec(total_blocks=512, block_size=16, num_layers=4, num_kv_heads=8, head_dim=128, prompt=200,
+             commit=192, forks=3, steps=8, seed=8),
+    W.HFSpec(total_blocks=256, block_size=8, num_layers=3, num_kv_heads=2, head_dim=12, prompt=37,
+             commit=32, forks=3, steps=12, seed=9),
+])
+def test_hf_cache_host_logic_equals_oracle(spec, monkeypatch):
+    """Larger HF sessions (200- and 37-token prompts, commits, forks decoding
+    one and three tokens per step) through the package's cache logic on CPU
+    equal the oracle's cache: outputs, tables and pool bytes."""
+    import torch
+
+    from agentkv_b200.hf_cache import AgentKVCache
+    from oracle import oracle as O
+
+    pool, kv = _hf_cpu_pool(spec, monkeypatch)
+    caches, keys, outs = _hf_session(spec, pool, AgentKVCache, torch.from_numpy)
+    opool = O.OracleKVPool(spec.total_blocks, spec.block_size, spec.num_layers, spec.num_kv_heads,
+                           spec.head_dim, spec.dtype)
+    ocaches, okeys, oouts = _hf_session(spec, opool, O.OracleKVCache, lambda a: a)
+    assert keys == okeys
+    assert outs.tobytes() == oouts.tobytes()
+    for c, oc in zip(caches, ocaches):
+        assert pool.get_block_ids(c.handle) == opool.get_block_ids(oc.handle)
+    assert kv.numpy().tobytes() == opool.kv.tobytes()
 
 
 def test_react_trace_host_logic_replays_reference(golden_dir, monkeypatch):
