@@ -34,7 +34,7 @@ import torch
 
 from .allocator import BlockHandle, SlabAllocator
 from .config import PoolConfig
-from .device_tree import DeviceTree, longest_first, match_batch, pack_queries  # noqa: F401
+from .device_tree import DeviceTree, QueryStage, longest_first, match_batch, pack_queries  # noqa: F401
 
 ROOT_NODE_ID: int = 0
 INVALID_NODE_ID: int = -1
@@ -123,9 +123,8 @@ class DualRadixTree:
         self._version = 0
         self._ids_cache: Dict[int, Tuple[tuple, List[int]]] = {}
         dev = allocator.device
-        self._q_off = torch.zeros(2, dtype=torch.int64, device=dev)
         self._q_out = torch.zeros(4, dtype=torch.int64, device=dev)
-        self._h_q = torch.zeros(4, dtype=torch.int64, pin_memory=dev.type == "cuda")
+        self._one_stage = QueryStage(dev)  # single lookups (create_root, match_prefix)
 
     # ── create / fork / allocate ──────────────────────────────────────────────
     def create_root(self, tokens: List[int]) -> NodeHandle:
@@ -425,13 +424,11 @@ class DualRadixTree:
         t = _as_i32(tokens)
         if len(t) == 0:
             return INVALID_NODE_ID, 0
-        dev = self._alloc.device
-        tok = torch.from_numpy(t).to(dev, non_blocking=False)
-        self._h_q[0] = 0
-        self._h_q[1] = len(t)
-        self._q_off.copy_(self._h_q[:2], non_blocking=True)
+        # the tokens go up through a pinned stage of its own (an asynchronous
+        # copy); the answer's read-back is the call's one wait
+        tok, q_off, _ = self._one_stage.pack([t])
         out = self._q_out.view(torch.int32)
-        self._dev_tree.match(tok, self._q_off, 1, self._cfg.block_size, out[0:1], out[1:2], None)
+        self._dev_tree.match(tok, q_off, 1, self._cfg.block_size, out[0:1], out[1:2], None)
         res = out[:2].cpu()
         self._dev_tree.check()
         node, mlen = int(res[0]), int(res[1])
