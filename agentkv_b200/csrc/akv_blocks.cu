@@ -122,8 +122,7 @@ k_zero_vec(char* __restrict__ pool, int64_t bpb, int32_t total, const int32_t* _
 }
 
 // ── bulk-async (TMA engine) kernels ────────────────────────────────────────
-constexpr int kBulkChunk = 32 * 1024;  // bytes per bulk copy
-constexpr int kBulkStages = 6;         // chunks in flight per CTA (192 KiB smem)
+constexpr int kBulkChunk = 32 * 1024;  // bytes per bulk store of the zero kernel
 
 AKV_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
