@@ -35,10 +35,22 @@ except ImportError:  # transformers absent: the class still works on its own
 
 
 class AgentKVCache(DynamicCache):
-    def __init__(self, pool: AgentKVPool, handle: NodeHandle) -> None:
+    def __init__(self, pool: AgentKVPool, handle: NodeHandle, *, append_only: bool = False) -> None:
+        """append_only=True keeps each layer's assembled K/V between updates
+        and appends the new tokens' rows to it instead of assembling the
+        whole sequence from the pool again: O(new tokens) per update.  The
+        bytes are the same as long as the agent's blocks change only through
+        this cache's updates (the pool still receives every row, so forks,
+        commits and to_legacy_cache see them); a caller that writes into the
+        agent's blocks by other means must leave it off (the default).  The
+        returned K/V are then views of the held buffers (stride along the
+        tokens is the buffer's capacity), which hold a layer's K and V
+        besides the pool's copy, as HF's own dynamic cache does."""
         super().__init__()
         self.pool = pool
         self.handle = handle
+        self.append_only = append_only
+        self._mirror: Dict[int, list] = {}  # layer -> [K buffer, V buffer, tokens held]
         self._seen_tokens = len(self.handle.tokens)
         self._next_seen_tokens = self._seen_tokens
         self.key_cache = []
@@ -95,13 +107,39 @@ class AgentKVCache(DynamicCache):
                 self._slots_dev = torch.from_numpy(slots.astype(np.int32)).to(kv.device)
                 self._slots_key = key
             K.kv_scatter(kv, self._slots_dev, layer_idx, key_states, value_states, status=st)
-        out_k, out_v = K.kv_gather(kv, table, layer_idx, self._next_seen_tokens, status=st)
+        if self.append_only:
+            out_k, out_v = self._append(layer_idx, key_states, value_states, table)
+        else:
+            out_k, out_v = K.kv_gather(kv, table, layer_idx, self._next_seen_tokens, status=st)
         if layer_idx == pool.config.num_layers - 1:
             self._seen_tokens = self._next_seen_tokens
         return out_k, out_v
 
+    def _append(self, layer: int, key_states: torch.Tensor, value_states: torch.Tensor,
+                table: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """The layer's K/V for append_only: the held buffers plus this update's
+        rows when they hold exactly the tokens before it, else assembled from
+        the pool (first update, or after a fork made a new cache)."""
+        kv = self.pool._allocator._kv_data
+        seen, nxt = self._seen_tokens, self._next_seen_tokens
+        m = self._mirror.get(layer)
+        if m is None or m[2] != seen or m[0].shape[2] < nxt:
+            k, v = K.kv_gather(kv, table, layer, nxt, status=self.pool._allocator._status)
+            cap = max(nxt + 256, 2 * nxt)  # room for the next updates' rows
+            kb = torch.empty((1, k.shape[1], cap, k.shape[3]), dtype=k.dtype, device=k.device)
+            vb = torch.empty_like(kb)
+            kb[:, :, :nxt].copy_(k)
+            vb[:, :, :nxt].copy_(v)
+            m = self._mirror[layer] = [kb, vb, nxt]
+        else:
+            kb, vb = m[0], m[1]
+            kb[:, :, seen:nxt].copy_(key_states)
+            vb[:, :, seen:nxt].copy_(value_states)
+            m[2] = nxt
+        return m[0][:, :, :nxt], m[1][:, :, :nxt]
+
     def fork(self) -> "AgentKVCache":
-        return AgentKVCache(self.pool, self.pool.fork(self.handle))
+        return AgentKVCache(self.pool, self.pool.fork(self.handle), append_only=self.append_only)
 
     def to_legacy_cache(self) -> Tuple[Tuple[torch.Tensor, torch.Tensor], ...]:
         ids = self.pool.get_block_ids(self.handle)

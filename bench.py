@@ -1025,13 +1025,14 @@ def hf_case(args) -> None:
     res["kv_gather"]["frac"] = round(res["kv_gather"]["gbs_algorithmic"] / peak, 4)
     del pool
     res["update_e2e"] = hf_update_figure(n_blocks, n_tok, args.steps, args.warmup)
+    res["update_e2e_append_only"] = hf_update_figure(n_blocks, n_tok, args.steps, args.warmup, append_only=True)
     print(json.dumps({"case": "hf_cache_gather", "tokens": n_tok, "layers": L, "heads": H, "head_dim": D,
                       "peak_gbs": peak, "peak_source": peak_kind, **res,
                       "speedup": round(res["torch_index_permute"]["ms_per_decode_step"] /
                                        res["kv_gather"]["ms_per_decode_step"], 2)}), flush=True)
 
 
-def hf_update_figure(n_blocks: int, n_tok: int, steps: int, warmup: int) -> dict:
+def hf_update_figure(n_blocks: int, n_tok: int, steps: int, warmup: int, append_only: bool = False) -> dict:
     """Decode steps through the public call, AgentKVCache.update on every
     layer (block allocation and copy-on-write checks on layer 0, the new
     token's rows written, the layer's K/V assembled): an agent forked from a
@@ -1050,7 +1051,7 @@ def hf_update_figure(n_blocks: int, n_tok: int, steps: int, warmup: int) -> dict
     pool.allocate_blocks(root, n_tok // bs)
     for _ in range(16):
         pool.commit_prefix(root, n_tok // 16)
-    cache = AgentKVCache(pool, pool.fork(root))
+    cache = AgentKVCache(pool, pool.fork(root), append_only=append_only)
     k = torch.randn((1, H, 1, D), generator=torch.Generator(device=dev).manual_seed(8), device=dev,
                     dtype=torch.float32).to(torch.bfloat16)
 
@@ -1072,7 +1073,7 @@ def hf_update_figure(n_blocks: int, n_tok: int, steps: int, warmup: int) -> dict
     ms = e0.elapsed_time(e1) / steps
     return {"ms_per_decode_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / L, 2),
             "host_wall_ms_per_step": round(wall * 1e3, 4), "tokens_at_start": n_tok,
-            "api": "AgentKVCache.update, every layer, one new token per step"}
+            "api": f"AgentKVCache.update(append_only={append_only}), every layer, one new token per step"}
 
 
 def match_traffic(n_seqs: int):

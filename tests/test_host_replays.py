@@ -186,7 +186,8 @@ def _hf_session(spec, pool, cache_cls, to_tensor):
     return caches, keys, np.concatenate(outs)
 
 
-def test_hf_cache_host_logic_replays_reference_session(golden_dir, monkeypatch):
+@pytest.mark.parametrize("append_only", [False, True])
+def test_hf_cache_host_logic_replays_reference_session(golden_dir, append_only, monkeypatch):
     """The package's HuggingFace cache logic (agentkv_b200/hf_cache.py: block
     allocation on layer 0, copy-on-write checks in the reference's order,
     slot arithmetic, truncation) replays the reference's recorded session on
@@ -198,10 +199,21 @@ def test_hf_cache_host_logic_replays_reference_session(golden_dir, monkeypatch):
 
     from agentkv_b200.hf_cache import AgentKVCache
 
+    import functools
+
     g = np.load(golden_dir / "hf_session.npz")
     spec = W.HFSpec(**json.loads(str(g["spec"])))
+    from agentkv_b200 import kernels as K
+
     pool, kv = _hf_cpu_pool(spec, monkeypatch)
-    caches, keys, outs = _hf_session(spec, pool, AgentKVCache, torch.from_numpy)
+    gathers = []
+    monkeypatch.setattr(K, "kv_gather", lambda *a, **k: (gathers.append(1), _kv_gather(*a, **k))[1])
+    cls = functools.partial(AgentKVCache, append_only=append_only)
+    caches, keys, outs = _hf_session(spec, pool, cls, torch.from_numpy)
+    assert all(c.append_only == append_only for c in caches)  # forks keep the mode
+    n_updates = len(keys)
+    # append_only assembles from the pool once per cache and layer, the default every update
+    assert len(gathers) == (len(caches) * spec.num_layers if append_only else n_updates)
     np.testing.assert_array_equal(np.asarray(keys), g["out_keys"])
     assert outs.tobytes() == g["outs"].tobytes()
     tables = np.concatenate([np.asarray(pool.get_block_ids(c.handle), np.int32) for c in caches])
@@ -216,7 +228,8 @@ def test_hf_cache_host_logic_replays_reference_session(golden_dir, monkeypatch):
     W.HFSpec(total_blocks=256, block_size=8, num_layers=3, num_kv_heads=2, head_dim=12, prompt=37,
              commit=32, forks=3, steps=12, seed=9),
 ])
-def test_hf_cache_host_logic_equals_oracle(spec, monkeypatch):
+@pytest.mark.parametrize("append_only", [False, True])
+def test_hf_cache_host_logic_equals_oracle(spec, append_only, monkeypatch):
     """Larger HF sessions (200- and 37-token prompts, commits, forks decoding
     one and three tokens per step) through the package's cache logic on CPU
     equal the oracle's cache: outputs, tables and pool bytes."""
@@ -225,8 +238,11 @@ def test_hf_cache_host_logic_equals_oracle(spec, monkeypatch):
     from agentkv_b200.hf_cache import AgentKVCache
     from oracle import oracle as O
 
+    import functools
+
     pool, kv = _hf_cpu_pool(spec, monkeypatch)
-    caches, keys, outs = _hf_session(spec, pool, AgentKVCache, torch.from_numpy)
+    cls = functools.partial(AgentKVCache, append_only=append_only)
+    caches, keys, outs = _hf_session(spec, pool, cls, torch.from_numpy)
     opool = O.OracleKVPool(spec.total_blocks, spec.block_size, spec.num_layers, spec.num_kv_heads,
                            spec.head_dim, spec.dtype)
     ocaches, okeys, oouts = _hf_session(spec, opool, O.OracleKVCache, lambda a: a)
