@@ -40,11 +40,15 @@ def _session(spec, pool, cache_cls, to_tensor):
     return caches, keys, np.concatenate(outs)
 
 
-def test_hf_session_matches_reference(golden_dir):
+@pytest.mark.parametrize("append_only", [False, True])
+def test_hf_session_matches_reference(golden_dir, append_only):
+    import functools
+
     g = np.load(golden_dir / "hf_session.npz")
     spec = W.HFSpec(**json.loads(str(g["spec"])))
     pool = _pool(spec)
-    caches, keys, outs = _session(spec, pool, AgentKVCache, lambda a: torch.from_numpy(a).to(DEV))
+    cls = functools.partial(AgentKVCache, append_only=append_only)
+    caches, keys, outs = _session(spec, pool, cls, lambda a: torch.from_numpy(a).to(DEV))
     np.testing.assert_array_equal(np.asarray(keys), g["out_keys"])
     assert outs.tobytes() == g["outs"].tobytes()
     tables = np.concatenate([np.asarray(pool.get_block_ids(c.handle), np.int32) for c in caches])
