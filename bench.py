@@ -983,7 +983,7 @@ def hf_case(args) -> None:
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     _, bs, L, H, D, _ = W.LLAMA3_8B_GEOMETRY
-    n_blocks, n_tok = max(256, min(args.blocks, 4096)), 4096
+    n_blocks, n_tok = max(320, min(args.blocks, 4096)), 4096  # room for the decode steps' new blocks
     pool = torch.empty((n_blocks, L, 2, H, bs, D), dtype=torch.bfloat16, device=dev)
     pool.normal_(generator=torch.Generator(device=dev).manual_seed(7))
     rng = np.random.default_rng(7)
@@ -1026,6 +1026,9 @@ def hf_case(args) -> None:
     del pool
     res["update_e2e"] = hf_update_figure(n_blocks, n_tok, args.steps, args.warmup)
     res["update_e2e_append_only"] = hf_update_figure(n_blocks, n_tok, args.steps, args.warmup, append_only=True)
+    res["update_reference_torch_path"] = hf_reference_update_figure(n_blocks, n_tok, args.steps, args.warmup)
+    res["update_speedup_vs_reference_torch_path"] = round(
+        res["update_reference_torch_path"]["ms_per_decode_step"] / res["update_e2e"]["ms_per_decode_step"], 2)
     print(json.dumps({"case": "hf_cache_gather", "tokens": n_tok, "layers": L, "heads": H, "head_dim": D,
                       "peak_gbs": peak, "peak_source": peak_kind, **res,
                       "speedup": round(res["torch_index_permute"]["ms_per_decode_step"] /
@@ -1074,6 +1077,52 @@ def hf_update_figure(n_blocks: int, n_tok: int, steps: int, warmup: int, append_
     return {"ms_per_decode_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / L, 2),
             "host_wall_ms_per_step": round(wall * 1e3, 4), "tokens_at_start": n_tok,
             "api": f"AgentKVCache.update(append_only={append_only}), every layer, one new token per step"}
+
+
+def hf_reference_update_figure(n_blocks: int, n_tok: int, steps: int, warmup: int) -> dict:
+    """The data movement of the reference's AgentKVCache.update on the GPU,
+    restated in torch (agentkv/hf_cache.py:100-153): per layer, the new
+    token's K and V rows written by indexed assignment, then the layer's
+    blocks gathered by advanced indexing, permuted, reshaped and cut to the
+    sequence length — one new token per step on an n_tok-token agent, the
+    same pool and table shape as hf_update_figure (its pool calls excluded)."""
+    import torch
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    _, bs, L, H, D, _ = W.LLAMA3_8B_GEOMETRY
+    pool = torch.zeros((n_blocks, L, 2, H, bs, D), dtype=torch.bfloat16, device=dev)
+    rng = np.random.default_rng(9)
+    ids = rng.permutation(n_blocks)[: n_tok // bs + 8].tolist()
+    k = torch.randn((1, H, 1, D), generator=torch.Generator(device=dev).manual_seed(9), device=dev,
+                    dtype=torch.float32).to(torch.bfloat16)
+    state = {"seen": n_tok}
+
+    def step():
+        seen = state["seen"]
+        nxt = seen + 1
+        table = torch.tensor(ids[: -(-nxt // bs)], dtype=torch.long, device=dev)
+        b, pos = ids[seen // bs], seen % bs
+        for layer in range(L):
+            pool[b, layer, 0, :, pos, :] = k[0, :, 0, :]
+            pool[b, layer, 1, :, pos, :] = k[0, :, 0, :]
+            data = pool[table, layer]
+            out_k = data[:, 0].permute(1, 0, 2, 3).reshape(1, H, -1, D)[:, :, :nxt]
+            out_v = data[:, 1].permute(1, 0, 2, 3).reshape(1, H, -1, D)[:, :, :nxt]
+            del out_k, out_v
+        state["seen"] = nxt if nxt < n_tok + 100 else n_tok
+
+    for _ in range(max(3, warmup)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"ms_per_decode_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / L, 2),
+            "api": "torch restatement of the reference's per-layer row writes + indexed gather"}
 
 
 def match_traffic(n_seqs: int):
