@@ -169,6 +169,11 @@ SIGNATURES = {
         C.c_int,
         [C.POINTER(AkvTreeView), _P, _P, _I32, _I32, _P, _P, _P, _P, _P, _I32, _P],
     ),
+    "akv_match_scratch_bytes": (C.c_int64, [_I32, _I64, _I32]),
+    "akv_match_prefix_split": (
+        C.c_int,
+        [C.POINTER(AkvTreeView), _P, _P, _I32, _I64, _I32, _P, _P, _P, _P, _P, _I64, _I32, _I32, _P, _P],
+    ),
 }
 
 

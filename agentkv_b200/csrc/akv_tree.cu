@@ -75,41 +75,42 @@ AKV_DEV int32_t warp_lookup(const int4* __restrict__ slots, int32_t mask, int32_
 constexpr int kWinPerLane = 8;  // query tokens a lane keeps: a 256-token window per warp
 constexpr int kSegment = 32;    // hops chased before their edges are verified (one per lane)
 
-// One warp per query.  The walk alternates two phases:
+// Where the reference's walk over one query stops, as seen from one range of
+// its token positions.  key = 2 * position + mismatch: the walk compares
+// every position before `position`, plus the mismatching token when
+// `mismatch` is 1, so the comparison count is position + mismatch.  The
+// stops of one walk are ordered by key, so over several ranges of a query
+// the smallest key is the reference's stop.  `matched` is the depth the walk
+// credits before flooring (the start of the stopping edge, or the end of the
+// last full edge) and `node` the node at that depth.
+struct MatchStop {
+  int64_t key;
+  int64_t matched;
+  int32_t node;
+};
+constexpr int64_t kNoStop = INT64_MAX;  // the range ends before the walk does
+
+// The reference's walk (radix_tree.py:513-570) over query Q[0, L), checked
+// on positions [a, b) only; one warp, all lanes.  The walk alternates two
+// phases:
 //  chase  — follow up to 32 hops using only each edge's first token: the next
 //           token position is the current depth plus the child's edge length,
 //           which the hash slot carries, and the query's tokens come from a
 //           256-token window held in registers, so a hop costs one dependent
-//           probe.  It stops at a missing child, at the end of the query, or
-//           at an edge that runs past the end of the query.
-//  verify — compare all tokens of the chased edges at once (their positions
-//           flattened across the warp) and find the first mismatch.  The
-//           reference's loop would have stopped at the first edge that
+//           probe.  It stops at a missing child, at the end of the query, at
+//           an edge that runs past the end of the query, or past b.
+//  verify — compare the chased edges' tokens that lie in [a, b) at once (their
+//           positions flattened across the warp) and find the first mismatch.
+//           The reference's loop would have stopped at the first edge that
 //           mismatches or only partly fits; everything before it is matched.
-// Hops past a mismatch are speculation and are discarded.  The comparison
-// count is the one the reference's loop makes: every token of each fully
-// matched edge, plus, on the stopping edge, its matched tokens and the
-// mismatching one.
+// Hops past a stop are speculation and are discarded.  Mismatches before a
+// are not looked for: the range that holds them reports them, and the
+// smallest key over all ranges wins.  With a = 0 and b = L this is the whole
+// lookup.
 template <int kVerifyChunks>
-__global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
-k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
-        int32_t nq, int32_t block_size, int32_t* __restrict__ out_node,
-        int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared,
-        const int32_t* __restrict__ order, AkvStatus* st) {
+AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict__ Q, int64_t L,
+                              int64_t a, int64_t b, int32_t q, AkvStatus* st, int lane) {
   constexpr uint32_t kFull = 0xffffffffu;
-  const int lane = threadIdx.x & 31;
-  const int32_t w = blockIdx.x * kMatchWarpsPerCta + (threadIdx.x >> 5);
-  if (w >= nq) return;
-  // `order` (optional) lists the queries longest first, so the long walks
-  // start early and spread over the SMs.
-  const int32_t q = order != nullptr ? order[w] : w;
-  if (static_cast<uint32_t>(q) >= static_cast<uint32_t>(nq)) {
-    if (lane == 0) akv_fail(st, AKV_ERR_INVALID_ARG, w, q, nq);
-    return;
-  }
-  const int64_t qlo = q_off[q];
-  const int64_t L = q_off[q + 1] - qlo;
-  const int32_t* __restrict__ Q = tokens + qlo;
   const int4* __restrict__ slots = reinterpret_cast<const int4*>(tree.slots);
   const int4* __restrict__ runs =
       tree.run_head != nullptr ? reinterpret_cast<const int4*>(tree.run_entries) : nullptr;
@@ -136,19 +137,23 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
   };
 
   int32_t cur = 0;  // ROOT_NODE_ID
-  int64_t matched = 0, compared = 0;
-  bool bad = false;
-  while (!bad) {
+  int64_t matched = 0;
+  while (true) {
     // ── chase ──
     int n = 0;
     int64_t d = matched;
     int32_t node = cur;
-    bool last_segment = false;
+    bool last_segment = false;  // the walk ends with this segment's hops
+    bool range_end = false;     // the hops reach past b < L
     int32_t my_child = -1, my_len = 0;
     int64_t my_d = 0;
     while (n < kSegment) {
       if (d >= L) {
         last_segment = true;
+        break;
+      }
+      if (d >= b) {
+        range_end = true;
         break;
       }
       // A node with exactly one child starts a run of its unary chain: up to
@@ -160,9 +165,8 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
       if (rp >= 0) {
         const int32_t rem = rp < tree.n_runs ? __ldg(&runs[rp]).w : 0;
         if (rem < 1 || static_cast<int64_t>(rp) + rem > tree.n_runs) {
-          bad = true;
           if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, node, rp);
-          break;
+          return MatchStop{0, 0, -1};
         }
         const int k = rem < kSegment - n ? rem : kSegment - n;
         int4 e = make_int4(-1, 0, 0, 0);
@@ -170,9 +174,8 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
         const uint32_t malformed =
             __ballot_sync(kFull, lane < k && (e.x < 0 || e.x >= tree.n_nodes || e.z < 0));
         if (malformed) {
-          bad = true;
           if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, node, rp);
-          break;
+          return MatchStop{0, 0, -1};
         }
         int64_t incl = lane < k ? e.z : 0;
 #pragma unroll
@@ -224,9 +227,8 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
         break;
       }
       if (child >= tree.n_nodes || clen < 0) {
-        bad = true;
         if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, child, tree.n_nodes);
-        break;
+        return MatchStop{0, 0, -1};
       }
       if (lane == n) {
         my_child = child;
@@ -241,7 +243,10 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
       d += clen;
       node = child;
     }
-    if (bad || n == 0) break;
+    if (n == 0) {  // a missing child at `matched`, the query's end, or the range's end
+      if (range_end) return MatchStop{kNoStop, 0, -1};
+      return MatchStop{2 * matched, matched, cur};
+    }
     // ── verify ──
     int64_t my_off = 0;
     bool my_bad = false;
@@ -252,9 +257,8 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
     }
     const uint32_t badm = __ballot_sync(kFull, my_bad);
     if (badm) {
-      bad = true;
       if (lane == __ffs(badm) - 1) akv_fail(st, AKV_ERR_TREE, q, my_child, my_len, my_off);
-      break;
+      return MatchStop{0, 0, -1};
     }
     const int32_t lim = lane < n ? static_cast<int32_t>(my_len < L - my_d ? my_len : L - my_d) : 0;
     int32_t incl = lim;
@@ -265,6 +269,10 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
     }
     const int32_t excl = incl - lim;
     const int32_t total = __shfl_sync(kFull, incl, 31);
+    // The chased edges are consecutive in depth: flattened position p is
+    // query position matched + p.  Only [a, b) is compared here.
+    const int32_t p_lo = a > matched ? static_cast<int32_t>(a - matched < total ? a - matched : total) : 0;
+    const int32_t p_hi = static_cast<int32_t>(b - matched < total ? b - matched : total);
     // entry holding flattened position p: the last e < n with excl_e <= p
     auto entry_of = [&](int32_t p) -> int {
       int lo = 0, hi = n - 1;
@@ -280,8 +288,8 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
       return lo;
     };
     int32_t first = -1;
-    for (int32_t base = 0; base < total; base += 32 * kVerifyChunks) {
-      int32_t a[kVerifyChunks], b[kVerifyChunks];
+    for (int32_t base = p_lo; base < p_hi; base += 32 * kVerifyChunks) {
+      int32_t av[kVerifyChunks], bv[kVerifyChunks];
       // Fast path: the whole step lies inside one edge (long edges).
       const int e0 = entry_of(base);
       const int32_t ex0 = __shfl_sync(kFull, excl, e0);
@@ -292,26 +300,26 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
 #pragma unroll
         for (int u = 0; u < kVerifyChunks; ++u) {
           const int32_t p = base + u * 32 + lane;
-          const bool ok = p < total;
-          a[u] = ok ? Q[de + p] : 0;
-          b[u] = ok ? __ldg(&tree.tokens[oe + p]) : 0;
+          const bool ok = p < p_hi;
+          av[u] = ok ? Q[de + p] : 0;
+          bv[u] = ok ? __ldg(&tree.tokens[oe + p]) : 0;
         }
       } else {
 #pragma unroll
         for (int u = 0; u < kVerifyChunks; ++u) {
           const int32_t p = base + u * 32 + lane;
-          const int e = entry_of(p < total ? p : total - 1);
+          const int e = entry_of(p < p_hi ? p : p_hi - 1);
           const int32_t j = p - __shfl_sync(kFull, excl, e);
           const int64_t de = __shfl_sync(kFull, my_d, e);
           const int64_t oe = __shfl_sync(kFull, my_off, e);
-          const bool ok = p < total;
-          a[u] = ok ? Q[de + j] : 0;
-          b[u] = ok ? __ldg(&tree.tokens[oe + j]) : 0;
+          const bool ok = p < p_hi;
+          av[u] = ok ? Q[de + j] : 0;
+          bv[u] = ok ? __ldg(&tree.tokens[oe + j]) : 0;
         }
       }
 #pragma unroll
       for (int u = 0; u < kVerifyChunks; ++u) {
-        const uint32_t m = __ballot_sync(kFull, a[u] != b[u]);
+        const uint32_t m = __ballot_sync(kFull, av[u] != bv[u]);
         if (m && first < 0) first = base + u * 32 + __ffs(m) - 1;
       }
       if (first >= 0) break;
@@ -321,27 +329,245 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
     const uint32_t short_m = __ballot_sync(kFull, lane < n && (lim < my_len || my_len == 0));
     const int e_short = short_m ? __ffs(short_m) - 1 : kSegment;
     const int e_stop = e_mis < e_short ? e_mis : e_short;
-    if (e_stop == kSegment) {  // every chased edge matched in full
-      compared += total;
-      matched = __shfl_sync(kFull, my_d, n - 1) + __shfl_sync(kFull, my_len, n - 1);
-      cur = __shfl_sync(kFull, my_child, n - 1);
-      if (last_segment) break;
+    if (e_stop == kSegment) {  // every chased edge matched in [a, b)
+      const int64_t end = __shfl_sync(kFull, my_d, n - 1) + __shfl_sync(kFull, my_len, n - 1);
+      const int32_t last = __shfl_sync(kFull, my_child, n - 1);
+      if (last_segment) return MatchStop{2 * end, end, last};
+      matched = end;
+      cur = last;
+      if (range_end) return MatchStop{kNoStop, 0, -1};
       continue;
     }
     const int32_t ex = __shfl_sync(kFull, excl, e_stop);
     const bool mism = e_mis == e_stop;
     const int32_t em = mism ? first - ex : __shfl_sync(kFull, lim, e_stop);
-    compared += ex + em + (mism ? 1 : 0);
-    matched = __shfl_sync(kFull, my_d, e_stop);
+    const int64_t stop_d = __shfl_sync(kFull, my_d, e_stop);
     const int32_t prev_child = __shfl_sync(kFull, my_child, e_stop > 0 ? e_stop - 1 : 0);
-    cur = e_stop > 0 ? prev_child : cur;
-    break;
+    return MatchStop{2 * (matched + ex + em) + (mism ? 1 : 0), stop_d, e_stop > 0 ? prev_child : cur};
+  }
+}
+
+AKV_DEV void match_write(const MatchStop& s, int32_t q, int32_t block_size, int32_t* out_node,
+                         int32_t* out_len, int64_t* out_compared) {
+  const int64_t m = (s.matched / block_size) * block_size;
+  out_node[q] = m == 0 ? -1 : s.node;
+  out_len[q] = static_cast<int32_t>(m);
+  if (out_compared != nullptr) out_compared[q] = (s.key >> 1) + (s.key & 1);
+}
+
+// One warp per query (the whole query is one range).  `order` (optional)
+// lists the queries longest first, so the long walks start early and spread
+// over the SMs.
+template <int kVerifyChunks>
+__global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
+k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
+        int32_t nq, int32_t block_size, int32_t* __restrict__ out_node,
+        int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared,
+        const int32_t* __restrict__ order, AkvStatus* st) {
+  const int lane = threadIdx.x & 31;
+  const int32_t w = blockIdx.x * kMatchWarpsPerCta + (threadIdx.x >> 5);
+  if (w >= nq) return;
+  const int32_t q = order != nullptr ? order[w] : w;
+  if (static_cast<uint32_t>(q) >= static_cast<uint32_t>(nq)) {
+    if (lane == 0) akv_fail(st, AKV_ERR_INVALID_ARG, w, q, nq);
+    return;
+  }
+  const int64_t qlo = q_off[q];
+  const int64_t L = q_off[q + 1] - qlo;
+  const MatchStop s = match_range<kVerifyChunks>(tree, tokens + qlo, L, 0, L, q, st, lane);
+  if (lane == 0) match_write(s, q, block_size, out_node, out_len, out_compared);
+}
+
+// ── split lookups: a query's positions in ranges of R tokens, one warp each ──
+// A batch is bounded by its longest query when one warp walks each query
+// (an 8,192-token query is 64 dependent verify rounds of 128 tokens).  Here
+// query q is cut into k_q = max(1, ceil(L_q / R)) ranges ("items"); the warp
+// of item j walks the tree up to position (j + 1) R and compares positions
+// [j R, (j + 1) R) only, so every warp does at most R tokens of comparison
+// and the SMs stay evenly loaded.  Each item reports the first stop it sees
+// (MatchStop); the warp that finishes a query's last item picks the smallest
+// key among them, which is the stop of the reference's loop.
+//
+// Scratch (caller-owned, akv_match_scratch_bytes): a 256-byte header (the
+// item count), one 16-byte stop record per item, the item list {q, j} and a
+// per-query count of finished items.
+constexpr int64_t kSplitHeader = 256;
+
+AKV_HD int64_t split_items_max(int32_t nq, int64_t n_tokens, int32_t R) {
+  return static_cast<int64_t>(nq) + n_tokens / R;  // sum of max(1, ceil(L/R)) <= nq + sum(L)/R
+}
+
+struct SplitScratch {
+  int32_t* n_items;
+  int4* stops;
+  int2* items;
+  int32_t* done;
+};
+
+AKV_HD SplitScratch split_scratch(void* base, int32_t nq, int64_t w_max) {
+  char* p = static_cast<char*>(base);
+  SplitScratch s;
+  s.n_items = reinterpret_cast<int32_t*>(p);
+  s.stops = reinterpret_cast<int4*>(p + kSplitHeader);
+  s.items = reinterpret_cast<int2*>(p + kSplitHeader + 16 * w_max);
+  s.done = reinterpret_cast<int32_t*>(p + kSplitHeader + 24 * w_max);
+  (void)nq;
+  return s;
+}
+
+AKV_HD int64_t split_scratch_bytes(int32_t nq, int64_t w_max) {
+  const int64_t b = kSplitHeader + 24 * w_max + 4 * static_cast<int64_t>(nq);
+  return (b + 255) / 256 * 256;
+}
+
+AKV_DEV int32_t split_count(int64_t L, int32_t R) {
+  return L <= 0 ? 1 : static_cast<int32_t>((L + R - 1) / R);
+}
+
+// Lists the items, queries in `order` (longest first), each query's items
+// consecutive; clears the per-query counts.  One CTA.  A query listed twice
+// in `order`, an index out of range or a query longer than INT32_MAX is
+// reported (AKV_ERR_INVALID_ARG) and no item is listed.
+constexpr int kItemThreads = 1024;
+
+__global__ void __launch_bounds__(kItemThreads)
+k_match_items(const int64_t* __restrict__ q_off, const int32_t* __restrict__ order, int32_t nq,
+              int32_t R, int64_t w_max, SplitScratch sc, AkvStatus* st) {
+  __shared__ int64_t warp_sum[kItemThreads / 32];
+  __shared__ int64_t carry;
+  __shared__ int32_t bad;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  if (tid == 0) {
+    carry = 0;
+    bad = 0;
+  }
+  for (int32_t i = tid; i < nq; i += kItemThreads) sc.done[i] = 0;
+  __syncthreads();
+  // `done` marks each listed query once, to catch repeats in `order`
+  for (int32_t r = tid; r < nq; r += kItemThreads) {
+    const int32_t q = order != nullptr ? order[r] : r;
+    if (static_cast<uint32_t>(q) >= static_cast<uint32_t>(nq) || atomicExch(&sc.done[q], 1) != 0) {
+      akv_fail(st, AKV_ERR_INVALID_ARG, r, q, nq);
+      bad = 1;
+      continue;
+    }
+    const int64_t L = q_off[q + 1] - q_off[q];
+    if (L < 0 || L > INT32_MAX) {
+      akv_fail(st, AKV_ERR_INVALID_ARG, r, q, nq, L);
+      bad = 1;
+    }
+  }
+  __syncthreads();
+  if (bad) {
+    if (tid == 0) *sc.n_items = 0;
+    return;
+  }
+  for (int32_t i = tid; i < nq; i += kItemThreads) sc.done[i] = 0;
+  for (int32_t base = 0; base < nq; base += kItemThreads) {
+    const int32_t r = base + tid;
+    int32_t q = 0, k = 0;
+    if (r < nq) {
+      q = order != nullptr ? order[r] : r;
+      k = split_count(q_off[q + 1] - q_off[q], R);
+    }
+    int64_t incl = k;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sum[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+      int64_t v = warp_sum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+      }
+      warp_sum[lane] = v;
+    }
+    __syncthreads();
+    const int64_t start = carry + (wid > 0 ? warp_sum[wid - 1] : 0) + incl - k;
+    for (int32_t j = 0; j < k; ++j) {
+      if (start + j < w_max) sc.items[start + j] = make_int2(q, j);
+    }
+    __syncthreads();
+    if (tid == 0) carry += warp_sum[kItemThreads / 32 - 1];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    if (carry > w_max) {
+      akv_fail(st, AKV_ERR_INVALID_ARG, nq, static_cast<int32_t>(w_max), 0, carry);
+      *sc.n_items = 0;
+    } else {
+      *sc.n_items = static_cast<int32_t>(carry);
+    }
+  }
+}
+
+template <int kVerifyChunks>
+__global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
+k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
+              int32_t block_size, int32_t R, SplitScratch sc, int32_t* __restrict__ out_node,
+              int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared, AkvStatus* st) {
+  constexpr uint32_t kFull = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int64_t it = static_cast<int64_t>(blockIdx.x) * kMatchWarpsPerCta + (threadIdx.x >> 5);
+  if (it >= *sc.n_items) return;
+  const int2 qj = sc.items[it];
+  const int32_t q = qj.x, j = qj.y;
+  const int64_t qlo = q_off[q];
+  const int64_t L = q_off[q + 1] - qlo;
+  const int64_t a = static_cast<int64_t>(j) * R;
+  const int64_t b = a + R < L ? a + R : L;
+  const MatchStop s = match_range<kVerifyChunks>(tree, tokens + qlo, L, a, b, q, st, lane);
+  const int32_t k = split_count(L, R);
+  if (k == 1) {
+    if (lane == 0) match_write(s, q, block_size, out_node, out_len, out_compared);
+    return;
+  }
+  int32_t prior = 0;
+  if (lane == 0) {
+    __stcg(&sc.stops[it], make_int4(static_cast<int32_t>(s.key & 0xffffffff), static_cast<int32_t>(s.key >> 32),
+                                    static_cast<int32_t>(s.matched), s.node));
+    __threadfence();
+    prior = atomicAdd(&sc.done[q], 1);
+  }
+  prior = __shfl_sync(kFull, prior, 0);
+  if (prior != k - 1) return;  // another item of this query finishes last
+  __threadfence();
+  // the last item of query q: the smallest key over its k stop records
+  const int64_t first_item = it - j;
+  int64_t best = kNoStop;
+  int32_t b_matched = 0, b_node = -1;
+  for (int32_t i = lane; i < k; i += 32) {
+    const int4 r = __ldcg(&sc.stops[first_item + i]);
+    const int64_t key = (static_cast<int64_t>(r.y) << 32) | static_cast<uint32_t>(r.x);
+    if (key < best) {
+      best = key;
+      b_matched = r.z;
+      b_node = r.w;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const int64_t ok = __shfl_xor_sync(kFull, best, o);
+    const int32_t om = __shfl_xor_sync(kFull, b_matched, o);
+    const int32_t on = __shfl_xor_sync(kFull, b_node, o);
+    if (ok < best) {
+      best = ok;
+      b_matched = om;
+      b_node = on;
+    }
   }
   if (lane == 0) {
-    const int64_t m = bad ? 0 : (matched / block_size) * block_size;
-    out_node[q] = m == 0 ? -1 : cur;
-    out_len[q] = static_cast<int32_t>(m);
-    if (out_compared != nullptr) out_compared[q] = compared;
+    if (best == kNoStop) {  // cannot happen for a well-formed walk; never report a match then
+      akv_fail(st, AKV_ERR_TREE, q, -1, k);
+      best = 0;
+      b_matched = 0;
+    }
+    match_write(MatchStop{best, b_matched, b_node}, q, block_size, out_node, out_len, out_compared);
   }
 }
 
@@ -379,6 +605,12 @@ int akv_tree_prepare() {
   AKV_LOAD(k_match<4>);
   AKV_LOAD(k_match<8>);
   AKV_LOAD(k_match<16>);
+  AKV_LOAD(k_match_items);
+  AKV_LOAD(k_match_split<1>);
+  AKV_LOAD(k_match_split<2>);
+  AKV_LOAD(k_match_split<4>);
+  AKV_LOAD(k_match_split<8>);
+  AKV_LOAD(k_match_split<16>);
   AKV_LOAD(k_tree_apply);
 #undef AKV_LOAD
   return AKV_OK;
@@ -412,29 +644,45 @@ extern "C" int akv_tree_apply(const AkvTreeView* tree, const int32_t* slot_updat
   return AKV_OK;
 }
 
+namespace {
+
+constexpr int32_t kSplitDefaultTokens = 1024;  // tokens per item (R)
+constexpr int kSplitDefaultChunks = 8;        // 256 tokens compared per verify round
+
+int match_args_ok(const AkvTreeView* tree, const int32_t* tokens, const int64_t* q_off, int32_t nq,
+                  int32_t block_size, const int32_t* out_node, const int32_t* out_len, int32_t chunks,
+                  const char* fn) {
+  AKV_ARG_CHECK(tree != nullptr && tree->tokens && tree->node_edge_off && tree->node_edge_len &&
+                    tree->slots,
+                "%s: incomplete tree view", fn);
+  AKV_ARG_CHECK(tree->n_nodes > 0, "%s: n_nodes=%d", fn, tree->n_nodes);
+  AKV_ARG_CHECK(tree->run_head == nullptr ||
+                    (tree->run_entries != nullptr && tree->n_runs > 0 && tree->run_nodes >= 0),
+                "%s: run_head set without run_entries / n_runs (%d) / run_nodes (%d)", fn,
+                tree->n_runs, tree->run_nodes);
+  AKV_ARG_CHECK(tree->slot_mask >= 31 && ((tree->slot_mask + 1) & tree->slot_mask) == 0,
+                "%s: slot count %d is not a power of two >= 32", fn, tree->slot_mask + 1);
+  AKV_ARG_CHECK(nq >= 0, "%s: nq=%d < 0", fn, nq);
+  AKV_ARG_CHECK(block_size > 0, "%s: block_size=%d", fn, block_size);
+  AKV_ARG_CHECK(chunks == 0 || chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8 || chunks == 16,
+                "%s: chunks=%d not in {0,1,2,4,8,16}", fn, chunks);
+  AKV_ARG_CHECK(nq == 0 || (tokens != nullptr && q_off != nullptr && out_node != nullptr &&
+                            out_len != nullptr),
+                "%s: NULL query or output array", fn);
+  return AKV_OK;
+}
+
+}  // namespace
+
 extern "C" int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* tokens,
                                         const int64_t* q_off, int32_t nq, int32_t block_size,
                                         int32_t* out_node, int32_t* out_len, int64_t* out_compared,
                                         const int32_t* order, AkvStatus* status, int32_t chunks,
                                         void* stream) {
-  AKV_ARG_CHECK(tree != nullptr && tree->tokens && tree->node_edge_off && tree->node_edge_len &&
-                    tree->slots,
-                "akv_match_prefix: incomplete tree view");
-  AKV_ARG_CHECK(tree->n_nodes > 0, "akv_match_prefix: n_nodes=%d", tree->n_nodes);
-  AKV_ARG_CHECK(tree->run_head == nullptr ||
-                    (tree->run_entries != nullptr && tree->n_runs > 0 && tree->run_nodes >= 0),
-                "akv_match_prefix: run_head set without run_entries / n_runs (%d) / run_nodes (%d)",
-                tree->n_runs, tree->run_nodes);
-  AKV_ARG_CHECK(tree->slot_mask >= 31 && ((tree->slot_mask + 1) & tree->slot_mask) == 0,
-                "akv_match_prefix: slot count %d is not a power of two >= 32",
-                tree->slot_mask + 1);
-  AKV_ARG_CHECK(nq >= 0, "akv_match_prefix: nq=%d < 0", nq);
-  AKV_ARG_CHECK(block_size > 0, "akv_match_prefix: block_size=%d", block_size);
+  if (int rc = match_args_ok(tree, tokens, q_off, nq, block_size, out_node, out_len, chunks,
+                             "akv_match_prefix"))
+    return rc;
   if (nq == 0) return AKV_OK;
-  AKV_ARG_CHECK(tokens != nullptr && q_off != nullptr && out_node != nullptr && out_len != nullptr,
-                "akv_match_prefix: NULL query or output array");
-  AKV_ARG_CHECK(chunks == 0 || chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8 || chunks == 16,
-                "akv_match_prefix: chunks=%d not in {0,1,2,4,8,16}", chunks);
   if (chunks == 0) chunks = 4;
   const int grid = akv_ceil_div(nq, kMatchWarpsPerCta);
   cudaStream_t s = akv_stream(stream);
@@ -473,4 +721,64 @@ extern "C" int akv_match_prefix(const AkvTreeView* tree, const int32_t* tokens, 
                                 void* stream) {
   return akv_match_prefix_variant(tree, tokens, q_off, nq, block_size, out_node, out_len, out_compared,
                                   nullptr, status, 0, stream);
+}
+
+extern "C" int64_t akv_match_scratch_bytes(int32_t nq, int64_t n_tokens, int32_t tokens_per_item) {
+  const int32_t R = tokens_per_item == 0 ? kSplitDefaultTokens : tokens_per_item;
+  if (nq < 0 || n_tokens < 0 || R < 32 || R % 32 != 0) return -1;
+  return split_scratch_bytes(nq, split_items_max(nq, n_tokens, R));
+}
+
+extern "C" int akv_match_prefix_split(const AkvTreeView* tree, const int32_t* tokens, const int64_t* q_off,
+                                      int32_t nq, int64_t n_tokens, int32_t block_size, int32_t* out_node,
+                                      int32_t* out_len, int64_t* out_compared, const int32_t* order,
+                                      void* scratch, int64_t scratch_bytes, int32_t tokens_per_item,
+                                      int32_t chunks, AkvStatus* status, void* stream) {
+  if (int rc = match_args_ok(tree, tokens, q_off, nq, block_size, out_node, out_len, chunks,
+                             "akv_match_prefix_split"))
+    return rc;
+  const int32_t R = tokens_per_item == 0 ? kSplitDefaultTokens : tokens_per_item;
+  AKV_ARG_CHECK(R >= 32 && R % 32 == 0, "akv_match_prefix_split: tokens_per_item=%d is not a multiple of 32",
+                tokens_per_item);
+  AKV_ARG_CHECK(n_tokens >= 0, "akv_match_prefix_split: n_tokens=%lld < 0", static_cast<long long>(n_tokens));
+  if (nq == 0) return AKV_OK;
+  const int64_t w_max = split_items_max(nq, n_tokens, R);
+  const int64_t need = split_scratch_bytes(nq, w_max);
+  AKV_ARG_CHECK(scratch != nullptr && scratch_bytes >= need,
+                "akv_match_prefix_split: scratch of %lld bytes, %lld needed (akv_match_scratch_bytes)",
+                static_cast<long long>(scratch_bytes), static_cast<long long>(need));
+  AKV_ARG_CHECK(reinterpret_cast<uintptr_t>(scratch) % 16 == 0,
+                "akv_match_prefix_split: scratch is not 16-byte aligned");
+  AKV_ARG_CHECK(w_max / kMatchWarpsPerCta < INT32_MAX, "akv_match_prefix_split: %lld items",
+                static_cast<long long>(w_max));
+  if (chunks == 0) chunks = kSplitDefaultChunks;
+  const SplitScratch sc = split_scratch(scratch, nq, w_max);
+  cudaStream_t s = akv_stream(stream);
+  k_match_items<<<1, kItemThreads, 0, s>>>(q_off, order, nq, R, w_max, sc, status);
+  AKV_LAUNCH_CHECK("akv_match_prefix_split(items)");
+  const int grid = akv_ceil_div(w_max, kMatchWarpsPerCta);
+  const int threads = kMatchWarpsPerCta * 32;
+  switch (chunks) {
+    case 1:
+      k_match_split<1><<<grid, threads, 0, s>>>(*tree, tokens, q_off, block_size, R, sc, out_node, out_len,
+                                                 out_compared, status);
+      break;
+    case 2:
+      k_match_split<2><<<grid, threads, 0, s>>>(*tree, tokens, q_off, block_size, R, sc, out_node, out_len,
+                                                 out_compared, status);
+      break;
+    case 4:
+      k_match_split<4><<<grid, threads, 0, s>>>(*tree, tokens, q_off, block_size, R, sc, out_node, out_len,
+                                                 out_compared, status);
+      break;
+    case 16:
+      k_match_split<16><<<grid, threads, 0, s>>>(*tree, tokens, q_off, block_size, R, sc, out_node, out_len,
+                                                  out_compared, status);
+      break;
+    default:
+      k_match_split<8><<<grid, threads, 0, s>>>(*tree, tokens, q_off, block_size, R, sc, out_node, out_len,
+                                                 out_compared, status);
+  }
+  AKV_LAUNCH_CHECK("akv_match_prefix_split");
+  return AKV_OK;
 }

@@ -126,6 +126,7 @@ class DeviceTree:
         self.status = torch.zeros(N.STATUS_BYTES // 4, dtype=torch.int32, device=device)
         self._view: Optional[N.AkvTreeView] = None
         self._stage: Optional["QueryStage"] = None  # match_batch's reusable buffers
+        self._split_scratch: Optional[torch.Tensor] = None  # akv_match_prefix_split's work space
 
     # ── mutations (host mirror) ──────────────────────────────────────────────
     def append_tokens(self, toks: np.ndarray) -> int:
@@ -559,21 +560,43 @@ class DeviceTree:
     # ── lookups ──────────────────────────────────────────────────────────────
     def match(self, tokens: torch.Tensor, q_off: torch.Tensor, nq: int, block_size: int,
               out_node: torch.Tensor, out_len: torch.Tensor, out_cmp: Optional[torch.Tensor],
-              chunks: int = 0, order: Optional[torch.Tensor] = None, runs: bool = False) -> None:
-        """Enqueue akv_match_prefix for nq queries packed in `tokens` / `q_off`
-        (device int32 / int64 tensors); `order` (device int32) is the launch
-        order of the queries, longest first by default in pack_queries.  With
-        runs=True unary chains are followed a run at a time (the runs are
-        rebuilt first if the tree changed: worth it for batches, not for the
-        single lookups of create_root)."""
+              chunks: int = 0, order: Optional[torch.Tensor] = None, runs: bool = False,
+              n_tokens: Optional[int] = None, tokens_per_item: int = 0) -> None:
+        """Enqueue a match_prefix lookup of nq queries packed in `tokens` /
+        `q_off` (device int32 / int64 tensors); `order` (device int32) is the
+        launch order of the queries, longest first by default in
+        pack_queries.  With runs=True unary chains are followed a run at a
+        time (the runs are rebuilt first if the tree changed: worth it for
+        batches, not for the single lookups of create_root).
+
+        With n_tokens (the batch's token count, known on the host) the
+        lookup is akv_match_prefix_split: every query's positions in ranges
+        of tokens_per_item tokens (0 = the library's default), one warp per
+        range, so a long query does not hold the batch; its scratch is this
+        tree's, grown as needed.  Without it, akv_match_prefix_variant (one
+        warp per query).  The answers are the same."""
         self.flush()
         if runs:
             self.build_runs()
-        N.check(N.lib.akv_match_prefix_variant(
-            self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, block_size, out_node.data_ptr(),
-            out_len.data_ptr(), out_cmp.data_ptr() if out_cmp is not None else None,
-            order.data_ptr() if order is not None else None, self.status.data_ptr(), chunks,
-            stream_handle(self.device)))
+        out_c = out_cmp.data_ptr() if out_cmp is not None else None
+        ordp = order.data_ptr() if order is not None else None
+        if n_tokens is None:
+            N.check(N.lib.akv_match_prefix_variant(
+                self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, block_size, out_node.data_ptr(),
+                out_len.data_ptr(), out_c, ordp, self.status.data_ptr(), chunks, stream_handle(self.device)))
+            return
+        need = int(N.lib.akv_match_scratch_bytes(nq, int(n_tokens), tokens_per_item))
+        if need < 0:
+            raise ValueError(f"match_prefix: bad split arguments (nq={nq}, n_tokens={n_tokens}, "
+                             f"tokens_per_item={tokens_per_item})")
+        if self._split_scratch is None or self._split_scratch.numel() < need:
+            cap = max(need, 2 * (self._split_scratch.numel() if self._split_scratch is not None else 0), 1 << 16)
+            self._split_scratch = torch.empty(cap, dtype=torch.uint8, device=self.device)
+        sc = self._split_scratch
+        N.check(N.lib.akv_match_prefix_split(
+            self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, int(n_tokens), block_size,
+            out_node.data_ptr(), out_len.data_ptr(), out_c, ordp, sc.data_ptr(), sc.numel(), tokens_per_item,
+            chunks, self.status.data_ptr(), stream_handle(self.device)))
 
     def check(self) -> None:
         s = self.status.cpu()
@@ -608,6 +631,7 @@ class QueryStage:
     def __init__(self, device: torch.device) -> None:
         self.device = device
         self._tok_cap = self._q_cap = 0
+        self.total = 0
 
     def _grow(self, total: int, nq: int) -> None:
         pin = self.device.type == "cuda"
@@ -640,6 +664,7 @@ class QueryStage:
         self.d_tok[:total].copy_(self.h_tok[:total], non_blocking=True)
         self.d_off[: nq + 1].copy_(self.h_off[: nq + 1], non_blocking=True)
         self.d_ord[:nq].copy_(self.h_ord[:nq], non_blocking=True)
+        self.total = total
         return self.d_tok[: max(total, 1)], self.d_off[: nq + 1], self.d_ord[: max(nq, 1)]
 
 
@@ -660,14 +685,19 @@ def longest_first(q_off, device: torch.device) -> torch.Tensor:
 
 
 def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_compared: bool = False,
-                runs: Optional[bool] = None):
+                runs: Optional[bool] = None, tokens_per_item: int = 0, split: bool = True,
+                chunks: int = 0):
     """Longest shared prefix of many queries in one akv_match_prefix launch on
     `tree` (the owner's replica or another GPU's): (node ids, match lengths
     [, tokens compared]) as numpy arrays, each equal to the reference's
     _match_prefix_locked (agentkv/core/radix_tree.py:513-570) on that query.
     runs=True follows the unary-chain runs (rebuilt first when stale),
     runs=False takes one hash probe per hop, None lets the tree decide
-    (DeviceTree.want_runs); the answers are the same."""
+    (DeviceTree.want_runs); the answers are the same.  The lookup splits
+    long queries into ranges of tokens_per_item tokens (0 = the library's
+    default; see DeviceTree.match); split=False uses one warp per query
+    instead.  chunks: 32-token chunks compared per verify step (0 = the
+    kernel's default)."""
     t0 = time.perf_counter()
     if runs is None:
         runs = tree.want_runs()
@@ -679,7 +709,8 @@ def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_co
     node = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
     mlen = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
     cmp_ = torch.empty(max(nq, 1), dtype=torch.int64, device=dev) if with_compared else None
-    tree.match(tok, q_off, nq, block_size, node, mlen, cmp_, order=order, runs=runs)
+    tree.match(tok, q_off, nq, block_size, node, mlen, cmp_, order=order, runs=runs, chunks=chunks,
+               n_tokens=tree._stage.total if split else None, tokens_per_item=tokens_per_item)
     tree.check()
     res = (node[:nq].cpu().numpy(), mlen[:nq].cpu().numpy())
     if with_compared:

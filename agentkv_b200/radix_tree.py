@@ -428,7 +428,8 @@ class DualRadixTree:
         # copy); the answer's read-back is the call's one wait
         tok, q_off, _ = self._one_stage.pack([t])
         out = self._q_out.view(torch.int32)
-        self._dev_tree.match(tok, q_off, 1, self._cfg.block_size, out[0:1], out[1:2], None)
+        self._dev_tree.match(tok, q_off, 1, self._cfg.block_size, out[0:1], out[1:2], None,
+                             n_tokens=len(t))
         res = out[:2].cpu()
         self._dev_tree.check()
         node, mlen = int(res[0]), int(res[1])

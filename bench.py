@@ -112,6 +112,10 @@ def parse_args():
     ap.add_argument("--match-queries", type=int, default=W.MatchSpec.n_queries)
     ap.add_argument("--match-chunks", type=int, default=0, choices=[0, 1, 2, 4, 8, 16],
                     help="match_prefix verify width: 32-token compares per lane per step (0: the default)")
+    ap.add_argument("--match-split", type=int, default=1,
+                    help="match_prefix splits queries into token ranges, one warp each (0: one warp per query)")
+    ap.add_argument("--match-tokens-per-item", type=int, default=0,
+                    help="match_prefix split range in tokens, a multiple of 32 (0: the library's default)")
     ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers", "hf", "react"],
                     help="tot: the headline step; sweep: batched copy/zero sweep; match: match_prefix on the "
                          "stress tree; layers: copies on vLLM's per-layer cache layout; hf: the HF cache's "
@@ -710,7 +714,8 @@ def match_cpu_baseline(pool, batches, gpu_results, max_seconds: float) -> dict:
 
 def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
                  n_queries: int = W.MatchSpec.n_queries, rank: int = 0, world: int = 1,
-                 use_runs: bool = True, cpu_seconds: float = 0.0, chunks: int = 0) -> dict:
+                 use_runs: bool = True, cpu_seconds: float = 0.0, chunks: int = 0, split: bool = True,
+                 tokens_per_item: int = 0) -> dict:
     """match_prefix on the stress tree.  With N ranks, rank 0 builds the tree
     through the pool API and broadcasts it (TreeReplicaSync) to every rank's
     replica; each rank then matches its own 4096-query batches (weak
@@ -757,6 +762,8 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
     packed = [pack_queries(q, dev) for q in batches]
     orders = [longest_first(off, dev) for _, off in packed]
     nq = spec.n_queries
+    # the split lookup's launch is sized by the largest batch's token count
+    ntok = max(sum(len(q) for q in b_) for b_ in batches) if split else None
     node = torch.empty(nq, dtype=torch.int32, device=dev)
     mlen = torch.empty(nq, dtype=torch.int32, device=dev)
     cmp_ = torch.empty(nq, dtype=torch.int64, device=dev)
@@ -764,7 +771,8 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
     qtokens = []
     results = []
     for (tok, off), order in zip(packed, orders):
-        tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks)
+        tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks,
+                   n_tokens=ntok, tokens_per_item=tokens_per_item)
         compared.append(int(cmp_.sum()))
         qtokens.append(int(off[-1]))
         results.append((node.cpu().numpy(), mlen.cpu().numpy(), cmp_.cpu().numpy()))
@@ -780,7 +788,8 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
 
     def run():
         for (tok, off), order in zip(packed, orders):
-            tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks)
+            tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks,
+                       n_tokens=ntok, tokens_per_item=tokens_per_item)
 
     ms, _ = timed(run, steps, warmup, world)
     per_batch_ms = ms / (steps * len(packed))
@@ -788,7 +797,8 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
 
     def run_warm():  # one batch again and again: its query tokens stay in L2
         for _ in range(len(packed)):
-            tree.match(tok0, off0, nq, 16, node, mlen, cmp_, order=order0, runs=use_runs, chunks=chunks)
+            tree.match(tok0, off0, nq, 16, node, mlen, cmp_, order=order0, runs=use_runs, chunks=chunks,
+                       n_tokens=ntok, tokens_per_item=tokens_per_item)
 
     ms_w, _ = timed(run_warm, steps, warmup, world)
     warm_ms = ms_w / (steps * len(packed))
@@ -820,7 +830,8 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": match_traffic(n_seqs) if use_runs else None,
             "peak_source": peak_kind,
-            "kernel": f"akv match_prefix (k_match), one {nq}-query batch",
+            "kernel": (f"akv match_prefix_split (k_match_items + k_match_split), one {nq}-query batch" if split
+                       else f"akv match_prefix (k_match), one {nq}-query batch"),
             "algorithmic_bytes_per_launch": alg,
             "note": "compulsory bytes: 4 B per query token compared, 4 B per distinct edge token touched, "
                     f"{MATCH_NODE_BYTES} B per distinct visited node (rank 0's batches); the kernel is "
@@ -849,7 +860,8 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         "replica_sync_s": round(sync_s, 2),
         "query_tokens_per_batch": int(statistics.mean(qtokens)),
         "unary_runs": bool(use_runs),
-        "verify_chunks": chunks or 4,
+        "verify_chunks": chunks or (8 if split else 4),
+        "split": {"tokens_per_item": tokens_per_item or 1024} if split else None,
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
@@ -1358,7 +1370,8 @@ def main():
         fig = match_figure(args.steps, args.warmup, args.match_seqs, args.match_queries, rank, world,
                            use_runs=bool(args.match_runs),
                            cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds,
-                           chunks=args.match_chunks)
+                           chunks=args.match_chunks, split=bool(args.match_split),
+                           tokens_per_item=args.match_tokens_per_item)
         if rank == 0:
             print(json.dumps(fig), flush=True)
         if world > 1:

@@ -428,6 +428,32 @@ AKV_API int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* tok
                                      const int32_t* order, AkvStatus* status, int32_t chunks,
                                      void* stream);
 
+/* Bytes of scratch akv_match_prefix_split needs for nq queries holding
+ * n_tokens tokens in all, at tokens_per_item (0 = default, 1024); -1 for
+ * arguments it would refuse. */
+AKV_API int64_t akv_match_scratch_bytes(int32_t nq, int64_t n_tokens, int32_t tokens_per_item);
+
+/* The same answers as akv_match_prefix_variant (the reference's
+ * _match_prefix_locked, agentkv/core/radix_tree.py:513-570, per query),
+ * with a query's token positions cut into ranges of tokens_per_item tokens
+ * (a multiple of 32; 0 = 1024), one warp per range, so a long query no
+ * longer holds the batch: each warp walks the tree to the end of its range,
+ * compares that range only, and the last warp of a query to finish picks
+ * the earliest stop among its ranges.  n_tokens = q_off[nq] - q_off[0]
+ * (an upper bound is fine: it sizes the launch).  `scratch` is
+ * caller-owned device memory of akv_match_scratch_bytes(nq, n_tokens,
+ * tokens_per_item) bytes, 16-byte aligned; its contents need no clearing
+ * and calls that share it must be ordered (one stream).  `order` as in
+ * akv_match_prefix_variant (a repeated or out-of-range entry sets
+ * AKV_ERR_INVALID_ARG in `status` and writes no answers); chunks: 32-token
+ * chunks compared per verify step (0 = 8).  Two launches. */
+AKV_API int akv_match_prefix_split(const AkvTreeView* tree, const int32_t* tokens,
+                                   const int64_t* q_off, int32_t nq, int64_t n_tokens,
+                                   int32_t block_size, int32_t* out_node, int32_t* out_len,
+                                   int64_t* out_compared, const int32_t* order, void* scratch,
+                                   int64_t scratch_bytes, int32_t tokens_per_item, int32_t chunks,
+                                   AkvStatus* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,9 +1,10 @@
 """Generate golden fixtures by running the reference AgentKV implementation.
 
-Run in a container that has the reference checked out (read-only) at
-/root/reference:
+Run where a checkout of the reference exists (it is only read), naming it
+with --reference or the AGENTKV_REFERENCE environment variable:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [--skip-full-match]
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py \
+        --reference /root/reference [--skip-full-match]
 
 It imports the reference's own `agentkv` package and records, for seeded
 inputs, what the reference's code returns: allocator op traces (ids,
@@ -19,6 +20,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import os
 import random
 import sys
 import time
@@ -26,7 +28,23 @@ from pathlib import Path
 
 import numpy as np
 
-REF = Path("/root/reference")
+def _reference_root() -> Path:
+    """The reference checkout: --reference PATH, else $AGENTKV_REFERENCE."""
+    argv = sys.argv[1:]
+    for i, a in enumerate(argv):
+        if a == "--reference" and i + 1 < len(argv):
+            return Path(argv[i + 1])
+        if a.startswith("--reference="):
+            return Path(a.split("=", 1)[1])
+    env = os.environ.get("AGENTKV_REFERENCE")
+    if env:
+        return Path(env)
+    sys.exit("make_golden.py: name the reference checkout with --reference PATH or AGENTKV_REFERENCE")
+
+
+REF = _reference_root()
+if not (REF / "agentkv" / "core" / "radix_tree.py").exists():
+    sys.exit(f"make_golden.py: {REF} does not hold the reference's agentkv package")
 OUT = Path(__file__).resolve().parent
 REPO = OUT.parent.parent
 sys.path.insert(0, str(REF))
@@ -640,6 +658,7 @@ def match_scenarios() -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", help="the reference checkout (read at import time above)")
     ap.add_argument("--skip-full-match", action="store_true")
     ap.add_argument("--only", default="")
     args = ap.parse_args()

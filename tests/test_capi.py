@@ -145,3 +145,36 @@ def test_host_argument_checks_of_kv_io():
     assert N.lib.akv_kv_gather(P, 8, 2, 2, 16, 256, 0, P, 1, 0, P, P, None, None) == N.AKV_OK
     rc = N.lib.akv_kv_scatter(P, 8, 2, 2, 16, 256, 5, P, 1, P, P, 256, 512, None, None)
     assert rc == N.AKV_ERR_INVALID_ARG
+
+
+def test_host_argument_checks_of_noalloc_decref():
+    """akv_decref_batch_noalloc refuses on the host, before any CUDA call:
+    an incomplete state, a pool larger than its static scratch covers, a bad
+    tick, a NULL status or ids, a negative count; an empty batch is a no-op.
+    (Dummy pointers: nothing is dereferenced.)"""
+    P = 16
+    tick = N.AkvTick(0, 0, 64, 0)
+
+    def state(n_blocks, ref=P):
+        return N.AkvAllocState(ref, P, P, P, P, None, None, None, n_blocks, 0)
+
+    f = N.lib.akv_decref_batch_noalloc
+    rc = f(C.byref(state(64, ref=None)), P, 1, C.byref(tick), None, P, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "incomplete" in N.last_error()
+    big = state(N.NOALLOC_MAX_BLOCKS + 1)
+    rc = f(C.byref(big), P, 1, C.byref(tick), None, P, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "exceeds" in N.last_error()
+    assert str(N.NOALLOC_MAX_BLOCKS) in N.last_error()
+    ok = state(N.NOALLOC_MAX_BLOCKS)
+    rc = f(C.byref(ok), P, 1, C.byref(N.AkvTick(0, 0, 0, 0)), None, P, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "tick" in N.last_error()
+    rc = f(C.byref(ok), P, 1, C.byref(tick), None, None, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "status" in N.last_error()
+    rc = f(C.byref(ok), P, -1, C.byref(tick), None, P, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "n=-1" in N.last_error()
+    rc = f(C.byref(ok), None, 3, C.byref(tick), None, P, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "ids is NULL" in N.last_error()
+    # an empty batch returns before the scratch lookup (no CUDA call); an
+    # oversized pool is refused even then
+    assert f(C.byref(ok), None, 0, C.byref(tick), None, P, None) == N.AKV_OK
+    assert f(C.byref(big), None, 0, C.byref(tick), None, P, None) == N.AKV_ERR_INVALID_ARG

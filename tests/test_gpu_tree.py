@@ -256,10 +256,18 @@ def test_match_prefix_stress_tree(golden_dir, name):
     # one hash probe per hop (no unary-chain runs): the same answers
     from agentkv_b200.device_tree import match_batch
 
-    hn, hl, hc = match_batch(pool._tree._dev_tree, queries, 16, with_compared=True, runs=False)
-    np.testing.assert_array_equal(hn, node)
-    np.testing.assert_array_equal(hl, mlen)
-    np.testing.assert_array_equal(hc, cmp_)
+    # with one hash probe per hop (no unary-chain runs), with one warp per
+    # query, and split into short ranges at every verify width: the same
+    # answers and comparison counts
+    for runs, split, tpi, chunks in ((False, True, 0, 0), (True, False, 0, 0), (False, False, 0, 4),
+                                     (True, True, 32, 1), (True, True, 64, 2), (False, True, 96, 4),
+                                     (True, True, 256, 8), (True, True, 512, 16), (True, True, 2048, 8)):
+        hn, hl, hc = match_batch(pool._tree._dev_tree, queries, 16, with_compared=True, runs=runs,
+                                 split=split, tokens_per_item=tpi, chunks=chunks)
+        tag = f"runs={runs} split={split} tokens_per_item={tpi} chunks={chunks}"
+        np.testing.assert_array_equal(hn, node, err_msg=tag)
+        np.testing.assert_array_equal(hl, mlen, err_msg=tag)
+        np.testing.assert_array_equal(hc, cmp_, err_msg=tag)
 
 
 def _oracle_tree_from(pool) -> dict:
@@ -309,6 +317,46 @@ def test_match_edge_cases():
     assert pool._tree._match_prefix_locked([100, 101, 102, 9]) == (-1, 0)
     node, mlen = pool.match_prefix_batch([[100, 101, 102], list(range(9)), []])
     assert mlen.tolist() == [0, 8, 0]
+    # split lookups: empty queries, lengths at and across range boundaries
+    from agentkv_b200.device_tree import match_batch
+
+    qs = [[], list(range(32)), list(range(12)) + [7] * 52, [100, 101, 102], list(range(8)) + [5] * 56, [0]]
+    for tpi in (0, 32, 64):
+        node, mlen, cmp_ = match_batch(pool._tree._dev_tree, qs, 4, with_compared=True, split=True,
+                                       tokens_per_item=tpi)
+        w_node, w_len, w_cmp = match_batch(pool._tree._dev_tree, qs, 4, with_compared=True, split=False)
+        assert mlen.tolist() == w_len.tolist() == [0, 8, 8, 0, 8, 0], tpi
+        assert cmp_.tolist() == w_cmp.tolist(), tpi
+        assert [n if m else -1 for n, m in zip(node, mlen)] == [n if m else -1 for n, m in zip(w_node, w_len)]
+
+
+def test_split_match_rejects_a_repeated_order_entry():
+    """A launch order that lists a query twice would make two warps finish
+    the same query: the split lookup reports it in the tree's status and
+    writes no answers."""
+    import torch
+
+    cfg = PoolConfig(total_blocks=64, block_size=4, num_layers=1, num_kv_heads=1, head_dim=1,
+                     dtype="float16", device="meta")
+    pool = AgentKVPool(config=cfg)
+    h = pool.create_root(list(range(12)))
+    pool.allocate_blocks(h, 3)
+    pool.commit_prefix(h, 8)
+    t = pool._tree._dev_tree
+    dev = t.device
+    tok = torch.arange(20, dtype=torch.int32, device=dev)
+    off = torch.tensor([0, 10, 20], dtype=torch.int64, device=dev)
+    node = torch.full((2,), 7, dtype=torch.int32, device=dev)
+    mlen = torch.full((2,), 7, dtype=torch.int32, device=dev)
+    order = torch.tensor([1, 1], dtype=torch.int32, device=dev)
+    t.match(tok, off, 2, 4, node, mlen, None, order=order, n_tokens=20, tokens_per_item=32)
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        t.check()
+    assert node.tolist() == [7, 7] and mlen.tolist() == [7, 7]
+    t.match(tok, off, 2, 4, node, mlen, None, order=torch.tensor([1, 0], dtype=torch.int32, device=dev),
+            n_tokens=20, tokens_per_item=32)
+    t.check()
+    assert mlen.tolist() == [8, 0]
 
 
 @pytest.mark.parametrize("mode", ["tree", "levels"])
@@ -416,7 +464,8 @@ def test_match_long_unary_chains():
     inside edges) and running past the chain's end give the oracle's
     (node, length, tokens compared), with the unary-chain runs (up to 32 hops
     per load, across the 32-hop segment boundary) and with one hash probe
-    per hop."""
+    per hop; one warp per query and split into ranges of 32 to 96 tokens
+    (stops at range boundaries, ranges past the walk's end)."""
     from agentkv_b200.device_tree import match_batch
 
     bs = 4
@@ -444,10 +493,12 @@ def test_match_long_unary_chains():
         queries.append(q)
     dev_tree = pool._tree._dev_tree
     want = [ot.match(q) for q in queries]
-    for runs in (True, False):
-        node, mlen, cmp_ = match_batch(dev_tree, queries, bs, with_compared=True, runs=runs)
+    for runs, split, tpi in ((True, True, 0), (False, True, 0), (True, False, 0), (False, False, 0),
+                             (True, True, 32), (False, True, 32), (True, True, 64), (True, True, 96)):
+        node, mlen, cmp_ = match_batch(dev_tree, queries, bs, with_compared=True, runs=runs, split=split,
+                                       tokens_per_item=tpi)
         got = [(int(n) if m else -1, int(m), int(c)) for n, m, c in zip(node, mlen, cmp_)]
-        assert got == [(int(n) if m else -1, int(m), int(c)) for n, m, c in want], runs
+        assert got == [(int(n) if m else -1, int(m), int(c)) for n, m, c in want], (runs, split, tpi)
     assert dev_tree.d_run_head is not None and int((dev_tree.d_run_head >= 0).sum()) >= 60
 
 
@@ -479,7 +530,7 @@ def test_match_prefix_many_equals_one_by_one(golden_dir):
 def test_match_scenarios_match_reference(golden_dir, name):
     """The hard lookup shapes of tests/match_scenarios.py on the device pool,
     with the unary-chain runs and with one probe per hop: the reference's
-    recorded (node, length) per query."""
+    recorded (node, length) per query, whole and split into 32-token ranges."""
     from agentkv_b200.device_tree import match_batch
     from match_scenarios import SCENARIOS, build
 
@@ -488,6 +539,8 @@ def test_match_scenarios_match_reference(golden_dir, name):
     pool = AgentKVPool(config=PoolConfig(total_blocks=1024, block_size=sc["block_size"], num_layers=1,
                                          num_kv_heads=1, head_dim=4, dtype="float16", device="meta"))
     build(pool, sc, pool.allocate_block)
-    for runs in (True, False):
-        node, mlen = match_batch(pool._tree._dev_tree, sc["queries"], sc["block_size"], runs=runs)
-        assert [[int(n) if m else -1, int(m)] for n, m in zip(node, mlen)] == want, runs
+    for runs, split, tpi in ((True, True, 0), (False, True, 0), (True, False, 0), (False, True, 32),
+                             (True, True, 32)):
+        node, mlen = match_batch(pool._tree._dev_tree, sc["queries"], sc["block_size"], runs=runs,
+                                 split=split, tokens_per_item=tpi)
+        assert [[int(n) if m else -1, int(m)] for n, m in zip(node, mlen)] == want, (runs, split, tpi)

@@ -263,9 +263,9 @@ def test_tree_orchestration_with_kernel_model(monkeypatch):
     replaced by their CPU model (tests/tree_kernel_model.py): DualRadixTree
     inserts mirrored into an owner DeviceTree (full and incremental deltas),
     a replica fed by TreeReplicaSync deltas with the owner's unary-chain runs,
-    and batched lookups under the rebuild policy, with runs and without —
-    all equal to the oracle's C match over the same host tree, comparison
-    counts included."""
+    and batched lookups under the rebuild policy, with runs and without, whole
+    and split into ranges of 32 to 96 tokens — all equal to the oracle's C
+    match over the same host tree, comparison counts included."""
     import torch
 
     from agentkv_b200 import _native as N
@@ -316,13 +316,18 @@ def test_tree_orchestration_with_kernel_model(monkeypatch):
         if i % 21 == 20:
             want = O.match_prefix_csr(_csr_of(tree._shared_nodes), flat, q_off, 16)
             want_node = np.where(want[1] > 0, want[0], -1)
-            for t, runs in ((owner, None), (owner, False), (replica, None)):
-                node, mlen, cmp_ = DT.match_batch(t, queries, 16, with_compared=True, runs=runs)
-                np.testing.assert_array_equal(mlen, want[1], err_msg=f"{i} {runs}")
+            # the split lookup at the default range and at ranges far shorter
+            # than the queries (many ranges per query, stops in any of them)
+            for t, runs, tpi in ((owner, None, 0), (owner, False, 0), (replica, None, 0), (owner, True, 32),
+                                 (replica, False, 64), (owner, None, 96)):
+                node, mlen, cmp_ = DT.match_batch(t, queries, 16, with_compared=True, runs=runs,
+                                                  tokens_per_item=tpi)
+                np.testing.assert_array_equal(mlen, want[1], err_msg=f"{i} {runs} {tpi}")
                 np.testing.assert_array_equal(np.where(mlen > 0, node, -1), want_node)
                 np.testing.assert_array_equal(cmp_, want[2])
             checks += 1
     assert checks >= 10 and model.run_hops > 1000, (checks, model.run_hops)
+    assert model.split_ranges > 20 * checks * len(queries), model.split_ranges
     # the replica's arrays equal the owner's after a final sync
     owner.build_runs()
     d = sync.share()

@@ -5,10 +5,11 @@ engine reserved all free GPU memory up front).  It keeps its work space in a
 static device array inside the library instead of caller-provided scratch.
 
 Checked through the C ABI against akv_decref_batch on identical allocator
-states, for two calls in a row: refcounts, free-list order, reclaimer
-queues, counters and the retired ids must be identical (integer work:
-bit-exact).  This file is collected last so that a failure here leaves
-every other test already run.
+states, for two calls in a row, with no reader open and with readers open
+(the retired ids then wait in the reclaimer's pending queue until the
+readers leave): refcounts, free-list order, reclaimer queues, counters and
+the retired ids must be identical (integer work: bit-exact).  This file is
+collected last so that a failure here leaves every other test already run.
 """
 
 import ctypes as C
@@ -43,17 +44,25 @@ def _same(a, b):
         np.testing.assert_array_equal(sa[k], sb[k], err_msg=k)
 
 
-def test_noalloc_decref_matches_decref_batch():
+def _compare_two_calls(readers: bool):
     n_blocks = 5000
-    rng = np.random.default_rng(2024)
+    rng = np.random.default_rng(2024 + readers)
     a, b = _alloc(n_blocks), _alloc(n_blocks)
     for x in (a, b):
         x.alloc_batch(3000)
-    live = a.alloc_batch(0)  # no-op, keeps both states identical
     ids = np.arange(n_blocks - 3000, n_blocks, dtype=np.int32)[::-1].copy()
     extra = np.repeat(ids, rng.integers(0, 3, size=len(ids)))
     for x in (a, b):
         x.inc_ref_batch(extra)
+    tokens = []
+    if readers:
+        # Move the epoch on, then open two readers (the epoch stays put while
+        # a reader holds it): ids retired now must wait in the pending queue,
+        # tagged with their op's epoch, instead of returning to the free list.
+        for x in (a, b):
+            for _ in range(3):
+                x.maybe_advance_epoch()
+            tokens.append((x, x.enter_read_section(), x.enter_read_section()))
     a.check()
     b.check()
     _same(a, b)
@@ -83,14 +92,20 @@ def test_noalloc_decref_matches_decref_batch():
         assert n_ret > 0
         np.testing.assert_array_equal(out_a.cpu().numpy(), out_b.cpu().numpy())
         refs = a._ref_counts.cpu().numpy()
-    del live
+    if readers:
+        assert a._reclaimer.pending_count() > 0
+        for x, t0, t1 in tokens:
+            x.leave_read_section(t0)
+            x.leave_read_section(t1)
+        a.check()
+        b.check()
+        _same(a, b)
+        assert a._reclaimer.pending_count() == 0
 
 
-def test_noalloc_rejects_states_beyond_its_scratch():
-    big = _alloc(N.NOALLOC_MAX_BLOCKS + 1)
-    ids = torch.zeros(1, dtype=torch.int32, device=big.device)
-    rc = N.lib.akv_decref_batch_noalloc(big._state, ids.data_ptr(), 1, big._tick(), None,
-                                        big._status.data_ptr(), torch.cuda.current_stream(big.device).cuda_stream)
-    assert rc == N.AKV_ERR_INVALID_ARG
-    assert "exceeds" in N.last_error()
-    assert int(big._ref_counts[0].item()) == 0
+def test_noalloc_decref_matches_decref_batch():
+    _compare_two_calls(readers=False)
+
+
+def test_noalloc_decref_with_open_readers_matches_decref_batch():
+    _compare_two_calls(readers=True)

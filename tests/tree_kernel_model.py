@@ -1,5 +1,5 @@
-"""CPU model of the two tree kernels — akv_tree_apply and
-akv_match_prefix_variant — reading the same AkvTreeView arrays from host
+"""CPU model of the tree kernels — akv_tree_apply, akv_match_prefix_variant
+and akv_match_prefix_split — reading the same AkvTreeView arrays from host
 memory, so that CPU tests can run the host-side orchestration of the device
 tree (deltas, replicas, unary-chain runs, their rebuild policy) on CPU
 DeviceTrees.  Test infrastructure only: the package's lookups run the CUDA
@@ -10,7 +10,11 @@ a node with a run it takes hops from consecutive run entries (as the kernel
 does), elsewhere from the slot table's linear probe; every hop's edge tokens
 are compared the way the reference loop (agentkv/core/radix_tree.py:
 513-570) compares them, counting comparisons; the match is floored to the
-block size, (-1, 0) when nothing is credited.
+block size, (-1, 0) when nothing is credited.  The split model restates the
+range decomposition: each range [a, b) of a query's positions walks the
+same hops, compares only its own positions and reports its first stop as a
+key (2 x position + mismatch); the smallest key over a query's ranges gives
+the answer.
 """
 
 from __future__ import annotations
@@ -52,18 +56,10 @@ class TreeKernelModel:
             ln[r[0]] = r[2]
         return 0
 
-    def akv_match_prefix_variant(self, view, tokens, q_off, nq, block_size, out_node, out_len, out_cmp,
-                                 order, status, chunks, stream) -> int:
-        self.match_calls += 1
+    def _walker(self, view):
+        """next_hop(node, token, pending) for the view: run entries where the
+        node has a run, else the slot table's linear probe."""
         slots = _arr(view.slots, C.c_int32, (view.slot_mask + 1, 4))
-        off = _arr(view.node_edge_off, C.c_int64, (view.n_nodes,))
-        elen = _arr(view.node_edge_len, C.c_int32, (view.n_nodes,))
-        arena = _arr(view.tokens, C.c_int32, (view.n_tokens,))
-        qo = _arr(q_off, C.c_int64, (nq + 1,))
-        q_all = _arr(tokens, C.c_int32, (int(qo[-1]),))
-        o_node = _arr(out_node, C.c_int32, (nq,))
-        o_len = _arr(out_len, C.c_int32, (nq,))
-        o_cmp = _arr(out_cmp, C.c_int64, (nq,)) if out_cmp else None
         runs = view.run_head is not None and view.run_head != 0
         if runs:
             head = _arr(view.run_head, C.c_int32, (view.run_nodes,))
@@ -81,6 +77,36 @@ class TreeKernelModel:
                 i = (i + 1) & mask
             return -1, 0
 
+        def next_hop(node, t, pending):
+            if not pending and runs and node < view.run_nodes and head[node] >= 0:
+                rp = int(head[node])
+                rem = int(ent[rp, 3])
+                assert rem >= 1 and rp + rem <= view.n_runs, (node, rp, rem)
+                pending.extend(tuple(int(x) for x in ent[rp + k]) for k in range(rem))
+            if pending:
+                c, tok, cl, _ = pending.pop(0)
+                self.run_hops += 1
+                return (c, cl) if t == tok else (-1, 0)
+            return probe(node, t)
+
+        return next_hop
+
+    def _arrays(self, view, tokens, q_off, nq):
+        off = _arr(view.node_edge_off, C.c_int64, (view.n_nodes,))
+        elen = _arr(view.node_edge_len, C.c_int32, (view.n_nodes,))
+        arena = _arr(view.tokens, C.c_int32, (view.n_tokens,))
+        qo = _arr(q_off, C.c_int64, (nq + 1,))
+        q_all = _arr(tokens, C.c_int32, (int(qo[-1]),))
+        return off, elen, arena, qo, q_all
+
+    def akv_match_prefix_variant(self, view, tokens, q_off, nq, block_size, out_node, out_len, out_cmp,
+                                 order, status, chunks, stream) -> int:
+        self.match_calls += 1
+        next_hop = self._walker(view)
+        off, elen, arena, qo, q_all = self._arrays(view, tokens, q_off, nq)
+        o_node = _arr(out_node, C.c_int32, (nq,))
+        o_len = _arr(out_len, C.c_int32, (nq,))
+        o_cmp = _arr(out_cmp, C.c_int64, (nq,)) if out_cmp else None
         for q in range(nq):
             Q = q_all[qo[q]:qo[q + 1]]
             L = len(Q)
@@ -88,17 +114,7 @@ class TreeKernelModel:
             node = 0
             pending = []  # run entries still to use, in order
             while d < L:
-                if not pending and runs and node < view.run_nodes and head[node] >= 0:
-                    rp = int(head[node])
-                    rem = int(ent[rp, 3])
-                    assert rem >= 1 and rp + rem <= view.n_runs, (node, rp, rem)
-                    pending = [tuple(int(x) for x in ent[rp + k]) for k in range(rem)]
-                if pending:
-                    c, t, cl, _ = pending.pop(0)
-                    self.run_hops += 1
-                    child, clen = (c, cl) if int(Q[d]) == t else (-1, 0)
-                else:
-                    child, clen = probe(node, int(Q[d]))
+                child, clen = next_hop(node, int(Q[d]), pending)
                 if child < 0:
                     break
                 assert int(elen[child]) == clen, (child, int(elen[child]), clen)
@@ -116,4 +132,57 @@ class TreeKernelModel:
             o_len[q] = m
             if o_cmp is not None:
                 o_cmp[q] = compared
+        return 0
+
+    def akv_match_prefix_split(self, view, tokens, q_off, nq, n_tokens, block_size, out_node, out_len,
+                               out_cmp, order, scratch, scratch_bytes, tokens_per_item, chunks, status,
+                               stream) -> int:
+        self.match_calls += 1
+        R = tokens_per_item or 1024
+        need = self._real.akv_match_scratch_bytes(nq, n_tokens, tokens_per_item)
+        assert need >= 0 and scratch_bytes >= need, (need, scratch_bytes)
+        next_hop = self._walker(view)
+        off, elen, arena, qo, q_all = self._arrays(view, tokens, q_off, nq)
+        assert int(qo[-1] - qo[0]) <= n_tokens, (int(qo[-1]), n_tokens)
+        o_node = _arr(out_node, C.c_int32, (nq,))
+        o_len = _arr(out_len, C.c_int32, (nq,))
+        o_cmp = _arr(out_cmp, C.c_int64, (nq,)) if out_cmp else None
+        self.split_ranges = getattr(self, "split_ranges", 0)
+
+        def range_stop(Q, a, b):
+            """(key, matched, node) of the first stop range [a, b) sees, or
+            None when the walk passes b without one."""
+            L = len(Q)
+            cur, d, pending = 0, 0, []
+            while True:
+                if d >= L:
+                    return 2 * d, d, cur
+                if d >= b:
+                    return None
+                child, clen = next_hop(cur, int(Q[d]), pending)
+                if child < 0 or clen == 0:
+                    return 2 * d, d, cur
+                assert int(elen[child]) == clen, (child, int(elen[child]), clen)
+                lim = min(clen, L - d)
+                lo, hi = max(a, d), min(b, d + lim)
+                if lo < hi:
+                    ne = np.flatnonzero(Q[lo:hi] != arena[off[child] + lo - d:off[child] + hi - d])
+                    if len(ne):
+                        return 2 * (lo + int(ne[0])) + 1, d, cur
+                if lim < clen:  # the edge runs past the query's end
+                    return 2 * L, d, cur
+                d += clen
+                cur = child
+
+        for q in range(nq):
+            Q = q_all[qo[q]:qo[q + 1]]
+            k = max(1, -(-len(Q) // R))
+            stops = [range_stop(Q, j * R, min((j + 1) * R, len(Q))) for j in range(k)]
+            self.split_ranges += k
+            key, matched, node = min(s for s in stops if s is not None)
+            m = (matched // block_size) * block_size
+            o_node[q] = node if m else -1
+            o_len[q] = m
+            if o_cmp is not None:
+                o_cmp[q] = (key >> 1) + (key & 1)
         return 0
