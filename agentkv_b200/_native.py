@@ -60,6 +60,8 @@ CTL_WORDS = 16
 AUX_WORDS = 2048
 NOALLOC_MAX_BLOCKS = 262144
 MAX_FANOUT_LEVELS = 16  # AKV_MAX_FANOUT_LEVELS
+MATCH_PIPELINED = 0x100  # AKV_MATCH_PIPELINED
+MATCH_MAX_RANGES = 64  # AKV_MATCH_MAX_RANGES
 
 # Copy kernel variants (akv_copy_blocks_variant).
 VARIANT_AUTO = 0
@@ -170,9 +172,10 @@ SIGNATURES = {
         [C.POINTER(AkvTreeView), _P, _P, _I32, _I32, _P, _P, _P, _P, _P, _I32, _P],
     ),
     "akv_match_scratch_bytes": (C.c_int64, [_I32, _I64, _I32]),
+    "akv_match_split_plan": (C.c_int, [_P, _I32, _I32, _P, _P]),
     "akv_match_prefix_split": (
         C.c_int,
-        [C.POINTER(AkvTreeView), _P, _P, _I32, _I64, _I32, _P, _P, _P, _P, _P, _I64, _I32, _I32, _P, _P],
+        [C.POINTER(AkvTreeView), _P, _P, _I32, _I32, _P, _P, _P, _P, _P, _I32, _I32, _P, _I64, _I32, _P, _P],
     ),
 }
 

@@ -107,7 +107,7 @@ constexpr int64_t kNoStop = INT64_MAX;  // the range ends before the walk does
 // are not looked for: the range that holds them reports them, and the
 // smallest key over all ranges wins.  With a = 0 and b = L this is the whole
 // lookup.
-template <int kVerifyChunks>
+template <int kVerifyChunks, bool kPipelined>
 AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict__ Q, int64_t L,
                               int64_t a, int64_t b, int32_t q, AkvStatus* st, int lane) {
   constexpr uint32_t kFull = 0xffffffffu;
@@ -288,13 +288,15 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
       return lo;
     };
     int32_t first = -1;
-    for (int32_t base = p_lo; base < p_hi; base += 32 * kVerifyChunks) {
-      int32_t av[kVerifyChunks], bv[kVerifyChunks];
-      // Fast path: the whole step lies inside one edge (long edges).
+    constexpr int32_t kStep = 32 * kVerifyChunks;
+    // One verify round: kVerifyChunks x 32 consecutive flattened positions
+    // from `base`, query tokens into av, edge tokens into bv.
+    auto load_round = [&](int32_t base, int32_t (&av)[kVerifyChunks], int32_t (&bv)[kVerifyChunks]) {
+      // Fast path: the whole round lies inside one edge (long edges).
       const int e0 = entry_of(base);
       const int32_t ex0 = __shfl_sync(kFull, excl, e0);
       const int32_t lim0 = __shfl_sync(kFull, lim, e0);
-      if (ex0 + lim0 >= base + 32 * kVerifyChunks || e0 == n - 1) {
+      if (ex0 + lim0 >= base + kStep || e0 == n - 1) {
         const int64_t de = __shfl_sync(kFull, my_d, e0) - ex0;
         const int64_t oe = __shfl_sync(kFull, my_off, e0) - ex0;
 #pragma unroll
@@ -317,12 +319,37 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
           bv[u] = ok ? __ldg(&tree.tokens[oe + j]) : 0;
         }
       }
+    };
+    auto check_round = [&](int32_t base, const int32_t (&av)[kVerifyChunks],
+                           const int32_t (&bv)[kVerifyChunks]) {
 #pragma unroll
       for (int u = 0; u < kVerifyChunks; ++u) {
         const uint32_t m = __ballot_sync(kFull, av[u] != bv[u]);
         if (m && first < 0) first = base + u * 32 + __ffs(m) - 1;
       }
-      if (first >= 0) break;
+    };
+    if constexpr (kPipelined) {
+      // Two rounds in flight: the next round's loads are issued before this
+      // round's compare (a round past a mismatch is loaded and discarded;
+      // every position loaded lies below p_hi, inside the query and the
+      // edge).
+      int32_t a0[kVerifyChunks], b0[kVerifyChunks], a1[kVerifyChunks], b1[kVerifyChunks];
+      if (p_lo < p_hi) load_round(p_lo, a0, b0);
+      for (int32_t base = p_lo; base < p_hi; base += 2 * kStep) {
+        if (base + kStep < p_hi) load_round(base + kStep, a1, b1);
+        check_round(base, a0, b0);
+        if (first >= 0 || base + kStep >= p_hi) break;
+        if (base + 2 * kStep < p_hi) load_round(base + 2 * kStep, a0, b0);
+        check_round(base + kStep, a1, b1);
+        if (first >= 0) break;
+      }
+    } else {
+      for (int32_t base = p_lo; base < p_hi; base += kStep) {
+        int32_t av[kVerifyChunks], bv[kVerifyChunks];
+        load_round(base, av, bv);
+        check_round(base, av, bv);
+        if (first >= 0) break;
+      }
     }
     // the first entry the reference would stop in
     const int e_mis = first >= 0 ? entry_of(first) : kSegment;
@@ -358,7 +385,7 @@ AKV_DEV void match_write(const MatchStop& s, int32_t q, int32_t block_size, int3
 // One warp per query (the whole query is one range).  `order` (optional)
 // lists the queries longest first, so the long walks start early and spread
 // over the SMs.
-template <int kVerifyChunks>
+template <int kVerifyChunks, bool kPipelined>
 __global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
 k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
         int32_t nq, int32_t block_size, int32_t* __restrict__ out_node,
@@ -374,49 +401,42 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
   }
   const int64_t qlo = q_off[q];
   const int64_t L = q_off[q + 1] - qlo;
-  const MatchStop s = match_range<kVerifyChunks>(tree, tokens + qlo, L, 0, L, q, st, lane);
+  const MatchStop s = match_range<kVerifyChunks, kPipelined>(tree, tokens + qlo, L, 0, L, q, st, lane);
   if (lane == 0) match_write(s, q, block_size, out_node, out_len, out_compared);
 }
 
 // ── split lookups: a query's positions in ranges of R tokens, one warp each ──
 // A batch is bounded by its longest query when one warp walks each query
-// (an 8,192-token query is 64 dependent verify rounds of 128 tokens).  Here
-// query q is cut into k_q = max(1, ceil(L_q / R)) ranges ("items"); the warp
-// of item j walks the tree up to position (j + 1) R and compares positions
-// [j R, (j + 1) R) only, so every warp does at most R tokens of comparison
-// and the SMs stay evenly loaded.  Each item reports the first stop it sees
-// (MatchStop); the warp that finishes a query's last item picks the smallest
-// key among them, which is the stop of the reference's loop.
+// (an 8,192-token query is 32 dependent verify rounds of 256 tokens).  Here
+// query q is cut into k_q = max(1, ceil(L_q / R)) ranges; the warp of range
+// j walks the tree up to position (j + 1) R and compares positions
+// [j R, (j + 1) R) only, so every warp compares at most R tokens and the
+// SMs stay evenly loaded.  Each range reports the first stop it sees
+// (MatchStop); the warp that finishes a query's last range picks the
+// smallest key among them, which is the stop of the reference's loop.
 //
-// Scratch (caller-owned, akv_match_scratch_bytes): a 256-byte header (the
-// item count), one 16-byte stop record per item, the item list {q, j} and a
-// per-query count of finished items.
-constexpr int64_t kSplitHeader = 256;
+// The queries are launched longest first (`order`), so range j exists for
+// exactly the first n_j ranks: warp w takes range j of rank w - start[j],
+// where start[j] = n_0 + ... + n_{j-1}; the host passes start[] (it knows
+// the lengths), so no list of ranges is built on the device.
+//
+// Scratch (caller-owned, akv_match_scratch_bytes): one 16-byte stop record
+// per range, then a per-query count of finished ranges that each query's
+// last range puts back to zero.
+constexpr int kMaxSplitRanges = AKV_MATCH_MAX_RANGES;
+
+struct SplitRanges {
+  int64_t start[kMaxSplitRanges + 1];  // start[j]: first warp of range j; start[n] = total
+  int32_t n;                           // ranges of the longest query
+  int32_t R;                           // tokens per range
+};
 
 AKV_HD int64_t split_items_max(int32_t nq, int64_t n_tokens, int32_t R) {
   return static_cast<int64_t>(nq) + n_tokens / R;  // sum of max(1, ceil(L/R)) <= nq + sum(L)/R
 }
 
-struct SplitScratch {
-  int32_t* n_items;
-  int4* stops;
-  int2* items;
-  int32_t* done;
-};
-
-AKV_HD SplitScratch split_scratch(void* base, int32_t nq, int64_t w_max) {
-  char* p = static_cast<char*>(base);
-  SplitScratch s;
-  s.n_items = reinterpret_cast<int32_t*>(p);
-  s.stops = reinterpret_cast<int4*>(p + kSplitHeader);
-  s.items = reinterpret_cast<int2*>(p + kSplitHeader + 16 * w_max);
-  s.done = reinterpret_cast<int32_t*>(p + kSplitHeader + 24 * w_max);
-  (void)nq;
-  return s;
-}
-
 AKV_HD int64_t split_scratch_bytes(int32_t nq, int64_t w_max) {
-  const int64_t b = kSplitHeader + 24 * w_max + 4 * static_cast<int64_t>(nq);
+  const int64_t b = 16 * w_max + 4 * static_cast<int64_t>(nq);
   return (b + 255) / 256 * 256;
 }
 
@@ -424,130 +444,63 @@ AKV_DEV int32_t split_count(int64_t L, int32_t R) {
   return L <= 0 ? 1 : static_cast<int32_t>((L + R - 1) / R);
 }
 
-// Lists the items, queries in `order` (longest first), each query's items
-// consecutive; clears the per-query counts.  One CTA.  A query listed twice
-// in `order`, an index out of range or a query longer than INT32_MAX is
-// reported (AKV_ERR_INVALID_ARG) and no item is listed.
-constexpr int kItemThreads = 1024;
-
-__global__ void __launch_bounds__(kItemThreads)
-k_match_items(const int64_t* __restrict__ q_off, const int32_t* __restrict__ order, int32_t nq,
-              int32_t R, int64_t w_max, SplitScratch sc, AkvStatus* st) {
-  __shared__ int64_t warp_sum[kItemThreads / 32];
-  __shared__ int64_t carry;
-  __shared__ int32_t bad;
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  if (tid == 0) {
-    carry = 0;
-    bad = 0;
-  }
-  for (int32_t i = tid; i < nq; i += kItemThreads) sc.done[i] = 0;
-  __syncthreads();
-  // `done` marks each listed query once, to catch repeats in `order`
-  for (int32_t r = tid; r < nq; r += kItemThreads) {
-    const int32_t q = order != nullptr ? order[r] : r;
-    if (static_cast<uint32_t>(q) >= static_cast<uint32_t>(nq) || atomicExch(&sc.done[q], 1) != 0) {
-      akv_fail(st, AKV_ERR_INVALID_ARG, r, q, nq);
-      bad = 1;
-      continue;
-    }
-    const int64_t L = q_off[q + 1] - q_off[q];
-    if (L < 0 || L > INT32_MAX) {
-      akv_fail(st, AKV_ERR_INVALID_ARG, r, q, nq, L);
-      bad = 1;
-    }
-  }
-  __syncthreads();
-  if (bad) {
-    if (tid == 0) *sc.n_items = 0;
-    return;
-  }
-  for (int32_t i = tid; i < nq; i += kItemThreads) sc.done[i] = 0;
-  for (int32_t base = 0; base < nq; base += kItemThreads) {
-    const int32_t r = base + tid;
-    int32_t q = 0, k = 0;
-    if (r < nq) {
-      q = order != nullptr ? order[r] : r;
-      k = split_count(q_off[q + 1] - q_off[q], R);
-    }
-    int64_t incl = k;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    if (lane == 31) warp_sum[wid] = incl;
-    __syncthreads();
-    if (wid == 0) {
-      int64_t v = warp_sum[lane];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int64_t y = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += y;
-      }
-      warp_sum[lane] = v;
-    }
-    __syncthreads();
-    const int64_t start = carry + (wid > 0 ? warp_sum[wid - 1] : 0) + incl - k;
-    for (int32_t j = 0; j < k; ++j) {
-      if (start + j < w_max) sc.items[start + j] = make_int2(q, j);
-    }
-    __syncthreads();
-    if (tid == 0) carry += warp_sum[kItemThreads / 32 - 1];
-    __syncthreads();
-  }
-  if (tid == 0) {
-    if (carry > w_max) {
-      akv_fail(st, AKV_ERR_INVALID_ARG, nq, static_cast<int32_t>(w_max), 0, carry);
-      *sc.n_items = 0;
-    } else {
-      *sc.n_items = static_cast<int32_t>(carry);
-    }
-  }
-}
-
-template <int kVerifyChunks>
+template <int kVerifyChunks, bool kPipelined>
 __global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
 k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
-              int32_t block_size, int32_t R, SplitScratch sc, int32_t* __restrict__ out_node,
-              int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared, AkvStatus* st) {
+              int32_t nq, int32_t block_size, const __grid_constant__ SplitRanges rg,
+              const int32_t* __restrict__ order, int4* __restrict__ stops, int32_t* __restrict__ done,
+              int32_t* __restrict__ out_node, int32_t* __restrict__ out_len,
+              int64_t* __restrict__ out_compared, AkvStatus* st) {
   constexpr uint32_t kFull = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const int64_t it = static_cast<int64_t>(blockIdx.x) * kMatchWarpsPerCta + (threadIdx.x >> 5);
-  if (it >= *sc.n_items) return;
-  const int2 qj = sc.items[it];
-  const int32_t q = qj.x, j = qj.y;
+  if (it >= rg.start[rg.n]) return;
+  int j = 0;  // range index: the last j with start[j] <= it
+  while (j + 1 < rg.n && rg.start[j + 1] <= it) ++j;
+  const int64_t r = it - rg.start[j];
+  const int32_t q = order[r];
+  if (static_cast<uint32_t>(q) >= static_cast<uint32_t>(nq)) {
+    if (lane == 0) akv_fail(st, AKV_ERR_INVALID_ARG, static_cast<int32_t>(r), q, nq);
+    return;
+  }
   const int64_t qlo = q_off[q];
   const int64_t L = q_off[q + 1] - qlo;
+  const int32_t R = rg.R;
+  const int32_t k = split_count(L, R);
+  // rank r must hold ranges 0 .. k-1 and no more: r < n_{k-1} and r >= n_k
+  const bool listed = k <= rg.n && r < rg.start[k] - rg.start[k - 1] &&
+                      (k == rg.n || r >= rg.start[k + 1] - rg.start[k]);
+  if (!listed || L > INT32_MAX) {
+    if (lane == 0 && j == 0) akv_fail(st, AKV_ERR_INVALID_ARG, static_cast<int32_t>(r), q, k, L);
+    return;
+  }
   const int64_t a = static_cast<int64_t>(j) * R;
   const int64_t b = a + R < L ? a + R : L;
-  const MatchStop s = match_range<kVerifyChunks>(tree, tokens + qlo, L, a, b, q, st, lane);
-  const int32_t k = split_count(L, R);
+  const MatchStop s = match_range<kVerifyChunks, kPipelined>(tree, tokens + qlo, L, a, b, q, st, lane);
   if (k == 1) {
     if (lane == 0) match_write(s, q, block_size, out_node, out_len, out_compared);
     return;
   }
   int32_t prior = 0;
   if (lane == 0) {
-    __stcg(&sc.stops[it], make_int4(static_cast<int32_t>(s.key & 0xffffffff), static_cast<int32_t>(s.key >> 32),
-                                    static_cast<int32_t>(s.matched), s.node));
+    __stcg(&stops[it], make_int4(static_cast<int32_t>(s.key & 0xffffffff), static_cast<int32_t>(s.key >> 32),
+                                 static_cast<int32_t>(s.matched), s.node));
     __threadfence();
-    prior = atomicAdd(&sc.done[q], 1);
+    prior = atomicAdd(&done[q], 1);
   }
   prior = __shfl_sync(kFull, prior, 0);
-  if (prior != k - 1) return;  // another item of this query finishes last
+  if (prior != k - 1) return;  // another range of this query finishes last
   __threadfence();
-  // the last item of query q: the smallest key over its k stop records
-  const int64_t first_item = it - j;
+  // the last range of query q: the smallest key over its k stop records
   int64_t best = kNoStop;
   int32_t b_matched = 0, b_node = -1;
   for (int32_t i = lane; i < k; i += 32) {
-    const int4 r = __ldcg(&sc.stops[first_item + i]);
-    const int64_t key = (static_cast<int64_t>(r.y) << 32) | static_cast<uint32_t>(r.x);
+    const int4 rec = __ldcg(&stops[rg.start[i] + r]);
+    const int64_t key = (static_cast<int64_t>(rec.y) << 32) | static_cast<uint32_t>(rec.x);
     if (key < best) {
       best = key;
-      b_matched = r.z;
-      b_node = r.w;
+      b_matched = rec.z;
+      b_node = rec.w;
     }
   }
 #pragma unroll
@@ -562,6 +515,7 @@ k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
     }
   }
   if (lane == 0) {
+    done[q] = 0;  // the scratch is left as it was found
     if (best == kNoStop) {  // cannot happen for a well-formed walk; never report a match then
       akv_fail(st, AKV_ERR_TREE, q, -1, k);
       best = 0;
@@ -598,19 +552,44 @@ __global__ void k_tree_apply(AkvTreeView tree, const int32_t* __restrict__ su, i
 
 }  // namespace
 
+// Every (verify width, pipelining) instantiation, in one table: the entry
+// points dispatch through it and akv_prepare loads it.
+struct MatchKernels {
+  int chunks;
+  bool pipelined;
+  decltype(&k_match<1, false>) whole;
+  decltype(&k_match_split<1, false>) split;
+};
+#define AKV_MATCH_ROW(c, p) {c, p, &k_match<c, p>, &k_match_split<c, p>}
+constexpr MatchKernels kMatchKernels[] = {
+    AKV_MATCH_ROW(1, false), AKV_MATCH_ROW(2, false), AKV_MATCH_ROW(4, false), AKV_MATCH_ROW(8, false),
+    AKV_MATCH_ROW(16, false), AKV_MATCH_ROW(2, true), AKV_MATCH_ROW(4, true), AKV_MATCH_ROW(8, true),
+};
+#undef AKV_MATCH_ROW
+
+const MatchKernels* match_kernels(int32_t chunks) {
+  const bool pipelined = (chunks & AKV_MATCH_PIPELINED) != 0;
+  const int c = chunks & ~AKV_MATCH_PIPELINED;
+  for (const MatchKernels& k : kMatchKernels)
+    if (k.chunks == c && k.pipelined == pipelined) return &k;
+  return nullptr;
+}
+
+template <typename F>
+int for_each_match_kernel(F&& f) {
+  for (const MatchKernels& k : kMatchKernels) {
+    if (int rc = f(reinterpret_cast<const void*>(k.whole), "akv_prepare: k_match")) return rc;
+    if (int rc = f(reinterpret_cast<const void*>(k.split), "akv_prepare: k_match_split")) return rc;
+  }
+  return AKV_OK;
+}
+
 int akv_tree_prepare() {
 #define AKV_LOAD(fn) if (int rc = akv_load_kernel(reinterpret_cast<const void*>(fn), "akv_prepare: " #fn)) return rc
-  AKV_LOAD(k_match<1>);
-  AKV_LOAD(k_match<2>);
-  AKV_LOAD(k_match<4>);
-  AKV_LOAD(k_match<8>);
-  AKV_LOAD(k_match<16>);
-  AKV_LOAD(k_match_items);
-  AKV_LOAD(k_match_split<1>);
-  AKV_LOAD(k_match_split<2>);
-  AKV_LOAD(k_match_split<4>);
-  AKV_LOAD(k_match_split<8>);
-  AKV_LOAD(k_match_split<16>);
+  if (int rc = for_each_match_kernel([](const void* fn, const char* name) {
+        return akv_load_kernel(fn, name);
+      }))
+    return rc;
   AKV_LOAD(k_tree_apply);
 #undef AKV_LOAD
   return AKV_OK;
@@ -664,8 +643,10 @@ int match_args_ok(const AkvTreeView* tree, const int32_t* tokens, const int64_t*
                 "%s: slot count %d is not a power of two >= 32", fn, tree->slot_mask + 1);
   AKV_ARG_CHECK(nq >= 0, "%s: nq=%d < 0", fn, nq);
   AKV_ARG_CHECK(block_size > 0, "%s: block_size=%d", fn, block_size);
-  AKV_ARG_CHECK(chunks == 0 || chunks == 1 || chunks == 2 || chunks == 4 || chunks == 8 || chunks == 16,
-                "%s: chunks=%d not in {0,1,2,4,8,16}", fn, chunks);
+  AKV_ARG_CHECK((chunks & ~AKV_MATCH_PIPELINED) == 0 ||
+                    match_kernels(chunks) != nullptr,
+                "%s: chunks=%d is not a verify width (1, 2, 4, 8 or 16; 2, 4 or 8 with "
+                "AKV_MATCH_PIPELINED)", fn, chunks);
   AKV_ARG_CHECK(nq == 0 || (tokens != nullptr && q_off != nullptr && out_node != nullptr &&
                             out_len != nullptr),
                 "%s: NULL query or output array", fn);
@@ -683,34 +664,11 @@ extern "C" int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* 
                              "akv_match_prefix"))
     return rc;
   if (nq == 0) return AKV_OK;
-  if (chunks == 0) chunks = 4;
+  if ((chunks & ~AKV_MATCH_PIPELINED) == 0) chunks |= 4;
+  const MatchKernels* k = match_kernels(chunks);
   const int grid = akv_ceil_div(nq, kMatchWarpsPerCta);
-  cudaStream_t s = akv_stream(stream);
-  switch (chunks) {
-    case 1:
-      k_match<1><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
-                                                          out_len, out_compared, order, status);
-      break;
-    case 4:
-      k_match<4><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
-                                                          out_len, out_compared, order, status);
-      break;
-    case 8:
-      k_match<8><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
-                                                          out_len, out_compared, order, status);
-      break;
-    case 2:
-      k_match<2><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
-                                                          out_len, out_compared, order, status);
-      break;
-    case 16:
-      k_match<16><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
-                                                           out_len, out_compared, order, status);
-      break;
-    default:
-      k_match<4><<<grid, kMatchWarpsPerCta * 32, 0, s>>>(*tree, tokens, q_off, nq, block_size, out_node,
-                                                          out_len, out_compared, order, status);
-  }
+  k->whole<<<grid, kMatchWarpsPerCta * 32, 0, akv_stream(stream)>>>(*tree, tokens, q_off, nq, block_size, out_node,
+                                                                    out_len, out_compared, order, status);
   AKV_LAUNCH_CHECK("akv_match_prefix");
   return AKV_OK;
 }
@@ -723,62 +681,87 @@ extern "C" int akv_match_prefix(const AkvTreeView* tree, const int32_t* tokens, 
                                   nullptr, status, 0, stream);
 }
 
-extern "C" int64_t akv_match_scratch_bytes(int32_t nq, int64_t n_tokens, int32_t tokens_per_item) {
-  const int32_t R = tokens_per_item == 0 ? kSplitDefaultTokens : tokens_per_item;
+extern "C" int64_t akv_match_scratch_bytes(int32_t nq, int64_t n_tokens, int32_t tokens_per_range) {
+  const int32_t R = tokens_per_range == 0 ? kSplitDefaultTokens : tokens_per_range;
   if (nq < 0 || n_tokens < 0 || R < 32 || R % 32 != 0) return -1;
   return split_scratch_bytes(nq, split_items_max(nq, n_tokens, R));
 }
 
+extern "C" int akv_match_split_plan(const int64_t* lengths, int32_t nq, int32_t tokens_per_range,
+                                    int64_t* range_starts, int32_t* n_ranges) {
+  AKV_ARG_CHECK(nq >= 0 && (nq == 0 || lengths != nullptr) && range_starts != nullptr && n_ranges != nullptr,
+                "akv_match_split_plan: bad arguments");
+  const int32_t R = tokens_per_range == 0 ? kSplitDefaultTokens : tokens_per_range;
+  AKV_ARG_CHECK(R >= 32 && R % 32 == 0, "akv_match_split_plan: tokens_per_range=%d is not a multiple of 32",
+                tokens_per_range);
+  int64_t kmax = 1;
+  for (int32_t i = 0; i < nq; ++i) {
+    AKV_ARG_CHECK(lengths[i] >= 0 && (i == 0 || lengths[i] <= lengths[i - 1]),
+                  "akv_match_split_plan: lengths must be >= 0 and longest first (entry %d)", i);
+  }
+  if (nq > 0) kmax = lengths[0] <= 0 ? 1 : (lengths[0] + R - 1) / R;
+  AKV_ARG_CHECK(kmax <= kMaxSplitRanges,
+                "akv_match_split_plan: a %lld-token query needs %lld ranges of %d (at most %d)",
+                static_cast<long long>(nq > 0 ? lengths[0] : 0), static_cast<long long>(kmax), R,
+                kMaxSplitRanges);
+  // n_j = queries longer than j R (all of them for j = 0); lengths fall, so
+  // each n_j is found by walking down from n_{j-1}
+  range_starts[0] = 0;
+  int32_t n_j = nq;
+  for (int64_t j = 0; j < kmax; ++j) {
+    if (j > 0)
+      while (n_j > 0 && lengths[n_j - 1] <= j * R) --n_j;
+    range_starts[j + 1] = range_starts[j] + n_j;
+  }
+  *n_ranges = static_cast<int32_t>(kmax);
+  return AKV_OK;
+}
+
 extern "C" int akv_match_prefix_split(const AkvTreeView* tree, const int32_t* tokens, const int64_t* q_off,
-                                      int32_t nq, int64_t n_tokens, int32_t block_size, int32_t* out_node,
-                                      int32_t* out_len, int64_t* out_compared, const int32_t* order,
-                                      void* scratch, int64_t scratch_bytes, int32_t tokens_per_item,
-                                      int32_t chunks, AkvStatus* status, void* stream) {
+                                      int32_t nq, int32_t block_size, int32_t* out_node, int32_t* out_len,
+                                      int64_t* out_compared, const int32_t* order, const int64_t* range_starts,
+                                      int32_t n_ranges, int32_t tokens_per_range, void* scratch,
+                                      int64_t scratch_bytes, int32_t chunks, AkvStatus* status, void* stream) {
   if (int rc = match_args_ok(tree, tokens, q_off, nq, block_size, out_node, out_len, chunks,
                              "akv_match_prefix_split"))
     return rc;
-  const int32_t R = tokens_per_item == 0 ? kSplitDefaultTokens : tokens_per_item;
-  AKV_ARG_CHECK(R >= 32 && R % 32 == 0, "akv_match_prefix_split: tokens_per_item=%d is not a multiple of 32",
-                tokens_per_item);
-  AKV_ARG_CHECK(n_tokens >= 0, "akv_match_prefix_split: n_tokens=%lld < 0", static_cast<long long>(n_tokens));
+  const int32_t R = tokens_per_range == 0 ? kSplitDefaultTokens : tokens_per_range;
+  AKV_ARG_CHECK(R >= 32 && R % 32 == 0, "akv_match_prefix_split: tokens_per_range=%d is not a multiple of 32",
+                tokens_per_range);
   if (nq == 0) return AKV_OK;
-  const int64_t w_max = split_items_max(nq, n_tokens, R);
-  const int64_t need = split_scratch_bytes(nq, w_max);
+  AKV_ARG_CHECK(order != nullptr && range_starts != nullptr,
+                "akv_match_prefix_split: order and range_starts are required");
+  AKV_ARG_CHECK(n_ranges >= 1 && n_ranges <= kMaxSplitRanges, "akv_match_prefix_split: n_ranges=%d not in [1, %d]",
+                n_ranges, kMaxSplitRanges);
+  SplitRanges rg{};
+  rg.n = n_ranges;
+  rg.R = R;
+  AKV_ARG_CHECK(range_starts[0] == 0 && range_starts[1] == nq,
+                "akv_match_prefix_split: range_starts must begin 0, nq (%lld, %lld)",
+                static_cast<long long>(range_starts[0]), static_cast<long long>(range_starts[1]));
+  for (int32_t j = 0; j <= n_ranges; ++j) {
+    rg.start[j] = range_starts[j];
+    if (j >= 2) {
+      const int64_t nj = range_starts[j] - range_starts[j - 1], nprev = range_starts[j - 1] - range_starts[j - 2];
+      AKV_ARG_CHECK(nj >= 1 && nj <= nprev,
+                    "akv_match_prefix_split: range %d holds %lld queries (range %d: %lld)", j - 1,
+                    static_cast<long long>(nj), j - 2, static_cast<long long>(nprev));
+    }
+  }
+  const int64_t w = rg.start[n_ranges];
+  const int64_t need = split_scratch_bytes(nq, w);
   AKV_ARG_CHECK(scratch != nullptr && scratch_bytes >= need,
-                "akv_match_prefix_split: scratch of %lld bytes, %lld needed (akv_match_scratch_bytes)",
-                static_cast<long long>(scratch_bytes), static_cast<long long>(need));
+                "akv_match_prefix_split: scratch of %lld bytes, %lld needed", static_cast<long long>(scratch_bytes),
+                static_cast<long long>(need));
   AKV_ARG_CHECK(reinterpret_cast<uintptr_t>(scratch) % 16 == 0,
                 "akv_match_prefix_split: scratch is not 16-byte aligned");
-  AKV_ARG_CHECK(w_max / kMatchWarpsPerCta < INT32_MAX, "akv_match_prefix_split: %lld items",
-                static_cast<long long>(w_max));
-  if (chunks == 0) chunks = kSplitDefaultChunks;
-  const SplitScratch sc = split_scratch(scratch, nq, w_max);
-  cudaStream_t s = akv_stream(stream);
-  k_match_items<<<1, kItemThreads, 0, s>>>(q_off, order, nq, R, w_max, sc, status);
-  AKV_LAUNCH_CHECK("akv_match_prefix_split(items)");
-  const int grid = akv_ceil_div(w_max, kMatchWarpsPerCta);
-  const int threads = kMatchWarpsPerCta * 32;
-  switch (chunks) {
-    case 1:
-      k_match_split<1><<<grid, threads, 0, s>>>(*tree, tokens, q_off, block_size, R, sc, out_node, out_len,
-                                                 out_compared, status);
-      break;
-    case 2:
-      k_match_split<2><<<grid, threads, 0, s>>>(*tree, tokens, q_off, block_size, R, sc, out_node, out_len,
-                                                 out_compared, status);
-      break;
-    case 4:
-      k_match_split<4><<<grid, threads, 0, s>>>(*tree, tokens, q_off, block_size, R, sc, out_node, out_len,
-                                                 out_compared, status);
-      break;
-    case 16:
-      k_match_split<16><<<grid, threads, 0, s>>>(*tree, tokens, q_off, block_size, R, sc, out_node, out_len,
-                                                  out_compared, status);
-      break;
-    default:
-      k_match_split<8><<<grid, threads, 0, s>>>(*tree, tokens, q_off, block_size, R, sc, out_node, out_len,
-                                                 out_compared, status);
-  }
+  AKV_ARG_CHECK(w / kMatchWarpsPerCta < INT32_MAX, "akv_match_prefix_split: %lld ranges", static_cast<long long>(w));
+  if ((chunks & ~AKV_MATCH_PIPELINED) == 0) chunks |= kSplitDefaultChunks;
+  int4* stops = static_cast<int4*>(scratch);
+  int32_t* done = reinterpret_cast<int32_t*>(static_cast<char*>(scratch) + 16 * w);
+  const int grid = akv_ceil_div(w, kMatchWarpsPerCta);
+  match_kernels(chunks)->split<<<grid, kMatchWarpsPerCta * 32, 0, akv_stream(stream)>>>(
+      *tree, tokens, q_off, nq, block_size, rg, order, stops, done, out_node, out_len, out_compared, status);
   AKV_LAUNCH_CHECK("akv_match_prefix_split");
   return AKV_OK;
 }

@@ -561,7 +561,7 @@ class DeviceTree:
     def match(self, tokens: torch.Tensor, q_off: torch.Tensor, nq: int, block_size: int,
               out_node: torch.Tensor, out_len: torch.Tensor, out_cmp: Optional[torch.Tensor],
               chunks: int = 0, order: Optional[torch.Tensor] = None, runs: bool = False,
-              n_tokens: Optional[int] = None, tokens_per_item: int = 0) -> None:
+              plan: Optional["SplitPlan"] = None) -> None:
         """Enqueue a match_prefix lookup of nq queries packed in `tokens` /
         `q_off` (device int32 / int64 tensors); `order` (device int32) is the
         launch order of the queries, longest first by default in
@@ -569,42 +569,99 @@ class DeviceTree:
         time (the runs are rebuilt first if the tree changed: worth it for
         batches, not for the single lookups of create_root).
 
-        With n_tokens (the batch's token count, known on the host) the
+        With a `plan` (split_plan of the queries' lengths in `order`) the
         lookup is akv_match_prefix_split: every query's positions in ranges
-        of tokens_per_item tokens (0 = the library's default), one warp per
-        range, so a long query does not hold the batch; its scratch is this
-        tree's, grown as needed.  Without it, akv_match_prefix_variant (one
-        warp per query).  The answers are the same."""
+        of plan.tokens_per_range tokens, one warp per range, so a long query
+        does not hold the batch; its scratch is this tree's.  Without it,
+        akv_match_prefix_variant (one warp per query).  The answers are the
+        same."""
         self.flush()
         if runs:
             self.build_runs()
         out_c = out_cmp.data_ptr() if out_cmp is not None else None
         ordp = order.data_ptr() if order is not None else None
-        if n_tokens is None:
+        if plan is None:
             N.check(N.lib.akv_match_prefix_variant(
                 self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, block_size, out_node.data_ptr(),
                 out_len.data_ptr(), out_c, ordp, self.status.data_ptr(), chunks, stream_handle(self.device)))
             return
-        need = int(N.lib.akv_match_scratch_bytes(nq, int(n_tokens), tokens_per_item))
-        if need < 0:
-            raise ValueError(f"match_prefix: bad split arguments (nq={nq}, n_tokens={n_tokens}, "
-                             f"tokens_per_item={tokens_per_item})")
+        if order is None:
+            raise ValueError("match_prefix: a split lookup needs the longest-first order")
+        need = plan.scratch_bytes(nq)
         if self._split_scratch is None or self._split_scratch.numel() < need:
             cap = max(need, 2 * (self._split_scratch.numel() if self._split_scratch is not None else 0), 1 << 16)
-            self._split_scratch = torch.empty(cap, dtype=torch.uint8, device=self.device)
+            # zero-filled: every lookup leaves its per-query counters at zero
+            self._split_scratch = torch.zeros(cap, dtype=torch.uint8, device=self.device)
         sc = self._split_scratch
         N.check(N.lib.akv_match_prefix_split(
-            self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, int(n_tokens), block_size,
-            out_node.data_ptr(), out_len.data_ptr(), out_c, ordp, sc.data_ptr(), sc.numel(), tokens_per_item,
-            chunks, self.status.data_ptr(), stream_handle(self.device)))
+            self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, block_size, out_node.data_ptr(),
+            out_len.data_ptr(), out_c, ordp, plan.starts_ptr, plan.n_ranges, plan.tokens_per_range,
+            sc.data_ptr(), sc.numel(), chunks, self.status.data_ptr(), stream_handle(self.device)))
 
     def check(self) -> None:
         s = self.status.cpu()
         if int(s[0]) != 0:
             self.status.zero_()
+            if self._split_scratch is not None:
+                self._split_scratch.zero_()  # a failed split lookup may leave counters set
             raise RuntimeError(
                 f"agentkv_b200 tree replica error: {N.ERROR_NAMES.get(int(s[0]), int(s[0]))} "
                 f"(query/update {int(s[1])}, node {int(s[2])})")
+
+
+# ── split lookups ────────────────────────────────────────────────────────────
+class SplitPlan:
+    """Range plan of a split lookup (akv_match_prefix_split): range j of a
+    query covers its positions [j R, (j + 1) R); with the queries launched
+    longest first, range j exists for the first n_j ranks, and starts[j] is
+    the first warp of range j.  Computed on the host from the lengths."""
+
+    __slots__ = ("starts", "n_ranges", "tokens_per_range", "_c_starts")
+
+    def __init__(self, starts: np.ndarray, tokens_per_range: int) -> None:
+        self.starts = np.ascontiguousarray(starts, np.int64)
+        self.n_ranges = len(self.starts) - 1
+        self.tokens_per_range = int(tokens_per_range)
+        self._c_starts = self.starts  # kept alive for the pointer below
+
+    @property
+    def starts_ptr(self) -> int:
+        return self._c_starts.ctypes.data
+
+    @property
+    def n_items(self) -> int:
+        return int(self.starts[-1])
+
+    def scratch_bytes(self, nq: int) -> int:
+        b = 16 * self.n_items + 4 * nq
+        return (b + 255) // 256 * 256
+
+
+SPLIT_DEFAULT_TOKENS = 1024  # the library's default range
+
+
+def split_plan(lengths_in_order, tokens_per_range: int = 0) -> SplitPlan:
+    """The range plan for queries of these lengths, given in launch order
+    (longest first).  Ranges are tokens_per_range tokens (0 = 1024), longer
+    (a multiple of 32) where the longest query would need more than
+    MATCH_MAX_RANGES of them."""
+    lens = np.asarray(lengths_in_order, np.int64)
+    if len(lens) and np.any(np.diff(lens) > 0):
+        raise ValueError("split_plan: lengths must be in longest-first order")
+    R = int(tokens_per_range) or SPLIT_DEFAULT_TOKENS
+    if R < 32 or R % 32:
+        raise ValueError(f"split_plan: tokens_per_range={tokens_per_range} is not a multiple of 32")
+    lmax = int(lens[0]) if len(lens) else 0
+    if -(-lmax // R) > N.MATCH_MAX_RANGES:
+        R = -(-lmax // N.MATCH_MAX_RANGES)
+        R = -(-R // 32) * 32
+    k = max(1, -(-lmax // R))
+    # n_j = queries longer than j R (every query for j = 0)
+    desc = -lens  # ascending
+    n = [len(lens)] + [int(np.searchsorted(desc, -j * R, side="left")) for j in range(1, k)]
+    starts = np.zeros(k + 1, np.int64)
+    np.cumsum(n, out=starts[1:])
+    return SplitPlan(starts, R)
 
 
 # ── batched lookups on any tree replica ───────────────────────────────────────
@@ -632,6 +689,7 @@ class QueryStage:
         self.device = device
         self._tok_cap = self._q_cap = 0
         self.total = 0
+        self.lens_in_order = np.zeros(0, np.int64)
 
     def _grow(self, total: int, nq: int) -> None:
         pin = self.device.type == "cuda"
@@ -660,7 +718,9 @@ class QueryStage:
         off = self.h_off.numpy()[: nq + 1]
         off[0] = 0
         np.cumsum(lens, out=off[1:])
-        self.h_ord.numpy()[:nq] = np.argsort(-lens, kind="stable")
+        order = np.argsort(-lens, kind="stable")
+        self.h_ord.numpy()[:nq] = order
+        self.lens_in_order = lens[order]
         self.d_tok[:total].copy_(self.h_tok[:total], non_blocking=True)
         self.d_off[: nq + 1].copy_(self.h_off[: nq + 1], non_blocking=True)
         self.d_ord[:nq].copy_(self.h_ord[:nq], non_blocking=True)
@@ -685,7 +745,7 @@ def longest_first(q_off, device: torch.device) -> torch.Tensor:
 
 
 def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_compared: bool = False,
-                runs: Optional[bool] = None, tokens_per_item: int = 0, split: bool = True,
+                runs: Optional[bool] = None, tokens_per_range: int = 0, split: bool = True,
                 chunks: int = 0):
     """Longest shared prefix of many queries in one akv_match_prefix launch on
     `tree` (the owner's replica or another GPU's): (node ids, match lengths
@@ -694,7 +754,7 @@ def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_co
     runs=True follows the unary-chain runs (rebuilt first when stale),
     runs=False takes one hash probe per hop, None lets the tree decide
     (DeviceTree.want_runs); the answers are the same.  The lookup splits
-    long queries into ranges of tokens_per_item tokens (0 = the library's
+    long queries into ranges of tokens_per_range tokens (0 = the library's
     default; see DeviceTree.match); split=False uses one warp per query
     instead.  chunks: 32-token chunks compared per verify step (0 = the
     kernel's default)."""
@@ -709,8 +769,8 @@ def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_co
     node = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
     mlen = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
     cmp_ = torch.empty(max(nq, 1), dtype=torch.int64, device=dev) if with_compared else None
-    tree.match(tok, q_off, nq, block_size, node, mlen, cmp_, order=order, runs=runs, chunks=chunks,
-               n_tokens=tree._stage.total if split else None, tokens_per_item=tokens_per_item)
+    plan = split_plan(tree._stage.lens_in_order, tokens_per_range) if (split and nq) else None
+    tree.match(tok, q_off, nq, block_size, node, mlen, cmp_, order=order, runs=runs, chunks=chunks, plan=plan)
     tree.check()
     res = (node[:nq].cpu().numpy(), mlen[:nq].cpu().numpy())
     if with_compared:

@@ -152,13 +152,16 @@ class FanoutGraph:
                                      merge=self.merge)
         return self._twin
 
-    def run_many(self, roots_list) -> list:
+    def run_many(self, roots_list, on_result=None) -> list:
         """run() on each entry of `roots_list` in turn, with the same results
         (each child table array, in order), keeping the GPU busy: two
         recorded instances of the fan-out alternate, so that while one
         replays, the host reads the other's child tables and writes its next
         roots.  The replays are ordered on one stream, so the allocator sees
-        the runs one after another exactly as with run()."""
+        the runs one after another exactly as with run().  With `on_result`
+        each run's tables go to on_result(i, tables) instead — a view of the
+        pinned read-back buffer, valid during the call — and nothing is kept
+        (long sequences of runs without a copy of every table)."""
         graphs = (self, self._twin_graph())
         n_roots = self.h_roots.numel()
         outs = []
@@ -166,13 +169,18 @@ class FanoutGraph:
             stream = torch.cuda.current_stream(self.dev)
             done = (torch.cuda.Event(), torch.cuda.Event())
             held = [False, False]
+            runs_done = [0]
 
             def collect(j: int) -> None:
                 done[j].synchronize()
                 g = graphs[j]
                 if g._h_status_np[0]:
                     self.alloc.check()
-                outs.append(g.h_tables.numpy().copy())
+                if on_result is None:
+                    outs.append(g.h_tables.numpy().copy())
+                else:
+                    on_result(runs_done[0], g.h_tables.numpy())
+                runs_done[0] += 1
                 held[j] = False
 
             for i, roots in enumerate(roots_list):

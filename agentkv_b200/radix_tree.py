@@ -34,7 +34,7 @@ import torch
 
 from .allocator import BlockHandle, SlabAllocator
 from .config import PoolConfig
-from .device_tree import DeviceTree, QueryStage, longest_first, match_batch, pack_queries  # noqa: F401
+from .device_tree import DeviceTree, QueryStage, longest_first, match_batch, pack_queries, split_plan  # noqa: F401
 
 ROOT_NODE_ID: int = 0
 INVALID_NODE_ID: int = -1
@@ -426,10 +426,10 @@ class DualRadixTree:
             return INVALID_NODE_ID, 0
         # the tokens go up through a pinned stage of its own (an asynchronous
         # copy); the answer's read-back is the call's one wait
-        tok, q_off, _ = self._one_stage.pack([t])
+        tok, q_off, order = self._one_stage.pack([t])
         out = self._q_out.view(torch.int32)
-        self._dev_tree.match(tok, q_off, 1, self._cfg.block_size, out[0:1], out[1:2], None,
-                             n_tokens=len(t))
+        self._dev_tree.match(tok, q_off, 1, self._cfg.block_size, out[0:1], out[1:2], None, order=order,
+                             plan=split_plan([len(t)]))
         res = out[:2].cpu()
         self._dev_tree.check()
         node, mlen = int(res[0]), int(res[1])

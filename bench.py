@@ -59,7 +59,8 @@ sys.path.insert(0, str(REPO))
 
 from agentkv_b200 import workloads as W  # noqa: E402
 
-METRIC = "CoW block-copy GB/s at Llama-3-8B KV shape (Tree-of-Thought fan-out, 8x3 levels)"
+METRIC = ("CoW block-copy GB/s (% HBM peak) at Llama-3-8B KV shape, Tree-of-Thought fan-out 8x3; "
+          "match_prefix queries/s under match_prefix")
 
 try:  # event records inside CUDA graphs (timing the copy launches of the timed replays)
     from cuda.bindings import runtime as _RT
@@ -75,6 +76,7 @@ def _record_in_graph(event, stream) -> None:
     if int(code) != 0:
         raise RuntimeError(f"cudaEventRecordWithFlags: {code}")
 UNIT = "GB/s"
+MATCH_DEFAULT_CHUNKS = 8
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -104,7 +106,14 @@ def parse_args():
     ap.add_argument("--copy-levels", default="merged", choices=["merged", "per-level"],
                     help="copy every level's CoW pairs in one launch after the last plan, or one launch per "
                          "level as soon as its plan is ready")
-    ap.add_argument("--match", action="store_true", help="also time match_prefix on the stress tree")
+    ap.add_argument("--fanouts-per-step", type=int, default=256,
+                    help="Tree-of-Thought fan-outs per bench step (a step is a batch of consecutive fan-outs, "
+                         "so that the timed region lasts about a second)")
+    ap.add_argument("--no-sweep", action="store_true", help="leave out the disjoint-pair copy/zero sweep")
+    ap.add_argument("--no-match", action="store_true", help="leave out the match_prefix figure")
+    ap.add_argument("--match", action="store_true", help="(kept for old command lines: the figure is on by default)")
+    ap.add_argument("--match-seconds", type=float, default=1.0,
+                    help="match_prefix: time batches for at least this long")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--match-seqs", type=int, default=W.MatchSpec.n_sequences)
     ap.add_argument("--match-runs", type=int, default=1,
@@ -112,9 +121,11 @@ def parse_args():
     ap.add_argument("--match-queries", type=int, default=W.MatchSpec.n_queries)
     ap.add_argument("--match-chunks", type=int, default=0, choices=[0, 1, 2, 4, 8, 16],
                     help="match_prefix verify width: 32-token compares per lane per step (0: the default)")
+    ap.add_argument("--match-pipelined", type=int, default=-1,
+                    help="match_prefix verify rounds two in flight (1) or one (0); -1: the default")
     ap.add_argument("--match-split", type=int, default=1,
                     help="match_prefix splits queries into token ranges, one warp each (0: one warp per query)")
-    ap.add_argument("--match-tokens-per-item", type=int, default=0,
+    ap.add_argument("--match-tokens-per-range", type=int, default=0,
                     help="match_prefix split range in tokens, a multiple of 32 (0: the library's default)")
     ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers", "hf", "react"],
                     help="tot: the headline step; sweep: batched copy/zero sweep; match: match_prefix on the "
@@ -124,6 +135,15 @@ def parse_args():
     ap.add_argument("--batches", default="1,8,64,512,4096", help="sweep batch sizes")
     ap.add_argument("--rotations", type=int, default=8, help="sweep: distinct pair sets cycled")
     return ap.parse_args()
+
+
+def match_chunks_arg(args) -> int:
+    """--match-chunks with --match-pipelined folded in (the C ABI's chunks
+    argument: the width, OR-ed with AKV_MATCH_PIPELINED)."""
+    c = args.match_chunks
+    if args.match_pipelined == 1:
+        c = (c or MATCH_DEFAULT_CHUNKS) | 0x100
+    return c
 
 
 def measured_peak():
@@ -496,7 +516,10 @@ def cpu_tot_run(trees: int, steps: int, warmup: int, threads: int, max_seconds: 
     (alloc, copy 2 MiB, dec_ref), 4 allocs; then every child freed.  Uses the
     oracle's C restatement of the allocator and multi-threaded block copies
     on a host pool of 4096 blocks (enough for the 3,176 blocks one fan-out
-    touches); `trees` fan-outs run back to back per step."""
+    touches); `trees` fan-outs run back to back per step.  Returns GB/s on
+    the compulsory bytes (each distinct source read once, each destination
+    written once: the GPU figure's count), steps, seconds, bytes per block,
+    threads and GB/s on the algorithmic 2 x bytes per pair."""
     from oracle import oracle as O
 
     n, bs, L, H, D, _ = W.LLAMA3_8B_GEOMETRY
@@ -553,8 +576,10 @@ def cpu_tot_run(trees: int, steps: int, warmup: int, threads: int, max_seconds: 
         if max_seconds is not None and time.perf_counter() - t_start > max_seconds and i + 1 >= 2:
             break
     copies = trees * sum(spec.children_per_level())
-    gbs = 2 * bpb * copies * len(times) / sum(times) / 1e9
-    return gbs, len(times), sum(times), bpb, threads
+    sources = trees * sum(spec.fanout ** lvl for lvl in range(spec.levels))
+    gbs = bpb * (sources + copies) * len(times) / sum(times) / 1e9
+    gbs_alg = 2 * bpb * copies * len(times) / sum(times) / 1e9
+    return gbs, len(times), sum(times), bpb, threads, gbs_alg
 
 
 def host_cpu() -> dict:
@@ -582,18 +607,28 @@ def cpu_thread_candidates():
 
 
 def reference_arm(args, rank, world):
+    """The reference algorithm's CPU path (the oracle's C restatement, block
+    copies over the host's threads) on the Tree-of-Thought workload; rank 0
+    alone.  A bench step of the GPU arm is --fanouts-per-step fan-outs; here
+    each step is a bounded sample of `world` fan-outs (the GPU arm's per-rank
+    work), timed on the same compulsory bytes."""
     if rank != 0:
         return
-    gbs, steps, secs, bpb, threads = cpu_tot_run(world, args.steps, args.warmup, 0)
+    gbs, steps, secs, bpb, threads, gbs_alg = cpu_tot_run(world, args.steps, args.warmup, 0)
     sample = (f"{world} Tree-of-Thought fan-out(s) per step ({world * 584} CoW copies of {bpb} B), "
               f"host pool of 4096 blocks, {steps} steps in {secs:.1f} s")
+    n_, bs, L, H, D, _ = W.LLAMA3_8B_GEOMETRY
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": round(1e3 * secs / steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded token ids and pool bytes)",
-        "config": {"workload": "tot_8b_fanout", "pool_blocks_per_tree": W.LLAMA3_8B_GEOMETRY[0],
-                   "bytes_per_block": bpb, "trees_per_step": world},
+        "config": {"workload": "tot_8b_fanout", "pool_blocks": n_ * world, "fanouts_per_step": world,
+                   "trees_per_fanout": world, "bytes_per_block": bpb, "cow_copies_per_fanout": 584 * world,
+                   "bytes_counted": "compulsory: each distinct source block read once + each destination "
+                                    "written once",
+                   "parallelism": "host threads", "heads_per_rank": H},
+        "algorithmic_gbs": round(gbs_alg, 3),
         "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample, "host": host_cpu()},
         "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -715,7 +750,7 @@ def match_cpu_baseline(pool, batches, gpu_results, max_seconds: float) -> dict:
 def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
                  n_queries: int = W.MatchSpec.n_queries, rank: int = 0, world: int = 1,
                  use_runs: bool = True, cpu_seconds: float = 0.0, chunks: int = 0, split: bool = True,
-                 tokens_per_item: int = 0) -> dict:
+                 tokens_per_item: int = 0, min_seconds: float = 0.0) -> dict:
     """match_prefix on the stress tree.  With N ranks, rank 0 builds the tree
     through the pool API and broadcasts it (TreeReplicaSync) to every rank's
     replica; each rank then matches its own 4096-query batches (weak
@@ -762,17 +797,19 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
     packed = [pack_queries(q, dev) for q in batches]
     orders = [longest_first(off, dev) for _, off in packed]
     nq = spec.n_queries
-    # the split lookup's launch is sized by the largest batch's token count
-    ntok = max(sum(len(q) for q in b_) for b_ in batches) if split else None
+    # the split lookups' range plans (host: the lengths in launch order)
+    from agentkv_b200.device_tree import split_plan
+
+    plans = [split_plan(np.sort(np.asarray([len(q) for q in b_], np.int64))[::-1], tokens_per_item)
+             if split else None for b_ in batches]
     node = torch.empty(nq, dtype=torch.int32, device=dev)
     mlen = torch.empty(nq, dtype=torch.int32, device=dev)
     cmp_ = torch.empty(nq, dtype=torch.int64, device=dev)
     compared = []
     qtokens = []
     results = []
-    for (tok, off), order in zip(packed, orders):
-        tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks,
-                   n_tokens=ntok, tokens_per_item=tokens_per_item)
+    for (tok, off), order, plan in zip(packed, orders, plans):
+        tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks, plan=plan)
         compared.append(int(cmp_.sum()))
         qtokens.append(int(off[-1]))
         results.append((node.cpu().numpy(), mlen.cpu().numpy(), cmp_.cpu().numpy()))
@@ -787,18 +824,27 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         alg = {k: int(statistics.mean(p[k] for p in per)) for k in per[0]}
 
     def run():
-        for (tok, off), order in zip(packed, orders):
-            tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks,
-                       n_tokens=ntok, tokens_per_item=tokens_per_item)
+        for (tok, off), order, plan in zip(packed, orders, plans):
+            tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks, plan=plan)
 
-    ms, _ = timed(run, steps, warmup, world)
+    # enough repetitions of the rotation for min_seconds (the same count on every rank)
+    ms_probe, _ = timed(run, 3, warmup, 1)
+    steps = max(steps, int(np.ceil(min_seconds / max(ms_probe / 3e3, 1e-6))))
+    if world > 1:
+        t = torch.tensor([steps], dtype=torch.int64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        steps = int(t.item())
+    sampler = ClockSampler(torch.cuda.current_device())
+    with sampler:
+        ms, wall = timed(run, steps, warmup, world)
+    clocks = sampler.summary()
     per_batch_ms = ms / (steps * len(packed))
-    (tok0, off0), order0 = packed[0], orders[0]
+    (tok0, off0), order0, plan0 = packed[0], orders[0], plans[0]
 
     def run_warm():  # one batch again and again: its query tokens stay in L2
         for _ in range(len(packed)):
             tree.match(tok0, off0, nq, 16, node, mlen, cmp_, order=order0, runs=use_runs, chunks=chunks,
-                       n_tokens=ntok, tokens_per_item=tokens_per_item)
+                       plan=plan0)
 
     ms_w, _ = timed(run_warm, steps, warmup, world)
     warm_ms = ms_w / (steps * len(packed))
@@ -828,15 +874,16 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         achieved = alg["total"] / (per_batch_ms / 1e3) / 1e9
         roofline = {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": match_traffic(n_seqs) if use_runs else None,
+            "frac": round(achieved / peak, 4),
+            "traffic": MATCH_TRAFFIC_NCU[n_seqs][0] if (use_runs and not split and n_seqs in MATCH_TRAFFIC_NCU)
+            else None,
             "peak_source": peak_kind,
-            "kernel": (f"akv match_prefix_split (k_match_items + k_match_split), one {nq}-query batch" if split
+            "kernel": (f"akv match_prefix_split (k_match_split), one {nq}-query batch" if split
                        else f"akv match_prefix (k_match), one {nq}-query batch"),
             "algorithmic_bytes_per_launch": alg,
             "note": "compulsory bytes: 4 B per query token compared, 4 B per distinct edge token touched, "
                     f"{MATCH_NODE_BYTES} B per distinct visited node (rank 0's batches); the kernel is "
-                    "bound by dependent-load latency and issue, not by DRAM bandwidth; DRAM traffic was "
-                    "captured on the 2,000-sequence tree only (profiles/match_prefix_stress2k.md)",
+                    "bound by dependent-load latency and issue, not by DRAM bandwidth",
         }
         if world == 1 and cpu_seconds > 0:
             cpu = match_cpu_baseline(pool, batches, [(r[0], r[1]) for r in results], cpu_seconds)
@@ -851,6 +898,9 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         "ms_per_batch": round(per_batch_ms, 4),
         "l2": f"{len(packed)} batches in rotation ({len(packed)} x {int(statistics.mean(qtokens)) * 4 / 1e6:.0f} MB "
               f"of query tokens, above the 126 MB L2); warm: batch 0 repeated",
+        "batches_timed": steps * len(packed),
+        "wall_s_timed": round(wall, 3),
+        "clocks": clocks,
         "warm_ms_per_batch": round(warm_ms, 4),
         "warm_queries_per_s": round(world * nq / (warm_ms / 1e3), 1),
         "warm_tokens_compared_per_ms_per_gpu": round(compared[0] / warm_ms, 1),
@@ -861,7 +911,8 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         "query_tokens_per_batch": int(statistics.mean(qtokens)),
         "unary_runs": bool(use_runs),
         "verify_chunks": chunks or (8 if split else 4),
-        "split": {"tokens_per_item": tokens_per_item or 1024} if split else None,
+        "split": ({"tokens_per_range": plans[0].tokens_per_range, "ranges_per_batch": plans[0].n_items}
+                  if split else None),
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
@@ -871,11 +922,9 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
 # ── copy / zero sweep ────────────────────────────────────────────────────────
 def sweep_case(args) -> None:
     """Batched copy and zero over disjoint random pairs of a Llama-3-8B-shaped
-    pool of --blocks blocks; each batch size cycles --rotations pair sets so
-    small batches do not stay in L2."""
+    pool of --blocks blocks (sweep_figure), beside the reference's GPU path
+    without Triton (one dst.copy_(src) per pair)."""
     import torch
-
-    from agentkv_b200 import kernels as K
 
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
@@ -884,55 +933,9 @@ def sweep_case(args) -> None:
     pool = torch.empty((n_blocks, L, 2, H, bs, D), dtype=torch.bfloat16, device=dev)
     pool.normal_(generator=torch.Generator(device=dev).manual_seed(3))
     bpb = L * 2 * H * bs * D * 2
-    peak, peak_kind = measured_peak()
-    out = {"case": "copy_zero_sweep", "pool_blocks": n_blocks, "bytes_per_block": bpb,
-           "variant": args.variant, "peak_gbs": peak, "peak_source": peak_kind, "batches": {}}
-    for n in [int(x) for x in args.batches.split(",")]:
-        if 2 * n > n_blocks:
-            continue
-        sets = [torch.from_numpy(W.copy_sweep_pairs(n, n_blocks, rotation=r)).to(dev)
-                for r in range(args.rotations)]
-        dsts = [p_[:, 1].contiguous() for p_ in sets]
-        zv = args.variant if args.variant <= 2 else 0  # zero has no tuning shapes
-        for i in range(args.warmup):
-            K.copy_blocks(pool, sets[i % len(sets)], variant=args.variant)
-            K.zero_blocks(pool, dsts[i % len(dsts)], variant=zv)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(args.steps):
-            K.copy_blocks(pool, sets[i % len(sets)], variant=args.variant)
-        e1.record()
-        torch.cuda.synchronize()
-        c_ms = e0.elapsed_time(e1) / args.steps
-        e0.record()
-        for i in range(args.steps):
-            K.zero_blocks(pool, dsts[i % len(dsts)], variant=zv)
-        e1.record()
-        torch.cuda.synchronize()
-        z_ms = e0.elapsed_time(e1) / args.steps
-        K.raise_for_status(K._status_buffer(dev))
-        # the reference's GPU path without Triton: one dst.copy_(src) per pair
-        # (agentkv/core/triton_kernels.py:194-196 via SlabAllocator.copy_block)
-        host_sets = [p_.cpu().tolist() for p_ in sets]
-        reps = max(1, min(args.steps, 4096 // n))
-        for s_, d_ in host_sets[0]:
-            pool[d_].copy_(pool[s_])
-        torch.cuda.synchronize()
-        e0.record()
-        for i in range(reps):
-            for s_, d_ in host_sets[i % len(host_sets)]:
-                pool[d_].copy_(pool[s_])
-        e1.record()
-        torch.cuda.synchronize()
-        t_ms = e0.elapsed_time(e1) / reps
-        c_gbs = 2 * bpb * n / (c_ms / 1e3) / 1e9
-        z_gbs = bpb * n / (z_ms / 1e3) / 1e9
-        t_gbs = 2 * bpb * n / (t_ms / 1e3) / 1e9
-        out["batches"][str(n)] = {"copy_ms": round(c_ms, 5), "copy_gbs": round(c_gbs, 1),
-                                  "copy_frac": round(c_gbs / peak, 4), "zero_ms": round(z_ms, 5),
-                                  "zero_gbs": round(z_gbs, 1), "zero_frac": round(z_gbs / peak, 4),
-                                  "torch_per_pair_ms": round(t_ms, 5), "torch_per_pair_gbs": round(t_gbs, 1)}
+    out = {"case": "copy_zero_sweep", "variant": args.variant}
+    out.update(sweep_figure(pool, bpb, [int(x) for x in args.batches.split(",")], args.rotations, args.steps,
+                            args.warmup, variant=args.variant, torch_path=True))
     print(json.dumps(out), flush=True)
 
 
@@ -1137,29 +1140,15 @@ def hf_reference_update_figure(n_blocks: int, n_tok: int, steps: int, warmup: in
             "api": "torch restatement of the reference's per-layer row writes + indexed gather"}
 
 
-def match_traffic(n_seqs: int):
-    """DRAM bytes (read + write) of one k_match batch launch on the
-    2,000-sequence stress tree from the committed ncu summary (the only tree
-    size captured), or None."""
-    p = REPO / "profiles" / "match_prefix_stress2k.md"
-    if n_seqs == 2000 and p.exists():
-        for line in p.read_text().splitlines():
-            if line.startswith("traffic_bytes_per_launch:"):
-                return int(line.split(":")[1])
-    return None
-
-
-def copy_traffic(n_pairs: int):
-    """DRAM bytes (read + write) of the step's dominant copy launch (all 584
-    pairs merged, or the 512-pair third level) from the committed ncu
-    summary, or None."""
-    name = {584: "copy_blocks_tot_merged.md", 512: "copy_blocks_tot_level3.md"}.get(n_pairs)
-    p = REPO / "profiles" / name if name else None
-    if p is not None and p.exists():
-        for line in p.read_text().splitlines():
-            if line.startswith("traffic_bytes_per_launch:"):
-                return int(line.split(":")[1])
-    return None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch,
+# from ncu captures of the same launch (constants: they describe the kernel
+# as captured, not the run that prints them).
+COPY_TRAFFIC_NCU = {
+    584: (1322233344, "ncu: the 584-pair Tree-of-Thought copy launch (k_copy_bulk<16384,12>), 3,200-block pool"),
+}
+MATCH_TRAFFIC_NCU = {
+    2000: (51047424, "ncu: one 4,096-query k_match batch on the 2,000-sequence stress tree"),
+}
 
 
 # ── ReAct multi-agent trace ──────────────────────────────────────────────────
@@ -1338,6 +1327,103 @@ def react_case(args) -> None:
 
 
 # ── main arm ─────────────────────────────────────────────────────────────────
+def tot_compulsory_bytes(bench) -> tuple:
+    """(compulsory, algorithmic) bytes of one step's copies on this rank:
+    compulsory = every distinct source block read once + every destination
+    written once (the bytes HBM must move however the copies are scheduled;
+    the 8 children of a parent copy the same source), algorithmic = 2 x
+    bytes per pair.  Counted from the step's own pair list when the copy is
+    one launch, else from the workload's shape."""
+    per_tree_pairs = sum(bench.spec.children_per_level())
+    if bench.merge and bench.last_pairs is not None:
+        p = bench.last_pairs.cpu().numpy()
+        n_src = len(np.unique(p[:, 0]))
+        n_dst = len(np.unique(p[:, 1]))
+        assert n_dst == len(p), "a destination repeats within a step"
+    else:
+        # every parent of every level is one source: 1 + 8 + 64 per tree
+        n_src = bench.trees * sum(bench.spec.fanout ** lvl for lvl in range(bench.spec.levels))
+        n_dst = bench.trees * per_tree_pairs
+    comp = (n_src + n_dst) * bench.slice_bytes
+    alg = 2 * bench.trees * per_tree_pairs * bench.slice_bytes
+    return comp, alg, n_src, n_dst
+
+
+def sweep_figure(pool, bpb: int, batches, rotations: int, steps: int, warmup: int, variant: int = 0,
+                 torch_path: bool = False) -> dict:
+    """Batched copy and zero over seeded disjoint random (src, dst) pairs of
+    `pool` (config 3's pair sets): per batch size, `rotations` distinct pair
+    sets cycled so small batches do not stay in L2; CUDA events over `steps`
+    launches after `warmup`.  GB/s = (read + write) bytes / time for the copy
+    (every pair's blocks are distinct, so these are also its compulsory
+    bytes), write bytes / time for the zero.  After timing, the last set's
+    destinations are checked equal to their sources (copy) and all zero bits
+    (zero)."""
+    import torch
+
+    from agentkv_b200 import kernels as K
+
+    dev = pool.device
+    n_blocks = pool.shape[0]
+    peak, peak_kind = measured_peak()
+    out = {"pool_blocks": n_blocks, "bytes_per_block": bpb, "peak_gbs": peak, "peak_source": peak_kind,
+           "rotations": rotations, "launches_timed": steps, "batches": {}}
+    for n in batches:
+        if 2 * n > n_blocks:
+            continue
+        sets = [torch.from_numpy(W.copy_sweep_pairs(n, n_blocks, rotation=r)).to(dev) for r in range(rotations)]
+        dsts = [p_[:, 1].contiguous() for p_ in sets]
+        zv = variant if variant <= 2 else 0  # zero has no tuning shapes
+        for i in range(warmup):
+            K.copy_blocks(pool, sets[i % len(sets)], variant=variant)
+            K.zero_blocks(pool, dsts[i % len(dsts)], variant=zv)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            K.copy_blocks(pool, sets[i % len(sets)], variant=variant)
+        e1.record()
+        torch.cuda.synchronize()
+        c_ms = e0.elapsed_time(e1) / steps
+        last = sets[(steps - 1) % len(sets)]
+        flat = pool.view(n_blocks, -1)
+        probe = last[:: max(1, n // 16)].long()
+        copied_ok = bool(torch.equal(flat[probe[:, 1]], flat[probe[:, 0]]))
+        e0.record()
+        for i in range(steps):
+            K.zero_blocks(pool, dsts[i % len(dsts)], variant=zv)
+        e1.record()
+        torch.cuda.synchronize()
+        z_ms = e0.elapsed_time(e1) / steps
+        zlast = dsts[(steps - 1) % len(dsts)][:: max(1, n // 16)].long()
+        zero_ok = bool((flat[zlast].view(torch.int16) == 0).all())
+        K.raise_for_status(K._status_buffer(dev))
+        c_gbs = 2 * bpb * n / (c_ms / 1e3) / 1e9
+        z_gbs = bpb * n / (z_ms / 1e3) / 1e9
+        row = {"copy_ms": round(c_ms, 5), "copy_gbs": round(c_gbs, 1), "copy_frac": round(c_gbs / peak, 4),
+               "zero_ms": round(z_ms, 5), "zero_gbs": round(z_gbs, 1), "zero_frac": round(z_gbs / peak, 4),
+               "copied_equal": copied_ok, "zeroed_all_bits": zero_ok}
+        if torch_path:
+            # the reference's GPU path without Triton: one dst.copy_(src) per pair
+            # (agentkv/core/triton_kernels.py:194-196 via SlabAllocator.copy_block)
+            host_sets = [p_.cpu().tolist() for p_ in sets]
+            reps = max(1, min(steps, 4096 // n))
+            for s_, d_ in host_sets[0]:
+                pool[d_].copy_(pool[s_])
+            torch.cuda.synchronize()
+            e0.record()
+            for i in range(reps):
+                for s_, d_ in host_sets[i % len(host_sets)]:
+                    pool[d_].copy_(pool[s_])
+            e1.record()
+            torch.cuda.synchronize()
+            t_ms = e0.elapsed_time(e1) / reps
+            row.update({"torch_per_pair_ms": round(t_ms, 5),
+                        "torch_per_pair_gbs": round(2 * bpb * n / (t_ms / 1e3) / 1e9, 1)})
+        out["batches"][str(n)] = row
+    return out
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -1370,8 +1456,8 @@ def main():
         fig = match_figure(args.steps, args.warmup, args.match_seqs, args.match_queries, rank, world,
                            use_runs=bool(args.match_runs),
                            cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds,
-                           chunks=args.match_chunks, split=bool(args.match_split),
-                           tokens_per_item=args.match_tokens_per_item)
+                           chunks=match_chunks_arg(args), split=bool(args.match_split),
+                           tokens_per_item=args.match_tokens_per_range, min_seconds=args.match_seconds)
         if rank == 0:
             print(json.dumps(fig), flush=True)
         if world > 1:
@@ -1387,6 +1473,7 @@ def main():
                                              device_id=torch.device("cuda", local))
     bench = ToTBench(rank, world, args.blocks, args.variant, args.trees, args.heads_per_rank, args.plan,
                      merge=args.copy_levels == "merged")
+    F = max(1, args.fanouts_per_step)
     graph = None
     if not args.no_graph and (world == 1 or args.graph_nccl):
         for _ in range(2):  # load every kernel and settle the allocator pools before capture
@@ -1395,16 +1482,16 @@ def main():
         torch.cuda.synchronize()
         if world > 1:
             torch.distributed.barrier()
-        # --graph-steps consecutive steps per graph (each step's planning
-        # overlaps the previous step's copy) and a one-step graph for the
-        # remainder
+        # --graph-steps consecutive fan-outs per graph (each fan-out's
+        # planning overlaps the previous one's copy) and a one-fan-out graph
+        # for the remainder
         gs = max(1, args.graph_steps)
         graph2 = bench.capture(gs) if gs > 1 else None
         marks2 = list(bench.graph_marks)
         graph = bench.capture(1)
         marks1 = list(bench.graph_marks)
 
-        def run_steps(n):
+        def run_fanouts(n):
             if graph2 is not None:
                 for _ in range(n // gs):
                     graph2.replay()
@@ -1412,31 +1499,34 @@ def main():
             for _ in range(n):
                 graph.replay()
     else:
-        def run_steps(n):
+        def run_fanouts(n):
             for _ in range(n):
                 bench.step()
         graph2 = None
         marks1 = marks2 = []
+
+    def run_steps(n):  # one bench step = F consecutive fan-outs
+        run_fanouts(n * F)
+
     use_graph = graph is not None
     sampler = ClockSampler(local)
     with sampler:
         ms, wall = timed_steps(run_steps, args.steps, args.warmup, world, join=bench.join)
     if bench.alloc is not None:
-        # every step frees what it allocated: only the roots remain allocated
+        # every fan-out frees what it allocated: only the roots remain allocated
         bench.alloc.check()
         st = bench.alloc.stats()
         assert st["allocated_blocks"] == len(bench.root_host), st
         assert st["pending_reclamation"] == 0, st
     clocks = sampler.summary()
     step_ms = ms / args.steps
+    fanout_ms = step_ms / F
     # the copy launches of the last timed replay, timed inside the graph
     live_marks = []
     if use_graph:
         gs = max(1, args.graph_steps)
-        live_marks = marks2 if (graph2 is not None and args.steps % gs == 0) else marks1
+        live_marks = marks2 if (graph2 is not None and (args.steps * F) % gs == 0) else marks1
     live_copy_ms = [a.elapsed_time(b) for a, b in live_marks]
-    copy_bytes = bench.copy_bytes_per_step_global()
-    value_gbs = copy_bytes / (step_ms / 1e3) / 1e9
 
     # copy-kernel roofline: per-launch durations with events on this stream
     bench.copy_events = []
@@ -1444,16 +1534,18 @@ def main():
         bench.step(time_copies=True)
     bench.join()
     torch.cuda.synchronize()
-    kbytes = sum(2 * bench.slice_bytes * n for (_, _, n) in bench.copy_events)
-    kms = sum(e0.elapsed_time(e1) for (e0, e1, _) in bench.copy_events)
+    comp_rank, alg_rank, n_src, n_dst = tot_compulsory_bytes(bench)
+    comp_step = comp_rank * world * F  # all ranks, one bench step
+    alg_step = alg_rank * world * F
+    value_gbs = comp_step / (step_ms / 1e3) / 1e9
     per_level = {}
     for (e0, e1, n) in bench.copy_events:
         per_level.setdefault(n, []).append(e0.elapsed_time(e1))
     peak, peak_kind = measured_peak()
-    # the dominant launch: all pairs in one launch, or the largest level
     big = max(per_level)
     big_ms = statistics.mean(per_level[big])
     copy_timing = "events around eager launches"
+    alone_ms = None
     if bench.merge and bench.last_pairs is not None:
         # The eager launches above can wait on the host between their start
         # event and the kernel; replaying a graph of the same copy launch back
@@ -1474,17 +1566,25 @@ def main():
         if live_copy_ms:
             big_ms = statistics.mean(live_copy_ms)
             copy_timing = (f"events recorded inside the timed CUDA graph around the copy launches of the last "
-                           f"timed replay ({len(live_copy_ms)} launches); the same launch alone, replayed back to "
-                           f"back: {alone_ms:.4f} ms")
+                           f"timed replay ({len(live_copy_ms)} launches)")
         else:
             big_ms = alone_ms
             copy_timing = "events around 10 back-to-back graph replays of the step's copy launch"
         per_level[big] = [big_ms]
-        kms = big_ms
-        kbytes = 2 * bench.slice_bytes * big
-    achieved = 2 * bench.slice_bytes * big / (big_ms / 1e3) / 1e9
-    traffic = copy_traffic(big) if bench.slice_heads == 8 and bench.trees == 1 else None
-    launches = len(bench.copy_events)
+    one_launch = bench.merge and bench.last_pairs is not None
+    launch_comp = comp_rank if one_launch else None
+    achieved = (launch_comp if one_launch else 2 * bench.slice_bytes * big) / (big_ms / 1e3) / 1e9
+    traffic = COPY_TRAFFIC_NCU.get(big) if (bench.slice_heads == 8 and bench.trees == 1 and one_launch) else None
+
+    # per-rank breakdown (every rank takes part in the gather)
+    per_rank = None
+    if world > 1:
+        mine = torch.tensor([step_ms, big_ms, alone_ms or 0.0], dtype=torch.float64, device="cuda")
+        allr = [torch.zeros_like(mine) for _ in range(world)]
+        torch.distributed.all_gather(allr, mine)
+        per_rank = {"fanout_ms": [round(float(t[0]) / F, 4) for t in allr],
+                    "copy_launch_ms_in_step": [round(float(t[1]), 4) for t in allr],
+                    "copy_launch_ms_alone": [round(float(t[2]), 4) for t in allr]}
 
     e2e = None
     if not args.no_e2e:
@@ -1499,54 +1599,80 @@ def main():
                              variant=args.variant)
             roots_np = bench.root_host.numpy()
             res["io"] = (fg.h2d_bytes, fg.d2h_bytes)
-            e2e_api = "FanoutGraph.run (one CUDA graph replay per step)"
+            e2e_api = "FanoutGraph.run (one CUDA graph replay and one wait per fan-out)"
 
-            def e2e_step():
+            def e2e_fanout():
                 fg.run(roots_np, copy=False)
         else:
             e2e_api = "SlabAllocator.fanout_tree + copy_blocks from host tables (eager)"
 
-            def e2e_step():
+            def e2e_fanout():
                 res["io"] = bench.step(e2e=True)
 
-        e_steps = max(3, args.steps // 2)
-        e_ms, _ = timed(e2e_step, e_steps, max(3, args.warmup), world, join=bench.join)
-        e_step = e_ms / e_steps
+        pc_fanouts = max(3, min(F * args.steps // 2, 400))
+        e_ms, _ = timed(e2e_fanout, pc_fanouts, max(3, args.warmup), world, join=bench.join)
+        e_fanout = e_ms / pc_fanouts
         h2d, d2h = res["io"]
-        e2e = {"value": round(copy_bytes / (e_step / 1e3) / 1e9, 2), "unit": UNIT,
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "ms_per_step": round(e_step, 4), "api": e2e_api}
+        e2e = {"value": round(comp_rank * world / (e_fanout / 1e3) / 1e9, 2), "unit": UNIT,
+               "h2d_bytes_per_step": int(h2d) * F, "d2h_bytes_per_step": int(d2h) * F,
+               "ms_per_step": round(e_fanout * F, 4), "api": e2e_api,
+               "fanouts_timed": pc_fanouts}
         if bench.plan == "replicated" and use_graph and not args.no_pipeline:
-            # the same steps through FanoutGraph.run_many: two recorded
-            # instances alternate, so the host's read-back of one step and its
-            # relaunch hide behind the other's replay (each step still copies
-            # its roots in from pinned memory and its tables back to the host)
+            # the same fan-outs through FanoutGraph.run_many: two recorded
+            # instances alternate, so the host's read-back of one fan-out and
+            # its relaunch hide behind the other's replay (each fan-out still
+            # copies its roots in from pinned memory and its tables back to
+            # the host, where the host reads them)
+            seen = [0]
+
+            def on_result(i, tables):
+                seen[0] += int(tables[-1] >= 0)
+
             try:
                 fg.run_many([roots_np] * 3)  # records the second instance, warms up
-                p_steps = max(3, args.steps)
-                p_ms, _ = timed(lambda: fg.run_many([roots_np] * p_steps), 1, 0, world, join=bench.join)
-                p_step = p_ms / p_steps
-                e2e["per_call"] = {"value": e2e["value"], "ms_per_step": e2e["ms_per_step"], "api": e2e_api}
-                e2e.update({"value": round(copy_bytes / (p_step / 1e3) / 1e9, 2), "ms_per_step": round(p_step, 4),
-                            "api": f"FanoutGraph.run_many ({p_steps} steps per call, two graph instances "
-                                   f"alternating)"})
+                n_many = args.steps * F
+                p_ms, _ = timed(lambda: fg.run_many([roots_np] * n_many, on_result=on_result), 1, 0, world,
+                                join=bench.join)
+                p_fanout = p_ms / n_many
+                assert seen[0] == n_many, seen
+                e2e["per_call"] = {k: e2e[k] for k in ("value", "ms_per_step", "api", "fanouts_timed")}
+                e2e.update({"value": round(comp_rank * world / (p_fanout / 1e3) / 1e9, 2),
+                            "ms_per_step": round(p_fanout * F, 4), "fanouts_timed": n_many,
+                            "api": f"FanoutGraph.run_many ({n_many} fan-outs in one call, two graph "
+                                   f"instances alternating)"})
             except Exception as exc:  # noqa: BLE001 - the per-call figure stands; say why
                 e2e["pipelined_error"] = repr(exc)[:200]
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, steps, secs, bpb, threads = cpu_tot_run(1, 1000, 1, 0, max_seconds=args.cpu_seconds)
+        gbs, n_fan, secs, bpb, threads, gbs_alg = cpu_tot_run(1, 1000, 1, 0, max_seconds=args.cpu_seconds)
         cpu = {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{steps} Tree-of-Thought steps ({steps * 584} CoW copies of {bpb} B) on a "
-                         f"4096-block host pool, {secs:.1f} s", "host": host_cpu()}
+               "algorithmic_gbs": round(gbs_alg, 3),
+               "sample": f"{n_fan} Tree-of-Thought fan-outs ({n_fan * 584} CoW copies of {bpb} B) on a "
+                         f"4096-block host pool, {secs:.1f} s; GB/s on the same compulsory bytes as the "
+                         f"GPU figure", "host": host_cpu()}
 
-    match = (match_figure(max(5, args.steps), args.warmup, args.match_seqs, args.match_queries)
-             if (args.match and rank == 0) else None)
+    sweep = None
+    if world == 1 and not args.no_sweep:
+        n_, bs, L, H, D, _ = W.LLAMA3_8B_GEOMETRY
+        sweep = sweep_figure(bench.pool, bench.slice_bytes, [512, 4096], args.rotations, 20, 3,
+                             variant=args.variant)
+        sweep["workload"] = "copy_zero_sweep_8b (seeded disjoint pairs on the same 60,000-block pool)"
+
+    match = None
+    if rank == 0 and world == 1 and not args.no_match:
+        del graph, graph2
+        graph = graph2 = None
+        torch.cuda.synchronize()
+        match = match_figure(args.warmup, args.warmup, args.match_seqs, args.match_queries,
+                             cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds,
+                             chunks=match_chunks_arg(args), split=bool(args.match_split),
+                             tokens_per_item=args.match_tokens_per_range, min_seconds=args.match_seconds)
 
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    del graph, graph2, run_steps  # a graph holding NCCL calls must go before the process group
+    del graph, graph2, run_steps, run_fanouts  # a graph holding NCCL calls must go before the process group
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -1564,37 +1690,51 @@ def main():
             "config": {
                 "workload": "tot_8b_fanout",
                 "pool_blocks": bench.n_blocks,
-                "trees_per_step": bench.trees,
+                "fanouts_per_step": F,
+                "trees_per_fanout": bench.trees,
                 "bytes_per_block": bench.slice_bytes * world,
-                "cow_copies_per_step": sum(bench.pairs_per_level),
+                "cow_copies_per_fanout": sum(bench.pairs_per_level),
+                "bytes_counted": (f"compulsory: {n_src} distinct source blocks read once + {n_dst} destination "
+                                  f"blocks written per fan-out and rank ({comp_rank} B); the per-pair figure "
+                                  f"(2 x bytes_per_block per pair, {alg_rank} B) is algorithmic_gbs"),
                 "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
                 "pair_lists": bench.plan if world > 1 else "local",
                 "heads_per_rank": bench.slice_heads,
-                "l2": "inputs larger than L2 (each step touches ~2.4 GB per GPU)",
+                "l2": "inputs larger than L2 (each fan-out touches ~1.4 GB per GPU)",
                 "copy_variant": args.variant,
                 "copy_levels": "merged" if bench.merge else "per-level",
                 "cuda_graph": use_graph,
-                "steps_per_graph": max(1, args.graph_steps) if use_graph else None,
+                "fanouts_per_graph": max(1, args.graph_steps) if use_graph else None,
             },
+            "algorithmic_gbs": round(alg_step / (step_ms / 1e3) / 1e9, 2),
+            "fanout_ms": round(fanout_ms, 5),
             "roofline": {
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": traffic,
-                "kernel": f"akv copy_blocks, {big}-pair launch", "peak_source": peak_kind,
+                "frac": round(achieved / peak, 4), "traffic": traffic[0] if traffic else None,
+                "traffic_source": traffic[1] if traffic else None,
+                "kernel": f"akv copy_blocks (k_copy_bulk), {big}-pair launch", "peak_source": peak_kind,
                 "launch_timing": copy_timing,
+                "launch_ms": round(big_ms, 4),
+                "launch_ms_alone": round(alone_ms, 4) if alone_ms else None,
+                "compulsory_bytes_per_launch": launch_comp,
                 "algorithmic_bytes_per_launch": 2 * bench.slice_bytes * big,
-                "dram_gbs": round(traffic / (big_ms / 1e3) / 1e9, 1) if traffic else None,
-                "all_levels_gbs": round(kbytes / (kms / 1e3) / 1e9, 1),
+                "algorithmic_gbs": round(2 * bench.slice_bytes * big / (big_ms / 1e3) / 1e9, 1),
+                "dram_gbs": round(traffic[0] / (big_ms / 1e3) / 1e9, 1) if traffic else None,
                 "per_level_ms": {str(k): round(statistics.mean(v), 4) for k, v in sorted(per_level.items())},
-                "note": "algorithmic bytes = 2 x bytes_per_block per pair; the 8 (64, 512) pairs of a level "
-                        "read 1 (8, 64) distinct source blocks, so L2 serves repeated reads (per_level_ms is "
-                        "keyed by the pairs per launch: 584 = every level in one launch)",
+                "note": "achieved = compulsory bytes (distinct sources + destinations) / launch time; the 8 "
+                        "children of a parent copy one source, so L2 serves 7 of 8 source reads and the "
+                        "algorithmic per-pair figure exceeds the HBM peak",
             },
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": bench.launches_per_step * args.steps,
+            "gpu_launches": bench.launches_per_step * F * args.steps,
             "clocks": clocks,
             "wall_s_timed": round(wall, 3),
         }
+        if per_rank is not None:
+            line["per_rank"] = per_rank
+        if sweep is not None:
+            line["sweep"] = sweep
         if match is not None:
             line["match_prefix"] = match
         print(json.dumps(line), flush=True)

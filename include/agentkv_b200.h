@@ -420,39 +420,60 @@ AKV_API int akv_match_prefix(const AkvTreeView* tree, const int32_t* tokens, con
 
 /* Same, with an optional processing order (`order[nq]`, a permutation of
  * the query indices; launching the longest queries first balances the SMs)
- * and the number of 32-token chunks a warp compares per step (1, 2, 4, 8 or
- * 16; 0 = default) for tuning.  Outputs stay indexed by query. */
+ * and the number of 32-token chunks a warp compares per verify round (1, 2,
+ * 4, 8 or 16; 0 = default 4), optionally OR-ed with AKV_MATCH_PIPELINED
+ * (widths 2, 4 and 8: the next round's loads are issued before the current
+ * round's compare).  Outputs stay indexed by query. */
+#define AKV_MATCH_PIPELINED 0x100
 AKV_API int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* tokens,
                                      const int64_t* q_off, int32_t nq, int32_t block_size,
                                      int32_t* out_node, int32_t* out_len, int64_t* out_compared,
                                      const int32_t* order, AkvStatus* status, int32_t chunks,
                                      void* stream);
 
-/* Bytes of scratch akv_match_prefix_split needs for nq queries holding
- * n_tokens tokens in all, at tokens_per_item (0 = default, 1024); -1 for
- * arguments it would refuse. */
-AKV_API int64_t akv_match_scratch_bytes(int32_t nq, int64_t n_tokens, int32_t tokens_per_item);
+/* Bytes of scratch akv_match_prefix_split needs at most for nq queries
+ * holding n_tokens tokens in all, at tokens_per_range (0 = default, 1024);
+ * -1 for arguments it would refuse.  Pure host function. */
+AKV_API int64_t akv_match_scratch_bytes(int32_t nq, int64_t n_tokens, int32_t tokens_per_range);
+
+/* Longest query a split lookup takes, in ranges. */
+#define AKV_MATCH_MAX_RANGES 64
+
+/* The range plan of a split lookup (pure host function): `lengths` are the
+ * queries' token counts in launch order, longest first; writes
+ * range_starts[0 .. n_ranges] (range_starts[j+1] - range_starts[j] = the
+ * number of queries longer than j * tokens_per_range, all nq for j = 0) and
+ * n_ranges = the longest query's range count, at most AKV_MATCH_MAX_RANGES
+ * (use longer ranges for longer queries). */
+AKV_API int akv_match_split_plan(const int64_t* lengths, int32_t nq, int32_t tokens_per_range,
+                                 int64_t* range_starts, int32_t* n_ranges);
 
 /* The same answers as akv_match_prefix_variant (the reference's
  * _match_prefix_locked, agentkv/core/radix_tree.py:513-570, per query),
- * with a query's token positions cut into ranges of tokens_per_item tokens
- * (a multiple of 32; 0 = 1024), one warp per range, so a long query no
- * longer holds the batch: each warp walks the tree to the end of its range,
- * compares that range only, and the last warp of a query to finish picks
- * the earliest stop among its ranges.  n_tokens = q_off[nq] - q_off[0]
- * (an upper bound is fine: it sizes the launch).  `scratch` is
- * caller-owned device memory of akv_match_scratch_bytes(nq, n_tokens,
- * tokens_per_item) bytes, 16-byte aligned; its contents need no clearing
- * and calls that share it must be ordered (one stream).  `order` as in
- * akv_match_prefix_variant (a repeated or out-of-range entry sets
- * AKV_ERR_INVALID_ARG in `status` and writes no answers); chunks: 32-token
- * chunks compared per verify step (0 = 8).  Two launches. */
+ * with each query's token positions cut into ranges of tokens_per_range
+ * tokens (a multiple of 32; 0 = 1024), one warp per range, so that a long
+ * query no longer holds the batch: each warp walks the tree to the end of
+ * its range, compares that range only, and the last warp of a query to
+ * finish picks the earliest stop among its ranges.
+ *   order         required: the launch order, longest query first
+ *   range_starts  HOST array from akv_match_split_plan (copied into the
+ *                 launch; n_ranges + 1 entries)
+ *   scratch       caller-owned device memory of at least
+ *                 akv_match_scratch_bytes(nq, total tokens, tokens_per_range)
+ *                 bytes, 16-byte aligned, ZERO-FILLED before its first use;
+ *                 every call that completes without an error leaves it
+ *                 zero-filled (re-zero it after an error); calls sharing it
+ *                 must be ordered (one stream)
+ *   chunks        as in akv_match_prefix_variant (0 = 8)
+ * A rank whose ranges disagree with range_starts sets AKV_ERR_INVALID_ARG in
+ * `status` and gets no answer.  One launch. */
 AKV_API int akv_match_prefix_split(const AkvTreeView* tree, const int32_t* tokens,
-                                   const int64_t* q_off, int32_t nq, int64_t n_tokens,
-                                   int32_t block_size, int32_t* out_node, int32_t* out_len,
-                                   int64_t* out_compared, const int32_t* order, void* scratch,
-                                   int64_t scratch_bytes, int32_t tokens_per_item, int32_t chunks,
-                                   AkvStatus* status, void* stream);
+                                   const int64_t* q_off, int32_t nq, int32_t block_size,
+                                   int32_t* out_node, int32_t* out_len, int64_t* out_compared,
+                                   const int32_t* order, const int64_t* range_starts,
+                                   int32_t n_ranges, int32_t tokens_per_range, void* scratch,
+                                   int64_t scratch_bytes, int32_t chunks, AkvStatus* status,
+                                   void* stream);
 
 #ifdef __cplusplus
 }

@@ -178,3 +178,65 @@ def test_host_argument_checks_of_noalloc_decref():
     # oversized pool is refused even then
     assert f(C.byref(ok), None, 0, C.byref(tick), None, P, None) == N.AKV_OK
     assert f(C.byref(big), None, 0, C.byref(tick), None, P, None) == N.AKV_ERR_INVALID_ARG
+
+
+def test_split_plan_python_equals_c():
+    """The range plan of a split lookup: the package's split_plan and the
+    library's host function akv_match_split_plan agree (queries longest
+    first; range j holds the queries longer than j x R, all of them for
+    j = 0), including empty queries, lengths on range boundaries and the
+    longer ranges taken when the longest query would need more than
+    AKV_MATCH_MAX_RANGES."""
+    from agentkv_b200.device_tree import split_plan
+
+    rng = np.random.default_rng(5)
+    cases = [[0], [32, 32, 0], [8192, 4096, 4095, 33, 32, 31, 0], [64 * 1024 + 1, 5]]
+    cases += [sorted(rng.integers(0, 9000, size=int(rng.integers(1, 300))).tolist(), reverse=True)
+              for _ in range(20)]
+    for lens in cases:
+        for R in (0, 32, 1024, 2048):
+            plan = split_plan(lens, R)
+            L = np.asarray(lens, np.int64)
+            starts = np.zeros(N.MATCH_MAX_RANGES + 1, np.int64)
+            n = C.c_int32(-1)
+            rc = N.lib.akv_match_split_plan(L.ctypes.data, len(L), plan.tokens_per_range, starts.ctypes.data,
+                                            C.byref(n))
+            assert rc == N.AKV_OK, N.last_error()
+            assert n.value == plan.n_ranges
+            np.testing.assert_array_equal(starts[: n.value + 1], plan.starts)
+            k = np.maximum(1, -(-L // plan.tokens_per_range))
+            assert plan.n_items == int(k.sum()) and plan.n_ranges <= N.MATCH_MAX_RANGES
+    L = np.asarray([1, 2], np.int64)
+    rc = N.lib.akv_match_split_plan(L.ctypes.data, 2, 32, np.zeros(4, np.int64).ctypes.data, C.byref(C.c_int32()))
+    assert rc == N.AKV_ERR_INVALID_ARG and "longest first" in N.last_error()
+
+
+def test_host_argument_checks_of_split_match():
+    """akv_match_prefix_split refuses on the host: a missing order or range
+    plan, a plan whose first range is not every query, ranges that grow,
+    too little scratch, a range length that is not a multiple of 32, an
+    unknown verify width.  (Dummy device pointers: nothing is dereferenced.)"""
+    P = 16
+    v = N.AkvTreeView(P, P, P, P, 8, 4, 31, None, None, 0, 0)
+    good = np.array([0, 3, 5], np.int64)
+    f = N.lib.akv_match_prefix_split
+
+    def call(order=P, starts=good, n_ranges=2, R=32, scratch=256, bytes_=1 << 20, chunks=0):
+        sp = starts.ctypes.data if starts is not None else None
+        return f(C.byref(v), P, P, 3, 16, P, P, None, order, sp, n_ranges, R, scratch, bytes_, chunks, None, None)
+
+    assert call(order=None) == N.AKV_ERR_INVALID_ARG and "required" in N.last_error()
+    assert call(starts=None) == N.AKV_ERR_INVALID_ARG
+    assert call(starts=np.array([0, 2, 3], np.int64)) == N.AKV_ERR_INVALID_ARG and "begin" in N.last_error()
+    assert call(starts=np.array([0, 3, 7], np.int64)) == N.AKV_ERR_INVALID_ARG and "holds" in N.last_error()
+    assert call(n_ranges=0) == N.AKV_ERR_INVALID_ARG
+    assert call(n_ranges=N.MATCH_MAX_RANGES + 1) == N.AKV_ERR_INVALID_ARG
+    assert call(bytes_=64) == N.AKV_ERR_INVALID_ARG and "needed" in N.last_error()
+    assert call(scratch=None) == N.AKV_ERR_INVALID_ARG
+    assert call(scratch=264) == N.AKV_ERR_INVALID_ARG and "aligned" in N.last_error()
+    assert call(R=48) == N.AKV_ERR_INVALID_ARG and "multiple of 32" in N.last_error()
+    assert call(chunks=3) == N.AKV_ERR_INVALID_ARG and "verify width" in N.last_error()
+    assert call(chunks=16 | N.MATCH_PIPELINED) == N.AKV_ERR_INVALID_ARG
+    assert N.lib.akv_match_scratch_bytes(3, 100, 48) == -1
+    assert N.lib.akv_match_scratch_bytes(4096, 18_000_000, 0) == \
+        (16 * (4096 + 18_000_000 // 1024) + 4 * 4096 + 255) // 256 * 256

@@ -263,8 +263,8 @@ def test_match_prefix_stress_tree(golden_dir, name):
                                      (True, True, 32, 1), (True, True, 64, 2), (False, True, 96, 4),
                                      (True, True, 256, 8), (True, True, 512, 16), (True, True, 2048, 8)):
         hn, hl, hc = match_batch(pool._tree._dev_tree, queries, 16, with_compared=True, runs=runs,
-                                 split=split, tokens_per_item=tpi, chunks=chunks)
-        tag = f"runs={runs} split={split} tokens_per_item={tpi} chunks={chunks}"
+                                 split=split, tokens_per_range=tpi, chunks=chunks)
+        tag = f"runs={runs} split={split} tokens_per_range={tpi} chunks={chunks}"
         np.testing.assert_array_equal(hn, node, err_msg=tag)
         np.testing.assert_array_equal(hl, mlen, err_msg=tag)
         np.testing.assert_array_equal(hc, cmp_, err_msg=tag)
@@ -323,17 +323,18 @@ def test_match_edge_cases():
     qs = [[], list(range(32)), list(range(12)) + [7] * 52, [100, 101, 102], list(range(8)) + [5] * 56, [0]]
     for tpi in (0, 32, 64):
         node, mlen, cmp_ = match_batch(pool._tree._dev_tree, qs, 4, with_compared=True, split=True,
-                                       tokens_per_item=tpi)
+                                       tokens_per_range=tpi)
         w_node, w_len, w_cmp = match_batch(pool._tree._dev_tree, qs, 4, with_compared=True, split=False)
         assert mlen.tolist() == w_len.tolist() == [0, 8, 8, 0, 8, 0], tpi
         assert cmp_.tolist() == w_cmp.tolist(), tpi
         assert [n if m else -1 for n, m in zip(node, mlen)] == [n if m else -1 for n, m in zip(w_node, w_len)]
 
 
-def test_split_match_rejects_a_repeated_order_entry():
-    """A launch order that lists a query twice would make two warps finish
-    the same query: the split lookup reports it in the tree's status and
-    writes no answers."""
+def test_split_match_rejects_a_plan_that_disagrees_with_the_order():
+    """A range plan that gives a query fewer or more ranges than its length
+    needs (here: a plan for two 10-token queries while one is 40 tokens
+    long, then a correct one): the split lookup reports it in the tree's
+    status, writes no answer for that query, and the next lookup works."""
     import torch
 
     cfg = PoolConfig(total_blocks=64, block_size=4, num_layers=1, num_kv_heads=1, head_dim=1,
@@ -344,17 +345,20 @@ def test_split_match_rejects_a_repeated_order_entry():
     pool.commit_prefix(h, 8)
     t = pool._tree._dev_tree
     dev = t.device
-    tok = torch.arange(20, dtype=torch.int32, device=dev)
-    off = torch.tensor([0, 10, 20], dtype=torch.int64, device=dev)
+    from agentkv_b200.device_tree import split_plan
+
+    tok = torch.arange(50, dtype=torch.int32, device=dev)
+    off = torch.tensor([0, 10, 50], dtype=torch.int64, device=dev)  # query 0: 10 tokens, query 1: 40
+    order = torch.tensor([1, 0], dtype=torch.int32, device=dev)  # longest first
     node = torch.full((2,), 7, dtype=torch.int32, device=dev)
     mlen = torch.full((2,), 7, dtype=torch.int32, device=dev)
-    order = torch.tensor([1, 1], dtype=torch.int32, device=dev)
-    t.match(tok, off, 2, 4, node, mlen, None, order=order, n_tokens=20, tokens_per_item=32)
+    # a plan for two 10-token queries: query 1 needs two 32-token ranges
+    t.match(tok, off, 2, 4, node, mlen, None, order=order, plan=split_plan([10, 10], 32))
     with pytest.raises(RuntimeError, match="invalid argument"):
         t.check()
-    assert node.tolist() == [7, 7] and mlen.tolist() == [7, 7]
-    t.match(tok, off, 2, 4, node, mlen, None, order=torch.tensor([1, 0], dtype=torch.int32, device=dev),
-            n_tokens=20, tokens_per_item=32)
+    assert node[1].item() == 7 and mlen[1].item() == 7  # no answer for the mis-planned query
+    assert mlen[0].item() == 8  # the other query is answered
+    t.match(tok, off, 2, 4, node, mlen, None, order=order, plan=split_plan([40, 10], 32))
     t.check()
     assert mlen.tolist() == [8, 0]
 
@@ -496,7 +500,7 @@ def test_match_long_unary_chains():
     for runs, split, tpi in ((True, True, 0), (False, True, 0), (True, False, 0), (False, False, 0),
                              (True, True, 32), (False, True, 32), (True, True, 64), (True, True, 96)):
         node, mlen, cmp_ = match_batch(dev_tree, queries, bs, with_compared=True, runs=runs, split=split,
-                                       tokens_per_item=tpi)
+                                       tokens_per_range=tpi)
         got = [(int(n) if m else -1, int(m), int(c)) for n, m, c in zip(node, mlen, cmp_)]
         assert got == [(int(n) if m else -1, int(m), int(c)) for n, m, c in want], (runs, split, tpi)
     assert dev_tree.d_run_head is not None and int((dev_tree.d_run_head >= 0).sum()) >= 60
@@ -542,5 +546,5 @@ def test_match_scenarios_match_reference(golden_dir, name):
     for runs, split, tpi in ((True, True, 0), (False, True, 0), (True, False, 0), (False, True, 32),
                              (True, True, 32)):
         node, mlen = match_batch(pool._tree._dev_tree, sc["queries"], sc["block_size"], runs=runs,
-                                 split=split, tokens_per_item=tpi)
+                                 split=split, tokens_per_range=tpi)
         assert [[int(n) if m else -1, int(m)] for n, m in zip(node, mlen)] == want, (runs, split, tpi)

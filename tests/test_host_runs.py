@@ -321,7 +321,7 @@ def test_tree_orchestration_with_kernel_model(monkeypatch):
             for t, runs, tpi in ((owner, None, 0), (owner, False, 0), (replica, None, 0), (owner, True, 32),
                                  (replica, False, 64), (owner, None, 96)):
                 node, mlen, cmp_ = DT.match_batch(t, queries, 16, with_compared=True, runs=runs,
-                                                  tokens_per_item=tpi)
+                                                  tokens_per_range=tpi)
                 np.testing.assert_array_equal(mlen, want[1], err_msg=f"{i} {runs} {tpi}")
                 np.testing.assert_array_equal(np.where(mlen > 0, node, -1), want_node)
                 np.testing.assert_array_equal(cmp_, want[2])

@@ -134,20 +134,23 @@ class TreeKernelModel:
                 o_cmp[q] = compared
         return 0
 
-    def akv_match_prefix_split(self, view, tokens, q_off, nq, n_tokens, block_size, out_node, out_len,
-                               out_cmp, order, scratch, scratch_bytes, tokens_per_item, chunks, status,
-                               stream) -> int:
+    def akv_match_prefix_split(self, view, tokens, q_off, nq, block_size, out_node, out_len, out_cmp, order,
+                               range_starts, n_ranges, tokens_per_range, scratch, scratch_bytes, chunks,
+                               status, stream) -> int:
         self.match_calls += 1
-        R = tokens_per_item or 1024
-        need = self._real.akv_match_scratch_bytes(nq, n_tokens, tokens_per_item)
-        assert need >= 0 and scratch_bytes >= need, (need, scratch_bytes)
+        R = tokens_per_range or 1024
+        starts = _arr(range_starts, C.c_int64, (n_ranges + 1,)).copy()
+        assert starts[0] == 0 and starts[1] == nq, starts
+        need = 16 * int(starts[-1]) + 4 * nq
+        assert scratch_bytes >= need, (need, scratch_bytes)
         next_hop = self._walker(view)
         off, elen, arena, qo, q_all = self._arrays(view, tokens, q_off, nq)
-        assert int(qo[-1] - qo[0]) <= n_tokens, (int(qo[-1]), n_tokens)
+        ordr = _arr(order, C.c_int32, (nq,))
         o_node = _arr(out_node, C.c_int32, (nq,))
         o_len = _arr(out_len, C.c_int32, (nq,))
         o_cmp = _arr(out_cmp, C.c_int64, (nq,)) if out_cmp else None
         self.split_ranges = getattr(self, "split_ranges", 0)
+        n_j = np.diff(starts)
 
         def range_stop(Q, a, b):
             """(key, matched, node) of the first stop range [a, b) sees, or
@@ -174,9 +177,12 @@ class TreeKernelModel:
                 d += clen
                 cur = child
 
-        for q in range(nq):
+        for r in range(nq):
+            q = int(ordr[r])
             Q = q_all[qo[q]:qo[q + 1]]
             k = max(1, -(-len(Q) // R))
+            # the plan gives rank r exactly ranges 0 .. k-1
+            assert k <= n_ranges and r < n_j[k - 1] and (k == n_ranges or r >= n_j[k]), (r, k, n_j)
             stops = [range_stop(Q, j * R, min((j + 1) * R, len(Q))) for j in range(k)]
             self.split_ranges += k
             key, matched, node = min(s for s in stops if s is not None)
