@@ -225,7 +225,17 @@ __global__ void k_incref_apply(AkvAllocState st, const int32_t* __restrict__ ids
   const int64_t left = ctl[C_LEFT], head = ctl[C_HEAD], d = ctl[C_REL] - head;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  for (int64_t k = tid; k < n; k += stride) atomicAdd(&st.ref_counts[ids[k]], 1);
+  // Warp-aggregated increments: lanes holding the same id add their count
+  // with one atomic (a fork increments every inherited block once per child,
+  // so a batch repeats ids; the fan-out planner lists them so that equal ids
+  // share warps).  The loop is warp-uniform: stride is a multiple of 32.
+  const int lane = threadIdx.x & 31;
+  for (int64_t k0 = tid - lane; k0 < n; k0 += stride) {
+    const int64_t k = k0 + lane;
+    const int32_t x = k < n ? ids[k] : -1;
+    const uint32_t peers = __match_any_sync(0xffffffffu, x);
+    if (x >= 0 && lane == __ffs(peers) - 1) atomicAdd(&st.ref_counts[x], __popc(peers));
+  }
   for (int64_t j = tid; j < d; j += stride)
     st.free_ring[wrap(left - d + j, N)] = st.limbo_ids[wrap(head + j, N)];
   if (last_cta(ctl) && threadIdx.x == 0) {
@@ -241,14 +251,23 @@ __global__ void k_incref_apply(AkvAllocState st, const int32_t* __restrict__ ids
 __global__ void k_dec_count(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n,
                             AkvStatus* status) {
   if (akv_failed(status)) return;
-  for (int32_t k = blockIdx.x * blockDim.x + threadIdx.x; k < n; k += gridDim.x * blockDim.x) {
-    const int32_t x = ids[k];
-    if (static_cast<uint32_t>(x) >= static_cast<uint32_t>(st.total_blocks)) {
+  // Warp-aggregated: lanes holding the same id add their count with one
+  // atomic, and the highest of them (the latest position) sets the last
+  // position.  The loop is warp-uniform (blockDim.x is a multiple of 32).
+  const int lane = threadIdx.x & 31;
+  const int32_t stride = gridDim.x * blockDim.x;
+  for (int32_t k0 = blockIdx.x * blockDim.x + threadIdx.x - lane; k0 < n; k0 += stride) {
+    const int32_t k = k0 + lane;
+    int32_t x = k < n ? ids[k] : -1;
+    if (k < n && static_cast<uint32_t>(x) >= static_cast<uint32_t>(st.total_blocks)) {
       akv_fail(status, AKV_ERR_OUT_OF_RANGE, k, x, st.total_blocks);
-      continue;
+      x = -1;
     }
-    atomicAdd(&st.scratch_count[x], 1);
-    atomicMax(&st.scratch_last[x], k + 1);
+    const uint32_t peers = __match_any_sync(0xffffffffu, x);
+    if (x >= 0 && lane == 31 - __clz(peers)) {
+      atomicAdd(&st.scratch_count[x], __popc(peers));
+      atomicMax(&st.scratch_last[x], k + 1);
+    }
   }
 }
 

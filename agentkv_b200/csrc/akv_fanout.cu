@@ -65,15 +65,17 @@ __global__ void k_fanout_plan(const int32_t* __restrict__ parent_tables,
 // copy and adds `append` blocks), so no level waits for the previous one.
 // Child g (global index, levels back to back, (parent, child) order within
 // a level) owns fresh ids [(1+A) g, (1+A)(g+1)): its CoW block, then its
-// appended blocks — the ids the per-child calls take.  The outputs are laid
-// out exactly as the per-level launches of k_fanout_plan would write them,
-// level after level.
+// appended blocks — the ids the per-child calls take.  Child tables, pairs
+// and dec_ref ids are laid out exactly as the per-level launches of
+// k_fanout_plan would write them, level after level; the inc_ref ids (a
+// multiset: their order does not change the batch's result) are
+// position-major, see below.
 struct TreeShape {
   int32_t levels, K, A, R;
   int64_t first[kAkvMaxFanoutLevels + 1];  // first global child of each level
   int64_t kpow[kAkvMaxFanoutLevels + 1];   // K^l
   int64_t tab_base[kAkvMaxFanoutLevels];   // level l's child tables in child_tables
-  int64_t inc_base[kAkvMaxFanoutLevels];   // level l's fork inc_ref ids in inc_ids
+  int64_t inc_base[kAkvMaxFanoutLevels + 1];  // level l's fork inc_ref ids in inc_ids; [levels] = total
 };
 
 __global__ void k_fanout_tree_plan(const int32_t* __restrict__ root_tables, const int64_t* __restrict__ root_off,
@@ -110,17 +112,53 @@ __global__ void k_fanout_tree_plan(const int32_t* __restrict__ root_tables, cons
     const int64_t len_x = L0 + static_cast<int64_t>(l + 1) * A;
     const int64_t toff = sh.tab_base[l] + per_root * (lo + static_cast<int64_t>(r) * (l + 1) * A) + i_r * len_x;
     for (int64_t j = threadIdx.x; j < len_x; j += blockDim.x) child_tables[toff + j] = elem(l, j);
-    // the fork's inc_ref of every block of the parent's table
-    const int64_t len_p = L0 + static_cast<int64_t>(l) * A;
-    const int64_t ioff = sh.inc_base[l] + per_root * (lo + static_cast<int64_t>(r) * l * A) + i_r * len_p;
-    for (int64_t j = threadIdx.x; j < len_p; j += blockDim.x)
-      inc_ids[ioff + j] = l == 0 ? root[j] : elem(l - 1, j);
     if (threadIdx.x == 0) {
       const int32_t src = l == 0 ? root[L0 - 1] : fresh[anc(l - 1) + A];
       pairs[2 * g] = src;
       pairs[2 * g + 1] = fresh[anc(l)];
       dec_ids[g] = src;
     }
+  }
+  // The forks' inc_ref ids, position-major: within level l and root r, entry
+  // j of every child's parent table in turn (children in order), so that the
+  // children of one parent — and, for the root's blocks, all children of a
+  // root — hold the same id in consecutive slots, which the inc_ref batch
+  // folds into one atomic per warp.  Written in output order (coalesced).
+  const int64_t n_inc = sh.inc_base[sh.levels];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t o = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; o < n_inc; o += stride) {
+    int l = 0;
+    while (o >= sh.inc_base[l + 1]) ++l;
+    const int64_t per_root = sh.kpow[l + 1];
+    // root r's region starts at inc_base[l] + per_root (lo_r + r l A)
+    int32_t r_lo = 0, r_hi = sh.R - 1;
+    while (r_lo < r_hi) {
+      const int32_t mid = (r_lo + r_hi + 1) >> 1;
+      const int64_t start = sh.inc_base[l] + per_root * (root_off[mid] - base + static_cast<int64_t>(mid) * l * A);
+      if (start <= o) r_lo = mid;
+      else r_hi = mid - 1;
+    }
+    const int32_t r = r_lo;
+    const int64_t lo = root_off[r] - base;
+    const int64_t L0 = root_off[r + 1] - root_off[r];
+    const int64_t rem = o - (sh.inc_base[l] + per_root * (lo + static_cast<int64_t>(r) * l * A));
+    const int64_t j = rem / per_root, i_r = rem - j * per_root;
+    const int32_t* __restrict__ root = root_tables + lo;
+    int32_t v;
+    if (l == 0 || j < L0 - 1) {
+      v = root[j];
+    } else {
+      // the parent's table entry j (level l-1, ancestors of child c)
+      const int64_t c = static_cast<int64_t>(r) * per_root + i_r;
+      const int64_t k = j - (L0 - 1);
+      int64_t m = k / A, e = k - m * A;
+      if (m > l - 1) {
+        m = l - 1;
+        e = A;
+      }
+      v = fresh[(1 + A) * (sh.first[m] + c / sh.kpow[l - m]) + e];
+    }
+    inc_ids[o] = v;
   }
 }
 
@@ -164,6 +202,7 @@ extern "C" int akv_fanout_tree_plan(const int32_t* root_tables, const int64_t* r
     tab += sh.kpow[l + 1] * (root_blocks + static_cast<int64_t>(n_roots) * (l + 1) * append);
     inc += sh.kpow[l + 1] * (root_blocks + static_cast<int64_t>(n_roots) * l * append);
   }
+  sh.inc_base[levels] = inc;
   const int64_t total = sh.first[levels];
   const int grid = static_cast<int>(total < kAkvSMs * 8 ? total : kAkvSMs * 8);
   k_fanout_tree_plan<<<grid, 256, 0, akv_stream(stream)>>>(root_tables, root_off, fresh_ids, sh, child_tables,

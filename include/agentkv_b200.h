@@ -350,9 +350,13 @@ AKV_API int akv_fanout_plan(const int32_t* parent_tables, const int64_t* parent_
  * [n_roots + 1], root_blocks = their total length), children of a level
  * being the parents of the next.  fresh_ids holds the ids of one
  * akv_alloc_batch of (1 + append) x (all children) — the ids the per-child
- * calls take, level after level.  child_tables, inc_ids, pairs and dec_ids
- * receive what the levels' akv_fanout_plan launches would write, level after
- * level.  With appended blocks a child's table depends only on its root's
+ * calls take, level after level.  child_tables, pairs and dec_ids receive
+ * what the levels' akv_fanout_plan launches would write, level after level;
+ * inc_ids receives the same ids (the same multiset per level), position-
+ * major within each level and root (entry j of every child's parent table,
+ * children in order, then entry j + 1), so that equal ids sit in adjacent
+ * slots and akv_incref_batch folds them into one atomic per warp.  With
+ * appended blocks a child's table depends only on its root's
  * table and its ancestors' fresh ids, so no level waits for another.  No
  * counterpart in the reference beyond the per-child calls it replaces
  * (agentkv/core/radix_tree.py:222-314). */
