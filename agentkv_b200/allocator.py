@@ -31,7 +31,7 @@ this package has no CPU implementation of the path.
 from __future__ import annotations
 
 import threading
-from typing import Optional, Tuple
+from typing import List, Optional, Tuple
 
 import numpy as np
 import torch
@@ -118,6 +118,14 @@ class SlabAllocator:
         self._status = self._io[0:8]
         self._h_in = torch.zeros(24, dtype=i32, pin_memory=True)
         self._h_out = torch.zeros(64, dtype=i32, pin_memory=True)
+        # The device epoch as of the last wait, kept on the host so that
+        # enter_read_section needs no read-back: every wait also brings back
+        # ctl[OPS .. EPOCH], and the host applies the epoch changes it can
+        # foresee (maybe_advance_epoch); a batch queued without a wait makes
+        # it unknown until the next wait.
+        self._h_ctl = torch.zeros(2, dtype=i64, pin_memory=True)
+        self._mirror_epoch = 0
+        self._mirror_ok = True
         self._state = N.AkvAllocState(
             self._ref_counts.data_ptr(), self._free_ring.data_ptr(), self._limbo_ids.data_ptr(),
             self._limbo_epochs.data_ptr(), self._ctl.data_ptr(), self._scratch_count.data_ptr(),
@@ -147,11 +155,28 @@ class SlabAllocator:
         return self._reclaimer.tick(self._cfg.epoch_interval)
 
     def _sync_io(self, n_out: int = 16) -> np.ndarray:
-        """Copy status + the first outputs to the host and wait."""
+        """Copy status + the first outputs (and the op counter and epoch) to
+        the host and wait."""
         h = self._h_out[: 8 + n_out]
         h.copy_(self._io[: 8 + n_out], non_blocking=True)
+        self._h_ctl.copy_(self._ctl[N.CTL_OPS : N.CTL_EPOCH + 1], non_blocking=True)
         torch.cuda.current_stream(self._dev).synchronize()
+        self._mirror_epoch = int(self._h_ctl[1])
+        self._mirror_ok = True
         return h.numpy().copy()
+
+    def _queued(self) -> None:
+        """A batch was queued without a wait: the host no longer knows the
+        epoch until the next wait."""
+        self._mirror_ok = False
+
+    def epoch(self) -> int:
+        """The reclaimer's current epoch: from the host mirror when no batch
+        has been queued since the last wait, else read from the device."""
+        with self._lock:
+            if self._mirror_ok:
+                return self._mirror_epoch
+            return int(self.ctl()[N.CTL_EPOCH])
 
     def _stage_ids(self, ids) -> int:
         """Put up to 24 ids into the device input slots; returns the pointer."""
@@ -218,6 +243,43 @@ class SlabAllocator:
             io = self._sync_io(1)
             self._raise_status(io, "alloc")
             return BlockHandle(int(io[8]))
+
+    def alloc_many(self, n: int) -> List[int]:
+        """n alloc() calls in one launch and one wait: the ids, in the order
+        the calls would return them; MemoryError (nothing taken) when fewer
+        than n are free."""
+        with self._lock:
+            if n <= 0:
+                return []
+            if n <= 32:
+                out = self._io[8 : 8 + n]
+                N.check(N.lib.akv_alloc_batch(self._state, n, out.data_ptr(), self._tick(),
+                                              self._status.data_ptr(), self._stream()))
+                io = self._sync_io(n)
+                self._raise_status(io, "alloc")
+                return io[8 : 8 + n].tolist()
+            out = torch.empty(n, dtype=torch.int32, device=self._dev)
+            N.check(N.lib.akv_alloc_batch(self._state, n, out.data_ptr(), self._tick(), self._status.data_ptr(),
+                                          self._stream()))
+            h = torch.empty(n, dtype=torch.int32, pin_memory=True)
+            h.copy_(out, non_blocking=True)
+            self._raise_status(self._sync_io(0), "alloc")
+            return h.tolist()
+
+    def cow_one(self, block_id: int) -> int:
+        """ensure_mutable on one residual block with one wait: the block the
+        slot owns afterwards (a fresh copy when the block was shared)."""
+        with self._lock:
+            ptr = self._stage_ids([block_id])
+            meta = self._kv_data.device.type == "meta"
+            io_ptr = self._io.data_ptr()
+            N.check(N.lib.akv_cow_batch(
+                self._state, None if meta else self._kv_data.data_ptr(), 0 if meta else self._cfg.bytes_per_block,
+                ptr, 1, io_ptr + 8 * 4, io_ptr + 9 * 4, io_ptr + 10 * 4, self._tick(), self._status.data_ptr(),
+                self._stream()))
+            io = self._sync_io(2)
+            self._raise_status(io, "ensure_mutable_block")
+            return int(io[8])
 
     def inc_ref(self, handle: BlockHandle) -> None:
         self._validate_handle(handle)
@@ -294,7 +356,10 @@ class SlabAllocator:
     def ctl(self) -> np.ndarray:
         """Host copy of the control words (waits)."""
         with self._lock:
-            return self._ctl.cpu().numpy()
+            c = self._ctl.cpu().numpy()
+            self._mirror_epoch = int(c[N.CTL_EPOCH])
+            self._mirror_ok = True
+            return c
 
     @property
     def free_count(self) -> int:
@@ -357,6 +422,7 @@ class SlabAllocator:
         with self._lock:
             N.check(N.lib.akv_alloc_batch(self._state, n, out.data_ptr() if n else None, self._tick(),
                                           self._status.data_ptr(), self._stream()))
+            self._queued()
         return out
 
     def inc_ref_batch(self, ids) -> None:
@@ -364,6 +430,7 @@ class SlabAllocator:
         with self._lock:
             N.check(N.lib.akv_incref_batch(self._state, t.data_ptr(), t.numel(), self._tick(),
                                            self._status.data_ptr(), self._stream()))
+            self._queued()
 
     def dec_ref_batch(self, ids, retired_out: Optional[torch.Tensor] = None) -> None:
         """n dec_ref() calls; retired ids (in retirement order) go to
@@ -373,6 +440,7 @@ class SlabAllocator:
             N.check(N.lib.akv_decref_batch(self._state, t.data_ptr(), t.numel(), self._tick(),
                                            retired_out.data_ptr() if retired_out is not None else None,
                                            self._status.data_ptr(), self._stream()))
+            self._queued()
 
     def cow_batch(self, blocks, out_blocks: Optional[torch.Tensor] = None,
                   out_copied: Optional[torch.Tensor] = None,
@@ -395,6 +463,7 @@ class SlabAllocator:
                 0 if meta else self._cfg.bytes_per_block, t.data_ptr(), n, out_blocks.data_ptr(),
                 out_copied.data_ptr(), pairs.data_ptr(), self._tick(), self._status.data_ptr(),
                 self._stream()))
+            self._queued()
         return out_blocks, out_copied
 
     def fanout_level(self, parent_tables: torch.Tensor, parent_off: torch.Tensor, parent_lens,

@@ -138,12 +138,19 @@ class FanoutGraph:
             raise ValueError(f"FanoutGraph.run: expected {self.h_roots.numel()} root ids, got {roots.size}")
         self._h_roots_np[:] = roots
         with torch.cuda.device(self.dev):
+            self._note_replay()
             self.graph.replay()
             torch.cuda.current_stream(self.dev).synchronize()
         if self._h_status_np[0]:
             self.alloc.check()
         out = self.h_tables.numpy()
         return out.copy() if copy else out
+
+    def _note_replay(self) -> None:
+        """A replay runs allocator batches the allocator's host side does not
+        see: its host copy of the epoch is stale until the next wait."""
+        if self.alloc is not None:
+            self.alloc._queued()
 
     def _twin_graph(self) -> "FanoutGraph":
         if self._twin is None:
@@ -191,6 +198,7 @@ class FanoutGraph:
                 if held[j]:
                     collect(j)  # run i - 2, before this instance is reused
                 graphs[j]._h_roots_np[:] = r
+                self._note_replay()
                 graphs[j].graph.replay()
                 done[j].record(stream)
                 held[j] = True

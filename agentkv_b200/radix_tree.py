@@ -199,9 +199,7 @@ class DualRadixTree:
             self._validate_handle_locked(handle)
             if n <= 0:
                 return []
-            ids = self._alloc.alloc_batch(n)
-            self._alloc.check()
-            new = [BlockHandle(int(b)) for b in ids.cpu().tolist()]
+            new = [BlockHandle(int(b)) for b in self._alloc.alloc_many(n)]  # one wait
             handle.residual_blocks.extend(new)
             return new
 
@@ -221,9 +219,7 @@ class DualRadixTree:
                     handle.residual_blocks[block_idx] = new_bh
                     return new_bh
                 return bh
-            out, _ = self._alloc.cow_batch([bh.block_id])
-            self._alloc.check()
-            nb = int(out.cpu()[0])
+            nb = self._alloc.cow_one(bh.block_id)  # one wait: status and the owned block
             if nb != bh.block_id:
                 bh = BlockHandle(nb)
                 handle.residual_blocks[block_idx] = bh

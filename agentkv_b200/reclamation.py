@@ -8,9 +8,11 @@ retired-id FIFO and the epoch / op counters live in the allocator's device
 state, and this class keeps what only the host knows — the reader set — and
 turns each reclaimer call into one launch:
 
-* ``enter_read_section`` reads the current epoch (the reader's token) and
+* ``enter_read_section`` takes the current epoch (the reader's token) and
   adds it to the set — a set, as in the reference, so two readers of one
-  epoch share one entry;
+  epoch share one entry.  The allocator keeps a host copy of the epoch,
+  refreshed at every wait and moved by ``maybe_advance``, so this costs no
+  read-back unless a batch was queued since the last wait;
 * ``leave_read_section`` discards the token and launches the release of every
   pending id older than the oldest remaining reader (all of them when no
   reader is left), ``_try_retire`` in the reference (reclamation.py:147-173);
@@ -48,7 +50,7 @@ class EpochReclaimer:
     def enter_read_section(self) -> int:
         a = self._alloc
         with a._lock:
-            token = int(a.ctl()[N.CTL_EPOCH])
+            token = a.epoch()  # the host's copy when it is current: no wait
             self._active_reader_epochs.add(token)
             return token
 
@@ -63,6 +65,10 @@ class EpochReclaimer:
         a = self._alloc
         with a._lock:
             N.check(N.lib.akv_epoch_advance(a._state, self.tick(a._cfg.epoch_interval), a._stream()))
+            # the same rule on the host copy: a reader always holds the
+            # current epoch, so the epoch moves exactly when none is open
+            if not self._active_reader_epochs:
+                a._mirror_epoch += 1
 
     def stats(self) -> dict:
         c = self._alloc.ctl()

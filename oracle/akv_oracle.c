@@ -318,6 +318,11 @@ void orc_alloc_state(const OrcAlloc* a, int32_t* ref_out, int32_t* free_out, int
   }
 }
 
+/* One block's refcount (the reference's int(self._ref_counts[bid].item())). */
+int32_t orc_ref_count(const OrcAlloc* a, int32_t id) {
+  return (id >= 0 && id < a->n) ? a->ref[id] : -1;
+}
+
 /* Pending ids (FIFO order) and deferred ids (append order). */
 void orc_alloc_limbo(const OrcAlloc* a, int32_t* pend_out, int64_t* pend_ep_out, int32_t* def_out) {
   for (int64_t i = 0; i < a->pend_size; ++i) {

@@ -69,6 +69,7 @@ def _load() -> C.CDLL:
         "orc_leave_read": (None, [P, I64]),
         "orc_maybe_advance": (None, [P]),
         "orc_alloc_state": (None, [P, P, P, P]),
+        "orc_ref_count": (C.c_int32, [P, C.c_int32]),
         "orc_alloc_limbo": (None, [P, P, P, P]),
         "orc_alloc_seq": (I32, [P, I32, P]),
         "orc_incref_seq": (I32, [P, P, I32]),
@@ -246,7 +247,7 @@ class OracleAllocator:
         }
 
     def ref_count(self, bid: int) -> int:
-        return int(self.state()["ref_counts"][bid])
+        return int(lib.orc_ref_count(self._h, bid))
 
     @property
     def free_count(self) -> int:

@@ -52,6 +52,9 @@ class OracleSlab:
         except O.OracleError as e:
             _raise(e)
 
+    def alloc_many(self, n: int) -> list:
+        return self.alloc_batch(n).tolist() if n > 0 else []
+
     def inc_ref_batch(self, ids) -> None:
         try:
             self.o.inc_ref_batch(np.asarray(ids, np.int32))
@@ -76,6 +79,10 @@ class OracleSlab:
         except O.OracleError as e:
             _raise(e)
         return torch.from_numpy(out.copy()), torch.from_numpy(copied.copy())
+
+    def cow_one(self, block_id: int) -> int:
+        out, _ = self.cow_batch([block_id])
+        return int(out[0])
 
     def ref_count(self, bh: BlockHandle) -> int:
         return self.o.ref_count(self._valid(bh))
