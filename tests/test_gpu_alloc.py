@@ -265,3 +265,50 @@ def test_cow_batch_exhaustion_is_all_or_nothing():
 def test_cpu_pool_is_rejected():
     with pytest.raises(ValueError, match="CUDA"):
         make_alloc(8, device="cpu")
+
+
+def test_host_epoch_copy_follows_the_device():
+    """SlabAllocator keeps the reclaimer's epoch on the host — refreshed at
+    every wait, moved by maybe_advance_epoch by the reference's rule (the
+    epoch moves exactly when no reader is open) — so that
+    enter_read_section needs no read-back.  Over random single calls,
+    batches, epoch advances and read sections, whenever the host copy
+    claims to be current it equals the device's epoch, and every reader's
+    token is the device's epoch at entry."""
+    from agentkv_b200.allocator import BlockHandle
+
+    cfg = PoolConfig(total_blocks=512, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1,
+                     dtype="float16", device="meta", epoch_interval=5)
+    a = SlabAllocator(cfg)
+    rng = np.random.default_rng(3)
+    refs = []  # one entry per reference held
+    readers = []
+    checked = 0
+    for step in range(400):
+        op = int(rng.integers(0, 8))
+        if op == 0 or len(refs) < 4:
+            refs.append(a.alloc())
+        elif op == 1:
+            b = refs[int(rng.integers(len(refs)))]
+            a.inc_ref(b)
+            refs.append(b)
+        elif op == 2:
+            a.dec_ref(refs.pop(int(rng.integers(len(refs)))))
+        elif op == 3:
+            refs += [BlockHandle(int(x)) for x in a.alloc_batch(3).cpu().tolist()]
+        elif op == 4:
+            drop = [refs.pop(int(rng.integers(len(refs)))) for _ in range(2)]
+            a.dec_ref_batch([b.block_id for b in drop])
+        elif op == 5:
+            a.maybe_advance_epoch()
+        elif op == 6 and len(readers) < 3:
+            device_epoch = int(a._ctl.cpu()[N.CTL_EPOCH])
+            readers.append(a.enter_read_section())
+            assert readers[-1] == device_epoch, step
+        elif readers:
+            a.leave_read_section(readers.pop(0))
+        if a._mirror_ok:
+            assert a._mirror_epoch == int(a._ctl.cpu()[N.CTL_EPOCH]), step
+            checked += 1
+    a.check()
+    assert checked > 200 and int(a._ctl.cpu()[N.CTL_ADVANCES]) > 10
