@@ -421,8 +421,8 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
 // the lengths), so no list of ranges is built on the device.
 //
 // Scratch (caller-owned, akv_match_scratch_bytes): one 16-byte stop record
-// per range, then a per-query count of finished ranges that each query's
-// last range puts back to zero.
+// per range, then a per-query count of finished ranges (cleared by the
+// entry point before the launch).
 constexpr int kMaxSplitRanges = AKV_MATCH_MAX_RANGES;
 
 struct SplitRanges {
@@ -515,7 +515,6 @@ k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
     }
   }
   if (lane == 0) {
-    done[q] = 0;  // the scratch is left as it was found
     if (best == kNoStop) {  // cannot happen for a well-formed walk; never report a match then
       akv_fail(st, AKV_ERR_TREE, q, -1, k);
       best = 0;
@@ -759,6 +758,10 @@ extern "C" int akv_match_prefix_split(const AkvTreeView* tree, const int32_t* to
   if ((chunks & ~AKV_MATCH_PIPELINED) == 0) chunks |= kSplitDefaultChunks;
   int4* stops = static_cast<int4*>(scratch);
   int32_t* done = reinterpret_cast<int32_t*>(static_cast<char*>(scratch) + 16 * w);
+  // The counters' place depends on this batch's range count, so they are
+  // cleared here (the stop records are written before they are read).
+  const cudaError_t e = cudaMemsetAsync(done, 0, 4 * static_cast<size_t>(nq), akv_stream(stream));
+  if (e != cudaSuccess) return akv_cuda_fail(e, "akv_match_prefix_split: clear counters");
   const int grid = akv_ceil_div(w, kMatchWarpsPerCta);
   match_kernels(chunks)->split<<<grid, kMatchWarpsPerCta * 32, 0, akv_stream(stream)>>>(
       *tree, tokens, q_off, nq, block_size, rg, order, stops, done, out_node, out_len, out_compared, status);

@@ -590,8 +590,7 @@ class DeviceTree:
         need = plan.scratch_bytes(nq)
         if self._split_scratch is None or self._split_scratch.numel() < need:
             cap = max(need, 2 * (self._split_scratch.numel() if self._split_scratch is not None else 0), 1 << 16)
-            # zero-filled: every lookup leaves its per-query counters at zero
-            self._split_scratch = torch.zeros(cap, dtype=torch.uint8, device=self.device)
+            self._split_scratch = torch.empty(cap, dtype=torch.uint8, device=self.device)
         sc = self._split_scratch
         N.check(N.lib.akv_match_prefix_split(
             self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, block_size, out_node.data_ptr(),
@@ -602,8 +601,6 @@ class DeviceTree:
         s = self.status.cpu()
         if int(s[0]) != 0:
             self.status.zero_()
-            if self._split_scratch is not None:
-                self._split_scratch.zero_()  # a failed split lookup may leave counters set
             raise RuntimeError(
                 f"agentkv_b200 tree replica error: {N.ERROR_NAMES.get(int(s[0]), int(s[0]))} "
                 f"(query/update {int(s[1])}, node {int(s[2])})")

@@ -464,13 +464,12 @@ AKV_API int akv_match_split_plan(const int64_t* lengths, int32_t nq, int32_t tok
  *                 launch; n_ranges + 1 entries)
  *   scratch       caller-owned device memory of at least
  *                 akv_match_scratch_bytes(nq, total tokens, tokens_per_range)
- *                 bytes, 16-byte aligned, ZERO-FILLED before its first use;
- *                 every call that completes without an error leaves it
- *                 zero-filled (re-zero it after an error); calls sharing it
- *                 must be ordered (one stream)
+ *                 bytes, 16-byte aligned; no initial contents needed (the
+ *                 call clears what it counts with, one memset); calls
+ *                 sharing it must be ordered (one stream)
  *   chunks        as in akv_match_prefix_variant (0 = 8)
  * A rank whose ranges disagree with range_starts sets AKV_ERR_INVALID_ARG in
- * `status` and gets no answer.  One launch. */
+ * `status` and gets no answer.  One memset and one launch. */
 AKV_API int akv_match_prefix_split(const AkvTreeView* tree, const int32_t* tokens,
                                    const int64_t* q_off, int32_t nq, int32_t block_size,
                                    int32_t* out_node, int32_t* out_len, int64_t* out_compared,
