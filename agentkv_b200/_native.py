@@ -61,6 +61,7 @@ AUX_WORDS = 2048
 NOALLOC_MAX_BLOCKS = 262144
 MAX_FANOUT_LEVELS = 16  # AKV_MAX_FANOUT_LEVELS
 MATCH_PIPELINED = 0x100  # AKV_MATCH_PIPELINED
+MATCH_PREFETCH = 0x200  # AKV_MATCH_PREFETCH
 MATCH_MAX_RANGES = 64  # AKV_MATCH_MAX_RANGES
 
 # Copy kernel variants (akv_copy_blocks_variant).
@@ -163,6 +164,7 @@ SIGNATURES = {
     "akv_fanout_tree_plan": (C.c_int, [_P, _P, _I32, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),
     "akv_tree_hash": (C.c_uint32, [_I32, _I32]),
     "akv_tree_apply": (C.c_int, [C.POINTER(AkvTreeView), _P, _I32, _P, _I32, _P, _P]),
+    "akv_tree_commands": (C.c_int, [C.POINTER(AkvTreeView), _I64, _P, _I32, _P, _I64, _P, _P]),
     "akv_match_prefix": (
         C.c_int,
         [C.POINTER(AkvTreeView), _P, _P, _I32, _I32, _P, _P, _P, _P, _P],

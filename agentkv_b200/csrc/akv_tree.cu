@@ -109,8 +109,15 @@ constexpr int64_t kNoStop = INT64_MAX;  // the range ends before the walk does
 // lookup.
 template <int kVerifyChunks, bool kPipelined>
 AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict__ Q, int64_t L,
-                              int64_t a, int64_t b, int32_t q, AkvStatus* st, int lane) {
+                              int64_t a, int64_t b, int32_t q, AkvStatus* st, int lane, bool prefetch) {
   constexpr uint32_t kFull = 0xffffffffu;
+  if (prefetch) {
+    // Ask L2 for the range's query tokens now (one request per 128-byte
+    // line, spread over the lanes): the verify rounds then find them there
+    // instead of waiting on DRAM one round at a time.
+    for (int64_t i = a + 32 * static_cast<int64_t>(lane); i < b; i += 32 * 32)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(Q + i));
+  }
   const int4* __restrict__ slots = reinterpret_cast<const int4*>(tree.slots);
   const int4* __restrict__ runs =
       tree.run_head != nullptr ? reinterpret_cast<const int4*>(tree.run_entries) : nullptr;
@@ -390,7 +397,7 @@ __global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
 k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
         int32_t nq, int32_t block_size, int32_t* __restrict__ out_node,
         int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared,
-        const int32_t* __restrict__ order, AkvStatus* st) {
+        const int32_t* __restrict__ order, AkvStatus* st, bool prefetch) {
   const int lane = threadIdx.x & 31;
   const int32_t w = blockIdx.x * kMatchWarpsPerCta + (threadIdx.x >> 5);
   if (w >= nq) return;
@@ -401,7 +408,7 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
   }
   const int64_t qlo = q_off[q];
   const int64_t L = q_off[q + 1] - qlo;
-  const MatchStop s = match_range<kVerifyChunks, kPipelined>(tree, tokens + qlo, L, 0, L, q, st, lane);
+  const MatchStop s = match_range<kVerifyChunks, kPipelined>(tree, tokens + qlo, L, 0, L, q, st, lane, prefetch);
   if (lane == 0) match_write(s, q, block_size, out_node, out_len, out_compared);
 }
 
@@ -450,7 +457,7 @@ k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
               int32_t nq, int32_t block_size, const __grid_constant__ SplitRanges rg,
               const int32_t* __restrict__ order, int4* __restrict__ stops, int32_t* __restrict__ done,
               int32_t* __restrict__ out_node, int32_t* __restrict__ out_len,
-              int64_t* __restrict__ out_compared, AkvStatus* st) {
+              int64_t* __restrict__ out_compared, AkvStatus* st, bool prefetch) {
   constexpr uint32_t kFull = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const int64_t it = static_cast<int64_t>(blockIdx.x) * kMatchWarpsPerCta + (threadIdx.x >> 5);
@@ -476,7 +483,7 @@ k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
   }
   const int64_t a = static_cast<int64_t>(j) * R;
   const int64_t b = a + R < L ? a + R : L;
-  const MatchStop s = match_range<kVerifyChunks, kPipelined>(tree, tokens + qlo, L, a, b, q, st, lane);
+  const MatchStop s = match_range<kVerifyChunks, kPipelined>(tree, tokens + qlo, L, a, b, q, st, lane, prefetch);
   if (k == 1) {
     if (lane == 0) match_write(s, q, block_size, out_node, out_len, out_compared);
     return;
@@ -524,6 +531,218 @@ k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
   }
 }
 
+// ── tree changes built on the device ───────────────────────────────────────
+// The host tree's structural changes (DualRadixTree._insert_shared_locked,
+// radix_tree.py:572-686, and the prune in _dec_shared_ref_locked, :695-717)
+// restated as commands that a replica applies to its own arrays, so that a
+// commit ships its tokens and a few ids instead of the slot, node and token
+// rows the change wrote.  One warp applies the commands in order.
+//   insert {parent, first new node id, offset and count of its tokens in the
+//          payload, arena length before it}: walk from `parent` by first
+//          token; a missing child gets a new leaf; a fully matched edge is
+//          descended; an edge that matches to its end with the tokens also
+//          ending changes nothing (the host replaces the node's blocks);
+//          otherwise the edge splits at the block boundary at or below the
+//          common prefix — at 0 the new leaf takes the parent's slot for that
+//          first token (the old child stays, unreachable from the parent), else
+//          a new middle node takes the common blocks and the rest goes to a
+//          new leaf under it.  New nodes take consecutive ids from the given
+//          one, new edge tokens go to the arena in the order the host appends
+//          them, and slots are claimed as the host's probe claims them: the
+//          key's own slot when present, else the first deleted slot on the
+//          probe path, else the empty slot that ends it.
+//   prune  {parent, node}: the parent's slot for the node's first token is
+//          deleted when it holds the node (parent -1: no parent left), and
+//          the node's edge is cleared.
+// The host keeps the arrays large enough (it grows and rehashes them with a
+// full upload); the kernel still bounds every index and reports
+// AKV_ERR_TREE (and stops) instead of writing out of range.  Arrays written
+// here are read back through volatile loads: a later command reads what an
+// earlier one wrote.
+constexpr int64_t kCmdInsert = 1, kCmdPrune = 2;
+constexpr int kCmdWords = 8;  // {kind, parent, node / first new id, src, n, arena, block size, 0}
+constexpr int32_t kSlotDeleted = -2;
+
+struct TreeArrays {
+  volatile int32_t* tokens;
+  volatile int64_t* off;
+  volatile int32_t* len;
+  volatile int4* slots;
+  int4* slots_w;  // the same slots, for whole-slot stores
+  int64_t token_cap;
+  int32_t n_nodes, mask;
+};
+
+// (slot holding (parent, token) or -1, first reusable slot on the probe
+// path or -1): the host's DeviceTree._probe, 32 slots per step.
+AKV_DEV void cmd_probe(const TreeArrays& t, int32_t parent, int32_t token, int lane, int32_t& found,
+                       int32_t& reusable) {
+  constexpr uint32_t kFull = 0xffffffffu;
+  const uint32_t h = tree_hash(parent, token);
+  found = -1;
+  reusable = -1;
+  for (int64_t base = 0; base <= t.mask; base += 32) {
+    const uint32_t idx = (h + static_cast<uint32_t>(base) + static_cast<uint32_t>(lane)) & static_cast<uint32_t>(t.mask);
+    const bool in = base + lane <= t.mask;
+    int32_t p = 0, tk = 0;
+    if (in) {
+      p = t.slots[idx].x;
+      tk = t.slots[idx].y;
+    }
+    const uint32_t hit = __ballot_sync(kFull, in && p == parent && tk == token);
+    const uint32_t empty = __ballot_sync(kFull, in && p == kEmpty);
+    const uint32_t del = __ballot_sync(kFull, in && p == kSlotDeleted);
+    const uint32_t stop = hit | empty;
+    const int first_stop = stop ? __ffs(stop) - 1 : 32;
+    const uint32_t del_before = first_stop == 32 ? del : (del & ((1u << first_stop) - 1u));
+    if (reusable < 0 && del_before)
+      reusable = static_cast<int32_t>(__shfl_sync(kFull, idx, __ffs(del_before) - 1));
+    if (stop) {
+      const int32_t at = static_cast<int32_t>(__shfl_sync(kFull, idx, first_stop));
+      if ((hit >> first_stop) & 1u) found = at;
+      else if (reusable < 0) reusable = at;
+      return;
+    }
+  }
+}
+
+// children[parent][token] = child (edge length clen), claiming a slot as the
+// host does; false when the table has no room.
+AKV_DEV bool cmd_set_child(const TreeArrays& t, int32_t parent, int32_t token, int32_t child, int32_t clen, int lane) {
+  int32_t found, reusable;
+  cmd_probe(t, parent, token, lane, found, reusable);
+  const int32_t s = found >= 0 ? found : reusable;
+  if (s < 0) return false;
+  if (lane == 0) t.slots_w[s] = make_int4(parent, token, child, clen);
+  __syncwarp();
+  return true;
+}
+
+AKV_DEV bool cmd_set_node(const TreeArrays& t, int32_t nid, int64_t off, int32_t len, int lane) {
+  if (nid < 0 || nid >= t.n_nodes) return false;
+  if (lane == 0) {
+    t.off[nid] = off;
+    t.len[nid] = len;
+  }
+  __syncwarp();
+  return true;
+}
+
+__global__ void __launch_bounds__(32)
+k_tree_commands(TreeArrays t, const int64_t* __restrict__ cmds, int32_t n_cmds, const int32_t* __restrict__ payload,
+                int64_t payload_len, AkvStatus* st) {
+  constexpr uint32_t kFull = 0xffffffffu;
+  const int lane = threadIdx.x;
+  for (int32_t c = 0; c < n_cmds; ++c) {
+    const int64_t* cm = cmds + static_cast<int64_t>(kCmdWords) * c;
+    const int64_t kind = cm[0];
+    if (kind == kCmdPrune) {
+      const int32_t parent = static_cast<int32_t>(cm[1]), nid = static_cast<int32_t>(cm[2]);
+      if (nid < 0 || nid >= t.n_nodes) {
+        if (lane == 0) akv_fail(st, AKV_ERR_TREE, c, nid, t.n_nodes);
+        return;
+      }
+      const int64_t eo = t.off[nid];
+      const int32_t el = t.len[nid];
+      if (parent >= 0 && el > 0 && eo >= 0 && eo < t.token_cap) {
+        int32_t found, reusable;
+        cmd_probe(t, parent, t.tokens[eo], lane, found, reusable);
+        if (found >= 0 && t.slots[found].z == nid) {
+          if (lane == 0) t.slots_w[found] = make_int4(kSlotDeleted, 0, 0, 0);
+          __syncwarp();
+        }
+      }
+      cmd_set_node(t, nid, 0, 0, lane);
+      continue;
+    }
+    if (kind != kCmdInsert) {
+      if (lane == 0) akv_fail(st, AKV_ERR_TREE, c, static_cast<int32_t>(kind), 0);
+      return;
+    }
+    int32_t node = static_cast<int32_t>(cm[1]);
+    int32_t next_id = static_cast<int32_t>(cm[2]);
+    const int64_t src = cm[3], n = cm[4];
+    int64_t arena = cm[5];
+    const int64_t block_size = cm[6];
+    if (src < 0 || n < 0 || src + n > payload_len || arena < 0 || block_size < 1) {
+      if (lane == 0) akv_fail(st, AKV_ERR_TREE, c, static_cast<int32_t>(n), 0, src);
+      return;
+    }
+    const int32_t* __restrict__ toks = payload + src;
+    // appends toks[pos, n) to the arena; its offset, or -1 without room
+    auto append = [&](int64_t pos) -> int64_t {
+      const int64_t m = n - pos, at = arena;
+      if (at + m > t.token_cap) return -1;
+      for (int64_t i = lane; i < m; i += 32) t.tokens[at + i] = toks[pos + i];
+      __syncwarp();
+      arena += m;
+      return at;
+    };
+    bool ok = true;
+    int64_t pos = 0;
+    while (ok && pos < n) {
+      const int32_t first = toks[pos];
+      int32_t found, reusable;
+      cmd_probe(t, node, first, lane, found, reusable);
+      if (found < 0) {  // a new leaf under `node`
+        const int64_t o = append(pos);
+        ok = o >= 0 && cmd_set_node(t, next_id, o, static_cast<int32_t>(n - pos), lane) &&
+             cmd_set_child(t, node, first, next_id, static_cast<int32_t>(n - pos), lane);
+        break;
+      }
+      const int32_t child = t.slots[found].z;
+      if (child < 0 || child >= t.n_nodes) {
+        ok = false;
+        break;
+      }
+      const int64_t co = t.off[child];
+      const int32_t cl = t.len[child];
+      if (co < 0 || co + cl > t.token_cap) {
+        ok = false;
+        break;
+      }
+      // common prefix of the child's edge and toks[pos, n)
+      const int64_t lim = cl < n - pos ? cl : n - pos;
+      int64_t common = lim;
+      for (int64_t i0 = 0; i0 < lim; i0 += 32) {
+        const int64_t i = i0 + lane;
+        const uint32_t diff = __ballot_sync(kFull, i < lim && t.tokens[co + i] != toks[pos + i]);
+        if (diff) {
+          common = i0 + __ffs(diff) - 1;
+          break;
+        }
+      }
+      if (common == cl && common == n - pos) break;  // the same edge again: nothing moves
+      if (common == cl) {                            // descend
+        node = child;
+        pos += common;
+        continue;
+      }
+      const int64_t split = (common / block_size) * block_size;
+      if (split == 0) {  // a new leaf takes the parent's slot for `first`
+        const int64_t o = append(pos);
+        ok = o >= 0 && cmd_set_node(t, next_id, o, static_cast<int32_t>(n - pos), lane) &&
+             cmd_set_child(t, node, first, next_id, static_cast<int32_t>(n - pos), lane);
+        break;
+      }
+      const int32_t mid = next_id++;
+      ok = cmd_set_node(t, mid, co, static_cast<int32_t>(split), lane) &&
+           cmd_set_node(t, child, co + split, static_cast<int32_t>(cl - split), lane) &&
+           cmd_set_child(t, mid, t.tokens[co + split], child, static_cast<int32_t>(cl - split), lane) &&
+           cmd_set_child(t, node, first, mid, static_cast<int32_t>(split), lane);
+      if (!ok || split == n - pos) break;
+      const int64_t o = append(pos + split);
+      ok = o >= 0 && cmd_set_node(t, next_id, o, static_cast<int32_t>(n - pos - split), lane) &&
+           cmd_set_child(t, mid, toks[pos + split], next_id, static_cast<int32_t>(n - pos - split), lane);
+      break;
+    }
+    if (!ok) {
+      if (lane == 0) akv_fail(st, AKV_ERR_TREE, c, node, next_id, pos);
+      return;
+    }
+  }
+}
+
 __global__ void k_tree_apply(AkvTreeView tree, const int32_t* __restrict__ su, int32_t n_slot,
                              const int64_t* __restrict__ nu, int32_t n_node, AkvStatus* st) {
   int4* slots = reinterpret_cast<int4*>(const_cast<int32_t*>(tree.slots));
@@ -568,7 +787,7 @@ constexpr MatchKernels kMatchKernels[] = {
 
 const MatchKernels* match_kernels(int32_t chunks) {
   const bool pipelined = (chunks & AKV_MATCH_PIPELINED) != 0;
-  const int c = chunks & ~AKV_MATCH_PIPELINED;
+  const int c = chunks & ~(AKV_MATCH_PIPELINED | AKV_MATCH_PREFETCH);
   for (const MatchKernels& k : kMatchKernels)
     if (k.chunks == c && k.pipelined == pipelined) return &k;
   return nullptr;
@@ -590,6 +809,7 @@ int akv_tree_prepare() {
       }))
     return rc;
   AKV_LOAD(k_tree_apply);
+  AKV_LOAD(k_tree_commands);
 #undef AKV_LOAD
   return AKV_OK;
 }
@@ -625,7 +845,8 @@ extern "C" int akv_tree_apply(const AkvTreeView* tree, const int32_t* slot_updat
 namespace {
 
 constexpr int32_t kSplitDefaultTokens = 1024;  // tokens per item (R)
-constexpr int kSplitDefaultChunks = 8;        // 256 tokens compared per verify round
+constexpr int kSplitDefaultChunks = 4;        // 128 tokens compared per verify round
+constexpr int kWholeDefaultChunks = 8;        // 256 (measured fastest on the match stress tree)
 
 int match_args_ok(const AkvTreeView* tree, const int32_t* tokens, const int64_t* q_off, int32_t nq,
                   int32_t block_size, const int32_t* out_node, const int32_t* out_len, int32_t chunks,
@@ -642,7 +863,7 @@ int match_args_ok(const AkvTreeView* tree, const int32_t* tokens, const int64_t*
                 "%s: slot count %d is not a power of two >= 32", fn, tree->slot_mask + 1);
   AKV_ARG_CHECK(nq >= 0, "%s: nq=%d < 0", fn, nq);
   AKV_ARG_CHECK(block_size > 0, "%s: block_size=%d", fn, block_size);
-  AKV_ARG_CHECK((chunks & ~AKV_MATCH_PIPELINED) == 0 ||
+  AKV_ARG_CHECK((chunks & ~(AKV_MATCH_PIPELINED | AKV_MATCH_PREFETCH)) == 0 ||
                     match_kernels(chunks) != nullptr,
                 "%s: chunks=%d is not a verify width (1, 2, 4, 8 or 16; 2, 4 or 8 with "
                 "AKV_MATCH_PIPELINED)", fn, chunks);
@@ -663,11 +884,12 @@ extern "C" int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* 
                              "akv_match_prefix"))
     return rc;
   if (nq == 0) return AKV_OK;
-  if ((chunks & ~AKV_MATCH_PIPELINED) == 0) chunks |= 4;
+  if ((chunks & ~(AKV_MATCH_PIPELINED | AKV_MATCH_PREFETCH)) == 0) chunks |= kWholeDefaultChunks;
   const MatchKernels* k = match_kernels(chunks);
   const int grid = akv_ceil_div(nq, kMatchWarpsPerCta);
   k->whole<<<grid, kMatchWarpsPerCta * 32, 0, akv_stream(stream)>>>(*tree, tokens, q_off, nq, block_size, out_node,
-                                                                    out_len, out_compared, order, status);
+                                                                    out_len, out_compared, order, status,
+                                                                    (chunks & AKV_MATCH_PREFETCH) != 0);
   AKV_LAUNCH_CHECK("akv_match_prefix");
   return AKV_OK;
 }
@@ -755,7 +977,7 @@ extern "C" int akv_match_prefix_split(const AkvTreeView* tree, const int32_t* to
   AKV_ARG_CHECK(reinterpret_cast<uintptr_t>(scratch) % 16 == 0,
                 "akv_match_prefix_split: scratch is not 16-byte aligned");
   AKV_ARG_CHECK(w / kMatchWarpsPerCta < INT32_MAX, "akv_match_prefix_split: %lld ranges", static_cast<long long>(w));
-  if ((chunks & ~AKV_MATCH_PIPELINED) == 0) chunks |= kSplitDefaultChunks;
+  if ((chunks & ~(AKV_MATCH_PIPELINED | AKV_MATCH_PREFETCH)) == 0) chunks |= kSplitDefaultChunks;
   int4* stops = static_cast<int4*>(scratch);
   int32_t* done = reinterpret_cast<int32_t*>(static_cast<char*>(scratch) + 16 * w);
   // The counters' place depends on this batch's range count, so they are
@@ -764,7 +986,33 @@ extern "C" int akv_match_prefix_split(const AkvTreeView* tree, const int32_t* to
   if (e != cudaSuccess) return akv_cuda_fail(e, "akv_match_prefix_split: clear counters");
   const int grid = akv_ceil_div(w, kMatchWarpsPerCta);
   match_kernels(chunks)->split<<<grid, kMatchWarpsPerCta * 32, 0, akv_stream(stream)>>>(
-      *tree, tokens, q_off, nq, block_size, rg, order, stops, done, out_node, out_len, out_compared, status);
+      *tree, tokens, q_off, nq, block_size, rg, order, stops, done, out_node, out_len, out_compared, status,
+      (chunks & AKV_MATCH_PREFETCH) != 0);
   AKV_LAUNCH_CHECK("akv_match_prefix_split");
+  return AKV_OK;
+}
+
+extern "C" int akv_tree_commands(const AkvTreeView* tree, int64_t token_cap, const int64_t* cmds, int32_t n_cmds,
+                                 const int32_t* payload, int64_t payload_len, AkvStatus* status, void* stream) {
+  AKV_ARG_CHECK(tree != nullptr && tree->tokens && tree->node_edge_off && tree->node_edge_len && tree->slots,
+                "akv_tree_commands: incomplete tree view");
+  AKV_ARG_CHECK(tree->slot_mask >= 31 && ((tree->slot_mask + 1) & tree->slot_mask) == 0,
+                "akv_tree_commands: slot count %d is not a power of two >= 32", tree->slot_mask + 1);
+  AKV_ARG_CHECK(n_cmds >= 0 && payload_len >= 0 && token_cap >= tree->n_tokens,
+                "akv_tree_commands: n_cmds=%d payload_len=%lld token_cap=%lld", n_cmds,
+                static_cast<long long>(payload_len), static_cast<long long>(token_cap));
+  if (n_cmds == 0) return AKV_OK;
+  AKV_ARG_CHECK(cmds != nullptr && (payload_len == 0 || payload != nullptr), "akv_tree_commands: NULL commands");
+  TreeArrays t;
+  t.tokens = const_cast<int32_t*>(tree->tokens);
+  t.off = const_cast<int64_t*>(tree->node_edge_off);
+  t.len = const_cast<int32_t*>(tree->node_edge_len);
+  t.slots = reinterpret_cast<volatile int4*>(const_cast<int32_t*>(tree->slots));
+  t.slots_w = reinterpret_cast<int4*>(const_cast<int32_t*>(tree->slots));
+  t.token_cap = token_cap;
+  t.n_nodes = tree->n_nodes;
+  t.mask = tree->slot_mask;
+  k_tree_commands<<<1, 32, 0, akv_stream(stream)>>>(t, cmds, n_cmds, payload, payload_len, status);
+  AKV_LAUNCH_CHECK("akv_tree_commands");
   return AKV_OK;
 }

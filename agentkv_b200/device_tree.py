@@ -127,9 +127,23 @@ class DeviceTree:
         self._view: Optional[N.AkvTreeView] = None
         self._stage: Optional["QueryStage"] = None  # match_batch's reusable buffers
         self._split_scratch: Optional[torch.Tensor] = None  # akv_match_prefix_split's work space
+        # Changes as commands (akv_tree_commands): the host tree's inserts and
+        # prunes since the last upload, applied on the device by the replica
+        # itself instead of uploading the rows they changed.  Used when every
+        # change since the last upload came from a recorded command and no
+        # array was resized or rehashed.
+        self.device_commands = True
+        self._cmds: list = []
+        self._cmd_tokens: list = []
+        self._cmd_tok_len = 0
+        self._cmd_scope = False
+        self._cmds_cover = True
+        self.command_uploads = 0  # uploads done as commands (for tests and figures)
 
     # ── mutations (host mirror) ──────────────────────────────────────────────
     def append_tokens(self, toks: np.ndarray) -> int:
+        if not self._cmd_scope:
+            self._cmds_cover = False
         toks = np.asarray(toks, np.int32)
         need = self.n_tokens + len(toks)
         if need > len(self.h_tokens):
@@ -147,6 +161,8 @@ class DeviceTree:
         return self.h_tokens[off : off + length]
 
     def set_node(self, nid: int, off: int, length: int) -> None:
+        if not self._cmd_scope:
+            self._cmds_cover = False
         if nid >= len(self.h_off):
             cap = max(nid + 1, 2 * len(self.h_off))
             for name in ("h_off", "h_len"):
@@ -185,6 +201,8 @@ class DeviceTree:
     def set_child(self, parent: int, token: int, child: int, child_len: int) -> None:
         """children[parent][token] = child; the slot also carries the child's
         edge length (the device walk chases hops with it)."""
+        if not self._cmd_scope:
+            self._cmds_cover = False
         key = (parent, token)
         s = self._slot_of.get(key)
         if s is None:
@@ -210,6 +228,8 @@ class DeviceTree:
             c.slots.add(s)
 
     def del_child(self, parent: int, token: int) -> None:
+        if not self._cmd_scope:
+            self._cmds_cover = False
         s = self._slot_of.pop((parent, token), None)
         if s is None:
             return
@@ -273,9 +293,74 @@ class DeviceTree:
         if self._peers is None:
             self._peers = _Changes()
 
+    # ── changes as commands ──────────────────────────────────────────────────
+    def begin_insert(self, parent: int, tokens: np.ndarray, first_new_id: int, block_size: int) -> None:
+        """The host tree is about to insert `tokens` under `parent`
+        (DualRadixTree._insert_shared_locked); its mirror changes until
+        end_command() are this insert's."""
+        toks = np.asarray(tokens, np.int32)
+        self._cmds.append((1, parent, first_new_id, self._cmd_tok_len, len(toks), self.n_tokens, block_size, 0))
+        self._cmd_tokens.append(toks)
+        self._cmd_tok_len += len(toks)
+        self._cmd_scope = True
+
+    def begin_prune(self, parent: int, node: int) -> None:
+        """The host tree is about to prune `node` (its parent, or -1 when the
+        parent is gone); its mirror changes until end_command() are this
+        prune's."""
+        self._cmds.append((2, parent, node, 0, 0, 0, 0, 0))
+        self._cmd_scope = True
+
+    def end_command(self) -> None:
+        self._cmd_scope = False
+
+    def _drop_commands(self) -> None:
+        self._cmds = []
+        self._cmd_tokens = []
+        self._cmd_tok_len = 0
+        self._cmds_cover = True
+
     # ── upload ───────────────────────────────────────────────────────────────
     def flush(self) -> None:
-        """Ship pending changes to the device (on the current stream)."""
+        """Ship pending changes to the device (on the current stream): as the
+        host tree's commands when they account for every change since the
+        last upload, else as the changed rows (or the whole arrays)."""
+        c = self._local
+        if (self.device_commands and self._cmds and self._cmds_cover and not c.full and not self._replica
+                and self.d_tokens.numel() >= self.n_tokens):
+            self._upload_commands()
+            c.tok_from = self.n_tokens
+            c.nodes.clear()
+            c.slots.clear()
+            self._drop_commands()
+            return
+        self._drop_commands()
+        d = self.take_delta()
+        if d is not None:
+            self.apply_delta(d)
+
+    def _upload_commands(self) -> None:
+        dev = self.device
+        cmds = torch.from_numpy(np.asarray(self._cmds, np.int64).reshape(-1, 8))
+        payload = np.concatenate(self._cmd_tokens) if self._cmd_tokens else np.zeros(1, np.int32)
+        pay = torch.from_numpy(np.ascontiguousarray(payload, np.int32))
+        if dev.type == "cuda":
+            cmds, pay = cmds.pin_memory(), pay.pin_memory()
+        cmds = cmds.to(dev, non_blocking=True)
+        pay = pay.to(dev, non_blocking=True)
+        self._dev_tokens = self.n_tokens
+        self._view = None
+        if any(c[0] == 1 for c in self._cmds):
+            self._drop_replica_runs()
+        N.check(N.lib.akv_tree_commands(self.view(), self.d_tokens.numel(), cmds.data_ptr(), len(self._cmds),
+                                        pay.data_ptr(), int(self._cmd_tok_len), self.status.data_ptr(),
+                                        stream_handle(dev)))
+        self._cmd_keep = (cmds, pay)  # alive until the launch has read them
+        self.command_uploads += 1
+
+    def flush_rows(self) -> None:
+        """flush() without commands: the changed rows."""
+        self._drop_commands()
         d = self.take_delta()
         if d is not None:
             self.apply_delta(d)
@@ -742,7 +827,7 @@ def longest_first(q_off, device: torch.device) -> torch.Tensor:
 
 
 def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_compared: bool = False,
-                runs: Optional[bool] = None, tokens_per_range: int = 0, split: bool = True,
+                runs: Optional[bool] = None, tokens_per_range: int = 0, split: bool = False,
                 chunks: int = 0):
     """Longest shared prefix of many queries in one akv_match_prefix launch on
     `tree` (the owner's replica or another GPU's): (node ids, match lengths
@@ -752,9 +837,10 @@ def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_co
     runs=False takes one hash probe per hop, None lets the tree decide
     (DeviceTree.want_runs); the answers are the same.  The lookup splits
     long queries into ranges of tokens_per_range tokens (0 = the library's
-    default; see DeviceTree.match); split=False uses one warp per query
-    instead.  chunks: 32-token chunks compared per verify step (0 = the
-    kernel's default)."""
+    default; see DeviceTree.match) when split=True; by default one warp
+    walks each query (measured faster on the match stress workload).
+    chunks: 32-token chunks compared per verify step (0 = the kernel's
+    default), optionally with N.MATCH_PIPELINED / N.MATCH_PREFETCH."""
     t0 = time.perf_counter()
     if runs is None:
         runs = tree.want_runs()

@@ -32,6 +32,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import numpy as np
 import torch
 
+from . import _native as N
 from .allocator import BlockHandle, SlabAllocator
 from .config import PoolConfig
 from .device_tree import DeviceTree, QueryStage, longest_first, match_batch, pack_queries, split_plan  # noqa: F401
@@ -378,11 +379,13 @@ class DualRadixTree:
                 )
             promote = _as_i32(handle.tokens[handle.shared_match_len:][:length])
             promote_blocks = handle.residual_blocks[:n_blocks]
-            new_node_id = self._insert_shared_locked(
-                handle.shared_node_id if handle.shared_node_id != INVALID_NODE_ID else ROOT_NODE_ID,
-                promote,
-                promote_blocks,
-            )
+            parent = handle.shared_node_id if handle.shared_node_id != INVALID_NODE_ID else ROOT_NODE_ID
+            # the replica applies the same insert itself (akv_tree_commands)
+            self._dev_tree.begin_insert(parent, promote, self._next_node_id, bs)
+            try:
+                new_node_id = self._insert_shared_locked(parent, promote, promote_blocks)
+            finally:
+                self._dev_tree.end_command()
             handle.residual_blocks = handle.residual_blocks[n_blocks:]
             handle.shared_node_id = new_node_id
             handle.shared_match_len += length
@@ -424,8 +427,8 @@ class DualRadixTree:
         # copy); the answer's read-back is the call's one wait
         tok, q_off, order = self._one_stage.pack([t])
         out = self._q_out.view(torch.int32)
-        self._dev_tree.match(tok, q_off, 1, self._cfg.block_size, out[0:1], out[1:2], None, order=order,
-                             plan=split_plan([len(t)]))
+        self._dev_tree.match(tok, q_off, 1, self._cfg.block_size, out[0:1], out[1:2], None,
+                             chunks=N.MATCH_PREFETCH)
         res = out[:2].cpu()
         self._dev_tree.check()
         node, mlen = int(res[0]), int(res[1])
@@ -510,6 +513,7 @@ class DualRadixTree:
             if node.ref_count <= 0 and nid != ROOT_NODE_ID and not node.children:
                 decs.extend(b.block_id for b in node.blocks)
                 parent_id = node.parent_id
+                self._dev_tree.begin_prune(parent_id if parent_id in self._shared_nodes else -1, nid)
                 if parent_id in self._shared_nodes:
                     parent = self._shared_nodes[parent_id]
                     for k in [k for k, v in parent.children.items() if v == nid]:
@@ -517,6 +521,7 @@ class DualRadixTree:
                         self._dev_tree.del_child(parent_id, k)
                 del self._shared_nodes[nid]
                 self._dev_tree.clear_node(nid)
+                self._dev_tree.end_command()
                 nid = parent_id
             else:
                 nid = self._shared_nodes[nid].parent_id

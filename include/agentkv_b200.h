@@ -415,6 +415,24 @@ AKV_API int akv_tree_apply(const AkvTreeView* tree, const int32_t* slot_updates,
                    const int64_t* node_updates, int32_t n_node,
                    AkvStatus* status, void* stream);
 
+/* The host tree's inserts and prunes, applied by the replica itself
+ * (DualRadixTree._insert_shared_locked, agentkv/core/radix_tree.py:572-686,
+ * with its block-aligned split, split == 0 overwrite and exact re-commit;
+ * the prune of _dec_shared_ref_locked, :695-717), so that a commit ships its
+ * tokens and a few ids instead of the rows it changed.  cmds: device int64
+ * [n_cmds][8], applied in order by one warp:
+ *   {1, parent, first new node id, payload offset, token count, arena length
+ *    before the insert, block size, 0}  insert the payload's tokens under
+ *                                       `parent`
+ *   {2, parent or -1, node, 0, ...}     prune `node`
+ * payload: device int32, every insert's tokens.  New nodes take consecutive
+ * ids, new edge tokens are appended to the arena and hash slots are claimed
+ * exactly as the host mirror does, so the arrays end byte-equal to the host
+ * mirror's.  The caller keeps the arrays large enough (token_cap = the
+ * arena's capacity); an index out of range sets AKV_ERR_TREE and stops. */
+AKV_API int akv_tree_commands(const AkvTreeView* tree, int64_t token_cap, const int64_t* cmds, int32_t n_cmds,
+                              const int32_t* payload, int64_t payload_len, AkvStatus* status, void* stream);
+
 /* One warp per query.  Query q is tokens[q_off[q] .. q_off[q+1]).  Writes
  * the reference's (node_id, match_len) — (-1, 0) when nothing matched — and
  * the number of token comparisons the reference loop performs. */
@@ -425,10 +443,14 @@ AKV_API int akv_match_prefix(const AkvTreeView* tree, const int32_t* tokens, con
 /* Same, with an optional processing order (`order[nq]`, a permutation of
  * the query indices; launching the longest queries first balances the SMs)
  * and the number of 32-token chunks a warp compares per verify round (1, 2,
- * 4, 8 or 16; 0 = default 4), optionally OR-ed with AKV_MATCH_PIPELINED
+ * 4, 8 or 16; 0 = default 8), optionally OR-ed with AKV_MATCH_PIPELINED
  * (widths 2, 4 and 8: the next round's loads are issued before the current
  * round's compare).  Outputs stay indexed by query. */
 #define AKV_MATCH_PIPELINED 0x100
+/* OR-ed into `chunks` as well: each warp first asks L2 for its query's
+ * tokens (prefetch.global.L2), so that the verify rounds wait on L2 rather
+ * than DRAM. */
+#define AKV_MATCH_PREFETCH 0x200
 AKV_API int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* tokens,
                                      const int64_t* q_off, int32_t nq, int32_t block_size,
                                      int32_t* out_node, int32_t* out_len, int64_t* out_compared,
@@ -467,7 +489,7 @@ AKV_API int akv_match_split_plan(const int64_t* lengths, int32_t nq, int32_t tok
  *                 bytes, 16-byte aligned; no initial contents needed (the
  *                 call clears what it counts with, one memset); calls
  *                 sharing it must be ordered (one stream)
- *   chunks        as in akv_match_prefix_variant (0 = 8)
+ *   chunks        as in akv_match_prefix_variant (0 = 4)
  * A rank whose ranges disagree with range_starts sets AKV_ERR_INVALID_ARG in
  * `status` and gets no answer.  One memset and one launch. */
 AKV_API int akv_match_prefix_split(const AkvTreeView* tree, const int32_t* tokens,

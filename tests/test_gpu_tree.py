@@ -21,6 +21,7 @@ import pytest
 import torch
 
 from agentkv_b200 import AgentKVPool, PoolConfig
+from agentkv_b200 import _native as N
 from agentkv_b200 import workloads as W
 from agentkv_b200.allocator import BlockHandle
 from oracle import oracle as O
@@ -259,9 +260,12 @@ def test_match_prefix_stress_tree(golden_dir, name):
     # with one hash probe per hop (no unary-chain runs), with one warp per
     # query, and split into short ranges at every verify width: the same
     # answers and comparison counts
+    P, F = N.MATCH_PIPELINED, N.MATCH_PREFETCH
     for runs, split, tpi, chunks in ((False, True, 0, 0), (True, False, 0, 0), (False, False, 0, 4),
                                      (True, True, 32, 1), (True, True, 64, 2), (False, True, 96, 4),
-                                     (True, True, 256, 8), (True, True, 512, 16), (True, True, 2048, 8)):
+                                     (True, True, 256, 8), (True, True, 512, 16), (True, True, 2048, 8),
+                                     (True, False, 0, 4 | P), (False, False, 0, 8 | P | F), (True, True, 64, 2 | P),
+                                     (True, True, 128, 8 | F), (True, False, 0, F), (True, False, 0, 16 | F)):
         hn, hl, hc = match_batch(pool._tree._dev_tree, queries, 16, with_compared=True, runs=runs,
                                  split=split, tokens_per_range=tpi, chunks=chunks)
         tag = f"runs={runs} split={split} tokens_per_range={tpi} chunks={chunks}"

@@ -68,3 +68,44 @@ def test_replica_from_deltas_matches_reference(golden_dir):
     assert torch.equal(replica.d_off, owner.d_off) and torch.equal(replica.d_len, owner.d_len)
     # nothing pending: share() says so
     assert sync.share() is None
+
+
+@pytest.mark.parametrize("seed", [1, 2, 3])
+def test_device_built_tree_changes_over_reference_traces(golden_dir, seed):
+    """akv_tree_commands on the GPU: the replica applies the host tree's
+    inserts and prunes itself.  Over the reference's recorded tree traces,
+    after every commit, free and create, the device arrays (tokens, edge
+    ranges, hash slots) equal the host mirror's byte for byte, with most
+    uploads done as commands."""
+    from test_host_replays import replay_tree_trace_with_array_checks
+
+    _, n_cmd, checked = replay_tree_trace_with_array_checks(golden_dir, seed, torch.device("cuda", 0))
+    assert checked > 50 and n_cmd > 20, (checked, n_cmd)
+
+
+def test_device_built_tree_changes_under_random_churn():
+    """The same under random commits and frees reaching every insert branch
+    (new leaf, descent, exact re-commit, split off and on block boundaries,
+    split == 0 overwrite) and many prunes: byte-equal arrays after every
+    step."""
+    from agentkv_b200 import AgentKVPool, PoolConfig
+    from tree_churn import churn
+
+    for seed in range(3):
+        pool = AgentKVPool(config=PoolConfig(total_blocks=400, block_size=4, num_layers=1, num_kv_heads=1,
+                                             head_dim=2, dtype="float16", device="meta", epoch_interval=7))
+        tree = pool._tree
+        dt = tree._dev_tree
+        before = dt.command_uploads
+
+        def check(step):
+            dt.flush()
+            k = dt.n_tokens
+            assert np.array_equal(dt.d_tokens[:k].cpu().numpy(), dt.h_tokens[:k]), (seed, step)
+            assert np.array_equal(dt.d_off.cpu().numpy(), dt.h_off), (seed, step)
+            assert np.array_equal(dt.d_len.cpu().numpy(), dt.h_len), (seed, step)
+            assert np.array_equal(dt.d_slots.cpu().numpy(), dt.h_slots), (seed, step)
+
+        churn(tree, np.random.default_rng(seed), 400, check)
+        dt.check()
+        assert dt.command_uploads - before > 100

@@ -693,3 +693,139 @@ def test_match_scenarios_host_logic(golden_dir, name, monkeypatch):
         node, mlen = match_batch(pool._tree._dev_tree, sc["queries"], sc["block_size"], runs=runs)
         got = [[int(n) if m else -1, int(m)] for n, m in zip(node, mlen)]
         assert got == want, runs
+
+
+def replay_tree_trace_with_array_checks(golden_dir, seed, dev, check_each_op=True):
+    """Replay the reference's recorded tree trace `seed` through the
+    package's DualRadixTree, uploading the tree after every op; returns
+    (tree, number of uploads done as commands, number of ops checked).  After
+    every upload the device arrays must equal the host mirror's byte for
+    byte.  The allocator is the device one when `dev` is a GPU, else the
+    oracle stand-in (the caller patches the tree kernels for CPU)."""
+    import torch
+
+    from agentkv_b200.radix_tree import DualRadixTree
+
+    g = json.loads((golden_dir / f"tree_trace_{seed}.json").read_text())
+    n, bs = g["n_blocks"], g["block_size"]
+    if dev.type == "cuda":
+        from agentkv_b200 import AgentKVPool
+
+        pool = AgentKVPool(config=PoolConfig(total_blocks=n, block_size=bs, num_layers=1, num_kv_heads=2,
+                                             head_dim=4, dtype="float16", device="cuda", epoch_interval=7))
+        tree, slab = pool._tree, pool._allocator
+    else:
+        from oracle_slab import OracleSlab
+
+        kv = torch.zeros((n, 1, 2, 2, bs, 4), dtype=torch.float16)
+        slab = OracleSlab(kv, 7)
+        tree = DualRadixTree(slab, PoolConfig(total_blocks=n, block_size=bs, num_layers=1, num_kv_heads=2,
+                                              head_dim=4, dtype="float16", device="meta", epoch_interval=7))
+    T_CREATE, T_FORK, T_ALLOC, T_COW, T_APPEND, T_COMMIT, T_FREE, T_MATCH, T_ADVANCE, T_ZERO = range(10)
+    live = {}
+    dt = tree._dev_tree
+    checked = 0
+    for step, rec in enumerate(g["ops"]):
+        op = rec["op"]
+        try:
+            if op == T_CREATE:
+                h = tree.create_root(rec["tokens"])
+                live[h.handle_id] = h
+            elif op == T_FORK:
+                c = tree.fork(live[rec["h"]])
+                live[c.handle_id] = c
+            elif op == T_ALLOC:
+                tree.allocate_block(live[rec["h"]])
+            elif op == T_COW:
+                tree.ensure_mutable_block(live[rec["h"]], rec["idx"])
+            elif op == T_APPEND:
+                tree.append_tokens(live[rec["h"]], rec["tokens"])
+            elif op == T_COMMIT:
+                tree.commit_prefix(live[rec["h"]], rec["length"])
+            elif op == T_FREE:
+                tree.free(live.pop(rec["h"]))
+            elif op == T_MATCH:
+                mh, _ = tree.match_prefix(rec["tokens"])
+                if mh is not None:
+                    live[mh.handle_id] = mh
+            elif op == T_ADVANCE:
+                slab.maybe_advance_epoch()
+        except (ValueError, MemoryError):
+            pass
+        if check_each_op and op in (T_COMMIT, T_FREE, T_CREATE):
+            dt.flush()
+            k = dt.n_tokens
+            assert np.array_equal(dt.d_tokens[:k].cpu().numpy(), dt.h_tokens[:k]), (seed, step, "tokens")
+            assert np.array_equal(dt.d_off.cpu().numpy(), dt.h_off), (seed, step, "edge offsets")
+            assert np.array_equal(dt.d_len.cpu().numpy(), dt.h_len), (seed, step, "edge lengths")
+            assert np.array_equal(dt.d_slots.cpu().numpy(), dt.h_slots), (seed, step, "slots")
+            checked += 1
+    return tree, dt.command_uploads, checked
+
+
+@pytest.mark.parametrize("seed", [1, 2, 3])
+def test_tree_commands_keep_the_replica_equal_to_the_host_mirror(golden_dir, seed, monkeypatch):
+    """The tree changes built by the replica itself (akv_tree_commands: the
+    host tree's inserts with their block-aligned split, split == 0 overwrite
+    and exact re-commit, and its prunes), here by the kernel's CPU model
+    (tree_kernel_model.py): over the reference's recorded tree traces, after
+    every commit, free and create the replica's arrays equal the host
+    mirror's byte for byte, with most uploads done as commands."""
+    import torch
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from tree_kernel_model import TreeKernelModel
+
+    model = TreeKernelModel(N.lib)
+    monkeypatch.setattr(N, "lib", model)
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    tree, n_cmd, checked = replay_tree_trace_with_array_checks(golden_dir, seed, torch.device("cpu"))
+    assert checked > 50 and n_cmd > 20, (checked, n_cmd)
+    assert model.command_calls == n_cmd
+
+
+def test_tree_commands_under_random_churn(monkeypatch):
+    """The same check under random commits and frees that hit every insert
+    branch — new leaf, descent, exact re-commit, split off and at block
+    boundaries, split == 0 overwrite — and many prunes (tree_churn.py): after
+    every step the replica's arrays, changed by akv_tree_commands' CPU
+    model, equal the host mirror's."""
+    import torch
+
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import device_tree as DT
+    from agentkv_b200.radix_tree import DualRadixTree
+    from oracle_slab import OracleSlab
+    from tree_churn import churn
+    from tree_kernel_model import TreeKernelModel
+
+    model = TreeKernelModel(N.lib)
+    monkeypatch.setattr(N, "lib", model)
+    monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
+    kinds = {}
+    orig = DT.DeviceTree._upload_commands
+
+    def counting(self):
+        for c in self._cmds:
+            kinds[c[0]] = kinds.get(c[0], 0) + 1
+        orig(self)
+
+    monkeypatch.setattr(DT.DeviceTree, "_upload_commands", counting)
+    for seed in range(3):
+        slab = OracleSlab(torch.zeros((400, 1, 2, 1, 4, 2), dtype=torch.float16), 7)
+        tree = DualRadixTree(slab, PoolConfig(total_blocks=400, block_size=4, num_layers=1, num_kv_heads=1,
+                                              head_dim=2, dtype="float16", device="meta", epoch_interval=7))
+        dt = tree._dev_tree
+
+        def check(step):
+            dt.flush()
+            k = dt.n_tokens
+            assert np.array_equal(dt.d_tokens[:k].numpy(), dt.h_tokens[:k]), (seed, step)
+            assert np.array_equal(dt.d_off.numpy(), dt.h_off), (seed, step)
+            assert np.array_equal(dt.d_len.numpy(), dt.h_len), (seed, step)
+            assert np.array_equal(dt.d_slots.numpy(), dt.h_slots), (seed, step)
+
+        churn(tree, np.random.default_rng(seed), 400, check)
+        assert tree._next_node_id > 60
+    assert kinds.get(1, 0) > 200 and kinds.get(2, 0) > 100, kinds

@@ -318,10 +318,10 @@ def test_tree_orchestration_with_kernel_model(monkeypatch):
             want_node = np.where(want[1] > 0, want[0], -1)
             # the split lookup at the default range and at ranges far shorter
             # than the queries (many ranges per query, stops in any of them)
-            for t, runs, tpi in ((owner, None, 0), (owner, False, 0), (replica, None, 0), (owner, True, 32),
-                                 (replica, False, 64), (owner, None, 96)):
-                node, mlen, cmp_ = DT.match_batch(t, queries, 16, with_compared=True, runs=runs,
-                                                  tokens_per_range=tpi)
+            for t, runs, tpi in ((owner, None, -1), (owner, False, -1), (replica, None, -1), (owner, None, 0),
+                                 (owner, True, 32), (replica, False, 64), (owner, None, 96)):
+                node, mlen, cmp_ = DT.match_batch(t, queries, 16, with_compared=True, runs=runs, split=tpi >= 0,
+                                                  tokens_per_range=max(tpi, 0))
                 np.testing.assert_array_equal(mlen, want[1], err_msg=f"{i} {runs} {tpi}")
                 np.testing.assert_array_equal(np.where(mlen > 0, node, -1), want_node)
                 np.testing.assert_array_equal(cmp_, want[2])

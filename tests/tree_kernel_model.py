@@ -1,6 +1,6 @@
-"""CPU model of the tree kernels — akv_tree_apply, akv_match_prefix_variant
-and akv_match_prefix_split — reading the same AkvTreeView arrays from host
-memory, so that CPU tests can run the host-side orchestration of the device
+"""CPU model of the tree kernels — akv_tree_apply, akv_tree_commands,
+akv_match_prefix_variant and akv_match_prefix_split — reading the same
+AkvTreeView arrays from host memory, so that CPU tests can run the host-side orchestration of the device
 tree (deltas, replicas, unary-chain runs, their rebuild policy) on CPU
 DeviceTrees.  Test infrastructure only: the package's lookups run the CUDA
 kernels and nothing else.
@@ -98,6 +98,99 @@ class TreeKernelModel:
         qo = _arr(q_off, C.c_int64, (nq + 1,))
         q_all = _arr(tokens, C.c_int32, (int(qo[-1]),))
         return off, elen, arena, qo, q_all
+
+    def akv_tree_commands(self, view, token_cap, cmds, n_cmds, payload, payload_len, status, stream) -> int:
+        """The device-side inserts and prunes, restated on the host arrays:
+        the same walk, split rules, arena appends and slot claims as the
+        kernel (and, by design, as the host mirror)."""
+        self.command_calls = getattr(self, "command_calls", 0) + 1
+        slots = _arr(view.slots, C.c_int32, (view.slot_mask + 1, 4))
+        off = _arr(view.node_edge_off, C.c_int64, (view.n_nodes,))
+        ln = _arr(view.node_edge_len, C.c_int32, (view.n_nodes,))
+        arena = _arr(view.tokens, C.c_int32, (token_cap,))
+        cm = _arr(cmds, C.c_int64, (n_cmds, 8))
+        pay = _arr(payload, C.c_int32, (payload_len,))
+        mask = view.slot_mask
+
+        def probe(parent, token):
+            i = tree_hash(parent, token) & mask
+            free = -1
+            for _ in range(mask + 1):
+                p = slots[i, 0]
+                if p == EMPTY:
+                    return -1, (free if free >= 0 else i)
+                if p == DELETED:
+                    if free < 0:
+                        free = i
+                elif p == parent and slots[i, 1] == token:
+                    return i, free
+                i = (i + 1) & mask
+            return -1, free
+
+        def set_child(parent, token, child, clen):
+            found, free = probe(parent, token)
+            s_ = found if found >= 0 else free
+            assert s_ >= 0, "slot table full"
+            slots[s_] = (parent, token, child, clen)
+
+        for kind, parent, a2, src, n, ar, bs, _ in (tuple(int(x) for x in r) for r in cm):
+            if kind == 2:
+                nid = a2
+                if parent >= 0 and ln[nid] > 0:
+                    found, _f = probe(parent, int(arena[off[nid]]))
+                    if found >= 0 and slots[found, 2] == nid:
+                        slots[found] = (DELETED, 0, 0, 0)
+                off[nid], ln[nid] = 0, 0
+                continue
+            assert kind == 1, kind
+            toks = pay[src:src + n]
+            node, nxt, pos = parent, a2, 0
+
+            def append(p0):
+                nonlocal ar
+                m = n - p0
+                assert ar + m <= token_cap
+                arena[ar:ar + m] = toks[p0:]
+                ar += m
+                return ar - m
+
+            while pos < n:
+                first = int(toks[pos])
+                found, _f = probe(node, first)
+                if found < 0:
+                    o = append(pos)
+                    off[nxt], ln[nxt] = o, n - pos
+                    set_child(node, first, nxt, n - pos)
+                    break
+                child = int(slots[found, 2])
+                co, cl = int(off[child]), int(ln[child])
+                lim = min(cl, n - pos)
+                ne = np.flatnonzero(arena[co:co + lim] != toks[pos:pos + lim])
+                common = int(ne[0]) if len(ne) else lim
+                if common == cl and common == n - pos:
+                    break
+                if common == cl:
+                    node, pos = child, pos + common
+                    continue
+                split = (common // bs) * bs
+                if split == 0:
+                    o = append(pos)
+                    off[nxt], ln[nxt] = o, n - pos
+                    set_child(node, first, nxt, n - pos)
+                    break
+                mid = nxt
+                nxt += 1
+                off[mid], ln[mid] = co, split
+                off[child], ln[child] = co + split, cl - split
+                set_child(mid, int(arena[co + split]), child, cl - split)
+                set_child(node, first, mid, split)
+                if split == n - pos:
+                    break
+                o = append(pos + split)
+                off[nxt], ln[nxt] = o, n - pos - split
+                set_child(mid, int(toks[pos + split]), nxt, n - pos - split)
+                break
+        return 0
 
     def akv_match_prefix_variant(self, view, tokens, q_off, nq, block_size, out_node, out_len, out_cmp,
                                  order, status, chunks, stream) -> int:
