@@ -89,6 +89,52 @@ def _metadata_device(device: str) -> torch.device:
     )
 
 
+class _IdStage:
+    """Uploads of host id lists through reused buffers: a pinned host buffer
+    and a device buffer of the same size, used in two halves.  A half is
+    written again only after the event recorded when it was left has
+    completed (its copies are done); the device half is reused in stream
+    order, after the kernels that read it (allocator calls share a stream).
+    Replaces a fresh pinned tensor and device tensor per call."""
+
+    def __init__(self, device: torch.device, cap: int = 1 << 15) -> None:
+        self.device = device
+        self._alloc_buffers(cap)
+
+    def _alloc_buffers(self, cap: int) -> None:
+        self.cap = cap
+        self.h = torch.empty(cap, dtype=torch.int32, pin_memory=True)
+        self.h_np = self.h.numpy()
+        self.d = torch.empty(cap, dtype=torch.int32, device=self.device)
+        self.half = 0
+        self.pos = 0
+        self.left = [None, None]  # event recorded when each half was last left
+
+    def put(self, ids: np.ndarray) -> torch.Tensor:
+        n = len(ids)
+        if n == 0:
+            return self.d[:0]
+        half = self.cap // 2
+        if n > half:
+            torch.cuda.current_stream(self.device).synchronize()
+            self._alloc_buffers(max(4 * n, 2 * self.cap))
+            half = self.cap // 2
+        if self.pos + n > half:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            self.left[self.half] = ev
+            self.half ^= 1
+            self.pos = 0
+            if self.left[self.half] is not None:
+                self.left[self.half].synchronize()
+        base = self.half * half + self.pos
+        self.h_np[base : base + n] = ids
+        dst = self.d[base : base + n]
+        dst.copy_(self.h[base : base + n], non_blocking=True)
+        self.pos += n
+        return dst
+
+
 class SlabAllocator:
     """Fixed-capacity KV block pool; see the module docstring."""
 
@@ -109,21 +155,28 @@ class SlabAllocator:
         self._free_ring = torch.empty(n, dtype=i32, device=dev)
         self._limbo_ids = torch.empty(n, dtype=i32, device=dev)
         self._limbo_epochs = torch.empty(n, dtype=i64, device=dev)
-        self._ctl = torch.zeros(N.CTL_WORDS, dtype=i64, device=dev)
+        # ctl and the io words share one allocation, so one copy brings back
+        # the status, the small outputs and the counters (op count, epoch,
+        # last batch's retirements) after a single call
+        self._ctlio = torch.zeros(N.CTL_WORDS + 32, dtype=i64, device=dev)
+        self._ctl = self._ctlio[: N.CTL_WORDS]
         self._scratch_count = torch.zeros(n, dtype=i32, device=dev)
         self._scratch_last = torch.zeros(n, dtype=i32, device=dev)
         self._scratch_aux = torch.zeros(N.AUX_WORDS, dtype=i32, device=dev)
         # io: [0:8] AkvStatus, [8:40] small outputs, [40:64] small inputs
-        self._io = torch.zeros(64, dtype=i32, device=dev)
+        self._io = self._ctlio[N.CTL_WORDS :].view(i32)
         self._status = self._io[0:8]
         self._h_in = torch.zeros(24, dtype=i32, pin_memory=True)
-        self._h_out = torch.zeros(64, dtype=i32, pin_memory=True)
+        self._h_in_np = self._h_in.numpy()
+        self._h_ctlio = torch.zeros(N.CTL_WORDS + 32, dtype=i64, pin_memory=True)
+        self._h_ctlio_np = self._h_ctlio.numpy()
+        self._h_io_np = self._h_ctlio_np[N.CTL_WORDS :].view(np.int32)
+        self._ids = _IdStage(dev)
         # The device epoch as of the last wait, kept on the host so that
         # enter_read_section needs no read-back: every wait also brings back
-        # ctl[OPS .. EPOCH], and the host applies the epoch changes it can
+        # the control words, and the host applies the epoch changes it can
         # foresee (maybe_advance_epoch); a batch queued without a wait makes
         # it unknown until the next wait.
-        self._h_ctl = torch.zeros(2, dtype=i64, pin_memory=True)
         self._mirror_epoch = 0
         self._mirror_ok = True
         self._state = N.AkvAllocState(
@@ -155,15 +208,14 @@ class SlabAllocator:
         return self._reclaimer.tick(self._cfg.epoch_interval)
 
     def _sync_io(self, n_out: int = 16) -> np.ndarray:
-        """Copy status + the first outputs (and the op counter and epoch) to
-        the host and wait."""
-        h = self._h_out[: 8 + n_out]
-        h.copy_(self._io[: 8 + n_out], non_blocking=True)
-        self._h_ctl.copy_(self._ctl[N.CTL_OPS : N.CTL_EPOCH + 1], non_blocking=True)
+        """Copy the control words, the status and the first outputs to the
+        host in one copy and wait; returns the io words (status, outputs)."""
+        hi = N.CTL_WORDS + (8 + n_out + 1) // 2
+        self._h_ctlio[N.CTL_OPS : hi].copy_(self._ctlio[N.CTL_OPS : hi], non_blocking=True)
         torch.cuda.current_stream(self._dev).synchronize()
-        self._mirror_epoch = int(self._h_ctl[1])
+        self._mirror_epoch = int(self._h_ctlio_np[N.CTL_EPOCH])
         self._mirror_ok = True
-        return h.numpy().copy()
+        return self._h_io_np[: 8 + n_out].copy()
 
     def _queued(self) -> None:
         """A batch was queued without a wait: the host no longer knows the
@@ -181,7 +233,7 @@ class SlabAllocator:
     def _stage_ids(self, ids) -> int:
         """Put up to 24 ids into the device input slots; returns the pointer."""
         k = len(ids)
-        self._h_in[:k] = torch.as_tensor(ids, dtype=torch.int32)
+        self._h_in_np[:k] = ids
         self._io[40 : 40 + k].copy_(self._h_in[:k], non_blocking=True)
         return self._io[40:].data_ptr()
 
@@ -296,11 +348,9 @@ class SlabAllocator:
             ptr = self._stage_ids([handle.block_id])
             N.check(N.lib.akv_decref_batch(self._state, ptr, 1, self._tick(), None,
                                            self._status.data_ptr(), self._stream()))
-            self._h_out[40:42].copy_(self._ctl[N.CTL_LAST_RETIRED : N.CTL_LAST_RETIRED + 1].view(torch.int32),
-                                     non_blocking=True)
-            io = self._sync_io(0)
+            io = self._sync_io(0)  # the copy includes ctl[LAST_RETIRED]
             self._raise_status(io, "dec_ref")
-            return int(self._h_out[40]) > 0
+            return int(self._h_ctlio_np[N.CTL_LAST_RETIRED]) > 0
 
     def get_block_tensor(self, handle: BlockHandle) -> torch.Tensor:
         self._validate_handle(handle)
@@ -410,10 +460,9 @@ class SlabAllocator:
     def _device_ids(self, ids) -> torch.Tensor:
         if isinstance(ids, torch.Tensor) and ids.device == self._dev and ids.dtype == torch.int32:
             return ids.contiguous()
-        t = torch.as_tensor(ids, dtype=torch.int32)
-        if t.device.type == "cpu" and not t.is_pinned():
-            t = t.pin_memory()
-        return t.to(self._dev, non_blocking=True)
+        if isinstance(ids, torch.Tensor):
+            ids = ids.cpu().numpy()
+        return self._ids.put(np.asarray(ids, np.int32).reshape(-1))
 
     def alloc_batch(self, n: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """n alloc() calls in one launch; returns the ids (device int32)."""

@@ -646,7 +646,7 @@ class DeviceTree:
     def match(self, tokens: torch.Tensor, q_off: torch.Tensor, nq: int, block_size: int,
               out_node: torch.Tensor, out_len: torch.Tensor, out_cmp: Optional[torch.Tensor],
               chunks: int = 0, order: Optional[torch.Tensor] = None, runs: bool = False,
-              plan: Optional["SplitPlan"] = None) -> None:
+              plan: Optional["SplitPlan"] = None, status: Optional[torch.Tensor] = None) -> None:
         """Enqueue a match_prefix lookup of nq queries packed in `tokens` /
         `q_off` (device int32 / int64 tensors); `order` (device int32) is the
         launch order of the queries, longest first by default in
@@ -659,16 +659,18 @@ class DeviceTree:
         of plan.tokens_per_range tokens, one warp per range, so a long query
         does not hold the batch; its scratch is this tree's.  Without it,
         akv_match_prefix_variant (one warp per query).  The answers are the
-        same."""
+        same.  `status` (8 int32 on the device) replaces the tree's status
+        record for this lookup."""
         self.flush()
         if runs:
             self.build_runs()
+        st = (status if status is not None else self.status).data_ptr()
         out_c = out_cmp.data_ptr() if out_cmp is not None else None
         ordp = order.data_ptr() if order is not None else None
         if plan is None:
             N.check(N.lib.akv_match_prefix_variant(
                 self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, block_size, out_node.data_ptr(),
-                out_len.data_ptr(), out_c, ordp, self.status.data_ptr(), chunks, stream_handle(self.device)))
+                out_len.data_ptr(), out_c, ordp, st, chunks, stream_handle(self.device)))
             return
         if order is None:
             raise ValueError("match_prefix: a split lookup needs the longest-first order")
@@ -680,7 +682,7 @@ class DeviceTree:
         N.check(N.lib.akv_match_prefix_split(
             self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, block_size, out_node.data_ptr(),
             out_len.data_ptr(), out_c, ordp, plan.starts_ptr, plan.n_ranges, plan.tokens_per_range,
-            sc.data_ptr(), sc.numel(), chunks, self.status.data_ptr(), stream_handle(self.device)))
+            sc.data_ptr(), sc.numel(), chunks, st, stream_handle(self.device)))
 
     def check(self) -> None:
         s = self.status.cpu()
@@ -808,6 +810,49 @@ class QueryStage:
         self.d_ord[:nq].copy_(self.h_ord[:nq], non_blocking=True)
         self.total = total
         return self.d_tok[: max(total, 1)], self.d_off[: nq + 1], self.d_ord[: max(nq, 1)]
+
+
+class SingleLookup:
+    """One query's lookup with one upload and one read-back: the query's
+    offsets and tokens go up from one pinned buffer in one copy, and the
+    answer comes back with its own status record in one copy.  For the
+    single lookups of create_root and match_prefix."""
+
+    def __init__(self, tree: "DeviceTree") -> None:
+        self.tree = tree
+        dev = tree.device
+        self.io = torch.zeros(16, dtype=torch.int32, device=dev)  # status [0:8], node [8], length [9]
+        self.h_io = torch.zeros(16, dtype=torch.int32, pin_memory=dev.type == "cuda")
+        self.h_io_np = self.h_io.numpy()
+        self._cap = 0
+
+    def _grow(self, n: int) -> None:
+        cap = max(4 + n, 2 * self._cap, 4096)
+        pin = self.tree.device.type == "cuda"
+        self.h = torch.zeros(cap, dtype=torch.int32, pin_memory=pin)
+        self.h_np = self.h.numpy()
+        self.d = torch.zeros(cap, dtype=torch.int32, device=self.tree.device)
+        self._cap = cap
+
+    def run(self, tokens: np.ndarray, block_size: int, chunks: int = 0) -> Tuple[int, int]:
+        n = len(tokens)
+        if 4 + n > self._cap:
+            self._grow(n)
+        self.h_np[:4].view(np.int64)[:] = (0, n)  # q_off = [0, n]
+        self.h_np[4 : 4 + n] = tokens
+        self.d[: 4 + n].copy_(self.h[: 4 + n], non_blocking=True)
+        self.tree.match(self.d[4:], self.d[:4].view(torch.int64), 1, block_size, self.io[8:9], self.io[9:10],
+                        None, chunks=chunks, status=self.io[0:8])
+        self.h_io.copy_(self.io, non_blocking=True)
+        if self.tree.device.type == "cuda":
+            torch.cuda.current_stream(self.tree.device).synchronize()
+        io = self.h_io_np
+        if int(io[0]) != 0:
+            code, index, node = int(io[0]), int(io[1]), int(io[2])
+            self.io[0:8].zero_()
+            raise RuntimeError(f"agentkv_b200 tree replica error: {N.ERROR_NAMES.get(code, code)} "
+                               f"(query/update {index}, node {node})")
+        return int(io[8]), int(io[9])
 
 
 def _upload(a: np.ndarray, device: torch.device) -> torch.Tensor:

@@ -35,7 +35,8 @@ import torch
 from . import _native as N
 from .allocator import BlockHandle, SlabAllocator
 from .config import PoolConfig
-from .device_tree import DeviceTree, QueryStage, longest_first, match_batch, pack_queries, split_plan  # noqa: F401
+from .device_tree import (DeviceTree, QueryStage, SingleLookup, longest_first, match_batch,  # noqa: F401
+                          pack_queries, split_plan)
 
 ROOT_NODE_ID: int = 0
 INVALID_NODE_ID: int = -1
@@ -124,8 +125,7 @@ class DualRadixTree:
         self._version = 0
         self._ids_cache: Dict[int, Tuple[tuple, List[int]]] = {}
         dev = allocator.device
-        self._q_out = torch.zeros(4, dtype=torch.int64, device=dev)
-        self._one_stage = QueryStage(dev)  # single lookups (create_root, match_prefix)
+        self._one = SingleLookup(self._dev_tree)  # single lookups (create_root, match_prefix)
 
     # ── create / fork / allocate ──────────────────────────────────────────────
     def create_root(self, tokens: List[int]) -> NodeHandle:
@@ -423,15 +423,9 @@ class DualRadixTree:
         t = _as_i32(tokens)
         if len(t) == 0:
             return INVALID_NODE_ID, 0
-        # the tokens go up through a pinned stage of its own (an asynchronous
-        # copy); the answer's read-back is the call's one wait
-        tok, q_off, order = self._one_stage.pack([t])
-        out = self._q_out.view(torch.int32)
-        self._dev_tree.match(tok, q_off, 1, self._cfg.block_size, out[0:1], out[1:2], None,
-                             chunks=N.MATCH_PREFETCH)
-        res = out[:2].cpu()
-        self._dev_tree.check()
-        node, mlen = int(res[0]), int(res[1])
+        # one upload (offsets and tokens) and one read-back (status and
+        # answer); the kernel asks L2 for the query's tokens first
+        node, mlen = self._one.run(t, self._cfg.block_size, chunks=N.MATCH_PREFETCH)
         if mlen == 0:
             return INVALID_NODE_ID, 0
         return node, mlen
