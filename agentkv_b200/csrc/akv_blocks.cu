@@ -16,7 +16,7 @@
 #include <algorithm>
 #include <atomic>
 
-#include "akv_common.cuh"
+#include "akv_bulk.cuh"
 
 namespace {
 
@@ -123,62 +123,6 @@ k_zero_vec(char* __restrict__ pool, int64_t bpb, int32_t total, const int32_t* _
 
 // ── bulk-async (TMA engine) kernels ────────────────────────────────────────
 constexpr int kBulkChunk = 32 * 1024;  // bytes per bulk store of the zero kernel
-
-AKV_DEV uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-AKV_DEV void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-AKV_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile(
-      "{\n\t.reg .b64 st;\n\t"
-      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
-      "r"(bytes)
-      : "memory");
-}
-
-// Waits for phase `parity` of the barrier, giving up after kAkvWaitLimitNs.
-AKV_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = akv_globaltimer();
-  while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (akv_globaltimer() - t0 > kAkvWaitLimitNs) return false;
-  }
-}
-
-AKV_DEV void bulk_load(uint32_t smem_dst, const void* gsrc, uint32_t bytes, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_dst),
-      "l"(gsrc), "r"(bytes), "r"(bar)
-      : "memory");
-}
-
-AKV_DEV void bulk_store(void* gdst, uint32_t smem_src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
-               "r"(smem_src), "r"(bytes)
-               : "memory");
-}
-
-AKV_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-
-template <int N>
-AKV_DEV void bulk_wait_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-
-AKV_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 struct BulkDesc {
   char* dst;

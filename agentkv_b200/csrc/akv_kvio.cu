@@ -12,10 +12,14 @@
 //   k_kv_gather  — for every (K/V, head, block of the table) the block's
 //                  [bs, head_dim] tile of this layer, which is contiguous in
 //                  the pool, to its place in the contiguous output (the last
-//                  block's tile cut to the sequence length).
+//                  block's tile cut to the sequence length).  When every
+//                  address and the row size are 16-byte multiples
+//                  (the usual case) each tile moves as one bulk copy through
+//                  shared memory (k_kv_gather_bulk), else with vector loads
+//                  and stores of the widest word that fits.
 // Both move bits only; pool block b is the span [b * bpb, (b + 1) * bpb) laid
 // out [L][2][H][bs][head_dim].
-#include "akv_common.cuh"
+#include "akv_bulk.cuh"
 
 namespace {
 
@@ -68,6 +72,137 @@ k_kv_gather(const char* __restrict__ pool, int64_t bpb, int32_t total, int32_t H
   }
 }
 
+// Bulk-copy gather: one warp per CTA, several CTAs per SM.  The warp works
+// out 32 tiles' addresses at a time (lane i: its tile's block id, source,
+// destination and byte count), and lane 0 moves them with bulk copies —
+// global -> shared on an mbarrier, then shared -> global — kStages tiles in
+// flight.  Tiles are dealt to the CTAs round robin (tile t to CTA t mod
+// grid).  Every wait is bounded; a timeout sets AKV_ERR_TIMEOUT, lets the
+// loads in flight land and returns.
+template <int kStages>
+__global__ void __launch_bounds__(32)
+k_kv_gather_bulk(const char* __restrict__ pool, int64_t bpb, int32_t total, int32_t H, int32_t bs,
+                 int64_t row_bytes, int64_t layer_off, const int32_t* __restrict__ block_ids, int32_t n_blocks,
+                 int64_t n_tokens, char* __restrict__ out_k, char* __restrict__ out_v, AkvStatus* st) {
+  constexpr uint32_t kFull = 0xffffffffu;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  __shared__ __align__(8) uint64_t bars[kStages];
+  __shared__ char* dsts[kStages];
+  __shared__ uint32_t sizes[kStages];
+  const int lane = threadIdx.x;
+  if (akv_failed(st)) return;
+  const int64_t tile = static_cast<int64_t>(bs) * row_bytes;
+  if (lane == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  const int64_t n_items = 2ll * H * n_blocks;
+  const int64_t grid = gridDim.x;
+  int64_t next_group = 0;  // this CTA's k-th tiles are blockIdx.x + k * grid
+  const char* my_src = nullptr;
+  char* my_dst = nullptr;
+  uint32_t my_bytes = 0;
+  int cur = 32;  // position in the current group of 32 (32: take the next group)
+  bool more = true;
+  auto load_group = [&]() {
+    const int64_t t = blockIdx.x + (next_group * 32 + lane) * grid;
+    ++next_group;
+    my_bytes = 0;
+    if (t < n_items) {
+      const int32_t j = static_cast<int32_t>(t % n_blocks);
+      const int64_t kh = t / n_blocks;
+      const int32_t h = static_cast<int32_t>(kh % H);
+      const int32_t kv = static_cast<int32_t>(kh / H);
+      const int32_t b = block_ids[j];
+      const int64_t first = static_cast<int64_t>(j) * bs;
+      const int64_t rows = min(static_cast<int64_t>(bs), n_tokens - first);
+      if (static_cast<uint32_t>(b) >= static_cast<uint32_t>(total)) {
+        if (kv == 0 && h == 0) akv_fail(st, AKV_ERR_OUT_OF_RANGE, j, b, total);
+      } else if (rows > 0) {
+        my_src = pool + static_cast<int64_t>(b) * bpb + layer_off + (static_cast<int64_t>(kv) * H + h) * tile;
+        my_dst = (kv ? out_v : out_k) + (static_cast<int64_t>(h) * n_tokens + first) * row_bytes;
+        my_bytes = static_cast<uint32_t>(rows * row_bytes);
+      }
+    }
+    // any lane past the end means later groups are empty too
+    more = __ballot_sync(kFull, t < n_items) == kFull;
+  };
+  // The next tile to move (warp-uniform); false when there is none.
+  auto next_tile = [&](const char*& src, char*& dst, uint32_t& bytes) -> bool {
+    while (true) {
+      if (cur == 32) {
+        if (next_group > 0 && !more) return false;
+        load_group();
+        cur = 0;
+      }
+      const uint32_t has = __ballot_sync(kFull, my_bytes != 0) & (kFull << cur);
+      if (!has) {
+        cur = 32;
+        continue;
+      }
+      const int l = __ffs(has) - 1;
+      src = reinterpret_cast<const char*>(__shfl_sync(kFull, reinterpret_cast<uint64_t>(my_src), l));
+      dst = reinterpret_cast<char*>(__shfl_sync(kFull, reinterpret_cast<uint64_t>(my_dst), l));
+      bytes = __shfl_sync(kFull, my_bytes, l);
+      cur = l + 1;
+      return true;
+    }
+  };
+  auto issue = [&](int64_t m, const char* src, char* dst, uint32_t bytes) {
+    if (lane == 0) {
+      const int s = static_cast<int>(m % kStages);
+      dsts[s] = dst;
+      sizes[s] = bytes;
+      const uint32_t bar = smem_u32(&bars[s]);
+      mbar_expect_tx(bar, bytes);
+      bulk_load(smem_u32(smem + static_cast<size_t>(s) * tile), src, bytes, bar);
+    }
+  };
+  int64_t loads = 0, stores = 0;
+  const char* src;
+  char* dst;
+  uint32_t bytes;
+  while (loads < kStages && next_tile(src, dst, bytes)) issue(loads++, src, dst, bytes);
+  bool timed_out = false;
+  while (stores < loads) {
+    const int s = static_cast<int>(stores % kStages);
+    const uint32_t parity = static_cast<uint32_t>((stores / kStages) & 1);
+    int ok = 1;
+    if (lane == 0) {
+      ok = mbar_wait(smem_u32(&bars[s]), parity) ? 1 : 0;
+      if (ok) {
+        bulk_store(dsts[s], smem_u32(smem + static_cast<size_t>(s) * tile), sizes[s]);
+        bulk_commit();
+      } else {
+        akv_fail(st, AKV_ERR_TIMEOUT, static_cast<int32_t>(blockIdx.x), -1, 0, stores);
+      }
+    }
+    if (!__shfl_sync(kFull, ok, 0)) {
+      timed_out = true;
+      break;
+    }
+    ++stores;
+    // the store issued one iteration ago has finished reading its stage
+    if (stores >= 2) {
+      if (lane == 0) bulk_wait_read<1>();
+      __syncwarp();
+      if (next_tile(src, dst, bytes)) issue(loads++, src, dst, bytes);
+    }
+  }
+  if (lane == 0) {
+    if (timed_out) {
+      for (int64_t m = stores + 1; m < loads; ++m)
+        mbar_wait(smem_u32(&bars[m % kStages]), static_cast<uint32_t>((m / kStages) & 1));
+    }
+    bulk_wait_all();
+  }
+}
+
+constexpr int kGatherStages = 8;
+constexpr int kGatherCtasPerSm = 4;
+constexpr int64_t kGatherMaxTile = 16 * 1024;  // stage size limit: 8 x 16 KiB per CTA
+
 template <typename W>
 __global__ void __launch_bounds__(kKvThreads)
 k_kv_scatter(char* __restrict__ pool, int64_t bpb, int32_t total, int32_t H, int32_t bs, int64_t row_bytes,
@@ -116,6 +251,11 @@ int kv_grid(int64_t work) {
 
 int akv_kvio_prepare() {
 #define AKV_LOAD(fn) if (int rc = akv_load_kernel(reinterpret_cast<const void*>(fn), "akv_prepare: " #fn)) return rc
+  AKV_LOAD(k_kv_gather_bulk<kGatherStages>);
+  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(k_kv_gather_bulk<kGatherStages>),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kGatherStages * kGatherMaxTile)) != cudaSuccess)
+    return akv_cuda_fail(cudaGetLastError(), "akv_prepare: k_kv_gather_bulk shared memory");
   AKV_LOAD(k_kv_gather<uint4>);
   AKV_LOAD(k_kv_gather<uint2>);
   AKV_LOAD(k_kv_gather<uint32_t>);
@@ -148,8 +288,18 @@ extern "C" int akv_kv_gather(const void* pool, int32_t total_blocks, int32_t num
   const uint64_t bits = reinterpret_cast<uintptr_t>(pool) | reinterpret_cast<uintptr_t>(out_k) |
                         reinterpret_cast<uintptr_t>(out_v) | static_cast<uint64_t>(row_bytes);
   const int w = kv_word(bits);
-  const int grid = kv_grid(2ll * num_kv_heads * n_blocks);
   cudaStream_t s = akv_stream(stream);
+  if (w == 16 && tile <= kGatherMaxTile) {
+    const int64_t tiles = 2ll * num_kv_heads * n_blocks;
+    const int64_t cap = static_cast<int64_t>(kAkvSMs) * kGatherCtasPerSm;
+    const int grid_b = static_cast<int>(tiles < cap ? tiles : cap);
+    k_kv_gather_bulk<kGatherStages><<<grid_b, 32, static_cast<size_t>(kGatherStages * tile), s>>>(
+        static_cast<const char*>(pool), bpb, total_blocks, num_kv_heads, block_size, row_bytes, layer_off,
+        block_ids, n_blocks, n_tokens, static_cast<char*>(out_k), static_cast<char*>(out_v), status);
+    AKV_LAUNCH_CHECK("akv_kv_gather(bulk)");
+    return AKV_OK;
+  }
+  const int grid = kv_grid(2ll * num_kv_heads * n_blocks);
   // (A variant that took 4 tiles per CTA and issued all their loads at once
   // measured slower: 11.9 us against 9.8 us for a 4,096-token layer.)
 #define AKV_GATHER(W)                                                                                        \
