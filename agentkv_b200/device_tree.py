@@ -74,13 +74,32 @@ class _Changes:
     """Changes of the host mirror not yet taken by one consumer (the local
     device upload, or the replicas on other GPUs)."""
 
-    __slots__ = ("slots", "nodes", "tok_from", "full")
+    __slots__ = ("slots", "nodes", "tok_from", "full", "cmds", "cmd_tokens", "cmd_len", "cover")
 
     def __init__(self) -> None:
         self.slots: set = set()
         self.nodes: set = set()
         self.tok_from = 0
         self.full = True
+        self.drop_commands()
+
+    def drop_commands(self) -> None:
+        """Forget the recorded commands (the rows or the whole arrays cover
+        the changes instead); the next change starts a new command list."""
+        self.cmds: list = []  # the host tree's inserts and prunes since the last take
+        self.cmd_tokens: list = []
+        self.cmd_len = 0
+        self.cover = True  # every change since the last take came from a command
+
+    def take(self, n_tokens: int) -> None:
+        """Everything recorded has been sent to this consumer."""
+        self.tok_from = n_tokens
+        self.nodes.clear()
+        self.slots.clear()
+        self.drop_commands()
+
+    def commands_ready(self) -> bool:
+        return bool(self.cmds) and self.cover and not self.full
 
 
 class DeviceTree:
@@ -133,17 +152,14 @@ class DeviceTree:
         # change since the last upload came from a recorded command and no
         # array was resized or rehashed.
         self.device_commands = True
-        self._cmds: list = []
-        self._cmd_tokens: list = []
-        self._cmd_tok_len = 0
         self._cmd_scope = False
-        self._cmds_cover = True
         self.command_uploads = 0  # uploads done as commands (for tests and figures)
 
     # ── mutations (host mirror) ──────────────────────────────────────────────
     def append_tokens(self, toks: np.ndarray) -> int:
         if not self._cmd_scope:
-            self._cmds_cover = False
+            for c in self._trackers():
+                c.cover = False
         toks = np.asarray(toks, np.int32)
         need = self.n_tokens + len(toks)
         if need > len(self.h_tokens):
@@ -162,7 +178,8 @@ class DeviceTree:
 
     def set_node(self, nid: int, off: int, length: int) -> None:
         if not self._cmd_scope:
-            self._cmds_cover = False
+            for c in self._trackers():
+                c.cover = False
         if nid >= len(self.h_off):
             cap = max(nid + 1, 2 * len(self.h_off))
             for name in ("h_off", "h_len"):
@@ -202,7 +219,8 @@ class DeviceTree:
         """children[parent][token] = child; the slot also carries the child's
         edge length (the device walk chases hops with it)."""
         if not self._cmd_scope:
-            self._cmds_cover = False
+            for c in self._trackers():
+                c.cover = False
         key = (parent, token)
         s = self._slot_of.get(key)
         if s is None:
@@ -229,7 +247,8 @@ class DeviceTree:
 
     def del_child(self, parent: int, token: int) -> None:
         if not self._cmd_scope:
-            self._cmds_cover = False
+            for c in self._trackers():
+                c.cover = False
         s = self._slot_of.pop((parent, token), None)
         if s is None:
             return
@@ -280,6 +299,7 @@ class DeviceTree:
             c.full = True
             c.slots.clear()
             c.nodes.clear()
+            c.cover = False
 
     def as_replica(self) -> None:
         """This tree's device arrays come from another GPU's deltas
@@ -299,71 +319,77 @@ class DeviceTree:
         (DualRadixTree._insert_shared_locked); its mirror changes until
         end_command() are this insert's."""
         toks = np.asarray(tokens, np.int32)
-        self._cmds.append((1, parent, first_new_id, self._cmd_tok_len, len(toks), self.n_tokens, block_size, 0))
-        self._cmd_tokens.append(toks)
-        self._cmd_tok_len += len(toks)
+        for c in self._trackers():
+            c.cmds.append((1, parent, first_new_id, c.cmd_len, len(toks), self.n_tokens, block_size, 0))
+            c.cmd_tokens.append(toks)
+            c.cmd_len += len(toks)
         self._cmd_scope = True
 
     def begin_prune(self, parent: int, node: int) -> None:
         """The host tree is about to prune `node` (its parent, or -1 when the
         parent is gone); its mirror changes until end_command() are this
         prune's."""
-        self._cmds.append((2, parent, node, 0, 0, 0, 0, 0))
+        for c in self._trackers():
+            c.cmds.append((2, parent, node, 0, 0, 0, 0, 0))
         self._cmd_scope = True
 
     def end_command(self) -> None:
         self._cmd_scope = False
 
-    def _drop_commands(self) -> None:
-        self._cmds = []
-        self._cmd_tokens = []
-        self._cmd_tok_len = 0
-        self._cmds_cover = True
+    def take_commands(self, peers: bool = False) -> Optional[dict]:
+        """The recorded commands for a consumer when they account for every
+        change it has not taken (no other change, no resize or rehash), as
+        host arrays {"commands" [n, 8] int64, "payload" int32, "n_tokens",
+        "tok_lo"}, and marks them taken; else None (take_delta then)."""
+        c = self._peers if peers else self._local
+        if c is None or not c.commands_ready():
+            return None
+        d = {"commands": np.asarray(c.cmds, np.int64).reshape(-1, 8),
+             "payload": np.concatenate(c.cmd_tokens) if c.cmd_tokens else np.zeros(0, np.int32),
+             "n_tokens": self.n_tokens, "tok_lo": c.tok_from}
+        c.take(self.n_tokens)
+        return d
 
     # ── upload ───────────────────────────────────────────────────────────────
     def flush(self) -> None:
         """Ship pending changes to the device (on the current stream): as the
         host tree's commands when they account for every change since the
         last upload, else as the changed rows (or the whole arrays)."""
-        c = self._local
-        if (self.device_commands and self._cmds and self._cmds_cover and not c.full and not self._replica
-                and self.d_tokens.numel() >= self.n_tokens):
-            self._upload_commands()
-            c.tok_from = self.n_tokens
-            c.nodes.clear()
-            c.slots.clear()
-            self._drop_commands()
-            return
-        self._drop_commands()
+        if self.device_commands and not self._replica and self.d_tokens.numel() >= self.n_tokens:
+            d = self.take_commands()
+            if d is not None:
+                self.apply_commands(d)
+                return
+        self._local.drop_commands()
         d = self.take_delta()
         if d is not None:
             self.apply_delta(d)
 
-    def _upload_commands(self) -> None:
+    def apply_commands(self, d: dict) -> None:
+        """Apply the host tree's inserts and prunes to the device arrays
+        (akv_tree_commands): from take_commands on this tree or, for a
+        replica on another GPU, on the owner's.  The arrays may be host
+        (numpy) or device tensors."""
         dev = self.device
-        cmds = torch.from_numpy(np.asarray(self._cmds, np.int64).reshape(-1, 8))
-        payload = np.concatenate(self._cmd_tokens) if self._cmd_tokens else np.zeros(1, np.int32)
-        pay = torch.from_numpy(np.ascontiguousarray(payload, np.int32))
-        if dev.type == "cuda":
-            cmds, pay = cmds.pin_memory(), pay.pin_memory()
-        cmds = cmds.to(dev, non_blocking=True)
-        pay = pay.to(dev, non_blocking=True)
-        self._dev_tokens = self.n_tokens
+        cmds, pay = d["commands"], d["payload"]
+        if not isinstance(cmds, torch.Tensor):
+            cmds = torch.from_numpy(np.ascontiguousarray(cmds, np.int64))
+            pay = torch.from_numpy(np.ascontiguousarray(pay, np.int32))
+            if dev.type == "cuda":
+                cmds, pay = cmds.pin_memory(), pay.pin_memory()
+        cmds = cmds.to(dev, non_blocking=True).reshape(-1, 8)
+        pay = pay.to(dev, non_blocking=True).reshape(-1)
+        n = cmds.shape[0]
+        if n == 0:
+            return
+        self._dev_tokens = int(d["n_tokens"])
         self._view = None
-        if any(c[0] == 1 for c in self._cmds):
-            self._drop_replica_runs()
-        N.check(N.lib.akv_tree_commands(self.view(), self.d_tokens.numel(), cmds.data_ptr(), len(self._cmds),
-                                        pay.data_ptr(), int(self._cmd_tok_len), self.status.data_ptr(),
-                                        stream_handle(dev)))
+        self._drop_replica_runs()  # a replica's runs describe the tree before these changes
+        N.check(N.lib.akv_tree_commands(self.view(), self.d_tokens.numel(), cmds.data_ptr(), n,
+                                        pay.data_ptr() if pay.numel() else None, pay.numel(),
+                                        self.status.data_ptr(), stream_handle(dev)))
         self._cmd_keep = (cmds, pay)  # alive until the launch has read them
         self.command_uploads += 1
-
-    def flush_rows(self) -> None:
-        """flush() without commands: the changed rows."""
-        self._drop_commands()
-        d = self.take_delta()
-        if d is not None:
-            self.apply_delta(d)
 
     def take_delta(self, peers: bool = False) -> Optional[dict]:
         """Changes of the host mirror not yet taken by this consumer (the local
@@ -395,10 +421,15 @@ class DeviceTree:
                 nu[:, 1] = self.h_off[idx]
                 nu[:, 2] = self.h_len[idx]
             d = {"full": False, "n_tokens": hi, "tok_lo": lo, "tokens": self.h_tokens[lo:hi], "su": su, "nu": nu}
-        c.tok_from = self.n_tokens
-        c.nodes.clear()
-        c.slots.clear()
+        c.take(self.n_tokens)
         return d
+
+    def apply_shared(self, d: dict) -> None:
+        """Apply what TreeReplicaSync.share returned: commands or a delta."""
+        if "commands" in d:
+            self.apply_commands(d)
+        else:
+            self.apply_delta(d)
 
     def apply_delta(self, d: dict) -> None:
         """Bring the device arrays up to date with a delta (from take_delta on

@@ -11,11 +11,16 @@ replicas hold identical arrays and each rank answers its queries locally
 Wire format of one delta: an int64 header
     [kind, n_tokens, tok_lo, token_cap, node_cap, slot_cap, n_slot_rows, n_node_rows,
      run_nodes, n_runs]
-(kind -1 = nothing changed, 0 = incremental, 1 = full), then, skipping empty
-arrays, for a full delta tokens[n_tokens] i32, edge_off[node_cap] i64,
-edge_len[node_cap] i32, slots[slot_cap x 4] i32; for an incremental one the
-appended tokens[n_tokens - tok_lo] i32, slot rows [n x 5] i32 and node rows
-[n x 3] i64.  When the owner's unary-chain runs were rebuilt since the last
+(kind -1 = nothing changed, 0 = incremental, 1 = full, 2 = commands), then,
+skipping empty arrays, for a full delta tokens[n_tokens] i32,
+edge_off[node_cap] i64, edge_len[node_cap] i32, slots[slot_cap x 4] i32; for
+an incremental one the appended tokens[n_tokens - tok_lo] i32, slot rows
+[n x 5] i32 and node rows [n x 3] i64; for commands (every change since the
+last share was one of the host tree's inserts or prunes, and nothing was
+resized) the command records [n x 8] i64 and their tokens i32 (the
+n_slot_rows / n_node_rows fields carry their counts), which every replica
+applies itself with akv_tree_commands — a commit then travels as its tokens
+and a few ids instead of the rows it changed.  When the owner's unary-chain runs were rebuilt since the last
 share (run_nodes >= 0), run_head[run_nodes] i32 and run entries
 [n_runs x 4] i32 follow, sent straight from the owner's device arrays; a
 replica whose tree changed without new runs drops its runs and matches with
@@ -31,7 +36,7 @@ import torch
 
 from .device_tree import DeviceTree
 
-KIND_NONE, KIND_INCREMENTAL, KIND_FULL = -1, 0, 1
+KIND_NONE, KIND_INCREMENTAL, KIND_FULL, KIND_COMMANDS = -1, 0, 1, 2
 
 
 class TreeReplicaSync:
@@ -68,9 +73,14 @@ class TreeReplicaSync:
         dev = self.device
         send_runs = None
         if self.rank == self.src:
-            d = self.tree.take_delta(peers=True)
+            d = self.tree.take_commands(peers=True) if self.tree.device_commands else None
+            if d is None:
+                self.tree._peers.drop_commands()
+                d = self.tree.take_delta(peers=True)
             if d is None:
                 head = [KIND_NONE, self.tree.n_tokens, self.tree.n_tokens, 0, 0, 0, 0, 0]
+            elif "commands" in d:
+                head = [KIND_COMMANDS, d["n_tokens"], d["tok_lo"], 0, 0, 0, len(d["commands"]), len(d["payload"])]
             elif d["full"]:
                 head = [KIND_FULL, d["n_tokens"], 0, d["token_cap"], len(d["off"]), len(d["slots"]), 0, 0]
             else:
@@ -105,6 +115,18 @@ class TreeReplicaSync:
             empty = torch.empty(0, dtype=torch.int32, device=dev)
             return {"full": False, "n_tokens": n_tok, "tok_lo": tok_lo, "tokens": empty,
                     "su": empty.view(0, 5), "nu": empty.to(torch.int64).view(0, 3), **run_arrays}
+        if kind == KIND_COMMANDS:
+            out = {"n_tokens": n_tok, "tok_lo": tok_lo}
+            for name, n, dtype in (("commands", n_su * 8, torch.int64), ("payload", n_nu, torch.int32)):
+                if d is not None:
+                    t = torch.from_numpy(np.ascontiguousarray(d[name]).reshape(-1)).to(dev, dtype=dtype)
+                else:
+                    t = torch.empty(n, dtype=dtype, device=dev)
+                self._bcast(t)
+                out[name] = t
+            out["commands"] = out["commands"].view(-1, 8)
+            out.update(run_arrays)
+            return out
         if kind == KIND_FULL:
             spec = [("tokens", n_tok, torch.int32), ("off", node_cap, torch.int64),
                     ("len", node_cap, torch.int32), ("slots", slot_cap * 4, torch.int32)]
@@ -131,7 +153,13 @@ class TreeReplicaSync:
         d = self.share(runs)
         if d is None:
             return
-        self.tree.apply_delta(d)
+        if "commands" in d:
+            if self.rank == self.src:
+                self.tree.flush()  # the owner's own arrays: its local commands (never applied twice)
+            else:
+                self.tree.apply_commands(d)
+        else:
+            self.tree.apply_delta(d)  # rows are idempotent: the owner may apply them again
         if self.rank != self.src and "run_head" in d:
             self.tree.set_runs(d["run_head"], d["runs"])
 

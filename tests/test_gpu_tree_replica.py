@@ -43,8 +43,8 @@ def test_replica_from_deltas_matches_reference(golden_dir):
             owner.build_runs()  # current runs on every share, so each one travels
             d = sync.share()
             if d is not None:
-                kinds.append(d["full"])
-                replica.apply_delta(d)
+                kinds.append("commands" if "commands" in d else ("full" if d["full"] else "rows"))
+                replica.apply_shared(d)
                 if "run_head" in d:
                     replica.set_runs(d["run_head"], d["runs"])
                     runs_seen += 1
@@ -54,7 +54,8 @@ def test_replica_from_deltas_matches_reference(golden_dir):
                 n1, l1 = match_batch(replica, queries[:64], 16)
                 np.testing.assert_array_equal(n1, n0)
                 np.testing.assert_array_equal(l1, l0)
-    assert any(kinds) and not all(kinds), kinds  # both full and incremental deltas
+    # the whole arrays after a resize, else the owner tree's insert commands
+    assert "full" in kinds and kinds.count("commands") > len(kinds) // 2, kinds
     assert runs_seen > 1 and replica.d_run_head is not None  # the owner's runs reached the replica
     node, mlen, cmp_ = match_batch(replica, queries, 16, with_compared=True)
     np.testing.assert_array_equal(node, g["node"])

@@ -524,10 +524,12 @@ def test_match_prefix_many_equals_one_by_one(golden_dir, monkeypatch):
 
 def test_tree_replica_flow_on_cpu(golden_dir, monkeypatch):
     """The tree-replica flow of the GPU test (owner pool built through the
-    pool calls, TreeReplicaSync deltas with the owner's runs into a second
-    DeviceTree, lookups on both) run on CPU with the stand-ins: the replica's
-    answers equal the reference's recorded ones and the owner's comparison
-    counts, and its arrays equal the owner's."""
+    pool calls, TreeReplicaSync shares — the whole arrays after a resize,
+    else the owner tree's insert commands that the replica applies itself —
+    with the owner's runs into a second DeviceTree, lookups on both) run on
+    CPU with the stand-ins: the replica's answers equal the reference's
+    recorded ones and the owner's comparison counts, and its arrays equal
+    the owner's."""
     import torch
 
     from agentkv_b200.device_tree import DeviceTree, match_batch
@@ -557,8 +559,8 @@ def test_tree_replica_flow_on_cpu(golden_dir, monkeypatch):
             owner.build_runs()
             d = sync.share()
             if d is not None:
-                kinds.append(d["full"])
-                replica.apply_delta(d)
+                kinds.append("commands" if "commands" in d else ("full" if d["full"] else "rows"))
+                replica.apply_shared(d)
                 if "run_head" in d:
                     replica.set_runs(d["run_head"], d["runs"])
                     runs_seen += 1
@@ -567,7 +569,7 @@ def test_tree_replica_flow_on_cpu(golden_dir, monkeypatch):
                 n1, l1 = match_batch(replica, queries[:64], 16)
                 np.testing.assert_array_equal(n1, n0)
                 np.testing.assert_array_equal(l1, l0)
-    assert any(kinds) and not all(kinds), kinds
+    assert "full" in kinds and kinds.count("commands") > len(kinds) // 2, kinds
     assert runs_seen > 1 and replica.d_run_head is not None
     node, mlen, cmp_ = match_batch(replica, queries, 16, with_compared=True)
     np.testing.assert_array_equal(node, g["node"])
@@ -804,14 +806,14 @@ def test_tree_commands_under_random_churn(monkeypatch):
     monkeypatch.setattr(N, "lib", model)
     monkeypatch.setattr(DT, "stream_handle", lambda dev: 0)
     kinds = {}
-    orig = DT.DeviceTree._upload_commands
+    orig = DT.DeviceTree.apply_commands
 
-    def counting(self):
-        for c in self._cmds:
-            kinds[c[0]] = kinds.get(c[0], 0) + 1
-        orig(self)
+    def counting(self, d):
+        for c in np.asarray(d["commands"]).reshape(-1, 8):
+            kinds[int(c[0])] = kinds.get(int(c[0]), 0) + 1
+        orig(self, d)
 
-    monkeypatch.setattr(DT.DeviceTree, "_upload_commands", counting)
+    monkeypatch.setattr(DT.DeviceTree, "apply_commands", counting)
     for seed in range(3):
         slab = OracleSlab(torch.zeros((400, 1, 2, 1, 4, 2), dtype=torch.float16), 7)
         tree = DualRadixTree(slab, PoolConfig(total_blocks=400, block_size=4, num_layers=1, num_kv_heads=1,

@@ -310,7 +310,7 @@ def test_tree_orchestration_with_kernel_model(monkeypatch):
                 owner.build_runs()  # else the policy decides whether new runs travel
             d = sync.share()
             if d is not None:
-                replica.apply_delta(d)
+                replica.apply_shared(d)
                 if "run_head" in d:
                     replica.set_runs(d["run_head"], d["runs"])
         if i % 21 == 20:
@@ -332,7 +332,7 @@ def test_tree_orchestration_with_kernel_model(monkeypatch):
     owner.build_runs()
     d = sync.share()
     if d is not None:
-        replica.apply_delta(d)
+        replica.apply_shared(d)
         if "run_head" in d:
             replica.set_runs(d["run_head"], d["runs"])
     owner.flush()
