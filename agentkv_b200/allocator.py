@@ -172,6 +172,12 @@ class SlabAllocator:
         self._h_ctlio_np = self._h_ctlio.numpy()
         self._h_io_np = self._h_ctlio_np[N.CTL_WORDS :].view(np.int32)
         self._ids = _IdStage(dev)
+        self._ctlio_ptr = self._ctlio.data_ptr()
+        self._io_ptr = self._io.data_ptr()
+        self._h_ctlio_ptr = self._h_ctlio.data_ptr()
+        self._h_in_ptr = self._h_in.data_ptr()
+        self._h_ref = torch.zeros(2, dtype=i32, pin_memory=True)
+        self._h_ref_np = self._h_ref.numpy()
         # The device epoch as of the last wait, kept on the host so that
         # enter_read_section needs no read-back: every wait also brings back
         # the control words, and the host applies the epoch changes it can
@@ -211,8 +217,9 @@ class SlabAllocator:
         """Copy the control words, the status and the first outputs to the
         host in one copy and wait; returns the io words (status, outputs)."""
         hi = N.CTL_WORDS + (8 + n_out + 1) // 2
-        self._h_ctlio[N.CTL_OPS : hi].copy_(self._ctlio[N.CTL_OPS : hi], non_blocking=True)
-        torch.cuda.current_stream(self._dev).synchronize()
+        off = 8 * N.CTL_OPS
+        N.check(N.lib.akv_copy_wait(self._h_ctlio_ptr + off, self._ctlio_ptr + off, 8 * hi - off, 1, 1,
+                                    self._stream()))
         self._mirror_epoch = int(self._h_ctlio_np[N.CTL_EPOCH])
         self._mirror_ok = True
         return self._h_io_np[: 8 + n_out].copy()
@@ -234,8 +241,9 @@ class SlabAllocator:
         """Put up to 24 ids into the device input slots; returns the pointer."""
         k = len(ids)
         self._h_in_np[:k] = ids
-        self._io[40 : 40 + k].copy_(self._h_in[:k], non_blocking=True)
-        return self._io[40:].data_ptr()
+        dst = self._io_ptr + 40 * 4
+        N.check(N.lib.akv_copy_wait(dst, self._h_in_ptr, 4 * k, 0, 0, self._stream()))
+        return dst
 
     def _raise_status(self, io: np.ndarray, op: str = "") -> None:
         code = int(io[0])
@@ -362,7 +370,7 @@ class SlabAllocator:
         self._validate_handle(dst)
         with self._lock:
             if self._kv_data.device.type == "meta":
-                rc = int(self._ref_counts[dst.block_id].item())
+                rc = self._read_ref(dst.block_id)
                 if rc != 1:
                     raise self._exception(N.AKV_ERR_NOT_EXCLUSIVE, dst.block_id, rc, "copy_block")
                 return
@@ -377,7 +385,7 @@ class SlabAllocator:
         self._validate_handle(handle)
         with self._lock:
             if self._kv_data.device.type == "meta":
-                rc = int(self._ref_counts[handle.block_id].item())
+                rc = self._read_ref(handle.block_id)
                 if rc != 1:
                     raise self._exception(N.AKV_ERR_NOT_EXCLUSIVE, handle.block_id, rc, "zero_block")
                 return
@@ -401,7 +409,13 @@ class SlabAllocator:
     def ref_count(self, handle: BlockHandle) -> int:
         self._validate_handle(handle)
         with self._lock:
-            return int(self._ref_counts[handle.block_id].item())
+            return self._read_ref(handle.block_id)
+
+    def _read_ref(self, block_id: int) -> int:
+        """One block's refcount (one copy and one wait)."""
+        N.check(N.lib.akv_copy_wait(self._h_ref.data_ptr(), self._ref_counts.data_ptr() + 4 * block_id, 4, 1, 1,
+                                    self._stream()))
+        return int(self._h_ref_np[0])
 
     def ctl(self) -> np.ndarray:
         """Host copy of the control words (waits)."""

@@ -36,6 +36,22 @@ extern "C" int akv_status_clear(AkvStatus* status, void* stream) {
   return AKV_OK;
 }
 
+extern "C" int akv_copy_wait(void* dst, const void* src, int64_t bytes, int32_t to_host, int32_t wait,
+                             void* stream) {
+  AKV_ARG_CHECK(bytes >= 0 && (bytes == 0 || (dst != nullptr && src != nullptr)), "akv_copy_wait: bad arguments");
+  cudaStream_t s = akv_stream(stream);
+  if (bytes > 0) {
+    const cudaError_t e = cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes),
+                                          to_host ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return akv_cuda_fail(e, "akv_copy_wait: copy");
+  }
+  if (wait) {
+    const cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return akv_cuda_fail(e, "akv_copy_wait: wait");
+  }
+  return AKV_OK;
+}
+
 extern "C" int akv_prepare(void) {
   if (int rc = akv_blocks_prepare()) return rc;
   if (int rc = akv_alloc_prepare()) return rc;

@@ -871,12 +871,18 @@ class SingleLookup:
             self._grow(n)
         self.h_np[:4].view(np.int64)[:] = (0, n)  # q_off = [0, n]
         self.h_np[4 : 4 + n] = tokens
-        self.d[: 4 + n].copy_(self.h[: 4 + n], non_blocking=True)
+        cuda = self.tree.device.type == "cuda"
+        stream = stream_handle(self.tree.device) if cuda else 0
+        if cuda:
+            N.check(N.lib.akv_copy_wait(self.d.data_ptr(), self.h.data_ptr(), 4 * (4 + n), 0, 0, stream))
+        else:
+            self.d[: 4 + n].copy_(self.h[: 4 + n])
         self.tree.match(self.d[4:], self.d[:4].view(torch.int64), 1, block_size, self.io[8:9], self.io[9:10],
                         None, chunks=chunks, status=self.io[0:8])
-        self.h_io.copy_(self.io, non_blocking=True)
-        if self.tree.device.type == "cuda":
-            torch.cuda.current_stream(self.tree.device).synchronize()
+        if cuda:
+            N.check(N.lib.akv_copy_wait(self.h_io.data_ptr(), self.io.data_ptr(), 4 * 16, 1, 1, stream))
+        else:
+            self.h_io.copy_(self.io)
         io = self.h_io_np
         if int(io[0]) != 0:
             code, index, node = int(io[0]), int(io[1]), int(io[2])

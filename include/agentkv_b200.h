@@ -75,6 +75,15 @@ AKV_API int akv_status_clear(AkvStatus* status, void* stream);
  * first use would happen inside a CUDA stream capture. */
 AKV_API int akv_prepare(void);
 
+/* A copy of `bytes` between a host buffer (pinned for an asynchronous copy)
+ * and device memory on `stream` (to_host = 1: device -> host), then, with
+ * wait = 1, a wait for the stream.  No counterpart in the reference (whose
+ * metadata lives on the host): the per-call API's one round trip — a call's
+ * inputs up, or its status, outputs and counters back — in one call from
+ * the host language. */
+AKV_API int akv_copy_wait(void* dst, const void* src, int64_t bytes, int32_t to_host, int32_t wait,
+                          void* stream);
+
 /* ── block movement ─────────────────────────────────────────────────────────
  * The pool is the reference's `_kv_data` tensor
  * [total_blocks, L, 2, H_kv, block_size, D] (agentkv/core/slab_allocator.py:155-164)
