@@ -100,9 +100,9 @@ def parse_args():
                          "in the step), or rank 0 plans and broadcasts each level's pairs / all pairs once")
     ap.add_argument("--graph-nccl", type=int, default=1,
                     help="N > 1: capture the step, NCCL pair broadcast included, as a CUDA graph")
-    ap.add_argument("--graph-steps", type=int, default=2,
-                    help="consecutive steps recorded in one CUDA graph (the next step's planning overlaps the "
-                         "current copy)")
+    ap.add_argument("--graph-steps", type=int, default=8,
+                    help="consecutive fan-outs recorded in one CUDA graph (the next fan-out's planning overlaps "
+                         "the current copy)")
     ap.add_argument("--copy-levels", default="merged", choices=["merged", "per-level"],
                     help="copy every level's CoW pairs in one launch after the last plan, or one launch per "
                          "level as soon as its plan is ready")
@@ -123,8 +123,9 @@ def parse_args():
                     help="match_prefix verify width: 32-token compares per lane per step (0: the default)")
     ap.add_argument("--match-pipelined", type=int, default=-1,
                     help="match_prefix verify rounds two in flight (1) or one (0); -1: the default")
-    ap.add_argument("--match-split", type=int, default=1,
-                    help="match_prefix splits queries into token ranges, one warp each (0: one warp per query)")
+    ap.add_argument("--match-split", type=int, default=0,
+                    help="match_prefix splits queries into token ranges, one warp each (default 0: one warp per "
+                         "query, measured faster on this workload)")
     ap.add_argument("--match-tokens-per-range", type=int, default=0,
                     help="match_prefix split range in tokens, a multiple of 32 (0: the library's default)")
     ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers", "hf", "react", "percall"],
@@ -750,7 +751,7 @@ def match_cpu_baseline(pool, batches, gpu_results, max_seconds: float) -> dict:
 
 def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
                  n_queries: int = W.MatchSpec.n_queries, rank: int = 0, world: int = 1,
-                 use_runs: bool = True, cpu_seconds: float = 0.0, chunks: int = 0, split: bool = True,
+                 use_runs: bool = True, cpu_seconds: float = 0.0, chunks: int = 0, split: bool = False,
                  tokens_per_item: int = 0, min_seconds: float = 0.0) -> dict:
     """match_prefix on the stress tree.  With N ranks, rank 0 builds the tree
     through the pool API and broadcasts it (TreeReplicaSync) to every rank's
@@ -911,7 +912,8 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         "replica_sync_s": round(sync_s, 2),
         "query_tokens_per_batch": int(statistics.mean(qtokens)),
         "unary_runs": bool(use_runs),
-        "verify_chunks": chunks or (8 if split else 4),
+        "verify_chunks": (chunks & 0xFF) or (4 if split else 8),
+        "verify_flags": {"pipelined": bool(chunks & 0x100), "prefetch": bool(chunks & 0x200)},
         "split": ({"tokens_per_range": plans[0].tokens_per_range, "ranges_per_batch": plans[0].n_items}
                   if split else None),
         "roofline": roofline,
