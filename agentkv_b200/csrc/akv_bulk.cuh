@@ -1,6 +1,6 @@
 // akv_bulk.cuh — mbarrier and bulk-async copy (TMA engine) helpers shared by
 // the bulk kernels: global -> shared loads completing on an mbarrier, shared
-// -> global stores in bulk groups.  All non-multicast, CTA-local.
+// -> global stores in bulk groups.  Every copy is CTA-local (one CTA's own shared memory).
 #pragma once
 
 #include "akv_common.cuh"
