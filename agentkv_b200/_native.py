@@ -133,6 +133,8 @@ SIGNATURES = {
     "akv_version": (C.c_int, []),
     "akv_last_error": (C.c_int, [C.c_char_p, C.c_int]),
     "akv_status_clear": (C.c_int, [_P, _P]),
+    "akv_agent_steps": (C.c_int, [C.POINTER(AkvAllocState), C.POINTER(AkvTick), _P, _P, _I32, _I32, _P, _I32, _P, _P,
+                                  _I32, _P, _I32, _P, _P]),
     "akv_copy_wait": (C.c_int, [_P, _P, _I64, _I32, _I32, _P]),
     "akv_prepare": (C.c_int, []),
     "akv_copy_blocks": (C.c_int, [_P, _I64, _I32, _P, _I32, _P, _P, _P]),

@@ -66,6 +66,7 @@ int akv_alloc_prepare();
 int akv_tree_prepare();
 int akv_fanout_prepare();
 int akv_kvio_prepare();
+int akv_agents_prepare();
 
 #define AKV_ARG_CHECK(cond, ...)              \
   do {                                        \

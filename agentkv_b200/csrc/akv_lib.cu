@@ -57,5 +57,6 @@ extern "C" int akv_prepare(void) {
   if (int rc = akv_alloc_prepare()) return rc;
   if (int rc = akv_tree_prepare()) return rc;
   if (int rc = akv_kvio_prepare()) return rc;
+  if (int rc = akv_agents_prepare()) return rc;
   return akv_fanout_prepare();
 }

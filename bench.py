@@ -135,6 +135,8 @@ def parse_args():
                          "head-sharded under torchrun; percall: per-call latency of the reference-facing API "
                          "(each prints its own line)")
     ap.add_argument("--batches", default="1,8,64,512,4096", help="sweep batch sizes")
+    ap.add_argument("--react-steps-per-launch", type=int, default=10,
+                    help="react: trace steps applied per akv_agent_steps launch")
     ap.add_argument("--rotations", type=int, default=8, help="sweep: distinct pair sets cycled")
     return ap.parse_args()
 
@@ -1256,17 +1258,20 @@ def react_cpu_baseline(spec, heads: int, max_seconds: float) -> dict:
 def react_case(args) -> None:
     """The ReAct multi-agent trace (a 16,384-token shared prefix, 32 agents,
     1,000 steps of forks, CoW tail copies, frees, appends and epoch advances)
-    at the Llama-3-70B KV shape (40,000 blocks).  Rank 0 plays each step
-    through the pool's per-call API on a metadata-only pool (the vLLM
-    adapter's pattern: copy_block replaced on the instance to record the
-    step's pairs), packs the pairs into one count + pairs buffer and
-    broadcasts it; every rank copies its KV-head slice of those blocks
-    (akv_copy_blocks_counted reads the count on the device).  One bench step
-    = one trace step, host calls included; warm-up and timed steps are
-    consecutive steps of the trace."""
+    at the Llama-3-70B KV shape (40,000 blocks).  Rank 0 holds the agents'
+    block tables on the device (DeviceAgents) and applies
+    --react-steps-per-launch trace steps per akv_agent_steps launch; each
+    step's copy-on-write pairs (a count + pairs buffer written by that
+    launch) are broadcast to every rank, which copies its KV-head slice of
+    those blocks (akv_copy_blocks_counted reads the count on the device).  One
+    bench step = one trace step; warm-up and timed steps are consecutive
+    steps of the trace.  Beside it, `percall`: the same steps through the
+    pool's per-call API on a metadata-only pool with the vLLM adapter's
+    copy_block hook recording the pairs (rank 0, one GPU)."""
     import torch
 
     from agentkv_b200 import AgentKVPool, PoolConfig
+    from agentkv_b200.agents import DeviceAgents
     from agentkv_b200.sharded import ShardedCopier
 
     rank = int(os.environ.get("RANK", "0"))
@@ -1286,46 +1291,77 @@ def react_case(args) -> None:
     pool_slice = torch.empty((n_, L, 2, heads, bs, D), dtype=torch.bfloat16, device=dev)
     copier = ShardedCopier(pool_slice)
     buf = copier.batch_buffer(spec.agents)  # at most one CoW per agent per step
-    trace = iter(W.react_trace(spec))
+    trace = W.react_trace(spec)
     warmup = max(3, args.warmup)
     steps = max(1, min(args.steps, spec.steps - warmup))
+    per_launch = max(1, args.react_steps_per_launch)
     pairs_done = [0]
-    if rank == 0:
-        meta = AgentKVPool(config=PoolConfig(total_blocks=n_, block_size=bs, num_layers=L, num_kv_heads=H,
+    state = {"next": 0, "rows": None, "row": 0}
+
+    def meta_pool():
+        return AgentKVPool(config=PoolConfig(total_blocks=n_, block_size=bs, num_layers=L, num_kv_heads=H,
                                              head_dim=D, dtype=dt, device="meta"))
-        step_pairs = []
-        orig = meta._allocator.copy_block
 
-        def record(src, dst):
-            step_pairs.append((src.block_id, dst.block_id))
-            orig(src, dst)
-
-        meta._allocator.copy_block = record
-        api = _ReActPool(meta)
-        root, agents = W.react_setup(api, spec)
+    if rank == 0:
+        meta = meta_pool()
+        root, agents = W.react_setup(_ReActPool(meta), spec)
+        dev_agents = DeviceAgents(meta, root, agents)
 
     def one_step():
         if rank == 0:
-            step_pairs.clear()
-            W.react_step(api, root, agents, next(trace))
-            copier.pack_batch(step_pairs, buf)
-            pairs_done[0] += len(step_pairs)
-        copier.share_batch(buf)
-        copier.copy_batch(buf)
+            rows = state["rows"]
+            if rows is None or state["row"] >= rows.shape[0]:
+                i = state["next"]
+                state["rows"] = rows = dev_agents.steps(trace[i:i + per_launch], pairs_cap=spec.agents)
+                state["next"] = i + rows.shape[0]
+                state["row"] = 0
+            b = rows[state["row"]]  # this step's count + pairs, written by the launch
+            state["row"] += 1
+        else:
+            b = buf
+        copier.share_batch(b)
+        copier.copy_batch(b)
 
     sampler = ClockSampler(local)
     with sampler:
         for _ in range(warmup):
             one_step()
-        pairs_done[0] = 0
         ms, wall = timed(one_step, steps, 0, world)
     clocks = sampler.summary()
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = react_cpu_baseline(spec, heads, args.cpu_seconds)
+    n_pairs_timed = None
+    if rank == 0:
+        dev_agents.check()
+    cpu = percall = None
+    if rank == 0 and world == 1:
+        # the per-call pattern on the same trace steps (timed alone, no copies)
+        meta2 = meta_pool()
+        step_pairs = []
+        orig = meta2._allocator.copy_block
+
+        def record(src, dst):
+            step_pairs.append((src.block_id, dst.block_id))
+            orig(src, dst)
+
+        meta2._allocator.copy_block = record
+        api = _ReActPool(meta2)
+        root2, agents2 = W.react_setup(api, spec)
+        for i in range(warmup):
+            W.react_step(api, root2, agents2, trace[i])
+        step_pairs.clear()
+        t0 = time.perf_counter()
+        for i in range(warmup, warmup + steps):
+            W.react_step(api, root2, agents2, trace[i])
+        pc_s = time.perf_counter() - t0
+        n_pairs_timed = len(step_pairs)
+        percall = {"value": round(steps / pc_s, 2), "unit": "steps/s", "ms_per_step": round(1e3 * pc_s / steps, 4),
+                   "api": "AgentKVPool per-call API (free / fork / ensure_mutable_block / allocate_block / "
+                          "maybe_advance_epoch) on a metadata pool, copy_block hook recording the pairs; host "
+                          "wall time, no copies"}
+        if not args.no_cpu_baseline:
+            cpu = react_cpu_baseline(spec, heads, args.cpu_seconds)
     if rank == 0:
         step_ms = ms / steps
-        print(json.dumps({
+        line = {
             "case": "react_70b",
             "metric": "ReAct trace steps/s (32 agents, Llama-3-70B KV)",
             "value": round(steps / (ms / 1e3), 2),
@@ -1343,113 +1379,21 @@ def react_case(args) -> None:
                        "bytes_per_block_per_rank": slice_bytes,
                        "parallelism": f"kv-head shard x{world}" if world > 1 else
                                       "single GPU, 4 of 8 KV heads (the full pool is 200 GB)",
-                       "trace_steps": f"{warmup}..{warmup + steps - 1} of {spec.steps}"},
-            "cow_pairs_per_step": round(pairs_done[0] / steps, 2),
-            "copy_gbs_per_rank": round(pairs_done[0] * 2 * slice_bytes / (ms / 1e3) / 1e9, 1),
+                       "trace_steps": f"{warmup}..{warmup + steps - 1} of {spec.steps}",
+                       "api": f"DeviceAgents: {per_launch} trace steps per akv_agent_steps launch, each step's "
+                              f"pairs broadcast and copied (akv_copy_blocks_counted)"},
+            "percall": percall,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "wall_s_timed": round(wall, 3),
-        }), flush=True)
+        }
+        if n_pairs_timed is not None:
+            line["cow_pairs_per_step"] = round(n_pairs_timed / steps, 2)
+            line["copy_gbs_per_rank"] = round(n_pairs_timed * 2 * slice_bytes / (ms / 1e3) / 1e9, 1)
+        print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
-
-
-def percall_timings(api, prompt, query, copy_hook: bool, reps: int, match_fn, free_match=None) -> dict:
-    """Median microseconds per call of the reference-facing per-call API on
-    `api` (AgentKVPool, or the oracle's tree with the same call set): the
-    vLLM adapter's calls (fork, allocate_block, ensure_mutable_block on a
-    shared last block, free) and the SGLang adapter's match_prefix.  One
-    round: fork the root, allocate a block, copy-on-write the last
-    inherited block, look the query up, free the child (and the match's
-    handle).  The root keeps 128 residual blocks, so a fork increments 128
-    refcounts and the copy-on-write copies a 2 MiB block."""
-    times = {k: [] for k in ("fork", "allocate_block", "ensure_mutable_block", "match_prefix", "free")}
-    root = api.create_root(prompt)
-    need = -(-len(prompt) // 16)
-    for _ in range(need):
-        api.allocate_block(root)
-    api.commit_prefix(root, len(prompt) // 2)  # half the prompt shared, half the root's own blocks
-    pc = time.perf_counter
-    for i in range(reps + 3):
-        t0 = pc()
-        child = api.fork(root)
-        t1 = pc()
-        api.allocate_block(child)
-        t2 = pc()
-        api.ensure_mutable_block(child, -2)
-        t3 = pc()
-        h, _ = match_fn(query)
-        t4 = pc()
-        api.free(child)
-        t5 = pc()
-        if h is not None and free_match is not None:
-            free_match(h)
-        if i >= 3:
-            for k, (a, b) in zip(times, ((t0, t1), (t1, t2), (t2, t3), (t3, t4), (t4, t5))):
-                times[k].append((b - a) * 1e6)
-    return {k: round(statistics.median(v), 2) for k, v in times.items()}
-
-
-def percall_case(args) -> None:
-    """Per-call latency of the reference-facing API (the calls the reference's
-    vLLM and SGLang adapters make one at a time: fork, allocate_block,
-    ensure_mutable_block, match_prefix, free) on a metadata-only pool and on
-    a CUDA pool at the Llama-3-8B shape, with and without the copy_block hook
-    the vLLM adapter installs, beside the oracle's restatement of the
-    reference's per-call path on the host (kind "port": its allocator is the
-    C restatement, its tree Python, as the reference's is)."""
-    import torch
-
-    from agentkv_b200 import AgentKVPool, PoolConfig
-    from oracle import oracle as O
-
-    torch.cuda.set_device(0)
-    n_, bs, L, H, D, dt = W.LLAMA3_8B_GEOMETRY
-    rng = np.random.default_rng(7)
-    prompt = rng.integers(0, 128256, size=4096).tolist()
-    query = prompt[:3000] + rng.integers(0, 128256, size=500).tolist()
-    reps = max(50, args.steps * 10)
-    out = {"case": "percall", "unit": "us per call (median)", "reps": reps,
-           "workload": "4096-token root (256 blocks), its first 2048 tokens committed to the tree; per round: "
-                       "fork it, allocate a block, copy-on-write the child's last inherited block, match_prefix "
-                       "a 3500-token query sharing 3000 tokens with the root, free the child", "pools": {}}
-    for name, device, blocks in (("meta", "meta", 60000), ("cuda", "cuda", 1024)):
-        for hook in (False, True):
-            pool = AgentKVPool(config=PoolConfig(total_blocks=blocks, block_size=bs, num_layers=L, num_kv_heads=H,
-                                                 head_dim=D, dtype=dt, device=device))
-            pairs = []
-            if hook:
-                orig = pool._allocator.copy_block
-
-                def record(src, dst, orig=orig):
-                    pairs.append((src.block_id, dst.block_id))
-                    orig(src, dst)
-
-                pool._allocator.copy_block = record
-            tree = pool._tree
-            res = percall_timings(pool, prompt, query, hook, reps, tree.match_prefix, free_match=pool.free)
-            torch.cuda.synchronize()
-            out["pools"][f"{name}{' + copy_block hook' if hook else ''}"] = res
-            del pool
-    # the reference's per-call path restated on the host: Python tree, C allocator
-    oa = O.OracleAllocator(60000)
-    ot = O.OracleTree(oa, bs)
-
-    def ofree(h):
-        ot.free(h)
-
-    res = percall_timings(ot, prompt, query, False, reps, ot.match_prefix, free_match=ofree)
-    # and with the 2 MiB block copies on a host pool, as a device="cpu" pool does them
-    bpb = L * 2 * H * bs * D * 2
-    host_pool = np.zeros((1024, bpb), np.uint8)
-    oa2 = O.OracleAllocator(1024)
-    ot2 = O.OracleTree(oa2, bs, copy_cb=lambda s_, d_: np.copyto(host_pool[d_], host_pool[s_]))
-    res2 = percall_timings(ot2, prompt, query, False, reps, ot2.match_prefix, free_match=ot2.free)
-    out["cpu_baseline"] = {"kind": "port", "cores": 1, "value": res,
-                           "sample": f"{reps} rounds on a 60,000-block metadata pool, one host thread",
-                           "with_copies": res2, "host": host_cpu()}
-    print(json.dumps(out), flush=True)
 
 
 # ── main arm ─────────────────────────────────────────────────────────────────

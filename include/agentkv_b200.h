@@ -375,6 +375,33 @@ AKV_API int akv_fanout_tree_plan(const int32_t* root_tables, const int64_t* root
                          const int32_t* fresh_ids, int32_t* child_tables, int32_t* inc_ids,
                          int32_t* pairs, int32_t* dec_ids, void* stream);
 
+/* ── agents stepped on the device ────────────────────────────────────────────
+ * A batch of the per-call steps the reference's multi-agent pattern makes,
+ * applied by one warp to agents whose residual block tables live in device
+ * memory (tables[n_agents][capacity], lens[n_agents]), with the reference's
+ * sequential allocator semantics op by op.  actions: int32 [n][3] {kind,
+ * slot, target}, step s = actions [step_off[s], step_off[s+1]) (device):
+ *   0 fork     free agent `target`, then fork agent `slot` into it
+ *              (DualRadixTree.free + fork, agentkv/core/radix_tree.py:
+ *              351-377, 222-264)
+ *   1 cow      ensure_mutable_block(agent, -1) (:286-314): a shared tail block
+ *              is replaced by a fresh copy (alloc, the pair, dec_ref); an agent
+ *              without blocks allocates one instead (:266-284)
+ *   2 free     free agent `slot`, restart it as a fork of the root table
+ *   3 advance  EpochReclaimer.maybe_advance (reclamation.py:129-143)
+ *   4 append   allocate_block(agent)
+ * Tables hold distinct ids (as a handle's residual blocks do).  Step s's
+ * copy-on-write pairs go to pairs_out + s * (2 + 2 * pairs_cap) as an int64
+ * count then the pairs (the akv_copy_blocks_counted format).  An action
+ * that fails changes nothing, every earlier one stays applied (as the
+ * reference's calls would), the error goes to `status` and the kernel stops.
+ * Shared-tree references of the agents are the caller's (they do not change
+ * the allocator).  One launch. */
+AKV_API int akv_agent_steps(const AkvAllocState* st, const AkvTick* tick, int32_t* tables, int32_t* lens,
+                            int32_t n_agents, int32_t capacity, const int32_t* root_table, int32_t root_len,
+                            const int32_t* actions, const int32_t* step_off, int32_t n_steps,
+                            int32_t* pairs_out, int32_t pairs_cap, AkvStatus* status, void* stream);
+
 /* ── shared radix tree: device replica and match_prefix ─────────────────────
  * Replaces DualRadixTree._match_prefix_locked (agentkv/core/radix_tree.py:
  * 513-570), reached from create_root (:203) and match_prefix (:379-416).

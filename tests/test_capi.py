@@ -240,3 +240,27 @@ def test_host_argument_checks_of_split_match():
     assert N.lib.akv_match_scratch_bytes(3, 100, 48) == -1
     assert N.lib.akv_match_scratch_bytes(4096, 18_000_000, 0) == \
         (16 * (4096 + 18_000_000 // 1024) + 4 * 4096 + 255) // 256 * 256
+
+
+def test_host_argument_checks_of_agent_steps():
+    """akv_agent_steps refuses on the host: an incomplete allocator state, a
+    bad tick, a NULL status, bad sizes (no agents, a root table longer than
+    the capacity, a negative step count), NULL arrays; zero steps is a
+    no-op.  (Dummy pointers: nothing is dereferenced.)"""
+    P = 16
+    tick = N.AkvTick(0, 0, 64, 0)
+    ok = N.AkvAllocState(P, P, P, P, P, None, None, None, 64, 0)
+    f = N.lib.akv_agent_steps
+
+    def call(st=ok, tk=tick, n_agents=4, cap=8, root_len=2, n_steps=1, status=P, actions=P):
+        return f(C.byref(st), C.byref(tk), P, P, n_agents, cap, P, root_len, actions, P, n_steps, P, 4, status, None)
+
+    assert call(st=N.AkvAllocState(None, P, P, P, P, None, None, None, 64, 0)) == N.AKV_ERR_INVALID_ARG
+    assert "incomplete" in N.last_error()
+    assert call(tk=N.AkvTick(0, 0, 0, 0)) == N.AKV_ERR_INVALID_ARG and "tick" in N.last_error()
+    assert call(status=None) == N.AKV_ERR_INVALID_ARG and "status" in N.last_error()
+    assert call(n_agents=0) == N.AKV_ERR_INVALID_ARG
+    assert call(root_len=9) == N.AKV_ERR_INVALID_ARG
+    assert call(n_steps=-1) == N.AKV_ERR_INVALID_ARG
+    assert call(actions=None) == N.AKV_ERR_INVALID_ARG and "NULL" in N.last_error()
+    assert call(n_steps=0, actions=None) == N.AKV_OK

@@ -141,3 +141,54 @@ def test_counted_copy_caps_and_empty():
     assert np.array_equal(pool.cpu().numpy(), host)
     with pytest.raises(ValueError):
         copier.pack_batch([[0, 1]] * 9, buf)
+
+
+@pytest.mark.parametrize("per_launch", [1, 10])
+def test_react_trace_device_agents(golden_dir, per_launch):
+    """The same trace through DeviceAgents: the agents' block tables on the
+    device, `per_launch` steps applied by one akv_agent_steps launch.  Each
+    step's copy-on-write pairs (read from the launch's pair buffer) equal the
+    reference's recorded ones; copying them step by step with the counted
+    copy gives the oracle's bytes; at the checkpoints the tables (after
+    sync()), refcounts, free list, counters and stats equal the recorded
+    ones."""
+    from agentkv_b200.agents import DeviceAgents
+
+    g, spec = _golden(golden_dir)
+    N_, bs, L, H, D, dt = W.LLAMA3_70B_GEOMETRY
+    meta = AgentKVPool(config=PoolConfig(total_blocks=N_, block_size=bs, num_layers=L, num_kv_heads=H,
+                                         head_dim=D, dtype=dt, device="meta"))
+    api = PoolReActAPI(meta)
+    root, agents = W.react_setup(api, spec)
+    dev_agents = DeviceAgents(meta, root, agents)
+    dev = torch.device("cuda", 0)
+    slice_pool = torch.empty((N_, 1, 2, 1, bs, 32), dtype=torch.bfloat16, device=dev)
+    host = _seeded_bytes(slice_pool, 14)
+    copier = ShardedCopier(slice_pool)
+    so = g["step_off"]
+    trace = W.react_trace(spec)
+    for i0 in range(0, spec.steps, per_launch):
+        chunk = trace[i0:i0 + per_launch]
+        buf = dev_agents.steps(chunk, pairs_cap=spec.agents)
+        for j in range(len(chunk)):
+            i = i0 + j
+            copier.copy_batch(buf[j])
+            want = g["pairs"][so[i]:so[i + 1]]
+            np.testing.assert_array_equal(DeviceAgents.pairs_of(buf, j), want, err_msg=f"step {i}")
+            O.copy_blocks(host, host.shape[1], want)
+        dev_agents.check()
+        for j in range(len(chunk)):
+            k = f"s{i0 + j + 1}"
+            if k + "_ref" in g.files:
+                assert j == len(chunk) - 1, "checkpoints fall on launch boundaries"
+                handles = dev_agents.sync()
+                tables = np.concatenate([np.asarray(meta.get_block_ids(h), np.int32) for h in handles])
+                np.testing.assert_array_equal(tables, g[k + "_tables"], err_msg=k)
+                np.testing.assert_array_equal(meta._allocator._ref_counts.cpu().numpy(), g[k + "_ref"])
+                np.testing.assert_array_equal(meta._allocator.free_list(), g[k + "_free"])
+                st, want = meta.stats(), json.loads(str(g[k + "_stats"]))
+                for key in ("free_blocks", "allocated_blocks", "peak_allocated", "total_allocs", "total_frees",
+                            "epoch", "active_handles", "shared_nodes", "shared_blocks"):
+                    assert st[key] == want[key], (k, key)
+    torch.cuda.synchronize()
+    assert np.array_equal(slice_pool.view(torch.uint8).reshape(N_, -1).cpu().numpy(), host)
