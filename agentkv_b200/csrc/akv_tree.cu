@@ -154,6 +154,10 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
     bool range_end = false;     // the hops reach past b < L
     int32_t my_child = -1, my_len = 0;
     int64_t my_d = 0;
+    // the hop's edge range when it came from a run (loaded beside the query
+    // tokens of that run, so the verify phase need not wait for it)
+    int64_t my_off = -1;
+    int32_t my_elen = -1;
     while (n < kSegment) {
       if (d >= L) {
         last_segment = true;
@@ -170,14 +174,17 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
       // first token — what the hash lookup of that hop would have decided.
       const int32_t rp = (runs != nullptr && node < tree.run_nodes) ? __ldg(&tree.run_head[node]) : -1;
       if (rp >= 0) {
-        const int32_t rem = rp < tree.n_runs ? __ldg(&runs[rp]).w : 0;
+        // The run's next 32 entries in one load (each lane one; those past
+        // the array's end read nothing), the run length from the first.
+        int4 e = make_int4(-1, 0, 0, 0);
+        if (static_cast<int64_t>(rp) + lane < tree.n_runs) e = __ldg(&runs[rp + lane]);
+        const int32_t rem = __shfl_sync(kFull, e.w, 0);
         if (rem < 1 || static_cast<int64_t>(rp) + rem > tree.n_runs) {
           if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, node, rp);
           return MatchStop{0, 0, -1};
         }
         const int k = rem < kSegment - n ? rem : kSegment - n;
-        int4 e = make_int4(-1, 0, 0, 0);
-        if (lane < k) e = __ldg(&runs[rp + lane]);
+        if (lane >= k) e = make_int4(-1, 0, 0, 0);
         const uint32_t malformed =
             __ballot_sync(kFull, lane < k && (e.x < 0 || e.x >= tree.n_nodes || e.z < 0));
         if (malformed) {
@@ -193,6 +200,13 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
         const int64_t di = d + incl - (lane < k ? e.z : 0);  // depth where entry `lane` starts
         int32_t qt = 0;
         if (lane < k && di < L) qt = Q[di];
+        // independent of the query token above: both loads are in flight at once
+        int64_t e_off = -1;
+        int32_t e_len = -1;
+        if (lane < k) {
+          e_off = __ldg(&tree.node_edge_off[e.x]);
+          e_len = __ldg(&tree.node_edge_len[e.x]);
+        }
         const uint32_t pass = __ballot_sync(kFull, lane < k && di < L && qt == e.y);
         const uint32_t in_run = k == 32 ? kFull : ((1u << k) - 1u);
         const uint32_t fail = ~pass & in_run;
@@ -210,10 +224,14 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
         const int32_t c_s = __shfl_sync(kFull, e.x, src);
         const int32_t l_s = __shfl_sync(kFull, e.z, src);
         const int64_t d_s = __shfl_sync(kFull, di, src);
+        const int64_t o_s = __shfl_sync(kFull, e_off, src);
+        const int32_t el_s = __shfl_sync(kFull, e_len, src);
         if (lane >= n && lane < n + taken) {
           my_child = c_s;
           my_len = l_s;
           my_d = d_s;
+          my_off = o_s;
+          my_elen = el_s;
         }
         if (taken > 0) {
           node = __shfl_sync(kFull, e.x, taken - 1);
@@ -241,6 +259,7 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
         my_child = child;
         my_len = clen;
         my_d = d;
+        my_off = -1;  // read at the verify phase
       }
       ++n;
       if (clen == 0 || d + clen > L) {  // empty edge / edge past the query end: the walk ends here
@@ -255,12 +274,13 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
       return MatchStop{2 * matched, matched, cur};
     }
     // ── verify ──
-    int64_t my_off = 0;
     bool my_bad = false;
     if (lane < n) {
-      my_off = tree.node_edge_off[my_child];
-      my_bad = my_off < 0 || my_off + my_len > tree.n_tokens ||
-               tree.node_edge_len[my_child] != my_len;
+      if (my_off < 0) {  // a hop found by a hash probe
+        my_off = tree.node_edge_off[my_child];
+        my_elen = tree.node_edge_len[my_child];
+      }
+      my_bad = my_off < 0 || my_off + my_len > tree.n_tokens || my_elen != my_len;
     }
     const uint32_t badm = __ballot_sync(kFull, my_bad);
     if (badm) {
