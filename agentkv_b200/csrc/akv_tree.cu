@@ -145,6 +145,12 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
 
   int32_t cur = 0;  // ROOT_NODE_ID
   int64_t matched = 0;
+  // When a segment ends at its 32nd hop inside a unary chain, the next
+  // segment's run is the next consecutive entries of the same run (a run
+  // starting inside a chain is a suffix of it): its entries are fetched
+  // before this segment's verify rounds and land while they run.
+  int32_t carry_rp = -1;
+  int4 carry_e = make_int4(-1, 0, 0, 0);
   while (true) {
     // ── chase ──
     int n = 0;
@@ -172,12 +178,19 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
       // entry), their depths from a prefix sum of the edge lengths, and each
       // hop is taken only if the query's token at its depth is the entry's
       // first token — what the hash lookup of that hop would have decided.
-      const int32_t rp = (runs != nullptr && node < tree.run_nodes) ? __ldg(&tree.run_head[node]) : -1;
-      if (rp >= 0) {
+      int32_t rp = -1;
+      int4 e = make_int4(-1, 0, 0, 0);
+      if (carry_rp >= 0 && n == 0) {  // fetched at the end of the previous segment
+        rp = carry_rp;
+        e = carry_e;
+      } else if (runs != nullptr && node < tree.run_nodes) {
+        rp = __ldg(&tree.run_head[node]);
         // The run's next 32 entries in one load (each lane one; those past
         // the array's end read nothing), the run length from the first.
-        int4 e = make_int4(-1, 0, 0, 0);
-        if (static_cast<int64_t>(rp) + lane < tree.n_runs) e = __ldg(&runs[rp + lane]);
+        if (rp >= 0 && static_cast<int64_t>(rp) + lane < tree.n_runs) e = __ldg(&runs[rp + lane]);
+      }
+      carry_rp = -1;
+      if (rp >= 0) {
         const int32_t rem = __shfl_sync(kFull, e.w, 0);
         if (rem < 1 || static_cast<int64_t>(rp) + rem > tree.n_runs) {
           if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, node, rp);
@@ -241,6 +254,11 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
         if (stop) {
           last_segment = true;
           break;
+        }
+        if (n == kSegment && taken == k && rem > k) {  // the chain goes on past this segment
+          carry_rp = rp + k;
+          carry_e = make_int4(-1, 0, 0, 0);
+          if (static_cast<int64_t>(carry_rp) + lane < tree.n_runs) carry_e = __ldg(&runs[carry_rp + lane]);
         }
         continue;
       }
@@ -412,8 +430,10 @@ AKV_DEV void match_write(const MatchStop& s, int32_t q, int32_t block_size, int3
 // One warp per query (the whole query is one range).  `order` (optional)
 // lists the queries longest first, so the long walks start early and spread
 // over the SMs.
+// At most 72 registers: 7 CTAs (28 warps) per SM, so a 4,096-query batch is
+// one wave.
 template <int kVerifyChunks, bool kPipelined>
-__global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
+__global__ void __launch_bounds__(kMatchWarpsPerCta * 32, 7)
 k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
         int32_t nq, int32_t block_size, int32_t* __restrict__ out_node,
         int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared,
