@@ -61,6 +61,11 @@ enum : int {
 // of batch positions, so that CTA order is batch order.
 constexpr int kDecThreads = 256;
 constexpr int kDecMaxCtas = 2 * kAkvSMs * 2;  // 592
+// Inc_ref / dec_ref batches of at most kSmallBatch ids run as one CTA of
+// kSmallThreads in a single launch (instead of two / four launches over the
+// grid): the per-call API's batches are a handful of ids.
+constexpr int kSmallThreads = 512;
+constexpr int32_t kSmallBatch = 2048;
 // The CoW planner runs in one CTA over at most this many requests per launch.
 constexpr int kCowThreads = 1024;
 constexpr int kCowChunk = 4096;
@@ -203,28 +208,34 @@ __global__ void k_alloc(AkvAllocState st, int32_t n, int32_t* __restrict__ out, 
 }
 
 // ── inc_ref ────────────────────────────────────────────────────────────────
-__global__ void k_incref_check(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n,
-                               AkvStatus* status) {
-  if (akv_failed(status)) return;
-  for (int32_t k = blockIdx.x * blockDim.x + threadIdx.x; k < n; k += gridDim.x * blockDim.x) {
+// Validation of ids [cta*blockDim + tid, n) strided over n_ctas CTAs; returns
+// true when this thread found a bad id.
+AKV_DEV bool incref_check_body(const AkvAllocState& st, const int32_t* __restrict__ ids, int32_t n,
+                               int32_t cta, int32_t n_ctas, AkvStatus* status) {
+  bool bad = false;
+  for (int32_t k = cta * blockDim.x + threadIdx.x; k < n; k += n_ctas * blockDim.x) {
     const int32_t x = ids[k];
     if (static_cast<uint32_t>(x) >= static_cast<uint32_t>(st.total_blocks)) {
       akv_fail(status, AKV_ERR_OUT_OF_RANGE, k, x, st.total_blocks);
+      bad = true;
       continue;
     }
     const int32_t r = st.ref_counts[x];
-    if (r <= 0) akv_fail(status, AKV_ERR_NOT_ALLOCATED, k, x, r);
+    if (r <= 0) {
+      akv_fail(status, AKV_ERR_NOT_ALLOCATED, k, x, r);
+      bad = true;
+    }
   }
+  return bad;
 }
 
-__global__ void k_incref_apply(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n,
-                               AkvTick tk, AkvStatus* status) {
-  if (akv_failed(status)) return;
-  int64_t* ctl = st.ctl;
+// The increments and the drain of the deferred ids, strided over n_ctas CTAs
+// (the cursors are read by every thread before any CTA moves them).
+AKV_DEV void incref_apply_body(const AkvAllocState& st, const int32_t* __restrict__ ids, int32_t n,
+                               int64_t left, int64_t head, int64_t d, int32_t cta, int32_t n_ctas) {
   const int64_t N = st.total_blocks;
-  const int64_t left = ctl[C_LEFT], head = ctl[C_HEAD], d = ctl[C_REL] - head;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(n_ctas) * blockDim.x;
+  const int64_t tid = cta * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   // Warp-aggregated increments: lanes holding the same id add their count
   // with one atomic (a fork increments every inherited block once per child,
   // so a batch repeats ids; the fan-out planner lists them so that equal ids
@@ -238,25 +249,68 @@ __global__ void k_incref_apply(AkvAllocState st, const int32_t* __restrict__ ids
   }
   for (int64_t j = tid; j < d; j += stride)
     st.free_ring[wrap(left - d + j, N)] = st.limbo_ids[wrap(head + j, N)];
-  if (last_cta(ctl) && threadIdx.x == 0) {
-    ctl[C_LEFT] = wrap(left - d, N);
-    ctl[C_SIZE] += d;
-    ctl[C_HEAD] = head + d;
-    apply_ticks(ctl, n, tk);
-  }
+}
+
+AKV_DEV void incref_finish(int64_t* ctl, int32_t n, int64_t left, int64_t head, int64_t d, int64_t N,
+                           const AkvTick& tk) {
+  ctl[C_LEFT] = wrap(left - d, N);
+  ctl[C_SIZE] += d;
+  ctl[C_HEAD] = head + d;
+  apply_ticks(ctl, n, tk);
+}
+
+__global__ void k_incref_check(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n,
+                               AkvStatus* status) {
+  if (akv_failed(status)) return;
+  incref_check_body(st, ids, n, blockIdx.x, gridDim.x, status);
+}
+
+__global__ void k_incref_apply(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n,
+                               AkvTick tk, AkvStatus* status) {
+  if (akv_failed(status)) return;
+  int64_t* ctl = st.ctl;
+  const int64_t left = ctl[C_LEFT], head = ctl[C_HEAD], d = ctl[C_REL] - head;
+  incref_apply_body(st, ids, n, left, head, d, blockIdx.x, gridDim.x);
+  if (last_cta(ctl) && threadIdx.x == 0) incref_finish(ctl, n, left, head, d, st.total_blocks, tk);
+}
+
+// Batches of at most kSmallBatch ids: check and apply in one CTA, one launch.
+__global__ void __launch_bounds__(kSmallThreads)
+k_incref_small(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n, AkvTick tk,
+               AkvStatus* status) {
+  if (akv_failed(status)) return;
+  const bool bad = incref_check_body(st, ids, n, 0, 1, status);
+  if (__syncthreads_or(bad)) return;
+  int64_t* ctl = st.ctl;
+  const int64_t left = ctl[C_LEFT], head = ctl[C_HEAD], d = ctl[C_REL] - head;
+  incref_apply_body(st, ids, n, left, head, d, 0, 1);
+  __syncthreads();  // every thread has read the cursors
+  if (threadIdx.x == 0) incref_finish(ctl, n, left, head, d, st.total_blocks, tk);
 }
 
 // ── dec_ref ────────────────────────────────────────────────────────────────
-// K1: per-id occurrence count and last position (1-based).
-__global__ void k_dec_count(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n,
-                            AkvStatus* status) {
-  if (akv_failed(status)) return;
-  // Warp-aggregated: lanes holding the same id add their count with one
-  // atomic, and the highest of them (the latest position) sets the last
-  // position.  The loop is warp-uniform (blockDim.x is a multiple of 32).
+// Layout of the plan that the dec_ref stages share (in the aux words of the
+// allocator's scratch, or in shared memory for the single-CTA form).
+struct DecPlan {
+  int64_t left_new;     // ring index of the new leftmost free id
+  int64_t n_ret;        // retirements in this batch
+  int64_t z;            // 1 when position 0 retires (no-reader case)
+  int64_t d;            // deferred ids drained at tick 0
+  int64_t head;         // limbo head before the batch
+  int64_t tail;         // limbo tail before the batch
+  int64_t epoch0, ops0;
+  int32_t readers, allowed;
+};
+
+// Stage 1: per-id occurrence count and last position (1-based), strided over
+// n_ctas CTAs.  Warp-aggregated: lanes holding the same id add their count
+// with one atomic, and the highest of them (the latest position) sets the
+// last position.  The loop is warp-uniform (blockDim.x is a multiple of 32).
+AKV_DEV void dec_count_body(const AkvAllocState& st, const int32_t* __restrict__ ids, int32_t n,
+                            int32_t cta, int32_t n_ctas, AkvStatus* status) {
   const int lane = threadIdx.x & 31;
-  const int32_t stride = gridDim.x * blockDim.x;
-  for (int32_t k0 = blockIdx.x * blockDim.x + threadIdx.x - lane; k0 < n; k0 += stride) {
+  const int32_t stride = n_ctas * blockDim.x;
+  for (int32_t k0 = cta * blockDim.x + threadIdx.x - lane; k0 < n; k0 += stride) {
     const int32_t k = k0 + lane;
     int32_t x = k < n ? ids[k] : -1;
     if (k < n && static_cast<uint32_t>(x) >= static_cast<uint32_t>(st.total_blocks)) {
@@ -271,25 +325,10 @@ __global__ void k_dec_count(AkvAllocState st, const int32_t* __restrict__ ids, i
   }
 }
 
-// Layout of the aux words the dec_ref kernels share (int64 view of limbo
-// space is not used; aux lives in scratch_last beyond N? no — in `aux`).
-struct DecPlan {
-  int64_t left_new;     // ring index of the new leftmost free id
-  int64_t n_ret;        // retirements in this batch
-  int64_t z;            // 1 when position 0 retires (no-reader case)
-  int64_t d;            // deferred ids drained at tick 0
-  int64_t head;         // limbo head before the batch
-  int64_t tail;         // limbo tail before the batch
-  int64_t epoch0, ops0;
-  int32_t readers, allowed;
-};
-
-// K2: validate at last occurrences, count retirements per CTA.
-__global__ void __launch_bounds__(kDecThreads)
-k_dec_flag(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n, int32_t chunk,
-           int32_t* __restrict__ cta_counts, AkvStatus* status) {
-  const int32_t lo = blockIdx.x * chunk;
-  const int32_t hi = min(n, lo + chunk);
+// Stage 2: validate positions [lo, hi) at last occurrences; returns the
+// retirements among them (to every thread).
+AKV_DEV int dec_flag_body(const AkvAllocState& st, const int32_t* __restrict__ ids, int32_t lo,
+                          int32_t hi, AkvStatus* status, int* ws) {
   int local = 0;
   if (!akv_failed(status)) {
     for (int32_t k = lo + threadIdx.x; k < hi; k += blockDim.x) {
@@ -304,39 +343,17 @@ k_dec_flag(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n, int32_t
       local += (c == r);
     }
   }
-  __shared__ int ws[32];
   int total;
   block_exclusive_scan(local, ws, total);
-  if (threadIdx.x == 0) cta_counts[blockIdx.x] = total;
+  return total;
 }
 
-// K3: one CTA — offsets per CTA, new cursors, plan for K4.
-__global__ void k_dec_plan(AkvAllocState st, int32_t n, int32_t n_ctas, int32_t* __restrict__ cta_counts,
-                           const int32_t* __restrict__ ids, DecPlan* plan, AkvTick tk,
-                           AkvStatus* status) {
-  __shared__ int ws[32];
-  __shared__ int64_t carry;
-  if (threadIdx.x == 0) carry = 0;
-  __syncthreads();
-  // Exclusive scan of cta_counts in place (n_ctas <= kDecMaxCtas).
-  for (int base = 0; base < n_ctas; base += blockDim.x) {
-    const int i = base + threadIdx.x;
-    const int v = i < n_ctas ? cta_counts[i] : 0;
-    int total;
-    const int ex = block_exclusive_scan(v, ws, total);
-    if (i < n_ctas) cta_counts[i] = static_cast<int>(carry) + ex;
-    __syncthreads();
-    if (threadIdx.x == 0) carry += total;
-    __syncthreads();
-  }
-  if (threadIdx.x != 0) return;
-  if (akv_failed(status)) {
-    plan->n_ret = -1;  // K4 only clears scratch
-    return;
-  }
+// Stage 3 (one thread): the new cursors and the plan for stage 4, given the
+// batch's n_ret retirements.
+AKV_DEV DecPlan dec_plan_body(const AkvAllocState& st, int32_t n, int64_t n_ret,
+                              const int32_t* __restrict__ ids, const AkvTick& tk) {
   int64_t* ctl = st.ctl;
   const int64_t N = st.total_blocks;
-  const int64_t n_ret = carry;
   const int64_t left = ctl[C_LEFT], f = ctl[C_SIZE];
   const int64_t head = ctl[C_HEAD], rel = ctl[C_REL], tail = ctl[C_TAIL];
   const int64_t d = rel - head;
@@ -376,21 +393,19 @@ __global__ void k_dec_plan(AkvAllocState st, int32_t n, int32_t n_ctas, int32_t*
   apply_ticks(ctl, n, tk);
   ctl[C_FREES] += n_ret;
   ctl[C_LAST_RETIRED] = n_ret;
-  *plan = p;
+  return p;
 }
 
-// K4: place retirements, apply refcounts, drain deferred, clear scratch.
-__global__ void __launch_bounds__(kDecThreads)
-k_dec_apply(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n, int32_t chunk,
-            const int32_t* __restrict__ cta_offsets, const DecPlan* __restrict__ plan_p,
-            int32_t* __restrict__ retired_out, AkvTick tk) {
-  const DecPlan p = *plan_p;
+// Stage 4: place the retirements of positions [lo, hi) (numbered from
+// q_base in batch order), apply the refcounts, clear the scratch; then drain
+// the deferred ids, strided over n_ctas CTAs.  n_ret < 0 (an error) only
+// clears the scratch.
+AKV_DEV void dec_apply_body(const AkvAllocState& st, const int32_t* __restrict__ ids, int32_t lo,
+                            int32_t hi, int64_t q_base, const DecPlan& p,
+                            int32_t* __restrict__ retired_out, const AkvTick& tk, int32_t cta,
+                            int32_t n_ctas, int* ws) {
   const int64_t N = st.total_blocks;
   const bool apply = p.n_ret >= 0;
-  const int32_t lo = blockIdx.x * chunk;
-  const int32_t hi = min(n, lo + chunk);
-  __shared__ int ws[32];
-  int64_t q_base = apply ? cta_offsets[blockIdx.x] : 0;
   for (int32_t base = lo; base < hi; base += blockDim.x) {
     const int32_t k = base + threadIdx.x;
     int32_t x = -1, c = 0, r = 0;
@@ -434,9 +449,88 @@ k_dec_apply(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n, int32_
   // op 0, left of op 0's own retirement (no-reader case); at the far left when
   // readers keep new retirements pending.
   const int64_t dstart = p.readers ? 0 : (p.n_ret - p.z);
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < p.d; j += stride)
+  const int64_t stride = static_cast<int64_t>(n_ctas) * blockDim.x;
+  for (int64_t j = cta * static_cast<int64_t>(blockDim.x) + threadIdx.x; j < p.d; j += stride)
     st.free_ring[wrap(p.left_new + dstart + j, N)] = st.limbo_ids[wrap(p.head + j, N)];
+}
+
+// K1: count.
+__global__ void k_dec_count(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n,
+                            AkvStatus* status) {
+  if (akv_failed(status)) return;
+  dec_count_body(st, ids, n, blockIdx.x, gridDim.x, status);
+}
+
+// K2: validate at last occurrences, count retirements per CTA.
+__global__ void __launch_bounds__(kDecThreads)
+k_dec_flag(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n, int32_t chunk,
+           int32_t* __restrict__ cta_counts, AkvStatus* status) {
+  const int32_t lo = blockIdx.x * chunk;
+  const int32_t hi = min(n, lo + chunk);
+  __shared__ int ws[32];
+  const int total = dec_flag_body(st, ids, lo, hi, status, ws);
+  if (threadIdx.x == 0) cta_counts[blockIdx.x] = total;
+}
+
+// K3: one CTA — offsets per CTA, new cursors, plan for K4.
+__global__ void k_dec_plan(AkvAllocState st, int32_t n, int32_t n_ctas, int32_t* __restrict__ cta_counts,
+                           const int32_t* __restrict__ ids, DecPlan* plan, AkvTick tk,
+                           AkvStatus* status) {
+  __shared__ int ws[32];
+  __shared__ int64_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  // Exclusive scan of cta_counts in place (n_ctas <= kDecMaxCtas).
+  for (int base = 0; base < n_ctas; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const int v = i < n_ctas ? cta_counts[i] : 0;
+    int total;
+    const int ex = block_exclusive_scan(v, ws, total);
+    if (i < n_ctas) cta_counts[i] = static_cast<int>(carry) + ex;
+    __syncthreads();
+    if (threadIdx.x == 0) carry += total;
+    __syncthreads();
+  }
+  if (threadIdx.x != 0) return;
+  if (akv_failed(status)) {
+    plan->n_ret = -1;  // K4 only clears scratch
+    return;
+  }
+  *plan = dec_plan_body(st, n, carry, ids, tk);
+}
+
+// K4: place retirements, apply refcounts, drain deferred, clear scratch.
+__global__ void __launch_bounds__(kDecThreads)
+k_dec_apply(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n, int32_t chunk,
+            const int32_t* __restrict__ cta_offsets, const DecPlan* __restrict__ plan_p,
+            int32_t* __restrict__ retired_out, AkvTick tk) {
+  const DecPlan p = *plan_p;
+  const int32_t lo = blockIdx.x * chunk;
+  const int32_t hi = min(n, lo + chunk);
+  __shared__ int ws[32];
+  const int64_t q_base = p.n_ret >= 0 ? cta_offsets[blockIdx.x] : 0;
+  dec_apply_body(st, ids, lo, hi, q_base, p, retired_out, tk, blockIdx.x, gridDim.x, ws);
+}
+
+// Batches of at most kSmallBatch ids: the four stages in one CTA, one launch.
+// __syncthreads between the stages makes each stage's global writes (the
+// scratch atomics, the cursors) visible to the next.
+__global__ void __launch_bounds__(kSmallThreads)
+k_dec_small(AkvAllocState st, const int32_t* __restrict__ ids, int32_t n,
+            int32_t* __restrict__ retired_out, AkvTick tk, AkvStatus* status) {
+  __shared__ int ws[32];
+  __shared__ DecPlan plan;
+  if (akv_failed(status)) return;  // nothing counted, nothing to clear
+  dec_count_body(st, ids, n, 0, 1, status);
+  __syncthreads();
+  const int n_ret = dec_flag_body(st, ids, 0, n, status, ws);
+  if (threadIdx.x == 0) {
+    if (akv_failed(status)) plan.n_ret = -1;  // stage 4 only clears scratch
+    else plan = dec_plan_body(st, n, n_ret, ids, tk);
+  }
+  __syncthreads();
+  const DecPlan p = plan;
+  dec_apply_body(st, ids, 0, n, 0, p, retired_out, tk, 0, 1, ws);
 }
 
 // ── reclaimer ──────────────────────────────────────────────────────────────
@@ -619,6 +713,8 @@ int akv_alloc_prepare() {
   AKV_LOAD(k_dec_flag);
   AKV_LOAD(k_dec_plan);
   AKV_LOAD(k_dec_apply);
+  AKV_LOAD(k_incref_small);
+  AKV_LOAD(k_dec_small);
   AKV_LOAD(k_release);
   AKV_LOAD(k_advance);
   AKV_LOAD(k_cow_plan);
@@ -661,6 +757,11 @@ extern "C" int akv_incref_batch(const AkvAllocState* st, const int32_t* ids, int
   if (n == 0) return AKV_OK;
   AKV_ARG_CHECK(ids != nullptr, "akv_incref_batch: ids is NULL");
   cudaStream_t s = akv_stream(stream);
+  if (n <= kSmallBatch) {
+    k_incref_small<<<1, kSmallThreads, 0, s>>>(*st, ids, n, *tick, status);
+    AKV_LAUNCH_CHECK("akv_incref_batch(small)");
+    return AKV_OK;
+  }
   const int g = grid_for(n, 256, kAkvSMs * 4);
   k_incref_check<<<g, 256, 0, s>>>(*st, ids, n, status);
   AKV_LAUNCH_CHECK("akv_incref_batch(check)");
@@ -679,6 +780,11 @@ extern "C" int akv_decref_batch(const AkvAllocState* st, const int32_t* ids, int
   if (n == 0) return AKV_OK;
   AKV_ARG_CHECK(ids != nullptr, "akv_decref_batch: ids is NULL");
   cudaStream_t s = akv_stream(stream);
+  if (n <= kSmallBatch) {
+    k_dec_small<<<1, kSmallThreads, 0, s>>>(*st, ids, n, retired_out, *tick, status);
+    AKV_LAUNCH_CHECK("akv_decref_batch(small)");
+    return AKV_OK;
+  }
   const int n_ctas = grid_for(n, kDecThreads, kDecMaxCtas);
   const int32_t chunk = akv_ceil_div(n, n_ctas);
   int32_t* cta_counts = st->scratch_aux;
@@ -810,6 +916,11 @@ extern "C" int akv_decref_batch_noalloc(const AkvAllocState* st, const int32_t* 
   cudaError_t e = cudaMemsetAsync(s2.scratch_count, 0, bytes, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(s2.scratch_last, 0, bytes, s);
   if (e != cudaSuccess) return akv_cuda_fail(e, "akv_decref_batch_noalloc: clear scratch");
+  if (n <= kSmallBatch) {
+    k_dec_small<<<1, kSmallThreads, 0, s>>>(s2, ids, n, retired_out, *tick, status);
+    AKV_LAUNCH_CHECK("akv_decref_batch_noalloc(small)");
+    return AKV_OK;
+  }
   const int n_ctas = grid_for(n, kDecThreads, kDecMaxCtas);
   const int32_t chunk = akv_ceil_div(n, n_ctas);
   int32_t* cta_counts = s2.scratch_aux;

@@ -217,6 +217,52 @@ def test_large_decref_batch_ordering():
     assert_same_as_oracle(a, o, "after large batch")
 
 
+@pytest.mark.parametrize("readers", [False, True])
+def test_single_cta_and_grid_batches_agree(readers):
+    """inc_ref / dec_ref batches of up to 2,048 ids run as one single-CTA
+    launch, longer ones over the grid: batches on both sides of that size
+    (with repeated ids, a deferred drain, an open read section, and a
+    double free on each side) leave the state the oracle's batches leave."""
+    n = 6000
+    rng = np.random.default_rng(21 + readers)
+    a = make_alloc(n, interval=5)
+    o = O.OracleAllocator(n, 5)
+    np.testing.assert_array_equal(a.alloc_batch(n).cpu().numpy(), o.alloc_batch(n))
+    if readers:
+        assert a.enter_read_section() == o.enter_read_section()
+    for size in (1, 2047, 2048, 2049, 5000):
+        ids = rng.integers(0, n, size=size).astype(np.int32)
+        a.inc_ref_batch(ids)
+        o.inc_ref_batch(ids)
+        a.check()
+        assert_same_as_oracle(a, o, f"inc {size}")
+        refs = o.state()["ref_counts"]
+        uniq = np.unique(ids)[: max(1, size // 3)]
+        decs = np.repeat(uniq, refs[uniq]).astype(np.int32)  # every listed block retires
+        rng.shuffle(decs)
+        out = torch.full((len(decs),), -7, dtype=torch.int32, device=a.device)
+        a.dec_ref_batch(decs, retired_out=out)
+        want = o.dec_ref_batch(decs)
+        a.check()
+        np.testing.assert_array_equal(out[: len(want)].cpu().numpy(), want)
+        assert_same_as_oracle(a, o, f"dec {size}")
+        a.maybe_advance_epoch()
+        o.maybe_advance_epoch()
+        # top the pool up again so the next size has live blocks to reference
+        free = len(o.state()["free_list"])
+        np.testing.assert_array_equal(a.alloc_batch(free).cpu().numpy(), o.alloc_batch(free))
+    for size in (100, 3000):  # one id too many: the whole batch is refused
+        live = np.flatnonzero(o.state()["ref_counts"] > 0)[:size]
+        decs = np.repeat(live, o.state()["ref_counts"][live]).astype(np.int32)
+        decs = np.append(decs, live[0])
+        with pytest.raises(O.OracleError):
+            o.dec_ref_batch(decs)
+        a.dec_ref_batch(decs)
+        with pytest.raises(ValueError, match="double-free"):
+            a.check()
+        assert_same_as_oracle(a, o, f"refused dec {size}")
+
+
 @pytest.mark.parametrize("seed", range(5))
 def test_cow_batch_matches_oracle(seed):
     rng = np.random.default_rng(seed)
