@@ -231,15 +231,16 @@ def test_single_cta_and_grid_batches_agree(readers):
     if readers:
         assert a.enter_read_section() == o.enter_read_section()
     for size in (1, 2047, 2048, 2049, 5000):
-        ids = rng.integers(0, n, size=size).astype(np.int32)
+        live = np.flatnonzero(o.state()["ref_counts"] > 0)
+        ids = rng.choice(live, size=size).astype(np.int32)
         a.inc_ref_batch(ids)
         o.inc_ref_batch(ids)
         a.check()
         assert_same_as_oracle(a, o, f"inc {size}")
         refs = o.state()["ref_counts"]
-        uniq = np.unique(ids)[: max(1, size // 3)]
-        decs = np.repeat(uniq, refs[uniq]).astype(np.int32)  # every listed block retires
+        decs = np.repeat(np.unique(ids), refs[np.unique(ids)]).astype(np.int32)
         rng.shuffle(decs)
+        decs = decs[:size]  # `size` ids: blocks listed ref_count times retire, the rest drop a count
         out = torch.full((len(decs),), -7, dtype=torch.int32, device=a.device)
         a.dec_ref_batch(decs, retired_out=out)
         want = o.dec_ref_batch(decs)
