@@ -182,6 +182,11 @@ SIGNATURES = {
         C.c_int,
         [C.POINTER(AkvTreeView), _P, _P, _I32, _I32, _P, _P, _P, _P, _P, _I32, _I32, _P, _I64, _I32, _P, _P],
     ),
+    "akv_match_staged_scratch_bytes": (C.c_int64, [_I32, _I64, _I32]),
+    "akv_match_prefix_staged": (
+        C.c_int,
+        [C.POINTER(AkvTreeView), _P, _P, _I32, _I64, _I32, _P, _P, _P, _P, _I32, _P, _I64, _P, _P],
+    ),
 }
 
 

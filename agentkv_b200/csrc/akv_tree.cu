@@ -90,6 +90,206 @@ struct MatchStop {
 };
 constexpr int64_t kNoStop = INT64_MAX;  // the range ends before the walk does
 
+// The query's tokens around the chase's position, for the hash-probe hops:
+// a 256-token window held in registers (8 per lane), reloaded when the
+// position leaves it.  Positions are warp-uniform and < L.
+struct QueryWindow {
+  const int32_t* __restrict__ Q;
+  int64_t L;
+  int lane;
+  int32_t win[kWinPerLane];
+  int64_t wbase = -(1LL << 40);
+
+  AKV_DEV QueryWindow(const int32_t* q, int64_t l, int ln) : Q(q), L(l), lane(ln) {}
+
+  AKV_DEV int32_t operator()(int64_t pos) {
+    if (pos < wbase || pos >= wbase + 32 * kWinPerLane) {
+      wbase = pos;
+#pragma unroll
+      for (int u = 0; u < kWinPerLane; ++u) {
+        const int64_t i = pos + u * 32 + lane;
+        win[u] = i < L ? Q[i] : 0;
+      }
+    }
+    const int64_t r = pos - wbase;
+    const int u = static_cast<int>(r >> 5);
+    int32_t v = 0;
+#pragma unroll
+    for (int uu = 0; uu < kWinPerLane; ++uu) v = (uu == u) ? win[uu] : v;
+    return __shfl_sync(0xffffffffu, v, static_cast<int>(r & 31));
+  }
+};
+
+// One segment of the chase phase, for one warp: up to 32 hops from `cur` at
+// depth `matched`, using only each edge's first token.  Lane i gets hop i
+// (child, edge length, depth, and the edge's offset and length in the token
+// arena when the hop came from a run, else -1).  The walk stops at a missing
+// child, at the end of the query, at an edge that is empty or runs past the
+// end of the query (taken, then the walk stops), or past b.  Returns false
+// (after recording AKV_ERR_TREE) on a malformed tree.
+struct Chase {
+  int n = 0;                   // hops in this segment
+  int64_t d = 0;               // depth after the last hop
+  int32_t node = 0;            // node after the last hop
+  bool last_segment = false;   // the walk ends with this segment's hops
+  bool range_end = false;      // the hops reach past b < L
+  int32_t my_child = -1, my_len = 0;
+  int64_t my_d = 0;
+  int64_t my_off = -1;         // from a run: the edge's offset (else -1, read later)
+  int32_t my_elen = -1;        // from a run: the edge's length in the node array
+  // When a segment ends at its 32nd hop inside a unary chain, the next
+  // segment's run is the next consecutive entries of the same run (a run
+  // starting inside a chain is a suffix of it): its entries are fetched at
+  // the end of this segment and land while the caller works on its hops.
+  int32_t carry_rp = -1;
+  int4 carry_e = make_int4(-1, 0, 0, 0);
+};
+
+template <typename QToken>
+AKV_DEV bool chase_segment(Chase& c, const AkvTreeView& tree, const int4* __restrict__ slots,
+                           const int4* __restrict__ runs, const int32_t* __restrict__ Q, int64_t L,
+                           int64_t b, int64_t matched, int32_t cur, int32_t q, AkvStatus* st, int lane,
+                           QToken& qtoken) {
+  constexpr uint32_t kFull = 0xffffffffu;
+  int n = 0;
+  int64_t d = matched;
+  int32_t node = cur;
+  c.last_segment = false;
+  c.range_end = false;
+  c.my_child = -1;
+  c.my_len = 0;
+  c.my_d = 0;
+  c.my_off = -1;
+  c.my_elen = -1;
+  while (n < kSegment) {
+    if (d >= L) {
+      c.last_segment = true;
+      break;
+    }
+    if (d >= b) {
+      c.range_end = true;
+      break;
+    }
+    // A node with exactly one child starts a run of its unary chain: up to
+    // 32 hops come from one load of consecutive run entries (each lane one
+    // entry), their depths from a prefix sum of the edge lengths, and each
+    // hop is taken only if the query's token at its depth is the entry's
+    // first token — what the hash lookup of that hop would have decided.
+    int32_t rp = -1;
+    int4 e = make_int4(-1, 0, 0, 0);
+    if (c.carry_rp >= 0 && n == 0) {  // fetched at the end of the previous segment
+      rp = c.carry_rp;
+      e = c.carry_e;
+    } else if (runs != nullptr && node < tree.run_nodes) {
+      rp = __ldg(&tree.run_head[node]);
+      // The run's next 32 entries in one load (each lane one; those past
+      // the array's end read nothing), the run length from the first.
+      if (rp >= 0 && static_cast<int64_t>(rp) + lane < tree.n_runs) e = __ldg(&runs[rp + lane]);
+    }
+    c.carry_rp = -1;
+    if (rp >= 0) {
+      const int32_t rem = __shfl_sync(kFull, e.w, 0);
+      if (rem < 1 || static_cast<int64_t>(rp) + rem > tree.n_runs) {
+        if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, node, rp);
+        return false;
+      }
+      const int k = rem < kSegment - n ? rem : kSegment - n;
+      if (lane >= k) e = make_int4(-1, 0, 0, 0);
+      const uint32_t malformed =
+          __ballot_sync(kFull, lane < k && (e.x < 0 || e.x >= tree.n_nodes || e.z < 0));
+      if (malformed) {
+        if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, node, rp);
+        return false;
+      }
+      int64_t incl = lane < k ? e.z : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t y = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int64_t di = d + incl - (lane < k ? e.z : 0);  // depth where entry `lane` starts
+      int32_t qt = 0;
+      if (lane < k && di < L) qt = Q[di];
+      // independent of the query token above: both loads are in flight at once
+      int64_t e_off = -1;
+      int32_t e_len = -1;
+      if (lane < k) {
+        e_off = __ldg(&tree.node_edge_off[e.x]);
+        e_len = __ldg(&tree.node_edge_len[e.x]);
+      }
+      const uint32_t pass = __ballot_sync(kFull, lane < k && di < L && qt == e.y);
+      const uint32_t in_run = k == 32 ? kFull : ((1u << k) - 1u);
+      const uint32_t fail = ~pass & in_run;
+      const int first_fail = fail ? __ffs(fail) - 1 : k;  // hops [0, first_fail) found their child
+      const uint32_t upto = first_fail == 32 ? kFull : ((1u << first_fail) - 1u);
+      // an empty edge or one running past the query end is taken, then the walk stops
+      const uint32_t stop_m = __ballot_sync(kFull, lane < k && (e.z == 0 || di + e.z > L)) & upto;
+      int taken = first_fail;
+      bool stop = first_fail < k;
+      if (stop_m) {
+        taken = __ffs(stop_m);
+        stop = true;
+      }
+      const int src = (lane - n) & 31;
+      const int32_t c_s = __shfl_sync(kFull, e.x, src);
+      const int32_t l_s = __shfl_sync(kFull, e.z, src);
+      const int64_t d_s = __shfl_sync(kFull, di, src);
+      const int64_t o_s = __shfl_sync(kFull, e_off, src);
+      const int32_t el_s = __shfl_sync(kFull, e_len, src);
+      if (lane >= n && lane < n + taken) {
+        c.my_child = c_s;
+        c.my_len = l_s;
+        c.my_d = d_s;
+        c.my_off = o_s;
+        c.my_elen = el_s;
+      }
+      if (taken > 0) {
+        node = __shfl_sync(kFull, e.x, taken - 1);
+        d = __shfl_sync(kFull, di, taken - 1) + __shfl_sync(kFull, e.z, taken - 1);
+      }
+      n += taken;
+      if (stop) {
+        c.last_segment = true;
+        break;
+      }
+      if (n == kSegment && taken == k && rem > k) {  // the chain goes on past this segment
+        c.carry_rp = rp + k;
+        c.carry_e = make_int4(-1, 0, 0, 0);
+        if (static_cast<int64_t>(c.carry_rp) + lane < tree.n_runs) c.carry_e = __ldg(&runs[c.carry_rp + lane]);
+      }
+      continue;
+    }
+    const int32_t t = qtoken(d);
+    int32_t clen = 0;
+    const int32_t child = warp_lookup(slots, tree.slot_mask, node, t, lane, clen);
+    if (child < 0) {
+      c.last_segment = true;
+      break;
+    }
+    if (child >= tree.n_nodes || clen < 0) {
+      if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, child, tree.n_nodes);
+      return false;
+    }
+    if (lane == n) {
+      c.my_child = child;
+      c.my_len = clen;
+      c.my_d = d;
+      c.my_off = -1;  // read at the verify phase
+    }
+    ++n;
+    if (clen == 0 || d + clen > L) {  // empty edge / edge past the query end: the walk ends here
+      c.last_segment = true;
+      break;
+    }
+    d += clen;
+    node = child;
+  }
+  c.n = n;
+  c.d = d;
+  c.node = node;
+  return true;
+}
+
 // The reference's walk (radix_tree.py:513-570) over query Q[0, L), checked
 // on positions [a, b) only; one warp, all lanes.  The walk alternates two
 // phases:
@@ -124,169 +324,20 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
 
   // (Prefetching the next 256-token window while the current one is chased
   // measured no faster: 0.182 against 0.179 ms per 4,096-query batch.)
-  int32_t win[kWinPerLane];
-  int64_t wbase = -(1LL << 40);
-  auto qtoken = [&](int64_t pos) -> int32_t {  // pos is warp-uniform and < L
-    if (pos < wbase || pos >= wbase + 32 * kWinPerLane) {
-      wbase = pos;
-#pragma unroll
-      for (int u = 0; u < kWinPerLane; ++u) {
-        const int64_t i = pos + u * 32 + lane;
-        win[u] = i < L ? Q[i] : 0;
-      }
-    }
-    const int64_t r = pos - wbase;
-    const int u = static_cast<int>(r >> 5);
-    int32_t v = 0;
-#pragma unroll
-    for (int uu = 0; uu < kWinPerLane; ++uu) v = (uu == u) ? win[uu] : v;
-    return __shfl_sync(kFull, v, static_cast<int>(r & 31));
-  };
+  QueryWindow qtoken{Q, L, lane};
 
   int32_t cur = 0;  // ROOT_NODE_ID
   int64_t matched = 0;
-  // When a segment ends at its 32nd hop inside a unary chain, the next
-  // segment's run is the next consecutive entries of the same run (a run
-  // starting inside a chain is a suffix of it): its entries are fetched
-  // before this segment's verify rounds and land while they run.
-  int32_t carry_rp = -1;
-  int4 carry_e = make_int4(-1, 0, 0, 0);
+  Chase c;
   while (true) {
-    // ── chase ──
-    int n = 0;
-    int64_t d = matched;
-    int32_t node = cur;
-    bool last_segment = false;  // the walk ends with this segment's hops
-    bool range_end = false;     // the hops reach past b < L
-    int32_t my_child = -1, my_len = 0;
-    int64_t my_d = 0;
-    // the hop's edge range when it came from a run (loaded beside the query
-    // tokens of that run, so the verify phase need not wait for it)
-    int64_t my_off = -1;
-    int32_t my_elen = -1;
-    while (n < kSegment) {
-      if (d >= L) {
-        last_segment = true;
-        break;
-      }
-      if (d >= b) {
-        range_end = true;
-        break;
-      }
-      // A node with exactly one child starts a run of its unary chain: up to
-      // 32 hops come from one load of consecutive run entries (each lane one
-      // entry), their depths from a prefix sum of the edge lengths, and each
-      // hop is taken only if the query's token at its depth is the entry's
-      // first token — what the hash lookup of that hop would have decided.
-      int32_t rp = -1;
-      int4 e = make_int4(-1, 0, 0, 0);
-      if (carry_rp >= 0 && n == 0) {  // fetched at the end of the previous segment
-        rp = carry_rp;
-        e = carry_e;
-      } else if (runs != nullptr && node < tree.run_nodes) {
-        rp = __ldg(&tree.run_head[node]);
-        // The run's next 32 entries in one load (each lane one; those past
-        // the array's end read nothing), the run length from the first.
-        if (rp >= 0 && static_cast<int64_t>(rp) + lane < tree.n_runs) e = __ldg(&runs[rp + lane]);
-      }
-      carry_rp = -1;
-      if (rp >= 0) {
-        const int32_t rem = __shfl_sync(kFull, e.w, 0);
-        if (rem < 1 || static_cast<int64_t>(rp) + rem > tree.n_runs) {
-          if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, node, rp);
-          return MatchStop{0, 0, -1};
-        }
-        const int k = rem < kSegment - n ? rem : kSegment - n;
-        if (lane >= k) e = make_int4(-1, 0, 0, 0);
-        const uint32_t malformed =
-            __ballot_sync(kFull, lane < k && (e.x < 0 || e.x >= tree.n_nodes || e.z < 0));
-        if (malformed) {
-          if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, node, rp);
-          return MatchStop{0, 0, -1};
-        }
-        int64_t incl = lane < k ? e.z : 0;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int64_t y = __shfl_up_sync(kFull, incl, o);
-          if (lane >= o) incl += y;
-        }
-        const int64_t di = d + incl - (lane < k ? e.z : 0);  // depth where entry `lane` starts
-        int32_t qt = 0;
-        if (lane < k && di < L) qt = Q[di];
-        // independent of the query token above: both loads are in flight at once
-        int64_t e_off = -1;
-        int32_t e_len = -1;
-        if (lane < k) {
-          e_off = __ldg(&tree.node_edge_off[e.x]);
-          e_len = __ldg(&tree.node_edge_len[e.x]);
-        }
-        const uint32_t pass = __ballot_sync(kFull, lane < k && di < L && qt == e.y);
-        const uint32_t in_run = k == 32 ? kFull : ((1u << k) - 1u);
-        const uint32_t fail = ~pass & in_run;
-        const int first_fail = fail ? __ffs(fail) - 1 : k;  // hops [0, first_fail) found their child
-        const uint32_t upto = first_fail == 32 ? kFull : ((1u << first_fail) - 1u);
-        // an empty edge or one running past the query end is taken, then the walk stops
-        const uint32_t stop_m = __ballot_sync(kFull, lane < k && (e.z == 0 || di + e.z > L)) & upto;
-        int taken = first_fail;
-        bool stop = first_fail < k;
-        if (stop_m) {
-          taken = __ffs(stop_m);
-          stop = true;
-        }
-        const int src = (lane - n) & 31;
-        const int32_t c_s = __shfl_sync(kFull, e.x, src);
-        const int32_t l_s = __shfl_sync(kFull, e.z, src);
-        const int64_t d_s = __shfl_sync(kFull, di, src);
-        const int64_t o_s = __shfl_sync(kFull, e_off, src);
-        const int32_t el_s = __shfl_sync(kFull, e_len, src);
-        if (lane >= n && lane < n + taken) {
-          my_child = c_s;
-          my_len = l_s;
-          my_d = d_s;
-          my_off = o_s;
-          my_elen = el_s;
-        }
-        if (taken > 0) {
-          node = __shfl_sync(kFull, e.x, taken - 1);
-          d = __shfl_sync(kFull, di, taken - 1) + __shfl_sync(kFull, e.z, taken - 1);
-        }
-        n += taken;
-        if (stop) {
-          last_segment = true;
-          break;
-        }
-        if (n == kSegment && taken == k && rem > k) {  // the chain goes on past this segment
-          carry_rp = rp + k;
-          carry_e = make_int4(-1, 0, 0, 0);
-          if (static_cast<int64_t>(carry_rp) + lane < tree.n_runs) carry_e = __ldg(&runs[carry_rp + lane]);
-        }
-        continue;
-      }
-      const int32_t t = qtoken(d);
-      int32_t clen = 0;
-      const int32_t child = warp_lookup(slots, tree.slot_mask, node, t, lane, clen);
-      if (child < 0) {
-        last_segment = true;
-        break;
-      }
-      if (child >= tree.n_nodes || clen < 0) {
-        if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, child, tree.n_nodes);
-        return MatchStop{0, 0, -1};
-      }
-      if (lane == n) {
-        my_child = child;
-        my_len = clen;
-        my_d = d;
-        my_off = -1;  // read at the verify phase
-      }
-      ++n;
-      if (clen == 0 || d + clen > L) {  // empty edge / edge past the query end: the walk ends here
-        last_segment = true;
-        break;
-      }
-      d += clen;
-      node = child;
-    }
+    if (!chase_segment(c, tree, slots, runs, Q, L, b, matched, cur, q, st, lane, qtoken))
+      return MatchStop{0, 0, -1};
+    const int n = c.n;
+    const bool last_segment = c.last_segment, range_end = c.range_end;
+    const int32_t my_child = c.my_child, my_len = c.my_len;
+    const int64_t my_d = c.my_d;
+    int64_t my_off = c.my_off;
+    int32_t my_elen = c.my_elen;
     if (n == 0) {  // a missing child at `matched`, the query's end, or the range's end
       if (range_end) return MatchStop{kNoStop, 0, -1};
       return MatchStop{2 * matched, matched, cur};
@@ -429,11 +480,11 @@ AKV_DEV void match_write(const MatchStop& s, int32_t q, int32_t block_size, int3
 
 // One warp per query (the whole query is one range).  `order` (optional)
 // lists the queries longest first, so the long walks start early and spread
-// over the SMs.
-// At most 72 registers: 7 CTAs (28 warps) per SM, so a 4,096-query batch is
-// one wave.
+// over the SMs.  (Capping the registers at 72, for 7 CTAs per SM and a
+// 4,096-query batch in one wave, measured slower: 0.0737 against 0.0701 ms
+// per batch on the stress tree, with spills.)
 template <int kVerifyChunks, bool kPipelined>
-__global__ void __launch_bounds__(kMatchWarpsPerCta * 32, 7)
+__global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
 k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
         int32_t nq, int32_t block_size, int32_t* __restrict__ out_node,
         int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared,
@@ -569,6 +620,285 @@ k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
     }
     match_write(MatchStop{best, b_matched, b_node}, q, block_size, out_node, out_len, out_compared);
   }
+}
+
+// ── staged lookups: every query chased first, its edges then verified in
+// windows spread over the whole grid ──
+// With one warp per query a batch lasts as long as its longest walk: an
+// 8,192-token query that matches a cached sequence is 32 dependent verify
+// rounds of 256 tokens, while most warps have long finished.  Here the
+// lookup is two launches:
+//  k_match_chase  — one warp per query runs the chase phase alone over the
+//                   whole query (chase_segment: hops decided by each edge's
+//                   first token) and writes its hops and, for every W-token
+//                   window of the chased span [0, D), the hop that holds the
+//                   window's first position;
+//  k_match_verify — one warp per window compares the query's tokens in it
+//                   with the hops' edge tokens.  The first mismatch over all
+//                   windows of a query (an atomic min on position) is the
+//                   reference loop's stop, and the warp that finishes the
+//                   query's last window writes its answer.
+// The answer is the one-warp walk's: the walk stops at the first hop along
+// the chased path that mismatches or only partly fits (only the last hop can
+// partly fit); hops past it are speculation and are discarded.  The chase may
+// run further ahead than the one-warp walk (up to the query's end), so on a
+// malformed tree it can report AKV_ERR_TREE where that walk would not.
+//
+// Scratch (caller-owned, akv_match_staged_scratch_bytes):
+//   hops  int4 [n_tokens]   {child, edge length, depth, edge offset or -1}:
+//                           query q's hops at q_off[q] + h (a query of L
+//                           tokens has at most L hops, as every hop before
+//                           the last takes at least one token)
+//   wins  int4 [n_tokens / W + nq + 1]  {q, hop, window, 1}, or 0 for an
+//                           unused slot: query q's windows from slot
+//                           q_off[q] / W + q (so no prefix sum is needed)
+//   qinfo int4 [nq]         {hops, D, windows, 0}
+//   stop  uint64 [nq]       (position << 32) | hop of the first mismatch
+//   left  int32 [nq]        windows of the query not finished yet
+// Every slot is written by the chase, so the scratch needs no clearing.
+// Token counts and edge offsets must fit in int32 (checked on the host).
+struct StagedScratch {
+  int4* hops;
+  int4* wins;
+  int4* qinfo;
+  unsigned long long* stop;
+  int32_t* left;
+};
+
+AKV_HD int64_t staged_round256(int64_t b) { return (b + 255) / 256 * 256; }
+
+AKV_HD int64_t staged_slots(int32_t nq, int64_t n_tokens, int32_t W) { return n_tokens / W + nq + 1; }
+
+// Carves the scratch at `base` (nullptr: only sizes it); returns its bytes.
+AKV_HD int64_t staged_layout(char* base, int32_t nq, int64_t n_tokens, int32_t W, StagedScratch* sc) {
+  int64_t o = 0;
+  auto take = [&](int64_t bytes) {
+    char* p = base != nullptr ? base + o : nullptr;
+    o += staged_round256(bytes);
+    return p;
+  };
+  char* hops = take(16 * n_tokens);
+  char* wins = take(16 * staged_slots(nq, n_tokens, W));
+  char* qinfo = take(16 * static_cast<int64_t>(nq));
+  char* stop = take(8 * static_cast<int64_t>(nq));
+  char* left = take(4 * static_cast<int64_t>(nq));
+  if (sc != nullptr) {
+    sc->hops = reinterpret_cast<int4*>(hops);
+    sc->wins = reinterpret_cast<int4*>(wins);
+    sc->qinfo = reinterpret_cast<int4*>(qinfo);
+    sc->stop = reinterpret_cast<unsigned long long*>(stop);
+    sc->left = reinterpret_cast<int32_t*>(left);
+  }
+  return o;
+}
+
+constexpr unsigned long long kNoMismatch = ~0ull;
+
+// The answer of query q from its hops, the first mismatch (or kNoMismatch)
+// and the query length.
+AKV_DEV void staged_finish(const int4* __restrict__ hops, int32_t n_hops, int64_t L, unsigned long long stop,
+                           int32_t q, int32_t block_size, int32_t* out_node, int32_t* out_len,
+                           int64_t* out_compared) {
+  MatchStop s{0, 0, 0};  // no hop: nothing matched at the root
+  if (stop != kNoMismatch) {  // the hop holding the first mismatch stops the walk
+    const int64_t P = static_cast<int64_t>(stop >> 32);
+    const int32_t h = static_cast<int32_t>(stop & 0xffffffffu);
+    s = MatchStop{2 * P + 1, hops[h].z, h > 0 ? hops[h - 1].x : 0};
+  } else if (n_hops > 0) {
+    const int4 last = hops[n_hops - 1];
+    const int64_t lim = last.y < L - last.z ? last.y : L - last.z;
+    if (lim < last.y || last.y == 0)  // the last edge only partly fits: the walk stops at its start
+      s = MatchStop{2 * (last.z + lim), last.z, n_hops > 1 ? hops[n_hops - 2].x : 0};
+    else  // every hop matched in full
+      s = MatchStop{2 * (static_cast<int64_t>(last.z) + last.y), static_cast<int64_t>(last.z) + last.y, last.x};
+  }
+  match_write(s, q, block_size, out_node, out_len, out_compared);
+}
+
+template <int kW>
+__global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
+k_match_chase(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
+              int32_t nq, int64_t n_tokens, int32_t block_size, const int32_t* __restrict__ order,
+              StagedScratch sc, int32_t* __restrict__ out_node, int32_t* __restrict__ out_len,
+              int64_t* __restrict__ out_compared, AkvStatus* st) {
+  constexpr uint32_t kFull = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int32_t w = blockIdx.x * kMatchWarpsPerCta + (threadIdx.x >> 5);
+  if (w >= nq) return;
+  const int32_t q = order != nullptr ? order[w] : w;
+  if (static_cast<uint32_t>(q) >= static_cast<uint32_t>(nq)) {
+    if (lane == 0) akv_fail(st, AKV_ERR_INVALID_ARG, w, q, nq);
+    return;
+  }
+  const int64_t qlo = q_off[q], qhi = q_off[q + 1];
+  if (qlo < 0 || qhi < qlo || qhi > n_tokens) {
+    if (lane == 0) akv_fail(st, AKV_ERR_INVALID_ARG, w, q, static_cast<int32_t>(qhi - qlo), qlo);
+    return;
+  }
+  const int64_t L = qhi - qlo;
+  const int32_t* __restrict__ Q = tokens + qlo;
+  const int4* __restrict__ slots = reinterpret_cast<const int4*>(tree.slots);
+  const int4* __restrict__ runs =
+      tree.run_head != nullptr ? reinterpret_cast<const int4*>(tree.run_entries) : nullptr;
+  int4* __restrict__ hops = sc.hops + qlo;
+  int4* __restrict__ wins = sc.wins + (qlo / kW + q);
+  QueryWindow qtoken{Q, L, lane};
+  Chase c;
+  int32_t cur = 0, h = 0;  // node reached, hops written
+  int64_t matched = 0, D = 0;
+  while (true) {
+    if (!chase_segment(c, tree, slots, runs, Q, L, L, matched, cur, q, st, lane, qtoken)) return;
+    const int n = c.n;
+    if (n == 0) break;
+    // a run hop brings its edge's offset and length: check them here (the
+    // verify reads them itself for the other hops)
+    const bool bad = lane < n && c.my_off >= 0 &&
+                     (c.my_off + c.my_len > tree.n_tokens || c.my_elen != c.my_len);
+    const uint32_t badm = __ballot_sync(kFull, bad);
+    if (badm) {
+      if (lane == __ffs(badm) - 1) akv_fail(st, AKV_ERR_TREE, q, c.my_child, c.my_len, c.my_off);
+      return;
+    }
+    const int64_t lim = lane < n ? (c.my_len < L - c.my_d ? c.my_len : L - c.my_d) : 0;
+    if (lane < n) {
+      hops[h + lane] = make_int4(c.my_child, c.my_len, static_cast<int32_t>(c.my_d),
+                                 c.my_off >= 0 ? static_cast<int32_t>(c.my_off) : -1);
+      // the windows whose first position lies in this hop
+      for (int64_t k = (c.my_d + kW - 1) / kW; k * kW < c.my_d + lim; ++k)
+        wins[k] = make_int4(q, h + lane, static_cast<int32_t>(k), 1);
+    }
+    h += n;
+    D = __shfl_sync(kFull, c.my_d + lim, n - 1);
+    if (c.last_segment) break;
+    matched = c.d;
+    cur = c.node;
+  }
+  const int64_t nw = (D + kW - 1) / kW;
+  // this query's unused slots, up to the next query's first; the last query
+  // in the packing also clears the slots after it, and the first those before
+  const bool packed_last = qhi == q_off[nq];
+  const int64_t s_hi = packed_last ? n_tokens / kW + nq + 1 - (qlo / kW + q) : qhi / kW + 1 - qlo / kW;
+  for (int64_t k = nw + lane; k < s_hi; k += 32) wins[k] = make_int4(0, 0, 0, 0);
+  if (qlo == q_off[0])
+    for (int64_t k = lane; k < qlo / kW; k += 32) sc.wins[k] = make_int4(0, 0, 0, 0);
+  __syncwarp();
+  if (lane == 0) {
+    sc.qinfo[q] = make_int4(h, static_cast<int32_t>(D), static_cast<int32_t>(nw), 0);
+    sc.stop[q] = kNoMismatch;
+    sc.left[q] = static_cast<int32_t>(nw);
+    if (nw == 0) staged_finish(hops, h, L, kNoMismatch, q, block_size, out_node, out_len, out_compared);
+  }
+}
+
+template <int kW>
+__global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
+k_match_verify(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
+               int64_t n_slots, int32_t block_size, StagedScratch sc, int32_t* __restrict__ out_node,
+               int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared, AkvStatus* st) {
+  constexpr uint32_t kFull = 0xffffffffu;
+  constexpr int kChunks = 8;  // 256 positions per round
+  constexpr int32_t kStep = 32 * kChunks;
+  const int lane = threadIdx.x & 31;
+  const int64_t slot = static_cast<int64_t>(blockIdx.x) * kMatchWarpsPerCta + (threadIdx.x >> 5);
+  if (slot >= n_slots || akv_failed(st)) return;
+  const int4 rec = sc.wins[slot];
+  if (rec.w == 0) return;
+  const int32_t q = rec.x;
+  const int64_t qlo = q_off[q];
+  const int64_t L = q_off[q + 1] - qlo;
+  const int4 qi = sc.qinfo[q];  // {hops, D, windows}
+  const int32_t* __restrict__ Q = tokens + qlo;
+  const int4* __restrict__ hops = sc.hops + qlo;
+  const int32_t pw = rec.z * kW;
+  const int32_t pe = pw + kW < qi.y ? pw + kW : qi.y;
+  int32_t first = -1, first_hop = -1;
+  int32_t p = pw;
+  for (int32_t g = rec.y; p < pe && first < 0; g += 32) {
+    // hops g .. g + 31, one per lane (lanes past the last hop hold none)
+    const int nh = qi.x - g < 32 ? qi.x - g : 32;
+    if (nh <= 0) {  // positions left but no hop for them: the scratch does not hold this batch's chase
+      if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, g, qi.x);
+      return;
+    }
+    int4 hp = make_int4(-1, 0, INT32_MAX, -1);
+    if (lane < nh) hp = hops[g + lane];
+    int64_t off = hp.w;
+    bool bad = false;
+    if (lane < nh && hp.w < 0) {  // a hop found by a hash probe: its edge from the node arrays
+      off = tree.node_edge_off[hp.x];
+      bad = off < 0 || off + hp.y > tree.n_tokens || tree.node_edge_len[hp.x] != hp.y;
+    }
+    const uint32_t badm = __ballot_sync(kFull, bad);
+    if (badm) {
+      if (lane == __ffs(badm) - 1) akv_fail(st, AKV_ERR_TREE, q, hp.x, hp.y, off);
+      return;
+    }
+    const int32_t lim = lane < nh ? static_cast<int32_t>(hp.y < L - hp.z ? hp.y : L - hp.z) : 0;
+    const int32_t gend_all = __shfl_sync(kFull, hp.z + lim, nh - 1);
+    const int32_t gend = gend_all < pe ? gend_all : pe;
+    // hop holding position x: the last lane with depth <= x
+    auto hop_of = [&](int32_t x) -> int {
+      int lo = 0, hi = nh - 1;
+#pragma unroll
+      for (int k = 0; k < 5; ++k) {
+        const int mid = (lo + hi + 1) >> 1;
+        const int32_t v = __shfl_sync(kFull, hp.z, mid);
+        if (lo < hi) {
+          if (v <= x) lo = mid;
+          else hi = mid - 1;
+        }
+      }
+      return lo;
+    };
+    for (int32_t base = p; base < gend; base += kStep) {
+      int32_t av[kChunks], bv[kChunks];
+      const int e0 = hop_of(base);
+      const int32_t d0 = __shfl_sync(kFull, hp.z, e0);
+      const int32_t l0 = __shfl_sync(kFull, lim, e0);
+      if (d0 + l0 >= base + kStep || d0 + l0 >= gend) {  // the round lies in one edge
+        const int64_t oe = __shfl_sync(kFull, off, e0) - d0;
+#pragma unroll
+        for (int u = 0; u < kChunks; ++u) {
+          const int32_t x = base + u * 32 + lane;
+          const bool ok = x < gend;
+          av[u] = ok ? Q[x] : 0;
+          bv[u] = ok ? __ldg(&tree.tokens[oe + x]) : 0;
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < kChunks; ++u) {
+          const int32_t x = base + u * 32 + lane;
+          const bool ok = x < gend;
+          const int e = hop_of(ok ? x : gend - 1);
+          const int64_t oe = __shfl_sync(kFull, off, e) - __shfl_sync(kFull, hp.z, e);
+          av[u] = ok ? Q[x] : 0;
+          bv[u] = ok ? __ldg(&tree.tokens[oe + x]) : 0;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kChunks; ++u) {
+        const uint32_t m = __ballot_sync(kFull, av[u] != bv[u]);
+        if (m && first < 0) first = base + u * 32 + __ffs(m) - 1;
+      }
+      if (first >= 0) {
+        first_hop = g + hop_of(first);
+        break;
+      }
+    }
+    p = gend;
+  }
+  int32_t prior = 0;
+  if (lane == 0) {
+    if (first >= 0)
+      atomicMin(&sc.stop[q], (static_cast<unsigned long long>(first) << 32) | static_cast<uint32_t>(first_hop));
+    __threadfence();
+    prior = atomicSub(&sc.left[q], 1);
+  }
+  prior = __shfl_sync(kFull, prior, 0);
+  if (prior != 1) return;  // another window of this query finishes last
+  __threadfence();
+  if (lane == 0)
+    staged_finish(hops, qi.x, L, atomicAdd(&sc.stop[q], 0ull), q, block_size, out_node, out_len, out_compared);
 }
 
 // ── tree changes built on the device ───────────────────────────────────────
@@ -833,11 +1163,35 @@ const MatchKernels* match_kernels(int32_t chunks) {
   return nullptr;
 }
 
+// The staged lookup's kernels, per window size.
+struct StagedKernels {
+  int32_t window;
+  decltype(&k_match_chase<256>) chase;
+  decltype(&k_match_verify<256>) verify;
+};
+constexpr StagedKernels kStagedKernels[] = {
+    {256, &k_match_chase<256>, &k_match_verify<256>},
+    {512, &k_match_chase<512>, &k_match_verify<512>},
+    {1024, &k_match_chase<1024>, &k_match_verify<1024>},
+};
+constexpr int32_t kStagedDefaultWindow = 512;
+
+const StagedKernels* staged_kernels(int32_t window_tokens) {
+  const int32_t w = window_tokens == 0 ? kStagedDefaultWindow : window_tokens;
+  for (const StagedKernels& k : kStagedKernels)
+    if (k.window == w) return &k;
+  return nullptr;
+}
+
 template <typename F>
 int for_each_match_kernel(F&& f) {
   for (const MatchKernels& k : kMatchKernels) {
     if (int rc = f(reinterpret_cast<const void*>(k.whole), "akv_prepare: k_match")) return rc;
     if (int rc = f(reinterpret_cast<const void*>(k.split), "akv_prepare: k_match_split")) return rc;
+  }
+  for (const StagedKernels& k : kStagedKernels) {
+    if (int rc = f(reinterpret_cast<const void*>(k.chase), "akv_prepare: k_match_chase")) return rc;
+    if (int rc = f(reinterpret_cast<const void*>(k.verify), "akv_prepare: k_match_verify")) return rc;
   }
   return AKV_OK;
 }
@@ -1054,5 +1408,47 @@ extern "C" int akv_tree_commands(const AkvTreeView* tree, int64_t token_cap, con
   t.mask = tree->slot_mask;
   k_tree_commands<<<1, 32, 0, akv_stream(stream)>>>(t, cmds, n_cmds, payload, payload_len, status);
   AKV_LAUNCH_CHECK("akv_tree_commands");
+  return AKV_OK;
+}
+
+extern "C" int64_t akv_match_staged_scratch_bytes(int32_t nq, int64_t n_tokens, int32_t window_tokens) {
+  const StagedKernels* k = staged_kernels(window_tokens);
+  if (k == nullptr || nq < 0 || n_tokens < 0 || n_tokens > INT32_MAX) return -1;
+  return staged_layout(nullptr, nq, n_tokens, k->window, nullptr);
+}
+
+extern "C" int akv_match_prefix_staged(const AkvTreeView* tree, const int32_t* tokens, const int64_t* q_off,
+                                       int32_t nq, int64_t n_tokens, int32_t block_size, int32_t* out_node,
+                                       int32_t* out_len, int64_t* out_compared, const int32_t* order,
+                                       int32_t window_tokens, void* scratch, int64_t scratch_bytes,
+                                       AkvStatus* status, void* stream) {
+  if (int rc = match_args_ok(tree, tokens, q_off, nq, block_size, out_node, out_len, 0,
+                             "akv_match_prefix_staged"))
+    return rc;
+  const StagedKernels* k = staged_kernels(window_tokens);
+  AKV_ARG_CHECK(k != nullptr, "akv_match_prefix_staged: window_tokens=%d is not 256, 512 or 1024",
+                window_tokens);
+  AKV_ARG_CHECK(n_tokens >= 0 && n_tokens <= INT32_MAX,
+                "akv_match_prefix_staged: n_tokens=%lld not in [0, INT32_MAX]", static_cast<long long>(n_tokens));
+  AKV_ARG_CHECK(tree->n_tokens <= INT32_MAX, "akv_match_prefix_staged: the tree holds %lld tokens (at most INT32_MAX)",
+                static_cast<long long>(tree->n_tokens));
+  if (nq == 0) return AKV_OK;
+  AKV_ARG_CHECK(status != nullptr, "akv_match_prefix_staged: status is NULL");
+  AKV_ARG_CHECK(scratch != nullptr && reinterpret_cast<uintptr_t>(scratch) % 256 == 0,
+                "akv_match_prefix_staged: scratch is NULL or not 256-byte aligned");
+  const int64_t need = staged_layout(nullptr, nq, n_tokens, k->window, nullptr);
+  AKV_ARG_CHECK(scratch_bytes >= need, "akv_match_prefix_staged: scratch of %lld bytes, %lld needed",
+                static_cast<long long>(scratch_bytes), static_cast<long long>(need));
+  StagedScratch sc{};
+  staged_layout(static_cast<char*>(scratch), nq, n_tokens, k->window, &sc);
+  const int64_t n_slots = staged_slots(nq, n_tokens, k->window);
+  cudaStream_t s = akv_stream(stream);
+  k->chase<<<akv_ceil_div(nq, kMatchWarpsPerCta), kMatchWarpsPerCta * 32, 0, s>>>(
+      *tree, tokens, q_off, nq, n_tokens, block_size, order, sc, out_node, out_len, out_compared, status);
+  AKV_LAUNCH_CHECK("akv_match_prefix_staged(chase)");
+  const int64_t grid = (n_slots + kMatchWarpsPerCta - 1) / kMatchWarpsPerCta;
+  k->verify<<<static_cast<unsigned>(grid), kMatchWarpsPerCta * 32, 0, s>>>(
+      *tree, tokens, q_off, n_slots, block_size, sc, out_node, out_len, out_compared, status);
+  AKV_LAUNCH_CHECK("akv_match_prefix_staged(verify)");
   return AKV_OK;
 }

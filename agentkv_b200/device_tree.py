@@ -146,6 +146,7 @@ class DeviceTree:
         self._view: Optional[N.AkvTreeView] = None
         self._stage: Optional["QueryStage"] = None  # match_batch's reusable buffers
         self._split_scratch: Optional[torch.Tensor] = None  # akv_match_prefix_split's work space
+        self._staged_scratch: Optional[torch.Tensor] = None  # akv_match_prefix_staged's work space
         # Changes as commands (akv_tree_commands): the host tree's inserts and
         # prunes since the last upload, applied on the device by the replica
         # itself instead of uploading the rows they changed.  Used when every
@@ -677,7 +678,8 @@ class DeviceTree:
     def match(self, tokens: torch.Tensor, q_off: torch.Tensor, nq: int, block_size: int,
               out_node: torch.Tensor, out_len: torch.Tensor, out_cmp: Optional[torch.Tensor],
               chunks: int = 0, order: Optional[torch.Tensor] = None, runs: bool = False,
-              plan: Optional["SplitPlan"] = None, status: Optional[torch.Tensor] = None) -> None:
+              plan: Optional["SplitPlan"] = None, status: Optional[torch.Tensor] = None,
+              staged: bool = False, window_tokens: int = 0, n_tokens: Optional[int] = None) -> None:
         """Enqueue a match_prefix lookup of nq queries packed in `tokens` /
         `q_off` (device int32 / int64 tensors); `order` (device int32) is the
         launch order of the queries, longest first by default in
@@ -690,14 +692,35 @@ class DeviceTree:
         of plan.tokens_per_range tokens, one warp per range, so a long query
         does not hold the batch; its scratch is this tree's.  Without it,
         akv_match_prefix_variant (one warp per query).  The answers are the
-        same.  `status` (8 int32 on the device) replaces the tree's status
-        record for this lookup."""
+        same.  With staged=True the lookup is akv_match_prefix_staged: one
+        warp per query follows the tree by first tokens, then one warp per
+        window_tokens-token window (0 = the library's default) compares the
+        followed path; n_tokens is the packing's token count (default
+        tokens.numel()).  `status` (8 int32 on the device) replaces the
+        tree's status record for this lookup."""
         self.flush()
         if runs:
             self.build_runs()
         st = (status if status is not None else self.status).data_ptr()
         out_c = out_cmp.data_ptr() if out_cmp is not None else None
         ordp = order.data_ptr() if order is not None else None
+        if staged:
+            if plan is not None:
+                raise ValueError("match_prefix: a lookup is either split or staged")
+            nt = tokens.numel() if n_tokens is None else int(n_tokens)
+            need = int(N.lib.akv_match_staged_scratch_bytes(nq, nt, window_tokens))
+            if need < 0:
+                raise ValueError(f"match_prefix: no staged lookup of {nq} queries, {nt} tokens, "
+                                 f"window {window_tokens}")
+            if self._staged_scratch is None or self._staged_scratch.numel() < need:
+                cap = max(need, 2 * (self._staged_scratch.numel() if self._staged_scratch is not None else 0))
+                self._staged_scratch = torch.empty(cap, dtype=torch.uint8, device=self.device)
+            sc = self._staged_scratch
+            N.check(N.lib.akv_match_prefix_staged(
+                self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, nt, block_size, out_node.data_ptr(),
+                out_len.data_ptr(), out_c, ordp, window_tokens, sc.data_ptr(), sc.numel(), st,
+                stream_handle(self.device)))
+            return
         if plan is None:
             N.check(N.lib.akv_match_prefix_variant(
                 self.view(runs), tokens.data_ptr(), q_off.data_ptr(), nq, block_size, out_node.data_ptr(),
@@ -910,7 +933,7 @@ def longest_first(q_off, device: torch.device) -> torch.Tensor:
 
 def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_compared: bool = False,
                 runs: Optional[bool] = None, tokens_per_range: int = 0, split: bool = False,
-                chunks: int = 0):
+                chunks: int = 0, staged: bool = False, window_tokens: int = 0):
     """Longest shared prefix of many queries in one akv_match_prefix launch on
     `tree` (the owner's replica or another GPU's): (node ids, match lengths
     [, tokens compared]) as numpy arrays, each equal to the reference's
@@ -922,7 +945,9 @@ def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_co
     default; see DeviceTree.match) when split=True; by default one warp
     walks each query (measured faster on the match stress workload).
     chunks: 32-token chunks compared per verify step (0 = the kernel's
-    default), optionally with N.MATCH_PIPELINED / N.MATCH_PREFETCH."""
+    default), optionally with N.MATCH_PIPELINED / N.MATCH_PREFETCH.
+    staged=True: the two-launch lookup (DeviceTree.match) with windows of
+    window_tokens tokens."""
     t0 = time.perf_counter()
     if runs is None:
         runs = tree.want_runs()
@@ -935,7 +960,8 @@ def match_batch(tree: DeviceTree, queries: Sequence, block_size: int, *, with_co
     mlen = torch.empty(max(nq, 1), dtype=torch.int32, device=dev)
     cmp_ = torch.empty(max(nq, 1), dtype=torch.int64, device=dev) if with_compared else None
     plan = split_plan(tree._stage.lens_in_order, tokens_per_range) if (split and nq) else None
-    tree.match(tok, q_off, nq, block_size, node, mlen, cmp_, order=order, runs=runs, chunks=chunks, plan=plan)
+    tree.match(tok, q_off, nq, block_size, node, mlen, cmp_, order=order, runs=runs, chunks=chunks, plan=plan,
+               staged=staged, window_tokens=window_tokens, n_tokens=tree._stage.total)
     tree.check()
     res = (node[:nq].cpu().numpy(), mlen[:nq].cpu().numpy())
     if with_compared:

@@ -536,6 +536,33 @@ AKV_API int akv_match_prefix_split(const AkvTreeView* tree, const int32_t* token
                                    int64_t scratch_bytes, int32_t chunks, AkvStatus* status,
                                    void* stream);
 
+/* Scratch bytes of a staged lookup (akv_match_prefix_staged) of nq queries
+ * in a packing of n_tokens tokens, at window_tokens (0 = default, 512);
+ * -1 for arguments it would refuse.  Pure host function. */
+AKV_API int64_t akv_match_staged_scratch_bytes(int32_t nq, int64_t n_tokens, int32_t window_tokens);
+
+/* The same answers as akv_match_prefix_variant (the reference's
+ * _match_prefix_locked, agentkv/core/radix_tree.py:513-570, per query), in
+ * two launches: one warp per query follows the tree by each edge's first
+ * token only and records its hops; then one warp per window_tokens-token
+ * window of every query's followed path compares the query with the edges,
+ * and the first mismatch over a query's windows decides its answer.  A long
+ * query is spread over many warps without being walked twice.
+ *   n_tokens      tokens in the packing: q_off[nq] <= n_tokens <= INT32_MAX
+ *   order         optional launch order of the queries, longest first
+ *   window_tokens 256, 512 or 1024 (0 = 512)
+ *   scratch       caller-owned device memory of at least
+ *                 akv_match_staged_scratch_bytes(nq, n_tokens, window_tokens)
+ *                 bytes, 256-byte aligned; no initial contents needed; calls
+ *                 sharing it must be ordered (one stream)
+ * The tree's token arena must hold at most INT32_MAX tokens.  Two launches. */
+AKV_API int akv_match_prefix_staged(const AkvTreeView* tree, const int32_t* tokens,
+                                    const int64_t* q_off, int32_t nq, int64_t n_tokens,
+                                    int32_t block_size, int32_t* out_node, int32_t* out_len,
+                                    int64_t* out_compared, const int32_t* order,
+                                    int32_t window_tokens, void* scratch, int64_t scratch_bytes,
+                                    AkvStatus* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

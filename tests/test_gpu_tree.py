@@ -272,6 +272,14 @@ def test_match_prefix_stress_tree(golden_dir, name):
         np.testing.assert_array_equal(hn, node, err_msg=tag)
         np.testing.assert_array_equal(hl, mlen, err_msg=tag)
         np.testing.assert_array_equal(hc, cmp_, err_msg=tag)
+    # the staged lookup (chase, then windows over the grid) at every window size
+    for runs, window in ((True, 0), (False, 0), (True, 256), (True, 1024), (False, 512)):
+        hn, hl, hc = match_batch(pool._tree._dev_tree, queries, 16, with_compared=True, runs=runs,
+                                 staged=True, window_tokens=window)
+        tag = f"staged runs={runs} window={window}"
+        np.testing.assert_array_equal(hn, node, err_msg=tag)
+        np.testing.assert_array_equal(hl, mlen, err_msg=tag)
+        np.testing.assert_array_equal(hc, cmp_, err_msg=tag)
 
 
 def _oracle_tree_from(pool) -> dict:
@@ -331,6 +339,16 @@ def test_match_edge_cases():
         w_node, w_len, w_cmp = match_batch(pool._tree._dev_tree, qs, 4, with_compared=True, split=False)
         assert mlen.tolist() == w_len.tolist() == [0, 8, 8, 0, 8, 0], tpi
         assert cmp_.tolist() == w_cmp.tolist(), tpi
+        assert [n if m else -1 for n, m in zip(node, mlen)] == [n if m else -1 for n, m in zip(w_node, w_len)]
+    # staged lookups: the same queries, and one whose followed path ends in a
+    # partly fitting edge
+    for window in (256, 512, 1024):
+        node, mlen, cmp_ = match_batch(pool._tree._dev_tree, qs + [list(range(6))], 4, with_compared=True,
+                                       staged=True, window_tokens=window)
+        w_node, w_len, w_cmp = match_batch(pool._tree._dev_tree, qs + [list(range(6))], 4, with_compared=True)
+        assert mlen.tolist() == w_len.tolist() == [0, 8, 8, 0, 8, 0, 0], window
+        assert w_cmp[-1] == 6, w_cmp
+        assert cmp_.tolist() == w_cmp.tolist(), window
         assert [n if m else -1 for n, m in zip(node, mlen)] == [n if m else -1 for n, m in zip(w_node, w_len)]
 
 
@@ -507,6 +525,11 @@ def test_match_long_unary_chains():
                                        tokens_per_range=tpi)
         got = [(int(n) if m else -1, int(m), int(c)) for n, m, c in zip(node, mlen, cmp_)]
         assert got == [(int(n) if m else -1, int(m), int(c)) for n, m, c in want], (runs, split, tpi)
+    for runs, window in ((True, 256), (False, 256), (True, 512), (True, 1024)):
+        node, mlen, cmp_ = match_batch(dev_tree, queries, bs, with_compared=True, runs=runs, staged=True,
+                                       window_tokens=window)
+        got = [(int(n) if m else -1, int(m), int(c)) for n, m, c in zip(node, mlen, cmp_)]
+        assert got == [(int(n) if m else -1, int(m), int(c)) for n, m, c in want], ("staged", runs, window)
     assert dev_tree.d_run_head is not None and int((dev_tree.d_run_head >= 0).sum()) >= 60
 
 
@@ -552,3 +575,7 @@ def test_match_scenarios_match_reference(golden_dir, name):
         node, mlen = match_batch(pool._tree._dev_tree, sc["queries"], sc["block_size"], runs=runs,
                                  split=split, tokens_per_range=tpi)
         assert [[int(n) if m else -1, int(m)] for n, m in zip(node, mlen)] == want, (runs, split, tpi)
+    for runs, window in ((True, 256), (False, 512)):
+        node, mlen = match_batch(pool._tree._dev_tree, sc["queries"], sc["block_size"], runs=runs, staged=True,
+                                 window_tokens=window)
+        assert [[int(n) if m else -1, int(m)] for n, m in zip(node, mlen)] == want, ("staged", runs, window)

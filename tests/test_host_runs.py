@@ -317,17 +317,23 @@ def test_tree_orchestration_with_kernel_model(monkeypatch):
             want = O.match_prefix_csr(_csr_of(tree._shared_nodes), flat, q_off, 16)
             want_node = np.where(want[1] > 0, want[0], -1)
             # the split lookup at the default range and at ranges far shorter
-            # than the queries (many ranges per query, stops in any of them)
+            # than the queries (many ranges per query, stops in any of them);
+            # the staged lookup at every window size
             for t, runs, tpi in ((owner, None, -1), (owner, False, -1), (replica, None, -1), (owner, None, 0),
-                                 (owner, True, 32), (replica, False, 64), (owner, None, 96)):
-                node, mlen, cmp_ = DT.match_batch(t, queries, 16, with_compared=True, runs=runs, split=tpi >= 0,
-                                                  tokens_per_range=max(tpi, 0))
+                                 (owner, True, 32), (replica, False, 64), (owner, None, 96),
+                                 (owner, None, "s0"), (replica, True, "s256"), (owner, False, "s1024")):
+                staged = isinstance(tpi, str)
+                node, mlen, cmp_ = DT.match_batch(
+                    t, queries, 16, with_compared=True, runs=runs, split=not staged and tpi >= 0,
+                    tokens_per_range=0 if staged else max(tpi, 0), staged=staged,
+                    window_tokens=int(tpi[1:]) if staged else 0)
                 np.testing.assert_array_equal(mlen, want[1], err_msg=f"{i} {runs} {tpi}")
                 np.testing.assert_array_equal(np.where(mlen > 0, node, -1), want_node)
                 np.testing.assert_array_equal(cmp_, want[2])
             checks += 1
     assert checks >= 10 and model.run_hops > 1000, (checks, model.run_hops)
     assert model.split_ranges > 20 * checks * len(queries), model.split_ranges
+    assert model.staged_windows > 3 * checks * len(queries), model.staged_windows
     # the replica's arrays equal the owner's after a final sync
     owner.build_runs()
     d = sync.share()

@@ -285,3 +285,71 @@ class TreeKernelModel:
             if o_cmp is not None:
                 o_cmp[q] = (key >> 1) + (key & 1)
         return 0
+
+    def akv_match_prefix_staged(self, view, tokens, q_off, nq, n_tokens, block_size, out_node, out_len, out_cmp,
+                                order, window_tokens, scratch, scratch_bytes, status, stream) -> int:
+        """The staged lookup as its two kernels do it: the chase follows
+        first tokens only and records hops; the windows of the chased span
+        report their first mismatch (position, hop); the smallest over the
+        windows, or else the last hop, decides the answer (staged_finish)."""
+        self.match_calls += 1
+        W = window_tokens or 512
+        need = self._real.akv_match_staged_scratch_bytes(nq, n_tokens, window_tokens)
+        assert 0 <= need <= scratch_bytes, (need, scratch_bytes)
+        next_hop = self._walker(view)
+        off, elen, arena, qo, q_all = self._arrays(view, tokens, q_off, nq)
+        assert int(qo[-1]) <= n_tokens
+        o_node = _arr(out_node, C.c_int32, (nq,))
+        o_len = _arr(out_len, C.c_int32, (nq,))
+        o_cmp = _arr(out_cmp, C.c_int64, (nq,)) if out_cmp else None
+        self.staged_windows = getattr(self, "staged_windows", 0)
+        for q in range(nq):
+            Q = q_all[qo[q]:qo[q + 1]]
+            L = len(Q)
+            hops, node, d, pending = [], 0, 0, []  # (child, edge length, depth)
+            while d < L:
+                child, clen = next_hop(node, int(Q[d]), pending)
+                if child < 0:
+                    break
+                assert int(elen[child]) == clen, (child, int(elen[child]), clen)
+                hops.append((child, clen, d))
+                if clen == 0 or d + clen > L:
+                    break
+                d += clen
+                node = child
+            lims = [min(c, L - dd) for _, c, dd in hops]
+            D = hops[-1][2] + lims[-1] if hops else 0
+            starts = [dd for _, _, dd in hops]
+            stop = None
+            for k in range(-(-D // W)):  # every window on its own, as the verify warps take them
+                self.staged_windows += 1
+                lo, hi = k * W, min((k + 1) * W, D)
+                h = int(np.searchsorted(starts, lo, side="right")) - 1
+                p = lo
+                while p < hi:
+                    child, _, dd = hops[h]
+                    e = min(hi, dd + lims[h])
+                    ne = np.flatnonzero(Q[p:e] != arena[off[child] + p - dd:off[child] + e - dd])
+                    if len(ne):
+                        cand = (p + int(ne[0]), h)
+                        stop = cand if stop is None else min(stop, cand)
+                        break
+                    p = e
+                    h += 1
+            if stop is not None:
+                P, h = stop
+                key, matched, nd = 2 * P + 1, hops[h][2], hops[h - 1][0] if h > 0 else 0
+            elif not hops:
+                key, matched, nd = 0, 0, 0
+            else:
+                child, clen, dd = hops[-1]
+                if lims[-1] < clen or clen == 0:
+                    key, matched, nd = 2 * (dd + lims[-1]), dd, hops[-2][0] if len(hops) > 1 else 0
+                else:
+                    key, matched, nd = 2 * (dd + clen), dd + clen, child
+            m = (matched // block_size) * block_size
+            o_node[q] = nd if m else -1
+            o_len[q] = m
+            if o_cmp is not None:
+                o_cmp[q] = (key >> 1) + (key & 1)
+        return 0
