@@ -145,7 +145,10 @@ struct Chase {
   int4 carry_e = make_int4(-1, 0, 0, 0);
 };
 
-template <typename QToken>
+// kProbeEdges: a hop found by a hash probe loads its edge's offset and
+// length at once (the loads are consumed only when the caller uses them);
+// else they are left at -1 for the caller to read.
+template <bool kProbeEdges, typename QToken>
 AKV_DEV bool chase_segment(Chase& c, const AkvTreeView& tree, const int4* __restrict__ slots,
                            const int4* __restrict__ runs, const int32_t* __restrict__ Q, int64_t L,
                            int64_t b, int64_t matched, int32_t cur, int32_t q, AkvStatus* st, int lane,
@@ -274,7 +277,12 @@ AKV_DEV bool chase_segment(Chase& c, const AkvTreeView& tree, const int4* __rest
       c.my_child = child;
       c.my_len = clen;
       c.my_d = d;
-      c.my_off = -1;  // read at the verify phase
+      if (kProbeEdges) {
+        c.my_off = __ldg(&tree.node_edge_off[child]);
+        c.my_elen = __ldg(&tree.node_edge_len[child]);
+      } else {
+        c.my_off = -1;  // read at the verify phase
+      }
     }
     ++n;
     if (clen == 0 || d + clen > L) {  // empty edge / edge past the query end: the walk ends here
@@ -330,7 +338,7 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
   int64_t matched = 0;
   Chase c;
   while (true) {
-    if (!chase_segment(c, tree, slots, runs, Q, L, b, matched, cur, q, st, lane, qtoken))
+    if (!chase_segment<false>(c, tree, slots, runs, Q, L, b, matched, cur, q, st, lane, qtoken))
       return MatchStop{0, 0, -1};
     const int n = c.n;
     const bool last_segment = c.last_segment, range_end = c.range_end;
@@ -630,14 +638,17 @@ k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
 // lookup is two launches:
 //  k_match_chase  — one warp per query runs the chase phase alone over the
 //                   whole query (chase_segment: hops decided by each edge's
-//                   first token) and writes its hops and, for every W-token
-//                   window of the chased span [0, D), the hop that holds the
-//                   window's first position;
+//                   first token, every hop's edge range loaded as it is
+//                   found) and writes its hops and, for every W-token window
+//                   of the chased span [0, D), a record of the window with
+//                   the hop that holds its first position;
 //  k_match_verify — one warp per window compares the query's tokens in it
-//                   with the hops' edge tokens.  The first mismatch over all
-//                   windows of a query (an atomic min on position) is the
-//                   reference loop's stop, and the warp that finishes the
-//                   query's last window writes its answer.
+//                   with the hops' edge tokens: a window inside one edge
+//                   (most of them) goes from its record straight to the
+//                   token loads.  The first mismatch over all windows of a
+//                   query (an atomic min on position) is the reference
+//                   loop's stop, and the warp that finishes the query's last
+//                   window writes its answer.
 // The answer is the one-warp walk's: the walk stops at the first hop along
 // the chased path that mismatches or only partly fits (only the last hop can
 // partly fit); hops past it are speculation and are discarded.  The chase may
@@ -645,12 +656,13 @@ k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
 // malformed tree it can report AKV_ERR_TREE where that walk would not.
 //
 // Scratch (caller-owned, akv_match_staged_scratch_bytes):
-//   hops  int4 [n_tokens]   {child, edge length, depth, edge offset or -1}:
-//                           query q's hops at q_off[q] + h (a query of L
-//                           tokens has at most L hops, as every hop before
-//                           the last takes at least one token)
-//   wins  int4 [n_tokens / W + nq + 1]  {q, hop, window, 1}, or 0 for an
-//                           unused slot: query q's windows from slot
+//   hops  int4 [n_tokens]   {child, edge length, depth, edge offset}: query
+//                           q's hops at q_off[q] + h (a query of L tokens has
+//                           at most L hops, as every hop before the last
+//                           takes at least one token)
+//   wins  2 x int4 [n_tokens / W + nq + 1]  {q, hop, window, q_off[q]} and
+//                           {hop depth, edge length, edge offset, L}, or q = -1
+//                           for an unused slot: query q's windows from slot
 //                           q_off[q] / W + q (so no prefix sum is needed)
 //   qinfo int4 [nq]         {hops, D, windows, 0}
 //   stop  uint64 [nq]       (position << 32) | hop of the first mismatch
@@ -678,7 +690,7 @@ AKV_HD int64_t staged_layout(char* base, int32_t nq, int64_t n_tokens, int32_t W
     return p;
   };
   char* hops = take(16 * n_tokens);
-  char* wins = take(16 * staged_slots(nq, n_tokens, W));
+  char* wins = take(32 * staged_slots(nq, n_tokens, W));
   char* qinfo = take(16 * static_cast<int64_t>(nq));
   char* stop = take(8 * static_cast<int64_t>(nq));
   char* left = take(4 * static_cast<int64_t>(nq));
@@ -741,19 +753,16 @@ k_match_chase(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
   const int4* __restrict__ runs =
       tree.run_head != nullptr ? reinterpret_cast<const int4*>(tree.run_entries) : nullptr;
   int4* __restrict__ hops = sc.hops + qlo;
-  int4* __restrict__ wins = sc.wins + (qlo / kW + q);
+  int4* __restrict__ wins = sc.wins + 2 * (qlo / kW + q);
   QueryWindow qtoken{Q, L, lane};
   Chase c;
   int32_t cur = 0, h = 0;  // node reached, hops written
   int64_t matched = 0, D = 0;
   while (true) {
-    if (!chase_segment(c, tree, slots, runs, Q, L, L, matched, cur, q, st, lane, qtoken)) return;
+    if (!chase_segment<true>(c, tree, slots, runs, Q, L, L, matched, cur, q, st, lane, qtoken)) return;
     const int n = c.n;
     if (n == 0) break;
-    // a run hop brings its edge's offset and length: check them here (the
-    // verify reads them itself for the other hops)
-    const bool bad = lane < n && c.my_off >= 0 &&
-                     (c.my_off + c.my_len > tree.n_tokens || c.my_elen != c.my_len);
+    const bool bad = lane < n && (c.my_off < 0 || c.my_off + c.my_len > tree.n_tokens || c.my_elen != c.my_len);
     const uint32_t badm = __ballot_sync(kFull, bad);
     if (badm) {
       if (lane == __ffs(badm) - 1) akv_fail(st, AKV_ERR_TREE, q, c.my_child, c.my_len, c.my_off);
@@ -761,11 +770,13 @@ k_match_chase(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
     }
     const int64_t lim = lane < n ? (c.my_len < L - c.my_d ? c.my_len : L - c.my_d) : 0;
     if (lane < n) {
-      hops[h + lane] = make_int4(c.my_child, c.my_len, static_cast<int32_t>(c.my_d),
-                                 c.my_off >= 0 ? static_cast<int32_t>(c.my_off) : -1);
+      const int32_t d32 = static_cast<int32_t>(c.my_d), off32 = static_cast<int32_t>(c.my_off);
+      hops[h + lane] = make_int4(c.my_child, c.my_len, d32, off32);
       // the windows whose first position lies in this hop
-      for (int64_t k = (c.my_d + kW - 1) / kW; k * kW < c.my_d + lim; ++k)
-        wins[k] = make_int4(q, h + lane, static_cast<int32_t>(k), 1);
+      for (int64_t k = (c.my_d + kW - 1) / kW; k * kW < c.my_d + lim; ++k) {
+        wins[2 * k] = make_int4(q, h + lane, static_cast<int32_t>(k), static_cast<int32_t>(qlo));
+        wins[2 * k + 1] = make_int4(d32, c.my_len, off32, static_cast<int32_t>(L));
+      }
     }
     h += n;
     D = __shfl_sync(kFull, c.my_d + lim, n - 1);
@@ -778,9 +789,9 @@ k_match_chase(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
   // in the packing also clears the slots after it, and the first those before
   const bool packed_last = qhi == q_off[nq];
   const int64_t s_hi = packed_last ? n_tokens / kW + nq + 1 - (qlo / kW + q) : qhi / kW + 1 - qlo / kW;
-  for (int64_t k = nw + lane; k < s_hi; k += 32) wins[k] = make_int4(0, 0, 0, 0);
+  for (int64_t k = nw + lane; k < s_hi; k += 32) wins[2 * k] = make_int4(-1, 0, 0, 0);
   if (qlo == q_off[0])
-    for (int64_t k = lane; k < qlo / kW; k += 32) sc.wins[k] = make_int4(0, 0, 0, 0);
+    for (int64_t k = lane; k < qlo / kW; k += 32) sc.wins[2 * k] = make_int4(-1, 0, 0, 0);
   __syncwarp();
   if (lane == 0) {
     sc.qinfo[q] = make_int4(h, static_cast<int32_t>(D), static_cast<int32_t>(nw), 0);
@@ -792,100 +803,100 @@ k_match_chase(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
 
 template <int kW>
 __global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
-k_match_verify(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
-               int64_t n_slots, int32_t block_size, StagedScratch sc, int32_t* __restrict__ out_node,
-               int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared, AkvStatus* st) {
+k_match_verify(AkvTreeView tree, const int32_t* __restrict__ tokens, int64_t n_slots, int32_t block_size,
+               StagedScratch sc, int32_t* __restrict__ out_node, int32_t* __restrict__ out_len,
+               int64_t* __restrict__ out_compared, AkvStatus* st) {
   constexpr uint32_t kFull = 0xffffffffu;
-  constexpr int kChunks = 8;  // 256 positions per round
+  constexpr int32_t kRound = kW < 512 ? kW : 512;  // positions per round inside one edge
+  constexpr int kRC = kRound / 32;
+  constexpr int kChunks = 8;  // rounds of 256 positions across several edges
   constexpr int32_t kStep = 32 * kChunks;
   const int lane = threadIdx.x & 31;
   const int64_t slot = static_cast<int64_t>(blockIdx.x) * kMatchWarpsPerCta + (threadIdx.x >> 5);
   if (slot >= n_slots || akv_failed(st)) return;
-  const int4 rec = sc.wins[slot];
-  if (rec.w == 0) return;
-  const int32_t q = rec.x;
-  const int64_t qlo = q_off[q];
-  const int64_t L = q_off[q + 1] - qlo;
-  const int4 qi = sc.qinfo[q];  // {hops, D, windows}
+  const int4 r0 = sc.wins[2 * slot];
+  const int4 r1 = sc.wins[2 * slot + 1];
+  if (r0.x < 0) return;
+  const int32_t q = r0.x, h0 = r0.y, pw = r0.z * kW, qlo = r0.w;
+  const int32_t d0 = r1.x, L = r1.w;
+  const int32_t end0 = d0 + (r1.y < L - d0 ? r1.y : L - d0);  // end of hop h0's positions
   const int32_t* __restrict__ Q = tokens + qlo;
   const int4* __restrict__ hops = sc.hops + qlo;
-  const int32_t pw = rec.z * kW;
-  const int32_t pe = pw + kW < qi.y ? pw + kW : qi.y;
+  int4 qi = make_int4(0, 0, 0, 0);  // {hops, D, windows}: needed only past hop h0
+  int32_t pe = pw + kW;
+  if (end0 < pe) {
+    qi = sc.qinfo[q];
+    pe = pe < qi.y ? pe : qi.y;
+  }
   int32_t first = -1, first_hop = -1;
-  int32_t p = pw;
-  for (int32_t g = rec.y; p < pe && first < 0; g += 32) {
-    // hops g .. g + 31, one per lane (lanes past the last hop hold none)
-    const int nh = qi.x - g < 32 ? qi.x - g : 32;
-    if (nh <= 0) {  // positions left but no hop for them: the scratch does not hold this batch's chase
-      if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, g, qi.x);
-      return;
-    }
-    int4 hp = make_int4(-1, 0, INT32_MAX, -1);
-    if (lane < nh) hp = hops[g + lane];
-    int64_t off = hp.w;
-    bool bad = false;
-    if (lane < nh && hp.w < 0) {  // a hop found by a hash probe: its edge from the node arrays
-      off = tree.node_edge_off[hp.x];
-      bad = off < 0 || off + hp.y > tree.n_tokens || tree.node_edge_len[hp.x] != hp.y;
-    }
-    const uint32_t badm = __ballot_sync(kFull, bad);
-    if (badm) {
-      if (lane == __ffs(badm) - 1) akv_fail(st, AKV_ERR_TREE, q, hp.x, hp.y, off);
-      return;
-    }
-    const int32_t lim = lane < nh ? static_cast<int32_t>(hp.y < L - hp.z ? hp.y : L - hp.z) : 0;
-    const int32_t gend_all = __shfl_sync(kFull, hp.z + lim, nh - 1);
-    const int32_t gend = gend_all < pe ? gend_all : pe;
-    // hop holding position x: the last lane with depth <= x
-    auto hop_of = [&](int32_t x) -> int {
-      int lo = 0, hi = nh - 1;
+  if (end0 >= pe) {  // the window lies in one edge: straight to the tokens
+    const int64_t oe = static_cast<int64_t>(r1.z) - d0;
+    for (int32_t base = pw; base < pe && first < 0; base += kRound) {
+      int32_t av[kRC], bv[kRC];
 #pragma unroll
-      for (int k = 0; k < 5; ++k) {
-        const int mid = (lo + hi + 1) >> 1;
-        const int32_t v = __shfl_sync(kFull, hp.z, mid);
-        if (lo < hi) {
-          if (v <= x) lo = mid;
-          else hi = mid - 1;
-        }
+      for (int u = 0; u < kRC; ++u) {
+        const int32_t x = base + u * 32 + lane;
+        const bool ok = x < pe;
+        av[u] = ok ? Q[x] : 0;
+        bv[u] = ok ? __ldg(&tree.tokens[oe + x]) : 0;
       }
-      return lo;
-    };
-    for (int32_t base = p; base < gend; base += kStep) {
-      int32_t av[kChunks], bv[kChunks];
-      const int e0 = hop_of(base);
-      const int32_t d0 = __shfl_sync(kFull, hp.z, e0);
-      const int32_t l0 = __shfl_sync(kFull, lim, e0);
-      if (d0 + l0 >= base + kStep || d0 + l0 >= gend) {  // the round lies in one edge
-        const int64_t oe = __shfl_sync(kFull, off, e0) - d0;
 #pragma unroll
-        for (int u = 0; u < kChunks; ++u) {
-          const int32_t x = base + u * 32 + lane;
-          const bool ok = x < gend;
-          av[u] = ok ? Q[x] : 0;
-          bv[u] = ok ? __ldg(&tree.tokens[oe + x]) : 0;
+      for (int u = 0; u < kRC; ++u) {
+        const uint32_t m = __ballot_sync(kFull, av[u] != bv[u]);
+        if (m && first < 0) first = base + u * 32 + __ffs(m) - 1;
+      }
+    }
+    if (first >= 0) first_hop = h0;
+  } else {  // several edges: the hops 32 at a time, one per lane
+    int32_t p = pw;
+    for (int32_t g = h0; p < pe && first < 0; g += 32) {
+      const int nh = qi.x - g < 32 ? qi.x - g : 32;
+      if (nh <= 0) {  // positions left but no hop for them: the scratch does not hold this batch's chase
+        if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, g, qi.x);
+        return;
+      }
+      int4 hp = make_int4(-1, 0, INT32_MAX, 0);
+      if (lane < nh) hp = hops[g + lane];
+      const int32_t lim = lane < nh ? (hp.y < L - hp.z ? hp.y : L - hp.z) : 0;
+      const int32_t gend_all = __shfl_sync(kFull, hp.z + lim, nh - 1);
+      const int32_t gend = gend_all < pe ? gend_all : pe;
+      // hop holding position x: the last lane with depth <= x
+      auto hop_of = [&](int32_t x) -> int {
+        int lo = 0, hi = nh - 1;
+#pragma unroll
+        for (int k = 0; k < 5; ++k) {
+          const int mid = (lo + hi + 1) >> 1;
+          const int32_t v = __shfl_sync(kFull, hp.z, mid);
+          if (lo < hi) {
+            if (v <= x) lo = mid;
+            else hi = mid - 1;
+          }
         }
-      } else {
+        return lo;
+      };
+      for (int32_t base = p; base < gend; base += kStep) {
+        int32_t av[kChunks], bv[kChunks];
 #pragma unroll
         for (int u = 0; u < kChunks; ++u) {
           const int32_t x = base + u * 32 + lane;
           const bool ok = x < gend;
           const int e = hop_of(ok ? x : gend - 1);
-          const int64_t oe = __shfl_sync(kFull, off, e) - __shfl_sync(kFull, hp.z, e);
+          const int64_t oe = static_cast<int64_t>(__shfl_sync(kFull, hp.w, e)) - __shfl_sync(kFull, hp.z, e);
           av[u] = ok ? Q[x] : 0;
           bv[u] = ok ? __ldg(&tree.tokens[oe + x]) : 0;
         }
-      }
 #pragma unroll
-      for (int u = 0; u < kChunks; ++u) {
-        const uint32_t m = __ballot_sync(kFull, av[u] != bv[u]);
-        if (m && first < 0) first = base + u * 32 + __ffs(m) - 1;
+        for (int u = 0; u < kChunks; ++u) {
+          const uint32_t m = __ballot_sync(kFull, av[u] != bv[u]);
+          if (m && first < 0) first = base + u * 32 + __ffs(m) - 1;
+        }
+        if (first >= 0) {
+          first_hop = g + hop_of(first);
+          break;
+        }
       }
-      if (first >= 0) {
-        first_hop = g + hop_of(first);
-        break;
-      }
+      p = gend;
     }
-    p = gend;
   }
   int32_t prior = 0;
   if (lane == 0) {
@@ -898,7 +909,8 @@ k_match_verify(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64
   if (prior != 1) return;  // another window of this query finishes last
   __threadfence();
   if (lane == 0)
-    staged_finish(hops, qi.x, L, atomicAdd(&sc.stop[q], 0ull), q, block_size, out_node, out_len, out_compared);
+    staged_finish(hops, sc.qinfo[q].x, L, atomicAdd(&sc.stop[q], 0ull), q, block_size, out_node, out_len,
+                  out_compared);
 }
 
 // ── tree changes built on the device ───────────────────────────────────────
@@ -1448,7 +1460,7 @@ extern "C" int akv_match_prefix_staged(const AkvTreeView* tree, const int32_t* t
   AKV_LAUNCH_CHECK("akv_match_prefix_staged(chase)");
   const int64_t grid = (n_slots + kMatchWarpsPerCta - 1) / kMatchWarpsPerCta;
   k->verify<<<static_cast<unsigned>(grid), kMatchWarpsPerCta * 32, 0, s>>>(
-      *tree, tokens, q_off, n_slots, block_size, sc, out_node, out_len, out_compared, status);
+      *tree, tokens, n_slots, block_size, sc, out_node, out_len, out_compared, status);
   AKV_LAUNCH_CHECK("akv_match_prefix_staged(verify)");
   return AKV_OK;
 }

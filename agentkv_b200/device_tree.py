@@ -823,6 +823,8 @@ class QueryStage:
     reused by the next pack(): the caller finishes the lookup (reads its
     results) first, as match_batch does."""
 
+    UPLOAD_SLICE = 2 << 20  # tokens (8 MB) per upload slice
+
     def __init__(self, device: torch.device) -> None:
         self.device = device
         self._tok_cap = self._q_cap = 0
@@ -851,15 +853,26 @@ class QueryStage:
         lens = np.fromiter((len(q) for q in queries), np.int64, nq)
         total = int(lens.sum())
         self._grow(total, nq)
-        if total:
-            np.concatenate([np.asarray(q, np.int32) for q in queries], out=self.h_tok.numpy()[:total])
         off = self.h_off.numpy()[: nq + 1]
         off[0] = 0
         np.cumsum(lens, out=off[1:])
+        # The packing goes up in slices of about UPLOAD_SLICE tokens, each as
+        # soon as it is written, so the upload of one slice overlaps the
+        # host's packing of the next.
+        h = self.h_tok.numpy()
+        cuts = [0] if total == 0 else np.unique(np.searchsorted(
+            off, np.arange(self.UPLOAD_SLICE, total, self.UPLOAD_SLICE), side="right")).tolist() + [nq]
+        a = 0
+        for b in cuts:
+            if b <= a:
+                continue
+            lo, hi = int(off[a]), int(off[b])
+            np.concatenate([np.asarray(q, np.int32) for q in queries[a:b]], out=h[lo:hi])
+            self.d_tok[lo:hi].copy_(self.h_tok[lo:hi], non_blocking=True)
+            a = b
         order = np.argsort(-lens, kind="stable")
         self.h_ord.numpy()[:nq] = order
         self.lens_in_order = lens[order]
-        self.d_tok[:total].copy_(self.h_tok[:total], non_blocking=True)
         self.d_off[: nq + 1].copy_(self.h_off[: nq + 1], non_blocking=True)
         self.d_ord[:nq].copy_(self.h_ord[:nq], non_blocking=True)
         self.total = total

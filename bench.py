@@ -869,9 +869,18 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         for i in range(reps):
             pool.match_prefix_batch(batches[i % len(batches)])
         e2e_s = (time.perf_counter() - t0) / reps
+        # where the time goes: the host packing (and its sliced upload) alone
+        stage = pool._tree._dev_tree._stage
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        stage.pack(batches[0])
+        pack_ms = (time.perf_counter() - t0) * 1e3
+        torch.cuda.synchronize()
+        upload_ms = (time.perf_counter() - t0) * 1e3
         h2d = int(statistics.mean(qtokens)) * 4 + (nq + 1) * 8 + nq * 4
         e2e = {"value": round(nq / e2e_s, 1), "unit": "queries/s", "ms_per_batch": round(e2e_s * 1e3, 3),
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": nq * 8,
+               "host_pack_ms": round(pack_ms, 3), "pack_and_upload_ms": round(upload_ms, 3),
                "api": "AgentKVPool.match_prefix_batch (host token lists in, numpy answers out)"}
     if rank == 0:
         peak, peak_kind = measured_peak()
