@@ -801,22 +801,18 @@ k_match_chase(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
   }
 }
 
+// One window of a staged lookup (record r0, r1), one warp.  Returns false
+// after recording an error.
 template <int kW>
-__global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
-k_match_verify(AkvTreeView tree, const int32_t* __restrict__ tokens, int64_t n_slots, int32_t block_size,
-               StagedScratch sc, int32_t* __restrict__ out_node, int32_t* __restrict__ out_len,
-               int64_t* __restrict__ out_compared, AkvStatus* st) {
+AKV_DEV bool verify_window(const AkvTreeView& tree, const int32_t* __restrict__ tokens, const int4& r0,
+                           const int4& r1, const StagedScratch& sc, int32_t block_size,
+                           int32_t* __restrict__ out_node, int32_t* __restrict__ out_len,
+                           int64_t* __restrict__ out_compared, AkvStatus* st, int lane) {
   constexpr uint32_t kFull = 0xffffffffu;
   constexpr int32_t kRound = kW < 512 ? kW : 512;  // positions per round inside one edge
   constexpr int kRC = kRound / 32;
   constexpr int kChunks = 8;  // rounds of 256 positions across several edges
   constexpr int32_t kStep = 32 * kChunks;
-  const int lane = threadIdx.x & 31;
-  const int64_t slot = static_cast<int64_t>(blockIdx.x) * kMatchWarpsPerCta + (threadIdx.x >> 5);
-  if (slot >= n_slots || akv_failed(st)) return;
-  const int4 r0 = sc.wins[2 * slot];
-  const int4 r1 = sc.wins[2 * slot + 1];
-  if (r0.x < 0) return;
   const int32_t q = r0.x, h0 = r0.y, pw = r0.z * kW, qlo = r0.w;
   const int32_t d0 = r1.x, L = r1.w;
   const int32_t end0 = d0 + (r1.y < L - d0 ? r1.y : L - d0);  // end of hop h0's positions
@@ -853,7 +849,7 @@ k_match_verify(AkvTreeView tree, const int32_t* __restrict__ tokens, int64_t n_s
       const int nh = qi.x - g < 32 ? qi.x - g : 32;
       if (nh <= 0) {  // positions left but no hop for them: the scratch does not hold this batch's chase
         if (lane == 0) akv_fail(st, AKV_ERR_TREE, q, g, qi.x);
-        return;
+        return false;
       }
       int4 hp = make_int4(-1, 0, INT32_MAX, 0);
       if (lane < nh) hp = hops[g + lane];
@@ -906,11 +902,29 @@ k_match_verify(AkvTreeView tree, const int32_t* __restrict__ tokens, int64_t n_s
     prior = atomicSub(&sc.left[q], 1);
   }
   prior = __shfl_sync(kFull, prior, 0);
-  if (prior != 1) return;  // another window of this query finishes last
+  if (prior != 1) return true;  // another window of this query finishes last
   __threadfence();
   if (lane == 0)
     staged_finish(hops, sc.qinfo[q].x, L, atomicAdd(&sc.stop[q], 0ull), q, block_size, out_node, out_len,
                   out_compared);
+  return true;
+}
+
+// One warp per window slot.  (Fewer warps looping over the slots, each
+// loading its next record while comparing, measured slower: 0.089 against
+// 0.055 ms per 4,096-query batch, cold.)
+template <int kW>
+__global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
+k_match_verify(AkvTreeView tree, const int32_t* __restrict__ tokens, int64_t n_slots, int32_t block_size,
+               StagedScratch sc, int32_t* __restrict__ out_node, int32_t* __restrict__ out_len,
+               int64_t* __restrict__ out_compared, AkvStatus* st) {
+  const int lane = threadIdx.x & 31;
+  const int64_t slot = static_cast<int64_t>(blockIdx.x) * kMatchWarpsPerCta + (threadIdx.x >> 5);
+  if (slot >= n_slots || akv_failed(st)) return;
+  const int4 r0 = sc.wins[2 * slot];
+  if (r0.x < 0) return;
+  const int4 r1 = sc.wins[2 * slot + 1];
+  verify_window<kW>(tree, tokens, r0, r1, sc, block_size, out_node, out_len, out_compared, st, lane);
 }
 
 // ── tree changes built on the device ───────────────────────────────────────
