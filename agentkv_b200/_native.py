@@ -25,6 +25,7 @@ AKV_ERR_DEPENDENT_PAIRS = 7
 AKV_ERR_CUDA = 8
 AKV_ERR_TIMEOUT = 9
 AKV_ERR_TREE = 10
+AKV_ERR_MIRROR = 11
 
 ERROR_NAMES = {
     AKV_OK: "ok",
@@ -38,6 +39,7 @@ ERROR_NAMES = {
     AKV_ERR_CUDA: "CUDA error",
     AKV_ERR_TIMEOUT: "device wait timed out",
     AKV_ERR_TREE: "malformed tree replica",
+    AKV_ERR_MIRROR: "replayed per-call log disagrees with the device state",
 }
 
 # ── ctl word indices ─────────────────────────────────────────────────────────
@@ -58,6 +60,8 @@ CTL_ADVANCES = 13
 CTL_RELEASED = 14
 CTL_WORDS = 16
 AUX_WORDS = 2048
+LOG_HEADER_WORDS = 8
+OP_ALLOC, OP_INCREF, OP_DECREF, OP_COW, OP_RELEASE, OP_ADVANCE = range(1, 7)
 NOALLOC_MAX_BLOCKS = 262144
 MAX_FANOUT_LEVELS = 16  # AKV_MAX_FANOUT_LEVELS
 MATCH_PIPELINED = 0x100  # AKV_MATCH_PIPELINED
@@ -182,6 +186,20 @@ SIGNATURES = {
         C.c_int,
         [C.POINTER(AkvTreeView), _P, _P, _I32, _I32, _P, _P, _P, _P, _P, _I32, _I32, _P, _I64, _I32, _P, _P],
     ),
+    "akv_mirror_create": (C.c_void_p, [_I32]),
+    "akv_mirror_destroy": (None, [_P]),
+    "akv_mirror_load": (C.c_int, [_P, _P, _P, _P, _P, _P]),
+    "akv_mirror_alloc": (C.c_int, [_P, _I32, C.POINTER(AkvTick), _P, _P]),
+    "akv_mirror_incref": (C.c_int, [_P, _P, _I32, C.POINTER(AkvTick), _P]),
+    "akv_mirror_decref": (C.c_int, [_P, _P, _I32, C.POINTER(AkvTick), _P, _P, _P]),
+    "akv_mirror_cow": (C.c_int, [_P, _I32, C.POINTER(AkvTick), _P, _P]),
+    "akv_mirror_release": (C.c_int, [_P, _I64]),
+    "akv_mirror_advance": (C.c_int, [_P, C.POINTER(AkvTick)]),
+    "akv_mirror_read": (C.c_int, [_P, _P, _P, _P, _P, _P]),
+    "akv_mirror_ref": (C.c_int32, [_P, _I32]),
+    "akv_mirror_log_words": (C.c_int64, [_P]),
+    "akv_mirror_take_log": (C.c_int, [_P, _P, _I64]),
+    "akv_alloc_replay": (C.c_int, [C.POINTER(AkvAllocState), _P, _I64, _P, _P]),
     "akv_match_staged_scratch_bytes": (C.c_int64, [_I32, _I64, _I32]),
     "akv_match_prefix_staged": (
         C.c_int,

@@ -67,6 +67,40 @@ AKV_DEV int64_t lane0_load64(const int64_t* p, int lane) {
   return __shfl_sync(kFull, v, 0);
 }
 
+AKV_DEV Cursors load_cursors(const Agents& g) {
+  const int64_t* ctl = g.st.ctl;
+  Cursors c;
+  c.left = lane0_load64(&ctl[AKV_CTL_FREE_LEFT], g.lane);
+  c.size = lane0_load64(&ctl[AKV_CTL_FREE_SIZE], g.lane);
+  c.head = lane0_load64(&ctl[AKV_CTL_LIMBO_HEAD], g.lane);
+  c.rel = lane0_load64(&ctl[AKV_CTL_LIMBO_REL], g.lane);
+  c.tail = lane0_load64(&ctl[AKV_CTL_LIMBO_TAIL], g.lane);
+  c.ops = lane0_load64(&ctl[AKV_CTL_OPS], g.lane);
+  c.epoch = lane0_load64(&ctl[AKV_CTL_EPOCH], g.lane);
+  c.allocs = lane0_load64(&ctl[AKV_CTL_ALLOCS], g.lane);
+  c.frees = lane0_load64(&ctl[AKV_CTL_FREES], g.lane);
+  c.peak = lane0_load64(&ctl[AKV_CTL_PEAK], g.lane);
+  c.advances = lane0_load64(&ctl[AKV_CTL_ADVANCES], g.lane);
+  c.released = lane0_load64(&ctl[AKV_CTL_RELEASED], g.lane);
+  return c;
+}
+
+// Lane 0 only.
+AKV_DEV void store_cursors(const Cursors& c, int64_t* ctl) {
+  ctl[AKV_CTL_FREE_LEFT] = c.left;
+  ctl[AKV_CTL_FREE_SIZE] = c.size;
+  ctl[AKV_CTL_LIMBO_HEAD] = c.head;
+  ctl[AKV_CTL_LIMBO_REL] = c.rel;
+  ctl[AKV_CTL_LIMBO_TAIL] = c.tail;
+  ctl[AKV_CTL_OPS] = c.ops;
+  ctl[AKV_CTL_EPOCH] = c.epoch;
+  ctl[AKV_CTL_ALLOCS] = c.allocs;
+  ctl[AKV_CTL_FREES] = c.frees;
+  ctl[AKV_CTL_PEAK] = c.peak;
+  ctl[AKV_CTL_ADVANCES] = c.advances;
+  ctl[AKV_CTL_RELEASED] = c.released;
+}
+
 AKV_DEV bool advance_allowed(const Cursors& c, const AkvTick& tk) {
   // a reader always holds the current epoch: the epoch moves only when none is open
   return !tk.readers_active || c.epoch > tk.readers_max;
@@ -74,12 +108,15 @@ AKV_DEV bool advance_allowed(const Cursors& c, const AkvTick& tk) {
 
 // The reclaimer's _try_retire: pending ids retired before the oldest reader
 // (all of them when no reader is open) become deferred, in FIFO order.
-AKV_DEV void try_retire(Cursors& c, const Agents& g) {
-  const int64_t safe = g.tk.readers_active ? g.tk.readers_min : c.epoch + 1;
+AKV_DEV void try_retire_to(Cursors& c, const Agents& g, int64_t safe) {
   while (c.rel < c.tail && lane0_load64(&g.st.limbo_epochs[wrapn(c.rel, g.N)], g.lane) < safe) {
     ++c.rel;
     ++c.released;
   }
+}
+
+AKV_DEV void try_retire(Cursors& c, const Agents& g) {
+  try_retire_to(c, g, g.tk.readers_active ? g.tk.readers_min : c.epoch + 1);
 }
 
 // _drain_deferred: the deferred ids go to the left of the free deque, keeping
@@ -141,9 +178,11 @@ AKV_DEV int32_t op_alloc(Cursors& c, const Agents& g) {
 
 // fork's inc_ref of every block of `src` (n ids), then `dst` holds the same
 // table.  Validated first: AKV_ERR_NOT_ALLOCATED / OUT_OF_RANGE change nothing.
+// With dst == nullptr only the increments and their ticks (the inc_ref
+// batch of a replayed log).
 AKV_DEV int fork_into(Cursors& c, const Agents& g, const int32_t* src, int32_t n, int32_t* dst, int32_t* dst_len,
                       int32_t& bad_id) {
-  if (n > g.cap) {
+  if (dst != nullptr && n > g.cap) {
     bad_id = n;
     return AKV_ERR_INVALID_ARG;
   }
@@ -166,12 +205,76 @@ AKV_DEV int fork_into(Cursors& c, const Agents& g, const int32_t* src, int32_t n
     const int32_t x = i < n ? vload(&src[i]) : -1;
     const uint32_t peers = __match_any_sync(kFull, x);
     if (x >= 0 && g.lane == __ffs(peers) - 1) atomicAdd(&g.st.ref_counts[x], __popc(peers));
-    if (i < n) dst[i] = x;
+    if (i < n && dst != nullptr) dst[i] = x;
   }
   __syncwarp();
-  if (g.lane == 0) *dst_len = n;
+  if (g.lane == 0 && dst_len != nullptr) *dst_len = n;
   __syncwarp();
   ticks(c, g, n);
+  return AKV_OK;
+}
+
+// n dec_ref() calls in order (ids may repeat): a block whose count reaches
+// zero retires at its own op.  32 ids at a time; a chunk holding a repeated
+// id goes one id at a time, so that the retirement lands on the id's last
+// occurrence.  A count already at zero is AKV_ERR_DOUBLE_FREE (the counts
+// before it are applied: the host validated the batch, so this means the
+// states differ).
+AKV_DEV int dec_ids(Cursors& c, const Agents& g, const int32_t* ids, int32_t n, int32_t& bad_id) {
+  int64_t done = 0;  // ops ticked so far
+  for (int32_t i0 = 0; i0 < n; i0 += 32) {
+    const int32_t i = i0 + g.lane;
+    int32_t x = i < n ? ids[i] : -1;
+    const uint32_t oob = __ballot_sync(kFull, i < n && static_cast<uint32_t>(x) >= static_cast<uint32_t>(g.N));
+    if (oob) {
+      bad_id = __shfl_sync(kFull, x, __ffs(oob) - 1);
+      return AKV_ERR_OUT_OF_RANGE;
+    }
+    const uint32_t peers = __match_any_sync(kFull, x);
+    const bool repeated = __any_sync(kFull, i < n && __popc(peers) > 1);
+    if (!repeated) {
+      const int32_t old = i < n ? atomicSub(&g.st.ref_counts[x], 1) : 1;
+      const uint32_t badm = __ballot_sync(kFull, old < 1);
+      if (badm) {
+        bad_id = __shfl_sync(kFull, x, __ffs(badm) - 1);
+        return AKV_ERR_DOUBLE_FREE;
+      }
+      uint32_t ret = __ballot_sync(kFull, i < n && old == 1);
+      while (ret) {
+        const int l = __ffs(ret) - 1;
+        ret &= ret - 1;
+        const int32_t p = i0 + l;
+        ticks(c, g, p - done);
+        retire(c, g, __shfl_sync(kFull, x, l));
+        ticks(c, g, 1);
+        done = p + 1;
+      }
+    } else {
+      const int32_t m = n - i0 < 32 ? n - i0 : 32;
+      for (int l = 0; l < m; ++l) {
+        const int32_t xl = __shfl_sync(kFull, x, l);
+        int32_t old = 0;
+        if (g.lane == 0) {
+          old = *reinterpret_cast<volatile int32_t*>(&g.st.ref_counts[xl]);
+          if (old >= 1) g.st.ref_counts[xl] = old - 1;
+        }
+        old = __shfl_sync(kFull, old, 0);
+        __syncwarp();
+        if (old < 1) {
+          bad_id = xl;
+          return AKV_ERR_DOUBLE_FREE;
+        }
+        if (old == 1) {
+          const int32_t p = i0 + l;
+          ticks(c, g, p - done);
+          retire(c, g, xl);
+          ticks(c, g, 1);
+          done = p + 1;
+        }
+      }
+    }
+  }
+  ticks(c, g, n - done);
   return AKV_OK;
 }
 
@@ -223,19 +326,7 @@ k_agent_steps(Agents g, const int32_t* __restrict__ actions, const int32_t* __re
   g.lane = threadIdx.x;
   if (akv_failed(g.status)) return;
   int64_t* ctl = g.st.ctl;
-  Cursors c;
-  c.left = lane0_load64(&ctl[AKV_CTL_FREE_LEFT], g.lane);
-  c.size = lane0_load64(&ctl[AKV_CTL_FREE_SIZE], g.lane);
-  c.head = lane0_load64(&ctl[AKV_CTL_LIMBO_HEAD], g.lane);
-  c.rel = lane0_load64(&ctl[AKV_CTL_LIMBO_REL], g.lane);
-  c.tail = lane0_load64(&ctl[AKV_CTL_LIMBO_TAIL], g.lane);
-  c.ops = lane0_load64(&ctl[AKV_CTL_OPS], g.lane);
-  c.epoch = lane0_load64(&ctl[AKV_CTL_EPOCH], g.lane);
-  c.allocs = lane0_load64(&ctl[AKV_CTL_ALLOCS], g.lane);
-  c.frees = lane0_load64(&ctl[AKV_CTL_FREES], g.lane);
-  c.peak = lane0_load64(&ctl[AKV_CTL_PEAK], g.lane);
-  c.advances = lane0_load64(&ctl[AKV_CTL_ADVANCES], g.lane);
-  c.released = lane0_load64(&ctl[AKV_CTL_RELEASED], g.lane);
+  Cursors c = load_cursors(g);
   const int64_t stride = 2 + 2 * static_cast<int64_t>(pairs_cap);
   int rc = AKV_OK;
   int32_t fail_at = 0, bad_id = -1, observed = 0;
@@ -328,26 +419,126 @@ k_agent_steps(Agents g, const int32_t* __restrict__ actions, const int32_t* __re
     __syncwarp();
   }
   if (g.lane == 0) {
-    ctl[AKV_CTL_FREE_LEFT] = c.left;
-    ctl[AKV_CTL_FREE_SIZE] = c.size;
-    ctl[AKV_CTL_LIMBO_HEAD] = c.head;
-    ctl[AKV_CTL_LIMBO_REL] = c.rel;
-    ctl[AKV_CTL_LIMBO_TAIL] = c.tail;
-    ctl[AKV_CTL_OPS] = c.ops;
-    ctl[AKV_CTL_EPOCH] = c.epoch;
-    ctl[AKV_CTL_ALLOCS] = c.allocs;
-    ctl[AKV_CTL_FREES] = c.frees;
-    ctl[AKV_CTL_PEAK] = c.peak;
-    ctl[AKV_CTL_ADVANCES] = c.advances;
-    ctl[AKV_CTL_RELEASED] = c.released;
+    store_cursors(c, ctl);
     if (rc != AKV_OK) akv_fail(g.status, rc, fail_at, bad_id, observed);
+  }
+}
+
+
+// ── replay of the host mirror's op log ─────────────────────────────────────
+// The per-call operations the host mirror (akv_mirror.cu) answered, applied
+// here in order with the same rules; every id the host handed out is checked
+// against the one this replay hands out.  Any difference, or an operation
+// the device state refuses, is AKV_ERR_MIRROR (the replay stops there).
+__global__ void __launch_bounds__(32)
+k_alloc_replay(Agents g, const int32_t* __restrict__ log, int64_t n_words) {
+  g.lane = threadIdx.x;
+  if (akv_failed(g.status)) return;
+  Cursors c = load_cursors(g);
+  int rc = AKV_OK;
+  int32_t bad_id = -1, observed = 0;
+  int64_t w = 0;
+  while (w < n_words && rc == AKV_OK) {
+    rc = AKV_ERR_MIRROR;  // until the record is applied
+    if (w + AKV_LOG_HEADER_WORDS > n_words) break;
+    const int32_t* h = log + w;
+    const int32_t op = h[0], n = h[1];
+    if (n < 0 || w + AKV_LOG_HEADER_WORDS + n > n_words) break;
+    g.tk.readers_min = (static_cast<int64_t>(h[3]) << 32) | static_cast<uint32_t>(h[2]);
+    g.tk.readers_max = (static_cast<int64_t>(h[5]) << 32) | static_cast<uint32_t>(h[4]);
+    g.tk.epoch_interval = h[6];
+    g.tk.readers_active = h[7];
+    const int32_t* p = h + AKV_LOG_HEADER_WORDS;
+    bad_id = op;
+    if ((op == AKV_OP_ALLOC || op == AKV_OP_INCREF || op == AKV_OP_DECREF || op == AKV_OP_COW ||
+         op == AKV_OP_ADVANCE) && g.tk.epoch_interval <= 0)
+      break;
+    if (op == AKV_OP_ALLOC) {
+      int32_t i = 0;
+      for (; i < n; ++i) {
+        const int32_t want = p[i];
+        const int32_t got = op_alloc(c, g);
+        if (got != want) {
+          bad_id = want;
+          observed = got;
+          break;
+        }
+      }
+      if (i < n) break;
+    } else if (op == AKV_OP_INCREF) {
+      int32_t bad = -1;
+      if (fork_into(c, g, p, n, nullptr, nullptr, bad) != AKV_OK) {
+        bad_id = bad;
+        break;
+      }
+    } else if (op == AKV_OP_DECREF) {
+      int32_t bad = -1;
+      if (dec_ids(c, g, p, n, bad) != AKV_OK) {
+        bad_id = bad;
+        break;
+      }
+    } else if (op == AKV_OP_COW) {
+      if (n != 2) break;
+      const int32_t x = p[0], want = p[1];
+      const int32_t r = static_cast<uint32_t>(x) < static_cast<uint32_t>(g.N) ? lane0_load(&g.st.ref_counts[x], g.lane)
+                                                                                : -1;
+      if (r <= 1) {
+        bad_id = x;
+        observed = r;
+        break;
+      }
+      const int32_t got = op_alloc(c, g);
+      if (got != want) {
+        bad_id = want;
+        observed = got;
+        break;
+      }
+      if (g.lane == 0) g.st.ref_counts[x] = r - 1;
+      __syncwarp();
+      ticks(c, g, 1);
+    } else if (op == AKV_OP_RELEASE) {
+      try_retire_to(c, g, g.tk.readers_min);
+    } else if (op == AKV_OP_ADVANCE) {
+      if (advance_allowed(c, g.tk)) {
+        ++c.epoch;
+        ++c.advances;
+      }
+      try_retire(c, g);
+    } else {
+      break;
+    }
+    rc = AKV_OK;
+    w += AKV_LOG_HEADER_WORDS + n;
+  }
+  if (g.lane == 0) {
+    store_cursors(c, g.st.ctl);
+    if (rc != AKV_OK) akv_fail(g.status, rc, static_cast<int32_t>(w), bad_id, observed, w);
   }
 }
 
 }  // namespace
 
 int akv_agents_prepare() {
-  return akv_load_kernel(reinterpret_cast<const void*>(k_agent_steps), "akv_prepare: k_agent_steps");
+  if (int rc = akv_load_kernel(reinterpret_cast<const void*>(k_agent_steps), "akv_prepare: k_agent_steps"))
+    return rc;
+  return akv_load_kernel(reinterpret_cast<const void*>(k_alloc_replay), "akv_prepare: k_alloc_replay");
+}
+
+extern "C" int akv_alloc_replay(const AkvAllocState* st, const int32_t* log, int64_t n_words, AkvStatus* status,
+                                void* stream) {
+  AKV_ARG_CHECK(st != nullptr && st->ref_counts && st->free_ring && st->limbo_ids && st->limbo_epochs && st->ctl &&
+                    st->total_blocks > 0,
+                "akv_alloc_replay: incomplete allocator state");
+  AKV_ARG_CHECK(status != nullptr, "akv_alloc_replay: status is NULL");
+  AKV_ARG_CHECK(n_words >= 0 && (n_words == 0 || log != nullptr), "akv_alloc_replay: bad log");
+  if (n_words == 0) return AKV_OK;
+  Agents g{};
+  g.st = *st;
+  g.N = st->total_blocks;
+  g.status = status;
+  k_alloc_replay<<<1, 32, 0, akv_stream(stream)>>>(g, log, n_words);
+  AKV_LAUNCH_CHECK("akv_alloc_replay");
+  return AKV_OK;
 }
 
 extern "C" int akv_agent_steps(const AkvAllocState* st, const AkvTick* tick, int32_t* tables, int32_t* lens,

@@ -50,7 +50,8 @@ enum {
   AKV_ERR_DEPENDENT_PAIRS = 7, /* a batch's dst is another pair's src/dst */
   AKV_ERR_CUDA = 8,            /* a CUDA runtime call failed (host) */
   AKV_ERR_TIMEOUT = 9,         /* a bounded device wait gave up */
-  AKV_ERR_TREE = 10            /* malformed tree replica (bad node index) */
+  AKV_ERR_TREE = 10,           /* malformed tree replica (bad node index) */
+  AKV_ERR_MIRROR = 11          /* a replayed op log disagrees with the device state */
 };
 
 /* Device-side status record (32 bytes).  code = first AKV_ERR_* seen,
@@ -562,6 +563,69 @@ AKV_API int akv_match_prefix_staged(const AkvTreeView* tree, const int32_t* toke
                                     int64_t* out_compared, const int32_t* order,
                                     int32_t window_tokens, void* scratch, int64_t scratch_bytes,
                                     AkvStatus* status, void* stream);
+
+/* ── per-call operations on a host mirror ──────────────────────────────── */
+/* A host copy of the allocator state that answers the per-call API at once
+ * (SlabAllocator.alloc / inc_ref / dec_ref, ensure_mutable_block, the
+ * reclaimer's release and advance: agentkv/core/slab_allocator.py:194-278,
+ * 416-437; reclamation.py:88-173), in the reference's sequential order, and
+ * logs each call for akv_alloc_replay.  Errors are returned at the call
+ * (nothing changed, nothing logged) with `err` filled as the device status
+ * would be.  Not thread-safe: the caller serialises calls (one lock). */
+typedef struct AkvMirror AkvMirror;
+
+/* Op log records: AKV_LOG_HEADER_WORDS int32 words {op, n, readers_min lo,
+ * hi, readers_max lo, hi, epoch_interval, readers_active}, then n words:
+ * ALLOC the ids handed out; INCREF / DECREF the ids; COW {block, new block};
+ * RELEASE (n = 0) the safe epoch in the readers_min words; ADVANCE (n = 0). */
+#define AKV_LOG_HEADER_WORDS 8
+enum {
+  AKV_OP_ALLOC = 1,
+  AKV_OP_INCREF = 2,
+  AKV_OP_DECREF = 3,
+  AKV_OP_COW = 4,
+  AKV_OP_RELEASE = 5,
+  AKV_OP_ADVANCE = 6
+};
+
+/* A mirror in the constructor state (akv_alloc_init's); NULL on failure. */
+AKV_API AkvMirror* akv_mirror_create(int32_t total_blocks);
+AKV_API void akv_mirror_destroy(AkvMirror* m);
+/* Replace the mirror's state with host copies of the device arrays
+ * (ref_counts, free_ring, limbo_ids [N] int32, limbo_epochs [N] int64,
+ * ctl [AKV_CTL_WORDS]); clears the log. */
+AKV_API int akv_mirror_load(AkvMirror* m, const int32_t* ref_counts, const int32_t* free_ring,
+                            const int32_t* limbo_ids, const int64_t* limbo_epochs, const int64_t* ctl);
+/* n alloc() calls: out_ids[n]; AKV_ERR_EXHAUSTED when they would run dry. */
+AKV_API int akv_mirror_alloc(AkvMirror* m, int32_t n, const AkvTick* tick, int32_t* out_ids, AkvStatus* err);
+/* n inc_ref() calls, all or nothing. */
+AKV_API int akv_mirror_incref(AkvMirror* m, const int32_t* ids, int32_t n, const AkvTick* tick, AkvStatus* err);
+/* n dec_ref() calls, all or nothing; the retired ids in order and their count. */
+AKV_API int akv_mirror_decref(AkvMirror* m, const int32_t* ids, int32_t n, const AkvTick* tick,
+                              int32_t* retired_out, int32_t* n_retired, AkvStatus* err);
+/* ensure_mutable on one block: *out_block is the block itself when its
+ * count is 1 (or 0), else a fresh block (alloc, then dec_ref of the old one;
+ * the data copy is the caller's). */
+AKV_API int akv_mirror_cow(AkvMirror* m, int32_t block, const AkvTick* tick, int32_t* out_block, AkvStatus* err);
+/* The reclaimer's release of pending ids older than safe_before_epoch. */
+AKV_API int akv_mirror_release(AkvMirror* m, int64_t safe_before_epoch);
+/* EpochReclaimer.maybe_advance. */
+AKV_API int akv_mirror_advance(AkvMirror* m, const AkvTick* tick);
+/* Copies of the state, in the device arrays' layout: the control words
+ * (AKV_CTL_WORDS int64), refcounts, free ring, limbo ids ([N] int32) and
+ * limbo epochs ([N] int64); any may be NULL. */
+AKV_API int akv_mirror_read(const AkvMirror* m, int64_t* ctl, int32_t* ref_counts, int32_t* free_ring,
+                            int32_t* limbo_ids, int64_t* limbo_epochs);
+/* One block's refcount (INT32_MIN for a bad id). */
+AKV_API int32_t akv_mirror_ref(const AkvMirror* m, int32_t block);
+/* Words logged since the last take; copy them out (cap >= the count) and clear. */
+AKV_API int64_t akv_mirror_log_words(const AkvMirror* m);
+AKV_API int akv_mirror_take_log(AkvMirror* m, int32_t* dst, int64_t cap);
+/* Apply an op log (device memory, n_words int32) to the device state with
+ * the same rules, one warp, checking each logged id against its own:
+ * AKV_ERR_MIRROR in `status` at the first difference.  One launch. */
+AKV_API int akv_alloc_replay(const AkvAllocState* st, const int32_t* log, int64_t n_words, AkvStatus* status,
+                             void* stream);
 
 #ifdef __cplusplus
 }
