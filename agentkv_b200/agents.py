@@ -111,12 +111,12 @@ class DeviceAgents:
             self._keep = dev_up
             a = self.alloc
             with a._lock:
+                a._device_op()  # the per-call log first; the mirror is reloaded when next needed
                 N.check(N.lib.akv_agent_steps(
                     a._state, a._tick(), self.tables.data_ptr(), self.lens.data_ptr(), self.n, self.cap,
                     self.root_table.data_ptr(), self.root_len, dev_up.data_ptr() + 4 * (n_steps + 1),
                     dev_up.data_ptr(), n_steps, self._pairs_buf.data_ptr(), cap, a._status.data_ptr(),
                     stream_handle(self.device)))
-                a._queued()
         return self._pairs_buf[:words].view(n_steps, 2 + 2 * cap)
 
     def _retire_slot(self, slot: int) -> None:

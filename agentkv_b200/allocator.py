@@ -13,14 +13,23 @@ mutate lives on the GPU:
 * ``_limbo_*``       retired ids waiting for the reclaimer (deferred + pending);
 * ``_ctl``           cursors and counters (op count, epoch, stats).
 
-Every operation is a launch of the C ABI (akv_alloc_batch / akv_incref_batch
-/ akv_decref_batch / akv_cow_batch / akv_limbo_release / akv_epoch_advance)
-that reproduces the reference's sequential semantics, including the order in
-which ids leave and re-enter the free list.  The single-op methods wait for
-their result (they return ids / booleans or raise at once, like the
-reference); the ``*_batch`` methods enqueue one launch for a whole batch and
-return device tensors without waiting — device-detected errors then surface
-at the next waiting call (or ``check()``).
+The batched operations are launches of the C ABI (akv_alloc_batch /
+akv_incref_batch / akv_decref_batch / akv_cow_batch / akv_limbo_release /
+akv_epoch_advance) that reproduce the reference's sequential semantics,
+including the order in which ids leave and re-enter the free list; they
+return device tensors without waiting, and device-detected errors surface at
+``check()``.
+
+The per-call methods (``alloc``, ``inc_ref``, ``dec_ref``, ``cow_one``,
+``ref_count``, the read sections, and ``*_batch`` calls with host ids) are
+answered by a host mirror of the same state (``HostMirror``, akv_mirror.cu),
+which applies each call at once with the same rules and raises the
+reference's exceptions at the call, without a device round trip.  The
+mirror logs the calls; before anything on the device reads or changes the
+allocator state, the log is replayed there in one launch (akv_alloc_replay,
+which checks every id the host handed out).  After device-side batches (the
+fan-out planners, DeviceAgents, batches of device ids) the mirror is reloaded
+from the device at the next per-call method, with one wait.
 
 The pool itself must live on a CUDA device, or on ``meta`` for the
 metadata-only pools of the vLLM / SGLang adapters (their free list and
@@ -40,11 +49,14 @@ from . import _native as N
 from .config import PoolConfig, torch_dtype
 from .kernels import copy_blocks as _copy_blocks
 from .kernels import stream_handle
+from .mirror import HostMirror, MirrorRefused
 from .reclamation import EpochReclaimer
 
 INVALID_BLOCK: int = -1
 
 _INT64_MAX = (1 << 63) - 1
+_LOG_FLUSH_WORDS = 1 << 15  # the op log is replayed on the device once it holds this many words
+_MIRROR_MAX_BATCH = 4096  # larger batches of host ids run as device batches (one warp replays the log)
 
 
 class BlockHandle:
@@ -178,13 +190,15 @@ class SlabAllocator:
         self._h_in_ptr = self._h_in.data_ptr()
         self._h_ref = torch.zeros(2, dtype=i32, pin_memory=True)
         self._h_ref_np = self._h_ref.numpy()
-        # The device epoch as of the last wait, kept on the host so that
-        # enter_read_section needs no read-back: every wait also brings back
-        # the control words, and the host applies the epoch changes it can
-        # foresee (maybe_advance_epoch); a batch queued without a wait makes
-        # it unknown until the next wait.
-        self._mirror_epoch = 0
-        self._mirror_ok = True
+        # The host mirror: current while _live (the device state is the
+        # mirror's minus its unreplayed log); _refused marks a batch the
+        # mirror refused, whose error waits in the device status for check().
+        self._mirror = HostMirror(n)
+        self._live = True
+        self._refused = False
+        self._log_np = np.zeros(_LOG_FLUSH_WORDS + 4096, np.int32)
+        self._log_stage = _IdStage(dev, cap=1 << 17)
+        self._h_state: Optional[torch.Tensor] = None  # pinned read-back of the device state
         self._state = N.AkvAllocState(
             self._ref_counts.data_ptr(), self._free_ring.data_ptr(), self._limbo_ids.data_ptr(),
             self._limbo_epochs.data_ptr(), self._ctl.data_ptr(), self._scratch_count.data_ptr(),
@@ -220,21 +234,89 @@ class SlabAllocator:
         off = 8 * N.CTL_OPS
         N.check(N.lib.akv_copy_wait(self._h_ctlio_ptr + off, self._ctlio_ptr + off, 8 * hi - off, 1, 1,
                                     self._stream()))
-        self._mirror_epoch = int(self._h_ctlio_np[N.CTL_EPOCH])
-        self._mirror_ok = True
         return self._h_io_np[: 8 + n_out].copy()
 
-    def _queued(self) -> None:
-        """A batch was queued without a wait: the host no longer knows the
-        epoch until the next wait."""
-        self._mirror_ok = False
+    # ── host mirror plumbing ──────────────────────────────────────────────────
+    def _flush(self) -> None:
+        """Replay the mirror's op log on the device (one upload, one launch,
+        no wait)."""
+        k = self._mirror.log_words()
+        if k == 0:
+            return
+        if k > len(self._log_np):
+            self._log_np = np.zeros(2 * k, np.int32)
+        self._mirror.take_log(self._log_np)
+        d = self._log_stage.put(self._log_np[:k])
+        N.check(N.lib.akv_alloc_replay(self._state, d.data_ptr(), k, self._status.data_ptr(), self._stream()))
+
+    def _maybe_flush(self) -> None:
+        if self._mirror.log_words() >= _LOG_FLUSH_WORDS:
+            self._flush()
+
+    def _device_op(self) -> None:
+        """Before a device-side operation on the allocator state: the device
+        catches up with the mirror's log, and the mirror is stale until it is
+        next needed (then reloaded from the device)."""
+        self._flush()
+        self._live = False
+
+    def _host(self) -> HostMirror:
+        """The mirror, current: reloaded from the device (one wait) after
+        device-side batches."""
+        if not self._live:
+            n = self._cfg.total_blocks
+            if self._h_state is None:
+                self._h_state = torch.empty(3 * n + 2 * (n + N.CTL_WORDS), dtype=torch.int32, pin_memory=True)
+            h = self._h_state
+            parts = (self._ref_counts, self._free_ring, self._limbo_ids)
+            for i, t in enumerate(parts):
+                h[i * n : (i + 1) * n].copy_(t, non_blocking=True)
+            h64 = h[3 * n :].view(torch.int64)
+            h64[:n].copy_(self._limbo_epochs, non_blocking=True)
+            h64[n:].copy_(self._ctl, non_blocking=True)
+            torch.cuda.current_stream(self._dev).synchronize()
+            a = h.numpy()
+            a64 = h64.numpy()
+            self._mirror.load(a[:n], a[n : 2 * n], a[2 * n : 3 * n], a64[:n], a64[n:])
+            self._live = True
+        return self._mirror
+
+    def _refuse(self, e: MirrorRefused, op: str, batch: bool) -> Exception:
+        """A call the mirror refused.  A per-call method raises it at once;
+        a batch posts it to the device status instead (after the log, so the
+        calls before it still replay), where the device's own later batches
+        see it and do nothing, and check() raises it."""
+        exc = self._exception(e.code, e.id, e.observed, op, e.index)
+        if batch:
+            self._flush()
+            self._h_in_np[:8] = 0
+            self._h_in_np[:4] = (e.code, e.index, e.id, e.observed)
+            N.check(N.lib.akv_copy_wait(self._status.data_ptr(), self._h_in_ptr, N.STATUS_BYTES, 0, 0,
+                                        self._stream()))
+            torch.cuda.current_stream(self._dev).synchronize()  # the staging words are reused
+            self._refused = True
+        return exc
+
+    def _pending(self) -> None:
+        """A per-call method after a refused batch raises its error, as the
+        next waiting call would have."""
+        if self._refused:
+            self.check()
+
+    def _host_ids(self, ids) -> Optional[np.ndarray]:
+        """The ids as a host int32 array, or None when they are device ids."""
+        if isinstance(ids, torch.Tensor):
+            if ids.device.type != "cpu":
+                return None
+            return ids.numpy().astype(np.int32, copy=False).reshape(-1)
+        return np.asarray(ids, np.int32).reshape(-1)
 
     def epoch(self) -> int:
-        """The reclaimer's current epoch: from the host mirror when no batch
-        has been queued since the last wait, else read from the device."""
+        """The reclaimer's current epoch (from the mirror when it is current,
+        else read from the device)."""
         with self._lock:
-            if self._mirror_ok:
-                return self._mirror_epoch
+            if self._live:
+                return self._mirror.ctl_word(N.CTL_EPOCH)
             return int(self.ctl()[N.CTL_EPOCH])
 
     def _stage_ids(self, ids) -> int:
@@ -293,72 +375,76 @@ class SlabAllocator:
         if handle.block_id < 0 or handle.block_id >= self._cfg.total_blocks:
             raise ValueError(f"block_id {handle.block_id} out of range [0, {self._cfg.total_blocks})")
 
-    # ── single operations (reference semantics, wait for the result) ──────────
+    # ── single operations (reference semantics, answered by the host mirror) ──
     def alloc(self) -> BlockHandle:
         """Claim a free block (ref_count 1); MemoryError when exhausted."""
         with self._lock:
-            out = self._io[8:].data_ptr()
-            N.check(N.lib.akv_alloc_batch(self._state, 1, out, self._tick(), self._status.data_ptr(),
-                                          self._stream()))
-            io = self._sync_io(1)
-            self._raise_status(io, "alloc")
-            return BlockHandle(int(io[8]))
+            self._pending()
+            try:
+                ids = self._host().alloc(1, self._tick())
+            except MirrorRefused as e:
+                raise self._refuse(e, "alloc", False) from None
+            self._maybe_flush()
+            return BlockHandle(int(ids[0]))
 
     def alloc_many(self, n: int) -> List[int]:
-        """n alloc() calls in one launch and one wait: the ids, in the order
-        the calls would return them; MemoryError (nothing taken) when fewer
-        than n are free."""
+        """n alloc() calls: the ids, in the order the calls would return
+        them; MemoryError (nothing taken) when fewer than n are free."""
         with self._lock:
             if n <= 0:
                 return []
-            if n <= 32:
-                out = self._io[8 : 8 + n]
-                N.check(N.lib.akv_alloc_batch(self._state, n, out.data_ptr(), self._tick(),
-                                              self._status.data_ptr(), self._stream()))
-                io = self._sync_io(n)
-                self._raise_status(io, "alloc")
-                return io[8 : 8 + n].tolist()
-            out = torch.empty(n, dtype=torch.int32, device=self._dev)
-            N.check(N.lib.akv_alloc_batch(self._state, n, out.data_ptr(), self._tick(), self._status.data_ptr(),
-                                          self._stream()))
-            h = torch.empty(n, dtype=torch.int32, pin_memory=True)
-            h.copy_(out, non_blocking=True)
-            self._raise_status(self._sync_io(0), "alloc")
-            return h.tolist()
+            self._pending()
+            try:
+                ids = self._host().alloc(n, self._tick())
+            except MirrorRefused as e:
+                raise self._refuse(e, "alloc", False) from None
+            self._maybe_flush()
+            return ids.tolist()
 
     def cow_one(self, block_id: int) -> int:
-        """ensure_mutable on one residual block with one wait: the block the
-        slot owns afterwards (a fresh copy when the block was shared)."""
+        """ensure_mutable on one residual block: the block the slot owns
+        afterwards (a fresh copy when the block was shared; the data copy is
+        enqueued on the device)."""
         with self._lock:
-            ptr = self._stage_ids([block_id])
-            meta = self._kv_data.device.type == "meta"
-            io_ptr = self._io.data_ptr()
-            N.check(N.lib.akv_cow_batch(
-                self._state, None if meta else self._kv_data.data_ptr(), 0 if meta else self._cfg.bytes_per_block,
-                ptr, 1, io_ptr + 8 * 4, io_ptr + 9 * 4, io_ptr + 10 * 4, self._tick(), self._status.data_ptr(),
-                self._stream()))
-            io = self._sync_io(2)
-            self._raise_status(io, "ensure_mutable_block")
-            return int(io[8])
+            self._pending()
+            try:
+                nb = self._host().cow(int(block_id), self._tick())
+            except MirrorRefused as e:
+                raise self._refuse(e, "ensure_mutable_block", False) from None
+            if nb != block_id and self._kv_data.device.type != "meta":
+                self._copy_pair(int(block_id), nb)
+            self._maybe_flush()
+            return nb
 
     def inc_ref(self, handle: BlockHandle) -> None:
         self._validate_handle(handle)
         with self._lock:
-            ptr = self._stage_ids([handle.block_id])
-            N.check(N.lib.akv_incref_batch(self._state, ptr, 1, self._tick(), self._status.data_ptr(),
-                                           self._stream()))
-            self._raise_status(self._sync_io(0), "inc_ref")
+            self._pending()
+            try:
+                self._host().incref(np.asarray([handle.block_id], np.int32), self._tick())
+            except MirrorRefused as e:
+                raise self._refuse(e, "inc_ref", False) from None
+            self._maybe_flush()
 
     def dec_ref(self, handle: BlockHandle) -> bool:
         """Decrement; True when the count reached zero (block retired)."""
         self._validate_handle(handle)
         with self._lock:
-            ptr = self._stage_ids([handle.block_id])
-            N.check(N.lib.akv_decref_batch(self._state, ptr, 1, self._tick(), None,
-                                           self._status.data_ptr(), self._stream()))
-            io = self._sync_io(0)  # the copy includes ctl[LAST_RETIRED]
-            self._raise_status(io, "dec_ref")
-            return int(self._h_ctlio_np[N.CTL_LAST_RETIRED]) > 0
+            self._pending()
+            try:
+                k, _ = self._host().decref(np.asarray([handle.block_id], np.int32), self._tick())
+            except MirrorRefused as e:
+                raise self._refuse(e, "dec_ref", False) from None
+            self._maybe_flush()
+            return k > 0
+
+    def _copy_pair(self, src: int, dst: int) -> None:
+        """One block copy on the device (exclusivity checked by the caller on
+        the mirror), without waiting."""
+        pair = self._ids.put(np.asarray([src, dst], np.int32))  # a staging slot no later call reuses early
+        N.check(N.lib.akv_copy_blocks(self._kv_data.data_ptr(), self._cfg.bytes_per_block,
+                                      self._cfg.total_blocks, pair.data_ptr(), 1, None, self._status.data_ptr(),
+                                      self._stream()))
 
     def get_block_tensor(self, handle: BlockHandle) -> torch.Tensor:
         self._validate_handle(handle)
@@ -369,10 +455,12 @@ class SlabAllocator:
         self._validate_handle(src)
         self._validate_handle(dst)
         with self._lock:
-            if self._kv_data.device.type == "meta":
+            if self._kv_data.device.type == "meta" or self._live:
                 rc = self._read_ref(dst.block_id)
                 if rc != 1:
                     raise self._exception(N.AKV_ERR_NOT_EXCLUSIVE, dst.block_id, rc, "copy_block")
+                if self._kv_data.device.type != "meta":
+                    self._copy_pair(src.block_id, dst.block_id)
                 return
             ptr = self._stage_ids([src.block_id, dst.block_id])
             N.check(N.lib.akv_copy_blocks(self._kv_data.data_ptr(), self._cfg.bytes_per_block,
@@ -384,11 +472,12 @@ class SlabAllocator:
         """Write +0.0 over an exclusively owned block."""
         self._validate_handle(handle)
         with self._lock:
-            if self._kv_data.device.type == "meta":
+            if self._kv_data.device.type == "meta" or self._live:
                 rc = self._read_ref(handle.block_id)
                 if rc != 1:
                     raise self._exception(N.AKV_ERR_NOT_EXCLUSIVE, handle.block_id, rc, "zero_block")
-                return
+                if self._kv_data.device.type == "meta":
+                    return
             ptr = self._stage_ids([handle.block_id])
             N.check(N.lib.akv_zero_blocks(self._kv_data.data_ptr(), self._cfg.bytes_per_block,
                                           self._cfg.total_blocks, ptr, 1, self._ref_counts.data_ptr(),
@@ -412,30 +501,50 @@ class SlabAllocator:
             return self._read_ref(handle.block_id)
 
     def _read_ref(self, block_id: int) -> int:
-        """One block's refcount (one copy and one wait)."""
+        """One block's refcount: from the mirror when it is current, else
+        one copy and one wait."""
+        if self._live:
+            return self._mirror.ref(block_id)
         N.check(N.lib.akv_copy_wait(self._h_ref.data_ptr(), self._ref_counts.data_ptr() + 4 * block_id, 4, 1, 1,
                                     self._stream()))
         return int(self._h_ref_np[0])
 
     def ctl(self) -> np.ndarray:
-        """Host copy of the control words (waits)."""
+        """Host copy of the device's control words, after the mirror's log
+        (waits)."""
         with self._lock:
-            c = self._ctl.cpu().numpy()
-            self._mirror_epoch = int(c[N.CTL_EPOCH])
-            self._mirror_ok = True
-            return c
+            self._flush()
+            return self._ctl.cpu().numpy()
+
+    def ref_counts(self) -> np.ndarray:
+        """The device's refcounts after the mirror's log (waits)."""
+        with self._lock:
+            self._flush()
+            return self._ref_counts.cpu().numpy()
+
+    def flush(self) -> None:
+        """Bring the device arrays up to date with the per-call operations
+        answered so far (one launch, no wait)."""
+        with self._lock:
+            self._flush()
+
+    def counters(self) -> np.ndarray:
+        """The control words: the mirror's when it is current (no wait),
+        else the device's."""
+        with self._lock:
+            return self._mirror.ctl() if self._live else self.ctl()
 
     @property
     def free_count(self) -> int:
-        return int(self.ctl()[N.CTL_FREE_SIZE])
+        return int(self.counters()[N.CTL_FREE_SIZE])
 
     @property
     def allocated_count(self) -> int:
-        c = self.ctl()
+        c = self.counters()
         return int(self._cfg.total_blocks - c[N.CTL_FREE_SIZE] - (c[N.CTL_LIMBO_TAIL] - c[N.CTL_LIMBO_HEAD]))
 
     def stats(self) -> dict:
-        c = self.ctl()
+        c = self.counters()
         n = self._cfg.total_blocks
         return {
             "total_blocks": n,
@@ -450,8 +559,9 @@ class SlabAllocator:
         }
 
     def free_list(self) -> np.ndarray:
-        """The free list left to right (waits)."""
+        """The device's free list left to right (waits)."""
         with self._lock:
+            self._flush()
             c = self._ctl.cpu().numpy()
             ring = self._free_ring.cpu().numpy()
         n = self._cfg.total_blocks
@@ -459,8 +569,10 @@ class SlabAllocator:
         return ring[idx]
 
     def limbo(self) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
-        """(deferred ids, pending ids, pending epochs) in FIFO order (waits)."""
+        """(deferred ids, pending ids, pending epochs) in FIFO order, from the
+        device (waits)."""
         with self._lock:
+            self._flush()
             c = self._ctl.cpu().numpy()
             ids = self._limbo_ids.cpu().numpy()
             eps = self._limbo_epochs.cpu().numpy()
@@ -479,31 +591,68 @@ class SlabAllocator:
         return self._ids.put(np.asarray(ids, np.int32).reshape(-1))
 
     def alloc_batch(self, n: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """n alloc() calls in one launch; returns the ids (device int32)."""
+        """n alloc() calls; returns the ids (device int32).  Errors surface at
+        check()."""
         if out is None:
             out = torch.empty(max(n, 0), dtype=torch.int32, device=self._dev)
         with self._lock:
+            if self._live and not self._refused and n <= _MIRROR_MAX_BATCH:
+                try:
+                    ids = self._mirror.alloc(n, self._tick())
+                except MirrorRefused as e:
+                    self._refuse(e, "alloc", True)
+                    return out
+                if n:
+                    out[:n].copy_(self._ids.put(ids), non_blocking=True)
+                self._maybe_flush()
+                return out
+            self._device_op()
             N.check(N.lib.akv_alloc_batch(self._state, n, out.data_ptr() if n else None, self._tick(),
                                           self._status.data_ptr(), self._stream()))
-            self._queued()
         return out
 
     def inc_ref_batch(self, ids) -> None:
-        t = self._device_ids(ids)
+        """n inc_ref() calls (ids may repeat), all or nothing; errors surface
+        at check()."""
+        host = self._host_ids(ids)
         with self._lock:
+            if host is not None and self._live and len(host) <= _MIRROR_MAX_BATCH:
+                if self._refused:
+                    return  # the device would skip it too: an error is pending
+                try:
+                    self._mirror.incref(host, self._tick())
+                except MirrorRefused as e:
+                    self._refuse(e, "inc_ref", True)
+                self._maybe_flush()
+                return
+            t = self._device_ids(ids)
+            self._device_op()
             N.check(N.lib.akv_incref_batch(self._state, t.data_ptr(), t.numel(), self._tick(),
                                            self._status.data_ptr(), self._stream()))
-            self._queued()
 
     def dec_ref_batch(self, ids, retired_out: Optional[torch.Tensor] = None) -> None:
         """n dec_ref() calls; retired ids (in retirement order) go to
-        `retired_out` when given; their count is ctl[LAST_RETIRED]."""
-        t = self._device_ids(ids)
+        `retired_out` when given; their count is ctl[LAST_RETIRED].  Errors
+        surface at check()."""
+        host = self._host_ids(ids)
         with self._lock:
+            if host is not None and self._live and len(host) <= _MIRROR_MAX_BATCH:
+                if self._refused:
+                    return
+                try:
+                    k, ret = self._mirror.decref(host, self._tick(), retired=retired_out is not None)
+                except MirrorRefused as e:
+                    self._refuse(e, "dec_ref", True)
+                    return
+                if retired_out is not None and k:
+                    retired_out[:k].copy_(self._ids.put(ret), non_blocking=True)
+                self._maybe_flush()
+                return
+            t = self._device_ids(ids)
+            self._device_op()
             N.check(N.lib.akv_decref_batch(self._state, t.data_ptr(), t.numel(), self._tick(),
                                            retired_out.data_ptr() if retired_out is not None else None,
                                            self._status.data_ptr(), self._stream()))
-            self._queued()
 
     def cow_batch(self, blocks, out_blocks: Optional[torch.Tensor] = None,
                   out_copied: Optional[torch.Tensor] = None,
@@ -521,12 +670,12 @@ class SlabAllocator:
             pairs = torch.empty(2 * max(n, 1), dtype=torch.int32, device=self._dev)
         meta = self._kv_data.device.type == "meta"
         with self._lock:
+            self._device_op()
             N.check(N.lib.akv_cow_batch(
                 self._state, None if meta else self._kv_data.data_ptr(),
                 0 if meta else self._cfg.bytes_per_block, t.data_ptr(), n, out_blocks.data_ptr(),
                 out_copied.data_ptr(), pairs.data_ptr(), self._tick(), self._status.data_ptr(),
                 self._stream()))
-            self._queued()
         return out_blocks, out_copied
 
     def fanout_level(self, parent_tables: torch.Tensor, parent_off: torch.Tensor, parent_lens,
@@ -551,6 +700,8 @@ class SlabAllocator:
         nc = P * K
         total = int(lens.sum())
         dev = self._dev
+        with self._lock:
+            self._device_op()  # the planner's batches run on the device
         fresh = self.alloc_batch((1 + A) * nc)
         child_tables = torch.empty(K * total + nc * A, dtype=torch.int32, device=dev)
         child_off = torch.empty(nc + 1, dtype=torch.int64, device=dev)
@@ -617,6 +768,8 @@ class SlabAllocator:
             l_ = np.repeat(l_ + A, K)
         n_fresh = sum((1 + A) * P * K for P, _ in shapes)
         n_pairs = sum(P * K for P, _ in shapes)
+        with self._lock:
+            self._device_op()  # the planner's batches run on the device
         fresh_all = self.alloc_batch(n_fresh)
         all_pairs = torch.empty((n_pairs, 2), dtype=torch.int32, device=dev)
         if A >= 1 and 0 < levels <= N.MAX_FANOUT_LEVELS and n_pairs:
@@ -705,6 +858,9 @@ class SlabAllocator:
                      ref_counts=self._ref_counts if check_refs else None, status=self._status)
 
     def check(self) -> None:
-        """Wait for queued work and raise the first device-detected error."""
+        """Wait for queued work (the per-call log replayed first) and raise
+        the first device-detected error."""
         with self._lock:
+            self._flush()
+            self._refused = False
             self._raise_status(self._sync_io(0))

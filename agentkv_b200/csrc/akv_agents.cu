@@ -222,6 +222,7 @@ AKV_DEV int fork_into(Cursors& c, const Agents& g, const int32_t* src, int32_t n
 // states differ).
 AKV_DEV int dec_ids(Cursors& c, const Agents& g, const int32_t* ids, int32_t n, int32_t& bad_id) {
   int64_t done = 0;  // ops ticked so far
+  const int64_t frees0 = c.frees;
   for (int32_t i0 = 0; i0 < n; i0 += 32) {
     const int32_t i = i0 + g.lane;
     int32_t x = i < n ? ids[i] : -1;
@@ -275,6 +276,8 @@ AKV_DEV int dec_ids(Cursors& c, const Agents& g, const int32_t* ids, int32_t n, 
     }
   }
   ticks(c, g, n - done);
+  if (g.lane == 0) g.st.ctl[AKV_CTL_LAST_RETIRED] = c.frees - frees0;
+  __syncwarp();
   return AKV_OK;
 }
 
@@ -482,10 +485,17 @@ k_alloc_replay(Agents g, const int32_t* __restrict__ log, int64_t n_words) {
       const int32_t x = p[0], want = p[1];
       const int32_t r = static_cast<uint32_t>(x) < static_cast<uint32_t>(g.N) ? lane0_load(&g.st.ref_counts[x], g.lane)
                                                                                 : -1;
-      if (r <= 1) {
+      if (r < 0 || (r <= 1) != (want == x)) {  // the host's decision must be the device's
         bad_id = x;
         observed = r;
         break;
+      }
+      if (g.lane == 0) g.st.ctl[AKV_CTL_LAST_COPIED] = want == x ? 0 : 1;
+      __syncwarp();
+      if (want == x) {
+        rc = AKV_OK;
+        w += AKV_LOG_HEADER_WORDS + n;
+        continue;
       }
       const int32_t got = op_alloc(c, g);
       if (got != want) {

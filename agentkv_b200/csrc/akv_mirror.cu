@@ -22,6 +22,7 @@
 // readers_max lo/hi, epoch_interval, readers_active} and n payload words:
 //   ALLOC   the n ids handed out         INCREF  the n ids
 //   DECREF  the n ids                    COW     {block, block owned after}
+//                                        (the same block: no copy)
 //   RELEASE n = 0, safe epoch in the readers_min words
 //   ADVANCE n = 0
 #include <algorithm>
@@ -255,9 +256,9 @@ extern "C" int akv_mirror_decref(AkvMirror* m, const int32_t* ids, int32_t n, co
     }
     ++seen[x];
   }
+  if (n == 0) return AKV_OK;
   int64_t* c = m->ctl;
   c[AKV_CTL_LAST_RETIRED] = 0;
-  if (n == 0) return AKV_OK;
   log_header(m, AKV_OP_DECREF, n, tk);
   m->log.insert(m->log.end(), ids, ids + n);
   for (int32_t k = 0; k < n; ++k) {
@@ -280,9 +281,14 @@ extern "C" int akv_mirror_cow(AkvMirror* m, int32_t block, const AkvTick* tk, in
     fail(err, AKV_ERR_OUT_OF_RANGE, 0, block, m->n);
     return AKV_ERR_OUT_OF_RANGE;
   }
-  m->ctl[AKV_CTL_LAST_COPIED] = 0;
   *out_block = block;
-  if (m->ref[block] <= 1) return AKV_OK;  // exclusively owned (or free): nothing to do
+  if (m->ref[block] <= 1) {  // exclusively owned (or free): nothing to do
+    m->ctl[AKV_CTL_LAST_COPIED] = 0;
+    log_header(m, AKV_OP_COW, 2, tk);
+    m->log.push_back(block);
+    m->log.push_back(block);
+    return AKV_OK;
+  }
   if (!can_pop(m, 1)) {
     fail(err, AKV_ERR_EXHAUSTED, 0, -1, static_cast<int32_t>(m->ctl[AKV_CTL_FREE_SIZE]));
     return AKV_ERR_EXHAUSTED;

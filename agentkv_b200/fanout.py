@@ -73,6 +73,7 @@ class FanoutGraph:
         self._twin: Optional["FanoutGraph"] = None  # run_many's second instance
         with torch.cuda.device(self.dev):  # kernels prepared and graph recorded on the allocator's GPU
             N.check(N.lib.akv_prepare())
+            self._note_replay()  # nothing of the allocator's own log may land in the recording
             self.graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
                 self._record()
@@ -147,10 +148,12 @@ class FanoutGraph:
         return out.copy() if copy else out
 
     def _note_replay(self) -> None:
-        """A replay runs allocator batches the allocator's host side does not
-        see: its host copy of the epoch is stale until the next wait."""
+        """A replay runs allocator batches on the device: the allocator's
+        per-call log goes first, and its host mirror is reloaded when next
+        needed."""
         if self.alloc is not None:
-            self.alloc._queued()
+            with self.alloc._lock:
+                self.alloc._device_op()
 
     def _twin_graph(self) -> "FanoutGraph":
         if self._twin is None:

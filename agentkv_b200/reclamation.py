@@ -3,21 +3,23 @@
 The reference's EpochReclaimer (agentkv/core/reclamation.py:55-190) keeps the
 epoch counter, the set of epochs that hold an open read section, and a FIFO
 of retired block ids that may only return to the free list once no reader
-that could still see them remains.  Here the ids never leave the GPU: the
-retired-id FIFO and the epoch / op counters live in the allocator's device
-state, and this class keeps what only the host knows — the reader set — and
-turns each reclaimer call into one launch:
+that could still see them remains.  Here the retired-id FIFO and the epoch /
+op counters are part of the allocator's state (on the device, and in the
+allocator's host mirror), and this class keeps what only the host knows — the
+reader set:
 
 * ``enter_read_section`` takes the current epoch (the reader's token) and
   adds it to the set — a set, as in the reference, so two readers of one
-  epoch share one entry.  The allocator keeps a host copy of the epoch,
-  refreshed at every wait and moved by ``maybe_advance``, so this costs no
-  read-back unless a batch was queued since the last wait;
-* ``leave_read_section`` discards the token and launches the release of every
-  pending id older than the oldest remaining reader (all of them when no
-  reader is left), ``_try_retire`` in the reference (reclamation.py:147-173);
-* ``maybe_advance`` launches the epoch bump (unless a reader holds the current
-  epoch) followed by the same release.
+  epoch share one entry.  The epoch comes from the allocator's host mirror
+  when it is current, so this costs no read-back;
+* ``leave_read_section`` discards the token and releases every pending id
+  older than the oldest remaining reader (all of them when no reader is
+  left), ``_try_retire`` in the reference (reclamation.py:147-173);
+* ``maybe_advance`` bumps the epoch (unless a reader holds the current epoch)
+  followed by the same release.
+
+Both apply to the mirror (and reach the device with its op log) when the
+mirror is current, else they are one launch each.
 
 Each allocator batch carries a summary of the reader set (AkvTick) so the
 device applies the reference's rules for ids that retire while readers are
@@ -59,19 +61,24 @@ class EpochReclaimer:
         with a._lock:
             self._active_reader_epochs.discard(token)
             safe = min(self._active_reader_epochs) if self._active_reader_epochs else _INT64_MAX
-            N.check(N.lib.akv_limbo_release(a._state, safe, a._stream()))
+            if a._live:
+                a._mirror.release(safe)
+                a._maybe_flush()
+            else:
+                N.check(N.lib.akv_limbo_release(a._state, safe, a._stream()))
 
     def maybe_advance(self) -> None:
         a = self._alloc
         with a._lock:
-            N.check(N.lib.akv_epoch_advance(a._state, self.tick(a._cfg.epoch_interval), a._stream()))
-            # the same rule on the host copy: a reader always holds the
-            # current epoch, so the epoch moves exactly when none is open
-            if not self._active_reader_epochs:
-                a._mirror_epoch += 1
+            tick = self.tick(a._cfg.epoch_interval)
+            if a._live:
+                a._mirror.advance(tick)
+                a._maybe_flush()
+            else:
+                N.check(N.lib.akv_epoch_advance(a._state, tick, a._stream()))
 
     def stats(self) -> dict:
-        c = self._alloc.ctl()
+        c = self._alloc.counters()
         return {
             "epoch": int(c[N.CTL_EPOCH]),
             "pending_blocks": int(c[N.CTL_LIMBO_TAIL] - c[N.CTL_LIMBO_REL]),
@@ -81,5 +88,5 @@ class EpochReclaimer:
         }
 
     def pending_count(self) -> int:
-        c = self._alloc.ctl()
+        c = self._alloc.counters()
         return int(c[N.CTL_LIMBO_TAIL] - c[N.CTL_LIMBO_REL])

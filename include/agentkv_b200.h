@@ -576,7 +576,8 @@ typedef struct AkvMirror AkvMirror;
 
 /* Op log records: AKV_LOG_HEADER_WORDS int32 words {op, n, readers_min lo,
  * hi, readers_max lo, hi, epoch_interval, readers_active}, then n words:
- * ALLOC the ids handed out; INCREF / DECREF the ids; COW {block, new block};
+ * ALLOC the ids handed out; INCREF / DECREF the ids; COW {block, the block
+ * owned afterwards (itself when no copy was needed)};
  * RELEASE (n = 0) the safe epoch in the readers_min words; ADVANCE (n = 0). */
 #define AKV_LOG_HEADER_WORDS 8
 enum {
@@ -623,7 +624,9 @@ AKV_API int64_t akv_mirror_log_words(const AkvMirror* m);
 AKV_API int akv_mirror_take_log(AkvMirror* m, int32_t* dst, int64_t cap);
 /* Apply an op log (device memory, n_words int32) to the device state with
  * the same rules, one warp, checking each logged id against its own:
- * AKV_ERR_MIRROR in `status` at the first difference.  One launch. */
+ * AKV_ERR_MIRROR in `status` at the first difference.  ctl's LAST_RETIRED /
+ * LAST_COPIED words end as the last DECREF / COW record left them.  One
+ * launch. */
 AKV_API int akv_alloc_replay(const AkvAllocState* st, const int32_t* log, int64_t n_words, AkvStatus* status,
                              void* stream);
 

@@ -21,7 +21,7 @@ HEADERS = sorted((REPO / "include").glob("*.h"))
 def declared_symbols():
     names = set()
     for h in HEADERS:
-        for m in re.finditer(r"^AKV_API\s+\w+\s+(akv_\w+)\s*\(", h.read_text(), re.M):
+        for m in re.finditer(r"^AKV_API\s+\w+\s*\**\s*(akv_\w+)\s*\(", h.read_text(), re.M):
             names.add(m.group(1))
     return names
 

@@ -34,7 +34,7 @@ def device_state(a: SlabAllocator) -> dict:
     c = a.ctl()
     deferred, pending, pend_eps = a.limbo()
     return {
-        "ref": a._ref_counts.cpu().numpy(),
+        "ref": a.ref_counts(),
         "free": a.free_list(),
         "deferred": deferred,
         "pending": pending,
@@ -314,48 +314,78 @@ def test_cpu_pool_is_rejected():
         make_alloc(8, device="cpu")
 
 
-def test_host_epoch_copy_follows_the_device():
-    """SlabAllocator keeps the reclaimer's epoch on the host — refreshed at
-    every wait, moved by maybe_advance_epoch by the reference's rule (the
-    epoch moves exactly when no reader is open) — so that
-    enter_read_section needs no read-back.  Over random single calls,
-    batches, epoch advances and read sections, whenever the host copy
-    claims to be current it equals the device's epoch, and every reader's
-    token is the device's epoch at entry."""
+def test_host_mirror_follows_the_device():
+    """The per-call methods are answered by the allocator's host mirror and
+    replayed on the device from its op log (akv_alloc_replay); device-side
+    batches make the mirror reload from the device.  Over random single
+    calls, host-id batches, device-id batches, copy-on-writes, epoch
+    advances and read sections, after every step the device arrays (after
+    the replay) equal the mirror's and the oracle's, every reader's token is
+    the device's epoch at entry, and the replay reports no difference."""
     from agentkv_b200.allocator import BlockHandle
 
     cfg = PoolConfig(total_blocks=512, block_size=16, num_layers=1, num_kv_heads=1, head_dim=1,
                      dtype="float16", device="meta", epoch_interval=5)
     a = SlabAllocator(cfg)
+    o = O.OracleAllocator(512, 5)
     rng = np.random.default_rng(3)
     refs = []  # one entry per reference held
     readers = []
-    checked = 0
+    reloads = 0
     for step in range(400):
-        op = int(rng.integers(0, 8))
+        op = int(rng.integers(0, 10))
         if op == 0 or len(refs) < 4:
-            refs.append(a.alloc())
+            b = a.alloc()
+            assert b.block_id == int(o.alloc_batch(1)[0]), step
+            refs.append(b)
         elif op == 1:
             b = refs[int(rng.integers(len(refs)))]
             a.inc_ref(b)
+            o.inc_ref_batch([b.block_id])
             refs.append(b)
         elif op == 2:
-            a.dec_ref(refs.pop(int(rng.integers(len(refs)))))
+            b = refs.pop(int(rng.integers(len(refs))))
+            assert a.dec_ref(b) == (len(o.dec_ref_batch([b.block_id])) > 0), step
         elif op == 3:
-            refs += [BlockHandle(int(x)) for x in a.alloc_batch(3).cpu().tolist()]
+            got = a.alloc_batch(3).cpu().tolist()
+            assert got == o.alloc_batch(3).tolist(), step
+            refs += [BlockHandle(int(x)) for x in got]
         elif op == 4:
             drop = [refs.pop(int(rng.integers(len(refs)))) for _ in range(2)]
             a.dec_ref_batch([b.block_id for b in drop])
+            o.dec_ref_batch([b.block_id for b in drop])
         elif op == 5:
             a.maybe_advance_epoch()
+            o.maybe_advance_epoch()
         elif op == 6 and len(readers) < 3:
-            device_epoch = int(a._ctl.cpu()[N.CTL_EPOCH])
+            device_epoch = int(a.ctl()[N.CTL_EPOCH])
             readers.append(a.enter_read_section())
-            assert readers[-1] == device_epoch, step
+            assert readers[-1] == device_epoch == o.enter_read_section(), step
+        elif op == 7:
+            # a batch of DEVICE ids: runs on the device, the mirror reloads later
+            b = refs[int(rng.integers(len(refs)))]
+            a.inc_ref_batch(torch.tensor([b.block_id], dtype=torch.int32, device=a.device))
+            o.inc_ref_batch([b.block_id])
+            refs.append(b)
+            reloads += not a._live
+        elif op == 8:
+            b = refs[int(rng.integers(len(refs)))]
+            nb = a.cow_one(b.block_id)
+            out, _ = o.cow_batch([b.block_id])
+            assert nb == int(out[0]), step
+            if nb != b.block_id:
+                refs.remove(b)
+                refs.append(BlockHandle(nb))
         elif readers:
-            a.leave_read_section(readers.pop(0))
-        if a._mirror_ok:
-            assert a._mirror_epoch == int(a._ctl.cpu()[N.CTL_EPOCH]), step
-            checked += 1
-    a.check()
-    assert checked > 200 and int(a._ctl.cpu()[N.CTL_ADVANCES]) > 10
+            t = readers.pop(0)
+            a.leave_read_section(t)
+            o.leave_read_section(t)
+        a.check()
+        assert_same_as_oracle(a, o, f"step {step}")
+        if a._live:
+            ctl, ref, ring, lid, lep = a._mirror.arrays()
+            np.testing.assert_array_equal(ref, a.ref_counts(), err_msg=f"mirror refs {step}")
+            dev_ctl = a.ctl()
+            keep = [i for i in range(N.CTL_WORDS) if i != N.CTL_DONE]
+            np.testing.assert_array_equal(ctl[keep], dev_ctl[keep], err_msg=f"mirror ctl {step}")
+    assert reloads > 10 and int(a.ctl()[N.CTL_ADVANCES]) > 10

@@ -102,7 +102,7 @@ def test_fanout_graph_tot_8b_reference_fixture(golden_dir):
     roots = a.alloc_batch(root_len).cpu().numpy()
     fg = FanoutGraph(a, [root_len], spec.levels, spec.fanout, spec.appended_blocks)
     np.testing.assert_array_equal(fg.run(roots), g["tables"])
-    np.testing.assert_array_equal(a._ref_counts.cpu().numpy(), g["ref_fanout"])
+    np.testing.assert_array_equal(a.ref_counts(), g["ref_fanout"])
     np.testing.assert_array_equal(a.free_list(), g["free_fanout"])
     st = json.loads(str(g["stats_fanout"]))
     for k in ("free_blocks", "allocated_blocks", "peak_allocated", "total_allocs", "epoch"):
@@ -129,7 +129,7 @@ def test_fanout_graph_tot_8b_reference_fixture(golden_dir):
             np.testing.assert_array_equal(a2.free_list(), g["free_freed"])
         want = _oracle_fanout(tree, [root], spec.levels, spec.fanout, spec.appended_blocks, True)
         np.testing.assert_array_equal(got, want, err_msg=f"run {run}")
-        np.testing.assert_array_equal(a2._ref_counts.cpu().numpy(), g["ref_freed"])
+        np.testing.assert_array_equal(a2.ref_counts(), g["ref_freed"])
         assert_same_as_oracle(a2, o, f"run {run}")
 
 
@@ -171,7 +171,7 @@ def test_fused_tree_plan_equals_level_plans(root_lens, levels, fanout, append):
             tables, pairs = r["child_tables"], r["pairs"]
         a.check()
         return ([t.cpu().numpy() for t in tables], [p.cpu().numpy() for p in pairs],
-                a._ref_counts.cpu().numpy(), a.free_list(), a.stats())
+                a.ref_counts(), a.free_list(), a.stats())
 
     t1, p1, r1, f1, s1 = run(False)
     t2, p2, r2, f2, s2 = run(True)
@@ -192,11 +192,11 @@ def test_fanout_edge_cases():
                      device="cuda")
     a = AgentKVPool(config=cfg)._allocator
     roots = a.alloc_batch(2).cpu().numpy()
-    before = (a._ref_counts.cpu().numpy().copy(), a.free_list().copy())
+    before = (a.ref_counts().copy(), a.free_list().copy())
     for levels, fanout in ((0, 3), (2, 0)):
         fg = FanoutGraph(a, [2], levels, fanout, 1, free_children=True)
         assert fg.run(roots).size == 0
-        np.testing.assert_array_equal(a._ref_counts.cpu().numpy(), before[0])
+        np.testing.assert_array_equal(a.ref_counts(), before[0])
         np.testing.assert_array_equal(a.free_list(), before[1])
     o = O.OracleAllocator(64)
     tree = O.OracleTree(o, 4)

@@ -66,7 +66,7 @@ def test_react_trace_device_pool(golden_dir):
         if k + "_ref" in g.files:
             tables = np.concatenate([np.asarray(pool.get_block_ids(h), np.int32) for h in agents])
             np.testing.assert_array_equal(tables, g[k + "_tables"], err_msg=k)
-            np.testing.assert_array_equal(pool._allocator._ref_counts.cpu().numpy(), g[k + "_ref"])
+            np.testing.assert_array_equal(pool._allocator.ref_counts(), g[k + "_ref"])
             np.testing.assert_array_equal(pool._allocator.free_list(), g[k + "_free"])
             assert_same_as_oracle(pool._allocator, oapi.alloc, k)
             st, want = pool.stats(), json.loads(str(g[k + "_stats"]))
@@ -184,7 +184,7 @@ def test_react_trace_device_agents(golden_dir, per_launch):
                 handles = dev_agents.sync()
                 tables = np.concatenate([np.asarray(meta.get_block_ids(h), np.int32) for h in handles])
                 np.testing.assert_array_equal(tables, g[k + "_tables"], err_msg=k)
-                np.testing.assert_array_equal(meta._allocator._ref_counts.cpu().numpy(), g[k + "_ref"])
+                np.testing.assert_array_equal(meta._allocator.ref_counts(), g[k + "_ref"])
                 np.testing.assert_array_equal(meta._allocator.free_list(), g[k + "_free"])
                 st, want = meta.stats(), json.loads(str(g[k + "_stats"]))
                 for key in ("free_blocks", "allocated_blocks", "peak_allocated", "total_allocs", "total_frees",

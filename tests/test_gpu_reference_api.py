@@ -396,7 +396,7 @@ def test_stress_shadow_model(seed, n_ops):
     for _ in range(10):
         a.maybe_advance_epoch()
     assert sh.violations == []
-    np.testing.assert_array_equal(a._ref_counts.cpu().numpy()[: 512], np.zeros(512))
+    np.testing.assert_array_equal(a.ref_counts()[: 512], np.zeros(512))
     assert a.free_count == 512, "leak"
 
 

@@ -32,7 +32,7 @@ def test_reference_stress_runner_replay(golden_dir, seed):
     tree = DualRadixTree(alloc, cfg)
     replay(g, tree, alloc.maybe_advance_epoch, lambda e: isinstance(e, MemoryError) and "exhausted" in str(e))
     alloc.check()
-    np.testing.assert_array_equal(alloc._ref_counts.cpu().numpy(), g["ref"])
+    np.testing.assert_array_equal(alloc.ref_counts(), g["ref"])
     np.testing.assert_array_equal(alloc.free_list(), g["free"])
     assert alloc.free_count == 512
     st, want = alloc.stats(), json.loads(str(g["stats"]))
@@ -59,7 +59,7 @@ def test_concurrent_replays_in_threads(golden_dir):
             replay(g, tree, alloc.maybe_advance_epoch,
                    lambda e: isinstance(e, MemoryError) and "exhausted" in str(e))
             alloc.check()
-            np.testing.assert_array_equal(alloc._ref_counts.cpu().numpy(), g["ref"])
+            np.testing.assert_array_equal(alloc.ref_counts(), g["ref"])
             np.testing.assert_array_equal(alloc.free_list(), g["free"])
         except Exception as e:  # noqa: BLE001 - reported below
             errors.append((seed, repr(e)))

@@ -104,7 +104,7 @@ def test_reference_tree_trace(golden_dir, seed):
             assert {str(k): pool.get_block_ids(h) for k, h in sorted(live.items())} == st["tables"]
             assert {str(k): [h.shared_node_id, h.shared_match_len] for k, h in sorted(live.items())} == st["shared"]
             assert tree_nodes(pool) == st["nodes"]
-            assert pool._allocator._ref_counts.cpu().tolist() == st["ref"]
+            assert pool._allocator.ref_counts().tolist() == st["ref"]
             assert pool._allocator.free_list().tolist() == st["free"]
             s = pool.stats()
             for k, v in st["stats"].items():
@@ -135,7 +135,7 @@ def test_quickstart_workload(golden_dir):
     assert [pool.get_block_ids(c) for c in kids] == g["children"]
     assert pool.get_block_ids(root) == g["root"]
     assert matches == g["matches"]
-    assert pool._allocator._ref_counts.cpu().tolist() == g["ref"]
+    assert pool._allocator.ref_counts().tolist() == g["ref"]
     assert pool._allocator.free_list().tolist() == g["free"]
     assert pool_digests(pool) == g["block_sha256"]
     s = pool.stats()
@@ -153,7 +153,7 @@ def _tot_pool():
 def _check_tot(pool, g, kids):
     tables = np.concatenate([np.asarray(pool.get_block_ids(c), np.int32) for c in kids])
     np.testing.assert_array_equal(tables, g["tables"])
-    np.testing.assert_array_equal(pool._allocator._ref_counts.cpu().numpy(), g["ref_fanout"])
+    np.testing.assert_array_equal(pool._allocator.ref_counts(), g["ref_fanout"])
     np.testing.assert_array_equal(pool._allocator.free_list(), g["free_fanout"])
     st = json.loads(str(g["stats_fanout"]))
     s = pool.stats()
@@ -185,7 +185,7 @@ def test_tot_single_op_api(golden_dir):
     _check_tot(pool, g, kids)
     for c in kids:
         pool.free(c)
-    np.testing.assert_array_equal(pool._allocator._ref_counts.cpu().numpy(), g["ref_freed"])
+    np.testing.assert_array_equal(pool._allocator.ref_counts(), g["ref_freed"])
     np.testing.assert_array_equal(pool._allocator.free_list(), g["free_freed"])
 
 
@@ -211,7 +211,7 @@ def test_tot_batched_api(golden_dir):
         level = nxt
     _check_tot(pool, g, kids)
     pool.free_many(kids)
-    np.testing.assert_array_equal(pool._allocator._ref_counts.cpu().numpy(), g["ref_freed"])
+    np.testing.assert_array_equal(pool._allocator.ref_counts(), g["ref_freed"])
     np.testing.assert_array_equal(pool._allocator.free_list(), g["free_freed"])
 
 
@@ -411,7 +411,7 @@ def test_tot_device_tables(golden_dir, mode):
     np.testing.assert_array_equal(torch.cat(tables).cpu().numpy(), g["tables"])
     for lvl in range(3):
         np.testing.assert_array_equal(pairs[lvl].cpu().numpy(), g[f"pairs_l{lvl}"])
-    np.testing.assert_array_equal(a._ref_counts.cpu().numpy(), g["ref_fanout"])
+    np.testing.assert_array_equal(a.ref_counts(), g["ref_fanout"])
     np.testing.assert_array_equal(a.free_list(), g["free_fanout"])
     st = json.loads(str(g["stats_fanout"]))
     s = a.stats()
@@ -419,7 +419,7 @@ def test_tot_device_tables(golden_dir, mode):
         assert s[k] == st[k], k
     a.dec_ref_batch(torch.cat(tables))
     a.check()
-    np.testing.assert_array_equal(a._ref_counts.cpu().numpy(), g["ref_freed"])
+    np.testing.assert_array_equal(a.ref_counts(), g["ref_freed"])
     np.testing.assert_array_equal(a.free_list(), g["free_freed"])
     st = json.loads(str(g["stats_freed"]))
     s = a.stats()
@@ -554,7 +554,7 @@ def test_match_prefix_many_equals_one_by_one(golden_dir):
     assert {k: n.ref_count for k, n in a._tree._shared_nodes.items()} == \
         {k: n.ref_count for k, n in b._tree._shared_nodes.items()}
     np.testing.assert_array_equal(a._allocator.free_list(), b._allocator.free_list())
-    np.testing.assert_array_equal(a._allocator._ref_counts.cpu().numpy(), b._allocator._ref_counts.cpu().numpy())
+    np.testing.assert_array_equal(a._allocator.ref_counts(), b._allocator.ref_counts())
 
 
 @pytest.mark.parametrize("name", ["colliding", "long_chain"])

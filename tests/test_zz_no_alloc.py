@@ -34,7 +34,7 @@ def _alloc(n):
 def _state(a: SlabAllocator):
     c = a.ctl()
     deferred, pending, eps = a.limbo()
-    return {"ref": a._ref_counts.cpu().numpy(), "free": a.free_list(), "deferred": deferred,
+    return {"ref": a.ref_counts(), "free": a.free_list(), "deferred": deferred,
             "pending": pending, "eps": eps, "ctl": np.delete(c, N.CTL_DONE)}
 
 
@@ -66,8 +66,11 @@ def _compare_two_calls(readers: bool):
     a.check()
     b.check()
     _same(a, b)
-    refs = a._ref_counts.cpu().numpy()
-    # b's state with its scratch pointers removed: the entry point must not need them
+    refs = a.ref_counts()
+    # b's state with its scratch pointers removed: the entry point must not need them.
+    # The direct calls change b's device state behind its host mirror.
+    with b._lock:
+        b._device_op()
     st = N.AkvAllocState.from_buffer_copy(b._state)
     st.scratch_count = None
     st.scratch_last = None
@@ -91,7 +94,7 @@ def _compare_two_calls(readers: bool):
         n_ret = int(a.ctl()[N.CTL_LAST_RETIRED])
         assert n_ret > 0
         np.testing.assert_array_equal(out_a.cpu().numpy(), out_b.cpu().numpy())
-        refs = a._ref_counts.cpu().numpy()
+        refs = a.ref_counts()
     if readers:
         assert a._reclaimer.pending_count() > 0
         for x, t0, t1 in tokens:
