@@ -395,14 +395,26 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
     constexpr int32_t kStep = 32 * kVerifyChunks;
     // One verify round: kVerifyChunks x 32 consecutive flattened positions
     // from `base`, query tokens into av, edge tokens into bv.
+    // Edges that lie back to back in the token arena, as the nodes of a
+    // chain split from one committed edge do (a split keeps the tokens in
+    // place): flattened position p is then arena position shift + matched + p
+    // across the whole segment, and every round reads two contiguous ranges.
+    const int64_t shift = __shfl_sync(kFull, my_off - my_d, 0);
+    const bool contiguous = __all_sync(kFull, lane >= n || my_off - my_d == shift);
     auto load_round = [&](int32_t base, int32_t (&av)[kVerifyChunks], int32_t (&bv)[kVerifyChunks]) {
-      // Fast path: the whole round lies inside one edge (long edges).
-      const int e0 = entry_of(base);
-      const int32_t ex0 = __shfl_sync(kFull, excl, e0);
-      const int32_t lim0 = __shfl_sync(kFull, lim, e0);
-      if (ex0 + lim0 >= base + kStep || e0 == n - 1) {
-        const int64_t de = __shfl_sync(kFull, my_d, e0) - ex0;
-        const int64_t oe = __shfl_sync(kFull, my_off, e0) - ex0;
+      // Fast path: the whole round lies inside one edge (long edges), or the
+      // edges are contiguous.
+      int64_t de = matched, oe = shift + matched;
+      bool one_range = contiguous;
+      if (!one_range) {
+        const int e0 = entry_of(base);
+        const int32_t ex0 = __shfl_sync(kFull, excl, e0);
+        const int32_t lim0 = __shfl_sync(kFull, lim, e0);
+        one_range = ex0 + lim0 >= base + kStep || e0 == n - 1;
+        de = __shfl_sync(kFull, my_d, e0) - ex0;
+        oe = __shfl_sync(kFull, my_off, e0) - ex0;
+      }
+      if (one_range) {
 #pragma unroll
         for (int u = 0; u < kVerifyChunks; ++u) {
           const int32_t p = base + u * 32 + lane;
@@ -870,14 +882,20 @@ AKV_DEV bool verify_window(const AkvTreeView& tree, const int32_t* __restrict__ 
         }
         return lo;
       };
+      // hops whose edges lie back to back in the arena read one range
+      const int32_t shift = __shfl_sync(kFull, hp.w - hp.z, 0);
+      const bool contiguous = __all_sync(kFull, lane >= nh || hp.w - hp.z == shift);
       for (int32_t base = p; base < gend; base += kStep) {
         int32_t av[kChunks], bv[kChunks];
 #pragma unroll
         for (int u = 0; u < kChunks; ++u) {
           const int32_t x = base + u * 32 + lane;
           const bool ok = x < gend;
-          const int e = hop_of(ok ? x : gend - 1);
-          const int64_t oe = static_cast<int64_t>(__shfl_sync(kFull, hp.w, e)) - __shfl_sync(kFull, hp.z, e);
+          int64_t oe = shift;
+          if (!contiguous) {
+            const int e = hop_of(ok ? x : gend - 1);
+            oe = static_cast<int64_t>(__shfl_sync(kFull, hp.w, e)) - __shfl_sync(kFull, hp.z, e);
+          }
           av[u] = ok ? Q[x] : 0;
           bv[u] = ok ? __ldg(&tree.tokens[oe + x]) : 0;
         }
