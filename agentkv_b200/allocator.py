@@ -476,8 +476,12 @@ class SlabAllocator:
                 rc = self._read_ref(handle.block_id)
                 if rc != 1:
                     raise self._exception(N.AKV_ERR_NOT_EXCLUSIVE, handle.block_id, rc, "zero_block")
-                if self._kv_data.device.type == "meta":
-                    return
+                if self._kv_data.device.type != "meta":  # checked on the mirror: no device check, no wait
+                    ids = self._ids.put(np.asarray([handle.block_id], np.int32))
+                    N.check(N.lib.akv_zero_blocks(self._kv_data.data_ptr(), self._cfg.bytes_per_block,
+                                                  self._cfg.total_blocks, ids.data_ptr(), 1, None,
+                                                  self._status.data_ptr(), self._stream()))
+                return
             ptr = self._stage_ids([handle.block_id])
             N.check(N.lib.akv_zero_blocks(self._kv_data.data_ptr(), self._cfg.bytes_per_block,
                                           self._cfg.total_blocks, ptr, 1, self._ref_counts.data_ptr(),
@@ -854,6 +858,9 @@ class SlabAllocator:
         """Copy a batch of independent (src, dst) pairs; dsts must be exclusive."""
         if self._kv_data.device.type == "meta":
             return
+        if check_refs:
+            with self._lock:
+                self._flush()  # the device refcounts the kernel checks include the per-call log
         _copy_blocks(self._kv_data, self._device_ids(pairs),
                      ref_counts=self._ref_counts if check_refs else None, status=self._status)
 

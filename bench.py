@@ -1264,6 +1264,103 @@ def react_cpu_baseline(spec, heads: int, max_seconds: float) -> dict:
             "host": host_cpu()}
 
 
+def percall_timings(api, prompt, query, copy_hook: bool, reps: int, match_fn, free_match=None) -> dict:
+    """Median microseconds per call of the reference-facing per-call API on
+    `api` (AgentKVPool, or the oracle's tree with the same call set): the
+    vLLM adapter's calls (fork, allocate_block, ensure_mutable_block on a
+    shared last block, free) and the SGLang adapter's match_prefix.  One
+    round: fork the root, allocate a block, copy-on-write the last
+    inherited block, look the query up, free the child (and the match's
+    handle).  The root keeps 128 residual blocks, so a fork increments 128
+    refcounts and the copy-on-write copies a 2 MiB block."""
+    times = {k: [] for k in ("fork", "allocate_block", "ensure_mutable_block", "match_prefix", "free")}
+    root = api.create_root(prompt)
+    need = -(-len(prompt) // 16)
+    for _ in range(need):
+        api.allocate_block(root)
+    api.commit_prefix(root, len(prompt) // 2)  # half the prompt shared, half the root's own blocks
+    pc = time.perf_counter
+    for i in range(reps + 3):
+        t0 = pc()
+        child = api.fork(root)
+        t1 = pc()
+        api.allocate_block(child)
+        t2 = pc()
+        api.ensure_mutable_block(child, -2)
+        t3 = pc()
+        h, _ = match_fn(query)
+        t4 = pc()
+        api.free(child)
+        t5 = pc()
+        if h is not None and free_match is not None:
+            free_match(h)
+        if i >= 3:
+            for k, (a, b) in zip(times, ((t0, t1), (t1, t2), (t2, t3), (t3, t4), (t4, t5))):
+                times[k].append((b - a) * 1e6)
+    return {k: round(statistics.median(v), 2) for k, v in times.items()}
+
+
+def percall_case(args) -> None:
+    """Per-call latency of the reference-facing API (the calls the reference's
+    vLLM and SGLang adapters make one at a time: fork, allocate_block,
+    ensure_mutable_block, match_prefix, free) on a metadata-only pool and on
+    a CUDA pool at the Llama-3-8B shape, with and without the copy_block hook
+    the vLLM adapter installs, beside the oracle's restatement of the
+    reference's per-call path on the host (kind "port": its allocator is the
+    C restatement, its tree Python, as the reference's is)."""
+    import torch
+
+    from agentkv_b200 import AgentKVPool, PoolConfig
+    from oracle import oracle as O
+
+    torch.cuda.set_device(0)
+    n_, bs, L, H, D, dt = W.LLAMA3_8B_GEOMETRY
+    rng = np.random.default_rng(7)
+    prompt = rng.integers(0, 128256, size=4096).tolist()
+    query = prompt[:3000] + rng.integers(0, 128256, size=500).tolist()
+    reps = max(50, args.steps * 10)
+    out = {"case": "percall", "unit": "us per call (median)", "reps": reps,
+           "workload": "4096-token root (256 blocks), its first 2048 tokens committed to the tree; per round: "
+                       "fork it, allocate a block, copy-on-write the child's last inherited block, match_prefix "
+                       "a 3500-token query sharing 3000 tokens with the root, free the child", "pools": {}}
+    for name, device, blocks in (("meta", "meta", 60000), ("cuda", "cuda", 1024)):
+        for hook in (False, True):
+            pool = AgentKVPool(config=PoolConfig(total_blocks=blocks, block_size=bs, num_layers=L, num_kv_heads=H,
+                                                 head_dim=D, dtype=dt, device=device))
+            pairs = []
+            if hook:
+                orig = pool._allocator.copy_block
+
+                def record(src, dst, orig=orig):
+                    pairs.append((src.block_id, dst.block_id))
+                    orig(src, dst)
+
+                pool._allocator.copy_block = record
+            tree = pool._tree
+            res = percall_timings(pool, prompt, query, hook, reps, tree.match_prefix, free_match=pool.free)
+            torch.cuda.synchronize()
+            out["pools"][f"{name}{' + copy_block hook' if hook else ''}"] = res
+            del pool
+    # the reference's per-call path restated on the host: Python tree, C allocator
+    oa = O.OracleAllocator(60000)
+    ot = O.OracleTree(oa, bs)
+
+    def ofree(h):
+        ot.free(h)
+
+    res = percall_timings(ot, prompt, query, False, reps, ot.match_prefix, free_match=ofree)
+    # and with the 2 MiB block copies on a host pool, as a device="cpu" pool does them
+    bpb = L * 2 * H * bs * D * 2
+    host_pool = np.zeros((1024, bpb), np.uint8)
+    oa2 = O.OracleAllocator(1024)
+    ot2 = O.OracleTree(oa2, bs, copy_cb=lambda s_, d_: np.copyto(host_pool[d_], host_pool[s_]))
+    res2 = percall_timings(ot2, prompt, query, False, reps, ot2.match_prefix, free_match=ot2.free)
+    out["cpu_baseline"] = {"kind": "port", "cores": 1, "value": res,
+                           "sample": f"{reps} rounds on a 60,000-block metadata pool, one host thread",
+                           "with_copies": res2, "host": host_cpu()}
+    print(json.dumps(out), flush=True)
+
+
 def react_case(args) -> None:
     """The ReAct multi-agent trace (a 16,384-token shared prefix, 32 agents,
     1,000 steps of forks, CoW tail copies, frees, appends and epoch advances)
