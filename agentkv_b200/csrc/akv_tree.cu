@@ -717,6 +717,7 @@ AKV_HD int64_t staged_layout(char* base, int32_t nq, int64_t n_tokens, int32_t W
 }
 
 constexpr unsigned long long kNoMismatch = ~0ull;
+constexpr int64_t kCheckMinTokens = 64;  // edges the chase checks 32 tokens into
 
 // The answer of query q from its hops, the first mismatch (or kNoMismatch)
 // and the query length.
@@ -780,8 +781,32 @@ k_match_chase(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
       if (lane == __ffs(badm) - 1) akv_fail(st, AKV_ERR_TREE, q, c.my_child, c.my_len, c.my_off);
       return;
     }
-    const int64_t lim = lane < n ? (c.my_len < L - c.my_d ? c.my_len : L - c.my_d) : 0;
-    if (lane < n) {
+    int64_t lim = lane < n ? (c.my_len < L - c.my_d ? c.my_len : L - c.my_d) : 0;
+    // A long edge whose first tokens already differ from the query holds
+    // the walk's stop: the chase ends there, and the windows stop at the
+    // mismatch instead of covering the edge and the speculation after it.
+    // (Siblings that share a first token and part of a block are common:
+    // the block-aligned split keeps one child per first token, so a query
+    // often takes an edge that differs a few tokens in.)  One warp-wide
+    // compare of the first 32 tokens per long edge.
+    int keep = n;
+    bool cut = false;
+    uint32_t longm = __ballot_sync(kFull, lane < n && lim >= kCheckMinTokens);
+    while (longm) {
+      const int e = __ffs(longm) - 1;
+      longm &= longm - 1;
+      const int64_t de = __shfl_sync(kFull, c.my_d, e);
+      const int64_t oe = __shfl_sync(kFull, c.my_off, e);
+      const uint32_t mm = __ballot_sync(kFull, Q[de + lane] != __ldg(&tree.tokens[oe + lane]));
+      if (mm) {
+        keep = e + 1;
+        cut = true;
+        const int64_t end = de + __ffs(mm);  // through the mismatching position
+        if (lane == e) lim = end - de;
+        break;
+      }
+    }
+    if (lane < keep) {
       const int32_t d32 = static_cast<int32_t>(c.my_d), off32 = static_cast<int32_t>(c.my_off);
       hops[h + lane] = make_int4(c.my_child, c.my_len, d32, off32);
       // the windows whose first position lies in this hop
@@ -790,9 +815,9 @@ k_match_chase(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
         wins[2 * k + 1] = make_int4(d32, c.my_len, off32, static_cast<int32_t>(L));
       }
     }
-    h += n;
-    D = __shfl_sync(kFull, c.my_d + lim, n - 1);
-    if (c.last_segment) break;
+    h += keep;
+    D = __shfl_sync(kFull, c.my_d + lim, keep - 1);
+    if (c.last_segment || cut) break;
     matched = c.d;
     cur = c.node;
   }
