@@ -196,6 +196,7 @@ class SlabAllocator:
         self._mirror = HostMirror(n)
         self._live = True
         self._refused = False
+        self._calls = 0
         self._log_np = np.zeros(_LOG_FLUSH_WORDS + 4096, np.int32)
         self._log_stage = _IdStage(dev, cap=1 << 17)
         self._h_state: Optional[torch.Tensor] = None  # pinned read-back of the device state
@@ -250,7 +251,10 @@ class SlabAllocator:
         N.check(N.lib.akv_alloc_replay(self._state, d.data_ptr(), k, self._status.data_ptr(), self._stream()))
 
     def _maybe_flush(self) -> None:
-        if self._mirror.log_words() >= _LOG_FLUSH_WORDS:
+        """Replay the log once it has grown large (looked at every 64 calls:
+        a call adds at most _MIRROR_MAX_BATCH + 8 words)."""
+        self._calls += 1
+        if self._calls & 63 == 0 and self._mirror.log_words() >= _LOG_FLUSH_WORDS:
             self._flush()
 
     def _device_op(self) -> None:
@@ -381,11 +385,11 @@ class SlabAllocator:
         with self._lock:
             self._pending()
             try:
-                ids = self._host().alloc(1, self._tick())
+                bid = self._host().alloc_one(self._tick())
             except MirrorRefused as e:
                 raise self._refuse(e, "alloc", False) from None
             self._maybe_flush()
-            return BlockHandle(int(ids[0]))
+            return BlockHandle(bid)
 
     def alloc_many(self, n: int) -> List[int]:
         """n alloc() calls: the ids, in the order the calls would return

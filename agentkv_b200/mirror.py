@@ -46,6 +46,7 @@ class HostMirror:
         self._err = N.AkvStatus()
         self._err_ptr = C.addressof(self._err)
         self._out = np.zeros(1024, np.int32)
+        self._out_ptr = _ptr(self._out)
         self._n_ret = np.zeros(1, np.int32)
         self._ctl = np.zeros(N.CTL_WORDS, np.int64)
 
@@ -58,6 +59,7 @@ class HostMirror:
     def _room(self, n: int) -> np.ndarray:
         if n > len(self._out):
             self._out = np.zeros(max(n, 2 * len(self._out)), np.int32)
+            self._out_ptr = _ptr(self._out)
         return self._out
 
     def _done(self, rc: int) -> None:
@@ -119,6 +121,11 @@ class HostMirror:
         out = self._room(n)
         self._done(N.lib.akv_mirror_alloc(self._h, n, tick, _ptr(out), self._err_ptr))
         return out[:n].copy()
+
+    def alloc_one(self, tick: N.AkvTick) -> int:
+        out = self._out
+        self._done(N.lib.akv_mirror_alloc(self._h, 1, tick, self._out_ptr, self._err_ptr))
+        return int(out[0])
 
     def incref(self, ids: np.ndarray, tick: N.AkvTick) -> None:
         ids = np.ascontiguousarray(ids, np.int32)

@@ -26,6 +26,7 @@ Batched extensions for schedulers: ``allocate_blocks``, ``fork_many``,
 from __future__ import annotations
 
 import threading
+from array import array
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -94,6 +95,9 @@ class NodeHandle:
 
 
 def _as_i32(tokens) -> np.ndarray:
+    if isinstance(tokens, list):
+        # array('i') converts a list of ints about twice as fast as numpy
+        return np.frombuffer(array("i", tokens), dtype=np.int32)
     return np.asarray(tokens, dtype=np.int32).reshape(-1)
 
 

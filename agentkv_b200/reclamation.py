@@ -42,24 +42,32 @@ class EpochReclaimer:
     def __init__(self, allocator: "SlabAllocator") -> None:
         self._alloc = allocator
         self._active_reader_epochs: Set[int] = set()
+        self._tick_cache = None  # (epoch_interval, AkvTick) for the current reader set
 
     def tick(self, epoch_interval: int) -> N.AkvTick:
+        """The reader-set summary every allocator call carries (kept until
+        the set changes: callers do not modify it)."""
+        c = self._tick_cache
+        if c is not None and c[0] == epoch_interval:
+            return c[1]
         r = self._active_reader_epochs
-        if r:
-            return N.AkvTick(min(r), max(r), epoch_interval, 1)
-        return N.AkvTick(0, 0, epoch_interval, 0)
+        t = N.AkvTick(min(r), max(r), epoch_interval, 1) if r else N.AkvTick(0, 0, epoch_interval, 0)
+        self._tick_cache = (epoch_interval, t)
+        return t
 
     def enter_read_section(self) -> int:
         a = self._alloc
         with a._lock:
             token = a.epoch()  # the host's copy when it is current: no wait
             self._active_reader_epochs.add(token)
+            self._tick_cache = None
             return token
 
     def leave_read_section(self, token: int) -> None:
         a = self._alloc
         with a._lock:
             self._active_reader_epochs.discard(token)
+            self._tick_cache = None
             safe = min(self._active_reader_epochs) if self._active_reader_epochs else _INT64_MAX
             if a._live:
                 a._mirror.release(safe)

@@ -32,10 +32,15 @@ def _alloc(n):
 
 
 def _state(a: SlabAllocator):
+    """The allocator's logical state.  The limbo cursors' raw values are left
+    out: a per-call dec_ref passes each retirement through the limbo queue
+    (the reference's order of steps), a dec_ref batch without readers puts
+    it straight on the free list, and both leave the same lists."""
     c = a.ctl()
     deferred, pending, eps = a.limbo()
     return {"ref": a.ref_counts(), "free": a.free_list(), "deferred": deferred,
-            "pending": pending, "eps": eps, "ctl": np.delete(c, N.CTL_DONE)}
+            "pending": pending, "eps": eps,
+            "ctl": np.delete(c, [N.CTL_DONE, N.CTL_LIMBO_HEAD, N.CTL_LIMBO_REL, N.CTL_LIMBO_TAIL])}
 
 
 def _same(a, b):
