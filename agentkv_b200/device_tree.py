@@ -834,7 +834,9 @@ class QueryStage:
     def _grow(self, total: int, nq: int) -> None:
         pin = self.device.type == "cuda"
         if total > self._tok_cap:
-            cap = max(total, self._tok_cap + self._tok_cap // 2, 1 << 16)
+            # with headroom: batches of one workload vary in size, and a
+            # regrown pinned buffer costs tens of milliseconds
+            cap = max(total + total // 4, self._tok_cap + self._tok_cap // 2, 1 << 16)
             self.h_tok = torch.empty(cap, dtype=torch.int32, pin_memory=pin)
             self.d_tok = torch.empty(cap, dtype=torch.int32, device=self.device)
             self._tok_cap = cap

@@ -861,11 +861,11 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
     if rank == 0 and world == 1:
         # through the public call with host queries: pack into the pinned
         # stage, upload, look up, read the answers back (one batch per call)
-        for b in range(min(2, len(batches))):
+        for b in range(len(batches)):  # every batch of the rotation once: the stage has grown to the largest
             pool.match_prefix_batch(batches[b])
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        reps = 4
+        reps = 2 * len(batches)
         for i in range(reps):
             pool.match_prefix_batch(batches[i % len(batches)])
         e2e_s = (time.perf_counter() - t0) / reps
