@@ -126,6 +126,10 @@ def parse_args():
     ap.add_argument("--match-split", type=int, default=0,
                     help="match_prefix splits queries into token ranges, one warp each (default 0: one warp per "
                          "query, measured faster on this workload)")
+    ap.add_argument("--match-staged", type=int, default=0,
+                    help="match_prefix as the two-launch staged lookup (chase, then windows over the grid)")
+    ap.add_argument("--match-window-tokens", type=int, default=0,
+                    help="staged lookup window in tokens: 256, 512 or 1024 (0: the library's default)")
     ap.add_argument("--match-tokens-per-range", type=int, default=0,
                     help="match_prefix split range in tokens, a multiple of 32 (0: the library's default)")
     ap.add_argument("--case", default="tot", choices=["tot", "sweep", "match", "layers", "hf", "react", "percall"],
@@ -754,8 +758,10 @@ def match_cpu_baseline(pool, batches, gpu_results, max_seconds: float) -> dict:
 def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
                  n_queries: int = W.MatchSpec.n_queries, rank: int = 0, world: int = 1,
                  use_runs: bool = True, cpu_seconds: float = 0.0, chunks: int = 0, split: bool = False,
-                 tokens_per_item: int = 0, min_seconds: float = 0.0) -> dict:
-    """match_prefix on the stress tree.  With N ranks, rank 0 builds the tree
+                 tokens_per_item: int = 0, min_seconds: float = 0.0, staged: bool = False,
+                 window_tokens: int = 0) -> dict:
+    """match_prefix on the stress tree (the one-warp walk; with staged=True
+    the two-launch lookup, akv_match_prefix_staged).  With N ranks, rank 0 builds the tree
     through the pool API and broadcasts it (TreeReplicaSync) to every rank's
     replica; each rank then matches its own 4096-query batches (weak
     scaling), timed as the max over ranks.  Rank 0 adds the kernel's
@@ -809,11 +815,14 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
     node = torch.empty(nq, dtype=torch.int32, device=dev)
     mlen = torch.empty(nq, dtype=torch.int32, device=dev)
     cmp_ = torch.empty(nq, dtype=torch.int64, device=dev)
+    totals = [int(off[-1].item()) for _, off in packed]
+    lookup = {"staged": staged, "window_tokens": window_tokens}
     compared = []
     qtokens = []
     results = []
-    for (tok, off), order, plan in zip(packed, orders, plans):
-        tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks, plan=plan)
+    for (tok, off), order, plan, nt in zip(packed, orders, plans, totals):
+        tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks, plan=plan,
+                   n_tokens=nt, **lookup)
         compared.append(int(cmp_.sum()))
         qtokens.append(int(off[-1]))
         results.append((node.cpu().numpy(), mlen.cpu().numpy(), cmp_.cpu().numpy()))
@@ -828,8 +837,9 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         alg = {k: int(statistics.mean(p[k] for p in per)) for k in per[0]}
 
     def run():
-        for (tok, off), order, plan in zip(packed, orders, plans):
-            tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks, plan=plan)
+        for (tok, off), order, plan, nt in zip(packed, orders, plans, totals):
+            tree.match(tok, off, nq, 16, node, mlen, cmp_, order=order, runs=use_runs, chunks=chunks, plan=plan,
+                       n_tokens=nt, **lookup)
 
     # enough repetitions of the rotation for min_seconds (the same count on every rank)
     ms_probe, _ = timed(run, 3, warmup, 1)
@@ -848,7 +858,7 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
     def run_warm():  # one batch again and again: its query tokens stay in L2
         for _ in range(len(packed)):
             tree.match(tok0, off0, nq, 16, node, mlen, cmp_, order=order0, runs=use_runs, chunks=chunks,
-                       plan=plan0)
+                       plan=plan0, n_tokens=totals[0], **lookup)
 
     ms_w, _ = timed(run_warm, steps, warmup, world)
     warm_ms = ms_w / (steps * len(packed))
@@ -892,7 +902,8 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
             else None,
             "peak_source": peak_kind,
             "kernel": (f"akv match_prefix_split (k_match_split), one {nq}-query batch" if split
-                       else f"akv match_prefix (k_match), one {nq}-query batch"),
+                       else f"akv match_prefix_staged (k_match_chase + k_match_verify), one {nq}-query batch"
+                       if staged else f"akv match_prefix (k_match), one {nq}-query batch"),
             "algorithmic_bytes_per_launch": alg,
             "note": "compulsory bytes: 4 B per query token compared, 4 B per distinct edge token touched, "
                     f"{MATCH_NODE_BYTES} B per distinct visited node (rank 0's batches); the kernel is "
@@ -925,6 +936,7 @@ def match_figure(steps: int, warmup: int, n_seqs: int = W.MatchSpec.n_sequences,
         "unary_runs": bool(use_runs),
         "verify_chunks": (chunks & 0xFF) or (4 if split else 8),
         "verify_flags": {"pipelined": bool(chunks & 0x100), "prefetch": bool(chunks & 0x200)},
+        "staged": {"window_tokens": window_tokens or 512} if staged else None,
         "split": ({"tokens_per_range": plans[0].tokens_per_range, "ranges_per_batch": plans[0].n_items}
                   if split else None),
         "roofline": roofline,
@@ -1636,7 +1648,8 @@ def main():
                            use_runs=bool(args.match_runs),
                            cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds,
                            chunks=match_chunks_arg(args), split=bool(args.match_split),
-                           tokens_per_item=args.match_tokens_per_range, min_seconds=args.match_seconds)
+                           tokens_per_item=args.match_tokens_per_range, min_seconds=args.match_seconds,
+                           staged=bool(args.match_staged), window_tokens=args.match_window_tokens)
         if rank == 0:
             print(json.dumps(fig), flush=True)
         if world > 1:
@@ -1846,7 +1859,8 @@ def main():
         match = match_figure(args.warmup, args.warmup, args.match_seqs, args.match_queries,
                              cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds,
                              chunks=match_chunks_arg(args), split=bool(args.match_split),
-                             tokens_per_item=args.match_tokens_per_range, min_seconds=args.match_seconds)
+                             tokens_per_item=args.match_tokens_per_range, min_seconds=args.match_seconds,
+                           staged=bool(args.match_staged), window_tokens=args.match_window_tokens)
 
     if world > 1:
         torch.distributed.barrier()
