@@ -27,7 +27,8 @@ NVCC_FLAGS = [
     "-std=c++17",
     "-lineinfo",
     "-Xcompiler",
-    "-fPIC,-fvisibility=hidden",
+    "-fPIC,-fvisibility=hidden,-pthread",
+    "-lpthread",
     "-cudart",
     "static",
 ]

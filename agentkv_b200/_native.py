@@ -186,6 +186,7 @@ SIGNATURES = {
         C.c_int,
         [C.POINTER(AkvTreeView), _P, _P, _I32, _I32, _P, _P, _P, _P, _P, _I32, _I32, _P, _I64, _I32, _P, _P],
     ),
+    "akv_gather_upload": (C.c_int, [_P, _P, _I32, _P, _P, _I32, _P]),
     "akv_mirror_create": (C.c_void_p, [_I32]),
     "akv_mirror_destroy": (None, [_P]),
     "akv_mirror_load": (C.c_int, [_P, _P, _P, _P, _P, _P]),

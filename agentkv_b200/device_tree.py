@@ -32,7 +32,9 @@ mirror when the tree has changed, and replicas receive the owner's.
 
 from __future__ import annotations
 
+import os
 import time
+from array import array
 from typing import Optional, Sequence, Tuple
 
 import numpy as np
@@ -814,6 +816,17 @@ def pack_queries(queries: Sequence, device: torch.device) -> Tuple[torch.Tensor,
     return _upload(flat, device), _upload(q_off, device)
 
 
+_GATHER_THREADS = max(1, min(8, os.cpu_count() or 1))
+
+
+def _i32(q) -> np.ndarray:
+    """A query as a contiguous int32 array (lists via array('i'), about twice
+    as fast as numpy's conversion)."""
+    if isinstance(q, list):
+        return np.frombuffer(array("i", q), dtype=np.int32)
+    return np.ascontiguousarray(q, dtype=np.int32).reshape(-1)
+
+
 class QueryStage:
     """Reusable buffers for packing lookup batches: host buffers (pinned on a
     GPU, so the uploads are asynchronous) and device buffers that grow with
@@ -822,8 +835,6 @@ class QueryStage:
     after the first batches nothing is allocated.  A batch's buffers are
     reused by the next pack(): the caller finishes the lookup (reads its
     results) first, as match_batch does."""
-
-    UPLOAD_SLICE = 2 << 20  # tokens (8 MB) per upload slice
 
     def __init__(self, device: torch.device) -> None:
         self.device = device
@@ -858,20 +869,19 @@ class QueryStage:
         off = self.h_off.numpy()[: nq + 1]
         off[0] = 0
         np.cumsum(lens, out=off[1:])
-        # The packing goes up in slices of about UPLOAD_SLICE tokens, each as
-        # soon as it is written, so the upload of one slice overlaps the
-        # host's packing of the next.
-        h = self.h_tok.numpy()
-        cuts = [0] if total == 0 else np.unique(np.searchsorted(
-            off, np.arange(self.UPLOAD_SLICE, total, self.UPLOAD_SLICE), side="right")).tolist() + [nq]
-        a = 0
-        for b in cuts:
-            if b <= a:
-                continue
-            lo, hi = int(off[a]), int(off[b])
-            np.concatenate([np.asarray(q, np.int32) for q in queries[a:b]], out=h[lo:hi])
-            self.d_tok[lo:hi].copy_(self.h_tok[lo:hi], non_blocking=True)
-            a = b
+        # One C call gathers the queries into the pinned buffer with several
+        # host threads and enqueues the upload (a single-threaded
+        # np.concatenate of a 73 MB batch took 14 ms on the GPU hosts).
+        if total:
+            arrs = [q if isinstance(q, np.ndarray) and q.dtype == np.int32 and q.flags.c_contiguous
+                    else _i32(q) for q in queries]
+            ptrs = np.fromiter((a.ctypes.data for a in arrs), np.uint64, nq)
+            cuda = self.device.type == "cuda"
+            N.check(N.lib.akv_gather_upload(ptrs.ctypes.data, lens.ctypes.data, nq, self.h_tok.data_ptr(),
+                                            self.d_tok.data_ptr() if cuda else None, _GATHER_THREADS,
+                                            stream_handle(self.device) if cuda else None))
+            if not cuda:
+                self.d_tok[:total].copy_(self.h_tok[:total])
         order = np.argsort(-lens, kind="stable")
         self.h_ord.numpy()[:nq] = order
         self.lens_in_order = lens[order]

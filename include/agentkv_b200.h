@@ -85,6 +85,15 @@ AKV_API int akv_prepare(void);
 AKV_API int akv_copy_wait(void* dst, const void* src, int64_t bytes, int32_t to_host, int32_t wait,
                           void* stream);
 
+/* Gather n host int32 arrays (src[i]: address, lens[i] tokens) back to back
+ * into `dst` (host; pinned for an asynchronous upload) with `threads` host
+ * threads (1-64; one for fewer than 65,536 tokens), then, with d_dst
+ * non-NULL, one asynchronous copy of the packing to d_dst on `stream`.  The
+ * host side of a batched lookup: the reference's callers hold one token list
+ * per query.  Returns after enqueuing the copy. */
+AKV_API int akv_gather_upload(const uint64_t* src, const int64_t* lens, int32_t n, int32_t* dst,
+                              int32_t* d_dst, int32_t threads, void* stream);
+
 /* ── block movement ─────────────────────────────────────────────────────────
  * The pool is the reference's `_kv_data` tensor
  * [total_blocks, L, 2, H_kv, block_size, D] (agentkv/core/slab_allocator.py:155-164)
