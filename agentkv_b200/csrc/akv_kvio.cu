@@ -195,7 +195,10 @@ k_kv_gather_bulk(const char* __restrict__ pool, int64_t bpb, int32_t total, int3
       for (int64_t m = stores + 1; m < loads; ++m)
         mbar_wait(smem_u32(&bars[m % kStages]), static_cast<uint32_t>((m / kStages) & 1));
     }
-    bulk_wait_all();
+    // The CTA may leave once its stores have read their shared-memory
+    // stages; their writes complete with the grid (waiting for them here
+    // only lengthens the kernel's tail).
+    bulk_wait_read<0>();
   }
 }
 
