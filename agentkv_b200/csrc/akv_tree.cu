@@ -298,6 +298,76 @@ AKV_DEV bool chase_segment(Chase& c, const AkvTreeView& tree, const int4* __rest
   return true;
 }
 
+// One verify round of 512 positions [b0, b0 + 512) of a single contiguous
+// range in 16-byte loads: the query token of position p at Q[qd + p], the
+// arena token at arena[oe + p], with oe + b0 a multiple of 4 so that the
+// arena loads are aligned; the query side (any alignment) is loaded as
+// aligned quads and realigned with lane shuffles.  Positions outside
+// [lo, hi) count as equal.  A quad that would reach past the query's end (L)
+// or the arena's (arena_n) is read element by element.  Needs Q's buffer and
+// the arena 16-byte aligned (so an address rounded down to 16 bytes stays
+// inside the buffer).  Returns the first mismatching position, or -1.
+AKV_DEV bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+AKV_DEV int4 ld_quad(const int32_t* __restrict__ base, int64_t idx, int64_t end) {
+  if (idx + 3 < end) return __ldg(reinterpret_cast<const int4*>(base + idx));
+  int4 v = make_int4(0, 0, 0, 0);
+  if (idx < end) v.x = __ldg(base + idx);
+  if (idx + 1 < end) v.y = __ldg(base + idx + 1);
+  if (idx + 2 < end) v.z = __ldg(base + idx + 2);
+  return v;
+}
+
+AKV_DEV int4 shfl_quad(const int4& v, int src) {
+  return make_int4(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src),
+                   __shfl_sync(0xffffffffu, v.z, src), __shfl_sync(0xffffffffu, v.w, src));
+}
+
+AKV_DEV int32_t verify_round_vec(const int32_t* __restrict__ Q, int64_t qd, int64_t L,
+                                 const int32_t* __restrict__ arena, int64_t arena_n, int64_t oe, int32_t b0,
+                                 int32_t lo, int32_t hi, int lane) {
+  constexpr uint32_t kFull = 0xffffffffu;
+  // the query's quads: Q index qa + 128 u + 4 lane, qa = (qd + b0) rounded down
+  // to a 16-byte address; the wanted values start r tokens into them
+  const int64_t qabs = static_cast<int64_t>(reinterpret_cast<uintptr_t>(Q) >> 2) + qd + b0;
+  const int r = static_cast<int>(qabs & 3);
+  const int64_t qa = qd + b0 - r;
+  int4 tq[4], qq[5];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    tq[u] = ld_quad(arena, oe + b0 + 128 * u + 4 * lane, arena_n);
+    qq[u] = ld_quad(Q, qa + 128 * u + 4 * lane, L);
+  }
+  qq[4] = make_int4(0, 0, 0, 0);
+  if (r != 0 && lane == 0) qq[4] = ld_quad(Q, qa + 512, L);  // lane 31's last tokens
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    int4 qv = qq[u];
+    if (r != 0) {  // warp-uniform
+      const int4 w0 = shfl_quad(qq[u], (lane + 1) & 31);
+      const int4 w1 = shfl_quad(qq[u + 1], (lane + 1) & 31);
+      const int4 nx = lane == 31 ? w1 : w0;  // the next quad in the query
+      if (r == 1) qv = make_int4(qv.y, qv.z, qv.w, nx.x);
+      else if (r == 2) qv = make_int4(qv.z, qv.w, nx.x, nx.y);
+      else qv = make_int4(qv.w, nx.x, nx.y, nx.z);
+    }
+    const int32_t p0 = b0 + 128 * u + 4 * lane;
+    int j = 4;  // this lane's first mismatching position in the quad
+    if (p0 + 3 >= lo && p0 < hi) {
+      if (qv.w != tq[u].w && p0 + 3 >= lo && p0 + 3 < hi) j = 3;
+      if (qv.z != tq[u].z && p0 + 2 >= lo && p0 + 2 < hi) j = 2;
+      if (qv.y != tq[u].y && p0 + 1 >= lo && p0 + 1 < hi) j = 1;
+      if (qv.x != tq[u].x && p0 >= lo && p0 < hi) j = 0;
+    }
+    const uint32_t m = __ballot_sync(kFull, j < 4);
+    if (m) {
+      const int l = __ffs(m) - 1;
+      return b0 + 128 * u + 4 * l + __shfl_sync(kFull, j, l);
+    }
+  }
+  return -1;
+}
+
 // The reference's walk (radix_tree.py:513-570) over query Q[0, L), checked
 // on positions [a, b) only; one warp, all lanes.  The walk alternates two
 // phases:
@@ -317,7 +387,8 @@ AKV_DEV bool chase_segment(Chase& c, const AkvTreeView& tree, const int4* __rest
 // lookup.
 template <int kVerifyChunks, bool kPipelined>
 AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict__ Q, int64_t L,
-                              int64_t a, int64_t b, int32_t q, AkvStatus* st, int lane, bool prefetch) {
+                              int64_t a, int64_t b, int32_t q, AkvStatus* st, int lane, bool prefetch,
+                              bool vec) {
   constexpr uint32_t kFull = 0xffffffffu;
   if (prefetch) {
     // Ask L2 for the range's query tokens now (one request per 128-byte
@@ -460,11 +531,35 @@ AKV_DEV MatchStop match_range(const AkvTreeView& tree, const int32_t* __restrict
         if (first >= 0) break;
       }
     } else {
-      for (int32_t base = p_lo; base < p_hi; base += kStep) {
+      for (int32_t base = p_lo; base < p_hi;) {
+        if constexpr (kVerifyChunks == 8) {
+          // 512 positions of one range per round in 16-byte loads: the
+          // segment's edges are contiguous, or the next 512 positions lie in
+          // one edge (or the last)
+          if (vec) {
+            int64_t oe = shift + matched;
+            bool one = contiguous;
+            if (!one) {
+              const int e0 = entry_of(base);
+              const int32_t ex0 = __shfl_sync(kFull, excl, e0);
+              one = ex0 + __shfl_sync(kFull, lim, e0) >= base + 512 || e0 == n - 1;
+              oe = __shfl_sync(kFull, my_off, e0) - ex0;
+            }
+            const int32_t b0 = base - static_cast<int32_t>((oe + base) & 3);
+            // (the query's quads start at or after the packing's first token)
+            if (one && matched + b0 >= 0) {
+              first = verify_round_vec(Q, matched, L, tree.tokens, tree.n_tokens, oe, b0, base, p_hi, lane);
+              if (first >= 0) break;
+              base = b0 + 512;
+              continue;
+            }
+          }
+        }
         int32_t av[kVerifyChunks], bv[kVerifyChunks];
         load_round(base, av, bv);
         check_round(base, av, bv);
         if (first >= 0) break;
+        base += kStep;
       }
     }
     // the first entry the reference would stop in
@@ -500,11 +595,12 @@ AKV_DEV void match_write(const MatchStop& s, int32_t q, int32_t block_size, int3
 
 // One warp per query (the whole query is one range).  `order` (optional)
 // lists the queries longest first, so the long walks start early and spread
-// over the SMs.  (Capping the registers at 72, for 7 CTAs per SM and a
-// 4,096-query batch in one wave, measured slower: 0.0737 against 0.0701 ms
-// per batch on the stress tree, with spills.)
+// over the SMs.  At most 96 registers (5 CTAs per SM): the 16-byte verify
+// rounds alone would take 126 and measured slower for it (0.0729 against
+// 0.0585 ms per batch on the stress tree; without those rounds, 80 registers,
+// 0.0631 ms; capped at 80 with them, 0.0603 ms with spills).
 template <int kVerifyChunks, bool kPipelined>
-__global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
+__global__ void __launch_bounds__(kMatchWarpsPerCta * 32, 5)
 k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
         int32_t nq, int32_t block_size, int32_t* __restrict__ out_node,
         int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared,
@@ -519,7 +615,8 @@ k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __r
   }
   const int64_t qlo = q_off[q];
   const int64_t L = q_off[q + 1] - qlo;
-  const MatchStop s = match_range<kVerifyChunks, kPipelined>(tree, tokens + qlo, L, 0, L, q, st, lane, prefetch);
+  const MatchStop s = match_range<kVerifyChunks, kPipelined>(tree, tokens + qlo, L, 0, L, q, st, lane, prefetch,
+                                                             aligned16(tokens) && aligned16(tree.tokens));
   if (lane == 0) match_write(s, q, block_size, out_node, out_len, out_compared);
 }
 
@@ -563,7 +660,7 @@ AKV_DEV int32_t split_count(int64_t L, int32_t R) {
 }
 
 template <int kVerifyChunks, bool kPipelined>
-__global__ void __launch_bounds__(kMatchWarpsPerCta * 32)
+__global__ void __launch_bounds__(kMatchWarpsPerCta * 32, 5)
 k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
               int32_t nq, int32_t block_size, const __grid_constant__ SplitRanges rg,
               const int32_t* __restrict__ order, int4* __restrict__ stops, int32_t* __restrict__ done,
@@ -594,7 +691,8 @@ k_match_split(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_
   }
   const int64_t a = static_cast<int64_t>(j) * R;
   const int64_t b = a + R < L ? a + R : L;
-  const MatchStop s = match_range<kVerifyChunks, kPipelined>(tree, tokens + qlo, L, a, b, q, st, lane, prefetch);
+  const MatchStop s = match_range<kVerifyChunks, kPipelined>(tree, tokens + qlo, L, a, b, q, st, lane, prefetch,
+                                                             aligned16(tokens) && aligned16(tree.tokens));
   if (k == 1) {
     if (lane == 0) match_write(s, q, block_size, out_node, out_len, out_compared);
     return;
