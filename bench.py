@@ -1096,6 +1096,9 @@ def hf_case(args) -> None:
     res["update_reference_torch_path"] = hf_reference_update_figure(n_blocks, n_tok, args.steps, args.warmup)
     res["update_speedup_vs_reference_torch_path"] = round(
         res["update_reference_torch_path"]["ms_per_decode_step"] / res["update_e2e"]["ms_per_decode_step"], 2)
+    res["update_speedup_note"] = ("the torch arm times the reference's row writes and indexed gather only; "
+                                  "update_e2e also includes the pool calls (block allocation, the "
+                                  "copy-on-write check, the block tables), so the ratio understates ours")
     print(json.dumps({"case": "hf_cache_gather", "tokens": n_tok, "layers": L, "heads": H, "head_dim": D,
                       "peak_gbs": peak, "peak_source": peak_kind, **res,
                       "speedup": round(res["torch_index_permute"]["ms_per_decode_step"] /
@@ -1199,7 +1202,8 @@ COPY_TRAFFIC_NCU = {
     584: (1322233344, "ncu: the 584-pair Tree-of-Thought copy launch (k_copy_bulk<16384,12>), 3,200-block pool"),
 }
 MATCH_TRAFFIC_NCU = {
-    2000: (51047424, "ncu: one 4,096-query k_match batch on the 2,000-sequence stress tree"),
+    2000: (52435200, "ncu: one 4,096-query k_match batch on the 2,000-sequence stress tree "
+                     "(profiles/match_prefix_stress2k.md, k_match with 16-byte verify rounds)"),
 }
 
 
