@@ -686,6 +686,44 @@ class SlabAllocator:
                 self._stream()))
         return out_blocks, out_copied
 
+    def cow_many(self, blocks) -> Tuple[np.ndarray, np.ndarray]:
+        """ensure_mutable over a batch of residual blocks (distinct slots), in
+        order, answered on the host mirror: (blocks now owned, 1 where a copy
+        happened) as host arrays, the block copies enqueued in one launch.
+        MemoryError, with nothing changed, when the copies would run the pool
+        dry."""
+        ids = np.asarray(blocks, np.int32).reshape(-1)
+        with self._lock:
+            self._pending()
+            m = self._host()
+            # all or nothing: count the copies first (a request copies while
+            # its block is still shared after the earlier requests' copies)
+            copies, taken = 0, {}
+            for x in ids.tolist():
+                r = m.ref(x)
+                if r == -(1 << 31):
+                    raise self._exception(N.AKV_ERR_OUT_OF_RANGE, x, 0, "ensure_mutable_block")
+                if r - taken.get(x, 0) > 1:
+                    copies += 1
+                    taken[x] = taken.get(x, 0) + 1
+            c = m.ctl()
+            avail = c[N.CTL_FREE_SIZE] + c[N.CTL_LIMBO_REL] - c[N.CTL_LIMBO_HEAD]
+            if copies and (c[N.CTL_FREE_SIZE] < 1 or avail < copies):
+                raise self._exception(N.AKV_ERR_EXHAUSTED, -1, int(c[N.CTL_FREE_SIZE]), "ensure_mutable_block")
+            tick = self._tick()
+            out = np.empty(len(ids), np.int32)
+            for i, x in enumerate(ids.tolist()):
+                out[i] = m.cow(x, tick)
+            copied = (out != ids).astype(np.int32)
+            if copies and self._kv_data.device.type != "meta":
+                pairs = np.stack([ids[copied == 1], out[copied == 1]], axis=1).reshape(-1)
+                d = self._ids.put(pairs)
+                N.check(N.lib.akv_copy_blocks(self._kv_data.data_ptr(), self._cfg.bytes_per_block,
+                                              self._cfg.total_blocks, d.data_ptr(), copies, None,
+                                              self._status.data_ptr(), self._stream()))
+            self._maybe_flush()
+            return out, copied
+
     def fanout_level(self, parent_tables: torch.Tensor, parent_off: torch.Tensor, parent_lens,
                      fanout: int, append: int, *, pool: Optional[torch.Tensor] = None,
                      copy: bool = True) -> dict:

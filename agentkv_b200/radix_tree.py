@@ -9,13 +9,16 @@ size, an insert that diverges inside the first block overwrites the sibling
 with the same first token, an exact re-commit replaces the node's blocks).
 
 What moved to the GPU:
-* every refcount change goes to the device allocator, one launch per tree
-  operation (fork inc_refs all inherited blocks in one batch, free dec_refs
-  the residual blocks and any pruned node blocks in one batch);
-* copy-on-write is one fused launch (akv_cow_batch: refcount test, alloc,
-  block copy, dec_ref) — unless the allocator's copy_block was replaced on the
-  instance (the vLLM adapter records CoW pairs that way), in which case the
-  reference's per-step sequence runs and calls that replacement;
+* every refcount change reaches the device allocator as one batch per tree
+  operation (fork inc_refs all inherited blocks, free dec_refs the residual
+  blocks and any pruned node blocks): answered at the call by the
+  allocator's host mirror and replayed on the device from its op log, or
+  launched directly on the device for batches of device ids;
+* copy-on-write decides on the mirror (refcount test, alloc, dec_ref) and
+  enqueues the block copies in one launch — unless the allocator's copy_block
+  was replaced on the instance (the vLLM adapter records CoW pairs that way),
+  in which case the reference's per-step sequence runs and calls that
+  replacement;
 * _match_prefix_locked is the akv_match_prefix kernel over the tree's device
   replica (device_tree.py), which every structural change keeps current.
 
@@ -248,10 +251,7 @@ class DualRadixTree:
                 return [self.ensure_mutable_block(h, i).block_id != b
                         for (h, i), b in zip(requests, [h.residual_blocks[i].block_id for h, i in requests])]
             blocks = np.fromiter((h.residual_blocks[i].block_id for h, i in requests), np.int32, len(requests))
-            out, copied = self._alloc.cow_batch(blocks)
-            self._alloc.check()
-            out_h = out.cpu().numpy()
-            cp_h = copied.cpu().numpy()
+            out_h, cp_h = self._alloc.cow_many(blocks)  # answered at the call, the copies enqueued
             for (h, i), nb, c in zip(requests, out_h, cp_h):
                 if c:
                     h.residual_blocks[i] = BlockHandle(int(nb))

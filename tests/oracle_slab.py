@@ -80,6 +80,10 @@ class OracleSlab:
             _raise(e)
         return torch.from_numpy(out.copy()), torch.from_numpy(copied.copy())
 
+    def cow_many(self, blocks):
+        out, copied = self.cow_batch(blocks)
+        return out.numpy(), copied.numpy()
+
     def cow_one(self, block_id: int) -> int:
         out, _ = self.cow_batch([block_id])
         return int(out[0])

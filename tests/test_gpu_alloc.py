@@ -309,6 +309,48 @@ def test_cow_batch_exhaustion_is_all_or_nothing():
         np.testing.assert_array_equal(before[k], after[k])
 
 
+@pytest.mark.parametrize("seed", range(3))
+def test_cow_many_matches_oracle(seed):
+    """ensure_mutable over a batch answered on the host mirror (cow_many),
+    the copies enqueued in one launch: the same blocks, copies, allocator
+    state and pool bytes as the oracle's batch, with contested blocks."""
+    rng = np.random.default_rng(40 + seed)
+    n_blocks, shape = 300, (1, 2, 4, 16)
+    a = make_alloc(n_blocks, interval=[3, 7, 64][seed], device="cuda", bpb_shape=shape)
+    o = O.OracleAllocator(n_blocks, [3, 7, 64][seed])
+    bpb = a.config.bytes_per_block
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    host = torch.randint(-30000, 30000, (n_blocks, bpb // 2), dtype=torch.int16, generator=g)
+    a._kv_data.view(torch.int16).view(n_blocks, -1).copy_(host)
+    host = host.numpy().view(np.uint8).reshape(n_blocks, -1).copy()
+    ids = np.asarray([a.alloc().block_id for _ in range(100)], np.int32)
+    o.alloc_batch(100)
+    incs = np.repeat(ids, rng.integers(0, 4, size=len(ids)))
+    a.inc_ref_batch(incs)
+    o.inc_ref_batch(incs)
+    for rnd in range(4):
+        blocks = rng.choice(ids, size=int(rng.integers(1, 60)))
+        ob, oc = a.cow_many(blocks)
+        want_b, want_c = o.cow_batch(blocks, host, bpb)
+        np.testing.assert_array_equal(ob, want_b, err_msg=f"round {rnd}")
+        np.testing.assert_array_equal(oc, want_c)
+        a.check()
+        assert_same_as_oracle(a, o, f"cow_many round {rnd}")
+        dev_bytes = a._kv_data.view(n_blocks, -1).view(torch.uint8).cpu().numpy()
+        np.testing.assert_array_equal(dev_bytes, host)
+        ids = np.unique(np.concatenate([ids, want_b]))
+    # exhaustion: refused at the call, nothing changed
+    free = len(o.state()["free_list"])
+    shared = np.flatnonzero(o.state()["ref_counts"] > 1)[: free + 1]
+    if len(shared) > free:
+        before = device_state(a)
+        with pytest.raises(MemoryError):
+            a.cow_many(shared)
+        after = device_state(a)
+        for k in ("ref", "free"):
+            np.testing.assert_array_equal(before[k], after[k])
+
+
 def test_cpu_pool_is_rejected():
     with pytest.raises(ValueError, match="CUDA"):
         make_alloc(8, device="cpu")
