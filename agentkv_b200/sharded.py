@@ -13,6 +13,13 @@ Batches of varying size travel as one fixed-size buffer (`pack_batch`): an
 int64 pair count followed by room for `max_pairs` pairs; the copy reads the
 count on the device (akv_copy_blocks_counted), so receiving ranks never wait
 on the host for it.
+
+Partitioned planning instead splits the block ids: rank r owns the range
+[r*B, (r+1)*B) (`partition`) and plans, with an allocator over B blocks, the
+agents whose blocks lie there; the ranks all-gather their pair lists
+(`gather_pairs`, ids made global by adding each rank's base) and every rank
+copies all of them on its slice.  Each rank's allocator work then stays the
+same as ranks are added, where a single planner's grows with them.
 """
 
 from __future__ import annotations
@@ -42,6 +49,15 @@ def head_slice(pool: torch.Tensor, rank: int, world: int) -> torch.Tensor:
     return pool[:, :, :, rank * h : (rank + 1) * h]
 
 
+def partition(total_blocks: int, rank: int, world: int) -> tuple:
+    """(base, count): the block ids rank `rank` plans for under partitioned
+    planning, [base, base + count)."""
+    if world < 1 or not 0 <= rank < world or total_blocks % world:
+        raise ValueError(f"{total_blocks} blocks do not split into {world} equal ranges (rank {rank})")
+    count = total_blocks // world
+    return rank * count, count
+
+
 class ShardedCopier:
     """Applies rank 0's copy batches to this rank's head slice."""
 
@@ -65,6 +81,30 @@ class ShardedCopier:
         if self.world > 1:
             dist.broadcast(buf, src=self.src, group=self.group)
         return buf
+
+    def gather_pairs(self, pairs: torch.Tensor, base: int, out: torch.Tensor,
+                     send: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Partitioned planning: every rank passes its (n, 2) int32 pairs in
+        its own ids (0 .. count-1 of its range, the same n on every rank) and
+        its range's `base`; `out` ((world * n, 2) int32) receives every
+        rank's pairs in rank order with global ids.  `send` ((n, 2) int32) is
+        the staging buffer for this rank's shifted pairs (allocated when
+        None).  On GPUs: one elementwise add and one NCCL all-gather on the
+        current stream, both capturable in a CUDA graph."""
+        import torch.distributed as dist
+
+        pairs = pairs.reshape(-1, 2)
+        if out.dtype != torch.int32 or pairs.dtype != torch.int32:
+            raise ValueError("gather_pairs: pairs and out must be int32")
+        if out.shape != (self.world * pairs.shape[0], 2):
+            raise ValueError(f"gather_pairs: out is {tuple(out.shape)}, expected "
+                             f"({self.world * pairs.shape[0]}, 2)")
+        send = torch.add(pairs, base, out=send if send is not None else torch.empty_like(pairs))
+        if self.world > 1:
+            dist.all_gather_into_tensor(out, send, group=self.group)
+        else:
+            out.copy_(send)
+        return out
 
     def copy(self, pairs: torch.Tensor, **kw) -> None:
         K.copy_blocks(self.pool, pairs, **kw)

@@ -95,9 +95,11 @@ def parse_args():
     ap.add_argument("--no-graph", action="store_true", help="launch every kernel from Python each step")
     ap.add_argument("--trees", type=int, default=0, help="fan-outs per step (default: one per GPU)")
     ap.add_argument("--heads-per-rank", type=int, default=0, help="KV heads per rank (default: 8 / GPUs)")
-    ap.add_argument("--plan", default="replicated", choices=["bcast-level", "bcast-once", "replicated"],
-                    help="N > 1: every rank runs the same deterministic allocator (default, no collective "
-                         "in the step), or rank 0 plans and broadcasts each level's pairs / all pairs once")
+    ap.add_argument("--plan", default="replicated", choices=["bcast-level", "bcast-once", "replicated", "sharded"],
+                    help="N > 1: every rank runs the same deterministic allocator for every tree (default, no "
+                         "collective in the step); rank 0 plans and broadcasts each level's pairs / all pairs "
+                         "once; or (sharded) each rank plans its own trees in its own range of block ids and "
+                         "the ranks all-gather the pair lists")
     ap.add_argument("--graph-nccl", type=int, default=1,
                     help="N > 1: capture the step, NCCL pair broadcast included, as a CUDA graph")
     ap.add_argument("--graph-steps", type=int, default=8,
@@ -238,11 +240,16 @@ class ToTBench:
         self.trees = trees or world
         self.n_blocks = blocks_per_tree * self.trees
         self.slice_heads = heads_per_rank or H // world
-        self.plan = plan if world > 1 else "replicated"
+        self.plan = plan if world > 1 or plan == "sharded" else "replicated"
         # all levels' pairs in one copy launch once the last level is planned
         # (valid because appended blocks make the levels' pairs independent)
         self.merge = merge and self.spec.appended_blocks >= 1 and self.plan != "bcast-level"
-        self.planner = rank == 0 or self.plan == "replicated"
+        self.planner = rank == 0 or self.plan in ("replicated", "sharded")
+        if self.plan == "sharded" and (self.trees % world or not self.merge):
+            raise SystemExit(f"--plan sharded: {self.trees} trees must split evenly over {world} ranks "
+                             "(and the levels' pairs go in one launch)")
+        # the trees this rank plans: all of them, or its own under --plan sharded
+        self.plan_trees = self.trees // world if self.plan == "sharded" else self.trees
         # this rank's head slice of every block: [N, L, 2, H/world, bs, D]
         self.pool = torch.empty((self.n_blocks, L, 2, self.slice_heads, bs, D), dtype=torch.bfloat16,
                                 device=self.dev)
@@ -256,7 +263,7 @@ class ToTBench:
         root_len = self.spec.root_tokens // bs
         # parent table lengths per level are fixed by the workload
         self.level_lens = []
-        lens = np.full(self.trees, root_len, np.int64)
+        lens = np.full(self.plan_trees, root_len, np.int64)
         for _ in range(self.spec.levels):
             self.level_lens.append(lens)
             lens = np.repeat(lens + self.spec.appended_blocks, self.spec.fanout)
@@ -267,14 +274,18 @@ class ToTBench:
             self.level_off.append(torch.from_numpy(off).to(self.dev))
         self.pairs_bufs = [torch.empty((n, 2), dtype=torch.int32, device=self.dev) for n in self.pairs_per_level]
         self.all_pairs_buf = torch.empty((sum(self.pairs_per_level), 2), dtype=torch.int32, device=self.dev)
-        from agentkv_b200.sharded import ShardedCopier
+        from agentkv_b200.sharded import ShardedCopier, partition
 
         self.copier = ShardedCopier(self.pool)
+        # --plan sharded: this rank's allocator covers its own range of the ids
+        self.id_base, plan_blocks = (partition(self.n_blocks, rank, world) if self.plan == "sharded"
+                                     else (0, self.n_blocks))
+        self.send_buf = torch.empty((sum(self.pairs_per_level) // world, 2), dtype=torch.int32, device=self.dev)
         if self.planner:
-            cfg = PoolConfig(total_blocks=self.n_blocks, block_size=bs, num_layers=L, num_kv_heads=H,
+            cfg = PoolConfig(total_blocks=plan_blocks, block_size=bs, num_layers=L, num_kv_heads=H,
                              head_dim=D, dtype=dt, device="meta")
             self.alloc = SlabAllocator(cfg)
-            self.root_tables = self.alloc.alloc_batch(root_len * self.trees)
+            self.root_tables = self.alloc.alloc_batch(root_len * self.plan_trees)
             self.alloc.check()
             self.root_host = self.root_tables.cpu().pin_memory()
             self.meta = torch.cuda.Stream(self.dev)
@@ -328,6 +339,13 @@ class ToTBench:
                                              self.spec.appended_blocks, level_offsets=self.level_off,
                                              on_level=on_level)
                 launches += res["launches"]
+                if self.plan == "sharded":
+                    # every rank's pairs, in global ids, before this rank's frees; a new
+                    # buffer per fan-out (the copy stream may still read the last one)
+                    gathered = torch.empty_like(self.all_pairs_buf)
+                    self.copier.gather_pairs(res["all_pairs"], self.id_base, gathered, send=self.send_buf)
+                    gathered.record_stream(cs)
+                    on_level(-1)
                 frees = res.get("all_tables")
                 if frees is None:
                     frees = torch.cat(res["child_tables"])
@@ -347,6 +365,9 @@ class ToTBench:
                 else:
                     allp = None
                 allp = self.copier.share_pairs(allp, sum(self.pairs_per_level), out=self.all_pairs_buf)
+            elif self.plan == "sharded":
+                allp = gathered
+                cs.wait_event(events[-1])  # recorded after the gather
             else:
                 allp = res["all_pairs"]
                 allp.record_stream(cs)

@@ -10,6 +10,9 @@
   rank copies its head slice with the count read on the device.  Every slice
   must equal the same heads of the oracle's pool after the reference's
   recorded pairs.
+* Partitioned planning: each rank plans a fan-out in its own range of block
+  ids, the ranks all-gather the pair lists and every slice takes all of them
+  (checked against the oracle's copy of the full pool).
 * match_prefix over replicas: rank 0 builds the stress tree through the pool
   API and broadcasts its deltas as it grows; each rank matches its
   contiguous range of the reference's recorded queries on its own replica;
@@ -82,6 +85,52 @@ def _worker(rank, port, q):
         dist.all_gather(gathered, allp)
         same = all(torch.equal(gathered[0], x) for x in gathered)
         q.put((rank, ok, same))
+    finally:
+        dist.destroy_process_group()
+
+
+def _partition_worker(rank, port, q):
+    """Partitioned planning: each rank runs a Tree-of-Thought fan-out on an
+    allocator over its own range of block ids, the ranks all-gather the pair
+    lists, and each rank copies every rank's pairs on its head slice."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from agentkv_b200 import sharded as S
+    from agentkv_b200.allocator import SlabAllocator
+    from agentkv_b200.config import PoolConfig
+    from oracle import oracle as O
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        n, L, H, bs, D = 400, 2, 8, 16, 32
+        g = torch.Generator(device="cpu").manual_seed(78)
+        full = torch.randint(-30000, 30000, (n, L, 2, H, bs, D), dtype=torch.int16, generator=g)
+        mine = S.head_slice(full, rank, WORLD).contiguous().to(dev)
+        copier = S.ShardedCopier(mine)
+        base, count = S.partition(n, rank, WORLD)
+        a = SlabAllocator(PoolConfig(total_blocks=count, block_size=bs, num_layers=L, num_kv_heads=H,
+                                     head_dim=D, dtype="float16", device="meta"))
+        roots = a.alloc_batch(6)
+        res = a.fanout_tree(roots, [3, 3], 2, 3, 1)
+        local = res["all_pairs"]
+        out = torch.empty((WORLD * local.shape[0], 2), dtype=torch.int32, device=dev)
+        got = copier.gather_pairs(local, base, out)
+        copier.copy(got)
+        a.check()
+        torch.cuda.synchronize()
+        everyone = [torch.empty_like(local) for _ in range(WORLD)]
+        dist.all_gather(everyone, local + base)
+        pairs_ok = bool(torch.equal(got, torch.cat(everyone)))
+        host = full.numpy().view(np.uint8).reshape(n, -1).copy()
+        O.copy_blocks(host, host.shape[1], got.cpu().numpy())
+        want = S.head_slice(torch.from_numpy(host.view(np.int16).reshape(full.shape)), rank, WORLD)
+        q.put((rank, bool(torch.equal(mine.cpu(), want)), pairs_ok))
     finally:
         dist.destroy_process_group()
 
@@ -248,3 +297,11 @@ def test_sharded_fanout_two_gpus():
     res = sorted(q.get(timeout=5) for _ in range(WORLD))
     assert all(ok for _, ok, _ in res), res
     assert all(same for _, _, same in res), res
+
+
+def test_partitioned_planning_two_gpus():
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+    res = _spawn(_partition_worker)
+    assert all(ok for _, ok, _ in res), res
+    assert all(pairs_ok for _, _, pairs_ok in res), res

@@ -66,6 +66,46 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def _partition_worker(rank, world, port, q):
+    """Partitioned planning: each rank plans its own range of block ids with
+    an allocator over that range alone; the gathered pairs, in global ids,
+    are every rank's pairs in rank order, and every slice takes all of them."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import oracle as O
+
+        n, L, H, bs, D = 32, 2, 4, 4, 8
+        g = torch.Generator().manual_seed(9)
+        full = torch.randint(-(2**30), 2**30, (n, L, 2, H, bs, D), dtype=torch.int32, generator=g)
+        mine = S.head_slice(full, rank, world).contiguous()
+        copier = S.ShardedCopier(mine)
+        base, count = S.partition(n, rank, world)
+        a = O.OracleAllocator(count)
+        roots = a.alloc_batch(3 + rank)  # the ranks' plans differ
+        kids = a.alloc_batch(5)
+        local = np.stack([np.resize(roots, 5), kids], 1).astype(np.int32)
+        out = torch.empty((world * 5, 2), dtype=torch.int32)
+        got = copier.gather_pairs(torch.from_numpy(local), base, out)
+        everyone = [torch.empty((5, 2), dtype=torch.int32) for _ in range(world)]
+        dist.all_gather(everyone, torch.from_numpy(local + base))
+        host = mine.numpy().view(np.uint8).reshape(n, -1).copy()
+        O.copy_blocks(host, host.shape[1], got.numpy())
+        mine_after = torch.from_numpy(host.view(np.int32).reshape(mine.shape))
+        parts = [torch.empty_like(mine_after) for _ in range(world)]
+        dist.all_gather(parts, mine_after)
+        if rank == 0:
+            fhost = full.numpy().view(np.uint8).reshape(n, -1).copy()
+            O.copy_blocks(fhost, fhost.shape[1], got.numpy())
+            want = torch.from_numpy(fhost.view(np.int32).reshape(full.shape))
+            in_range = all(((p_ >= r * count) & (p_ < (r + 1) * count)).all() for r, p_ in enumerate(everyone))
+            q.put((bool(torch.equal(got, torch.cat(everyone))) and bool(in_range),
+                   bool(torch.equal(torch.cat(parts, dim=3), want))))
+    finally:
+        dist.destroy_process_group()
+
+
 def _batch_worker(rank, world, port, q, golden):
     """Variable-size batches (count + pairs in one buffer) of the ReAct
     trace's recorded pairs, one broadcast per step."""
@@ -229,6 +269,25 @@ def test_sharded_pairs_and_slices_gloo():
     same_pool, same_pairs = _run(_worker)
     assert same_pairs, "ranks saw different pair lists"
     assert same_pool, "reassembled head slices differ from the unsharded copy"
+
+
+def test_partitioned_planning_gloo():
+    same_pairs, same_pool = _run(_partition_worker)
+    assert same_pairs, "the gathered pairs are not every rank's pairs in rank order, in global ids"
+    assert same_pool, "reassembled head slices differ from the unsharded copy of every rank's pairs"
+
+
+def test_partition_math():
+    assert S.partition(120, 0, 2) == (0, 60) and S.partition(120, 1, 2) == (60, 60)
+    assert S.partition(480000, 7, 8) == (420000, 60000)
+    for bad in ((10, 0, 3), (8, 2, 2), (8, -1, 2)):
+        with pytest.raises(ValueError):
+            S.partition(*bad)
+    copier = S.ShardedCopier(torch.zeros(4, 1, 2, 1, 1, 1))
+    with pytest.raises(ValueError):  # out must hold world x n pairs
+        copier.gather_pairs(torch.zeros((3, 2), dtype=torch.int32), 0, torch.empty((4, 2), dtype=torch.int32))
+    got = copier.gather_pairs(torch.tensor([[1, 2]], dtype=torch.int32), 5, torch.empty((1, 2), dtype=torch.int32))
+    assert got.tolist() == [[6, 7]]
 
 
 def test_head_slicing_math():
