@@ -771,7 +771,7 @@ class SlabAllocator:
                 "child_lens": np.repeat(lens + A, K), "launches": launches}
 
     def fanout_tree(self, root_tables: torch.Tensor, root_lens, levels: int, fanout: int, append: int,
-                    *, level_offsets=None, on_level=None) -> dict:
+                    *, level_offsets=None, on_level=None, pairs_out: Optional[torch.Tensor] = None) -> dict:
         """A whole multi-level fan-out (Tree-of-Thought): `levels` levels of
         fanout_level starting from the roots, children of one level being the
         parents of the next, children in (parent, child) order.
@@ -791,9 +791,11 @@ class SlabAllocator:
         append >= 1, `all_tables` every level's child tables); with append >= 1
         (`independent`) no pair's source is another pair's destination (a
         child's last block, the next level's source, is an appended block),
-        so all levels may be copied in one launch.  Returns per-level device
-        tensors child_tables / pairs, all_pairs, independent and the launch
-        count."""
+        so all levels may be copied in one launch.  `pairs_out`, an int32
+        (n_pairs, 2) tensor on the allocator's device, becomes all_pairs, so
+        that an on_level callback can pass the pairs planned so far on.
+        Returns per-level device tensors child_tables / pairs, all_pairs,
+        independent and the launch count."""
         K, A = int(fanout), int(append)
         if K < 0 or A < 0 or levels < 0:
             raise ValueError(f"fanout_tree: negative fanout / append / levels ({K}, {A}, {levels})")
@@ -816,8 +818,11 @@ class SlabAllocator:
         n_pairs = sum(P * K for P, _ in shapes)
         with self._lock:
             self._device_op()  # the planner's batches run on the device
+        if pairs_out is not None and (pairs_out.dtype != torch.int32 or pairs_out.device != dev or
+                                      tuple(pairs_out.shape) != (n_pairs, 2) or not pairs_out.is_contiguous()):
+            raise ValueError(f"fanout_tree: pairs_out must be a contiguous int32 ({n_pairs}, 2) tensor on {dev}")
         fresh_all = self.alloc_batch(n_fresh)
-        all_pairs = torch.empty((n_pairs, 2), dtype=torch.int32, device=dev)
+        all_pairs = pairs_out if pairs_out is not None else torch.empty((n_pairs, 2), dtype=torch.int32, device=dev)
         if A >= 1 and 0 < levels <= N.MAX_FANOUT_LEVELS and n_pairs:
             return self._fanout_tree_fused(root_tables, lens, shapes, K, A, fresh_all, all_pairs,
                                            level_offsets, on_level)

@@ -20,6 +20,13 @@ two recorded instances, hiding the host's read-back and relaunch behind the
 other instance's replay.  Requirements: the roots' table lengths are
 fixed at construction, and nothing else uses the allocator between runs on
 another stream.
+
+With a `copier` (sharded.ShardedCopier) the fan-out takes part in
+partitioned planning: the allocator covers this rank's range of block ids
+(starting at `id_base`), the recorded step all-gathers every rank's pair
+list after its plan and copies all of them on `pool`, this rank's head slice
+of every rank's blocks.  Every rank replays its graph the same number of
+times, in the same order.
 """
 
 from __future__ import annotations
@@ -37,8 +44,12 @@ from .allocator import SlabAllocator
 class FanoutGraph:
     def __init__(self, alloc: SlabAllocator, root_lens, levels: int, fanout: int, append: int, *,
                  pool: Optional[torch.Tensor] = None, free_children: bool = False, variant: int = 0,
-                 merge: bool = True) -> None:
+                 merge: bool = True, copier=None, id_base: int = 0) -> None:
         self.alloc = alloc
+        self.copier, self.id_base = copier, int(id_base)
+        if copier is not None and not (merge and int(append) >= 1):
+            raise ValueError("FanoutGraph: partitioned planning copies every level in one launch "
+                             "(merge=True, append >= 1)")
         self.dev = alloc.device
         self.levels, self.fanout, self.append = int(levels), int(fanout), int(append)
         self.root_lens = np.asarray(root_lens, np.int64)
@@ -86,16 +97,24 @@ class FanoutGraph:
         meta = self._meta = torch.cuda.Stream(self.dev)
         meta.wait_stream(cs)
         events = []
+        local = gathered = None
+        if self.copier is not None:
+            # the gather starts as soon as the last level is planned, before the
+            # refcount batches, so the copy waits for the plan and the gather only
+            local = torch.empty((self.copies_per_run, 2), dtype=torch.int32, device=self.dev)
+            gathered = torch.empty((self.copier.world * self.copies_per_run, 2), dtype=torch.int32, device=self.dev)
         with torch.cuda.stream(meta):
             self.d_roots.copy_(self.h_roots, non_blocking=True)
 
-            def on_level(_lvl):
+            def on_level(lvl):
+                if gathered is not None and lvl == self.levels - 1:
+                    self.copier.gather_pairs(local, self.id_base, gathered)  # every rank's pairs, global ids
                 ev = torch.cuda.Event()
                 ev.record(meta)
                 events.append(ev)
 
             res = self.alloc.fanout_tree(self.d_roots, self.root_lens, self.levels, self.fanout, self.append,
-                                         level_offsets=self.level_off, on_level=on_level)
+                                         level_offsets=self.level_off, on_level=on_level, pairs_out=local)
             launches = res["launches"]
             tables = res.get("all_tables")
             if tables is None:
@@ -107,8 +126,10 @@ class FanoutGraph:
         if self.pool.device.type != "meta" and events:
             if self.merge and res["independent"]:
                 # every level's pairs in one launch once the last level is planned
+                # (and, with a copier, once every rank's pairs are here)
                 cs.wait_event(events[-1])
-                K.copy_blocks(self.pool, res["all_pairs"], variant=self.variant, status=self._copy_status)
+                K.copy_blocks(self.pool, res["all_pairs"] if gathered is None else gathered, variant=self.variant,
+                              status=self._copy_status)
                 launches += 1
             else:
                 for lvl, pairs in enumerate(res["pairs"]):
@@ -117,7 +138,7 @@ class FanoutGraph:
                     launches += 1
         cs.wait_stream(meta)
         self.h_status.copy_(self.alloc._status, non_blocking=True)
-        self._keep = (res, tables, events)
+        self._keep = (res, tables, events, gathered)
         self.launches_per_run = launches
 
     @property
@@ -159,7 +180,7 @@ class FanoutGraph:
         if self._twin is None:
             self._twin = FanoutGraph(self.alloc, self.root_lens, self.levels, self.fanout, self.append,
                                      pool=self.pool, free_children=self.free_children, variant=self.variant,
-                                     merge=self.merge)
+                                     merge=self.merge, copier=self.copier, id_base=self.id_base)
         return self._twin
 
     def run_many(self, roots_list, on_result=None) -> list:

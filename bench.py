@@ -95,11 +95,11 @@ def parse_args():
     ap.add_argument("--no-graph", action="store_true", help="launch every kernel from Python each step")
     ap.add_argument("--trees", type=int, default=0, help="fan-outs per step (default: one per GPU)")
     ap.add_argument("--heads-per-rank", type=int, default=0, help="KV heads per rank (default: 8 / GPUs)")
-    ap.add_argument("--plan", default="replicated", choices=["bcast-level", "bcast-once", "replicated", "sharded"],
-                    help="N > 1: every rank runs the same deterministic allocator for every tree (default, no "
-                         "collective in the step); rank 0 plans and broadcasts each level's pairs / all pairs "
-                         "once; or (sharded) each rank plans its own trees in its own range of block ids and "
-                         "the ranks all-gather the pair lists")
+    ap.add_argument("--plan", default=None, choices=["bcast-level", "bcast-once", "replicated", "sharded"],
+                    help="N > 1: each rank plans its own trees in its own range of block ids and the ranks "
+                         "all-gather the pair lists (sharded, the default); every rank runs the same "
+                         "deterministic allocator for every tree (replicated, no collective in the step); or "
+                         "rank 0 plans and broadcasts each level's pairs / all pairs once")
     ap.add_argument("--graph-nccl", type=int, default=1,
                     help="N > 1: capture the step, NCCL pair broadcast included, as a CUDA graph")
     ap.add_argument("--graph-steps", type=int, default=8,
@@ -330,22 +330,26 @@ class ToTBench:
                 else:
                     roots = self.root_tables
 
-                def on_level(_lvl):
+                local = gathered = None
+                if self.plan == "sharded":
+                    # every rank's pairs in global ids, gathered as soon as the last
+                    # level is planned; new buffers per fan-out (the copy stream may
+                    # still read the last ones)
+                    local = torch.empty_like(self.send_buf)
+                    gathered = torch.empty_like(self.all_pairs_buf)
+                    gathered.record_stream(cs)
+
+                def on_level(lvl):
+                    if gathered is not None and lvl == self.spec.levels - 1:
+                        self.copier.gather_pairs(local, self.id_base, gathered, send=self.send_buf)
                     ev = torch.cuda.Event()
                     ev.record(self.meta)
                     events.append(ev)
 
                 res = self.alloc.fanout_tree(roots, self.level_lens[0], self.spec.levels, self.spec.fanout,
                                              self.spec.appended_blocks, level_offsets=self.level_off,
-                                             on_level=on_level)
+                                             on_level=on_level, pairs_out=local)
                 launches += res["launches"]
-                if self.plan == "sharded":
-                    # every rank's pairs, in global ids, before this rank's frees; a new
-                    # buffer per fan-out (the copy stream may still read the last one)
-                    gathered = torch.empty_like(self.all_pairs_buf)
-                    self.copier.gather_pairs(res["all_pairs"], self.id_base, gathered, send=self.send_buf)
-                    gathered.record_stream(cs)
-                    on_level(-1)
                 frees = res.get("all_tables")
                 if frees is None:
                     frees = torch.cat(res["child_tables"])
@@ -367,7 +371,7 @@ class ToTBench:
                 allp = self.copier.share_pairs(allp, sum(self.pairs_per_level), out=self.all_pairs_buf)
             elif self.plan == "sharded":
                 allp = gathered
-                cs.wait_event(events[-1])  # recorded after the gather
+                cs.wait_event(events[-1])  # recorded after the gather was issued
             else:
                 allp = res["all_pairs"]
                 allp.record_stream(cs)
@@ -1688,7 +1692,8 @@ def main():
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
-    bench = ToTBench(rank, world, args.blocks, args.variant, args.trees, args.heads_per_rank, args.plan,
+    plan = args.plan or ("sharded" if world > 1 else "replicated")
+    bench = ToTBench(rank, world, args.blocks, args.variant, args.trees, args.heads_per_rank, plan,
                      merge=args.copy_levels == "merged")
     F = max(1, args.fanouts_per_step)
     graph = None
@@ -1806,14 +1811,17 @@ def main():
     e2e = None
     if not args.no_e2e:
         res = {}
-        if bench.plan == "replicated" and use_graph:
+        graph_e2e = bench.plan in ("replicated", "sharded") and use_graph
+        if graph_e2e:
             # the public FanoutGraph API: host root tables in, every child's
             # table and the status word back to host memory, one graph replay
+            # (under --plan sharded the graph also all-gathers the pair lists)
             from agentkv_b200.fanout import FanoutGraph
 
             fg = FanoutGraph(bench.alloc, bench.level_lens[0], bench.spec.levels, bench.spec.fanout,
                              bench.spec.appended_blocks, pool=bench.pool, free_children=True,
-                             variant=args.variant)
+                             variant=args.variant,
+                             copier=bench.copier if bench.plan == "sharded" else None, id_base=bench.id_base)
             roots_np = bench.root_host.numpy()
             res["io"] = (fg.h2d_bytes, fg.d2h_bytes)
             e2e_api = "FanoutGraph.run (one CUDA graph replay and one wait per fan-out)"
@@ -1834,7 +1842,7 @@ def main():
                "h2d_bytes_per_step": int(h2d) * F, "d2h_bytes_per_step": int(d2h) * F,
                "ms_per_step": round(e_fanout * F, 4), "api": e2e_api,
                "fanouts_timed": pc_fanouts}
-        if bench.plan == "replicated" and use_graph and not args.no_pipeline:
+        if graph_e2e and not args.no_pipeline:
             # the same fan-outs through FanoutGraph.run_many: two recorded
             # instances alternate, so the host's read-back of one fan-out and
             # its relaunch hide behind the other's replay (each fan-out still
@@ -1859,6 +1867,9 @@ def main():
                                    f"instances alternating)"})
             except Exception as exc:  # noqa: BLE001 - the per-call figure stands; say why
                 e2e["pipelined_error"] = repr(exc)[:200]
+        if graph_e2e:
+            torch.cuda.synchronize()
+            fg = None  # its graphs (with NCCL calls under --plan sharded) go before the process group
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

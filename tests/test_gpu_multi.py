@@ -129,6 +129,21 @@ def _partition_worker(rank, port, q):
         pairs_ok = bool(torch.equal(got, torch.cat(everyone)))
         host = full.numpy().view(np.uint8).reshape(n, -1).copy()
         O.copy_blocks(host, host.shape[1], got.cpu().numpy())
+        # the same through a recorded FanoutGraph (gather inside the graph), replayed
+        # three times with every child freed after its copy
+        from agentkv_b200.fanout import FanoutGraph
+
+        fg = FanoutGraph(a, [3, 3], 2, 3, 1, pool=mine, free_children=True, copier=copier, id_base=base)
+        roots_np = roots.cpu().numpy()
+        for _ in range(3):
+            fg.run(roots_np)
+            gathered = fg._keep[3].cpu()
+            everyone = [torch.empty_like(local) for _ in range(WORLD)]
+            dist.all_gather(everyone, fg._keep[0]["all_pairs"] + base)
+            pairs_ok &= bool(torch.equal(gathered, torch.cat(everyone).cpu()))
+            O.copy_blocks(host, host.shape[1], gathered.numpy())
+        torch.cuda.synchronize()
+        fg = None
         want = S.head_slice(torch.from_numpy(host.view(np.int16).reshape(full.shape)), rank, WORLD)
         q.put((rank, bool(torch.equal(mine.cpu(), want)), pairs_ok))
     finally:
