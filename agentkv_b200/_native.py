@@ -72,6 +72,11 @@ MATCH_MAX_RANGES = 64  # AKV_MATCH_MAX_RANGES
 VARIANT_AUTO = 0
 VARIANT_VEC = 1
 VARIANT_BULK = 2
+# bulk copies whose items are claimed from a counter in the status record
+# (16 KiB x 12 / 32 KiB x 6 per SM); the status record must not be shared by
+# launches that overlap on the GPU
+VARIANT_CLAIMED_16K = 14
+VARIANT_CLAIMED_32K = 15
 
 
 class AkvStatus(C.Structure):

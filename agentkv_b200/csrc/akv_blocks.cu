@@ -179,7 +179,19 @@ struct LayerCaches {
 // blocks; invalid pairs are skipped by the load cursor and the store cursor
 // replays the loads' descriptors from shared memory.  CHUNK bytes per bulk
 // copy, STAGES chunks in flight.
-template <int CHUNK, int STAGES, typename Layout, bool CHUNK_MAJOR = false>
+//
+// CLAIM > 0 hands items out dynamically instead: the issuing thread takes
+// CLAIM consecutive items at a time from a counter (the status record's last
+// word, atomicAdd), asking for its next range when it starts on the current
+// one, so a CTA that starts late — its SM still busy with another stream's
+// kernel — takes fewer items instead of holding back the end of the launch.
+// The counter holds the items claimed in bits 0-39 and the CTAs that have
+// stopped claiming in bits 40-63; the last CTA to stop sets it back to zero,
+// so it is zero between launches.  Launches that share one status record
+// must not overlap on the GPU.
+constexpr int kClaimDoneShift = 40;
+
+template <int CHUNK, int STAGES, typename Layout, bool CHUNK_MAJOR = false, int CLAIM = 0>
 __global__ void __launch_bounds__(32)
 k_copy_bulk(Layout lay, int32_t total, const int32_t* __restrict__ pairs, int32_t n_pairs,
             int64_t chunks_per_span, const int32_t* __restrict__ refs, AkvStatus* st,
@@ -189,16 +201,45 @@ k_copy_bulk(Layout lay, int32_t total, const int32_t* __restrict__ pairs, int32_
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ __align__(8) uint64_t bars[kBulkStages];
   __shared__ BulkDesc desc[kBulkStages];
-  if (!lay.valid(st)) return;  // the whole warp takes part
+  if (!lay.valid(st)) return;  // the whole warp takes part; the same answer in every CTA
   if (threadIdx.x != 0) return;
-  if (akv_failed(st)) return;
+  unsigned long long* const claims = reinterpret_cast<unsigned long long*>(&st->_reserved);
+  if (akv_failed(st)) {
+    if constexpr (CLAIM > 0) {
+      // Still counted as stopped, so that the counter goes back to zero.
+      const unsigned long long old = atomicAdd(claims, 1ull << kClaimDoneShift);
+      if ((old >> kClaimDoneShift) == gridDim.x - 1) atomicExch(claims, 0ull);
+    }
+    return;
+  }
   if (n_dev != nullptr) n_pairs = static_cast<int32_t>(min(static_cast<int64_t>(n_pairs), *n_dev));
   for (int s = 0; s < kBulkStages; ++s) mbar_init(smem_u32(&bars[s]), 1);
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 
   const int64_t per_pair = lay.segs() * chunks_per_span;
   const int64_t n_items = static_cast<int64_t>(n_pairs) * per_pair;
-  int64_t t = blockIdx.x;
+  constexpr unsigned long long kClaimMask = (1ull << kClaimDoneShift) - 1;
+  int64_t t, claim_end = 0, claim_next = 0;
+  if constexpr (CLAIM > 0) {
+    t = static_cast<int64_t>(atomicAdd(claims, static_cast<unsigned long long>(CLAIM)) & kClaimMask);
+    claim_end = t + CLAIM;
+    claim_next = static_cast<int64_t>(atomicAdd(claims, static_cast<unsigned long long>(CLAIM)) & kClaimMask);
+  } else {
+    t = blockIdx.x;
+  }
+  // The next item of this CTA after t.
+  auto advance = [&]() {
+    if constexpr (CLAIM > 0) {
+      if (++t == claim_end && t < n_items) {
+        t = claim_next;
+        claim_end = t + CLAIM;
+        if (t < n_items)  // ask for the range after this one while this one is copied
+          claim_next = static_cast<int64_t>(atomicAdd(claims, static_cast<unsigned long long>(CLAIM)) & kClaimMask);
+      }
+    } else {
+      t += gridDim.x;
+    }
+  };
   // Advances t to the next valid item of this CTA; false at the end.
   auto next_valid = [&](int32_t& src, int32_t& dst, int64_t& k) -> bool {
     while (t < n_items) {
@@ -211,7 +252,7 @@ k_copy_bulk(Layout lay, int32_t total, const int32_t* __restrict__ pairs, int32_
         k = t - static_cast<int64_t>(p) * per_pair;
       }
       if (pair_ok(pairs, p, total, refs, k == 0, st, src, dst)) return true;
-      t += gridDim.x;
+      advance();
     }
     return false;
   };
@@ -241,7 +282,7 @@ k_copy_bulk(Layout lay, int32_t total, const int32_t* __restrict__ pairs, int32_
   int64_t c;
   while (loads < kBulkStages && next_valid(src, dst, c)) {
     issue_load(loads++, src, dst, c);
-    t += gridDim.x;
+    advance();
   }
   bool timed_out = false;
   while (stores < loads) {
@@ -261,7 +302,7 @@ k_copy_bulk(Layout lay, int32_t total, const int32_t* __restrict__ pairs, int32_
       bulk_wait_read<1>();
       if (next_valid(src, dst, c)) {
         issue_load(loads++, src, dst, c);
-        t += gridDim.x;
+        advance();
       }
     }
   }
@@ -270,6 +311,12 @@ k_copy_bulk(Layout lay, int32_t total, const int32_t* __restrict__ pairs, int32_
     // each wait is bounded as well.
     for (int64_t m = stores + 1; m < loads; ++m)
       mbar_wait(smem_u32(&bars[m % kBulkStages]), static_cast<uint32_t>((m / kBulkStages) & 1));
+  }
+  if constexpr (CLAIM > 0) {
+    // Every claim this CTA made has been answered (the last one after its
+    // final use of t), so once all CTAs have stopped no claim is pending.
+    const unsigned long long old = atomicAdd(claims, 1ull << kClaimDoneShift);
+    if ((old >> kClaimDoneShift) == gridDim.x - 1) atomicExch(claims, 0ull);
   }
   bulk_wait_all();
 }
@@ -417,7 +464,8 @@ bool bulk_eligible(const void* pool, int64_t bpb) {
   return (reinterpret_cast<uintptr_t>(pool) % 16 == 0) && (bpb % 16 == 0);
 }
 
-template <int CHUNK, int STAGES, int CTAS_PER_SM, typename Layout = OnePool, bool CHUNK_MAJOR = false>
+template <int CHUNK, int STAGES, int CTAS_PER_SM, typename Layout = OnePool, bool CHUNK_MAJOR = false,
+          int CLAIM = 0>
 int copy_bulk_launch_t(Layout lay, int32_t total, const int32_t* pairs, int32_t n,
                        const int32_t* refs, AkvStatus* st, cudaStream_t s, const int64_t* n_dev) {
   // The shared-memory limit is a per-device function attribute: set it
@@ -429,7 +477,7 @@ int copy_bulk_launch_t(Layout lay, int32_t total, const int32_t* pairs, int32_t 
   if (e != cudaSuccess) return akv_cuda_fail(e, "akv_copy_blocks(bulk): cudaGetDevice");
   const uint64_t bit = uint64_t{1} << (dev & 63);
   if (!(attr_set.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(k_copy_bulk<CHUNK, STAGES, Layout, CHUNK_MAJOR>,
+    e = cudaFuncSetAttribute(k_copy_bulk<CHUNK, STAGES, Layout, CHUNK_MAJOR, CLAIM>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              smem);
     if (e != cudaSuccess) return akv_cuda_fail(e, "akv_copy_blocks(bulk): smem attribute");
@@ -439,8 +487,8 @@ int copy_bulk_launch_t(Layout lay, int32_t total, const int32_t* pairs, int32_t 
   const int64_t work = chunks * lay.segs() * n;
   const int64_t max_grid = static_cast<int64_t>(kAkvSMs) * CTAS_PER_SM;
   const int grid = static_cast<int>(work < max_grid ? work : max_grid);
-  k_copy_bulk<CHUNK, STAGES, Layout, CHUNK_MAJOR><<<grid, 32, smem, s>>>(lay, total, pairs, n, chunks, refs,
-                                                                        st, n_dev);
+  k_copy_bulk<CHUNK, STAGES, Layout, CHUNK_MAJOR, CLAIM><<<grid, 32, smem, s>>>(lay, total, pairs, n, chunks,
+                                                                               refs, st, n_dev);
   AKV_LAUNCH_CHECK("akv_copy_blocks(bulk)");
   return AKV_OK;
 }
@@ -473,6 +521,9 @@ int copy_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* pair
     // (balancing SMs that start late or run slower beside other kernels).
     case 10: return copy_bulk_launch_t<16384, 6, 8>(lay, total, pairs, n, refs, st, s, n_dev);
     case 11: return copy_bulk_launch_t<32768, 3, 8>(lay, total, pairs, n, refs, st, s, n_dev);
+    // Dynamic claims (128 KiB per claim) from the status record's counter.
+    case 12: return copy_bulk_launch_t<16384, 12, 1, OnePool, false, 8>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 13: return copy_bulk_launch_t<32768, 6, 1, OnePool, false, 4>(lay, total, pairs, n, refs, st, s, n_dev);
     default: return copy_bulk_launch_t<16384, 12, 1>(lay, total, pairs, n, refs, st, s, n_dev);
   }
 }
@@ -505,6 +556,8 @@ int akv_blocks_prepare() {
       AKV_ITEM((k_copy_bulk<32768, 3, OnePool, true>), 32768 * 3),
       AKV_ITEM((k_copy_bulk<16384, 12, OnePool, true>), 16384 * 12),
       AKV_ITEM((k_copy_bulk<32768, 6, OnePool, true>), 32768 * 6),
+      AKV_ITEM((k_copy_bulk<16384, 12, OnePool, false, 8>), 16384 * 12),
+      AKV_ITEM((k_copy_bulk<32768, 6, OnePool, false, 4>), 32768 * 6),
       AKV_ITEM((k_copy_bulk<16384, 12, LayerCaches>), 16384 * 12),
       AKV_ITEM((k_copy_bulk<32768, 6, LayerCaches>), 32768 * 6),
       AKV_ITEM((k_copy_bulk<65536, 3, LayerCaches>), 65536 * 3),
@@ -557,7 +610,9 @@ extern "C" int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int3
   AKV_ARG_CHECK(bytes_per_block > 0, "akv_copy_blocks: bytes_per_block=%lld",
                 static_cast<long long>(bytes_per_block));
   AKV_ARG_CHECK(total_blocks > 0, "akv_copy_blocks: total_blocks=%d", total_blocks);
-  AKV_ARG_CHECK(variant >= 0 && variant <= 13, "akv_copy_blocks: unknown variant %d", variant);
+  AKV_ARG_CHECK(variant >= 0 && variant <= 15, "akv_copy_blocks: unknown variant %d", variant);
+  AKV_ARG_CHECK(variant < 14 || status != nullptr,
+                "akv_copy_blocks: variant %d keeps its work counter in the status record (NULL status)", variant);
   char* p = static_cast<char*>(pool);
   cudaStream_t s = akv_stream(stream);
   // Automatic choice: the bulk-async engine whenever the spans are 16-byte

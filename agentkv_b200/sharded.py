@@ -29,6 +29,7 @@ from typing import Optional
 import numpy as np
 import torch
 
+from . import _native as N
 from . import kernels as K
 
 
@@ -67,6 +68,9 @@ class ShardedCopier:
         self.pool = pool_slice
         self.group = group
         self.src = src
+        # the status record of this copier's copies alone (the claimed copy
+        # variant keeps its work counter there); read with check()
+        self.status = torch.zeros(N.STATUS_BYTES // 4, dtype=torch.int32, device=pool_slice.device)
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
 
@@ -107,7 +111,18 @@ class ShardedCopier:
         return out
 
     def copy(self, pairs: torch.Tensor, **kw) -> None:
+        """Copy (n, 2) pairs on this rank's slice.  Without an explicit
+        variant and status the copy uses this copier's own status record and
+        the variant kernels.claimed_variant picks for the slice size."""
+        if kw.get("status") is None and self.pool.device.type == "cuda":
+            kw["status"] = self.status
+            if kw.get("variant", N.VARIANT_AUTO) == N.VARIANT_AUTO:
+                kw["variant"] = K.claimed_variant(self.pool)
         K.copy_blocks(self.pool, pairs, **kw)
+
+    def check(self) -> None:
+        """Raises for an error the copier's copies recorded (synchronises)."""
+        K.raise_for_status(self.status)
 
     # ── variable-size batches: [int64 count | max_pairs x (src, dst)] ────────
     @staticmethod

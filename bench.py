@@ -1220,6 +1220,23 @@ def hf_reference_update_figure(n_blocks: int, n_tok: int, steps: int, warmup: in
             "api": "torch restatement of the reference's per-layer row writes + indexed gather"}
 
 
+def copy_kernel_name(pool, variant: int) -> str:
+    """What the copy launches of the step run, for the config record."""
+    from agentkv_b200 import _native as N
+    from agentkv_b200 import kernels as K
+
+    v = K.claimed_variant(pool) if variant == N.VARIANT_AUTO else variant
+    bpb = pool[0].numel() * pool.element_size()
+    if v == N.VARIANT_CLAIMED_32K:
+        return "k_copy_bulk 32 KiB x 6 per SM, items claimed 128 KiB at a time"
+    if v == N.VARIANT_CLAIMED_16K:
+        return "k_copy_bulk 16 KiB x 12 per SM, items claimed 128 KiB at a time"
+    if v in (N.VARIANT_AUTO, N.VARIANT_BULK):
+        return ("k_copy_bulk 16 KiB x 12 per SM, items dealt round robin" if bpb >= (2 << 20)
+                else "k_copy_bulk 32 KiB x 6 per SM, items dealt round robin")
+    return f"copy variant {v}"
+
+
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch,
 # from ncu captures of the same launch (constants: they describe the kernel
 # as captured, not the run that prints them).
@@ -1227,8 +1244,8 @@ COPY_TRAFFIC_NCU = {
     584: (1322233344, "ncu: the 584-pair Tree-of-Thought copy launch (k_copy_bulk<16384,12>), 3,200-block pool"),
 }
 MATCH_TRAFFIC_NCU = {
-    2000: (52435200, "ncu: one 4,096-query k_match batch on the 2,000-sequence stress tree "
-                     "(profiles/match_prefix_stress2k.md, k_match with 16-byte verify rounds)"),
+    2000: (52435200, "ncu: one 4,096-query k_match batch (16-byte verify rounds) on the 2,000-sequence "
+                     "stress tree"),
 }
 
 
@@ -1844,27 +1861,29 @@ def main():
                "fanouts_timed": pc_fanouts}
         if graph_e2e and not args.no_pipeline:
             # the same fan-outs through FanoutGraph.run_many: two recorded
-            # instances alternate, so the host's read-back of one fan-out and
-            # its relaunch hide behind the other's replay (each fan-out still
-            # copies its roots in from pinned memory and its tables back to
-            # the host, where the host reads them)
+            # instances of --graph-steps fan-outs each alternate, so the host's
+            # read-back of one replay and its relaunch hide behind the other's
+            # replay, and inside a replay each fan-out's planning overlaps the
+            # previous copy (each fan-out still copies its roots in from pinned
+            # memory and its tables back to the host, where the host reads them)
             seen = [0]
+            k_rep = max(1, args.graph_steps)
 
             def on_result(i, tables):
                 seen[0] += int(tables[-1] >= 0)
 
             try:
-                fg.run_many([roots_np] * 3)  # records the second instance, warms up
+                fg.run_many([roots_np] * (2 * k_rep + 1), per_replay=k_rep)  # records the instances, warms up
                 n_many = args.steps * F
-                p_ms, _ = timed(lambda: fg.run_many([roots_np] * n_many, on_result=on_result), 1, 0, world,
-                                join=bench.join)
+                p_ms, _ = timed(lambda: fg.run_many([roots_np] * n_many, on_result=on_result, per_replay=k_rep),
+                                1, 0, world, join=bench.join)
                 p_fanout = p_ms / n_many
                 assert seen[0] == n_many, seen
                 e2e["per_call"] = {k: e2e[k] for k in ("value", "ms_per_step", "api", "fanouts_timed")}
                 e2e.update({"value": round(comp_rank * world / (p_fanout / 1e3) / 1e9, 2),
                             "ms_per_step": round(p_fanout * F, 4), "fanouts_timed": n_many,
                             "api": f"FanoutGraph.run_many ({n_many} fan-outs in one call, two graph "
-                                   f"instances alternating)"})
+                                   f"instances of {k_rep} fan-outs alternating)"})
             except Exception as exc:  # noqa: BLE001 - the per-call figure stands; say why
                 e2e["pipelined_error"] = repr(exc)[:200]
         if graph_e2e:
@@ -1931,6 +1950,7 @@ def main():
                 "heads_per_rank": bench.slice_heads,
                 "l2": "inputs larger than L2 (each fan-out touches ~1.4 GB per GPU)",
                 "copy_variant": args.variant,
+                "copy_kernel": copy_kernel_name(bench.pool, args.variant),
                 "copy_levels": "merged" if bench.merge else "per-level",
                 "cuda_graph": use_graph,
                 "fanouts_per_graph": max(1, args.graph_steps) if use_graph else None,

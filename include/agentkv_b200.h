@@ -123,7 +123,11 @@ AKV_API int akv_copy_blocks(void* pool, int64_t bytes_per_block, int32_t total_b
  * 2 CTAs per SM; 8 KiB x 24; chunk-major order (chunk c of every pair before
  * chunk c + 1) with 32 KiB x 3, 16 KiB x 12, 32 KiB x 6; 32 KiB x 3;
  * 16 KiB x 6 and 32 KiB x 3 on grids of 8 CTAs per SM, 2 resident at a
- * time, the rest placed on whichever SM frees up first). */
+ * time, the rest placed on whichever SM frees up first); 14-15 = 16 KiB x 12
+ * and 32 KiB x 6 with items handed out dynamically, 128 KiB per claim, from a
+ * counter kept in the status record's last word (zero between launches;
+ * status must be non-NULL, and launches sharing one status record must not
+ * overlap on the GPU). */
 AKV_API int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int32_t total_blocks,
                             const int32_t* pairs, int32_t n_pairs,
                             const int32_t* ref_counts, AkvStatus* status,

@@ -37,7 +37,7 @@ def random_pairs(n_blocks, n, seed):
     return np.stack([perm[:n], perm[n:]], 1).copy()
 
 
-@pytest.mark.parametrize("variant", [N.VARIANT_VEC, N.VARIANT_BULK, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13])
+@pytest.mark.parametrize("variant", [N.VARIANT_VEC, N.VARIANT_BULK, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15])
 @pytest.mark.parametrize("n_blocks,bpb", GEOMETRIES)
 def test_copy_blocks_bitexact(n_blocks, bpb, variant):
     host, pool = random_pool(n_blocks, bpb, seed=n_blocks + bpb)
@@ -47,6 +47,43 @@ def test_copy_blocks_bitexact(n_blocks, bpb, variant):
         K.copy_blocks(pool, torch.from_numpy(pairs), variant=variant, check=True)
         torch.cuda.synchronize()
         assert np.array_equal(pool.cpu().numpy(), host), f"n={n}"
+
+
+@pytest.mark.parametrize("variant", [14, 15])
+def test_dynamic_claims_counter_returns_to_zero(variant):
+    """Variants 14-15 take their items from a counter in the status record's
+    last word: after every launch — a clean one, one that meets a pair it
+    must skip, one that starts with an error already recorded — the counter
+    is zero again, and the bytes equal the oracle's (skipped pairs left
+    alone, as the static shapes do)."""
+    n_blocks, bpb = 64, 65536
+    host, pool = random_pool(n_blocks, bpb, seed=5)
+    st = torch.zeros(N.STATUS_BYTES // 4, dtype=torch.int32, device=DEV)
+
+    def counter():
+        return int(st.cpu().numpy().view(np.int64)[3])
+
+    for n in (1, 7, 32):
+        pairs = random_pairs(n_blocks, n, seed=100 + n)
+        O.copy_blocks(host, bpb, pairs)
+        K.copy_blocks(pool, torch.from_numpy(pairs), variant=variant, status=st)
+        torch.cuda.synchronize()
+        assert counter() == 0 and int(st[0]) == 0
+        assert np.array_equal(pool.cpu().numpy(), host), f"n={n}"
+    # a destination that is not exclusively owned: skipped and reported
+    pairs = random_pairs(n_blocks, 16, seed=7)
+    refs = torch.ones(n_blocks, dtype=torch.int32, device=DEV)
+    refs[int(pairs[5, 1])] = 2
+    O.copy_blocks(host, bpb, np.delete(pairs, 5, axis=0))
+    K.copy_blocks(pool, torch.from_numpy(pairs), variant=variant, status=st, ref_counts=refs)
+    torch.cuda.synchronize()
+    assert int(st[0]) == N.AKV_ERR_NOT_EXCLUSIVE and counter() == 0
+    assert np.array_equal(pool.cpu().numpy(), host)
+    # an error already recorded: nothing is copied, the counter stays zero
+    K.copy_blocks(pool, torch.from_numpy(random_pairs(n_blocks, 16, seed=8)), variant=variant, status=st)
+    torch.cuda.synchronize()
+    assert counter() == 0
+    assert np.array_equal(pool.cpu().numpy(), host)
 
 
 @pytest.mark.parametrize("variant", [N.VARIANT_VEC, N.VARIANT_BULK])

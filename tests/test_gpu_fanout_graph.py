@@ -212,12 +212,14 @@ def test_fanout_edge_cases():
         FanoutGraph(a, [0], 1, 2, 1)
 
 
-@pytest.mark.parametrize("merge", [True, False])
-def test_run_many_matches_oracle(merge):
-    """FanoutGraph.run_many (two recorded instances alternating) returns, for
-    each of its runs in order, what the oracle's per-child sequence gives,
-    and leaves the allocator, the reclaimer and the pool bytes as the oracle
-    leaves them; runs mixed with run() stay in sequence."""
+@pytest.mark.parametrize("merge,per_replay", [(True, 1), (False, 1), (True, 3), (False, 2)])
+def test_run_many_matches_oracle(merge, per_replay):
+    """FanoutGraph.run_many (two recorded instances alternating, each holding
+    per_replay fan-outs, the runs left over through one-fan-out instances)
+    returns, for each of its runs in order, what the oracle's per-child
+    sequence gives, and leaves the allocator, the reclaimer and the pool
+    bytes as the oracle leaves them; runs mixed with run() stay in
+    sequence."""
     n_blocks, root_lens, levels, fanout, append = 1024, [3, 2], 2, 3, 1
     cfg = PoolConfig(total_blocks=n_blocks, block_size=16, num_layers=2, num_kv_heads=2, head_dim=64,
                      dtype="bfloat16", device="cuda")
@@ -235,8 +237,8 @@ def test_run_many_matches_oracle(merge):
         roots.append(h)
     d_roots = a.alloc_batch(sum(root_lens)).cpu().numpy()
     fg = FanoutGraph(a, root_lens, levels, fanout, append, free_children=True, merge=merge)
-    for n_runs in (1, 5, 2):
-        got = fg.run_many([d_roots] * n_runs)
+    for n_runs in (1, 5, 2, 7):
+        got = fg.run_many([d_roots] * n_runs, per_replay=per_replay)
         assert len(got) == n_runs
         for r in range(n_runs):
             want = _oracle_fanout(tree, roots, levels, fanout, append, True)

@@ -381,3 +381,39 @@ def test_run_many_sequencing(monkeypatch):
         a.run_many([np.zeros(2, np.int32)])
     assert not log
     assert a.run_many([]) == []
+    # per_replay=2: two instances of 2 fan-outs each alternate over the first
+    # 4 runs, the fifth goes through the one-fan-out pair
+    def fake2(name):
+        g = fake(name)
+        g.per_replay = 2
+        g.h_roots = torch.zeros(6, dtype=torch.int32)
+        g._h_roots_np = g.h_roots.numpy()
+        g.h_tables = torch.zeros(12, dtype=torch.int32)
+
+        class Graph:
+            def replay(self_inner):
+                r = g._h_roots_np.reshape(2, 3)
+                g.h_tables.numpy()[:] = np.concatenate([np.tile(x, 2) * 10 for x in r])
+                log.append(("replay", name, int(r[0, 0]), int(r[1, 0])))
+
+        g.graph = Graph()
+        return g
+
+    a._grouped = {}
+    made = []
+
+    def instance(k):
+        made.append(k)
+        return fake2(f"g{len(made)}")
+
+    a._instance = instance
+    log.clear()
+    outs = a.run_many(roots, per_replay=2)
+    assert made == [2, 2]
+    assert all(np.array_equal(o, np.tile(r, 2) * 10) for o, r in zip(outs, roots)) and len(outs) == 5
+    replays = [e for e in log if e[0] == "replay"]
+    assert replays == [("replay", "g1", 0, 1), ("replay", "g2", 2, 3), ("replay", "a", 4)]
+    a.run_many(roots[:4], per_replay=2)  # the grouped instances are kept
+    assert made == [2, 2]
+    with pytest.raises(ValueError, match="per_replay"):
+        a.run_many(roots, per_replay=0)
