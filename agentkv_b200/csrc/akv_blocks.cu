@@ -524,6 +524,10 @@ int copy_bulk_launch(char* pool, int64_t bpb, int32_t total, const int32_t* pair
     // Dynamic claims (128 KiB per claim) from the status record's counter.
     case 12: return copy_bulk_launch_t<16384, 12, 1, OnePool, false, 8>(lay, total, pairs, n, refs, st, s, n_dev);
     case 13: return copy_bulk_launch_t<32768, 6, 1, OnePool, false, 4>(lay, total, pairs, n, refs, st, s, n_dev);
+    // Claim sizes for tuning: 256 KiB (32 KiB x 8, 16 KiB x 16) and 32 KiB.
+    case 14: return copy_bulk_launch_t<32768, 6, 1, OnePool, false, 8>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 15: return copy_bulk_launch_t<16384, 12, 1, OnePool, false, 16>(lay, total, pairs, n, refs, st, s, n_dev);
+    case 16: return copy_bulk_launch_t<16384, 12, 1, OnePool, false, 2>(lay, total, pairs, n, refs, st, s, n_dev);
     default: return copy_bulk_launch_t<16384, 12, 1>(lay, total, pairs, n, refs, st, s, n_dev);
   }
 }
@@ -558,6 +562,9 @@ int akv_blocks_prepare() {
       AKV_ITEM((k_copy_bulk<32768, 6, OnePool, true>), 32768 * 6),
       AKV_ITEM((k_copy_bulk<16384, 12, OnePool, false, 8>), 16384 * 12),
       AKV_ITEM((k_copy_bulk<32768, 6, OnePool, false, 4>), 32768 * 6),
+      AKV_ITEM((k_copy_bulk<32768, 6, OnePool, false, 8>), 32768 * 6),
+      AKV_ITEM((k_copy_bulk<16384, 12, OnePool, false, 16>), 16384 * 12),
+      AKV_ITEM((k_copy_bulk<16384, 12, OnePool, false, 2>), 16384 * 12),
       AKV_ITEM((k_copy_bulk<16384, 12, LayerCaches>), 16384 * 12),
       AKV_ITEM((k_copy_bulk<32768, 6, LayerCaches>), 32768 * 6),
       AKV_ITEM((k_copy_bulk<65536, 3, LayerCaches>), 65536 * 3),
@@ -610,7 +617,7 @@ extern "C" int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int3
   AKV_ARG_CHECK(bytes_per_block > 0, "akv_copy_blocks: bytes_per_block=%lld",
                 static_cast<long long>(bytes_per_block));
   AKV_ARG_CHECK(total_blocks > 0, "akv_copy_blocks: total_blocks=%d", total_blocks);
-  AKV_ARG_CHECK(variant >= 0 && variant <= 15, "akv_copy_blocks: unknown variant %d", variant);
+  AKV_ARG_CHECK(variant >= 0 && variant <= 18, "akv_copy_blocks: unknown variant %d", variant);
   AKV_ARG_CHECK(variant < 14 || status != nullptr,
                 "akv_copy_blocks: variant %d keeps its work counter in the status record (NULL status)", variant);
   char* p = static_cast<char*>(pool);

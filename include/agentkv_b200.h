@@ -127,7 +127,8 @@ AKV_API int akv_copy_blocks(void* pool, int64_t bytes_per_block, int32_t total_b
  * and 32 KiB x 6 with items handed out dynamically, 128 KiB per claim, from a
  * counter kept in the status record's last word (zero between launches;
  * status must be non-NULL, and launches sharing one status record must not
- * overlap on the GPU). */
+ * overlap on the GPU); 16-18 = the same with other claim sizes: 32 KiB x 6
+ * claiming 256 KiB, 16 KiB x 12 claiming 256 KiB and 32 KiB. */
 AKV_API int akv_copy_blocks_variant(void* pool, int64_t bytes_per_block, int32_t total_blocks,
                             const int32_t* pairs, int32_t n_pairs,
                             const int32_t* ref_counts, AkvStatus* status,

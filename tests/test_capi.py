@@ -102,16 +102,16 @@ def test_tree_hash_python_equals_c():
 
 def test_host_argument_checks_of_tuning_entry_points():
     """Arguments the library refuses on the host, before any CUDA call: copy
-    variants past 15, the dynamically claiming variants 14-15 without a
+    variants past 18, the dynamically claiming variants 14-18 without a
     status record (their work counter lives there), layer-copy variants past
     4 and unaligned layer spans,
     match widths outside {1,2,4,8,16}, run arrays without their entries,
     fan-out plans deeper than AKV_MAX_FANOUT_LEVELS or without appended
     blocks.  (Pointers are dummies: nothing is dereferenced.)"""
     P = 16  # a dummy non-NULL pointer
-    rc = N.lib.akv_copy_blocks_variant(P, 64, 4, P, 1, None, None, 16, None)
-    assert rc == N.AKV_ERR_INVALID_ARG and "unknown variant 16" in N.last_error()
-    for v in (14, 15):
+    rc = N.lib.akv_copy_blocks_variant(P, 64, 4, P, 1, None, None, 19, None)
+    assert rc == N.AKV_ERR_INVALID_ARG and "unknown variant 19" in N.last_error()
+    for v in (14, 15, 16, 17, 18):
         rc = N.lib.akv_copy_blocks_variant(P, 64, 4, P, 1, None, None, v, None)
         assert rc == N.AKV_ERR_INVALID_ARG and "NULL status" in N.last_error()
     rc = N.lib.akv_copy_blocks_layers(P, 2, 4096, 4096, 8, P, 1, None, None, 5, None)

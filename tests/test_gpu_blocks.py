@@ -37,7 +37,7 @@ def random_pairs(n_blocks, n, seed):
     return np.stack([perm[:n], perm[n:]], 1).copy()
 
 
-@pytest.mark.parametrize("variant", [N.VARIANT_VEC, N.VARIANT_BULK, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15])
+@pytest.mark.parametrize("variant", [N.VARIANT_VEC, N.VARIANT_BULK, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18])
 @pytest.mark.parametrize("n_blocks,bpb", GEOMETRIES)
 def test_copy_blocks_bitexact(n_blocks, bpb, variant):
     host, pool = random_pool(n_blocks, bpb, seed=n_blocks + bpb)
@@ -49,9 +49,9 @@ def test_copy_blocks_bitexact(n_blocks, bpb, variant):
         assert np.array_equal(pool.cpu().numpy(), host), f"n={n}"
 
 
-@pytest.mark.parametrize("variant", [14, 15])
+@pytest.mark.parametrize("variant", [14, 15, 16, 17, 18])
 def test_dynamic_claims_counter_returns_to_zero(variant):
-    """Variants 14-15 take their items from a counter in the status record's
+    """Variants 14-18 take their items from a counter in the status record's
     last word: after every launch — a clean one, one that meets a pair it
     must skip, one that starts with an error already recorded — the counter
     is zero again, and the bytes equal the oracle's (skipped pairs left
