@@ -185,6 +185,11 @@ struct LayerCaches {
 // word, atomicAdd), asking for its next range when it starts on the current
 // one, so a CTA that starts late — its SM still busy with another stream's
 // kernel — takes fewer items instead of holding back the end of the launch.
+// Small batches claim fewer items at a time (down to one), so that every CTA
+// of the grid still gets work: at most n_items / (4 x grid) per claim.  The
+// first grid x claim items are dealt without the counter (CTA b takes the
+// b-th range), so a CTA's first load waits on no atomic; the counter hands
+// out the items after them.
 // The counter holds the items claimed in bits 0-39 and the CTAs that have
 // stopped claiming in bits 40-63; the last CTA to stop sets it back to zero,
 // so it is zero between launches.  Launches that share one status record
@@ -220,10 +225,14 @@ k_copy_bulk(Layout lay, int32_t total, const int32_t* __restrict__ pairs, int32_
   const int64_t n_items = static_cast<int64_t>(n_pairs) * per_pair;
   constexpr unsigned long long kClaimMask = (1ull << kClaimDoneShift) - 1;
   int64_t t, claim_end = 0, claim_next = 0;
+  // items per claim: the same in every CTA (n_items and the grid are)
+  const int64_t claim = CLAIM > 0 ? max(int64_t{1}, min(int64_t{CLAIM}, n_items / (4 * int64_t{gridDim.x}))) : 0;
+  const int64_t dealt = static_cast<int64_t>(gridDim.x) * claim;  // items before the counter's
   if constexpr (CLAIM > 0) {
-    t = static_cast<int64_t>(atomicAdd(claims, static_cast<unsigned long long>(CLAIM)) & kClaimMask);
-    claim_end = t + CLAIM;
-    claim_next = static_cast<int64_t>(atomicAdd(claims, static_cast<unsigned long long>(CLAIM)) & kClaimMask);
+    t = static_cast<int64_t>(blockIdx.x) * claim;
+    claim_end = t + claim;
+    claim_next =
+        dealt + static_cast<int64_t>(atomicAdd(claims, static_cast<unsigned long long>(claim)) & kClaimMask);
   } else {
     t = blockIdx.x;
   }
@@ -232,9 +241,10 @@ k_copy_bulk(Layout lay, int32_t total, const int32_t* __restrict__ pairs, int32_
     if constexpr (CLAIM > 0) {
       if (++t == claim_end && t < n_items) {
         t = claim_next;
-        claim_end = t + CLAIM;
+        claim_end = t + claim;
         if (t < n_items)  // ask for the range after this one while this one is copied
-          claim_next = static_cast<int64_t>(atomicAdd(claims, static_cast<unsigned long long>(CLAIM)) & kClaimMask);
+          claim_next = dealt + static_cast<int64_t>(
+                                   atomicAdd(claims, static_cast<unsigned long long>(claim)) & kClaimMask);
       }
     } else {
       t += gridDim.x;

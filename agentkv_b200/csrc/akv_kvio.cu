@@ -19,42 +19,9 @@
 //                  and stores of the widest word that fits.
 // Both move bits only; pool block b is the span [b * bpb, (b + 1) * bpb) laid
 // out [L][2][H][bs][head_dim].
-#include <utility>
-
 #include "akv_bulk.cuh"
 
 namespace {
-
-// Programmatic dependent launch.  A model layer's K/V I/O is a chain of
-// short launches (scatter, gather, the next layer's scatter ...), each a few
-// microseconds, so a launch's start-up is a sizeable share of it.  Every
-// kernel here is launched with programmatic stream serialization: it may be
-// scheduled while the kernel before it on the stream is still running,
-// waits (griddepcontrol.wait) until that kernel has completed and its writes
-// are visible before it reads or writes anything, and lets the kernel after
-// it be scheduled as soon as all of its own CTAs have started.  After a
-// launch that is not a kernel (a copy, an event), or with no dependency,
-// the wait returns at once.
-AKV_DEV void pdl_wait_and_release() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), int grid, int block, size_t smem, cudaStream_t s,
-                       Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(static_cast<unsigned>(block));
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
 
 constexpr int kKvThreads = 128;
 constexpr int kKvUnroll = 4;
@@ -64,7 +31,6 @@ __global__ void __launch_bounds__(kKvThreads)
 k_kv_gather(const char* __restrict__ pool, int64_t bpb, int32_t total, int32_t H, int32_t bs,
             int64_t row_bytes, int64_t layer_off, const int32_t* __restrict__ block_ids, int32_t n_blocks,
             int64_t n_tokens, char* __restrict__ out_k, char* __restrict__ out_v, AkvStatus* st) {
-  pdl_wait_and_release();
   if (akv_failed(st)) return;
   const int64_t tile_bytes = static_cast<int64_t>(bs) * row_bytes;
   const int64_t n_tiles = 2ll * H * n_blocks;
@@ -124,7 +90,6 @@ k_kv_gather_bulk(const char* __restrict__ pool, int64_t bpb, int32_t total, int3
   __shared__ char* dsts[kStages];
   __shared__ uint32_t sizes[kStages];
   const int lane = threadIdx.x;
-  pdl_wait_and_release();
   if (akv_failed(st)) return;
   const int64_t tile = static_cast<int64_t>(bs) * row_bytes;
   if (lane == 0) {
@@ -247,7 +212,6 @@ k_kv_scatter(char* __restrict__ pool, int64_t bpb, int32_t total, int32_t H, int
              int64_t layer_off, const int32_t* __restrict__ slots, int32_t n_new,
              const char* __restrict__ k_src, const char* __restrict__ v_src, int64_t stride_h,
              int64_t stride_t, AkvStatus* st) {
-  pdl_wait_and_release();
   if (akv_failed(st)) return;
   const int64_t words_per_row = row_bytes / static_cast<int64_t>(sizeof(W));
   const int64_t n_rows = 2ll * H * n_new;
@@ -332,30 +296,28 @@ extern "C" int akv_kv_gather(const void* pool, int32_t total_blocks, int32_t num
     const int64_t tiles = 2ll * num_kv_heads * n_blocks;
     const int64_t cap = static_cast<int64_t>(kAkvSMs) * kGatherCtasPerSm;
     const int grid_b = static_cast<int>(tiles < cap ? tiles : cap);
-    const cudaError_t e = launch_pdl(
-        k_kv_gather_bulk<kGatherStages>, grid_b, 32, static_cast<size_t>(kGatherStages * tile), s,
+    k_kv_gather_bulk<kGatherStages><<<grid_b, 32, static_cast<size_t>(kGatherStages * tile), s>>>(
         static_cast<const char*>(pool), bpb, total_blocks, num_kv_heads, block_size, row_bytes, layer_off,
         block_ids, n_blocks, n_tokens, static_cast<char*>(out_k), static_cast<char*>(out_v), status);
-    if (e != cudaSuccess) return akv_cuda_fail(e, "akv_kv_gather(bulk)");
+    AKV_LAUNCH_CHECK("akv_kv_gather(bulk)");
     return AKV_OK;
   }
   const int grid = kv_grid(2ll * num_kv_heads * n_blocks);
   // (A variant that took 4 tiles per CTA and issued all their loads at once
   // measured slower: 11.9 us against 9.8 us for a 4,096-token layer.)
-#define AKV_GATHER(W)                                                                                       \
-  launch_pdl(k_kv_gather<W>, grid, kKvThreads, 0, s, static_cast<const char*>(pool), bpb, total_blocks,      \
-             num_kv_heads, block_size, row_bytes, layer_off, block_ids, n_blocks, n_tokens,                 \
-             static_cast<char*>(out_k), static_cast<char*>(out_v), status)
-  cudaError_t e;
+#define AKV_GATHER(W)                                                                                        \
+  k_kv_gather<W><<<grid, kKvThreads, 0, s>>>(static_cast<const char*>(pool), bpb, total_blocks, num_kv_heads, \
+                                             block_size, row_bytes, layer_off, block_ids, n_blocks, n_tokens, \
+                                             static_cast<char*>(out_k), static_cast<char*>(out_v), status)
   switch (w) {
-    case 16: e = AKV_GATHER(uint4); break;
-    case 8: e = AKV_GATHER(uint2); break;
-    case 4: e = AKV_GATHER(uint32_t); break;
-    case 2: e = AKV_GATHER(uint16_t); break;
-    default: e = AKV_GATHER(uint8_t); break;
+    case 16: AKV_GATHER(uint4); break;
+    case 8: AKV_GATHER(uint2); break;
+    case 4: AKV_GATHER(uint32_t); break;
+    case 2: AKV_GATHER(uint16_t); break;
+    default: AKV_GATHER(uint8_t); break;
   }
 #undef AKV_GATHER
-  if (e != cudaSuccess) return akv_cuda_fail(e, "akv_kv_gather");
+  AKV_LAUNCH_CHECK("akv_kv_gather");
   return AKV_OK;
 }
 
@@ -380,19 +342,19 @@ extern "C" int akv_kv_scatter(void* pool, int32_t total_blocks, int32_t num_laye
   const int64_t words = 2ll * num_kv_heads * n_new * (row_bytes / w);
   const int grid = kv_grid((words + kKvThreads - 1) / kKvThreads);
   cudaStream_t s = akv_stream(stream);
-#define AKV_SCATTER(W)                                                                                      \
-  launch_pdl(k_kv_scatter<W>, grid, kKvThreads, 0, s, static_cast<char*>(pool), bpb, total_blocks,           \
-             num_kv_heads, block_size, row_bytes, layer_off, slots, n_new, static_cast<const char*>(k_src),  \
-             static_cast<const char*>(v_src), src_stride_head, src_stride_token, status)
-  cudaError_t e;
+#define AKV_SCATTER(W)                                                                                        \
+  k_kv_scatter<W><<<grid, kKvThreads, 0, s>>>(static_cast<char*>(pool), bpb, total_blocks, num_kv_heads,       \
+                                              block_size, row_bytes, layer_off, slots, n_new,                  \
+                                              static_cast<const char*>(k_src), static_cast<const char*>(v_src), \
+                                              src_stride_head, src_stride_token, status)
   switch (w) {
-    case 16: e = AKV_SCATTER(uint4); break;
-    case 8: e = AKV_SCATTER(uint2); break;
-    case 4: e = AKV_SCATTER(uint32_t); break;
-    case 2: e = AKV_SCATTER(uint16_t); break;
-    default: e = AKV_SCATTER(uint8_t); break;
+    case 16: AKV_SCATTER(uint4); break;
+    case 8: AKV_SCATTER(uint2); break;
+    case 4: AKV_SCATTER(uint32_t); break;
+    case 2: AKV_SCATTER(uint16_t); break;
+    default: AKV_SCATTER(uint8_t); break;
   }
 #undef AKV_SCATTER
-  if (e != cudaSuccess) return akv_cuda_fail(e, "akv_kv_scatter");
+  AKV_LAUNCH_CHECK("akv_kv_scatter");
   return AKV_OK;
 }

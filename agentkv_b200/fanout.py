@@ -88,7 +88,7 @@ class FanoutGraph:
         self.d_roots = torch.empty(k * self.n_root_entries, dtype=torch.int32, device=self.dev)
         # copy errors land in the allocator's status word when both share a device;
         # the copies are then the only launches that use its work counter, so
-        # the automatic choice may take the claimed variant (head slices)
+        # the automatic choice takes the claimed variant
         self._copy_status = alloc._status if self.pool.device == alloc.device else None
         if self.variant == N.VARIANT_AUTO and self._copy_status is not None and self.pool.device.type == "cuda":
             self.variant = K.claimed_variant(self.pool)

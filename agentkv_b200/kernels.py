@@ -27,8 +27,10 @@ _STATUS: dict = {}
 
 
 def _status_buffer(device: torch.device) -> torch.Tensor:
-    """A per-device scratch AkvStatus for calls that do not pass their own."""
-    key = (device.type, device.index)
+    """A scratch AkvStatus for calls that do not pass their own: one per
+    device and current stream, so launches on different streams never share
+    one (the block copy keeps its work counter in it)."""
+    key = (device.type, device.index, stream_handle(device) if device.type == "cuda" else 0)
     buf = _STATUS.get(key)
     if buf is None:
         buf = torch.zeros(N.STATUS_BYTES // 4, dtype=torch.int32, device=device)
@@ -126,17 +128,22 @@ def zero_block(block: torch.Tensor) -> None:
 
 # ── batched block movement ───────────────────────────────────────────────────
 def claimed_variant(pool: torch.Tensor) -> int:
-    """The copy variant for a caller that owns the status record its copies
-    use (no other launch with that record overlaps them on the GPU): the
-    dynamically claimed 32 KiB x 6 bulk copy for blocks below 2 MiB — the
-    head slices of a sharded pool, where the statically dealt copy ran
-    0.243 / 0.227 ms for a Tree-of-Thought step's 1 MiB / 256 KiB slices
-    against 0.215 / 0.218 ms claimed — else the automatic choice (for whole
-    2 MiB blocks the static 16 KiB x 12 copy measured 0.220 ms against
-    0.294 ms claimed)."""
+    """The automatic copy variant of copy_blocks, whose status record belongs
+    to one stream (no other launch with that record overlaps its copies on
+    the GPU): the bulk copy of 32 KiB x 6 chunks per SM whose items are
+    claimed 128 KiB at a time from a counter in that record.  On seeded
+    disjoint pairs of 2 MiB blocks it copied 512 / 4,096 pairs in 0.324 /
+    2.533 ms against 0.346 / 2.750 ms for the statically dealt 16 KiB x 12
+    copy the library's own automatic choice makes.  Measured on Tree-of-Thought steps
+    (8 children per source, the allocator's kernels of the next fan-out on a
+    side stream): the copy launch in the step took 0.2245 / 0.226 / 0.235 /
+    0.235 ms for whole 2 MiB blocks and 1 MiB / 512 KiB / 256 KiB head slices,
+    against 0.2316 / 0.263 / 0.272 / 0.250 ms for the statically dealt copy
+    the automatic choice makes.  Pools whose blocks are not 16-byte aligned
+    keep the automatic choice (vector copies)."""
     total, bpb = _pool_geometry(pool)
     aligned = pool.data_ptr() % 16 == 0 and bpb % 16 == 0
-    return N.VARIANT_CLAIMED_32K if (aligned and bpb < (2 << 20)) else N.VARIANT_AUTO
+    return N.VARIANT_CLAIMED_32K if aligned else N.VARIANT_AUTO
 
 
 def _pool_geometry(pool: torch.Tensor) -> tuple:
@@ -172,8 +179,11 @@ def copy_blocks(
     The pairs must be independent (no dst repeated, no dst used as another
     pair's src); `validate=True` checks that on the host before launching.
     With `ref_counts` every dst must have refcount 1.  Device-detected errors
-    land in `status` (a per-device buffer by default) and raise on `check=True`
-    (which synchronises).
+    land in `status` (by default a buffer of this device and stream) and
+    raise on `check=True` (which synchronises).  The automatic variant is
+    the claimed bulk copy (claimed_variant), which keeps a work counter in
+    the status record: a record passed in must not be in use by another
+    launch that overlaps this one on the GPU (one record per stream).
     """
     if not _require_cuda(pool, "copy_blocks"):
         return
@@ -185,6 +195,8 @@ def copy_blocks(
     if validate:
         validate_pairs(pairs_t.cpu().numpy(), total)
     st = status if status is not None else _status_buffer(pool.device)
+    if variant == N.VARIANT_AUTO:
+        variant = claimed_variant(pool)
     N.check(
         N.lib.akv_copy_blocks_variant(
             pool.data_ptr(), bpb, total, pairs_t.data_ptr(), n,

@@ -113,7 +113,7 @@ class ShardedCopier:
     def copy(self, pairs: torch.Tensor, **kw) -> None:
         """Copy (n, 2) pairs on this rank's slice.  Without an explicit
         variant and status the copy uses this copier's own status record and
-        the variant kernels.claimed_variant picks for the slice size."""
+        the variant kernels.claimed_variant picks."""
         if kw.get("status") is None and self.pool.device.type == "cuda":
             kw["status"] = self.status
             if kw.get("variant", N.VARIANT_AUTO) == N.VARIANT_AUTO:

@@ -1241,7 +1241,8 @@ def copy_kernel_name(pool, variant: int) -> str:
 # from ncu captures of the same launch (constants: they describe the kernel
 # as captured, not the run that prints them).
 COPY_TRAFFIC_NCU = {
-    584: (1322233344, "ncu: the 584-pair Tree-of-Thought copy launch (k_copy_bulk<16384,12>), 3,200-block pool"),
+    584: (1319668736, "ncu: the 584-pair Tree-of-Thought copy launch (k_copy_bulk<32768,6,OnePool,0,4>, items "
+                      "claimed), 3,200-block pool"),
 }
 MATCH_TRAFFIC_NCU = {
     2000: (52435200, "ncu: one 4,096-query k_match batch (16-byte verify rounds) on the 2,000-sequence "
@@ -1813,7 +1814,9 @@ def main():
     one_launch = bench.merge and bench.last_pairs is not None
     launch_comp = comp_rank if one_launch else None
     achieved = (launch_comp if one_launch else 2 * bench.slice_bytes * big) / (big_ms / 1e3) / 1e9
-    traffic = COPY_TRAFFIC_NCU.get(big) if (bench.slice_heads == 8 and bench.trees == 1 and one_launch) else None
+    # the constant describes the claimed copy the automatic choice launches
+    traffic = (COPY_TRAFFIC_NCU.get(big) if (bench.slice_heads == 8 and bench.trees == 1 and one_launch
+                                             and args.variant == 0) else None)
 
     # per-rank breakdown (every rank takes part in the gather)
     per_rank = None

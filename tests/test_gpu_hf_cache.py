@@ -139,3 +139,60 @@ def test_gather_scatter_kernels(dtype, D):
     assert K.read_status(st)[0] == N.AKV_ERR_OUT_OF_RANGE
     with pytest.raises(N.NativeError):
         K.kv_gather(pool, torch.from_numpy(ids), 0, 7 * bs + 1)
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_chained_scatter_gather_see_each_other(graph):
+    """A decode step's chain of short launches, as the layers issue them:
+    scatter a new row, gather the layer (which must read that row), scatter
+    the next token's row into the block the gather just read, gather
+    again ...  The scatters and gathers may be scheduled before the launch
+    ahead of them ends (programmatic dependent launch); each must still see
+    every write before it.  Eagerly and replayed from a CUDA graph, the
+    gathered K/V equal a host model of the same writes."""
+    n, L, H, bs, D = 64, 4, 8, 16, 128
+    pool = torch.zeros((n, L, 2, H, bs, D), dtype=torch.bfloat16, device=DEV)
+    pool.view(-1).copy_(torch.randn(pool.numel(), device=DEV).to(torch.bfloat16))
+    host = pool.cpu().clone()
+    rng = np.random.default_rng(11)
+    ids = torch.from_numpy(rng.permutation(n)[:8].astype(np.int32)).to(DEV)
+    ids_host = ids.cpu().long()
+    n_steps = 6
+    first = 100  # the sequence holds `first + s` tokens before step s's row
+    rows_k = torch.randn(n_steps, L, 1, H, 1, D, device=DEV).to(torch.bfloat16)
+    rows_v = torch.randn(n_steps, L, 1, H, 1, D, device=DEV).to(torch.bfloat16)
+    slots = [torch.tensor([int(ids_host[(first + s) // bs]) * bs + (first + s) % bs], dtype=torch.int32,
+                          device=DEV) for s in range(n_steps)]
+    outs = []
+
+    def chain():
+        outs.clear()
+        for s in range(n_steps):
+            for layer in range(L):
+                K.kv_scatter(pool, slots[s], layer, rows_k[s, layer], rows_v[s, layer])
+                outs.append(K.kv_gather(pool, ids, layer, first + s + 1))
+
+    if graph:
+        pool_before = pool.clone()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
+            chain()
+        pool.copy_(pool_before)  # capturing ran nothing, but start from the same bytes regardless
+        g.replay()
+    else:
+        chain()
+    torch.cuda.synchronize()
+    i = 0
+    for s in range(n_steps):
+        pos = first + s
+        b = int(ids_host[pos // bs])
+        for layer in range(L):
+            host[b, layer, 0, :, pos % bs, :] = rows_k[s, layer, 0, :, 0, :].cpu()
+            host[b, layer, 1, :, pos % bs, :] = rows_v[s, layer, 0, :, 0, :].cpu()
+            data = host[ids_host, layer]
+            want_k = data[:, 0].permute(1, 0, 2, 3).reshape(1, H, -1, D)[:, :, :pos + 1]
+            want_v = data[:, 1].permute(1, 0, 2, 3).reshape(1, H, -1, D)[:, :, :pos + 1]
+            k, v = outs[i]
+            i += 1
+            assert torch.equal(k.cpu(), want_k) and torch.equal(v.cpu(), want_v), (s, layer)
+    assert torch.equal(pool.cpu(), host)
