@@ -43,6 +43,12 @@ import torch
 from . import _native as N
 from .kernels import stream_handle
 
+try:
+    from . import _akv_pyhost as _pyhost
+except ImportError as exc:  # built beside libagentkv_b200.so by _build.build()
+    raise ImportError("agentkv_b200: the host helper _akv_pyhost is not built; run "
+                      "`python -m agentkv_b200._build`") from exc
+
 _M64 = (1 << 64) - 1
 EMPTY = -1
 DELETED = -2
@@ -863,7 +869,21 @@ class QueryStage:
         """(tokens int32, offsets int64, longest-first order int32) on the
         device, enqueued on the current stream."""
         nq = len(queries)
-        lens = np.fromiter((len(q) for q in queries), np.int64, nq)
+        # Every query's address and length: int32 buffers (numpy arrays,
+        # array('i')) are read in one C loop; anything else (lists, other
+        # dtypes) is converted here and kept alive until the gather is done.
+        ptrs = np.empty(nq, np.uint64)
+        lens = np.empty(nq, np.int64)
+        converted = []
+        i = 0
+        while i < nq:
+            i = _pyhost.token_arrays(queries, i, ptrs, lens)
+            if i < nq:
+                a = _i32(queries[i])
+                converted.append(a)
+                ptrs[i] = a.ctypes.data if a.size else 0
+                lens[i] = a.size
+                i += 1
         total = int(lens.sum())
         self._grow(total, nq)
         off = self.h_off.numpy()[: nq + 1]
@@ -873,9 +893,6 @@ class QueryStage:
         # host threads and enqueues the upload (a single-threaded
         # np.concatenate of a 73 MB batch took 14 ms on the GPU hosts).
         if total:
-            arrs = [q if isinstance(q, np.ndarray) and q.dtype == np.int32 and q.flags.c_contiguous
-                    else _i32(q) for q in queries]
-            ptrs = np.fromiter((a.ctypes.data for a in arrs), np.uint64, nq)
             cuda = self.device.type == "cuda"
             N.check(N.lib.akv_gather_upload(ptrs.ctypes.data, lens.ctypes.data, nq, self.h_tok.data_ptr(),
                                             self.d_tok.data_ptr() if cuda else None, _GATHER_THREADS,

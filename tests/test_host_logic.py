@@ -304,6 +304,16 @@ def test_query_packing():
         qs = [rng.integers(0, 1000, size=int(rng.integers(0, 90))).astype(np.int32) for _ in range(nq)]
         if nq > 2:
             qs[1] = []  # an empty query (a Python list)
+        if nq > 10:
+            # every form a caller may hold: lists, other integer dtypes, a
+            # strided view, array('i'), a zero-length int32 array
+            import array
+
+            qs[3] = [int(x) for x in rng.integers(0, 1000, size=17)]
+            qs[4] = rng.integers(0, 1000, size=9).astype(np.int64)
+            qs[5] = rng.integers(0, 1000, size=30).astype(np.int32)[::2]
+            qs[6] = array.array("i", [int(x) for x in rng.integers(0, 1000, size=11)])
+            qs[7] = np.zeros(0, np.int32)
         lens = np.array([len(q) for q in qs], np.int64)
         off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
         flat = np.concatenate([np.asarray(q, np.int32) for q in qs]) if nq else np.zeros(0, np.int32)
@@ -316,6 +326,32 @@ def test_query_packing():
         want_order = np.argsort(-lens, kind="stable")
         np.testing.assert_array_equal(order.numpy()[:nq], want_order)
         np.testing.assert_array_equal(longest_first(q_off, cpu).numpy(), want_order)
+
+
+def test_host_helper_reads_token_array_addresses():
+    """_akv_pyhost.token_arrays: the address and element count of every item
+    that is a C-contiguous 4-byte integer buffer, from `start` on, stopping
+    at (and returning the index of) the first item that is not."""
+    import array
+
+    from agentkv_b200 import _akv_pyhost as H
+
+    a = np.arange(10, dtype=np.int32)
+    b = np.frombuffer(array.array("i", [1, 2, 3]), dtype=np.int32)
+    items = [a, b, [1, 2], a.astype(np.int64), a[::2], array.array("i", [5]), np.zeros(0, np.int32), b"abcd"]
+    ptrs = np.zeros(len(items), np.uint64)
+    lens = np.zeros(len(items), np.int64)
+    assert H.token_arrays(items, 0, ptrs, lens) == 2
+    assert (int(ptrs[0]), int(lens[0]), int(ptrs[1]), int(lens[1])) == (a.ctypes.data, 10, b.ctypes.data, 3)
+    assert H.token_arrays(items, 3, ptrs, lens) == 3
+    assert H.token_arrays(items, 4, ptrs, lens) == 4
+    assert H.token_arrays(items, 5, ptrs, lens) == 7
+    assert lens[5] == 1 and lens[6] == 0
+    assert H.token_arrays(items, 8, ptrs, lens) == 8
+    with pytest.raises(ValueError):
+        H.token_arrays(items, 0, ptrs[:3], lens)
+    with pytest.raises(ValueError):
+        H.token_arrays(items, 9, ptrs, lens)
 
 
 def test_run_many_sequencing(monkeypatch):
