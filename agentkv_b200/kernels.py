@@ -91,20 +91,26 @@ class BlockOpError(RuntimeError):
 
 # ── drop-ins for triton_kernels.copy_block / zero_block ──────────────────────
 def copy_block(src: torch.Tensor, dst: torch.Tensor) -> None:
-    """Copy one KV block (triton_kernels.py:171-203) — src and dst are two
-    block views of one pool tensor, as SlabAllocator passes them."""
+    """Copy one KV block (triton_kernels.py:171-203).  Two contiguous CUDA
+    blocks of one dtype that lie a whole number of blocks apart — two block
+    views of one pool tensor, as SlabAllocator passes them — are copied by
+    akv_copy_blocks.  Any other pair of tensors of one shape is copied with
+    dst.copy_(src), the reference's own path for tensors its kernel does not
+    take (triton_kernels.py:184-196)."""
     assert src.shape == dst.shape, f"Shape mismatch: {src.shape} vs {dst.shape}"
     if not _require_cuda(src, "copy_block"):
         return
-    if not (src.is_contiguous() and dst.is_contiguous()) or src.dtype != dst.dtype:
-        raise ValueError("copy_block: src and dst must be contiguous blocks of one dtype")
     nbytes = src.numel() * src.element_size()
     if nbytes == 0:
         return
     a, b = src.data_ptr(), dst.data_ptr()
     base = min(a, b)
-    if (max(a, b) - base) % nbytes != 0:
-        raise ValueError("copy_block: src and dst must be blocks of one pool tensor")
+    one_pool = (src.is_contiguous() and dst.is_contiguous() and src.dtype == dst.dtype
+                and src.device == dst.device and (max(a, b) - base) % nbytes == 0
+                and (max(a, b) - base) // nbytes < (1 << 31) - 1)
+    if not one_pool:
+        dst.copy_(src)
+        return
     pairs = torch.tensor([[(a - base) // nbytes, (b - base) // nbytes]], dtype=torch.int32, device=src.device)
     total = (max(a, b) - base) // nbytes + 1
     N.check(

@@ -114,8 +114,9 @@ def test_zero_writes_positive_zero_bits():
 
 
 def test_dropin_copy_block_and_zero_block():
-    """kernels.copy_block / zero_block keep triton_kernels' signatures and
-    take two block views of one pool."""
+    """kernels.copy_block / zero_block keep triton_kernels' signatures: two
+    block views of one pool go through the library's copy, any other two
+    tensors of one shape are copied as the reference copies them."""
     pool = torch.randn((16, 2, 2, 4, 16, 64), dtype=torch.float16, device=DEV)
     ref = pool.clone()
     K.copy_block(pool[3], pool[9])
@@ -130,6 +131,19 @@ def test_dropin_copy_block_and_zero_block():
         K.copy_block(pool[0], pool[1, 0])
     with pytest.raises(ValueError):
         K.copy_block(pool[0].cpu(), pool[1].cpu())
+    # any two CUDA tensors of one shape, as the reference's copy_block takes:
+    # a block of another tensor, a strided view, a different dtype
+    other = torch.randn((2, 2, 4, 16, 64), dtype=torch.float16, device=DEV)
+    K.copy_block(other, pool[7])
+    ref[7] = other
+    strided = torch.randn((2, 2, 4, 64, 16), dtype=torch.float16, device=DEV).transpose(-1, -2)
+    K.copy_block(strided, pool[8])
+    ref[8] = strided
+    wide = torch.randn((2, 2, 4, 16, 64), dtype=torch.float32, device=DEV)
+    K.copy_block(wide, pool[10])
+    ref[10] = wide.to(torch.float16)
+    torch.cuda.synchronize()
+    assert torch.equal(pool.view(torch.int16), ref.view(torch.int16))
 
 
 def test_meta_blocks_are_noops():
