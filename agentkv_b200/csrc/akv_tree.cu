@@ -27,6 +27,14 @@ namespace {
 
 constexpr int kEmpty = -1;  // a deleted slot holds parent -2 and never matches
 constexpr int kMatchWarpsPerCta = 4;
+// Warps (queries) per CTA of the whole-query lookup, k_match.  A CTA's slot
+// on the SM frees only when its last query ends, so fewer warps per CTA hand
+// the SM to the next queries sooner; the register cap stays 20 warps per SM.
+#ifndef AKV_MATCH_WHOLE_WARPS
+#define AKV_MATCH_WHOLE_WARPS 4
+#endif
+constexpr int kWholeWarpsPerCta = AKV_MATCH_WHOLE_WARPS;
+static_assert(20 % kWholeWarpsPerCta == 0, "k_match: warps per CTA must divide 20");
 
 AKV_DEV uint32_t tree_hash(int32_t parent, int32_t token) {
   // MurmurHash3's 64-bit finalizer over (parent, token).
@@ -600,13 +608,13 @@ AKV_DEV void match_write(const MatchStop& s, int32_t q, int32_t block_size, int3
 // 0.0585 ms per batch on the stress tree; without those rounds, 80 registers,
 // 0.0631 ms; capped at 80 with them, 0.0603 ms with spills).
 template <int kVerifyChunks, bool kPipelined>
-__global__ void __launch_bounds__(kMatchWarpsPerCta * 32, 5)
+__global__ void __launch_bounds__(kWholeWarpsPerCta * 32, 20 / kWholeWarpsPerCta)
 k_match(AkvTreeView tree, const int32_t* __restrict__ tokens, const int64_t* __restrict__ q_off,
         int32_t nq, int32_t block_size, int32_t* __restrict__ out_node,
         int32_t* __restrict__ out_len, int64_t* __restrict__ out_compared,
         const int32_t* __restrict__ order, AkvStatus* st, bool prefetch) {
   const int lane = threadIdx.x & 31;
-  const int32_t w = blockIdx.x * kMatchWarpsPerCta + (threadIdx.x >> 5);
+  const int32_t w = blockIdx.x * kWholeWarpsPerCta + (threadIdx.x >> 5);
   if (w >= nq) return;
   const int32_t q = order != nullptr ? order[w] : w;
   if (static_cast<uint32_t>(q) >= static_cast<uint32_t>(nq)) {
@@ -1447,8 +1455,8 @@ extern "C" int akv_match_prefix_variant(const AkvTreeView* tree, const int32_t* 
   if (nq == 0) return AKV_OK;
   if ((chunks & ~(AKV_MATCH_PIPELINED | AKV_MATCH_PREFETCH)) == 0) chunks |= kWholeDefaultChunks;
   const MatchKernels* k = match_kernels(chunks);
-  const int grid = akv_ceil_div(nq, kMatchWarpsPerCta);
-  k->whole<<<grid, kMatchWarpsPerCta * 32, 0, akv_stream(stream)>>>(*tree, tokens, q_off, nq, block_size, out_node,
+  const int grid = akv_ceil_div(nq, kWholeWarpsPerCta);
+  k->whole<<<grid, kWholeWarpsPerCta * 32, 0, akv_stream(stream)>>>(*tree, tokens, q_off, nq, block_size, out_node,
                                                                     out_len, out_compared, order, status,
                                                                     (chunks & AKV_MATCH_PREFETCH) != 0);
   AKV_LAUNCH_CHECK("akv_match_prefix");

@@ -22,6 +22,8 @@
 import os
 import socket
 
+import time
+
 import numpy as np
 import pytest
 import torch
@@ -52,6 +54,7 @@ def _worker(rank, port, q):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
+    holder = {"fg": None}
     try:
         n, L, H, bs, D = 400, 2, 8, 16, 32
         g = torch.Generator(device="cpu").manual_seed(77)
@@ -107,6 +110,7 @@ def _partition_worker(rank, port, q):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
+    holder = {"fg": None}
     try:
         n, L, H, bs, D = 400, 2, 8, 16, 32
         g = torch.Generator(device="cpu").manual_seed(78)
@@ -133,20 +137,28 @@ def _partition_worker(rank, port, q):
         # three times with every child freed after its copy
         from agentkv_b200.fanout import FanoutGraph
 
-        fg = FanoutGraph(a, [3, 3], 2, 3, 1, pool=mine, free_children=True, copier=copier, id_base=base)
+        fg = holder["fg"] = FanoutGraph(a, [3, 3], 2, 3, 1, pool=mine, free_children=True, copier=copier,
+                                        id_base=base)
         roots_np = roots.cpu().numpy()
         for _ in range(3):
             fg.run(roots_np)
-            gathered = fg._keep[3].cpu()
+            res_r, _, _, _, gathered_r = fg._keep[0]  # the replay's one fan-out
+            gathered = gathered_r.cpu()
             everyone = [torch.empty_like(local) for _ in range(WORLD)]
-            dist.all_gather(everyone, fg._keep[0]["all_pairs"] + base)
+            dist.all_gather(everyone, res_r["all_pairs"] + base)
             pairs_ok &= bool(torch.equal(gathered, torch.cat(everyone).cpu()))
             O.copy_blocks(host, host.shape[1], gathered.numpy())
         torch.cuda.synchronize()
-        fg = None
+        fg = holder["fg"] = None
         want = S.head_slice(torch.from_numpy(host.view(np.int16).reshape(full.shape)), rank, WORLD)
         q.put((rank, bool(torch.equal(mine.cpu(), want)), pairs_ok))
     finally:
+        # a graph that holds NCCL calls must go before the process group, on
+        # an error too, or destroy_process_group waits for good
+        fg = holder["fg"] = None
+        import gc
+
+        gc.collect()
         dist.destroy_process_group()
 
 
@@ -281,9 +293,15 @@ def _spawn(target, extra=()):
     procs = [ctx.Process(target=target, args=(r, port, q, *extra)) for r in range(WORLD)]
     for p in procs:
         p.start()
+    deadline = time.monotonic() + 180
     for p in procs:
-        p.join(timeout=300)
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        p.join(timeout=max(1.0, deadline - time.monotonic()))
+    codes = [p.exitcode for p in procs]
+    for p in procs:  # a rank still running at the deadline is ended, not left behind
+        if p.exitcode is None:
+            p.kill()
+            p.join(timeout=30)
+    assert all(c == 0 for c in codes), codes
     return sorted(q.get(timeout=5) for _ in range(WORLD))
 
 
