@@ -30,8 +30,10 @@ constexpr int kMatchWarpsPerCta = 4;
 // Warps (queries) per CTA of the whole-query lookup, k_match.  A CTA's slot
 // on the SM frees only when its last query ends, so fewer warps per CTA hand
 // the SM to the next queries sooner; the register cap stays 20 warps per SM.
+// One query per CTA: 0.0446 ms per 4,096-query batch on the match stress
+// tree against 0.0585 ms with two and 0.0583 ms with four.
 #ifndef AKV_MATCH_WHOLE_WARPS
-#define AKV_MATCH_WHOLE_WARPS 4
+#define AKV_MATCH_WHOLE_WARPS 1
 #endif
 constexpr int kWholeWarpsPerCta = AKV_MATCH_WHOLE_WARPS;
 static_assert(20 % kWholeWarpsPerCta == 0, "k_match: warps per CTA must divide 20");
@@ -603,7 +605,7 @@ AKV_DEV void match_write(const MatchStop& s, int32_t q, int32_t block_size, int3
 
 // One warp per query (the whole query is one range).  `order` (optional)
 // lists the queries longest first, so the long walks start early and spread
-// over the SMs.  At most 96 registers (5 CTAs per SM): the 16-byte verify
+// over the SMs.  At most 96 registers (20 warps per SM): the 16-byte verify
 // rounds alone would take 126 and measured slower for it (0.0729 against
 // 0.0585 ms per batch on the stress tree; without those rounds, 80 registers,
 // 0.0631 ms; capped at 80 with them, 0.0603 ms with spills).
