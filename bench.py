@@ -1245,8 +1245,8 @@ COPY_TRAFFIC_NCU = {
                       "claimed), 3,200-block pool"),
 }
 MATCH_TRAFFIC_NCU = {
-    2000: (52435200, "ncu: one 4,096-query k_match batch (16-byte verify rounds) on the 2,000-sequence "
-                     "stress tree"),
+    2000: (52336896, "ncu: one 4,096-query k_match batch (16-byte verify rounds, one query per CTA) on the "
+                     "2,000-sequence stress tree"),
 }
 
 
