@@ -453,3 +453,50 @@ def test_run_many_sequencing(monkeypatch):
     assert made == [2, 2]
     with pytest.raises(ValueError, match="per_replay"):
         a.run_many(roots, per_replay=0)
+
+
+def _claimed_schedule(n_items: int, grid: int, claim_max: int, rng) -> list:
+    """A CPU model of k_copy_bulk's claimed item hand-out (CLAIM > 0): the
+    claim size, each CTA's dealt first range, the counter's ranges after
+    them (each CTA asks for its next range when it starts the current one)
+    and the stop rule, with the CTAs' steps interleaved at random.  Returns
+    every item each CTA processes."""
+    claim = max(1, min(claim_max, n_items // (4 * grid)))
+    dealt = grid * claim
+    counter = 0
+    done = []
+    state = []
+    for b in range(grid):
+        t = b * claim
+        nxt = dealt + counter
+        counter += claim
+        state.append([t, t + claim, nxt])
+    live = [b for b in range(grid) if state[b][0] < n_items]
+    while live:
+        b = live[rng.integers(len(live))]
+        t, end, nxt = state[b]
+        done.append(t)
+        t += 1
+        if t == end and t < n_items:
+            t, end = nxt, nxt + claim
+            if t < n_items:
+                nxt = dealt + counter
+                counter += claim
+        state[b] = [t, end, nxt]
+        if t >= n_items:
+            live.remove(b)
+    return done
+
+
+def test_claimed_copy_hands_out_every_item_once():
+    """The claimed copy's index arithmetic (k_copy_bulk with CLAIM > 0), on
+    the CPU: for batch sizes from one chunk to many claims per CTA, grids
+    smaller and larger than the batch (a counted launch may find fewer pairs
+    than its grid was sized for) and random interleavings of the CTAs, every
+    item is copied exactly once and no CTA runs past the batch."""
+    rng = np.random.default_rng(5)
+    for n_items in (1, 3, 64, 148, 149, 592, 593, 4096, 9344):
+        for grid in (1, 7, 148):
+            for claim_max in (1, 4, 8):
+                got = _claimed_schedule(n_items, grid, claim_max, rng)
+                assert sorted(got) == list(range(n_items)), (n_items, grid, claim_max)
