@@ -57,7 +57,10 @@ enum {
 /* Device-side status record (32 bytes).  code = first AKV_ERR_* seen,
  * index = batch position of the offending element, id = offending block id
  * (or node id), observed = the refcount (or other value) that failed the
- * check, aux = extra detail (e.g. the iteration count of a timed-out wait). */
+ * check, aux = extra detail (e.g. the iteration count of a timed-out wait).
+ * _reserved is the work counter of the claimed block copies
+ * (akv_copy_blocks_variant 14-18), zero between their launches; a record
+ * belongs to one stream at a time. */
 typedef struct AkvStatus {
   int32_t code;
   int32_t index;
