@@ -1,5 +1,6 @@
 // akv_lib.cu — library-level entry points: version, last error, status reset.
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstring>
 #include <thread>
@@ -67,30 +68,47 @@ extern "C" int akv_gather_upload(const uint64_t* src, const int64_t* lens, int32
     off[i + 1] = off[i] + lens[i];
   }
   const int64_t total = off[n];
-  // each thread copies whole arrays, about total / threads tokens in all
-  auto work = [&](int32_t t, int32_t parts) {
-    const int64_t lo_tok = total * t / parts, hi_tok = total * (t + 1) / parts;
-    const int32_t a = static_cast<int32_t>(std::upper_bound(off.begin(), off.end(), lo_tok) - off.begin()) - 1;
-    for (int32_t i = std::max(a, 0); i < n && off[i] < hi_tok; ++i) {
-      if (off[i] < lo_tok) continue;  // starts in the previous thread's share
-      if (lens[i]) std::memcpy(dst + off[i], reinterpret_cast<const int32_t*>(src[i]), 4 * static_cast<size_t>(lens[i]));
+  // Tokens [lo, hi) of the packing, from whichever arrays cover them.
+  auto copy_range = [&](int64_t lo, int64_t hi) {
+    if (lo >= hi) return;
+    int32_t i = static_cast<int32_t>(std::upper_bound(off.begin(), off.end(), lo) - off.begin()) - 1;
+    for (i = std::max(i, 0); i < n && off[i] < hi; ++i) {
+      const int64_t a = std::max(off[i], lo), b = std::min(off[i + 1], hi);
+      if (b > a)
+        std::memcpy(dst + a, reinterpret_cast<const int32_t*>(src[i]) + (a - off[i]), 4 * static_cast<size_t>(b - a));
     }
   };
+  // With an upload, the packing goes in slices: slice k's copy to the device
+  // is enqueued as soon as every thread has written its share of it, so the
+  // transfer of one slice overlaps the gather of the next.
   const int32_t parts = total < (1 << 16) ? 1 : threads;
-  if (parts == 1) {
-    work(0, 1);
-  } else {
-    std::vector<std::thread> pool;
-    pool.reserve(parts - 1);
-    for (int32_t t = 1; t < parts; ++t) pool.emplace_back(work, t, parts);
-    work(0, parts);
-    for (auto& th : pool) th.join();
+  const int32_t slices = (d_dst != nullptr && total >= (1 << 20)) ? 4 : 1;
+  std::vector<std::atomic<int32_t>> done(static_cast<size_t>(slices));
+  for (auto& d : done) d.store(0);
+  auto worker = [&](int32_t t) {
+    for (int32_t k = 0; k < slices; ++k) {
+      const int64_t lo = total * k / slices, hi = total * (k + 1) / slices;
+      copy_range(lo + (hi - lo) * t / parts, lo + (hi - lo) * (t + 1) / parts);
+      done[k].fetch_add(1, std::memory_order_release);
+    }
+  };
+  std::vector<std::thread> pool;
+  pool.reserve(parts - 1);
+  for (int32_t t = 1; t < parts; ++t) pool.emplace_back(worker, t);
+  // The calling thread copies share 0 of each slice, waits for the others'
+  // shares of it and enqueues its upload.
+  cudaError_t err = cudaSuccess;
+  for (int32_t k = 0; k < slices; ++k) {
+    const int64_t lo = total * k / slices, hi = total * (k + 1) / slices;
+    copy_range(lo, lo + (hi - lo) / parts);
+    done[k].fetch_add(1, std::memory_order_release);
+    while (done[k].load(std::memory_order_acquire) < parts) std::this_thread::yield();
+    if (d_dst != nullptr && hi > lo && err == cudaSuccess)
+      err = cudaMemcpyAsync(d_dst + lo, dst + lo, 4 * static_cast<size_t>(hi - lo), cudaMemcpyHostToDevice,
+                            akv_stream(stream));
   }
-  if (d_dst != nullptr && total > 0) {
-    const cudaError_t e = cudaMemcpyAsync(d_dst, dst, 4 * static_cast<size_t>(total), cudaMemcpyHostToDevice,
-                                          akv_stream(stream));
-    if (e != cudaSuccess) return akv_cuda_fail(e, "akv_gather_upload: copy");
-  }
+  for (auto& th : pool) th.join();
+  if (err != cudaSuccess) return akv_cuda_fail(err, "akv_gather_upload: copy");
   return AKV_OK;
 }
 
